@@ -1,0 +1,158 @@
+/*
+ * opc_b200.h -- C ABI of the B200 (sm_100a) fused 2-bit codebook dequant-matmul library.
+ *
+ * This is the drop-in boundary for opacc1ty's fused dequant path.  Every entry point takes
+ * plain pointers and sizes; CUDA streams are passed as `void*` (a cudaStream_t, NULL = legacy
+ * default stream).  Unless stated otherwise all data pointers are DEVICE pointers.  Calls are
+ * stream-ordered and asynchronous; no entry point on the hot path (opc_gemv) allocates memory or
+ * synchronises the host.
+ *
+ * Error convention: every `int` entry point returns OPC_OK (0) on success and a negative
+ * OPC_ERR_* code on failure; opc_last_error() then returns a human-readable message for the
+ * calling thread.  This replaces the reference's Python exceptions raised by
+ * MetalKernelManager (opacc1ty/utils/metal_utils.py:111,171,183,307) and the C runtime's
+ * `-1` + engine->error string (runtime/src/bf2_format.c:151-225).
+ *
+ * Layer data starts out in the reference's .bf2 layout (opacc1ty/format/bf2.py:121-134):
+ *   codebooks      [M][4][svs] fp16
+ *   indices        [M][K/svs]  uint8, values 0..3 (one byte per index, not packed)
+ *   outlier values [n][K]      fp16, whole output rows
+ *   outlier ids    [n]         integer row ids
+ * opc_repack_layer converts it once, at load time, into the device layout the kernels stream
+ * (see opc_layer_plan below).  Only sub_vector_size == 1 (the 2 bits/weight scalar-codebook
+ * case, 4 fp16 centroids per output row) is implemented; other sizes return
+ * OPC_ERR_UNSUPPORTED.
+ */
+#ifndef OPC_B200_H
+#define OPC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define OPC_ABI_VERSION 1
+
+enum {
+  OPC_OK = 0,
+  OPC_ERR_INVALID = -1,     /* bad argument: shape, pointer, alignment, out-of-range id */
+  OPC_ERR_UNSUPPORTED = -2, /* valid request this build does not implement (e.g. svs != 1) */
+  OPC_ERR_CUDA = -3,        /* a CUDA runtime call failed; message has the CUDA error */
+  OPC_ERR_WORKSPACE = -4,   /* workspace missing or smaller than opc_gemv_workspace_bytes() */
+  OPC_ERR_DEVICE = -5       /* a kernel reported an error through the device error word */
+};
+
+/* Geometry of one repacked layer.  Filled by opc_plan_layer(); the caller allocates the four
+ * device buffers with the byte sizes given here.
+ *
+ * Device layout ("units" are 512-byte blocks streamed by the GEMV):
+ *   units[0 .. packed_units)      packed 2-bit indices: row tile t (16 rows) x k block b (128
+ *                                 columns) is unit t*k_units + b.  Inside a unit, lane l of a
+ *                                 warp owns bytes [16l, 16l+16): four 32-bit words whose 2-bit
+ *                                 fields are laid out so that one IMAD + one PRMT yields an
+ *                                 mma.sync A-fragment register (two fp16 weights).
+ *   units[packed_units .. total)  outlier rows, 16 per tile, fp16, one 16x16 block per unit,
+ *                                 stored directly in mma.sync A-fragment order.
+ *   codebooks   [M_pad] x 8 bytes: for each row the low bytes of its 4 fp16 centroids, then
+ *               the high bytes (outlier rows and padding rows are zero).
+ *   tile_mask   [row_tiles] uint16: bit i set when row 16t+i is an outlier row.
+ *   outlier_rows[outlier_tiles*16] int32: output row of each outlier slot, -1 for padding.
+ */
+typedef struct opc_layer_plan {
+  int32_t M, K, n_outliers, sub_vector_size;
+  int32_t M_pad, K_pad;                 /* M rounded up to 16, K rounded up to 128 */
+  int32_t row_tiles, k_units;           /* M_pad/16, K_pad/128 */
+  int32_t outlier_tiles, outlier_k_units; /* ceil(n_outliers/16), K_pad/16 */
+  int64_t packed_units, total_units;
+  int64_t units_bytes, codebook_bytes, tile_mask_bytes, outlier_rows_bytes;
+} opc_layer_plan;
+
+/* A repacked layer: the plan plus the caller-owned device buffers it describes. */
+typedef struct opc_layer {
+  opc_layer_plan plan;
+  void* units;
+  void* codebooks;
+  void* tile_mask;
+  int32_t* outlier_rows;
+} opc_layer;
+
+typedef struct opc_device_props {
+  char name[256];
+  int32_t device, sm_count, cc_major, cc_minor;
+  int64_t total_mem_bytes;
+  int32_t max_smem_per_block_optin, max_threads_per_block, l2_bytes, warp_size;
+} opc_device_props;
+
+/* Library version string ("opc_b200 <semver> abi <n>"); replaces bf_version()
+ * (runtime/include/opacc1ty.h:205). */
+const char* opc_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* opc_last_error(void);
+
+/* Properties of CUDA device `device`; mirrors get_metal_device_info() / GPUInfo
+ * (opacc1ty/utils/metal_utils.py:24-76).  Returns OPC_ERR_CUDA when no device is present. */
+int opc_device_info(int32_t device, opc_device_props* out);
+
+/* Compute the device geometry for an M x K layer with n_outliers outlier rows.
+ * Replaces the size arithmetic of BF2Reader._build_index (opacc1ty/format/bf2.py:204-213). */
+int opc_plan_layer(int32_t M, int32_t K, int32_t n_outliers, int32_t sub_vector_size,
+                   opc_layer_plan* plan);
+
+/* Repack one .bf2 layer into `layer`'s device buffers (load time, not the hot path).
+ *   codebooks_f16   device [M][4][svs] fp16
+ *   indices_u8      device [M][K/svs] uint8; an index > 3 is rejected (OPC_ERR_INVALID), as
+ *                   the reference's codebook lookup would raise
+ *   outlier_f16     device [n_rows][K] fp16 (may be NULL when n_rows == 0)
+ *   outlier_ids     HOST   [n_rows] int64 row ids.  Ids outside [0, M) are rejected.  A
+ *                   repeated id keeps its LAST row, matching the sequential replacement of
+ *                   dequantize_layer (opacc1ty/export/converter.py:59-63).
+ * Outlier rows get an all-zero codebook, so "add the outlier dot product in the epilogue"
+ * (kernels/dequant_gemv.metal:118-131) and "replace the row" (converter.py:63) coincide.
+ * `layer->plan.n_outliers` must equal opc_count_distinct_ids(outlier_ids, n_rows).
+ * Synchronises `stream`. */
+int opc_repack_layer(const opc_layer* layer, const void* codebooks_f16, const uint8_t* indices_u8,
+                     const void* outlier_f16, const int64_t* outlier_ids, int32_t n_rows,
+                     void* stream);
+
+/* Number of distinct ids in a host id list (the n_outliers to plan with). */
+int32_t opc_count_distinct_ids(const int64_t* ids, int32_t n);
+
+/* Workspace bytes opc_gemv needs for `layer` on `device` (a scratch area for partial sums,
+ * then one counter per 16-row tile).  The workspace must be zero-filled once before first use
+ * (opc_workspace_init); every opc_gemv leaves its counters at zero again.  One workspace may
+ * serve any number of layers and batch sizes whose calls are ordered on one stream (size it for
+ * the layer with the most rows); calls that can overlap on the GPU need separate workspaces. */
+size_t opc_gemv_workspace_bytes(const opc_layer_plan* plan, int32_t batch, int32_t device);
+
+/* Zero `bytes` of workspace on `stream`. */
+int opc_workspace_init(void* workspace, size_t bytes, void* stream);
+
+/* Fused dequant-GEMV / small-batch GEMM:  y[b][r] = sum_k x[b][k] * W_hat[r][k]
+ * for b < batch (1..64), r < M, with W_hat = codebook lookup + outlier-row replacement.
+ *   x  device fp16, row b at x + b*ldx (ldx >= K, in elements)
+ *   y  device fp16, row b at y + b*ldy (ldy >= M)
+ * Accumulates in fp32 on the tensor cores (mma.sync m16n8k16), rounds once to fp16.
+ * Replaces MetalKernelManager.dequant_gemv (opacc1ty/utils/metal_utils.py:202-288) and
+ * metal_forward_layer (runtime/src/metal_backend.m:224-331).  Launched with programmatic
+ * dependent launch: the weight stream of this call starts while the previous opc_gemv on the
+ * stream is still finishing.  Results are deterministic (fixed summation order). */
+int opc_gemv(const opc_layer* layer, const void* x, int64_t ldx, void* y, int64_t ldy,
+             int32_t batch, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Write the dequantized matrix W_hat [M][K] fp16 (row r at w + r*ldw) from the repacked
+ * layer.  Bit-exact restatement of dequantize_layer (opacc1ty/export/converter.py:26-67),
+ * decoded with the same device routine the GEMV uses. */
+int opc_dequant(const opc_layer* layer, void* w, int64_t ldw, void* stream);
+
+/* Read and clear the device error word of `device` (synchronises the device).  Kernels with
+ * bounded waits record a nonzero code there instead of hanging; 0 = no error. */
+int opc_take_device_error(int32_t device, int32_t* code);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* OPC_B200_H */

@@ -1,0 +1,194 @@
+"""Command-line entry points (the quantize / benchmark surface of opacc1ty/cli/main.py).
+
+    python -m opac1ty_b200.cli quantize MODEL_PATH [-o out.bf2] [--sub-vector-size 1] ...
+    python -m opac1ty_b200.cli info FILE.bf2 [--layers] [--json-output]
+    python -m opac1ty_b200.cli benchmark FILE.bf2 [--batch 1] [--iters 50]
+    python -m opac1ty_b200.cli layer-bench --shape 28672x4096 [--outliers 0.01] [--batch 1]
+
+``benchmark`` replaces the reference's analytical estimate (cli/main.py:221-316) with CUDA-event
+timing of the model's quantized layers on the GPU.  ``layer-bench`` times one synthetic layer
+(the small case the kernel profiles are taken on).
+"""
+
+from __future__ import annotations
+
+import json
+import re
+import sys
+import time
+from pathlib import Path
+
+import click
+
+
+@click.group()
+@click.version_option(version="0.1.0", prog_name="opac1ty_b200")
+def cli():
+    """2-bit codebook quantization with fused sm_100a dequant-matmul kernels."""
+
+
+def _load_state_dict(path: Path) -> dict:
+    from safetensors import safe_open
+
+    files = sorted(path.glob("*.safetensors")) if path.is_dir() else [path]
+    sd = {}
+    for f in files:
+        with safe_open(str(f), framework="pt", device="cpu") as h:
+            for k in h.keys():
+                sd[k] = h.get_tensor(k)
+    return sd
+
+
+def _infer_model_config(sd: dict) -> dict:
+    """Architecture hints from tensor names and shapes (cli/main.py:413-473, condensed)."""
+    cfg = {"architecture": "unknown"}
+    layers = {int(m.group(1)) for k in sd for m in [re.search(r"(?:layers?|h)\.(\d+)", k)] if m}
+    if layers:
+        cfg["num_hidden_layers"] = max(layers) + 1
+    for k, t in sd.items():
+        if t.dim() == 2 and t.shape[0] > 512:
+            if "embed" in k.lower() or "wte" in k.lower():
+                cfg["hidden_size"], cfg["vocab_size"] = int(t.shape[1]), int(t.shape[0])
+            elif t.shape[0] == t.shape[1] and t.shape[0] > 1024:
+                cfg.setdefault("hidden_size", int(t.shape[0]))
+    for k, t in sd.items():
+        if t.dim() == 2 and t.shape[0] > cfg.get("hidden_size", 1024) * 2:
+            cfg["intermediate_size"] = int(t.shape[0])
+            break
+    if any("self_attn" in k for k in sd) and any("q_proj" in k for k in sd):
+        cfg["architecture"] = "llama"
+    if "hidden_size" in cfg:
+        cfg.setdefault("num_attention_heads", cfg["hidden_size"] // 128)
+    return cfg
+
+
+@cli.command()
+@click.argument("model_path", type=click.Path(exists=True))
+@click.option("--bits", type=int, default=2)
+@click.option("--output", "-o", type=click.Path(), default=None)
+@click.option("--outlier-fraction", type=float, default=0.01)
+@click.option("--sub-vector-size", type=int, default=8)
+@click.option("--codebook-iters", type=int, default=100)
+@click.option("--no-error-feedback", is_flag=True)
+@click.option("--device", type=click.Choice(["cpu", "cuda"]), default="cpu")
+@click.option("--json-output", is_flag=True)
+def quantize(model_path, bits, output, outlier_fraction, sub_vector_size, codebook_iters, no_error_feedback, device,
+             json_output):
+    """Quantize a safetensors model (file or directory) to .bf2 (options of cli/main.py:64-80)."""
+    from .format import BF2Writer
+    from .quantize import QuantizeConfig, VectorQuantizer
+
+    model_path = Path(model_path)
+    out = Path(output) if output else Path(model_path.stem + ".bf2")
+    sd = _load_state_dict(model_path)
+    mcfg = _infer_model_config(sd)
+    t0 = time.time()
+    q = VectorQuantizer(QuantizeConfig(bits=bits, sub_vector_size=sub_vector_size, outlier_fraction=outlier_fraction,
+                                       use_error_feedback=not no_error_feedback, codebook_iters=codebook_iters,
+                                       device=device))
+    res = q.quantize_model(sd, mcfg, progress=not json_output)
+    elapsed = time.time() - t0
+    BF2Writer(str(out)).write(res, mcfg, res["_quantize_config"], progress=not json_output)
+    orig = sum(t.numel() for t in sd.values()) * 2 / 1e9
+    comp = out.stat().st_size / 1e9
+    info = {"original_size_gb": round(orig, 2), "compressed_size_gb": round(comp, 2),
+            "compression_ratio": round(orig / comp, 1) if comp else None, "quantization_time_s": round(elapsed, 1),
+            "output_path": str(out)}
+    click.echo(json.dumps(info) if json_output else "\n".join(f"{k}: {v}" for k, v in info.items()))
+
+
+@cli.command()
+@click.argument("bf2_path", type=click.Path(exists=True))
+@click.option("--layers", is_flag=True)
+@click.option("--json-output", is_flag=True)
+def info(bf2_path, layers, json_output):
+    """Show a .bf2 file's metadata and layers."""
+    from .format import BF2Reader
+
+    with BF2Reader(bf2_path) as r:
+        d = {"model": r.model_config, "quantization": r.quantize_config,
+             "compressed_size_gb": round(Path(bf2_path).stat().st_size / 1e9, 3), "n_layers": len(r.layer_names()),
+             "layers": r.layer_names() if layers else None}
+    click.echo(json.dumps(d, indent=2) if json_output else "\n".join(f"{k}: {v}" for k, v in d.items() if v is not None))
+
+
+def _time_gemv(dl, batch: int, iters: int):
+    import torch
+
+    from . import layer as L, synthetic
+
+    x = torch.from_numpy(synthetic.activations(batch, dl.K, seed=1)).to(dl.device)
+    y = torch.empty(batch, dl.M, dtype=torch.float16, device=dl.device)
+    ws = torch.zeros(L.workspace_bytes(dl, batch), dtype=torch.uint8, device=dl.device)
+    for _ in range(3):
+        L.gemv(dl, x, out=y, workspace=ws)
+    s = torch.cuda.current_stream(dl.device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(iters):
+        L.gemv(dl, x, out=y, workspace=ws)
+    e1.record(s)
+    torch.cuda.synchronize(dl.device)
+    return e0.elapsed_time(e1) * 1000.0 / iters
+
+
+@cli.command()
+@click.argument("bf2_path", type=click.Path(exists=True))
+@click.option("--batch", type=int, default=1)
+@click.option("--iters", type=int, default=50)
+@click.option("--json-output", is_flag=True)
+def benchmark(bf2_path, batch, iters, json_output):
+    """Time every quantized (svs=1) layer of a .bf2 file on the GPU with CUDA events."""
+    from . import layer as L
+    from .format import BF2Reader
+    from .utils import get_cuda_device_info
+
+    gpu = get_cuda_device_info()
+    if gpu is None:
+        raise click.ClickException("no CUDA device")
+    rows, total_us, total_bytes = [], 0.0, 0
+    with BF2Reader(bf2_path) as r:
+        for name in r.layer_names():
+            ly = r.load_layer(name)
+            if ly["type"] != "quantized" or ly["codebooks"].shape[2] != 1:
+                continue
+            dl = L.prepare_layer(ly, name=name)
+            us = _time_gemv(dl, batch, iters)
+            nb = dl.algorithmic_bytes(batch)
+            rows.append({"layer": name, "shape": list(dl.shape), "us": round(us, 2), "gbs": round(nb / us / 1e3, 1)})
+            total_us += us
+            total_bytes += nb
+    out = {"gpu": gpu.name, "batch": batch, "layers": rows, "total_us": round(total_us, 2),
+           "tok_s": round(batch * 1e6 / total_us, 1) if total_us else None,
+           "gbs": round(total_bytes / total_us / 1e3, 1) if total_us else None}
+    click.echo(json.dumps(out, indent=None if json_output else 2))
+
+
+@cli.command("layer-bench")
+@click.option("--shape", default="28672x4096", help="MxK")
+@click.option("--outliers", type=float, default=0.01, help="outlier row fraction (0 = none)")
+@click.option("--batch", type=int, default=1)
+@click.option("--iters", type=int, default=20)
+def layer_bench(shape, outliers, batch, iters):
+    """Time one synthetic layer's fused GEMV (CUDA events); prints one JSON line."""
+    import torch
+
+    from . import layer as L, synthetic
+    from .utils import get_cuda_device_info
+
+    M, K = (int(v) for v in shape.lower().split("x"))
+    dev = torch.device("cuda", 0)
+    ly = synthetic.random_layer_device(M, K, synthetic.n_outliers_for(M, outliers), seed=0, device=dev)
+    dl = L.prepare_layer(ly, dev)
+    us = _time_gemv(dl, batch, iters)
+    nb = dl.algorithmic_bytes(batch)
+    click.echo(json.dumps({"gpu": get_cuda_device_info().name, "shape": [M, K], "n_outliers": dl.n_outliers,
+                           "batch": batch, "us": us, "bytes": nb, "gbs": nb / us / 1e3}))
+
+
+def main():
+    cli(standalone_mode=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,432 @@
+// opc_lib.cu -- C ABI (include/opc_b200.h) over the sm_100a kernels.  Single translation
+// unit: the kernels live in the included .cuh files.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <utility>
+#include <vector>
+
+#include "../../include/opc_b200.h"
+#include "opc_device.cuh"
+#include "opc_gemv.cuh"
+#include "opc_layer.cuh"
+
+#define OPC_VERSION_STRING "opc_b200 0.1.0 abi 1"
+
+namespace {
+
+thread_local char g_last_error[1024] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(OPC_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+#define OPC_CUDA(call, what)                           \
+  do {                                                 \
+    cudaError_t e_ = (call);                           \
+    if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+  } while (0)
+
+int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+struct DeviceCache {
+  int sm_count = 0;
+  int max_smem_optin = 0;
+};
+std::mutex g_mu;
+std::map<int, DeviceCache> g_dev;
+
+int device_cache(int dev, DeviceCache* out) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  DeviceCache& c = g_dev[dev];
+  if (c.sm_count == 0) {
+    OPC_CUDA(cudaDeviceGetAttribute(&c.sm_count, cudaDevAttrMultiProcessorCount, dev),
+             "cudaDeviceGetAttribute(SM count)");
+    OPC_CUDA(cudaDeviceGetAttribute(&c.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev),
+             "cudaDeviceGetAttribute(smem optin)");
+  }
+  *out = c;
+  return OPC_OK;
+}
+
+bool plan_ok(const opc_layer_plan* p) {
+  return p && p->M > 0 && p->K > 0 && p->n_outliers >= 0 && p->n_outliers <= p->M && p->sub_vector_size == 1 &&
+         p->row_tiles == ceil_div(p->M, opc::kTileRows) && p->k_units == ceil_div(p->K, opc::kPackedCols) &&
+         p->M_pad == p->row_tiles * opc::kTileRows && p->K_pad == p->k_units * opc::kPackedCols &&
+         p->outlier_tiles == ceil_div(p->n_outliers, opc::kTileRows) &&
+         p->outlier_k_units == p->K_pad / opc::kDenseCols &&
+         p->packed_units == static_cast<int64_t>(p->row_tiles) * p->k_units &&
+         p->total_units == p->packed_units + static_cast<int64_t>(p->outlier_tiles) * p->outlier_k_units;
+}
+
+opc::LayerGeom geom_of(const opc_layer_plan& p) {
+  opc::LayerGeom G;
+  G.Up = p.packed_units;
+  G.U = p.total_units;
+  G.M = p.M;
+  G.K = p.K;
+  G.K_pad = p.K_pad;
+  G.M_pad = p.M_pad;
+  G.MT = p.row_tiles;
+  G.KT = p.k_units;
+  G.OT = p.outlier_tiles;
+  G.KO = p.outlier_k_units;
+  return G;
+}
+
+// ---------------------------------------------------------------------------
+// GEMV launch configuration.
+// ---------------------------------------------------------------------------
+constexpr int kCtasPerSm = 2;
+#ifndef OPC_XS_MAX_BYTES
+#define OPC_XS_MAX_BYTES (96 * 1024)  // largest x copy staged in shared memory
+#endif
+constexpr int kXsMaxBytes = OPC_XS_MAX_BYTES;
+constexpr int kMaxBatch = 64;
+
+int nt_for_batch(int batch) {
+  if (batch <= 8) return 1;
+  if (batch <= 16) return 2;
+  if (batch <= 32) return 4;
+  return 8;
+}
+
+// At most kCtasPerSm CTAs per SM and at least one unit per warp where the layer allows (the
+// kernel's partition needs grid <= total units, which this guarantees).
+int64_t gemv_grid(const opc_layer_plan& p, int sm_count) {
+  const int64_t by_units = std::max<int64_t>(1, p.total_units / opc::kGemvWarps);
+  return std::min<int64_t>(static_cast<int64_t>(sm_count) * kCtasPerSm, by_units);
+}
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Cross-CTA partial sums: two slots of NT*128 floats per CTA.
+size_t slots_bytes(int sm_count, int nt) {
+  const int64_t ctas_max = static_cast<int64_t>(sm_count) * kCtasPerSm;
+  return static_cast<size_t>(ctas_max) * 2 * nt * 128 * sizeof(float);
+}
+
+// Workspace layout: [partial-sum slots sized for the largest batch | per-segment counters].
+// The counters sit at the same offset for every batch and every layer, so one zeroed
+// workspace can serve any sequence of calls: the counters are zero between calls (each
+// finisher resets its own) and the slot area is plain scratch.
+size_t counters_offset(int sm_count) { return align_up(slots_bytes(sm_count, nt_for_batch(kMaxBatch)), 256); }
+
+size_t workspace_bytes(const opc_layer_plan& p, int /*batch*/, int sm_count) {
+  return counters_offset(sm_count) + align_up(static_cast<size_t>(p.row_tiles + p.outlier_tiles) * sizeof(int32_t), 256);
+}
+
+template <int NT, bool XS>
+int launch_gemv_t(const opc::GemvArgs& args, int64_t grid, size_t smem, cudaStream_t stream, int dev) {
+  auto kern = opc::gemv_kernel<NT, XS>;
+  static std::mutex mu;
+  static std::map<int, size_t> configured;  // device -> dynamic smem limit already set
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = configured.find(dev);
+    if (it == configured.end() || it->second < smem) {
+      OPC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)),
+               "cudaFuncSetAttribute(max dynamic smem)");
+      configured[dev] = smem;
+    }
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(opc::kGemvThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  OPC_CUDA(cudaLaunchKernelEx(&cfg, kern, args), "launch gemv_kernel");
+  return OPC_OK;
+}
+
+template <int NT>
+int launch_gemv_nt(const opc::GemvArgs& a, bool xs, int64_t grid, size_t smem, cudaStream_t s, int dev) {
+  return xs ? launch_gemv_t<NT, true>(a, grid, smem, s, dev) : launch_gemv_t<NT, false>(a, grid, smem, s, dev);
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+}  // namespace
+
+extern "C" {
+
+const char* opc_version(void) { return OPC_VERSION_STRING; }
+
+const char* opc_last_error(void) { return g_last_error; }
+
+int opc_device_info(int32_t device, opc_device_props* out) {
+  if (!out) return fail(OPC_ERR_INVALID, "opc_device_info: out is NULL");
+  int n = 0;
+  OPC_CUDA(cudaGetDeviceCount(&n), "cudaGetDeviceCount");
+  if (device < 0 || device >= n) return fail(OPC_ERR_INVALID, "opc_device_info: device %d of %d", device, n);
+  cudaDeviceProp p;
+  OPC_CUDA(cudaGetDeviceProperties(&p, device), "cudaGetDeviceProperties");
+  memset(out, 0, sizeof(*out));
+  strncpy(out->name, p.name, sizeof(out->name) - 1);
+  out->device = device;
+  out->sm_count = p.multiProcessorCount;
+  out->cc_major = p.major;
+  out->cc_minor = p.minor;
+  out->total_mem_bytes = static_cast<int64_t>(p.totalGlobalMem);
+  out->max_smem_per_block_optin = static_cast<int32_t>(p.sharedMemPerBlockOptin);
+  out->max_threads_per_block = p.maxThreadsPerBlock;
+  out->l2_bytes = p.l2CacheSize;
+  out->warp_size = p.warpSize;
+  return OPC_OK;
+}
+
+int opc_plan_layer(int32_t M, int32_t K, int32_t n_outliers, int32_t sub_vector_size, opc_layer_plan* plan) {
+  if (!plan) return fail(OPC_ERR_INVALID, "opc_plan_layer: plan is NULL");
+  if (M <= 0 || K <= 0) return fail(OPC_ERR_INVALID, "opc_plan_layer: bad shape M=%d K=%d", M, K);
+  if (n_outliers < 0 || n_outliers > M)
+    return fail(OPC_ERR_INVALID, "opc_plan_layer: n_outliers=%d outside [0, M=%d]", n_outliers, M);
+  if (sub_vector_size != 1)
+    return fail(OPC_ERR_UNSUPPORTED, "opc_plan_layer: sub_vector_size=%d (only 1 is implemented)", sub_vector_size);
+  memset(plan, 0, sizeof(*plan));
+  plan->M = M;
+  plan->K = K;
+  plan->n_outliers = n_outliers;
+  plan->sub_vector_size = sub_vector_size;
+  plan->row_tiles = static_cast<int32_t>(ceil_div(M, opc::kTileRows));
+  plan->k_units = static_cast<int32_t>(ceil_div(K, opc::kPackedCols));
+  plan->M_pad = plan->row_tiles * opc::kTileRows;
+  plan->K_pad = plan->k_units * opc::kPackedCols;
+  plan->outlier_tiles = static_cast<int32_t>(ceil_div(n_outliers, opc::kTileRows));
+  plan->outlier_k_units = plan->K_pad / opc::kDenseCols;
+  plan->packed_units = static_cast<int64_t>(plan->row_tiles) * plan->k_units;
+  plan->total_units = plan->packed_units + static_cast<int64_t>(plan->outlier_tiles) * plan->outlier_k_units;
+  plan->units_bytes = plan->total_units * opc::kUnitBytes;
+  plan->codebook_bytes = static_cast<int64_t>(plan->M_pad) * 8;
+  plan->tile_mask_bytes = static_cast<int64_t>(plan->row_tiles) * 2;
+  plan->outlier_rows_bytes = static_cast<int64_t>(std::max(plan->outlier_tiles, 1)) * opc::kTileRows * 4;
+  return OPC_OK;
+}
+
+int32_t opc_count_distinct_ids(const int64_t* ids, int32_t n) {
+  if (!ids || n <= 0) return 0;
+  std::vector<int64_t> v(ids, ids + n);
+  std::sort(v.begin(), v.end());
+  return static_cast<int32_t>(std::unique(v.begin(), v.end()) - v.begin());
+}
+
+int opc_repack_layer(const opc_layer* L, const void* codebooks_f16, const uint8_t* indices_u8, const void* outlier_f16,
+                     const int64_t* outlier_ids, int32_t n_rows, void* stream_v) {
+  if (!L || !plan_ok(&L->plan)) return fail(OPC_ERR_INVALID, "opc_repack_layer: invalid layer plan");
+  const opc_layer_plan& p = L->plan;
+  if (!L->units || !L->codebooks || !L->tile_mask || !L->outlier_rows)
+    return fail(OPC_ERR_INVALID, "opc_repack_layer: layer buffers not allocated");
+  if (!codebooks_f16 || !indices_u8) return fail(OPC_ERR_INVALID, "opc_repack_layer: codebooks/indices NULL");
+  if (n_rows < 0 || (n_rows > 0 && (!outlier_ids || !outlier_f16)))
+    return fail(OPC_ERR_INVALID, "opc_repack_layer: %d outlier rows but ids/values NULL", n_rows);
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+
+  // Effective outlier list: a repeated id keeps its last row; sorted by id.
+  std::map<int64_t, int32_t> last_src;
+  for (int32_t i = 0; i < n_rows; ++i) {
+    const int64_t id = outlier_ids[i];
+    if (id < 0 || id >= p.M)
+      return fail(OPC_ERR_INVALID, "opc_repack_layer: outlier id %lld outside [0, %d)", static_cast<long long>(id), p.M);
+    last_src[id] = i;
+  }
+  if (static_cast<int32_t>(last_src.size()) != p.n_outliers)
+    return fail(OPC_ERR_INVALID, "opc_repack_layer: plan has %d outliers but the id list has %zu distinct ids",
+                p.n_outliers, last_src.size());
+
+  std::vector<uint16_t> mask(p.row_tiles, 0);
+  const int n_slots = std::max(p.outlier_tiles, 1) * opc::kTileRows;
+  std::vector<int32_t> orow(n_slots, -1), src(n_slots, -1);
+  int s = 0;
+  for (const auto& kv : last_src) {
+    mask[kv.first / opc::kTileRows] |= static_cast<uint16_t>(1u << (kv.first % opc::kTileRows));
+    orow[s] = static_cast<int32_t>(kv.first);
+    src[s] = kv.second;
+    ++s;
+  }
+
+  int32_t* d_src = nullptr;
+  int* d_bad = nullptr;
+  int rc = OPC_OK;
+  auto cleanup = [&]() {
+    if (d_src) cudaFree(d_src);
+    if (d_bad) cudaFree(d_bad);
+  };
+#define OPC_REPACK_CUDA(call, what)      \
+  do {                                   \
+    cudaError_t e_ = (call);             \
+    if (e_ != cudaSuccess) {             \
+      rc = cuda_fail(e_, what);          \
+      cleanup();                         \
+      return rc;                         \
+    }                                    \
+  } while (0)
+
+  OPC_REPACK_CUDA(cudaMalloc(&d_src, n_slots * sizeof(int32_t)), "cudaMalloc(repack slots)");
+  OPC_REPACK_CUDA(cudaMalloc(&d_bad, sizeof(int)), "cudaMalloc(repack flag)");
+  OPC_REPACK_CUDA(cudaMemsetAsync(d_bad, 0, sizeof(int), stream), "cudaMemsetAsync");
+  OPC_REPACK_CUDA(cudaMemcpyAsync(L->tile_mask, mask.data(), mask.size() * 2, cudaMemcpyHostToDevice, stream),
+                  "copy tile mask");
+  OPC_REPACK_CUDA(cudaMemcpyAsync(L->outlier_rows, orow.data(), n_slots * 4, cudaMemcpyHostToDevice, stream),
+                  "copy outlier rows");
+  OPC_REPACK_CUDA(cudaMemcpyAsync(d_src, src.data(), n_slots * 4, cudaMemcpyHostToDevice, stream),
+                  "copy outlier sources");
+
+  const opc::LayerGeom G = geom_of(p);
+  const int tpb = 256;
+  const int64_t n_idx_words = p.packed_units * (opc::kUnitBytes / 4);
+  opc::repack_indices_kernel<<<static_cast<unsigned>(ceil_div(n_idx_words, tpb)), tpb, 0, stream>>>(
+      G, indices_u8, static_cast<uint32_t*>(L->units), d_bad);
+  OPC_REPACK_CUDA(cudaGetLastError(), "launch repack_indices_kernel");
+  opc::repack_codebooks_kernel<<<static_cast<unsigned>(ceil_div(p.M_pad, tpb)), tpb, 0, stream>>>(
+      G, static_cast<const uint16_t*>(codebooks_f16), static_cast<const uint16_t*>(L->tile_mask),
+      static_cast<uint2*>(L->codebooks));
+  OPC_REPACK_CUDA(cudaGetLastError(), "launch repack_codebooks_kernel");
+  const int64_t n_out_words = (p.total_units - p.packed_units) * (opc::kUnitBytes / 4);
+  if (n_out_words > 0) {
+    opc::repack_outliers_kernel<<<static_cast<unsigned>(ceil_div(n_out_words, tpb)), tpb, 0, stream>>>(
+        G, static_cast<const uint16_t*>(outlier_f16), d_src, static_cast<uint32_t*>(L->units));
+    OPC_REPACK_CUDA(cudaGetLastError(), "launch repack_outliers_kernel");
+  }
+  int bad = 0;
+  OPC_REPACK_CUDA(cudaMemcpyAsync(&bad, d_bad, sizeof(int), cudaMemcpyDeviceToHost, stream), "read repack flag");
+  OPC_REPACK_CUDA(cudaStreamSynchronize(stream), "cudaStreamSynchronize(repack)");
+  cleanup();
+#undef OPC_REPACK_CUDA
+  if (bad) return fail(OPC_ERR_INVALID, "opc_repack_layer: an index value is outside 0..3");
+  return OPC_OK;
+}
+
+size_t opc_gemv_workspace_bytes(const opc_layer_plan* plan, int32_t batch, int32_t device) {
+  if (!plan || batch < 1) return 0;
+  DeviceCache dc;
+  if (device_cache(device, &dc) != OPC_OK) return 0;
+  return workspace_bytes(*plan, std::min<int32_t>(batch, kMaxBatch), dc.sm_count);
+}
+
+int opc_workspace_init(void* workspace, size_t bytes, void* stream) {
+  if (!workspace && bytes) return fail(OPC_ERR_INVALID, "opc_workspace_init: NULL workspace");
+  OPC_CUDA(cudaMemsetAsync(workspace, 0, bytes, static_cast<cudaStream_t>(stream)), "cudaMemsetAsync(workspace)");
+  return OPC_OK;
+}
+
+int opc_gemv(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ldy, int32_t batch, void* workspace,
+             size_t workspace_bytes_given, void* stream_v) {
+  if (!L || !plan_ok(&L->plan)) return fail(OPC_ERR_INVALID, "opc_gemv: invalid layer plan");
+  const opc_layer_plan& p = L->plan;
+  if (!L->units || !L->codebooks || !L->tile_mask || !L->outlier_rows)
+    return fail(OPC_ERR_INVALID, "opc_gemv: layer buffers not allocated");
+  if (batch < 1 || batch > kMaxBatch) return fail(OPC_ERR_INVALID, "opc_gemv: batch %d outside [1, %d]", batch, kMaxBatch);
+  if (!x || !y) return fail(OPC_ERR_INVALID, "opc_gemv: x or y is NULL");
+  if (ldx < p.K || ldy < p.M)
+    return fail(OPC_ERR_INVALID, "opc_gemv: ldx=%lld < K=%d or ldy=%lld < M=%d", static_cast<long long>(ldx), p.K,
+                static_cast<long long>(ldy), p.M);
+  if (!aligned(x, 2) || !aligned(y, 2)) return fail(OPC_ERR_INVALID, "opc_gemv: x/y not 2-byte aligned");
+  if (!aligned(L->units, 16) || !aligned(L->codebooks, 8))
+    return fail(OPC_ERR_INVALID, "opc_gemv: layer buffers misaligned (units 16 B, codebooks 8 B)");
+  int dev = 0;
+  OPC_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  DeviceCache dc;
+  int rc = device_cache(dev, &dc);
+  if (rc != OPC_OK) return rc;
+  const size_t need = workspace_bytes(p, batch, dc.sm_count);
+  if (!workspace || workspace_bytes_given < need || !aligned(workspace, 256))
+    return fail(OPC_ERR_WORKSPACE, "opc_gemv: workspace %zu bytes at %p, need %zu (256-byte aligned, zeroed)",
+                workspace_bytes_given, workspace, need);
+
+  const int nt = nt_for_batch(batch);
+  if (p.total_units >= (int64_t(1) << 31)) return fail(OPC_ERR_UNSUPPORTED, "opc_gemv: layer too large (2^31 units)");
+  opc::GemvArgs a;
+  memset(&a, 0, sizeof(a));
+  a.units = static_cast<const uint8_t*>(L->units);
+  a.cb = static_cast<const uint2*>(L->codebooks);
+  a.tile_mask = static_cast<const uint16_t*>(L->tile_mask);
+  a.orow = L->outlier_rows;
+  a.x = static_cast<const __half*>(x);
+  a.y = static_cast<__half*>(y);
+  a.gslots = static_cast<float*>(workspace);
+  a.counters = reinterpret_cast<int32_t*>(static_cast<char*>(workspace) + counters_offset(dc.sm_count));
+  a.ldx = ldx;
+  a.ldy = ldy;
+  a.Up = static_cast<int32_t>(p.packed_units);
+  a.U = static_cast<int32_t>(p.total_units);
+  a.M = p.M;
+  a.K = p.K;
+  a.K_pad = p.K_pad;
+  a.MT = p.row_tiles;
+  a.KT = p.k_units;
+  a.OT = p.outlier_tiles;
+  a.KO = p.outlier_k_units;
+  a.batch = batch;
+  a.x_vec16 = (p.K % 8 == 0) && (ldx % 8 == 0) && aligned(x, 16);
+  a.x_vec8 = (p.K % 4 == 0) && (ldx % 4 == 0) && aligned(x, 8);
+  a.shr2 = 1u << 30;
+  a.shr4 = 1u << 28;
+  a.shr6 = 1u << 26;
+  a.sel_add = opc::kSelAdd;
+  // x rows 0..batch-1 plus a 64-byte zero block (the B operand of absent batch columns).
+  const size_t xs_bytes = align_up(static_cast<size_t>(batch) * opc::xs_row_bytes(p.k_units) + 64, 128);
+  const bool xs = xs_bytes <= static_cast<size_t>(kXsMaxBytes);
+  a.xs_bytes = xs ? static_cast<int32_t>(xs_bytes) : 0;
+  const size_t slots_smem = static_cast<size_t>(opc::kGemvWarps) * 2 * nt * 128 * sizeof(float) + opc::kGemvWarps * 2 * sizeof(int32_t);
+  const size_t smem = a.xs_bytes + static_cast<size_t>(opc::kGemvWarps) * (opc::kRingBytesPerWarp + opc::kBarBytesPerWarp) + slots_smem;
+  if (smem > static_cast<size_t>(dc.max_smem_optin))
+    return fail(OPC_ERR_UNSUPPORTED, "opc_gemv: needs %zu bytes of shared memory, device allows %d", smem,
+                dc.max_smem_optin);
+  const int64_t grid = gemv_grid(p, dc.sm_count);
+  cudaStream_t s = static_cast<cudaStream_t>(stream_v);
+  switch (nt) {
+    case 1: return launch_gemv_nt<1>(a, xs, grid, smem, s, dev);
+    case 2: return launch_gemv_nt<2>(a, xs, grid, smem, s, dev);
+    case 4: return launch_gemv_nt<4>(a, xs, grid, smem, s, dev);
+    default: return launch_gemv_nt<8>(a, xs, grid, smem, s, dev);
+  }
+}
+
+int opc_dequant(const opc_layer* L, void* w, int64_t ldw, void* stream_v) {
+  if (!L || !plan_ok(&L->plan)) return fail(OPC_ERR_INVALID, "opc_dequant: invalid layer plan");
+  const opc_layer_plan& p = L->plan;
+  if (!w || ldw < p.K) return fail(OPC_ERR_INVALID, "opc_dequant: bad output (ldw=%lld, K=%d)", static_cast<long long>(ldw), p.K);
+  if (!aligned(L->units, 16)) return fail(OPC_ERR_INVALID, "opc_dequant: units not 16-byte aligned");
+  const opc::LayerGeom G = geom_of(p);
+  const int warps = 8;
+  opc::dequant_kernel<<<static_cast<unsigned>(ceil_div(p.total_units, warps)), warps * 32, 0,
+                        static_cast<cudaStream_t>(stream_v)>>>(
+      G, static_cast<const uint8_t*>(L->units), static_cast<const uint2*>(L->codebooks),
+      static_cast<const uint16_t*>(L->tile_mask), L->outlier_rows, static_cast<uint16_t*>(w), ldw);
+  OPC_CUDA(cudaGetLastError(), "launch dequant_kernel");
+  return OPC_OK;
+}
+
+int opc_take_device_error(int32_t device, int32_t* code) {
+  if (!code) return fail(OPC_ERR_INVALID, "opc_take_device_error: code is NULL");
+  int prev = 0;
+  OPC_CUDA(cudaGetDevice(&prev), "cudaGetDevice");
+  OPC_CUDA(cudaSetDevice(device), "cudaSetDevice");
+  int v = 0, zero = 0;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&v, opc::g_opc_device_error, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(opc::g_opc_device_error, &zero, sizeof(int));
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return cuda_fail(e, "opc_take_device_error");
+  *code = v;
+  return OPC_OK;
+}
+
+}  // extern "C"
