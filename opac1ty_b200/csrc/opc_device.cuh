@@ -39,38 +39,48 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
   return d;
 }
-// Both selectors of a masked field word m (index pairs at bits (0, 8) and (16, 24)) from one
-// 32x32->64 multiply-add: m * 0x110011 + 0x00004040'00004040.  The copies of the (0, 8) pair
-// land in bits 0..15 of the low word, those of the (16, 24) pair in bits 0..15 of the high word;
-// the other partial products stay in bits 16..31 of the low word without carrying out of it
-// (their sum is at most 0x66660000), so neither selector is disturbed.
-// `add` must hold 0x0000404000004040; it is passed in a register (a kernel argument) so the
-// addition stays inside the multiply-add instead of becoming two separate adds.
-__device__ __forceinline__ void sel_pair(uint32_t m, uint64_t add, uint32_t& s0, uint32_t& s1) {
-  asm("{\n .reg .u64 t;\n mad.wide.u32 t, %2, 1114129, %3;\n mov.b64 {%0, %1}, t;\n}\n"
-      : "=r"(s0), "=r"(s1)
-      : "r"(m), "l"(add));
+// Half-word broadcast on the FMA pipe: HADD2 of (hi, hi) with -0.  x + (-0) == x bit for bit
+// for every non-NaN fp16 value (signed zeros and subnormals included), and the words this is
+// applied to never hold a NaN half (their exponent field is at most 16), so the result is
+// exactly (x >> 16) | (x & 0xffff0000).  `negz` must be 0x80008000; it is passed in a register
+// so the addition is not folded away.
+__device__ __forceinline__ uint32_t hswz(uint32_t x, uint32_t negz) {
+  uint32_t d;
+  asm("{\n .reg .b16 lo, hi;\n .reg .b32 t;\n mov.b32 {lo, hi}, %1;\n mov.b32 t, {hi, hi};\n"
+      " add.rn.f16x2 %0, t, %2;\n}\n"
+      : "=r"(d)
+      : "r"(x), "r"(negz));
+  return d;
 }
+constexpr uint32_t kNegZero2 = 0x80008000u;
 
-// Decode the A-fragment registers of both k-steps (parity 0 -> A0, parity 1 -> A1) of one
-// packed word from its four masked field words m[r] = (w >> 2r) & 0x03030303.
-// cbl/cbh: split codebooks of rows g (index 0) and g+8 (index 1).
-constexpr uint64_t kSelAdd = 0x0000404000004040ull;
-
-__device__ __forceinline__ void decode_word(const uint32_t m[4], const uint32_t cbl[2], const uint32_t cbh[2],
-                                            uint64_t sel_add, uint32_t A0[4], uint32_t A1[4]) {
+// Decode one packed word into the A-fragment registers of its two k-steps (parity 0 -> A0,
+// parity 1 -> A1).  cbl/cbh: split codebooks of rows g (index 0) and g+8 (index 1).
+//
+// Field (r, h) pairs sit at bits (2r + 16h, 2r + 16h + 8).  The work is split between the ALU
+// pipe (8 PRMT, 4 LOP3, 2 SHF) and the FMA pipe (5 IMAD, 6 HADD2), which issue in parallel:
+//   r = 0..2: t = (w >> 2r) & 0x03030303; P = t*0x11 + 0x40404040 holds the parity-0 selector in
+//             its low half and the parity-1 selector in its high half; hswz(P) moves the latter.
+//   r = 3:    m = w & 0xC0C0C0C0; m*0x4400 + 0x40400000 lifts the (6, 14) pair into the high
+//             half (the (22, 30) pair overflows out of 32 bits), hswz brings it down; the
+//             (22, 30) pair goes through hswz(m) first.
+__device__ __forceinline__ void decode_word(uint32_t w, const uint32_t cbl[2], const uint32_t cbh[2],
+                                            uint32_t negz, uint32_t A0[4], uint32_t A1[4]) {
 #pragma unroll
-  for (int r = 0; r < 4; ++r) {
-    uint32_t s0, s1;
-    sel_pair(m[r], sel_add, s0, s1);
-    A0[r] = prmt(cbl[r & 1], cbh[r & 1], s0);
-    A1[r] = prmt(cbl[r & 1], cbh[r & 1], s1);
+  for (int r = 0; r < 3; ++r) {
+    const uint32_t t = (w >> (2 * r)) & kFieldMask;
+    uint32_t P;
+    asm("mad.lo.u32 %0, %1, 17, 1077952576;" : "=r"(P) : "r"(t));  // t*0x11 + 0x40404040
+    A0[r] = prmt(cbl[r & 1], cbh[r & 1], P);
+    A1[r] = prmt(cbl[r & 1], cbh[r & 1], hswz(P, negz));
   }
-}
-
-__device__ __forceinline__ void split_fields(uint32_t w, uint32_t m[4]) {
-#pragma unroll
-  for (int r = 0; r < 4; ++r) m[r] = (w >> (2 * r)) & kFieldMask;
+  const uint32_t m = w & 0xC0C0C0C0u;
+  uint32_t qa, qb;
+  asm("mad.lo.u32 %0, %1, 17408, 1077936128;" : "=r"(qa) : "r"(m));  // m*0x4400 + 0x40400000
+  const uint32_t mh = hswz(m, negz);
+  asm("mad.lo.u32 %0, %1, 17408, 1077936128;" : "=r"(qb) : "r"(mh));
+  A0[3] = prmt(cbl[1], cbh[1], hswz(qa, negz));
+  A1[3] = prmt(cbl[1], cbh[1], hswz(qb, negz));
 }
 
 // ---------------------------------------------------------------------------

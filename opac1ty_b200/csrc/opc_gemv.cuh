@@ -58,8 +58,7 @@ struct GemvArgs {
   int32_t xs_bytes;             // shared bytes reserved for x (0: read x from global)
   int32_t x_vec16;              // x rows 16-byte loadable (K%8==0, ldx%8==0, aligned)
   int32_t x_vec8;               // x rows 8-byte loadable (K%4==0, ldx%4==0, aligned)
-  uint32_t shr2, shr4, shr6;    // 2^30, 2^28, 2^26: right shifts done as IMAD.HI
-  uint64_t sel_add;             // kSelAdd, kept in a register by the decode
+  uint32_t negz;                // kNegZero2 (0x80008000), kept in a register by the decode
 };
 
 struct Seg {
@@ -124,8 +123,7 @@ __device__ __forceinline__ void zero_acc(float acc[2][NT][4]) {
 // Per-lane constants of the hot loop, hoisted out of the kernel-parameter bank.
 template <int NT>
 struct LaneCtx {
-  uint32_t shr2, shr4, shr6;
-  uint64_t sel_add;
+  uint32_t negz;
   // Shared-memory address of this lane's 64-byte column group in x row 8nt+g, advancing kts
   // bytes per k block.  Lanes whose batch column does not exist point at a 64-byte zero block
   // with kts = 0.  (32-bit shared-window addresses keep the address arithmetic 32-bit.)
@@ -142,15 +140,8 @@ __device__ __forceinline__ void packed_unit(const GemvArgs& a, const LaneCtx<NT>
   const uint32_t w[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    // m[r] = (w >> 2r) & 0x03030303; the shifts run as IMAD.HI (multipliers are kernel
-    // arguments, so they are not folded back into ALU shifts).
-    uint32_t mf[4];
-    mf[0] = w[j] & kFieldMask;
-    mf[1] = __umulhi(w[j], lc.shr2) & kFieldMask;
-    mf[2] = __umulhi(w[j], lc.shr4) & kFieldMask;
-    mf[3] = __umulhi(w[j], lc.shr6) & kFieldMask;
     uint32_t A0[4], A1[4];
-    decode_word(mf, m.cbl, m.cbh, lc.sel_add, A0, A1);
+    decode_word(w[j], m.cbl, m.cbh, lc.negz, A0, A1);
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       uint4 b;
@@ -417,10 +408,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
   __syncthreads();  // x staged; every warp's slot ids initialised
 
   LaneCtx<NT> lc;
-  lc.shr2 = a.shr2;
-  lc.shr4 = a.shr4;
-  lc.shr6 = a.shr6;
-  lc.sel_add = a.sel_add;
+  lc.negz = a.negz;
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
     const int bcol = 8 * nt + g;

@@ -111,9 +111,8 @@ __global__ void dequant_kernel(LayerGeom G, const uint8_t* __restrict__ units, c
     const bool live1 = r0 + 8 < G.M && !((mask >> (g + 8)) & 1u);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      uint32_t mf[4], A0[4], A1[4];
-      split_fields(wv[j], mf);
-      decode_word(mf, cbl, cbh, kSelAdd, A0, A1);
+      uint32_t A0[4], A1[4];
+      decode_word(wv[j], cbl, cbh, kNegZero2, A0, A1);
 #pragma unroll
       for (int h = 0; h < 2; ++h)
 #pragma unroll

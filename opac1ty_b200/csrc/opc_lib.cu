@@ -376,10 +376,7 @@ int opc_gemv(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ld
   a.batch = batch;
   a.x_vec16 = (p.K % 8 == 0) && (ldx % 8 == 0) && aligned(x, 16);
   a.x_vec8 = (p.K % 4 == 0) && (ldx % 4 == 0) && aligned(x, 8);
-  a.shr2 = 1u << 30;
-  a.shr4 = 1u << 28;
-  a.shr6 = 1u << 26;
-  a.sel_add = opc::kSelAdd;
+  a.negz = opc::kNegZero2;
   // x rows 0..batch-1 plus a 64-byte zero block (the B operand of absent batch columns).
   const size_t xs_bytes = align_up(static_cast<size_t>(batch) * opc::xs_row_bytes(p.k_units) + 64, 128);
   const bool xs = xs_bytes <= static_cast<size_t>(kXsMaxBytes);
