@@ -142,6 +142,21 @@ int opc_workspace_init(void* workspace, size_t bytes, void* stream);
 int opc_gemv(const opc_layer* layer, const void* x, int64_t ldx, void* y, int64_t ldy,
              int32_t batch, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Allocation-free opc_gemv, for callers that cannot allocate device memory: plugin hosts
+ * that hand a plugin only its preallocated input and output buffers, or serving processes
+ * whose whole device memory belongs to their own pool.  No counterpart in the reference.
+ * Same computation, arguments and results as opc_gemv, but the scratch comes from a 448 KiB
+ * array compiled into this library (every GPU that loads the library keeps it until exit)
+ * rather than a workspace, and the call allocates and frees nothing.  Limits: batch 1..8 and
+ * at most 16384 tiles (row tiles of 16 rows plus outlier tiles), i.e. M <= 262144; larger
+ * requests return OPC_ERR_INVALID with the reason.  The first call on each device looks up the
+ * array's device address (cudaGetSymbolAddress); make that first call before any stream
+ * capture.  Every call shares the one array, so calls that may overlap on the GPU (different
+ * streams, or different host threads on one device) race and must be serialised by the
+ * caller; each call clears the counters it needs before its kernel runs. */
+int opc_gemv_noalloc(const opc_layer* layer, const void* x, int64_t ldx, void* y, int64_t ldy,
+                     int32_t batch, void* stream);
+
 /* Write the dequantized matrix W_hat [M][K] fp16 (row r at w + r*ldw) from the repacked
  * layer.  Bit-exact restatement of dequantize_layer (opacc1ty/export/converter.py:26-67),
  * decoded with the same device routine the GEMV uses. */

@@ -104,6 +104,9 @@ PROTOTYPES = {
         [_c.POINTER(Layer), _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_int64, _c.c_int32, _c.c_void_p, _c.c_size_t,
          _c.c_void_p],
     ),
+    "opc_gemv_noalloc": (
+        _c.c_int, [_c.POINTER(Layer), _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_int64, _c.c_int32, _c.c_void_p],
+    ),
     "opc_dequant": (_c.c_int, [_c.POINTER(Layer), _c.c_void_p, _c.c_int64, _c.c_void_p]),
     "opc_take_device_error": (_c.c_int, [_c.c_int32, _c.POINTER(_c.c_int32)]),
 }

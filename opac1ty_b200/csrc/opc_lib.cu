@@ -396,6 +396,124 @@ int opc_gemv(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ld
   }
 }
 
+}  // extern "C"
+
+// ---------------------------------------------------------------------------------------------
+// Allocation-free GEMV.  Some callers of this library cannot allocate device memory: a plugin
+// host that hands its plugins only preallocated input and output buffers, or a serving process
+// whose whole device memory is owned by its own pool, where a cudaMalloc would fail or would
+// go unaccounted.  For them the GEMV's scratch (cross-CTA partial sums and per-tile counters)
+// lives in this file-scope device array instead of a caller workspace.  It is 448 KiB, and
+// every GPU that loads the library keeps it until the process exits.
+// ---------------------------------------------------------------------------------------------
+namespace {
+
+constexpr int kStaticMaxCtas = 384;         // grid cap of the allocation-free variant
+constexpr int kStaticMaxSegments = 16384;   // row tiles + outlier tiles of the largest layer
+constexpr int kStaticMaxBatch = 8;          // one n-tile of partial sums per slot
+constexpr size_t kStaticSlotsBytes = static_cast<size_t>(kStaticMaxCtas) * 2 * 128 * sizeof(float);
+constexpr size_t kStaticScratchBytes = kStaticSlotsBytes + static_cast<size_t>(kStaticMaxSegments) * sizeof(int32_t);
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kStaticScratchBytes];
+
+std::mutex g_noalloc_mu;
+std::map<int, void*> g_noalloc_ptr;  // device -> device address of g_noalloc_scratch
+
+// Device address of the scratch array on the current device.  In host code the array's name
+// only stands in for the symbol, so the address is looked up once per device, with that device
+// current, and cached.
+int noalloc_scratch(int dev, void** out) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  auto it = g_noalloc_ptr.find(dev);
+  if (it == g_noalloc_ptr.end()) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(allocation-free GEMV scratch)");
+    it = g_noalloc_ptr.emplace(dev, p).first;
+  }
+  *out = it->second;
+  return OPC_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int opc_gemv_noalloc(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ldy, int32_t batch,
+                     void* stream_v) {
+  if (!L || !plan_ok(&L->plan)) return fail(OPC_ERR_INVALID, "opc_gemv_noalloc: invalid layer plan");
+  const opc_layer_plan& p = L->plan;
+  if (!L->units || !L->codebooks || !L->tile_mask || !L->outlier_rows)
+    return fail(OPC_ERR_INVALID, "opc_gemv_noalloc: layer buffers not allocated");
+  if (batch < 1 || batch > kStaticMaxBatch)
+    return fail(OPC_ERR_INVALID, "opc_gemv_noalloc: batch %d outside [1, %d] (the static scratch holds one n-tile)",
+                batch, kStaticMaxBatch);
+  if (static_cast<int64_t>(p.row_tiles) + p.outlier_tiles > kStaticMaxSegments)
+    return fail(OPC_ERR_INVALID,
+                "opc_gemv_noalloc: %d row tiles + %d outlier tiles exceed the static scratch limit of %d tiles "
+                "(M up to %d rows); use opc_gemv with a workspace",
+                p.row_tiles, p.outlier_tiles, kStaticMaxSegments, kStaticMaxSegments * opc::kTileRows);
+  if (!x || !y) return fail(OPC_ERR_INVALID, "opc_gemv_noalloc: x or y is NULL");
+  if (ldx < p.K || ldy < p.M)
+    return fail(OPC_ERR_INVALID, "opc_gemv_noalloc: ldx=%lld < K=%d or ldy=%lld < M=%d", static_cast<long long>(ldx),
+                p.K, static_cast<long long>(ldy), p.M);
+  if (!aligned(x, 2) || !aligned(y, 2)) return fail(OPC_ERR_INVALID, "opc_gemv_noalloc: x/y not 2-byte aligned");
+  if (!aligned(L->units, 16) || !aligned(L->codebooks, 8))
+    return fail(OPC_ERR_INVALID, "opc_gemv_noalloc: layer buffers misaligned (units 16 B, codebooks 8 B)");
+  if (p.total_units >= (int64_t(1) << 31))
+    return fail(OPC_ERR_UNSUPPORTED, "opc_gemv_noalloc: layer too large (2^31 units)");
+  int dev = 0;
+  OPC_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  DeviceCache dc;
+  int rc = device_cache(dev, &dc);
+  if (rc != OPC_OK) return rc;
+  void* scratch = nullptr;
+  rc = noalloc_scratch(dev, &scratch);
+  if (rc != OPC_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream_v);
+  int32_t* counters = reinterpret_cast<int32_t*>(static_cast<char*>(scratch) + kStaticSlotsBytes);
+  // The counters must start at zero.  Each call's finishers leave them zero, but the array
+  // outlives any one call, so clear this layer's counters explicitly (no allocation involved).
+  OPC_CUDA(cudaMemsetAsync(counters, 0, (static_cast<size_t>(p.row_tiles) + p.outlier_tiles) * sizeof(int32_t), s),
+           "cudaMemsetAsync(static scratch counters)");
+
+  opc::GemvArgs a;
+  memset(&a, 0, sizeof(a));
+  a.units = static_cast<const uint8_t*>(L->units);
+  a.cb = static_cast<const uint2*>(L->codebooks);
+  a.tile_mask = static_cast<const uint16_t*>(L->tile_mask);
+  a.orow = L->outlier_rows;
+  a.x = static_cast<const __half*>(x);
+  a.y = static_cast<__half*>(y);
+  a.gslots = static_cast<float*>(scratch);
+  a.counters = counters;
+  a.ldx = ldx;
+  a.ldy = ldy;
+  a.Up = static_cast<int32_t>(p.packed_units);
+  a.U = static_cast<int32_t>(p.total_units);
+  a.M = p.M;
+  a.K = p.K;
+  a.K_pad = p.K_pad;
+  a.MT = p.row_tiles;
+  a.KT = p.k_units;
+  a.OT = p.outlier_tiles;
+  a.KO = p.outlier_k_units;
+  a.batch = batch;
+  a.x_vec16 = (p.K % 8 == 0) && (ldx % 8 == 0) && aligned(x, 16);
+  a.x_vec8 = (p.K % 4 == 0) && (ldx % 4 == 0) && aligned(x, 8);
+  a.negz = opc::kNegZero2;
+  const size_t xs_bytes = align_up(static_cast<size_t>(batch) * opc::xs_row_bytes(p.k_units) + 64, 128);
+  const bool xs = xs_bytes <= static_cast<size_t>(kXsMaxBytes);
+  a.xs_bytes = xs ? static_cast<int32_t>(xs_bytes) : 0;
+  const size_t slots_smem = static_cast<size_t>(opc::kGemvWarps) * 2 * 128 * sizeof(float) + opc::kGemvWarps * 2 * sizeof(int32_t);
+  const size_t smem = a.xs_bytes + static_cast<size_t>(opc::kGemvWarps) * (opc::kRingBytesPerWarp + opc::kBarBytesPerWarp) + slots_smem;
+  if (smem > static_cast<size_t>(dc.max_smem_optin))
+    return fail(OPC_ERR_UNSUPPORTED, "opc_gemv_noalloc: needs %zu bytes of shared memory, device allows %d", smem,
+                dc.max_smem_optin);
+  const int64_t grid = std::min<int64_t>(gemv_grid(p, dc.sm_count), kStaticMaxCtas);
+  return launch_gemv_nt<1>(a, xs, grid, smem, s, dev);
+}
+
 int opc_dequant(const opc_layer* L, void* w, int64_t ldw, void* stream_v) {
   if (!L || !plan_ok(&L->plan)) return fail(OPC_ERR_INVALID, "opc_dequant: invalid layer plan");
   const opc_layer_plan& p = L->plan;

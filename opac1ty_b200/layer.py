@@ -228,3 +228,19 @@ def gemv(dl: DeviceLayer, x: torch.Tensor, out: Optional[torch.Tensor] = None,
                      workspace.data_ptr(), workspace.numel() * workspace.element_size(), stream)
     )
     return out.squeeze(0) if squeeze and out.dim() == 2 else out
+
+
+def gemv_noalloc(dl: DeviceLayer, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """y = x @ W_hat^T through ``opc_gemv_noalloc``: no workspace, the library's built-in scratch
+    (batch <= 8).  For callers that must not allocate device memory; ``out`` should then be
+    passed in.  Calls that may overlap on the GPU share the scratch and must be serialised."""
+    squeeze = x.dim() == 1
+    x2 = x.unsqueeze(0) if squeeze else x
+    if x2.dim() != 2 or x2.shape[1] != dl.K or x2.dtype != torch.float16 or x2.stride(1) != 1:
+        raise ValueError(f"gemv_noalloc: x must be float16 [B, {dl.K}] with unit stride")
+    if out is None:
+        out = torch.empty(x2.shape[0], dl.M, dtype=torch.float16, device=dl.device)
+    y2 = out.unsqueeze(0) if out.dim() == 1 else out
+    _lib.check(_lib.load().opc_gemv_noalloc(ctypes.byref(dl.c_layer), x2.data_ptr(), x2.stride(0), y2.data_ptr(),
+                                            y2.stride(0), x2.shape[0], _stream_ptr(dl.device)))
+    return out
