@@ -1,0 +1,236 @@
+"""Output-channel (row) tensor parallelism of the decode chain over NCCL.
+
+Every projection matrix is split by output rows into ``world`` contiguous shards: codebooks,
+indices and outlier rows are all per output row, so a shard is an ordinary quantized layer of
+``rows`` x K (outlier ids falling in the shard, remapped to local ids) and nothing is
+replicated.  Each rank computes its slice of y from the full x, then an all-gather over NVLink
+restores the full y for the next GEMV:
+
+    qkv_local = W_qkv[shard] . x          -> all_gather -> qkv
+    o_local   = W_o[shard]   . q          -> all_gather -> o
+    gu_local  = W_gu[shard]  . o          -> all_gather -> gate|up
+    x_local   = W_down[shard]. gate       -> all_gather -> x
+
+Shards are multiples of 16 rows (one row tile) and all ranks use the same shard size, so
+``all_gather_into_tensor`` concatenates them in rank order; the last rank's shard may be
+shorter, its padding lies past row M and is never read.
+
+The chain logic (``tp_chain_step``) takes the GEMV and the all-gather as callables, so the same
+code runs with the CUDA library and NCCL on GPUs and with a CPU GEMV and gloo in the tests.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Callable, Dict, List, Optional, Sequence, Tuple
+
+import torch
+
+from . import decode as D
+from . import layer as L
+from . import synthetic
+
+ROW_ALIGN = 16
+
+
+def shard_rows_count(M: int, world: int, align: int = ROW_ALIGN) -> int:
+    """Rows per shard: ceil(M / world) rounded up to ``align``."""
+    per = -(-M // world)
+    return -(-per // align) * align
+
+
+def shard_bounds(M: int, world: int, align: int = ROW_ALIGN) -> List[Tuple[int, int]]:
+    """[r0, r1) of every rank's shard (rank i owns rows i*S .. min((i+1)*S, M))."""
+    S = shard_rows_count(M, world, align)
+    return [(min(i * S, M), min((i + 1) * S, M)) for i in range(world)]
+
+
+def shard_layer(layer: dict, r0: int, r1: int) -> dict:
+    """Rows [r0, r1) of a reference "quantized" layer dict (opacc1ty/quantize/vq.py:191-200
+    layout): codebooks and indices sliced, outlier rows whose id lies in the shard kept with
+    ids shifted to local numbering (a repeated id keeps its order, so the last one still wins)."""
+    M, K = (int(v) for v in layer["shape"])
+    if not (0 <= r0 <= r1 <= M):
+        raise ValueError(f"shard_layer: bad row range [{r0}, {r1}) for M={M}")
+    out = {
+        "type": "quantized",
+        "shape": (r1 - r0, K),
+        "codebooks": layer["codebooks"][r0:r1],
+        "indices": layer["indices"][r0:r1],
+        "outlier_values": None,
+        "outlier_indices": None,
+    }
+    oi = layer.get("outlier_indices")
+    ov = layer.get("outlier_values")
+    if oi is not None and ov is not None and len(oi):
+        ids = torch.as_tensor(oi).to(torch.int64).cpu()
+        keep = (ids >= r0) & (ids < r1)
+        if bool(keep.any()):
+            sel = torch.nonzero(keep).flatten()
+            out["outlier_indices"] = ids[sel] - r0
+            out["outlier_values"] = torch.as_tensor(ov)[sel.to(torch.as_tensor(ov).device)]
+    return out
+
+
+def gathered_view(gathered: torch.Tensor, world: int, batch: int, S: int, M: int) -> torch.Tensor:
+    """Full [batch, M] activations from an all-gather output laid out [world][batch][S]."""
+    g = gathered.view(world, batch, S)
+    if batch == 1:
+        return g.view(1, world * S)[:, :M]
+    return g.permute(1, 0, 2).reshape(batch, world * S)[:, :M]
+
+
+@dataclass
+class ShardedProj:
+    """One projection's local shard plus its buffers: y_local [batch, S], gathered [world*batch*S]."""
+
+    layer: object          # DeviceLayer on GPU, or a layer dict for CPU GEMVs; None if empty
+    M: int                 # full output rows
+    S: int                 # rows per shard (all ranks)
+    rows: int              # rows of this rank's shard (<= S; the last shard may be shorter)
+    y_local: torch.Tensor
+    gathered: torch.Tensor
+
+
+def tp_chain_step(x: torch.Tensor, blocks: Sequence[Dict[str, ShardedProj]], hidden: int, intermediate: int,
+                  world: int, gemv: Callable, all_gather: Callable) -> torch.Tensor:
+    """One decode step of the row-sharded chain.  ``gemv(layer, x, out)`` writes out = x . W^T,
+    ``all_gather(out_tensor, in_tensor)`` gathers shards in rank order.  Returns the full x."""
+    batch = x.shape[0]
+    cur = x
+    for blk in blocks:
+        for name in ("qkv", "o", "gate_up", "down"):
+            p = blk[name]
+            if name == "o":
+                inp = cur[:, :hidden]
+            elif name == "down":
+                inp = cur[:, :intermediate]
+            else:
+                inp = cur
+            if inp.stride(1) != 1 or (batch > 1 and not inp.is_contiguous()):
+                inp = inp.contiguous()
+            if p.rows > 0:
+                gemv(p.layer, inp, p.y_local[:, :p.rows])
+            all_gather(p.gathered, p.y_local)
+            cur = gathered_view(p.gathered, world, batch, p.S, p.M)
+    return cur
+
+
+def _alloc_proj(layer, M: int, rows: int, world: int, batch: int, device) -> ShardedProj:
+    S = shard_rows_count(M, world)
+    y = torch.zeros(batch, S, dtype=torch.float16, device=device)
+    g = torch.zeros(world * batch * S, dtype=torch.float16, device=device)
+    return ShardedProj(layer if rows > 0 else None, M, S, rows, y, g)
+
+
+@dataclass
+class TPDecodeStack:
+    """This rank's shards of every decoder block (DeviceLayers) plus the chain buffers."""
+
+    blocks: List[Dict[str, ShardedProj]]
+    hidden: int
+    intermediate: int
+    kv: int
+    rank: int
+    world: int
+    device: torch.device
+    batch: int = 1
+    group: object = None
+    graph: Optional[torch.cuda.CUDAGraph] = None
+    bufs: Dict[str, torch.Tensor] = field(default_factory=dict)
+
+    @staticmethod
+    def _shard_block(fused: Dict[str, dict], rank: int, world: int, batch: int, device) -> Dict[str, ShardedProj]:
+        blk = {}
+        for name in ("qkv", "o", "gate_up", "down"):
+            ly = fused[name]
+            M = int(ly["shape"][0])
+            r0, r1 = shard_bounds(M, world)[rank]
+            dl = L.prepare_layer(shard_layer(ly, r0, r1), device, name) if r1 > r0 else None
+            blk[name] = _alloc_proj(dl, M, r1 - r0, world, batch, device)
+        return blk
+
+    @classmethod
+    def from_fused_blocks(cls, fused_blocks: Sequence[Dict[str, dict]], cfg: dict, rank: int, world: int,
+                          device=None, batch: int = 1, group=None) -> "TPDecodeStack":
+        """Shard reference layer dicts of fused blocks ({"qkv", "o", "gate_up", "down"}, built
+        with ``decode.concat_rows``) and keep this rank's shards on ``device``."""
+        device = L._as_cuda_device(device)
+        blocks = [cls._shard_block(fb, rank, world, batch, device) for fb in fused_blocks]
+        st = cls(blocks, cfg["hidden"], cfg["intermediate"], cfg["kv"], rank, world, device, batch, group)
+        st._alloc()
+        return st
+
+    @classmethod
+    def synthetic(cls, cfg: dict, rank: int, world: int, n_layers: Optional[int] = None, device=None,
+                  batch: int = 1, outlier_fraction: float = 0.01, seed: int = 0, group=None) -> "TPDecodeStack":
+        """Same seeded weights as ``DecodeStack.synthetic`` (every rank generates each full
+        layer on its device and keeps its own row shard)."""
+        shapes = synthetic.decoder_shapes(cfg)
+        n_layers = cfg["layers"] if n_layers is None else n_layers
+        device = L._as_cuda_device(device)
+        blocks = []
+        for li in range(n_layers):
+            bd = {}
+            for pi, (name, (M, K)) in enumerate(shapes.items()):
+                n_out = synthetic.n_outliers_for(M, outlier_fraction)
+                bd[name] = synthetic.random_layer_device(M, K, n_out, seed=seed + 1000 * li + pi, device=device)
+            fused = {
+                "qkv": D.concat_rows([bd["q_proj"], bd["k_proj"], bd["v_proj"]]),
+                "o": bd["o_proj"],
+                "gate_up": D.concat_rows([bd["gate_proj"], bd["up_proj"]]),
+                "down": bd["down_proj"],
+            }
+            del bd
+            blocks.append(cls._shard_block(fused, rank, world, batch, device))
+            del fused
+        st = cls(blocks, cfg["hidden"], cfg["intermediate"], cfg["kv"], rank, world, device, batch, group)
+        st._alloc()
+        return st
+
+    def _alloc(self):
+        self.bufs = {"x": torch.zeros(self.batch, self.hidden, dtype=torch.float16, device=self.device)}
+        need = max([L.workspace_bytes(dl, self.batch) for dl in self.layers()] + [1])
+        self.workspace = torch.zeros(need, dtype=torch.uint8, device=self.device)
+
+    def layers(self) -> List[L.DeviceLayer]:
+        return [p.layer for b in self.blocks for p in b.values() if p.layer is not None]
+
+    def algorithmic_bytes(self) -> int:
+        """This rank's GEMV bytes per step (its shards; x is read in full by every rank)."""
+        return sum(dl.algorithmic_bytes(self.batch) for dl in self.layers())
+
+    def launches_per_step(self) -> int:
+        return 4 * len(self.blocks)
+
+    def _gemv(self, dl, x, out):
+        L.gemv(dl, x, out=out, workspace=self.workspace)
+
+    def _all_gather(self, out, inp):
+        import torch.distributed as dist
+
+        dist.all_gather_into_tensor(out, inp.reshape(-1), group=self.group)
+
+    def step_eager(self):
+        x = tp_chain_step(self.bufs["x"], self.blocks, self.hidden, self.intermediate, self.world,
+                          self._gemv, self._all_gather)
+        self.bufs["x"].copy_(x)
+        return self.bufs["x"]
+
+    def capture(self) -> torch.cuda.CUDAGraph:
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            self.step_eager()
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        with torch.cuda.graph(g):
+            self.step_eager()
+        self.graph = g
+        return g
+
+    def step(self):
+        if self.graph is None:
+            return self.step_eager()
+        self.graph.replay()
+        return self.bufs["x"]
