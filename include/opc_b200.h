@@ -51,14 +51,21 @@ enum {
  *   units[0 .. packed_units)      packed 2-bit indices: row tile t (16 rows) x k block b (128
  *                                 columns) is unit t*k_units + b.  Inside a unit, lane l of a
  *                                 warp owns bytes [16l, 16l+16): four 32-bit words whose 2-bit
- *                                 fields are laid out so that one IMAD + one PRMT yields an
- *                                 mma.sync A-fragment register (two fp16 weights).
- *   units[packed_units .. total)  outlier rows, 16 per tile, fp16, one 16x16 block per unit,
- *                                 stored directly in mma.sync A-fragment order.
+ *                                 fields are laid out so that a masked word is directly a PRMT
+ *                                 selector of four int8 weights, and one IMAD turns a field pair
+ *                                 into a selector of two fp16 weights (mma.sync A fragments).
+ *   then (total_units - packed_units) outlier units for the integer kernel (batch 1..2): 16 rows x
+ *                                 16 columns, each value as two int8 parts of a per-row integer
+ *                                 form, in mma.sync A-fragment order;
+ *   then as many outlier units for the fp16 kernel (16x16 fp16 blocks in A-fragment order).
+ *   units_bytes = (packed_units + 2 * outlier units) * 512.
  *   codebooks   [M_pad] x 8 bytes: for each row the low bytes of its 4 fp16 centroids, then
- *               the high bytes (outlier rows and padding rows are zero).
+ *               the high bytes; then [M_pad] x 16 bytes: the centroids as integers
+ *               c * 2^e (|.| <= 2^14) in two int8 parts (4 high, 4 low) and the int32 e.
+ *               Outlier rows and padding rows are zero.
  *   tile_mask   [row_tiles] uint16: bit i set when row 16t+i is an outlier row.
- *   outlier_rows[outlier_tiles*16] int32: output row of each outlier slot, -1 for padding.
+ *   outlier_rows[outlier_tiles*16] int32: output row of each outlier slot, -1 for padding; then
+ *               as many int32 exponents of the slots' integer rows.
  */
 typedef struct opc_layer_plan {
   int32_t M, K, n_outliers, sub_vector_size;
@@ -134,7 +141,11 @@ int opc_workspace_init(void* workspace, size_t bytes, void* stream);
  * for b < batch (1..64), r < M, with W_hat = codebook lookup + outlier-row replacement.
  *   x  device fp16, row b at x + b*ldx (ldx >= K, in elements)
  *   y  device fp16, row b at y + b*ldy (ldy >= M)
- * Accumulates in fp32 on the tensor cores (mma.sync m16n8k16), rounds once to fp16.
+ * Batch 1..2 (when the staged x fits in shared memory): x is staged per CTA as 24-bit integers
+ * (x * 2^e_x, e_x from max |x|), the centroids are the 15-bit integer codebooks above; the dot
+ * products accumulate exactly in integers (mma.sync int8, int64 combination) and are scaled and
+ * rounded once to fp16.  Larger batches: fp16 x fp16 products accumulated in fp32
+ * (mma.sync m16n8k16), rounded once to fp16.
  * Replaces MetalKernelManager.dequant_gemv (opacc1ty/utils/metal_utils.py:202-288) and
  * metal_forward_layer (runtime/src/metal_backend.m:224-331).  Launched with programmatic
  * dependent launch: the weight stream of this call starts while the previous opc_gemv on the

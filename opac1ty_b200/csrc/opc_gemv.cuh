@@ -38,13 +38,15 @@ constexpr int kChunkBytes = kChunkUnits * kUnitBytes;
 constexpr int kRingBytesPerWarp = kStages * kChunkBytes;
 constexpr int kBarBytesPerWarp = kStages * 8;
 
-// Permuted shared-memory copy of x: for batch row b, k block kt (128 columns) and lane column
-// group q, the 8 k-steps' B fragments x[b][128kt + 16s + 4q + 0..3] (s = 0..7) are 64
-// contiguous bytes.  Rows are padded by 16 bytes so different batch rows use different banks.
+// Permuted shared-memory copy of x: for batch row b and k block kt (128 columns), k sits at
+// position xs_pos16(k - 128kt), so the B fragments of lane q (4 words x 8 halves) are the 64
+// contiguous bytes at position 32q.  Rows are padded by 16 bytes so different batch rows use
+// different banks.
 __host__ __device__ constexpr int xs_row_bytes(int KT) { return KT * 256 + 16; }
 
 struct GemvArgs {
-  const uint8_t* units;
+  const uint8_t* units;         // packed units (unit u at units + 512u)
+  const uint8_t* ounits;        // fp16 outlier units (unit u >= Up at ounits + 512(u - Up))
   const uint2* cb;              // [M_pad] split codebooks
   const uint16_t* tile_mask;    // [MT]
   const int32_t* orow;          // [OT*16]
@@ -100,8 +102,8 @@ __device__ __forceinline__ Meta load_meta(const GemvArgs& a, int32_t seg, int g)
   return m;
 }
 
-// B fragment from global memory (natural layout): x[bcol][k..k+3], zero outside [0, K).
-__device__ __forceinline__ uint2 load_b_global(const GemvArgs& a, int bcol, int k) {
+// x[bcol][k..k+3] from global memory (natural layout), zero outside [0, K).
+__device__ __forceinline__ uint2 load_x4_global(const GemvArgs& a, int bcol, int k) {
   const __half* p = a.x + bcol * a.ldx + k;
   if (a.x_vec8 && k + 4 <= a.K) return __ldcg(reinterpret_cast<const uint2*>(p));
   uint16_t h[4];
@@ -109,6 +111,8 @@ __device__ __forceinline__ uint2 load_b_global(const GemvArgs& a, int bcol, int 
   for (int e = 0; e < 4; ++e) h[e] = (k + e < a.K) ? __ldcg(reinterpret_cast<const unsigned short*>(p) + e) : 0;
   return make_uint2(h[0] | (uint32_t(h[1]) << 16), h[2] | (uint32_t(h[3]) << 16));
 }
+// (x0,x1 | x2,x3) -> (x0,x2 | x1,x3): the staged order of 4 consecutive halves.
+__device__ __forceinline__ uint2 swap_mid(uint2 v) { return make_uint2(prmt(v.x, v.y, 0x5410u), prmt(v.x, v.y, 0x7632u)); }
 
 template <int NT>
 __device__ __forceinline__ void zero_acc(float acc[2][NT][4]) {
@@ -151,8 +155,8 @@ __device__ __forceinline__ void packed_unit(const GemvArgs& a, const LaneCtx<NT>
         b = make_uint4(0, 0, 0, 0);
         const int bcol = 8 * nt + g;
         if (bcol < a.batch) {
-          const int k = kt * kPackedCols + (2 * j) * 16 + 4 * q;
-          const uint2 b0 = load_b_global(a, bcol, k), b1 = load_b_global(a, bcol, k + 16);
+          const int k = kt * kPackedCols + 32 * j + 8 * q;
+          const uint2 b0 = swap_mid(load_x4_global(a, bcol, k)), b1 = swap_mid(load_x4_global(a, bcol, k + 4));
           b = make_uint4(b0.x, b0.y, b1.x, b1.y);
         }
       }
@@ -162,7 +166,8 @@ __device__ __forceinline__ void packed_unit(const GemvArgs& a, const LaneCtx<NT>
   }
 }
 
-// One outlier unit: a 16x16 fp16 block already in A-fragment order (k-step ks of the row).
+// One outlier unit: a 16x16 fp16 block already in A-fragment order; unit ks of the segment
+// covers the staged positions 32q + 4(ks&7) + 0..3 of k block ks>>3.
 template <int NT, bool XS>
 __device__ __forceinline__ void dense_unit(const GemvArgs& a, const LaneCtx<NT>& lc, uint32_t unit, int ks,
                                            int g, int q, float acc[2][NT][4]) {
@@ -177,7 +182,8 @@ __device__ __forceinline__ void dense_unit(const GemvArgs& a, const LaneCtx<NT>&
     } else {
       b = make_uint2(0, 0);
       const int bcol = 8 * nt + g;
-      if (bcol < a.batch) b = load_b_global(a, bcol, ks * kDenseCols + 4 * q);
+      // staged positions 32q + 4s + 0..3 = k offsets (0,2,1,3) from 32(s>>1) + 8q + 4(s&1)
+      if (bcol < a.batch) b = swap_mid(load_x4_global(a, bcol, kt * kPackedCols + 32 * (s >> 1) + 8 * q + 4 * (s & 1)));
     }
     mma16816(acc[0][nt], A, b.x, b.y);
   }
@@ -343,8 +349,9 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
     const int slot = c % kStages;
     const uint32_t bar = bar_base + slot * 8;
     mbar_expect_tx(bar, static_cast<uint32_t>(cnt * kUnitBytes));
-    bulk_g2s(ring_base + slot * kChunkBytes, a.units + static_cast<int64_t>(pcur.u) * kUnitBytes,
-             static_cast<uint32_t>(cnt * kUnitBytes), bar);
+    const uint8_t* src = pcur.u < a.Up ? a.units + static_cast<int64_t>(pcur.u) * kUnitBytes
+                                       : a.ounits + static_cast<int64_t>(pcur.u - a.Up) * kUnitBytes;
+    bulk_g2s(ring_base + slot * kChunkBytes, src, static_cast<uint32_t>(cnt * kUnitBytes), bar);
   };
   Cursor pc = cursor_at(a, u0);
   int32_t pchunk = 0;
@@ -397,10 +404,12 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
         const int c = base + i * kGemvThreads + threadIdx.x;
         if (c < total) {
           const int b = c / per_row, k = (c - b * per_row) * 8;
-          const int kt = k >> 7, within = k & 127, s = within >> 4, hh = (within >> 3) & 1;
-          const uint32_t dst = xs_base + static_cast<uint32_t>(b * xs_row_bytes(a.KT) + (kt * 4 + 2 * hh) * 64 + s * 8);
-          asm volatile("st.shared.v2.u32 [%0], {%1,%2};" ::"r"(dst), "r"(v[i].x), "r"(v[i].y) : "memory");
-          asm volatile("st.shared.v2.u32 [%0], {%1,%2};" ::"r"(dst + 64), "r"(v[i].z), "r"(v[i].w) : "memory");
+          // 8 consecutive k (offsets 0..7 of one lane column group and word) -> 16 bytes at
+          // position xs_pos16(k & 127), halves in the order (0,2,1,3,4,6,5,7)
+          const uint32_t dst = xs_base + static_cast<uint32_t>(b * xs_row_bytes(a.KT) + (k >> 7) * 256 +
+                                                               xs_pos16(k & 127) * 2);
+          const uint2 lo = swap_mid(make_uint2(v[i].x, v[i].y)), hi = swap_mid(make_uint2(v[i].z, v[i].w));
+          sts128(dst, make_uint4(lo.x, lo.y, hi.x, hi.y));
         }
       }
     }

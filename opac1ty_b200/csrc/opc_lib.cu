@@ -14,9 +14,10 @@
 #include "../../include/opc_b200.h"
 #include "opc_device.cuh"
 #include "opc_gemv.cuh"
+#include "opc_gemvq.cuh"
 #include "opc_layer.cuh"
 
-#define OPC_VERSION_STRING "opc_b200 0.1.0 abi 1"
+#define OPC_VERSION_STRING "opc_b200 0.2.0 abi 1"
 
 namespace {
 
@@ -119,15 +120,31 @@ size_t slots_bytes(int sm_count, int nt) {
   return static_cast<size_t>(ctas_max) * 2 * nt * 128 * sizeof(float);
 }
 
-// Workspace layout: [partial-sum slots sized for the largest batch | per-segment counters].
-// The counters sit at the same offset for every batch and every layer, so one zeroed
-// workspace can serve any sequence of calls: the counters are zero between calls (each
-// finisher resets its own) and the slot area is plain scratch.
+// Workspace layout: [fp16-kernel partial-sum slots sized for the largest batch | per-segment
+// counters | int8-kernel int64 accumulators].  The counters sit at the same offset for every
+// batch and every layer, so one zeroed workspace can serve any sequence of calls: counters and
+// accumulators are zero between calls (each finisher resets what it used) and the slot area is
+// plain scratch.  The accumulators of a large layer may overlap the counters of a smaller one;
+// both are zero whenever no call is running.
 size_t counters_offset(int sm_count) { return align_up(slots_bytes(sm_count, nt_for_batch(kMaxBatch)), 256); }
-
-size_t workspace_bytes(const opc_layer_plan& p, int /*batch*/, int sm_count) {
+size_t acc_offset(const opc_layer_plan& p, int sm_count) {
   return counters_offset(sm_count) + align_up(static_cast<size_t>(p.row_tiles + p.outlier_tiles) * sizeof(int32_t), 256);
 }
+
+size_t workspace_bytes(const opc_layer_plan& p, int /*batch*/, int sm_count) {
+  return acc_offset(p, sm_count) + static_cast<size_t>(p.M_pad) * opc::kQMaxBatch * sizeof(unsigned long long);
+}
+
+// Byte offsets inside the layer buffers (see opc_layer.cuh).
+int64_t outlier_units(const opc_layer_plan& p) { return p.total_units - p.packed_units; }
+const uint8_t* ounits_q(const opc_layer* L) { return static_cast<const uint8_t*>(L->units) + L->plan.packed_units * opc::kUnitBytes; }
+const uint8_t* ounits_h(const opc_layer* L) {
+  return static_cast<const uint8_t*>(L->units) + (L->plan.packed_units + outlier_units(L->plan)) * opc::kUnitBytes;
+}
+const uint4* codebooks_q(const opc_layer* L) {
+  return reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(L->codebooks) + static_cast<int64_t>(L->plan.M_pad) * 8);
+}
+int n_slots_of(const opc_layer_plan& p) { return std::max(p.outlier_tiles, 1) * opc::kTileRows; }
 
 template <int NT, bool XS>
 int launch_gemv_t(const opc::GemvArgs& args, int64_t grid, size_t smem, cudaStream_t stream, int dev) {
@@ -163,6 +180,38 @@ int launch_gemv_nt(const opc::GemvArgs& a, bool xs, int64_t grid, size_t smem, c
 }
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// int8 kernel: shared memory for `stages` ring stages per consumer warp.
+size_t gemvq_smem(int xs_bytes, int stages) {
+  return static_cast<size_t>(xs_bytes) + static_cast<size_t>(opc::kQConsumers) * stages * (opc::kQChunkBytes + 16) +
+         sizeof(opc::SmemSlotsQ);
+}
+
+int launch_gemvq(const opc::GemvQArgs& args, int64_t grid, size_t smem, cudaStream_t stream, int dev) {
+  static std::mutex mu;
+  static std::map<int, size_t> configured;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = configured.find(dev);
+    if (it == configured.end() || it->second < smem) {
+      OPC_CUDA(cudaFuncSetAttribute(opc::gemvq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)),
+               "cudaFuncSetAttribute(max dynamic smem, gemvq)");
+      configured[dev] = smem;
+    }
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(opc::kQThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  OPC_CUDA(cudaLaunchKernelEx(&cfg, opc::gemvq_kernel, args), "launch gemvq_kernel");
+  return OPC_OK;
+}
 
 }  // namespace
 
@@ -213,10 +262,11 @@ int opc_plan_layer(int32_t M, int32_t K, int32_t n_outliers, int32_t sub_vector_
   plan->outlier_k_units = plan->K_pad / opc::kDenseCols;
   plan->packed_units = static_cast<int64_t>(plan->row_tiles) * plan->k_units;
   plan->total_units = plan->packed_units + static_cast<int64_t>(plan->outlier_tiles) * plan->outlier_k_units;
-  plan->units_bytes = plan->total_units * opc::kUnitBytes;
-  plan->codebook_bytes = static_cast<int64_t>(plan->M_pad) * 8;
+  // units: packed, then the outlier units of the int8 kernel, then those of the fp16 kernel
+  plan->units_bytes = (2 * plan->total_units - plan->packed_units) * opc::kUnitBytes;
+  plan->codebook_bytes = static_cast<int64_t>(plan->M_pad) * (8 + 16);
   plan->tile_mask_bytes = static_cast<int64_t>(plan->row_tiles) * 2;
-  plan->outlier_rows_bytes = static_cast<int64_t>(std::max(plan->outlier_tiles, 1)) * opc::kTileRows * 4;
+  plan->outlier_rows_bytes = static_cast<int64_t>(std::max(plan->outlier_tiles, 1)) * opc::kTileRows * 8;
   return OPC_OK;
 }
 
@@ -251,7 +301,7 @@ int opc_repack_layer(const opc_layer* L, const void* codebooks_f16, const uint8_
                 p.n_outliers, last_src.size());
 
   std::vector<uint16_t> mask(p.row_tiles, 0);
-  const int n_slots = std::max(p.outlier_tiles, 1) * opc::kTileRows;
+  const int n_slots = n_slots_of(p);
   std::vector<int32_t> orow(n_slots, -1), src(n_slots, -1);
   int s = 0;
   for (const auto& kv : last_src) {
@@ -296,12 +346,18 @@ int opc_repack_layer(const opc_layer* L, const void* codebooks_f16, const uint8_
   OPC_REPACK_CUDA(cudaGetLastError(), "launch repack_indices_kernel");
   opc::repack_codebooks_kernel<<<static_cast<unsigned>(ceil_div(p.M_pad, tpb)), tpb, 0, stream>>>(
       G, static_cast<const uint16_t*>(codebooks_f16), static_cast<const uint16_t*>(L->tile_mask),
-      static_cast<uint2*>(L->codebooks));
+      static_cast<uint2*>(L->codebooks), const_cast<uint4*>(codebooks_q(L)));
   OPC_REPACK_CUDA(cudaGetLastError(), "launch repack_codebooks_kernel");
-  const int64_t n_out_words = (p.total_units - p.packed_units) * (opc::kUnitBytes / 4);
+  int32_t* oexp = L->outlier_rows + n_slots;
+  opc::outlier_exponent_kernel<<<static_cast<unsigned>(n_slots), tpb, 0, stream>>>(
+      G, static_cast<const uint16_t*>(outlier_f16), d_src, oexp);
+  OPC_REPACK_CUDA(cudaGetLastError(), "launch outlier_exponent_kernel");
+  const int64_t n_out_words = outlier_units(p) * (opc::kUnitBytes / 4);
   if (n_out_words > 0) {
     opc::repack_outliers_kernel<<<static_cast<unsigned>(ceil_div(n_out_words, tpb)), tpb, 0, stream>>>(
-        G, static_cast<const uint16_t*>(outlier_f16), d_src, static_cast<uint32_t*>(L->units));
+        G, static_cast<const uint16_t*>(outlier_f16), d_src, oexp,
+        reinterpret_cast<uint32_t*>(const_cast<uint8_t*>(ounits_q(L))),
+        reinterpret_cast<uint32_t*>(const_cast<uint8_t*>(ounits_h(L))));
     OPC_REPACK_CUDA(cudaGetLastError(), "launch repack_outliers_kernel");
   }
   int bad = 0;
@@ -352,9 +408,52 @@ int opc_gemv(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ld
 
   const int nt = nt_for_batch(batch);
   if (p.total_units >= (int64_t(1) << 31)) return fail(OPC_ERR_UNSUPPORTED, "opc_gemv: layer too large (2^31 units)");
+  cudaStream_t s = static_cast<cudaStream_t>(stream_v);
+
+  // Batch 1..2: the integer kernel, when its staged x and at least two ring stages fit.
+  if (batch <= opc::kQMaxBatch) {
+    const int xs_q = static_cast<int>(align_up(static_cast<size_t>(3 * batch) * opc::xsq_col_bytes(p.k_units) +
+                                                   opc::kQZeroBytes, 128));
+    int stages = opc::kQMaxStages;
+    while (stages >= 2 && gemvq_smem(xs_q, stages) > static_cast<size_t>(dc.max_smem_optin)) --stages;
+    if (stages >= 2) {
+      opc::GemvQArgs q;
+      memset(&q, 0, sizeof(q));
+      q.units = static_cast<const uint8_t*>(L->units);
+      q.ounits = ounits_q(L);
+      q.cbq = codebooks_q(L);
+      q.tile_mask = static_cast<const uint16_t*>(L->tile_mask);
+      q.orow = L->outlier_rows;
+      q.oexp = L->outlier_rows + n_slots_of(p);
+      q.x = static_cast<const __half*>(x);
+      q.y = static_cast<__half*>(y);
+      q.acc = reinterpret_cast<unsigned long long*>(static_cast<char*>(workspace) + acc_offset(p, dc.sm_count));
+      q.counters = reinterpret_cast<int32_t*>(static_cast<char*>(workspace) + counters_offset(dc.sm_count));
+      q.ldx = ldx;
+      q.ldy = ldy;
+      q.Up = static_cast<int32_t>(p.packed_units);
+      q.U = static_cast<int32_t>(p.total_units);
+      q.M = p.M;
+      q.K = p.K;
+      q.K_pad = p.K_pad;
+      q.MT = p.row_tiles;
+      q.KT = p.k_units;
+      q.OT = p.outlier_tiles;
+      q.KO = p.outlier_k_units;
+      q.batch = batch;
+      q.stages = stages;
+      q.xs_bytes = xs_q;
+      q.x_vec16 = (p.K % 8 == 0) && (ldx % 8 == 0) && aligned(x, 16);
+      q.negz = opc::kNegZero2;
+      const int64_t grid = std::min<int64_t>(dc.sm_count, std::max<int64_t>(1, p.total_units / opc::kQConsumers));
+      return launch_gemvq(q, grid, gemvq_smem(xs_q, stages), s, dev);
+    }
+  }
+
   opc::GemvArgs a;
   memset(&a, 0, sizeof(a));
   a.units = static_cast<const uint8_t*>(L->units);
+  a.ounits = ounits_h(L);
   a.cb = static_cast<const uint2*>(L->codebooks);
   a.tile_mask = static_cast<const uint16_t*>(L->tile_mask);
   a.orow = L->outlier_rows;
@@ -387,7 +486,6 @@ int opc_gemv(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ld
     return fail(OPC_ERR_UNSUPPORTED, "opc_gemv: needs %zu bytes of shared memory, device allows %d", smem,
                 dc.max_smem_optin);
   const int64_t grid = gemv_grid(p, dc.sm_count);
-  cudaStream_t s = static_cast<cudaStream_t>(stream_v);
   switch (nt) {
     case 1: return launch_gemv_nt<1>(a, xs, grid, smem, s, dev);
     case 2: return launch_gemv_nt<2>(a, xs, grid, smem, s, dev);
@@ -480,6 +578,7 @@ int opc_gemv_noalloc(const opc_layer* L, const void* x, int64_t ldx, void* y, in
   opc::GemvArgs a;
   memset(&a, 0, sizeof(a));
   a.units = static_cast<const uint8_t*>(L->units);
+  a.ounits = ounits_h(L);
   a.cb = static_cast<const uint2*>(L->codebooks);
   a.tile_mask = static_cast<const uint16_t*>(L->tile_mask);
   a.orow = L->outlier_rows;
@@ -523,7 +622,7 @@ int opc_dequant(const opc_layer* L, void* w, int64_t ldw, void* stream_v) {
   const int warps = 8;
   opc::dequant_kernel<<<static_cast<unsigned>(ceil_div(p.total_units, warps)), warps * 32, 0,
                         static_cast<cudaStream_t>(stream_v)>>>(
-      G, static_cast<const uint8_t*>(L->units), static_cast<const uint2*>(L->codebooks),
+      G, static_cast<const uint8_t*>(L->units), ounits_h(L), static_cast<const uint2*>(L->codebooks),
       static_cast<const uint16_t*>(L->tile_mask), L->outlier_rows, static_cast<uint16_t*>(w), ldw);
   OPC_CUDA(cudaGetLastError(), "launch dequant_kernel");
   return OPC_OK;
