@@ -57,8 +57,9 @@ enum {
  *   then (total_units - packed_units) outlier units for the integer kernel (batch 1..2): 16 rows x
  *                                 16 columns, each value as two int8 parts of a per-row integer
  *                                 form, in mma.sync A-fragment order;
- *   then as many outlier units for the fp16 kernel (16x16 fp16 blocks in A-fragment order).
- *   units_bytes = (packed_units + 2 * outlier units) * 512.
+ *   then as many outlier units for the fp16 kernel (16x16 fp16 blocks in A-fragment order);
+ *   then the outlier rows row-major, [outlier_tiles*16][K_pad] fp16 (prefill GEMM).
+ *   units_bytes = (packed_units + 2 * outlier units) * 512 + max(outlier_tiles,1)*16*K_pad*2.
  *   codebooks   [M_pad] x 8 bytes: for each row the low bytes of its 4 fp16 centroids, then
  *               the high bytes; then [M_pad] x 16 bytes: the centroids as integers
  *               c * 2^e (|.| <= 2^14) in two int8 parts (4 high, 4 low) and the int32 e.
@@ -167,6 +168,42 @@ int opc_gemv(const opc_layer* layer, const void* x, int64_t ldx, void* y, int64_
  * caller; each call clears the counters it needs before its kernel runs. */
 int opc_gemv_noalloc(const opc_layer* layer, const void* x, int64_t ldx, void* y, int64_t ldy,
                      int32_t batch, void* stream);
+
+/* Prefill GEMM on the 5th-generation tensor cores:  y[t][r] = sum_k x[t][k] * W_hat[r][k]
+ * for t < n_tok tokens.  Replaces the reference's dequant_gemm_2bit pipeline
+ * (kernels/dequant_gemm.metal:34-149, loaded by metal_utils.py:188-196).
+ *   x  device fp16 [n_tok][ldx], 16-byte aligned, ldx a multiple of 8 (read with TMA)
+ *   y  device fp16 [n_tok][ldy] (ldy >= M)
+ * Weight tiles of 128 rows are decoded from the packed indices into shared memory and multiplied
+ * with 256-token x tiles by tcgen05.mma (fp16 x fp16 -> fp32 in tensor memory), rounded once to
+ * fp16; outlier rows are computed by a second launch from the row-major outlier copy.  No
+ * workspace.  Other x layouts return OPC_ERR_UNSUPPORTED (use opc_gemv, batch <= 64). */
+int opc_gemm(const opc_layer* layer, const void* x, int64_t ldx, void* y, int64_t ldy, int32_t n_tok,
+             void* stream);
+
+/* Decode chain: a sequence of dependent GEMVs run by ONE persistent cooperative kernel (one CTA
+ * per SM; a producer warp streams every step's weights ahead across step boundaries; a grid
+ * barrier between steps).  Replaces per-step dispatch of MetalKernelManager.dequant_gemv for
+ * a forward pass (runtime/src/inference.c:117-233 calls one layer at a time).  Each step is the
+ * batch 1..2 integer GEMV of opc_gemv; results equal opc_gemv's bit for bit.
+ *   steps[0].x      the chain input (device fp16, ldx)
+ *   steps[j].x      for j >= 1 must be steps[j-1].y with the same leading dimension (a prefix:
+ *                   steps[j].layer K <= steps[j-1].layer M)
+ * Requires batch 1..2 and batch * K_pad <= 32768 for every step.  opc_chain_create copies the
+ * step list to the device and allocates the chain's scratch (freed by opc_chain_destroy);
+ * opc_chain_launch clears the scratch and launches on `stream` (capturable into a CUDA graph).
+ * One chain must not run on two streams at once. */
+typedef struct opc_chain opc_chain;
+typedef struct opc_chain_step {
+  const opc_layer* layer;
+  const void* x;
+  int64_t ldx;
+  void* y;
+  int64_t ldy;
+} opc_chain_step;
+int opc_chain_create(const opc_chain_step* steps, int32_t n_steps, int32_t batch, opc_chain** out);
+int opc_chain_launch(opc_chain* chain, void* stream);
+int opc_chain_destroy(opc_chain* chain);
 
 /* Write the dequantized matrix W_hat [M][K] fp16 (row r at w + r*ldw) from the repacked
  * layer.  Bit-exact restatement of dequantize_layer (opacc1ty/export/converter.py:26-67),

@@ -70,6 +70,16 @@ class Layer(ctypes.Structure):
     ]
 
 
+class ChainStep(ctypes.Structure):
+    _fields_ = [
+        ("layer", ctypes.POINTER(Layer)),
+        ("x", ctypes.c_void_p),
+        ("ldx", ctypes.c_int64),
+        ("y", ctypes.c_void_p),
+        ("ldy", ctypes.c_int64),
+    ]
+
+
 class DeviceProps(ctypes.Structure):
     _fields_ = [
         ("name", ctypes.c_char * 256),
@@ -107,6 +117,12 @@ PROTOTYPES = {
     "opc_gemv_noalloc": (
         _c.c_int, [_c.POINTER(Layer), _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_int64, _c.c_int32, _c.c_void_p],
     ),
+    "opc_gemm": (
+        _c.c_int, [_c.POINTER(Layer), _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_int64, _c.c_int32, _c.c_void_p],
+    ),
+    "opc_chain_create": (_c.c_int, [_c.POINTER(ChainStep), _c.c_int32, _c.c_int32, _c.POINTER(_c.c_void_p)]),
+    "opc_chain_launch": (_c.c_int, [_c.c_void_p, _c.c_void_p]),
+    "opc_chain_destroy": (_c.c_int, [_c.c_void_p]),
     "opc_dequant": (_c.c_int, [_c.POINTER(Layer), _c.c_void_p, _c.c_int64, _c.c_void_p]),
     "opc_take_device_error": (_c.c_int, [_c.c_int32, _c.POINTER(_c.c_int32)]),
 }

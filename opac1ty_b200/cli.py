@@ -186,6 +186,39 @@ def layer_bench(shape, outliers, batch, iters):
                            "batch": batch, "us": us, "bytes": nb, "gbs": nb / us / 1e3}))
 
 
+@cli.command("gemm-bench")
+@click.option("--shape", default="28672x4096", help="MxK")
+@click.option("--tokens", type=int, default=2048)
+@click.option("--outliers", type=float, default=0.01, help="outlier row fraction (0 = none)")
+@click.option("--iters", type=int, default=10)
+def gemm_bench(shape, tokens, outliers, iters):
+    """Time one synthetic layer's prefill GEMM (tcgen05, CUDA events); prints one JSON line."""
+    import torch
+
+    from . import gemm as G, layer as L, synthetic
+    from .utils import get_cuda_device_info
+
+    M, K = (int(v) for v in shape.lower().split("x"))
+    dev = torch.device("cuda", 0)
+    ly = synthetic.random_layer_device(M, K, synthetic.n_outliers_for(M, outliers), seed=0, device=dev)
+    dl = L.prepare_layer(ly, dev)
+    x = torch.randn(tokens, K, device=dev).half()
+    y = torch.empty(tokens, M, dtype=torch.float16, device=dev)
+    for _ in range(3):
+        G.gemm(dl, x, out=y)
+    s = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(iters):
+        G.gemm(dl, x, out=y)
+    e1.record(s)
+    torch.cuda.synchronize(dev)
+    us = e0.elapsed_time(e1) * 1000.0 / iters
+    fl = G.flops(dl, tokens)
+    click.echo(json.dumps({"gpu": get_cuda_device_info().name, "shape": [M, K], "tokens": tokens,
+                           "n_outliers": dl.n_outliers, "us": us, "tflops": fl / us / 1e6}))
+
+
 def main():
     cli(standalone_mode=True)
 

@@ -2,9 +2,11 @@
 // bit-exact dequantization kernel used to prove that layout against the reference.
 //
 // Device buffers of a repacked layer (sizes in opc_plan_layer):
-//   units     [packed units | int8 outlier units | fp16 outlier units], 512 bytes each
+//   units     [packed units | int8 outlier units | fp16 outlier units], 512 bytes each, then the
+//             outlier rows row-major [slots][K_pad] fp16 (the prefill GEMM's dense pass)
 //   codebooks [M_pad] x 8 B split fp16 centroids, then [M_pad] x 16 B integer codebooks
-//             {4 x int8 high part, 4 x int8 low part, int32 exponent, 0}
+//             {4 x int8 high part, 4 x int8 low part, int32 exponent, 0}; an outlier row's entry
+//             is {0, 0, exponent of its integer row, outlier slot}
 //   tile_mask [MT] uint16
 //   outlier_rows [slots] int32 output rows, then [slots] int32 exponents of the int8 rows
 #pragma once
@@ -97,9 +99,12 @@ __global__ void repack_codebooks_kernel(LayerGeom G, const uint16_t* __restrict_
   outq[r] = vq;
 }
 
-// Exponent of each outlier slot's integer row (one block per slot).
+// Exponent of each outlier slot's integer row (one block per slot).  The integer-codebook entry
+// of an outlier row (zero centroids) also records {.z = exponent, .w = slot}, so a row can be
+// mapped to its slot (used by the decode-chain kernel).
 __global__ void outlier_exponent_kernel(LayerGeom G, const uint16_t* __restrict__ ov,
-                                        const int32_t* __restrict__ slot_src, int32_t* __restrict__ oexp) {
+                                        const int32_t* __restrict__ slot_src, const int32_t* __restrict__ orow,
+                                        int32_t* __restrict__ oexp, uint4* __restrict__ cbq) {
   const int slot = blockIdx.x;
   const int src = slot_src[slot];
   float m = 0.f;
@@ -115,7 +120,10 @@ __global__ void outlier_exponent_kernel(LayerGeom G, const uint16_t* __restrict_
   if (threadIdx.x == 0) {
     float t = 0.f;
     for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t = fmaxf(t, red[w]);
-    oexp[slot] = int_exponent(t);
+    const int e = int_exponent(t);
+    oexp[slot] = e;
+    const int row = orow[slot];
+    if (row >= 0) cbq[row] = make_uint4(0u, 0u, static_cast<uint32_t>(e), static_cast<uint32_t>(slot));
   }
 }
 
@@ -167,6 +175,17 @@ __global__ void repack_outliers_kernel(LayerGeom G, const uint16_t* __restrict__
     const uint32_t hi = value(src, kb + kin_of_pos16(p0 + 1));
     out_h[wi] = lo | (hi << 16);
   }
+}
+
+// Row-major copy of the outlier rows by slot, zero-padded to K_pad (padding slots are zero).
+__global__ void repack_dense_outliers_kernel(LayerGeom G, const uint16_t* __restrict__ ov,
+                                             const int32_t* __restrict__ slot_src, int32_t n_slots,
+                                             uint16_t* __restrict__ out) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= static_cast<int64_t>(n_slots) * G.K_pad) return;
+  const int slot = static_cast<int>(i / G.K_pad), k = static_cast<int>(i % G.K_pad);
+  const int src = slot_src[slot];
+  out[i] = (src >= 0 && k < G.K) ? ov[static_cast<int64_t>(src) * G.K + k] : static_cast<uint16_t>(0);
 }
 
 // W_hat [M][K] fp16 from the repacked layer.  One warp per unit of the packed region and of the

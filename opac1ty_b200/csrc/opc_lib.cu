@@ -1,5 +1,7 @@
 // opc_lib.cu -- C ABI (include/opc_b200.h) over the sm_100a kernels.  Single translation
 // unit: the kernels live in the included .cuh files.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -13,6 +15,8 @@
 
 #include "../../include/opc_b200.h"
 #include "opc_device.cuh"
+#include "opc_chain.cuh"
+#include "opc_gemm.cuh"
 #include "opc_gemv.cuh"
 #include "opc_gemvq.cuh"
 #include "opc_layer.cuh"
@@ -145,6 +149,10 @@ const uint4* codebooks_q(const opc_layer* L) {
   return reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(L->codebooks) + static_cast<int64_t>(L->plan.M_pad) * 8);
 }
 int n_slots_of(const opc_layer_plan& p) { return std::max(p.outlier_tiles, 1) * opc::kTileRows; }
+const __half* dense_outliers(const opc_layer* L) {
+  return reinterpret_cast<const __half*>(static_cast<const uint8_t*>(L->units) +
+                                         (2 * L->plan.total_units - L->plan.packed_units) * opc::kUnitBytes);
+}
 
 template <int NT, bool XS>
 int launch_gemv_t(const opc::GemvArgs& args, int64_t grid, size_t smem, cudaStream_t stream, int dev) {
@@ -185,6 +193,38 @@ bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) %
 size_t gemvq_smem(int xs_bytes, int stages) {
   return static_cast<size_t>(xs_bytes) + static_cast<size_t>(opc::kQConsumers) * stages * (opc::kQChunkBytes + 16) +
          sizeof(opc::SmemSlotsQ);
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link-time libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+template <bool kDense>
+int launch_gemm_t(const CUtensorMap& tx, const opc::GemmArgs& a, dim3 grid, cudaStream_t stream, int dev) {
+  static std::mutex mu;
+  static std::map<int, bool> configured;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!configured[dev]) {
+      OPC_CUDA(cudaFuncSetAttribute(opc::gemm_kernel<kDense>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(opc::kGmSmemBytes)),
+               "cudaFuncSetAttribute(max dynamic smem, gemm)");
+      configured[dev] = true;
+    }
+  }
+  opc::gemm_kernel<kDense><<<grid, opc::kGmThreads, opc::kGmSmemBytes, stream>>>(tx, a);
+  OPC_CUDA(cudaGetLastError(), "launch gemm_kernel");
+  return OPC_OK;
 }
 
 int launch_gemvq(const opc::GemvQArgs& args, int64_t grid, size_t smem, cudaStream_t stream, int dev) {
@@ -263,7 +303,9 @@ int opc_plan_layer(int32_t M, int32_t K, int32_t n_outliers, int32_t sub_vector_
   plan->packed_units = static_cast<int64_t>(plan->row_tiles) * plan->k_units;
   plan->total_units = plan->packed_units + static_cast<int64_t>(plan->outlier_tiles) * plan->outlier_k_units;
   // units: packed, then the outlier units of the int8 kernel, then those of the fp16 kernel
-  plan->units_bytes = (2 * plan->total_units - plan->packed_units) * opc::kUnitBytes;
+  // and the row-major outlier rows of the prefill GEMM
+  plan->units_bytes = (2 * plan->total_units - plan->packed_units) * opc::kUnitBytes +
+                      static_cast<int64_t>(std::max(plan->outlier_tiles, 1)) * opc::kTileRows * plan->K_pad * 2;
   plan->codebook_bytes = static_cast<int64_t>(plan->M_pad) * (8 + 16);
   plan->tile_mask_bytes = static_cast<int64_t>(plan->row_tiles) * 2;
   plan->outlier_rows_bytes = static_cast<int64_t>(std::max(plan->outlier_tiles, 1)) * opc::kTileRows * 8;
@@ -349,8 +391,9 @@ int opc_repack_layer(const opc_layer* L, const void* codebooks_f16, const uint8_
       static_cast<uint2*>(L->codebooks), const_cast<uint4*>(codebooks_q(L)));
   OPC_REPACK_CUDA(cudaGetLastError(), "launch repack_codebooks_kernel");
   int32_t* oexp = L->outlier_rows + n_slots;
+  int32_t* d_orow = L->outlier_rows;
   opc::outlier_exponent_kernel<<<static_cast<unsigned>(n_slots), tpb, 0, stream>>>(
-      G, static_cast<const uint16_t*>(outlier_f16), d_src, oexp);
+      G, static_cast<const uint16_t*>(outlier_f16), d_src, d_orow, oexp, const_cast<uint4*>(codebooks_q(L)));
   OPC_REPACK_CUDA(cudaGetLastError(), "launch outlier_exponent_kernel");
   const int64_t n_out_words = outlier_units(p) * (opc::kUnitBytes / 4);
   if (n_out_words > 0) {
@@ -360,6 +403,11 @@ int opc_repack_layer(const opc_layer* L, const void* codebooks_f16, const uint8_
         reinterpret_cast<uint32_t*>(const_cast<uint8_t*>(ounits_h(L))));
     OPC_REPACK_CUDA(cudaGetLastError(), "launch repack_outliers_kernel");
   }
+  const int64_t n_dense = static_cast<int64_t>(n_slots) * p.K_pad;
+  opc::repack_dense_outliers_kernel<<<static_cast<unsigned>(ceil_div(n_dense, tpb)), tpb, 0, stream>>>(
+      G, static_cast<const uint16_t*>(outlier_f16), d_src, n_slots,
+      reinterpret_cast<uint16_t*>(const_cast<__half*>(dense_outliers(L))));
+  OPC_REPACK_CUDA(cudaGetLastError(), "launch repack_dense_outliers_kernel");
   int bad = 0;
   OPC_REPACK_CUDA(cudaMemcpyAsync(&bad, d_bad, sizeof(int), cudaMemcpyDeviceToHost, stream), "read repack flag");
   OPC_REPACK_CUDA(cudaStreamSynchronize(stream), "cudaStreamSynchronize(repack)");
@@ -625,6 +673,234 @@ int opc_dequant(const opc_layer* L, void* w, int64_t ldw, void* stream_v) {
       G, static_cast<const uint8_t*>(L->units), ounits_h(L), static_cast<const uint2*>(L->codebooks),
       static_cast<const uint16_t*>(L->tile_mask), L->outlier_rows, static_cast<uint16_t*>(w), ldw);
   OPC_CUDA(cudaGetLastError(), "launch dequant_kernel");
+  return OPC_OK;
+}
+
+int opc_gemm(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ldy, int32_t n_tok, void* stream_v) {
+  if (!L || !plan_ok(&L->plan)) return fail(OPC_ERR_INVALID, "opc_gemm: invalid layer plan");
+  const opc_layer_plan& p = L->plan;
+  if (!L->units || !L->codebooks || !L->tile_mask || !L->outlier_rows)
+    return fail(OPC_ERR_INVALID, "opc_gemm: layer buffers not allocated");
+  if (n_tok < 1) return fail(OPC_ERR_INVALID, "opc_gemm: n_tok %d < 1", n_tok);
+  if (!x || !y) return fail(OPC_ERR_INVALID, "opc_gemm: x or y is NULL");
+  if (ldx < p.K || ldy < p.M)
+    return fail(OPC_ERR_INVALID, "opc_gemm: ldx=%lld < K=%d or ldy=%lld < M=%d", static_cast<long long>(ldx), p.K,
+                static_cast<long long>(ldy), p.M);
+  if (!aligned(x, 16) || ldx % 8 != 0)
+    return fail(OPC_ERR_UNSUPPORTED, "opc_gemm: x must be 16-byte aligned with ldx a multiple of 8 (TMA)");
+  if (!aligned(y, 2)) return fail(OPC_ERR_INVALID, "opc_gemm: y not 2-byte aligned");
+  if (!aligned(L->units, 16) || !aligned(L->codebooks, 8))
+    return fail(OPC_ERR_INVALID, "opc_gemm: layer buffers misaligned");
+  if (static_cast<int64_t>(n_tok) > (int64_t(65535) * opc::kGmN))
+    return fail(OPC_ERR_UNSUPPORTED, "opc_gemm: n_tok %d too large", n_tok);
+  auto encode = tensor_map_encoder();
+  if (!encode) return fail(OPC_ERR_CUDA, "opc_gemm: cuTensorMapEncodeTiled unavailable");
+  int dev = 0;
+  OPC_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  DeviceCache dc;
+  int rc = device_cache(dev, &dc);
+  if (rc != OPC_OK) return rc;
+  if (opc::kGmSmemBytes > static_cast<size_t>(dc.max_smem_optin))
+    return fail(OPC_ERR_UNSUPPORTED, "opc_gemm: needs %zu bytes of shared memory", opc::kGmSmemBytes);
+
+  CUtensorMap tx;
+  const cuuint64_t gdim[2] = {static_cast<cuuint64_t>(p.K), static_cast<cuuint64_t>(n_tok)};
+  const cuuint64_t gstride[1] = {static_cast<cuuint64_t>(ldx) * 2};
+  const cuuint32_t box[2] = {opc::kGmK, opc::kGmN};
+  const cuuint32_t estride[2] = {1, 1};
+  const CUresult cr = encode(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(x), gdim, gstride, box, estride,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cr != CUDA_SUCCESS) return fail(OPC_ERR_CUDA, "opc_gemm: cuTensorMapEncodeTiled failed (%d)", static_cast<int>(cr));
+
+  opc::GemmArgs a;
+  memset(&a, 0, sizeof(a));
+  a.units = static_cast<const uint8_t*>(L->units);
+  a.cb = static_cast<const uint2*>(L->codebooks);
+  a.tile_mask = static_cast<const uint16_t*>(L->tile_mask);
+  a.dense = dense_outliers(L);
+  a.orow = L->outlier_rows;
+  a.y = static_cast<__half*>(y);
+  a.ldy = ldy;
+  a.M = p.M;
+  a.K_pad = p.K_pad;
+  a.MT = p.row_tiles;
+  a.KT = p.k_units;
+  a.n_tok = n_tok;
+  a.n_slots = p.outlier_tiles * opc::kTileRows;
+  cudaStream_t s = static_cast<cudaStream_t>(stream_v);
+  const unsigned n_tiles = static_cast<unsigned>(ceil_div(n_tok, opc::kGmN));
+  rc = launch_gemm_t<false>(tx, a, dim3(static_cast<unsigned>(ceil_div(p.M_pad, opc::kGmM)), n_tiles), s, dev);
+  if (rc != OPC_OK || p.n_outliers == 0) return rc;
+  return launch_gemm_t<true>(tx, a, dim3(static_cast<unsigned>(ceil_div(a.n_slots, opc::kGmM)), n_tiles), s, dev);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------------------------
+// Decode chain (persistent cooperative kernel).
+// ---------------------------------------------------------------------------------------------
+struct opc_chain {
+  int device = 0;
+  int32_t n_layers = 0, batch = 1, stages = 2, xs_bytes = 0, grid = 0;
+  size_t smem = 0;
+  void* dev_mem = nullptr;          // [layers | sync | acc]
+  opc::ChainLayer* d_layers = nullptr;
+  unsigned int* d_sync = nullptr;
+  size_t clear_bytes = 0;           // sync + acc, cleared before every launch
+};
+
+extern "C" {
+
+int opc_chain_create(const opc_chain_step* steps, int32_t n_steps, int32_t batch, opc_chain** out) {
+  if (!out) return fail(OPC_ERR_INVALID, "opc_chain_create: out is NULL");
+  *out = nullptr;
+  if (!steps || n_steps < 1) return fail(OPC_ERR_INVALID, "opc_chain_create: no steps");
+  if (batch < 1 || batch > opc::kQMaxBatch)
+    return fail(OPC_ERR_UNSUPPORTED, "opc_chain_create: batch %d (the chain runs batch 1..%d)", batch, opc::kQMaxBatch);
+  int dev = 0;
+  OPC_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  DeviceCache dc;
+  int rc = device_cache(dev, &dc);
+  if (rc != OPC_OK) return rc;
+  std::vector<opc::ChainLayer> hl(n_steps);
+  int32_t kt_max = 1;
+  size_t acc_bytes = 0;
+  std::vector<size_t> acc_off(n_steps);
+  for (int j = 0; j < n_steps; ++j) {
+    const opc_chain_step& st = steps[j];
+    if (!st.layer || !plan_ok(&st.layer->plan)) return fail(OPC_ERR_INVALID, "opc_chain_create: step %d: invalid layer", j);
+    const opc_layer* L = st.layer;
+    const opc_layer_plan& p = L->plan;
+    if (!L->units || !L->codebooks || !L->tile_mask || !L->outlier_rows || !aligned(L->units, 16))
+      return fail(OPC_ERR_INVALID, "opc_chain_create: step %d: layer buffers missing or misaligned", j);
+    if (!st.x || !st.y || st.ldx < p.K || st.ldy < p.M || !aligned(st.x, 2) || !aligned(st.y, 2))
+      return fail(OPC_ERR_INVALID, "opc_chain_create: step %d: bad x/y (ldx=%lld K=%d ldy=%lld M=%d)", j,
+                  static_cast<long long>(st.ldx), p.K, static_cast<long long>(st.ldy), p.M);
+    if (j > 0) {
+      const opc_chain_step& pv = steps[j - 1];
+      if (st.x != pv.y || st.ldx != pv.ldy || p.K > pv.layer->plan.M)
+        return fail(OPC_ERR_UNSUPPORTED,
+                    "opc_chain_create: step %d: x must be the previous step's y (same pointer and leading "
+                    "dimension, K <= previous M)", j);
+    }
+    if (static_cast<int64_t>(batch) * p.K_pad > 32768)
+      return fail(OPC_ERR_UNSUPPORTED, "opc_chain_create: step %d: batch*K_pad = %lld > 32768", j,
+                  static_cast<long long>(batch) * p.K_pad);
+    if (p.total_units >= (int64_t(1) << 31)) return fail(OPC_ERR_UNSUPPORTED, "opc_chain_create: layer too large");
+    opc::ChainLayer& c = hl[j];
+    memset(&c, 0, sizeof(c));
+    c.units = static_cast<const uint8_t*>(L->units);
+    c.ounits = ounits_q(L);
+    c.cbq = codebooks_q(L);
+    c.tile_mask = static_cast<const uint16_t*>(L->tile_mask);
+    c.orow = L->outlier_rows;
+    c.oexp = L->outlier_rows + n_slots_of(p);
+    c.x = static_cast<const __half*>(st.x);
+    c.y = static_cast<__half*>(st.y);
+    c.ldx = st.ldx;
+    c.ldy = st.ldy;
+    c.Up = static_cast<int32_t>(p.packed_units);
+    c.U = static_cast<int32_t>(p.total_units);
+    c.M = p.M;
+    c.K = p.K;
+    c.K_pad = p.K_pad;
+    c.MT = p.row_tiles;
+    c.KT = p.k_units;
+    c.OT = p.outlier_tiles;
+    c.KO = p.outlier_k_units;
+    c.x_vec16 = (p.K % 8 == 0) && (st.ldx % 8 == 0) && aligned(st.x, 16);
+    kt_max = std::max(kt_max, p.k_units);
+    acc_off[j] = acc_bytes;
+    acc_bytes += align_up(static_cast<size_t>(n_slots_of(p)) * opc::kQMaxBatch * sizeof(unsigned long long), 256);
+  }
+  const int xs = static_cast<int>(align_up(static_cast<size_t>(3 * batch) * opc::xsq_col_bytes(kt_max) + opc::kQZeroBytes, 128));
+  auto smem_for = [&](int stages) {
+    return static_cast<size_t>(xs) + static_cast<size_t>(opc::kQConsumers) * stages * (opc::kQChunkBytes + 16) +
+           sizeof(opc::ChainShared);
+  };
+  int stages = opc::kQMaxStages;
+  while (stages >= 2 && smem_for(stages) > static_cast<size_t>(dc.max_smem_optin)) --stages;
+  if (stages < 2) return fail(OPC_ERR_UNSUPPORTED, "opc_chain_create: staged x too large for shared memory");
+  const size_t smem = smem_for(stages);
+  OPC_CUDA(cudaFuncSetAttribute(opc::chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)),
+           "cudaFuncSetAttribute(max dynamic smem, chain)");
+  int per_sm = 0;
+  OPC_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, opc::chain_kernel, opc::kQThreads, smem),
+           "cudaOccupancyMaxActiveBlocksPerMultiprocessor(chain)");
+  if (per_sm < 1) return fail(OPC_ERR_UNSUPPORTED, "opc_chain_create: chain kernel does not fit on an SM");
+
+  const size_t layers_bytes = align_up(sizeof(opc::ChainLayer) * n_steps, 256);
+  const size_t sync_bytes = 256;
+  opc_chain* ch = new opc_chain();
+  ch->device = dev;
+  ch->n_layers = n_steps;
+  ch->batch = batch;
+  ch->stages = stages;
+  ch->xs_bytes = xs;
+  ch->smem = smem;
+  ch->grid = dc.sm_count;
+  ch->clear_bytes = sync_bytes + acc_bytes;
+  cudaError_t e = cudaMalloc(&ch->dev_mem, layers_bytes + sync_bytes + acc_bytes);
+  if (e != cudaSuccess) {
+    delete ch;
+    return cuda_fail(e, "cudaMalloc(chain)");
+  }
+  char* base = static_cast<char*>(ch->dev_mem);
+  ch->d_layers = reinterpret_cast<opc::ChainLayer*>(base);
+  ch->d_sync = reinterpret_cast<unsigned int*>(base + layers_bytes);
+  unsigned long long* acc = reinterpret_cast<unsigned long long*>(base + layers_bytes + sync_bytes);
+  for (int j = 0; j < n_steps; ++j) hl[j].acc = reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(acc) + acc_off[j]);
+  e = cudaMemcpy(ch->d_layers, hl.data(), sizeof(opc::ChainLayer) * n_steps, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemset(ch->d_sync, 0, ch->clear_bytes);
+  if (e != cudaSuccess) {
+    cudaFree(ch->dev_mem);
+    delete ch;
+    return cuda_fail(e, "chain setup copy");
+  }
+  *out = ch;
+  return OPC_OK;
+}
+
+int opc_chain_launch(opc_chain* ch, void* stream_v) {
+  if (!ch) return fail(OPC_ERR_INVALID, "opc_chain_launch: chain is NULL");
+  int dev = 0;
+  OPC_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  if (dev != ch->device) return fail(OPC_ERR_INVALID, "opc_chain_launch: chain lives on device %d, current is %d", ch->device, dev);
+  cudaStream_t s = static_cast<cudaStream_t>(stream_v);
+  OPC_CUDA(cudaMemsetAsync(ch->d_sync, 0, ch->clear_bytes, s), "cudaMemsetAsync(chain scratch)");
+  opc::ChainArgs a;
+  memset(&a, 0, sizeof(a));
+  a.layers = ch->d_layers;
+  a.sync = ch->d_sync;
+  a.n_layers = ch->n_layers;
+  a.batch = ch->batch;
+  a.stages = ch->stages;
+  a.xs_bytes = ch->xs_bytes;
+  a.negz = opc::kNegZero2;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(ch->grid));
+  cfg.blockDim = dim3(opc::kQThreads);
+  cfg.dynamicSmemBytes = ch->smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  OPC_CUDA(cudaLaunchKernelEx(&cfg, opc::chain_kernel, a), "launch chain_kernel");
+  return OPC_OK;
+}
+
+int opc_chain_destroy(opc_chain* ch) {
+  if (!ch) return OPC_OK;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(ch->device);
+  const cudaError_t e = cudaFree(ch->dev_mem);
+  cudaSetDevice(prev);
+  delete ch;
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFree(chain)");
   return OPC_OK;
 }
 

@@ -38,8 +38,10 @@ def test_plan_shapes():
     p = plan_layer(4096, 4096, 40)
     assert (p.row_tiles, p.k_units, p.outlier_tiles, p.outlier_k_units) == (256, 32, 3, 256)
     assert p.packed_units == 8192 and p.total_units == 8192 + 3 * 256
-    # packed units + int8 outlier units + fp16 outlier units; split fp16 + integer codebooks
-    assert p.units_bytes == (8192 + 2 * 3 * 256) * 512 and p.codebook_bytes == 4096 * (8 + 16)
+    # packed units + int8 outlier units + fp16 outlier units + row-major outlier rows (3*16 x 4096
+    # fp16); split fp16 + integer codebooks
+    assert p.units_bytes == (8192 + 2 * 3 * 256) * 512 + 48 * 4096 * 2
+    assert p.codebook_bytes == 4096 * (8 + 16)
     assert p.outlier_rows_bytes == 3 * 16 * 8
     p = plan_layer(17, 37, 2)
     assert (p.M_pad, p.K_pad, p.row_tiles, p.k_units) == (32, 128, 2, 1)

@@ -1,0 +1,79 @@
+"""Prefill GEMM (tcgen05) parity through the C ABI: y = x . W_hat^T against the oracle's fp64
+recompute on the dequantized weights.  Tolerance: norm-wise max relative error 2e-3."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+from opac1ty_b200 import gemm as G
+from opac1ty_b200 import layer as L
+from opac1ty_b200 import synthetic
+
+REL_TOL = 2e-3
+
+
+def _run(cuda_device, M, K, n_out, n_tok, seed=0, **kw):
+    ly = synthetic.random_layer(M, K, n_out, seed=seed, **kw)
+    dl = L.prepare_layer(ly, cuda_device)
+    x = synthetic.activations(n_tok, K, seed=seed + 1)
+    y = G.gemm(dl, torch.from_numpy(x).to(cuda_device))
+    torch.cuda.synchronize()
+    y64 = oracle.gemv_f64(oracle.dequantize_np(ly), x)
+    return y.cpu().numpy(), y64, dl
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,K,n_out,n_tok", [
+    (128, 128, 0, 1),
+    (256, 512, 3, 64),
+    (300, 520, 5, 300),       # ragged M, K, tokens
+    (1024, 1024, 10, 512),
+    (4096, 4096, 40, 512),
+    (640, 14336, 7, 257),     # long K (down projection), one partial token tile
+])
+def test_gemm_matches_fp64(cuda_device, M, K, n_out, n_tok):
+    y, y64, _ = _run(cuda_device, M, K, n_out, n_tok)
+    assert y.shape == (n_tok, M)
+    assert np.all(np.isfinite(y))
+    assert oracle.rel_err(y, y64) <= REL_TOL
+
+
+@pytest.mark.gpu
+def test_gemm_unaligned_k_and_duplicate_ids(cuda_device):
+    M, K, n_tok = 200, 37, 33
+    ly = synthetic.random_layer(M, K, 4, seed=3, shuffle_ids=True)
+    ly["outlier_indices"] = torch.cat([ly["outlier_indices"], ly["outlier_indices"][:1], torch.tensor([M - 1])])
+    ly["outlier_values"] = torch.cat([ly["outlier_values"], ly["outlier_values"][:1] * 3, ly["outlier_values"][1:2]])
+    dl = L.prepare_layer(ly, cuda_device)
+    x = synthetic.activations(n_tok, K, seed=9)
+    y = G.gemm(dl, torch.from_numpy(x).to(cuda_device)).cpu().numpy()
+    y64 = oracle.gemv_f64(oracle.dequantize_np(ly), x)
+    assert oracle.rel_err(y, y64) <= REL_TOL
+
+
+@pytest.mark.gpu
+def test_gemm_matches_gemv_and_is_deterministic(cuda_device):
+    M, K, n_tok = 512, 2048, 40
+    ly = synthetic.random_layer(M, K, 6, seed=4)
+    dl = L.prepare_layer(ly, cuda_device)
+    x = torch.from_numpy(synthetic.activations(n_tok, K, seed=5)).to(cuda_device)
+    y1 = G.gemm(dl, x)
+    y2 = G.gemm(dl, x)
+    yv = L.gemv(dl, x)
+    torch.cuda.synchronize()
+    assert torch.equal(y1, y2)
+    y64 = oracle.gemv_f64(oracle.dequantize_np(ly), x.cpu().numpy())
+    assert oracle.rel_err(y1.cpu().numpy(), y64) <= REL_TOL
+    assert oracle.rel_err(yv.cpu().numpy(), y64) <= REL_TOL
+
+
+@pytest.mark.gpu
+def test_gemm_reports_no_device_error(cuda_device):
+    from opac1ty_b200 import _lib
+    import ctypes
+
+    _run(cuda_device, 256, 256, 2, 100)
+    code = ctypes.c_int32(-1)
+    _lib.check(_lib.load().opc_take_device_error(0, ctypes.byref(code)))
+    assert code.value == 0
