@@ -189,7 +189,7 @@ int opc_gemm(const opc_layer* layer, const void* x, int64_t ldx, void* y, int64_
  *   steps[0].x      the chain input (device fp16, ldx)
  *   steps[j].x      for j >= 1 must be steps[j-1].y with the same leading dimension (a prefix:
  *                   steps[j].layer K <= steps[j-1].layer M)
- * Requires batch 1..2 and batch * K_pad <= 32768 for every step.  opc_chain_create copies the
+ * Requires batch 1..2 and batch * K_pad <= 30720 for every step.  opc_chain_create copies the
  * step list to the device and allocates the chain's scratch (freed by opc_chain_destroy);
  * opc_chain_launch clears the scratch and launches on `stream` (capturable into a CUDA graph).
  * One chain must not run on two streams at once. */
@@ -204,6 +204,15 @@ typedef struct opc_chain_step {
 int opc_chain_create(const opc_chain_step* steps, int32_t n_steps, int32_t batch, opc_chain** out);
 int opc_chain_launch(opc_chain* chain, void* stream);
 int opc_chain_destroy(opc_chain* chain);
+/* Tracing: with a device buffer of opc_chain_trace_bytes() set, every launch records per step
+ * and per CTA eight %globaltimer stamps (ns), taken by the CTA's first consumer thread: input
+ * ready (after the grid barrier), its own x loads done, exponents known, x staged, its own units
+ * done, all units done, writes fenced, flag published.  Layout [step][cta][8] uint64; NULL
+ * turns tracing off.
+ * opc_chain_grid() is the number of CTAs (one per SM). */
+size_t opc_chain_trace_bytes(const opc_chain* chain);
+int32_t opc_chain_grid(const opc_chain* chain);
+int opc_chain_set_trace(opc_chain* chain, void* trace);
 
 /* Write the dequantized matrix W_hat [M][K] fp16 (row r at w + r*ldw) from the repacked
  * layer.  Bit-exact restatement of dequantize_layer (opacc1ty/export/converter.py:26-67),

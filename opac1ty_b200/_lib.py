@@ -123,6 +123,9 @@ PROTOTYPES = {
     "opc_chain_create": (_c.c_int, [_c.POINTER(ChainStep), _c.c_int32, _c.c_int32, _c.POINTER(_c.c_void_p)]),
     "opc_chain_launch": (_c.c_int, [_c.c_void_p, _c.c_void_p]),
     "opc_chain_destroy": (_c.c_int, [_c.c_void_p]),
+    "opc_chain_trace_bytes": (_c.c_size_t, [_c.c_void_p]),
+    "opc_chain_grid": (_c.c_int32, [_c.c_void_p]),
+    "opc_chain_set_trace": (_c.c_int, [_c.c_void_p, _c.c_void_p]),
     "opc_dequant": (_c.c_int, [_c.POINTER(Layer), _c.c_void_p, _c.c_int64, _c.c_void_p]),
     "opc_take_device_error": (_c.c_int, [_c.c_int32, _c.POINTER(_c.c_int32)]),
 }

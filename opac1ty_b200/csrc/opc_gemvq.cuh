@@ -25,7 +25,7 @@
 
 namespace opc {
 
-constexpr int kQConsumers = 16;                    // consumer warps per CTA
+constexpr int kQConsumers = 15;                    // consumer warps per CTA (+1 producer: 4 warps per SM sub-partition)
 constexpr int kQProducerWarp = kQConsumers;        // warp index of the producer
 constexpr int kQThreads = (kQConsumers + 1) * 32;
 constexpr int kQConsumerThreads = kQConsumers * 32;
@@ -317,32 +317,49 @@ __global__ void __launch_bounds__(kQThreads, 1) gemvq_kernel(const GemvQArgs a) 
   griddep_wait();  // x and the workspace may be written by the previous kernel
 
   // Stage x: pass 1, max |x| per batch row; pass 2, integer digits at their staged positions.
+  // Each pass loads 8 chunks of 8 halves per thread at once (all loads in flight together).
   {
     const int per_row = a.K_pad / 8;
     const int total = a.batch * per_row;
+    auto load8 = [&](int base, uint4 v[8]) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int c = base + i * kQConsumerThreads;
+        v[i] = make_uint4(0, 0, 0, 0);
+        if (c < total) {
+          const int b = c / per_row, k = (c - b * per_row) * 8;
+          if (a.x_vec16) {
+            if (k < a.K) v[i] = __ldcg(reinterpret_cast<const uint4*>(a.x + b * a.ldx + k));
+          } else {
+            uint16_t h[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              h[e] = (k + e < a.K) ? __ldcg(reinterpret_cast<const unsigned short*>(a.x + b * a.ldx + k + e)) : 0;
+            v[i] = make_uint4(h[0] | (uint32_t(h[1]) << 16), h[2] | (uint32_t(h[3]) << 16),
+                              h[4] | (uint32_t(h[5]) << 16), h[6] | (uint32_t(h[7]) << 16));
+          }
+        }
+      }
+    };
     float mx[kQMaxBatch] = {0.f, 0.f};
-    for (int c = tid; c < total; c += kQConsumerThreads) {
-      const int b = c / per_row, k = (c - b * per_row) * 8;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (a.x_vec16) {
-        if (k < a.K) v = __ldcg(reinterpret_cast<const uint4*>(a.x + b * a.ldx + k));
-      } else {
-        uint16_t h[8];
+    for (int base = tid; base < total; base += 8 * kQConsumerThreads) {
+      uint4 v[8];
+      load8(base, v);
 #pragma unroll
-        for (int e = 0; e < 8; ++e)
-          h[e] = (k + e < a.K) ? __ldcg(reinterpret_cast<const unsigned short*>(a.x + b * a.ldx + k + e)) : 0;
-        v = make_uint4(h[0] | (uint32_t(h[1]) << 16), h[2] | (uint32_t(h[3]) << 16), h[4] | (uint32_t(h[5]) << 16),
-                       h[6] | (uint32_t(h[7]) << 16));
-      }
-      const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
-      float m = 0.f;
+      for (int i = 0; i < 8; ++i) {
+        const int c = base + i * kQConsumerThreads;
+        if (c < total) {
+          const uint32_t wv[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+          float m = 0.f;
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&wv[e]));
-        m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&wv[e]));
+            m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
+          }
+          if (c / per_row == 0) mx[0] = fmaxf(mx[0], m);
+          else mx[1] = fmaxf(mx[1], m);
+        }
       }
-      if (b == 0) mx[0] = fmaxf(mx[0], m);
-      else mx[1] = fmaxf(mx[1], m);
     }
 #pragma unroll
     for (int b = 0; b < kQMaxBatch; ++b)
@@ -369,37 +386,34 @@ __global__ void __launch_bounds__(kQThreads, 1) gemvq_kernel(const GemvQArgs a) 
     }
     if (tid < kQMaxBatch) ss->ex[tid] = ex[tid];
     const uint32_t colb = static_cast<uint32_t>(xsq_col_bytes(a.KT));
-    for (int c = tid; c < total; c += kQConsumerThreads) {
-      const int b = c / per_row, k = (c - b * per_row) * 8;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (a.x_vec16) {
-        if (k < a.K) v = __ldcg(reinterpret_cast<const uint4*>(a.x + b * a.ldx + k));
-      } else {
-        uint16_t h[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e)
-          h[e] = (k + e < a.K) ? __ldcg(reinterpret_cast<const unsigned short*>(a.x + b * a.ldx + k + e)) : 0;
-        v = make_uint4(h[0] | (uint32_t(h[1]) << 16), h[2] | (uint32_t(h[3]) << 16), h[4] | (uint32_t(h[5]) << 16),
-                       h[6] | (uint32_t(h[7]) << 16));
-      }
-      const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
-      const int e = b == 0 ? ex[0] : ex[1];
-      uint32_t d[3][2] = {{0, 0}, {0, 0}, {0, 0}};
+    for (int base = tid; base < total; base += 8 * kQConsumerThreads) {
+      uint4 v[8];
+      load8(base, v);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const __half hv = __ushort_as_half(static_cast<unsigned short>((wv[i >> 1] >> (16 * (i & 1))) & 0xffffu));
-        const int n = __float2int_rn(ldexpf(__half2float(hv), e));
-        const int d2 = ((n + 128) & 255) - 128;
-        const int n1 = (n - d2) >> 8;
-        const int d1 = ((n1 + 128) & 255) - 128;
-        const int d0 = (n1 - d1) >> 8;
-        d[0][i >> 2] |= (static_cast<uint32_t>(d0) & 0xffu) << (8 * (i & 3));
-        d[1][i >> 2] |= (static_cast<uint32_t>(d1) & 0xffu) << (8 * (i & 3));
-        d[2][i >> 2] |= (static_cast<uint32_t>(d2) & 0xffu) << (8 * (i & 3));
-      }
-      const uint32_t pos = static_cast<uint32_t>((k >> 7) * 128 + xs_pos8(k & 127));
+        const int c = base + i * kQConsumerThreads;
+        if (c < total) {
+          const int b = c / per_row, k = (c - b * per_row) * 8;
+          const uint32_t wv[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+          const float sc = __int_as_float((127 + (b == 0 ? ex[0] : ex[1])) << 23);  // exact 2^e
+          uint32_t d[3][2] = {{0, 0}, {0, 0}, {0, 0}};
 #pragma unroll
-      for (int dd = 0; dd < 3; ++dd) sts64(xs_base + (3 * b + dd) * colb + pos, d[dd][0], d[dd][1]);
+          for (int t = 0; t < 8; ++t) {
+            const __half hv = __ushort_as_half(static_cast<unsigned short>((wv[t >> 1] >> (16 * (t & 1))) & 0xffffu));
+            const int n = __float2int_rn(__half2float(hv) * sc);
+            const int d2 = ((n + 128) & 255) - 128;
+            const int n1 = (n - d2) >> 8;
+            const int d1 = ((n1 + 128) & 255) - 128;
+            const int d0 = (n1 - d1) >> 8;
+            d[0][t >> 2] |= (static_cast<uint32_t>(d0) & 0xffu) << (8 * (t & 3));
+            d[1][t >> 2] |= (static_cast<uint32_t>(d1) & 0xffu) << (8 * (t & 3));
+            d[2][t >> 2] |= (static_cast<uint32_t>(d2) & 0xffu) << (8 * (t & 3));
+          }
+          const uint32_t pos = static_cast<uint32_t>((k >> 7) * 128 + xs_pos8(k & 127));
+#pragma unroll
+          for (int dd = 0; dd < 3; ++dd) sts64(xs_base + (3 * b + dd) * colb + pos, d[dd][0], d[dd][1]);
+        }
+      }
     }
   }
   named_barrier(1, kQConsumerThreads);  // x staged, exponents published

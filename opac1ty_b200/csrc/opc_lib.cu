@@ -742,12 +742,13 @@ int opc_gemm(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ld
 // ---------------------------------------------------------------------------------------------
 struct opc_chain {
   int device = 0;
-  int32_t n_layers = 0, batch = 1, stages = 2, xs_bytes = 0, grid = 0;
+  int32_t n_layers = 0, batch = 1, stages = 2, xs_bytes = 0, grid = 0, xc = 8;
   size_t smem = 0;
   void* dev_mem = nullptr;          // [layers | sync | acc]
   opc::ChainLayer* d_layers = nullptr;
   unsigned int* d_sync = nullptr;
   size_t clear_bytes = 0;           // sync + acc, cleared before every launch
+  unsigned long long* trace = nullptr;  // optional per-phase timestamps (caller-owned)
 };
 
 extern "C" {
@@ -765,6 +766,7 @@ int opc_chain_create(const opc_chain_step* steps, int32_t n_steps, int32_t batch
   if (rc != OPC_OK) return rc;
   std::vector<opc::ChainLayer> hl(n_steps);
   int32_t kt_max = 1;
+  int64_t bk_max = 0;
   size_t acc_bytes = 0;
   std::vector<size_t> acc_off(n_steps);
   for (int j = 0; j < n_steps; ++j) {
@@ -784,9 +786,9 @@ int opc_chain_create(const opc_chain_step* steps, int32_t n_steps, int32_t batch
                     "opc_chain_create: step %d: x must be the previous step's y (same pointer and leading "
                     "dimension, K <= previous M)", j);
     }
-    if (static_cast<int64_t>(batch) * p.K_pad > 32768)
-      return fail(OPC_ERR_UNSUPPORTED, "opc_chain_create: step %d: batch*K_pad = %lld > 32768", j,
-                  static_cast<long long>(batch) * p.K_pad);
+    if (static_cast<int64_t>(batch) * p.K_pad > 64 * opc::kQConsumerThreads)
+      return fail(OPC_ERR_UNSUPPORTED, "opc_chain_create: step %d: batch*K_pad = %lld > %d", j,
+                  static_cast<long long>(batch) * p.K_pad, 64 * opc::kQConsumerThreads);
     if (p.total_units >= (int64_t(1) << 31)) return fail(OPC_ERR_UNSUPPORTED, "opc_chain_create: layer too large");
     opc::ChainLayer& c = hl[j];
     memset(&c, 0, sizeof(c));
@@ -811,6 +813,7 @@ int opc_chain_create(const opc_chain_step* steps, int32_t n_steps, int32_t batch
     c.KO = p.outlier_k_units;
     c.x_vec16 = (p.K % 8 == 0) && (st.ldx % 8 == 0) && aligned(st.x, 16);
     kt_max = std::max(kt_max, p.k_units);
+    bk_max = std::max<int64_t>(bk_max, static_cast<int64_t>(batch) * p.K_pad);
     acc_off[j] = acc_bytes;
     acc_bytes += align_up(static_cast<size_t>(n_slots_of(p)) * opc::kQMaxBatch * sizeof(unsigned long long), 256);
   }
@@ -823,15 +826,20 @@ int opc_chain_create(const opc_chain_step* steps, int32_t n_steps, int32_t batch
   while (stages >= 2 && smem_for(stages) > static_cast<size_t>(dc.max_smem_optin)) --stages;
   if (stages < 2) return fail(OPC_ERR_UNSUPPORTED, "opc_chain_create: staged x too large for shared memory");
   const size_t smem = smem_for(stages);
-  OPC_CUDA(cudaFuncSetAttribute(opc::chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)),
+  const int xc = bk_max <= 4 * 8 * opc::kQConsumerThreads ? 4 : 8;
+  auto kern = xc == 4 ? opc::chain_kernel<4> : opc::chain_kernel<8>;
+  OPC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)),
            "cudaFuncSetAttribute(max dynamic smem, chain)");
   int per_sm = 0;
-  OPC_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, opc::chain_kernel, opc::kQThreads, smem),
+  OPC_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, opc::kQThreads, smem),
            "cudaOccupancyMaxActiveBlocksPerMultiprocessor(chain)");
   if (per_sm < 1) return fail(OPC_ERR_UNSUPPORTED, "opc_chain_create: chain kernel does not fit on an SM");
+  if (dc.sm_count > opc::kQConsumerThreads)
+    return fail(OPC_ERR_UNSUPPORTED, "opc_chain_create: %d SMs exceed the barrier's %d pollers", dc.sm_count,
+                opc::kQConsumerThreads);
 
   const size_t layers_bytes = align_up(sizeof(opc::ChainLayer) * n_steps, 256);
-  const size_t sync_bytes = 256;
+  const size_t sync_bytes = align_up(static_cast<size_t>(dc.sm_count) * sizeof(unsigned int), 256);
   opc_chain* ch = new opc_chain();
   ch->device = dev;
   ch->n_layers = n_steps;
@@ -840,6 +848,7 @@ int opc_chain_create(const opc_chain_step* steps, int32_t n_steps, int32_t batch
   ch->xs_bytes = xs;
   ch->smem = smem;
   ch->grid = dc.sm_count;
+  ch->xc = xc;
   ch->clear_bytes = sync_bytes + acc_bytes;
   cudaError_t e = cudaMalloc(&ch->dev_mem, layers_bytes + sync_bytes + acc_bytes);
   if (e != cudaSuccess) {
@@ -873,6 +882,7 @@ int opc_chain_launch(opc_chain* ch, void* stream_v) {
   memset(&a, 0, sizeof(a));
   a.layers = ch->d_layers;
   a.sync = ch->d_sync;
+  a.trace = ch->trace;
   a.n_layers = ch->n_layers;
   a.batch = ch->batch;
   a.stages = ch->stages;
@@ -888,7 +898,25 @@ int opc_chain_launch(opc_chain* ch, void* stream_v) {
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  OPC_CUDA(cudaLaunchKernelEx(&cfg, opc::chain_kernel, a), "launch chain_kernel");
+  if (ch->xc == 4) {
+    OPC_CUDA(cudaLaunchKernelEx(&cfg, opc::chain_kernel<4>, a), "launch chain_kernel");
+  } else {
+    OPC_CUDA(cudaLaunchKernelEx(&cfg, opc::chain_kernel<8>, a), "launch chain_kernel");
+  }
+  return OPC_OK;
+}
+
+size_t opc_chain_trace_bytes(const opc_chain* ch) {
+  if (!ch) return 0;
+  return static_cast<size_t>(ch->n_layers) * ch->grid * opc::kChainTracePhases * sizeof(unsigned long long);
+}
+
+int32_t opc_chain_grid(const opc_chain* ch) { return ch ? ch->grid : 0; }
+
+int opc_chain_set_trace(opc_chain* ch, void* trace) {
+  if (!ch) return fail(OPC_ERR_INVALID, "opc_chain_set_trace: chain is NULL");
+  if (trace && !aligned(trace, 8)) return fail(OPC_ERR_INVALID, "opc_chain_set_trace: buffer not 8-byte aligned");
+  ch->trace = static_cast<unsigned long long*>(trace);
   return OPC_OK;
 }
 

@@ -9,8 +9,10 @@ One decode step runs, for every decoder block, the projection chain the benchmar
 
 Attention, norms, RoPE, the activation and residual adds are outside the measured path (they
 are not part of opacc1ty's fused dequant path).  Each launch depends on the previous one, so a
-step is 4 dependent kernels per block; the chain is captured once into a CUDA graph and every
-launch carries the programmatic-dependent-launch attribute, so each GEMV starts streaming its
+step is 4 dependent GEMVs per block.  At batch 1..2 the whole step runs as ONE persistent
+kernel (``opac1ty_b200.chain``: weights of every GEMV streamed without pause, a grid barrier
+between dependent GEMVs); otherwise every GEMV is its own launch, captured once into a CUDA
+graph, each carrying the programmatic-dependent-launch attribute so it starts streaming its
 weights while its predecessor finishes.
 
 ``concat_rows`` builds the fused layers from per-projection reference layer dicts (codebooks,
@@ -78,10 +80,12 @@ class DecodeStack:
     batch: int = 1
     graph: Optional[torch.cuda.CUDAGraph] = None
     bufs: Dict[str, torch.Tensor] = field(default_factory=dict)
+    use_chain: bool = True
+    chain: object = None
 
     @classmethod
     def from_block_dicts(cls, block_dicts: Sequence[Dict[str, dict]], hidden: int, intermediate: int, kv: int,
-                         device, batch: int = 1) -> "DecodeStack":
+                         device, batch: int = 1, use_chain: bool = True) -> "DecodeStack":
         device = L._as_cuda_device(device)
         blocks = []
         for bd in block_dicts:
@@ -90,13 +94,13 @@ class DecodeStack:
             gu = L.prepare_layer(concat_rows([bd["gate_proj"], bd["up_proj"]]), device, "gate_up")
             down = L.prepare_layer(bd["down_proj"], device, "down_proj")
             blocks.append(Block(qkv, o, gu, down))
-        st = cls(blocks, hidden, intermediate, kv, device, batch)
+        st = cls(blocks, hidden, intermediate, kv, device, batch, use_chain=use_chain)
         st._alloc()
         return st
 
     @classmethod
     def synthetic(cls, cfg: dict, n_layers: Optional[int] = None, device=None, batch: int = 1,
-                  outlier_fraction: float = 0.01, seed: int = 0) -> "DecodeStack":
+                  outlier_fraction: float = 0.01, seed: int = 0, use_chain: bool = True) -> "DecodeStack":
         """Random-initialised 2-bit weights with the given model shapes (synthetic.random_layer)."""
         shapes = synthetic.decoder_shapes(cfg)
         n_layers = cfg["layers"] if n_layers is None else n_layers
@@ -113,7 +117,7 @@ class DecodeStack:
             down = L.prepare_layer(bd["down_proj"], device, "down_proj")
             del bd
             blocks.append(Block(qkv, o, gu, down))
-        st = cls(blocks, cfg["hidden"], cfg["intermediate"], cfg["kv"], device, batch)
+        st = cls(blocks, cfg["hidden"], cfg["intermediate"], cfg["kv"], device, batch, use_chain=use_chain)
         st._alloc()
         return st
 
@@ -128,6 +132,16 @@ class DecodeStack:
         }
         need = max(L.workspace_bytes(dl, B) for b in self.blocks for dl in b.layers())
         self.workspace = torch.zeros(need, dtype=torch.uint8, device=dev)
+        self.chain = None
+        if self.use_chain and B <= 2:
+            from .chain import Chain
+
+            steps = []
+            b = self.bufs
+            for blk in self.blocks:
+                steps += [(blk.qkv, b["x"], b["qkv"]), (blk.o, b["qkv"], b["o"]),
+                          (blk.gate_up, b["o"], b["gu"]), (blk.down, b["gu"], b["x"])]
+            self.chain = Chain(steps)
 
     def layers(self) -> List[L.DeviceLayer]:
         return [dl for b in self.blocks for dl in b.layers()]
@@ -136,10 +150,17 @@ class DecodeStack:
         return sum(dl.algorithmic_bytes(self.batch) for dl in self.layers())
 
     def launches_per_step(self) -> int:
-        return 4 * len(self.blocks)
+        return 1 if self.chain is not None else 4 * len(self.blocks)
 
     def step_eager(self):
         """One decode step on the current stream; input and output in bufs["x"]."""
+        if self.chain is not None:
+            self.chain.launch()
+            return self.bufs["x"]
+        return self.step_launches()
+
+    def step_launches(self):
+        """The same step as one GEMV launch per projection."""
         b = self.bufs
         h, f = self.hidden, self.intermediate
         ws = self.workspace
