@@ -21,6 +21,7 @@ OPC_ERR_UNSUPPORTED = -2
 OPC_ERR_CUDA = -3
 OPC_ERR_WORKSPACE = -4
 OPC_ERR_DEVICE = -5
+OPC_CHAIN_L2_PREFETCH = 1
 
 _ERR_NAMES = {
     OPC_ERR_INVALID: "OPC_ERR_INVALID",
@@ -126,6 +127,7 @@ PROTOTYPES = {
     "opc_chain_trace_bytes": (_c.c_size_t, [_c.c_void_p]),
     "opc_chain_grid": (_c.c_int32, [_c.c_void_p]),
     "opc_chain_set_trace": (_c.c_int, [_c.c_void_p, _c.c_void_p]),
+    "opc_chain_set_option": (_c.c_int, [_c.c_void_p, _c.c_int32, _c.c_int32]),
     "opc_dequant": (_c.c_int, [_c.POINTER(Layer), _c.c_void_p, _c.c_int64, _c.c_void_p]),
     "opc_take_device_error": (_c.c_int, [_c.c_int32, _c.POINTER(_c.c_int32)]),
 }

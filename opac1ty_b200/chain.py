@@ -68,6 +68,9 @@ class Chain:
         _lib.check(_lib.load().opc_chain_set_trace(self._handle, None))
         self._trace = None
 
+    def set_l2_prefetch(self, on: bool):
+        _lib.check(_lib.load().opc_chain_set_option(self._handle, _lib.OPC_CHAIN_L2_PREFETCH, int(bool(on))))
+
     def close(self):
         if getattr(self, "_handle", None) and self._handle.value:
             with torch.cuda.device(self.device):

@@ -42,10 +42,11 @@ struct ChainArgs {
   unsigned int* sync;        // [grid] per-CTA "layers finished" flags (zero at launch)
   unsigned long long* trace; // optional [n_layers][grid][8] globaltimer stamps (ns) per CTA,
                              // taken by its first consumer thread: input ready, own x loads
-                             // done, exponents known, x staged, own units done, all units
-                             // done, writes fenced, flag published
+                             // done, exponents known, x staged, own units done, own writes
+                             // fenced, CTA's writes fenced, flag published
   int32_t n_layers, batch, stages, xs_bytes;
   uint32_t negz;
+  int32_t l2_prefetch;       // prefetch each consumer's share of the next layer into L2
 };
 constexpr int kChainTracePhases = 8;
 
@@ -73,6 +74,9 @@ __device__ __forceinline__ ChainPart chain_part(const ChainLayer& L, int c, int 
     wo = wo < 1 ? 1 : (wo > kQConsumers - 1 ? kQConsumers - 1 : wo);
     p.wp = kQConsumers - wo;
   }
+  // Every packed warp gets at least one unit, so the warps sharing a tile are exactly the parts
+  // between the parts of its first and last unit (the split-tile contributor count relies on it).
+  if (p.wp > np) p.wp = np;
   return p;
 }
 __device__ __forceinline__ void chain_warp_range(const ChainPart& p, int w, int32_t* u0, int32_t* u1) {
@@ -117,6 +121,7 @@ __device__ __forceinline__ void chain_next_segment(const ChainLayer& L, ChainCur
   c.end = c.begin + (c.seg < L.MT ? L.KT : L.KO);
 }
 
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 __device__ __forceinline__ uint32_t ld_acquire_u32(const unsigned int* p) {
   uint32_t v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -133,12 +138,22 @@ __device__ __forceinline__ void st_release_u32(unsigned int* p, uint32_t v) {
   asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 // One warp polls all G flags (lane l: flags l, l+32, ...) until every one reaches target.
+__device__ __forceinline__ uint32_t ld_relaxed_u32(const unsigned int* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Each lane reads its flags with independent relaxed loads (all in flight together); once every
+// flag has reached target an acquire fence orders the caller's later reads after them.
 __device__ __forceinline__ bool poll_flags_warp(const unsigned int* flags, int G, int lane, uint32_t target) {
   uint64_t t0 = 0;
   for (;;) {
-    bool mine = true;
-    for (int t = lane; t < G; t += 32) mine = mine && (ld_acquire_u32(flags + t) >= target);
-    if (__all_sync(0xffffffffu, mine)) return true;
+    uint32_t lo = 0xffffffffu;
+    for (int t = lane; t < G; t += 32) lo = min(lo, ld_relaxed_u32(flags + t));
+    if (__all_sync(0xffffffffu, lo >= target)) {
+      fence_acq_rel_gpu();
+      return true;
+    }
     const uint64_t now = globaltimer_ns();
     if (t0 == 0) t0 = now;
     else if (now - t0 > kWaitLimitNs) return false;
@@ -164,36 +179,47 @@ __device__ __forceinline__ __half prev_outlier_value(const PrevInfo& P, int s, i
   return scale_to_half(t, __ldg(P.oexp + s) + ex);
 }
 
+constexpr int kChainSplitSlots = 32;  // packed tiles per CTA and layer (host-checked)
+
 struct ChainShared {
-  SmemSlotsQ slots;
-  int32_t patch_row[kChainPatchMax];      // previous layer's outlier rows by slot (sorted)
+  float amax[kQConsumers][kQMaxBatch];    // staging: per-warp max |x|
+  unsigned long long tile_acc[kChainSplitSlots][kTileRows][kQMaxBatch];  // split packed tiles
+  int32_t tile_cnt[kChainSplitSlots];
+  int32_t patch_row[kChainPatchMax];      // previous layer's outlier rows by slot
   int32_t patch_exp[kChainPatchMax];      // and their integer-row exponents
   uint16_t patch_val[kChainPatchMax][kQMaxBatch];
   uint16_t prev_mask[kChainMaskMax];      // previous layer's tile masks of the rows x reads
   int32_t abort;
 };
 
-// Sum packed segment S over the packed warps [0, wp) of this CTA (ranges over [c0, c1)) and
-// write its rows (the segment always lies inside [c0, c1)).  The reducing warp is the first one
-// touching S, for which S is its last segment, so `m` is the meta it already holds.
-__device__ void chain_reduce_packed(const GemvQArgs& qa, SmemSlotsQ* ss, int32_t sbegin, int32_t send, const MetaQ& m,
-                                    int32_t c0, int32_t c1, int wp, int lane, int q, const int32_t* ex) {
-  const int32_t n = c1 - c0;
-  const int32_t lo = sbegin > c0 ? sbegin : c0;
-  const int32_t hi = (send < c1 ? send : c1) - 1;
-  const int wa = partq_of(lo - c0, n, wp), wb = partq_of(hi - c0, n, wp);
-  long long tot[2] = {0, 0};
-  for (int w = wa; w <= wb; ++w) {
-    const int32_t ws = c0 + partq_start(w, n, wp), we = c0 + partq_start(w + 1, n, wp);
-    if (we <= ws) continue;
-    const int sl = (ws >= sbegin) ? 0 : 1;
-    tot[0] += ss->v[w][sl][lane][0];
-    tot[1] += ss->v[w][sl][lane][1];
+// A warp's partial dot products of packed tile `seg` (this CTA's local tile lt), shared with
+// other warps of the CTA: added exactly into the tile's shared int64 accumulators; the warp that
+// completes the count of contributors writes the tile's rows and clears the slot.
+__device__ void chain_split_add(ChainShared* sh, const GemvQArgs& qa, const MetaQ& m, const long long t[2], int lt,
+                                int n_contrib, int lane, int g, int q, int ex0, int ex1) {
+  const int slot = lt & (kChainSplitSlots - 1);
+  const int b = q >> 1;
+  const bool live = !(q & 1) && b < qa.batch;
+  if (live) {
+    atomicAdd(&sh->tile_acc[slot][g][b], static_cast<unsigned long long>(t[0]));
+    atomicAdd(&sh->tile_acc[slot][g + 8][b], static_cast<unsigned long long>(t[1]));
   }
-  write_outq(qa, m, tot, q, ex);
+  __threadfence_block();
+  __syncwarp();
+  int old = 0;
+  if (lane == 0) old = atomicAdd(&sh->tile_cnt[slot], 1);
+  old = __shfl_sync(0xffffffffu, old, 0);
+  if (old != n_contrib - 1) return;
+  __threadfence_block();
+  long long fin[2] = {0, 0};
+  if (live) {
+    fin[0] = static_cast<long long>(atomicExch(&sh->tile_acc[slot][g][b], 0ull));
+    fin[1] = static_cast<long long>(atomicExch(&sh->tile_acc[slot][g + 8][b], 0ull));
+  }
+  if (lane == 0) sh->tile_cnt[slot] = 0;
+  write_outq(qa, m, fin, q, ex0, ex1);
 }
 
-// kXC: x chunks (8 halves) staged per consumer thread, i.e. batch * K_pad <= kXC * 8 * 480.
 template <int kXC>
 __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs args) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -208,7 +234,6 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
   const uint32_t full_base = ring_base + kQConsumers * S * kQChunkBytes;
   const uint32_t empty_base = full_base + kQConsumers * S * 8;
   ChainShared* sh = reinterpret_cast<ChainShared*>(smem + args.xs_bytes + kQConsumers * S * (kQChunkBytes + 16));
-  SmemSlotsQ* ss = &sh->slots;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kQConsumers * S; ++i) {
@@ -218,6 +243,9 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     fence_mbar_init();
     sh->abort = 0;
   }
+  for (int i = threadIdx.x; i < kChainSplitSlots * kTileRows * kQMaxBatch; i += blockDim.x)
+    (&sh->tile_acc[0][0][0])[i] = 0ull;
+  for (int i = threadIdx.x; i < kChainSplitSlots; i += blockDim.x) sh->tile_cnt[i] = 0;
   __syncthreads();
 
   // ------------------------------------------------------------------ producer warp
@@ -230,6 +258,26 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     const ChainLayer* Lp = nullptr;
     bool active = i < kQConsumers;
     // advance to the first layer with a non-empty range for this consumer
+    const uint64_t evict_first = l2_policy_evict_first();
+    // When this lane starts layer j, its consumer's share of layer j+1 is prefetched into L2, so
+    // HBM streams the next layer during this one's compute and its ring refills hit L2.
+    auto prefetch_next = [&](int jn) {
+      if (!args.l2_prefetch || jn >= args.n_layers) return;
+      const ChainLayer N = args.layers[jn];
+      const ChainPart p = chain_part(N, cta, G);
+      int32_t a0, a1;
+      chain_warp_range(p, i, &a0, &a1);
+      if (a0 >= a1) return;
+      const uint8_t* src = a0 < N.Up ? N.units + static_cast<int64_t>(a0) * kUnitBytes
+                                     : N.ounits + static_cast<int64_t>(a0 - N.Up) * kUnitBytes;
+      int64_t bytes = static_cast<int64_t>(a1 - a0) * kUnitBytes;
+      while (bytes > 0) {
+        const uint32_t n = bytes > 65536 ? 65536u : static_cast<uint32_t>(bytes);
+        l2_prefetch_bulk(src, n);
+        src += n;
+        bytes -= n;
+      }
+    };
     auto next_range = [&]() {
       while (j < args.n_layers) {
         Lp = args.layers + j;
@@ -237,6 +285,7 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
         const ChainPart p = chain_part(L, cta, G);
         int32_t u0;
         chain_warp_range(p, i, &u0, &u1);
+        prefetch_next(j + 1);
         if (u0 < u1) {
           pc = chain_cursor(L, u0);
           return true;
@@ -261,7 +310,10 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
           const int32_t Up = Lp->Up;
           const uint8_t* src = pc.u < Up ? Lp->units + static_cast<int64_t>(pc.u) * kUnitBytes
                                          : Lp->ounits + static_cast<int64_t>(pc.u - Up) * kUnitBytes;
-          bulk_g2s(ring + slot * kQChunkBytes, src, static_cast<uint32_t>(cnt * kUnitBytes), bar);
+          if (args.l2_prefetch)
+            bulk_g2s_hint(ring + slot * kQChunkBytes, src, static_cast<uint32_t>(cnt * kUnitBytes), bar, evict_first);
+          else
+            bulk_g2s(ring + slot * kQChunkBytes, src, static_cast<uint32_t>(cnt * kUnitBytes), bar);
           pc.u += cnt;
           if (pc.u == pc.end && pc.u < u1) {
             const ChainLayer L = *Lp;
@@ -314,8 +366,6 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     const ChainPart part = chain_part(L, cta, G);
     int32_t u0, u1;
     chain_warp_range(part, warp, &u0, &u1);
-    const bool packed_warp = warp < part.wp;
-    if (tid < kQConsumers * 2) ss->seg[tid >> 1][tid & 1] = -1;
     ChainCursor cc = chain_cursor(L, u0 < u1 ? u0 : 0);
     MetaQ cur, nxt;
     if (u0 < u1) {
@@ -340,8 +390,7 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     if (j > 0) {
       if (mask_in_smem)
         for (int t = tid; t < (L.K + 15) / 16; t += kQConsumerThreads) sh->prev_mask[t] = __ldg(P.tile_mask + t);
-      if (P.n_slots <= kChainPatchMax)
-        for (int s = tid; s < P.n_slots; s += kQConsumerThreads) {
+      for (int s = tid; s < P.n_slots && s < kChainPatchMax; s += kQConsumerThreads) {
           sh->patch_row[s] = __ldg(P.orow + s);
           sh->patch_exp[s] = __ldg(P.oexp + s);
         }
@@ -354,7 +403,7 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
           atomicCAS(&g_opc_device_error, 0, kDevErrTmaTimeout);
         }
       }
-      __threadfence();
+      fence_acq_rel_gpu();
       named_barrier(1, kQConsumerThreads);
       if (sh->abort) {
         ok = false;
@@ -369,12 +418,11 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     // this thread's x chunks with the previous layer's outlier flags of their rows, and (slot
     // threads) the previous layer's outlier values.  Outlier rows of y_{j-1} are read from the
     // slot accumulators, never from y, and published through a shared patch table sorted by row.
-    int32_t ex[kQMaxBatch] = {0, 0};
+    int ex0 = 0, ex1 = 0;  // x exponents of batch rows 0, 1 (scalars: no local memory)
     {
       const int per_row = L.K_pad / 8;
       const int total = B * per_row;
       const int n_pslots = has_prev ? P.n_slots : 0;
-      const bool patch_in_smem = n_pslots <= kChainPatchMax;
       uint4 v[kXC];
       uint32_t tmw[kXC];
 #pragma unroll
@@ -387,7 +435,7 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
           if (k < L.K) {
             const __half* src = L.x + b * L.ldx + k;
             if (L.x_vec16) {
-              v[i] = __ldcg(reinterpret_cast<const uint4*>(src));
+              v[i] = ld_cg_v4(src);
             } else {
               uint16_t h[8];
 #pragma unroll
@@ -408,8 +456,8 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
       float mx[kQMaxBatch] = {0.f, 0.f};
       // slot threads: the previous layer's outlier values (y rows owned by this CTA written here)
       for (int s = tid; s < n_pslots; s += kQConsumerThreads) {
-        const int row = patch_in_smem ? sh->patch_row[s] : __ldg(P.orow + s);
-        const int e0 = patch_in_smem ? sh->patch_exp[s] : __ldg(P.oexp + s);
+        const int row = s < kChainPatchMax ? sh->patch_row[s] : __ldg(P.orow + s);
+        const int e0 = s < kChainPatchMax ? sh->patch_exp[s] : __ldg(P.oexp + s);
         const long long t0 = static_cast<long long>(__ldcg(P.acc + 2 * s));
         const long long t1 = B > 1 ? static_cast<long long>(__ldcg(P.acc + 2 * s + 1)) : 0ll;
         const __half h0 = scale_to_half(t0, e0 + ex_prev[0]);
@@ -418,8 +466,8 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
           P.y[row] = h0;
           if (B > 1) P.y[P.ldy + row] = h1;
         }
-        if (patch_in_smem) {
-          if (row < 0) sh->patch_row[s] = 0x7fffffff;  // padding slots sort last
+        if (s < kChainPatchMax) {
+          sh->patch_row[s] = row;
           sh->patch_val[s][0] = __half_as_ushort(h0);
           sh->patch_val[s][1] = __half_as_ushort(h1);
         }
@@ -450,22 +498,20 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
       for (int b = 0; b < kQMaxBatch; ++b)
         for (int o = 16; o > 0; o >>= 1) mx[b] = fmaxf(mx[b], __shfl_xor_sync(0xffffffffu, mx[b], o));
       if (lane == 0) {
-        ss->amax[warp][0] = mx[0];
-        ss->amax[warp][1] = mx[1];
+        sh->amax[warp][0] = mx[0];
+        sh->amax[warp][1] = mx[1];
       }
       if (tid < 8) sts128(xs_base + args.xs_bytes - kQZeroBytes + tid * 16, make_uint4(0, 0, 0, 0));
       named_barrier(1, kQConsumerThreads);
       if (tr && tid == 0) tr[2] = globaltimer_ns();
-#pragma unroll
-      for (int b = 0; b < kQMaxBatch; ++b) {
-        float m = 0.f;
-        for (int w = 0; w < kQConsumers; ++w) m = fmaxf(m, ss->amax[w][b]);
-        int e2 = 0;
-        if (m > 0.f) {
-          frexpf(m, &e2);
-          e2 = 22 - e2;
+      {
+        float m0 = 0.f, m1 = 0.f;
+        for (int w = 0; w < kQConsumers; ++w) {
+          m0 = fmaxf(m0, sh->amax[w][0]);
+          m1 = fmaxf(m1, sh->amax[w][1]);
         }
-        ex[b] = e2;
+        ex0 = m0 > 0.f ? 22 - frexp_exponent(m0) : 0;
+        ex1 = m1 > 0.f ? 22 - frexp_exponent(m1) : 0;
       }
       const uint32_t colb = static_cast<uint32_t>(xsq_col_bytes(L.KT));
 #pragma unroll
@@ -473,33 +519,13 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
         const int c = tid + i * kQConsumerThreads;
         if (c < total) {
           const int b = c / per_row, k = (c - b * per_row) * 8;
-          uint32_t wv[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
-          if (tmw[i]) {
-#pragma unroll
-            for (int e = 0; e < 8; ++e)
-              if ((tmw[i] >> e) & 1u) {
-                uint32_t hv;
-                if (patch_in_smem) {  // slots are in increasing row order: binary search
-                  int lo = 0, hi = n_pslots - 1;
-                  while (lo < hi) {
-                    const int mid = (lo + hi) >> 1;
-                    if (sh->patch_row[mid] < k + e) lo = mid + 1;
-                    else hi = mid;
-                  }
-                  hv = sh->patch_val[lo][b];
-                } else {
-                  const int sl = static_cast<int>(__ldg(P.cbq + k + e).w);
-                  hv = __half_as_ushort(prev_outlier_value(P, sl, b, b ? ex_prev[1] : ex_prev[0]));
-                }
-                wv[e >> 1] = (e & 1) ? ((wv[e >> 1] & 0xffffu) | (hv << 16)) : ((wv[e >> 1] & 0xffff0000u) | hv);
-              }
-          }
-          const float sc = pow2f(b == 0 ? ex[0] : ex[1]);
+          const uint32_t wv[4] = {v[i].x, v[i].y, v[i].z, v[i].w};  // outlier rows fixed below
+          const float sc = pow2f(b == 0 ? ex0 : ex1);
           uint32_t d[3][2] = {{0, 0}, {0, 0}, {0, 0}};
 #pragma unroll
           for (int t = 0; t < 8; ++t) {
             const __half hv = __ushort_as_half(static_cast<unsigned short>((wv[t >> 1] >> (16 * (t & 1))) & 0xffffu));
-            const int n = __float2int_rn(__half2float(hv) * sc);
+            const int n = round_small_int(__half2float(hv) * sc);
             const int d2 = ((n + 128) & 255) - 128;
             const int n1 = (n - d2) >> 8;
             const int d1 = ((n1 + 128) & 255) - 128;
@@ -513,6 +539,39 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
           for (int dd = 0; dd < 3; ++dd) sts64(xs_base + (3 * b + dd) * colb + pos, d[dd][0], d[dd][1]);
         }
       }
+      if (n_pslots > 0) {
+        // Outlier rows of the previous layer: one thread per slot overwrites its row's digits
+        // (the chunks above converted whatever y held there).
+        named_barrier(1, kQConsumerThreads);
+        for (int s = tid; s < n_pslots; s += kQConsumerThreads) {
+          int row;
+          uint32_t hv[kQMaxBatch];
+          if (s < kChainPatchMax) {
+            row = sh->patch_row[s];
+            hv[0] = sh->patch_val[s][0];
+            hv[1] = sh->patch_val[s][1];
+          } else {
+            row = __ldg(P.orow + s);
+            hv[0] = __half_as_ushort(prev_outlier_value(P, s, 0, ex_prev[0]));
+            hv[1] = B > 1 ? __half_as_ushort(prev_outlier_value(P, s, 1, ex_prev[1])) : 0u;
+          }
+          if (row < 0 || row >= L.K) continue;
+          const uint32_t pos = static_cast<uint32_t>((row >> 7) * 128 + xs_pos8(row & 127));
+#pragma unroll
+          for (int b = 0; b < kQMaxBatch; ++b) {
+            if (b >= B) break;
+            const int n = round_small_int(__half2float(__ushort_as_half(static_cast<unsigned short>(hv[b]))) *
+                                          pow2f(b ? ex1 : ex0));
+            const int d2 = ((n + 128) & 255) - 128;
+            const int n1 = (n - d2) >> 8;
+            const int d1 = ((n1 + 128) & 255) - 128;
+            const int d0 = (n1 - d1) >> 8;
+            sts8(xs_base + (3 * b + 0) * colb + pos, static_cast<uint32_t>(d0));
+            sts8(xs_base + (3 * b + 1) * colb + pos, static_cast<uint32_t>(d1));
+            sts8(xs_base + (3 * b + 2) * colb + pos, static_cast<uint32_t>(d2));
+          }
+        }
+      }
       named_barrier(1, kQConsumerThreads);
     }
     if (tr && tid == 0) tr[3] = globaltimer_ns();
@@ -524,6 +583,13 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     const uint32_t kts = live_col ? 128u : 0u;
     const uint32_t xq = colbase + 32 * q, xo = colbase + 4 * q;
 
+    // number of packed warps whose ranges share the tile starting at unit sb
+    const int32_t tile0 = part.pu0 / (L.KT > 0 ? L.KT : 1);
+    auto contrib = [&](int32_t sb) {
+      const int32_t n = part.pu1 - part.pu0;
+      const int32_t lo = sb - part.pu0, hi = sb + L.KT - 1 - part.pu0;
+      return partq_of(hi, n, part.wp) - partq_of(lo, n, part.wp) + 1;
+    };
     if (u0 < u1) {
       AccQ A;
       zero_accq(A);
@@ -591,8 +657,8 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
           } else {
             long long t[2];
             finish_dot(A, q, t);
-            if (cc.begin < u0) put_slotq(ss, warp, 0, lane, cc.seg, t);
-            else write_outq(qa, cur, t, q, ex);
+            if (cc.begin < u0) chain_split_add(sh, qa, cur, t, cc.seg - tile0, contrib(cc.begin), lane, g, q, ex0, ex1);
+            else write_outq(qa, cur, t, q, ex0, ex1);
           }
           zero_accq(A);
           chain_next_segment(L, cc);
@@ -606,8 +672,8 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
         } else {
           long long t[2];
           finish_dot(A, q, t);
-          if (cc.begin >= u0 && cc.end <= u1) write_outq(qa, cur, t, q, ex);
-          else put_slotq(ss, warp, cc.begin <= u0 ? 0 : 1, lane, cc.seg, t);
+          if (cc.begin >= u0 && cc.end <= u1) write_outq(qa, cur, t, q, ex0, ex1);
+          else chain_split_add(sh, qa, cur, t, cc.seg - tile0, contrib(cc.begin), lane, g, q, ex0, ex1);
         }
       } else {
         atomicCAS(&g_opc_device_error, 0, kDevErrTmaTimeout);
@@ -615,23 +681,8 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
       }
     }
     if (tr && tid == 0) tr[4] = globaltimer_ns();
-    named_barrier(1, kQConsumerThreads);  // partials of split packed tiles are in shared memory
+    fence_acq_rel_gpu();                  // this thread's writes of layer j are visible GPU-wide
     if (tr && tid == 0) tr[5] = globaltimer_ns();
-    if (ok && packed_warp && u0 < u1) {
-      const int32_t s0 = ss->seg[warp][0], s1 = ss->seg[warp][1];
-      const int32_t c0 = part.pu0, c1 = part.pu1;
-      if (s0 >= 0) {
-        const int32_t sb = s0 * L.KT, se = sb + L.KT;
-        const bool first_is_last = (se >= u1);
-        if ((sb < u0 && u0 == c0) || (first_is_last && sb >= u0))
-          chain_reduce_packed(qa, ss, sb, se, cur, c0, c1, part.wp, lane, q, ex);
-      }
-      if (s1 >= 0) {
-        const int32_t sb = s1 * L.KT, se = sb + L.KT;
-        if (sb >= u0 || u0 == c0) chain_reduce_packed(qa, ss, sb, se, cur, c0, c1, part.wp, lane, q, ex);
-      }
-    }
-    __threadfence();                      // this thread's writes of layer j are visible GPU-wide
     named_barrier(1, kQConsumerThreads);  // ... for every thread of the CTA
     if (sh->abort) ok = false;
     if (tid == 0) {
@@ -639,8 +690,8 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
       st_release_u32(args.sync + cta, static_cast<uint32_t>(j + 1));
       if (tr) tr[7] = globaltimer_ns();
     }
-    ex_prev[0] = ex[0];
-    ex_prev[1] = ex[1];
+    ex_prev[0] = ex0;
+    ex_prev[1] = ex1;
   }
 
   // ---- last layer's outlier rows, once every CTA has finished it

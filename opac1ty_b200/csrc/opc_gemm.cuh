@@ -4,10 +4,10 @@
 // Reference: kernels/dequant_gemm.metal:34-149 (dequantize a weight tile into threadgroup memory,
 // then a scalar multiply-accumulate); semantics opacc1ty/export/converter.py:26-67 + matmul.
 //
-// One CTA computes a 128-row x 256-token tile, K in stages of 64:
-//   warp 0      TMA: the X tile (256 tokens x 64 fp16, 128-byte swizzle) and the 8 packed units
+// One CTA computes a 128-row x N-token tile (N = 256, or 128 for small problems), K in stages of 64:
+//   warp 0      TMA: the X tile (N tokens x 64 fp16, 128-byte swizzle) and the 8 packed units
 //               of the tile's 8 row tiles (bulk copies, no multicast) into the stage
-//   warp 1      allocates 256 TMEM columns; one lane issues 4 tcgen05.mma (K = 16 each) per
+//   warp 1      allocates N TMEM columns; one lane issues 4 tcgen05.mma (K = 16 each) per
 //               stage and commits them to the stage's "empty" mbarrier
 //   warps 2..5  one weight row per thread: decode the row's 64 indices of the stage through its
 //               fp16 codebook (PRMT lookups) into the A tile, written in the canonical K-major
@@ -24,14 +24,17 @@
 
 namespace opc {
 
-constexpr int kGmM = 128, kGmN = 256, kGmK = 64;
+constexpr int kGmM = 128, kGmK = 64;          // weight rows per tile, K per stage
 constexpr int kGmStages = 4;
 constexpr int kGmThreads = 192;
 constexpr int kGmABytes = kGmM * kGmK * 2;   // 16 KB
-constexpr int kGmBBytes = kGmN * kGmK * 2;   // 32 KB
 constexpr int kGmUBytes = 8 * kUnitBytes;    // 8 row tiles x one unit
-constexpr int kGmTmemCols = 256;
-constexpr size_t kGmSmemBytes = 1024 /*alignment slack*/ + kGmStages * (kGmABytes + kGmBBytes + kGmUBytes) + 256;
+// Token tile N (256, or 128 when 256-token tiles would leave SMs idle): x stage N*64 fp16,
+// N fp32 TMEM columns.
+__host__ __device__ constexpr int gm_b_bytes(int N) { return N * kGmK * 2; }
+__host__ __device__ constexpr size_t gm_smem_bytes(int N) {
+  return 1024 /*alignment slack*/ + kGmStages * (kGmABytes + gm_b_bytes(N) + kGmUBytes) + 256;
+}
 
 struct GemmArgs {
   const uint8_t* units;        // packed units
@@ -48,8 +51,10 @@ struct GemmArgs {
 __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
   return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
 }
-// Instruction descriptor: kind::f16, A = B = fp16, D = fp32, both K-major, N = 256, M = 128.
-constexpr uint32_t kGmIdesc = (1u << 4) | (static_cast<uint32_t>(kGmN >> 3) << 17) | (static_cast<uint32_t>(kGmM >> 4) << 24);
+// Instruction descriptor: kind::f16, A = B = fp16, D = fp32, both K-major, M = 128, N tokens.
+__host__ __device__ constexpr uint32_t gm_idesc(int N) {
+  return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(kGmM >> 4) << 24);
+}
 
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int32_t x, int32_t y, uint32_t bar) {
   asm volatile(
@@ -101,8 +106,10 @@ __device__ __forceinline__ uint32_t sw128_off(int r, int c) {
   return static_cast<uint32_t>(1024 * (r >> 3) + 128 * (r & 7) + 16 * (c ^ (r & 7)));
 }
 
-template <bool kDense>
+template <bool kDense, int kN>
 __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap tx, const GemmArgs a) {
+  constexpr int kGmBBytes = gm_b_bytes(kN);
+  constexpr int kGmTmemCols = kN;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -114,7 +121,7 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_consta
 
   const int warp = __shfl_sync(0xffffffffu, static_cast<int>(threadIdx.x >> 5), 0);
   const int lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * kGmM, n0 = blockIdx.y * kGmN;
+  const int m0 = blockIdx.x * kGmM, n0 = blockIdx.y * kN;
   const int nk = a.K_pad / kGmK;
   const int t0 = m0 / kTileRows;
   const int n_rt = kDense ? 0 : min(8, a.MT - t0);  // row tiles with units in this M tile
@@ -172,7 +179,7 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_consta
         const uint64_t ad = umma_desc_sw128(sA + st * kGmABytes), bd = umma_desc_sw128(sB + st * kGmBBytes);
 #pragma unroll
         for (int kk = 0; kk < kGmK / 16; ++kk)  // +32 bytes per K = 16 step inside the swizzle atom
-          umma_f16(tmem, ad + 2 * kk, bd + 2 * kk, kGmIdesc, (s > 0 || kk > 0) ? 1u : 0u);
+          umma_f16(tmem, ad + 2 * kk, bd + 2 * kk, gm_idesc(kN), (s > 0 || kk > 0) ? 1u : 0u);
         umma_commit(empty_b + 8 * st);
       }
       if (ok) umma_commit(accf_b);
@@ -244,7 +251,7 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_consta
       tc_fence_after();
       const uint32_t trow = tmem + (static_cast<uint32_t>(32 * quarter) << 16);
 #pragma unroll 1
-      for (int cc = 0; cc < kGmN / 32; ++cc) {
+      for (int cc = 0; cc < kN / 32; ++cc) {
         uint32_t v[32];
         tmem_ld32(trow + cc * 32, v);
         if (out_row >= 0) {

@@ -106,8 +106,8 @@ __device__ __forceinline__ MetaQ load_metaq(const GemvQArgs& a, int32_t seg, int
   MetaQ m;
   if (seg < a.MT) {
     const int r0 = seg * kTileRows + g;
-    const uint4 c0 = __ldg(a.cbq + r0), c1 = __ldg(a.cbq + r0 + 8);
-    const uint32_t mask = __ldg(a.tile_mask + seg);
+    const uint4 c0 = ld_nc_v4(a.cbq + r0), c1 = ld_nc_v4(a.cbq + r0 + 8);
+    const uint32_t mask = ld_nc_u16(a.tile_mask + seg);
     m.qh[0] = c0.x; m.ql[0] = c0.y; m.e[0] = static_cast<int32_t>(c0.z);
     m.qh[1] = c1.x; m.ql[1] = c1.y; m.e[1] = static_cast<int32_t>(c1.z);
     m.row[0] = (r0 < a.M && !((mask >> g) & 1u)) ? r0 : -1;
@@ -115,10 +115,10 @@ __device__ __forceinline__ MetaQ load_metaq(const GemvQArgs& a, int32_t seg, int
   } else {
     const int s = (seg - a.MT) * kTileRows + g;
     m.qh[0] = m.qh[1] = m.ql[0] = m.ql[1] = 0u;
-    m.row[0] = __ldg(a.orow + s);
-    m.row[1] = __ldg(a.orow + s + 8);
-    m.e[0] = __ldg(a.oexp + s);
-    m.e[1] = __ldg(a.oexp + s + 8);
+    m.row[0] = static_cast<int32_t>(ld_nc_u32(a.orow + s));
+    m.row[1] = static_cast<int32_t>(ld_nc_u32(a.orow + s + 8));
+    m.e[0] = static_cast<int32_t>(ld_nc_u32(a.oexp + s));
+    m.e[1] = static_cast<int32_t>(ld_nc_u32(a.oexp + s + 8));
   }
   return m;
 }
@@ -168,13 +168,15 @@ struct SmemSlotsQ {
   float amax[kQConsumers][kQMaxBatch]; // staging reduction
 };
 
-__device__ __forceinline__ void write_outq(const GemvQArgs& a, const MetaQ& m, const long long t[2], int q,
-                                           const int32_t* ex) {
+// x exponents of batch rows 0 and 1 are passed as scalars (no array, so no local memory).
+__device__ __forceinline__ void write_outq(const GemvQArgs& a, const MetaQ& m, const long long t[2], int q, int ex0,
+                                           int ex1) {
   const int b = q >> 1;
   if ((q & 1) || b >= a.batch) return;
+  const int ex = b ? ex1 : ex0;
 #pragma unroll
   for (int r = 0; r < 2; ++r)
-    if (m.row[r] >= 0) a.y[b * a.ldy + m.row[r]] = scale_to_half(t[r], m.e[r] + ex[b]);
+    if (m.row[r] >= 0) a.y[b * a.ldy + m.row[r]] = scale_to_half(t[r], m.e[r] + ex);
 }
 
 __device__ __forceinline__ void put_slotq(SmemSlotsQ* ss, int warp, int sl, int lane, int32_t seg, const long long t[2]) {
@@ -201,7 +203,7 @@ __device__ void reduce_segmentq(const GemvQArgs& a, SmemSlotsQ* ss, SegQ S, int3
   }
   const MetaQ m = load_metaq(a, S.id, g);
   if (S.begin >= c0 && S.end <= c1) {
-    write_outq(a, m, tot, q, ss->ex);
+    write_outq(a, m, tot, q, ss->ex[0], ss->ex[1]);
     return;
   }
   const int b = q >> 1;
@@ -226,7 +228,7 @@ __device__ void reduce_segmentq(const GemvQArgs& a, SmemSlotsQ* ss, SegQ S, int3
     for (int r = 0; r < 2; ++r)
       if (m.row[r] >= 0)
         fin[r] = static_cast<long long>(atomicExch(a.acc + static_cast<int64_t>(m.row[r]) * 2 + b, 0ull));
-    write_outq(a, m, fin, q, ss->ex);
+    write_outq(a, m, fin, q, ss->ex[0], ss->ex[1]);
   }
   if (lane == 0) atomicExch(a.counters + S.id, 0);
 }
@@ -329,7 +331,7 @@ __global__ void __launch_bounds__(kQThreads, 1) gemvq_kernel(const GemvQArgs a) 
         if (c < total) {
           const int b = c / per_row, k = (c - b * per_row) * 8;
           if (a.x_vec16) {
-            if (k < a.K) v[i] = __ldcg(reinterpret_cast<const uint4*>(a.x + b * a.ldx + k));
+            if (k < a.K) v[i] = ld_cg_v4(a.x + b * a.ldx + k);
           } else {
             uint16_t h[8];
 #pragma unroll
@@ -371,20 +373,18 @@ __global__ void __launch_bounds__(kQThreads, 1) gemvq_kernel(const GemvQArgs a) 
     if (tid < 8)  // zero block (B operand of absent columns)
       sts128(xs_base + a.xs_bytes - kQZeroBytes + tid * 16, make_uint4(0, 0, 0, 0));
     named_barrier(1, kQConsumerThreads);
-    int ex[kQMaxBatch];
-#pragma unroll
-    for (int b = 0; b < kQMaxBatch; ++b) {
-      float m = 0.f;
-      for (int w = 0; w < kQConsumers; ++w) m = fmaxf(m, ss->amax[w][b]);
-      // m * 2^e in [2^21, 2^22): digits d0 in [-64, 64], d1, d2 in [-128, 127]
-      int e2 = 0;
-      if (m > 0.f) {
-        frexpf(m, &e2);
-        e2 = 22 - e2;
-      }
-      ex[b] = e2;
+    // m * 2^e in [2^21, 2^22): digits d0 in [-64, 64], d1, d2 in [-128, 127]
+    float m0 = 0.f, m1 = 0.f;
+    for (int w = 0; w < kQConsumers; ++w) {
+      m0 = fmaxf(m0, ss->amax[w][0]);
+      m1 = fmaxf(m1, ss->amax[w][1]);
     }
-    if (tid < kQMaxBatch) ss->ex[tid] = ex[tid];
+    const int ex0 = m0 > 0.f ? 22 - frexp_exponent(m0) : 0;
+    const int ex1 = m1 > 0.f ? 22 - frexp_exponent(m1) : 0;
+    if (tid == 0) {
+      ss->ex[0] = ex0;
+      ss->ex[1] = ex1;
+    }
     const uint32_t colb = static_cast<uint32_t>(xsq_col_bytes(a.KT));
     for (int base = tid; base < total; base += 8 * kQConsumerThreads) {
       uint4 v[8];
@@ -395,12 +395,12 @@ __global__ void __launch_bounds__(kQThreads, 1) gemvq_kernel(const GemvQArgs a) 
         if (c < total) {
           const int b = c / per_row, k = (c - b * per_row) * 8;
           const uint32_t wv[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
-          const float sc = __int_as_float((127 + (b == 0 ? ex[0] : ex[1])) << 23);  // exact 2^e
+          const float sc = __int_as_float((127 + (b == 0 ? ex0 : ex1)) << 23);  // exact 2^e
           uint32_t d[3][2] = {{0, 0}, {0, 0}, {0, 0}};
 #pragma unroll
           for (int t = 0; t < 8; ++t) {
             const __half hv = __ushort_as_half(static_cast<unsigned short>((wv[t >> 1] >> (16 * (t & 1))) & 0xffffu));
-            const int n = __float2int_rn(__half2float(hv) * sc);
+            const int n = round_small_int(__half2float(hv) * sc);
             const int d2 = ((n + 128) & 255) - 128;
             const int n1 = (n - d2) >> 8;
             const int d1 = ((n1 + 128) & 255) - 128;
@@ -492,7 +492,7 @@ __global__ void __launch_bounds__(kQThreads, 1) gemvq_kernel(const GemvQArgs a) 
         if (cc.begin < u0)
           put_slotq(ss, warp, 0, lane, cc.seg, t);
         else
-          write_outq(a, cur, t, q, ss->ex);
+          write_outq(a, cur, t, q, ss->ex[0], ss->ex[1]);
         zero_accq(A);
         nextq_segment(a, cc);
         cur = nxt;
@@ -503,7 +503,7 @@ __global__ void __launch_bounds__(kQThreads, 1) gemvq_kernel(const GemvQArgs a) 
       long long t[2];
       finish_dot(A, q, t);
       if (cc.begin >= u0 && cc.end <= u1)
-        write_outq(a, cur, t, q, ss->ex);
+        write_outq(a, cur, t, q, ss->ex[0], ss->ex[1]);
       else
         put_slotq(ss, warp, cc.begin <= u0 ? 0 : 1, lane, cc.seg, t);
     } else {

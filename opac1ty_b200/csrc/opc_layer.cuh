@@ -25,9 +25,7 @@ struct LayerGeom {
 // [-64, 64]).  e = 14 - (binary exponent of amax), so amax * 2^e lies in [2^13, 2^14).
 __device__ __forceinline__ int int_exponent(float amax) {
   if (!(amax > 0.f)) return 0;
-  int ex;
-  frexpf(amax, &ex);  // amax = f * 2^ex, f in [0.5, 1)
-  return 14 - ex;
+  return 14 - frexp_exponent(amax);  // amax comes from fp16 values: a normal float
 }
 __device__ __forceinline__ void int_parts(float v, int e, int* hi, int* lo) {
   const int n = __float2int_rn(ldexpf(v, e));

@@ -209,20 +209,20 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-template <bool kDense>
+template <bool kDense, int kN>
 int launch_gemm_t(const CUtensorMap& tx, const opc::GemmArgs& a, dim3 grid, cudaStream_t stream, int dev) {
   static std::mutex mu;
   static std::map<int, bool> configured;
   {
     std::lock_guard<std::mutex> lk(mu);
     if (!configured[dev]) {
-      OPC_CUDA(cudaFuncSetAttribute(opc::gemm_kernel<kDense>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(opc::kGmSmemBytes)),
+      OPC_CUDA(cudaFuncSetAttribute(opc::gemm_kernel<kDense, kN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(opc::gm_smem_bytes(kN))),
                "cudaFuncSetAttribute(max dynamic smem, gemm)");
       configured[dev] = true;
     }
   }
-  opc::gemm_kernel<kDense><<<grid, opc::kGmThreads, opc::kGmSmemBytes, stream>>>(tx, a);
+  opc::gemm_kernel<kDense, kN><<<grid, opc::kGmThreads, opc::gm_smem_bytes(kN), stream>>>(tx, a);
   OPC_CUDA(cudaGetLastError(), "launch gemm_kernel");
   return OPC_OK;
 }
@@ -691,7 +691,7 @@ int opc_gemm(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ld
   if (!aligned(y, 2)) return fail(OPC_ERR_INVALID, "opc_gemm: y not 2-byte aligned");
   if (!aligned(L->units, 16) || !aligned(L->codebooks, 8))
     return fail(OPC_ERR_INVALID, "opc_gemm: layer buffers misaligned");
-  if (static_cast<int64_t>(n_tok) > (int64_t(65535) * opc::kGmN))
+  if (static_cast<int64_t>(n_tok) > (int64_t(65535) * 128))
     return fail(OPC_ERR_UNSUPPORTED, "opc_gemm: n_tok %d too large", n_tok);
   auto encode = tensor_map_encoder();
   if (!encode) return fail(OPC_ERR_CUDA, "opc_gemm: cuTensorMapEncodeTiled unavailable");
@@ -700,13 +700,16 @@ int opc_gemm(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ld
   DeviceCache dc;
   int rc = device_cache(dev, &dc);
   if (rc != OPC_OK) return rc;
-  if (opc::kGmSmemBytes > static_cast<size_t>(dc.max_smem_optin))
-    return fail(OPC_ERR_UNSUPPORTED, "opc_gemm: needs %zu bytes of shared memory", opc::kGmSmemBytes);
+  // 256-token tiles unless they would leave more than a tenth of the SMs without a tile.
+  const int64_t m_tiles = ceil_div(p.M_pad, opc::kGmM);
+  const int tn = (m_tiles * ceil_div(n_tok, 256) * 10 >= static_cast<int64_t>(dc.sm_count) * 9) ? 256 : 128;
+  if (opc::gm_smem_bytes(tn) > static_cast<size_t>(dc.max_smem_optin))
+    return fail(OPC_ERR_UNSUPPORTED, "opc_gemm: needs %zu bytes of shared memory", opc::gm_smem_bytes(tn));
 
   CUtensorMap tx;
   const cuuint64_t gdim[2] = {static_cast<cuuint64_t>(p.K), static_cast<cuuint64_t>(n_tok)};
   const cuuint64_t gstride[1] = {static_cast<cuuint64_t>(ldx) * 2};
-  const cuuint32_t box[2] = {opc::kGmK, opc::kGmN};
+  const cuuint32_t box[2] = {opc::kGmK, static_cast<cuuint32_t>(tn)};
   const cuuint32_t estride[2] = {1, 1};
   const CUresult cr = encode(&tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(x), gdim, gstride, box, estride,
                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -729,10 +732,16 @@ int opc_gemm(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ld
   a.n_tok = n_tok;
   a.n_slots = p.outlier_tiles * opc::kTileRows;
   cudaStream_t s = static_cast<cudaStream_t>(stream_v);
-  const unsigned n_tiles = static_cast<unsigned>(ceil_div(n_tok, opc::kGmN));
-  rc = launch_gemm_t<false>(tx, a, dim3(static_cast<unsigned>(ceil_div(p.M_pad, opc::kGmM)), n_tiles), s, dev);
+  const unsigned n_tiles = static_cast<unsigned>(ceil_div(n_tok, tn));
+  const dim3 gp(static_cast<unsigned>(m_tiles), n_tiles), gd(static_cast<unsigned>(ceil_div(a.n_slots, opc::kGmM)), n_tiles);
+  if (tn == 256) {
+    rc = launch_gemm_t<false, 256>(tx, a, gp, s, dev);
+    if (rc != OPC_OK || p.n_outliers == 0) return rc;
+    return launch_gemm_t<true, 256>(tx, a, gd, s, dev);
+  }
+  rc = launch_gemm_t<false, 128>(tx, a, gp, s, dev);
   if (rc != OPC_OK || p.n_outliers == 0) return rc;
-  return launch_gemm_t<true>(tx, a, dim3(static_cast<unsigned>(ceil_div(a.n_slots, opc::kGmM)), n_tiles), s, dev);
+  return launch_gemm_t<true, 128>(tx, a, gd, s, dev);
 }
 
 }  // extern "C"
@@ -749,6 +758,7 @@ struct opc_chain {
   unsigned int* d_sync = nullptr;
   size_t clear_bytes = 0;           // sync + acc, cleared before every launch
   unsigned long long* trace = nullptr;  // optional per-phase timestamps (caller-owned)
+  int32_t l2_prefetch = 1;
 };
 
 extern "C" {
@@ -786,6 +796,9 @@ int opc_chain_create(const opc_chain_step* steps, int32_t n_steps, int32_t batch
                     "opc_chain_create: step %d: x must be the previous step's y (same pointer and leading "
                     "dimension, K <= previous M)", j);
     }
+    if (p.row_tiles / dc.sm_count + 2 > opc::kChainSplitSlots)
+      return fail(OPC_ERR_UNSUPPORTED, "opc_chain_create: step %d: %d row tiles exceed %d per SM", j, p.row_tiles,
+                  opc::kChainSplitSlots - 2);
     if (static_cast<int64_t>(batch) * p.K_pad > 64 * opc::kQConsumerThreads)
       return fail(OPC_ERR_UNSUPPORTED, "opc_chain_create: step %d: batch*K_pad = %lld > %d", j,
                   static_cast<long long>(batch) * p.K_pad, 64 * opc::kQConsumerThreads);
@@ -888,6 +901,7 @@ int opc_chain_launch(opc_chain* ch, void* stream_v) {
   a.stages = ch->stages;
   a.xs_bytes = ch->xs_bytes;
   a.negz = opc::kNegZero2;
+  a.l2_prefetch = ch->l2_prefetch;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(ch->grid));
   cfg.blockDim = dim3(opc::kQThreads);
@@ -918,6 +932,14 @@ int opc_chain_set_trace(opc_chain* ch, void* trace) {
   if (trace && !aligned(trace, 8)) return fail(OPC_ERR_INVALID, "opc_chain_set_trace: buffer not 8-byte aligned");
   ch->trace = static_cast<unsigned long long*>(trace);
   return OPC_OK;
+}
+
+int opc_chain_set_option(opc_chain* ch, int32_t option, int32_t value) {
+  if (!ch) return fail(OPC_ERR_INVALID, "opc_chain_set_option: chain is NULL");
+  switch (option) {
+    case OPC_CHAIN_L2_PREFETCH: ch->l2_prefetch = value ? 1 : 0; return OPC_OK;
+    default: return fail(OPC_ERR_INVALID, "opc_chain_set_option: unknown option %d", option);
+  }
 }
 
 int opc_chain_destroy(opc_chain* ch) {
