@@ -37,6 +37,8 @@ struct ChainLayer {
   int32_t x_vec16;           // x rows 16-byte loadable
 };
 
+static_assert(sizeof(ChainLayer) % 16 == 0, "ChainLayer is copied in 16-byte pieces");
+
 struct ChainArgs {
   const ChainLayer* layers;
   unsigned int* sync;        // [grid] per-CTA "layers finished" flags (zero at launch)
@@ -134,6 +136,9 @@ constexpr int kChainMaskMax = 2048;  // row tiles of the previous layer covered 
 // Grid barrier over per-CTA flags: CTA c publishes "finished layer j" with a release store of j+1
 // into flags[c]; a waiter's threads t < G each poll flags[t] with acquire loads (bounded), then
 // meet at a CTA barrier.  No atomic is shared by all CTAs.
+__device__ __forceinline__ void st_relaxed_u32(unsigned int* p, uint32_t v) {
+  asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 __device__ __forceinline__ void st_release_u32(unsigned int* p, uint32_t v) {
   asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -182,6 +187,7 @@ __device__ __forceinline__ __half prev_outlier_value(const PrevInfo& P, int s, i
 constexpr int kChainSplitSlots = 32;  // packed tiles per CTA and layer (host-checked)
 
 struct ChainShared {
+  ChainLayer layer[2];                    // descriptors of layers j (slot j&1) and j+1
   float amax[kQConsumers][kQMaxBatch];    // staging: per-warp max |x|
   unsigned long long tile_acc[kChainSplitSlots][kTileRows][kQMaxBatch];  // split packed tiles
   int32_t tile_cnt[kChainSplitSlots];
@@ -246,6 +252,8 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
   for (int i = threadIdx.x; i < kChainSplitSlots * kTileRows * kQMaxBatch; i += blockDim.x)
     (&sh->tile_acc[0][0][0])[i] = 0ull;
   for (int i = threadIdx.x; i < kChainSplitSlots; i += blockDim.x) sh->tile_cnt[i] = 0;
+  if (threadIdx.x < sizeof(ChainLayer) / 16 && args.n_layers > 0)
+    reinterpret_cast<uint4*>(&sh->layer[0])[threadIdx.x] = reinterpret_cast<const uint4*>(args.layers)[threadIdx.x];
   __syncthreads();
 
   // ------------------------------------------------------------------ producer warp
@@ -355,7 +363,9 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
   bool ok = true;
 
   for (int j = 0; j < args.n_layers && ok; ++j) {
-    const ChainLayer L = args.layers[j];
+    // Descriptors live in shared memory (layer j+1's is copied at the end of layer j), so reading
+    // them costs no global round trip and holds no registers.
+    const ChainLayer& L = sh->layer[j & 1];
     // Everything about this warp's share that does not depend on x, before waiting for x.
     GemvQArgs qa;  // the per-layer view the shared helpers take
     qa.units = L.units; qa.ounits = L.ounits; qa.cbq = L.cbq; qa.tile_mask = L.tile_mask; qa.orow = L.orow;
@@ -368,33 +378,23 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     chain_warp_range(part, warp, &u0, &u1);
     ChainCursor cc = chain_cursor(L, u0 < u1 ? u0 : 0);
     MetaQ cur, nxt;
-    if (u0 < u1) {
+    if (u0 < u1) {  // issued before the wait; first used by the units loop
       cur = load_metaq(qa, cc.seg, g);
       nxt = (cc.seg + 1 < L.MT + L.OT) ? load_metaq(qa, cc.seg + 1, g) : cur;
     }
     PrevInfo P = {};
     if (j > 0) {
-      const ChainLayer* Lp = args.layers + (j - 1);
-      P.tile_mask = Lp->tile_mask;
-      P.orow = Lp->orow;
-      P.oexp = Lp->oexp;
-      P.cbq = Lp->cbq;
-      P.acc = Lp->acc;
-      P.y = Lp->y;
-      P.ldy = Lp->ldy;
-      P.n_slots = Lp->OT * kTileRows;
+      const ChainLayer& Lp = sh->layer[(j - 1) & 1];
+      P.tile_mask = Lp.tile_mask;
+      P.orow = Lp.orow;
+      P.oexp = Lp.oexp;
+      P.cbq = Lp.cbq;
+      P.acc = Lp.acc;
+      P.y = Lp.y;
+      P.ldy = Lp.ldy;
+      P.n_slots = Lp.OT * kTileRows;
     }
-    // The previous layer's static outlier metadata that staging needs, into shared memory before
-    // waiting (its tile masks over the rows x reads, and its slot rows and exponents).
     const bool mask_in_smem = j > 0 && (L.K + 15) / 16 <= kChainMaskMax;
-    if (j > 0) {
-      if (mask_in_smem)
-        for (int t = tid; t < (L.K + 15) / 16; t += kQConsumerThreads) sh->prev_mask[t] = __ldg(P.tile_mask + t);
-      for (int s = tid; s < P.n_slots && s < kChainPatchMax; s += kQConsumerThreads) {
-          sh->patch_row[s] = __ldg(P.orow + s);
-          sh->patch_exp[s] = __ldg(P.oexp + s);
-        }
-    }
     // ---- wait for layer j-1 everywhere
     if (j > 0) {
       if (warp == 0 && !poll_flags_warp(args.sync, G, lane, static_cast<uint32_t>(j))) {
@@ -681,13 +681,28 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
       }
     }
     if (tr && tid == 0) tr[4] = globaltimer_ns();
+    if (j + 1 < args.n_layers) {
+      // For layer j+1: its descriptor, and layer j's static outlier metadata that its staging
+      // reads (shared memory is free: layer j's staging is over).  Issued before the write
+      // fence, so these loads overlap it.
+      if (tid < sizeof(ChainLayer) / 16)
+        reinterpret_cast<uint4*>(&sh->layer[(j + 1) & 1])[tid] = ld_nc_v4(reinterpret_cast<const uint4*>(args.layers + j + 1) + tid);
+      const int kn = args.layers[j + 1].K;
+      if ((kn + 15) / 16 <= kChainMaskMax)
+        for (int t = tid; t < (kn + 15) / 16; t += kQConsumerThreads) sh->prev_mask[t] = __ldg(L.tile_mask + t);
+      const int ns = L.OT * kTileRows;
+      for (int s2 = tid; s2 < ns && s2 < kChainPatchMax; s2 += kQConsumerThreads) {
+        sh->patch_row[s2] = __ldg(L.orow + s2);
+        sh->patch_exp[s2] = __ldg(L.oexp + s2);
+      }
+    }
     fence_acq_rel_gpu();                  // this thread's writes of layer j are visible GPU-wide
     if (tr && tid == 0) tr[5] = globaltimer_ns();
     named_barrier(1, kQConsumerThreads);  // ... for every thread of the CTA
     if (sh->abort) ok = false;
     if (tid == 0) {
       if (tr) tr[6] = globaltimer_ns();
-      st_release_u32(args.sync + cta, static_cast<uint32_t>(j + 1));
+      st_relaxed_u32(args.sync + cta, static_cast<uint32_t>(j + 1));  // ordered by the fences above
       if (tr) tr[7] = globaltimer_ns();
     }
     ex_prev[0] = ex0;

@@ -758,7 +758,7 @@ struct opc_chain {
   unsigned int* d_sync = nullptr;
   size_t clear_bytes = 0;           // sync + acc, cleared before every launch
   unsigned long long* trace = nullptr;  // optional per-phase timestamps (caller-owned)
-  int32_t l2_prefetch = 1;
+  int32_t l2_prefetch = 0;
 };
 
 extern "C" {
