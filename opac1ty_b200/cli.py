@@ -186,12 +186,45 @@ def layer_bench(shape, outliers, batch, iters):
                            "batch": batch, "us": us, "bytes": nb, "gbs": nb / us / 1e3}))
 
 
+@cli.command("decode-bench")
+@click.option("--model", type=click.Choice(["8b", "70b"]), default="8b")
+@click.option("--blocks", type=int, default=None, help="decoder blocks (default: the model's)")
+@click.option("--batch", type=int, default=1)
+@click.option("--iters", type=int, default=20)
+@click.option("--launches", is_flag=True, help="one GEMV launch per projection instead of the chain kernel")
+def decode_bench(model, blocks, batch, iters, launches):
+    """Time the decode step (q|k|v, o, gate|up, down per block) of synthetic 2-bit weights."""
+    import torch
+
+    from . import decode, synthetic
+    from .utils import get_cuda_device_info
+
+    cfg = synthetic.LLAMA_8B if model == "8b" else synthetic.LLAMA_70B
+    dev = torch.device("cuda", 0)
+    st = decode.DecodeStack.synthetic(cfg, n_layers=blocks, device=dev, batch=batch, use_chain=not launches)
+    for _ in range(3):
+        st.step_eager()
+    torch.cuda.synchronize(dev)
+    s = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(iters):
+        st.step_eager()
+    e1.record(s)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / iters
+    nb = st.algorithmic_bytes()
+    click.echo(json.dumps({"gpu": get_cuda_device_info().name, "model": model, "blocks": len(st.blocks),
+                           "batch": batch, "chain": st.chain is not None, "ms_per_step": ms,
+                           "tok_s": batch * 1000.0 / ms, "gbs": nb / (ms * 1e-3) / 1e9}))
+
+
 @cli.command("gemm-bench")
 @click.option("--shape", default="28672x4096", help="MxK")
 @click.option("--tokens", type=int, default=2048)
 @click.option("--outliers", type=float, default=0.01, help="outlier row fraction (0 = none)")
 @click.option("--iters", type=int, default=10)
-def gemm_bench(shape, tokens, outliers, iters):
+def gemm_bench(shape, tokens, outliers, iters):  # noqa: D401
     """Time one synthetic layer's prefill GEMM (tcgen05, CUDA events); prints one JSON line."""
     import torch
 
