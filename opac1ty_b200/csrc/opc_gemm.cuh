@@ -13,9 +13,9 @@
 //               fp16 codebook (PRMT lookups) into the A tile, written in the canonical K-major
 //               128-byte-swizzle layout; after the last stage, read the row's 256 accumulators
 //               from TMEM (the warp's TMEM lane quarter) and store Y.
-// Outlier rows have all-zero codebooks, so the packed pass computes 0 for them and skips their
-// writes; a second launch in dense mode computes them from the row-major outlier copy (A tiles
-// copied instead of decoded) and scatters them to their output rows.
+// Outlier rows have all-zero codebooks, so the packed tiles compute 0 for them and skip their
+// writes; extra CTAs of the same launch (blockIdx.x >= m_tiles) compute them from the row-major
+// outlier copy (A tiles copied instead of decoded) and scatter them to their output rows.
 #pragma once
 
 #include <cuda.h>
@@ -45,6 +45,8 @@ struct GemmArgs {
   __half* y;
   int64_t ldy;
   int32_t M, K_pad, MT, KT, n_tok, n_slots;
+  int32_t m_tiles;             // CTAs with blockIdx.x < m_tiles decode packed tiles; the rest copy
+                               // outlier rows (dense A tiles)
 };
 
 // UMMA shared-memory descriptor: K-major, 128-byte swizzle, 8-row groups 1024 bytes apart.
@@ -106,8 +108,9 @@ __device__ __forceinline__ uint32_t sw128_off(int r, int c) {
   return static_cast<uint32_t>(1024 * (r >> 3) + 128 * (r & 7) + 16 * (c ^ (r & 7)));
 }
 
-template <bool kDense, int kN>
+template <int kN>
 __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap tx, const GemmArgs a) {
+  const bool kDense = static_cast<int>(blockIdx.x) >= a.m_tiles;
   constexpr int kGmBBytes = gm_b_bytes(kN);
   constexpr int kGmTmemCols = kN;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -121,7 +124,8 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_consta
 
   const int warp = __shfl_sync(0xffffffffu, static_cast<int>(threadIdx.x >> 5), 0);
   const int lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * kGmM, n0 = blockIdx.y * kN;
+  const int m0 = (kDense ? static_cast<int>(blockIdx.x) - a.m_tiles : static_cast<int>(blockIdx.x)) * kGmM;
+  const int n0 = blockIdx.y * kN;
   const int nk = a.K_pad / kGmK;
   const int t0 = m0 / kTileRows;
   const int n_rt = kDense ? 0 : min(8, a.MT - t0);  // row tiles with units in this M tile

@@ -27,6 +27,7 @@ from typing import Dict, List, Optional, Sequence
 
 import torch
 
+from . import _lib
 from . import layer as L
 from . import synthetic
 
@@ -141,7 +142,10 @@ class DecodeStack:
             for blk in self.blocks:
                 steps += [(blk.qkv, b["x"], b["qkv"]), (blk.o, b["qkv"], b["o"]),
                           (blk.gate_up, b["o"], b["gu"]), (blk.down, b["gu"], b["x"])]
-            self.chain = Chain(steps)
+            try:
+                self.chain = Chain(steps)
+            except _lib.OpcError:  # shape outside the chain kernel's limits: one launch per GEMV
+                self.chain = None
 
     def layers(self) -> List[L.DeviceLayer]:
         return [dl for b in self.blocks for dl in b.layers()]
