@@ -2,7 +2,8 @@
 """Benchmark: fused 2-bit VQ GEMV at Llama-3.1-8B decode shapes (batch 1, 32 decoder blocks).
 
 One step = one decode token through the projection chain of all 32 blocks (qkv -> o -> gate|up
--> down per block, 128 dependent GEMV launches; opac1ty_b200.decode).  Weights are
+-> down per block, 128 dependent GEMVs; opac1ty_b200.decode), run by the persistent decode-chain
+kernel (one launch per step) for batch 1..2, else one GEMV launch per projection.  Weights are
 random-initialised 2-bit layers of the named shapes with 1 % outlier rows (synthetic data; no
 checkpoint).  The weight set (1.9 GB) is far larger than L2, so no L2 flush is needed between
 steps.
@@ -18,8 +19,11 @@ matmul, restated in C in oracle/) on all host cores, on a bounded sample (1 of 3
 scaled), in the same metric.
 
 N > 1 GPUs (torchrun): output-channel tensor parallelism (opac1ty_b200.tp) -- every projection
-row-sharded across the ranks, an NCCL all-gather of each GEMV's output slice over NVLink.
-value and the roofline count the whole model's bytes per step (summed over ranks).
+row-sharded across the ranks.  Default (--tp-impl chain, batch 1..2): one persistent kernel per
+rank per step that stores its output rows straight into every rank's activations over NVLink
+(CUDA IPC peer pointers) with a cross-rank flag barrier between projections.  --tp-impl nccl:
+one GEMV launch per projection followed by an NCCL all-gather (the baseline form).  value and
+the roofline count the whole model's bytes per step (summed over ranks).
 """
 
 from __future__ import annotations
@@ -205,6 +209,8 @@ def run_ours(args):
         from opac1ty_b200 import tp
 
         stack = tp.TPDecodeStack.synthetic(cfg, rank=rank, world=world, device=dev, batch=args.batch)
+        if args.tp_impl == "chain" and args.batch <= 2:
+            stack.enable_chain()
     else:
         stack = decode.DecodeStack.synthetic(cfg, device=dev, batch=args.batch)
     torch.cuda.synchronize()
@@ -280,6 +286,14 @@ def run_ours(args):
                "sample": f"1 of 32 decoder blocks (7 projections), median of {reps} passes, scaled x32; "
                          f"CPU: {cpu_model()}"}
 
+    fused = getattr(stack, "chain", None) is not None
+    if world == 1:
+        tp_desc = "single GPU"
+    elif fused:
+        tp_desc = f"tp{world} (row shards; one fused kernel per rank: peer stores + flag barrier over NVLink)"
+    else:
+        tp_desc = f"tp{world} (row shards; GEMV launch + NCCL all-gather per projection)"
+    kernel_name = "opc::chain_kernel" if fused else "opc::gemvq_kernel / opc::gemv_kernel"
     if rank == 0:
         line = {
             "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -287,13 +301,13 @@ def run_ours(args):
             "vs_baseline": None, "dtype": "fp16 (2-bit codebook weights, fp32 accumulate)", "data": "synthetic",
             "config": {"workload": WORKLOAD, "batch": args.batch, "blocks": 32, "launches_per_step":
                        stack.launches_per_step(), "l2": "inputs larger than L2 (1.9 GB of weights per step)",
-                       "parallelism": f"tp{world} (row shards + NCCL all-gather)" if world > 1 else "single GPU",
+                       "parallelism": tp_desc,
                        "cuda_graph": True,
                        "pdl": True},
             "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": peaks["hbm_gbs"] * world, "unit": "GB/s",
                          "frac": achieved_gbs / (peaks["hbm_gbs"] * world), "traffic": None,
                          "peak_source": peaks["source"], "algorithmic_bytes_per_step": step_bytes,
-                         "kernel": "opc::gemv_kernel<1,true>"},
+                         "kernel": kernel_name},
             "hbm_tbs": achieved_gbs / 1000.0,
             "kernels": kernels,
             "clocks": clocks,
@@ -307,6 +321,7 @@ def run_ours(args):
         stack.graph = None
         torch.cuda.synchronize()
         dist.barrier()
+        stack.close()
         dist.destroy_process_group()
     return 0
 
@@ -349,6 +364,8 @@ def main(argv=None):
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
+    ap.add_argument("--tp-impl", choices=["chain", "nccl"], default="chain",
+                    help="N > 1: fused row-sharded chain kernel (default) or GEMV + NCCL all-gather")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3

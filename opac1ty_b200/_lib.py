@@ -22,6 +22,8 @@ OPC_ERR_CUDA = -3
 OPC_ERR_WORKSPACE = -4
 OPC_ERR_DEVICE = -5
 OPC_CHAIN_L2_PREFETCH = 1
+OPC_PEER_HANDLE_BYTES = 64
+OPC_MAX_RANKS = 8
 
 _ERR_NAMES = {
     OPC_ERR_INVALID: "OPC_ERR_INVALID",
@@ -125,9 +127,26 @@ PROTOTYPES = {
     "opc_chain_launch": (_c.c_int, [_c.c_void_p, _c.c_void_p]),
     "opc_chain_destroy": (_c.c_int, [_c.c_void_p]),
     "opc_chain_trace_bytes": (_c.c_size_t, [_c.c_void_p]),
+    "opc_chain_set_option": (_c.c_int, [_c.c_void_p, _c.c_int32, _c.c_int32]),
     "opc_chain_grid": (_c.c_int32, [_c.c_void_p]),
     "opc_chain_set_trace": (_c.c_int, [_c.c_void_p, _c.c_void_p]),
-    "opc_chain_set_option": (_c.c_int, [_c.c_void_p, _c.c_int32, _c.c_int32]),
+    "opc_peer_alloc": (_c.c_int, [_c.c_size_t, _c.POINTER(_c.c_void_p), _c.c_void_p]),
+    "opc_peer_open": (_c.c_int, [_c.c_void_p, _c.POINTER(_c.c_void_p)]),
+    "opc_peer_close": (_c.c_int, [_c.c_void_p]),
+    "opc_peer_free": (_c.c_int, [_c.c_void_p]),
+    "opc_chain_tp_scratch_bytes": (
+        _c.c_int, [_c.POINTER(ChainStep), _c.c_int32, _c.c_int32, _c.POINTER(_c.c_size_t)],
+    ),
+    "opc_chain_tp_info": (
+        _c.c_int,
+        [_c.POINTER(ChainStep), _c.c_int32, _c.c_int32, _c.c_int32, _c.c_void_p, _c.c_size_t, _c.c_size_t,
+         _c.c_void_p, _c.POINTER(_c.c_size_t)],
+    ),
+    "opc_chain_create_tp": (
+        _c.c_int,
+        [_c.POINTER(ChainStep), _c.c_int32, _c.c_int32, _c.c_int32, _c.c_int32, _c.POINTER(_c.c_void_p),
+         _c.POINTER(_c.c_void_p), _c.POINTER(_c.c_void_p)],
+    ),
     "opc_dequant": (_c.c_int, [_c.POINTER(Layer), _c.c_void_p, _c.c_int64, _c.c_void_p]),
     "opc_take_device_error": (_c.c_int, [_c.c_int32, _c.POINTER(_c.c_int32)]),
 }

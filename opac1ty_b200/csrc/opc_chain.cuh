@@ -1,5 +1,6 @@
 // opc_chain.cuh -- persistent decode-chain kernel: a whole sequence of dependent fused 2-bit
-// GEMVs (one decode token through every projection of every block) in one cooperative launch.
+// GEMVs (one decode token through every projection of every block) in one cooperative launch,
+// on one GPU or row-sharded over several GPUs of a node.
 //
 // Each layer is the integer-split GEMV of opc_gemvq.cuh (8 PRMT + 3 ALU operations and two int8
 // mma.sync per 16 weights, exact int64 dot products).  What changes is the orchestration:
@@ -8,49 +9,82 @@
 //    units for the CTA's 15 consumer warps through their rings and runs ahead across layer
 //    boundaries (weights do not depend on activations), so HBM keeps streaming while the
 //    consumers wait for a layer's input.
-//  * Layer j+1 needs all of layer j's output: a grid barrier (per-CTA flags, release/acquire at
-//    GPU scope, bounded wait) separates them.  Each CTA then stages x itself from y_j.
+//  * Layer j+1 needs all of layer j's output: a barrier over per-CTA flags (bounded wait)
+//    separates them.  Each CTA then stages x itself from y_j.
 //  * Packed row tiles are handed out whole (CTA c gets tiles round(c*MT/G) .. round((c+1)*MT/G)),
 //    so a tile is split only between warps of one CTA and reduced in shared memory; no
 //    cross-CTA reduction exists for them.  Outlier tiles (16 fp16 rows, 8x heavier per row) are
 //    split evenly across all CTAs and their partial dot products are added exactly into int64
 //    accumulators per outlier slot; the next layer's staging reads those for its outlier rows,
-//    and the CTA owning slot s (s mod G) writes that row of y.
+//    and one CTA of the owning rank writes that row of y.
+//
+// Row sharding over `world` GPUs (one process per GPU): every rank holds a contiguous shard of
+// each layer's output rows and computes it from the full x.  There is no separate all-gather:
+// the kernel stores each output row straight into every rank's copy of the full y over NVLink
+// (peer pointers mapped by CUDA IPC), and the barrier flags are per (rank, CTA) words in every
+// rank's memory, written by their owner with system-scope stores.  Outlier rows are read by
+// every rank from the owner's slot accumulators (system-scope loads of peer memory) through a
+// table of all ranks' outlier rows.  Nothing in this kernel uses TMA or bulk copies with
+// cluster multicast: peer memory is touched only by plain loads and stores.
+//
+// Flags count layers across launches (epoch * (layers + 2) + progress, compared modulo 2^32), so
+// they are never cleared between launches; a launch that gives up poisons the epoch word and
+// every later launch of the chain refuses to run.
 #pragma once
 
 #include "opc_gemvq.cuh"
 
 namespace opc {
 
+constexpr int kMaxRanks = 8;
+
+// One outlier row of a layer's full output (every rank's rows are listed on every rank).
+struct OutlierRef {
+  const unsigned long long* acc;  // its slot's int64 dot products [batch 0, 1] on the owner
+  int32_t row;                    // row of the full output
+  int32_t exp;                    // exponent of the slot's integer row
+  int32_t owner;                  // rank computing it
+  int32_t pad;
+};
+static_assert(sizeof(OutlierRef) == 24, "OutlierRef layout is shared with the host");
+
 struct ChainLayer {
-  const uint8_t* units;      // packed units
-  const uint8_t* ounits;     // int8 outlier units
-  const uint4* cbq;          // [M_pad] integer codebooks; outlier rows {0, 0, e, slot}
-  const uint16_t* tile_mask; // [MT]
-  const int32_t* orow;       // [OT*16]
-  const int32_t* oexp;       // [OT*16]
-  const __half* x;           // layer input (layer 0: the chain input; else a prefix of the previous y)
-  __half* y;                 // layer output
-  unsigned long long* acc;   // [OT*16][2] outlier-slot dot products (zero at launch)
+  const uint8_t* units;       // packed units (this rank's rows)
+  const uint8_t* ounits;      // int8 outlier units
+  const uint4* cbq;           // [M_pad] integer codebooks; outlier rows {0, 0, e, slot}
+  const uint16_t* tile_mask;  // [MT]
+  const int32_t* orow;        // [OT*16] local row of each outlier slot
+  const int32_t* oexp;        // [OT*16]
+  const __half* x;            // layer input (layer 0: the chain input; else a prefix of the previous y)
+  unsigned long long* acc;    // [OT*16][2] this rank's outlier-slot dot products (zero at launch)
+  __half* y_peer[kMaxRanks];  // this rank's first row in rank p's copy of the full output
+  const OutlierRef* oref;     // [n_oref] every outlier row of the full output
+  const uint16_t* mask_full;  // [ceil(m_full / 16)] outlier flags of the full output's rows
   int64_t ldx, ldy;
   int32_t Up, U, M, K, K_pad, MT, KT, OT, KO;
-  int32_t x_vec16;           // x rows 16-byte loadable
+  int32_t x_vec16;            // x rows 16-byte loadable
+  int32_t n_oref, row_off;    // outlier rows of the full output; this rank's first row
+  int32_t m_full, pad[3];     // rows of the full output
 };
 
 static_assert(sizeof(ChainLayer) % 16 == 0, "ChainLayer is copied in 16-byte pieces");
 
 struct ChainArgs {
   const ChainLayer* layers;
-  unsigned int* sync;        // [grid] per-CTA "layers finished" flags (zero at launch)
+  unsigned int* sync;        // [world][grid] flags of every rank's CTAs, in this rank's memory
+  unsigned int* sync_peer[kMaxRanks];  // rank p's flag array (sync_peer[rank] == sync)
+  unsigned int* epoch;       // launches completed; bit 31 = poisoned
   unsigned long long* trace; // optional [n_layers][grid][8] globaltimer stamps (ns) per CTA,
                              // taken by its first consumer thread: input ready, own x loads
-                             // done, exponents known, x staged, own units done, own writes
-                             // fenced, CTA's writes fenced, flag published
+                             // done, exponents known, x staged, own units done, next layer's
+                             // tables requested, CTA barrier passed, flag published (fenced)
   int32_t n_layers, batch, stages, xs_bytes;
   uint32_t negz;
   int32_t l2_prefetch;       // prefetch each consumer's share of the next layer into L2
+  int32_t rank, world;
 };
 constexpr int kChainTracePhases = 8;
+constexpr uint32_t kChainPoisoned = 0x80000000u;
 
 // This CTA's share of a layer: packed units [pu0, pu1) (whole tiles) and outlier units
 // [ou0, ou1); warps 0..wp-1 take the packed share, the other consumer warps the outlier share.
@@ -123,40 +157,52 @@ __device__ __forceinline__ void chain_next_segment(const ChainLayer& L, ChainCur
   c.end = c.begin + (c.seg < L.MT ? L.KT : L.KO);
 }
 
+// Memory-model helpers.  One GPU: GPU scope.  Several GPUs: system scope, because peers write
+// this GPU's flags and outputs and read its accumulators over NVLink.
 __device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
-__device__ __forceinline__ uint32_t ld_acquire_u32(const unsigned int* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ void fence_scope(bool sys) {
+  if (sys) fence_acq_rel_sys();
+  else fence_acq_rel_gpu();
 }
-
-constexpr int kChainPatchMax = 512;  // outlier slots of a layer whose values go through shared memory
-constexpr int kChainMaskMax = 2048;  // row tiles of the previous layer covered by x (tile masks in smem)
-
-// Grid barrier over per-CTA flags: CTA c publishes "finished layer j" with a release store of j+1
-// into flags[c]; a waiter's threads t < G each poll flags[t] with acquire loads (bounded), then
-// meet at a CTA barrier.  No atomic is shared by all CTAs.
-__device__ __forceinline__ void st_relaxed_u32(unsigned int* p, uint32_t v) {
-  asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ void st_release_u32(unsigned int* p, uint32_t v) {
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-// One warp polls all G flags (lane l: flags l, l+32, ...) until every one reaches target.
 __device__ __forceinline__ uint32_t ld_relaxed_u32(const unsigned int* p) {
   uint32_t v;
   asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-// Each lane reads its flags with independent relaxed loads (all in flight together); once every
-// flag has reached target an acquire fence orders the caller's later reads after them.
-__device__ __forceinline__ bool poll_flags_warp(const unsigned int* flags, int G, int lane, uint32_t target) {
+__device__ __forceinline__ uint32_t ld_relaxed_sys_u32(const unsigned int* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_relaxed_u32(unsigned int* p, uint32_t v) {
+  asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_relaxed_sys_u32(unsigned int* p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Barrier over per-CTA flags: CTA c of rank r publishes "finished layer j" by storing
+// base + j + 1 into flags[r*G + c] of every rank, after its threads met at a CTA barrier and the
+// publishing thread fenced.  A waiting CTA's warp 0 polls all flags with independent relaxed
+// loads (lane l: flags l, l+32, ...; all in flight together) until every one has reached target
+// (modulo 2^32), bounded by kWaitLimitNs; then an acquire fence orders the caller's later reads.
+__device__ __forceinline__ bool poll_flags_warp(const unsigned int* flags, int n, int lane, uint32_t target, bool sys) {
   uint64_t t0 = 0;
   for (;;) {
-    uint32_t lo = 0xffffffffu;
-    for (int t = lane; t < G; t += 32) lo = min(lo, ld_relaxed_u32(flags + t));
-    if (__all_sync(0xffffffffu, lo >= target)) {
-      fence_acq_rel_gpu();
+    bool reached = true;
+#pragma unroll 4
+    for (int t = lane; t < n; t += 32) {
+      const uint32_t v = sys ? ld_relaxed_sys_u32(flags + t) : ld_relaxed_u32(flags + t);
+      reached &= static_cast<int32_t>(v - target) >= 0;
+    }
+    if (__all_sync(0xffffffffu, reached)) {
+      fence_scope(sys);
       return true;
     }
     const uint64_t now = globaltimer_ns();
@@ -168,44 +214,50 @@ __device__ __forceinline__ bool poll_flags_warp(const unsigned int* flags, int G
 // Exact 2^e for e in [-126, 127].
 __device__ __forceinline__ float pow2f(int e) { return __int_as_float((127 + e) << 23); }
 
-// What the staging of layer j needs from layer j-1 (kept in registers, loaded before the wait).
-struct PrevInfo {
-  const uint16_t* tile_mask;
-  const int32_t* orow;
-  const int32_t* oexp;
-  const uint4* cbq;
-  const unsigned long long* acc;
-  __half* y;
-  int64_t ldy;
-  int32_t n_slots;
-};
-__device__ __forceinline__ __half prev_outlier_value(const PrevInfo& P, int s, int b, int ex) {
-  const long long t = static_cast<long long>(__ldcg(P.acc + 2 * s + b));
-  return scale_to_half(t, __ldg(P.oexp + s) + ex);
-}
+// Value of an outlier row from its slot accumulator t, slot exponent e and x exponent ex.
+__device__ __forceinline__ __half outlier_half(long long t, int e, int ex) { return scale_to_half(t, e + ex); }
 
-constexpr int kChainSplitSlots = 32;  // packed tiles per CTA and layer (host-checked)
+constexpr int kChainPatchMax = 512;  // outlier rows of a layer whose values go through shared memory
+constexpr int kChainMaskMax = 2048;  // row tiles of the previous layer covered by x (tile masks in smem)
+constexpr int kChainSplitSlots = 32; // packed tiles per CTA and layer (host-checked)
 
 struct ChainShared {
   ChainLayer layer[2];                    // descriptors of layers j (slot j&1) and j+1
   float amax[kQConsumers][kQMaxBatch];    // staging: per-warp max |x|
   unsigned long long tile_acc[kChainSplitSlots][kTileRows][kQMaxBatch];  // split packed tiles
   int32_t tile_cnt[kChainSplitSlots];
-  int32_t patch_row[kChainPatchMax];      // previous layer's outlier rows by slot
-  int32_t patch_exp[kChainPatchMax];      // and their integer-row exponents
-  uint16_t patch_val[kChainPatchMax][kQMaxBatch];
-  uint16_t prev_mask[kChainMaskMax];      // previous layer's tile masks of the rows x reads
+  const unsigned long long* patch_acc[kChainPatchMax];  // previous layer's outlier rows: accumulators,
+  int32_t patch_row[kChainPatchMax];      // rows of the full output,
+  int32_t patch_exp[kChainPatchMax];      // integer-row exponents,
+  uint16_t patch_val[kChainPatchMax][kQMaxBatch];  // values (written during staging),
+  uint8_t patch_owner[kChainPatchMax];    // owning ranks
+  uint16_t prev_mask[kChainMaskMax];      // previous layer's outlier flags of the rows x reads
   int32_t abort;
+  uint32_t epoch;
 };
+
+// Rows m.row[0..1] (local) of this warp's tile with dot products t into every rank's output.
+__device__ __forceinline__ void chain_write_rows(const ChainLayer& L, int P, int B, const MetaQ& m, const long long t[2],
+                                                 int q, int ex0, int ex1) {
+  const int b = q >> 1;
+  if ((q & 1) || b >= B) return;
+  const int ex = b ? ex1 : ex0;
+  const __half h0 = scale_to_half(t[0], m.e[0] + ex), h1 = scale_to_half(t[1], m.e[1] + ex);
+  for (int p = 0; p < P; ++p) {
+    __half* yb = L.y_peer[p] + b * L.ldy;
+    if (m.row[0] >= 0) yb[m.row[0]] = h0;
+    if (m.row[1] >= 0) yb[m.row[1]] = h1;
+  }
+}
 
 // A warp's partial dot products of packed tile `seg` (this CTA's local tile lt), shared with
 // other warps of the CTA: added exactly into the tile's shared int64 accumulators; the warp that
 // completes the count of contributors writes the tile's rows and clears the slot.
-__device__ void chain_split_add(ChainShared* sh, const GemvQArgs& qa, const MetaQ& m, const long long t[2], int lt,
-                                int n_contrib, int lane, int g, int q, int ex0, int ex1) {
+__device__ void chain_split_add(ChainShared* sh, const ChainLayer& L, int P, int B, const MetaQ& m, const long long t[2],
+                                int lt, int n_contrib, int lane, int g, int q, int ex0, int ex1) {
   const int slot = lt & (kChainSplitSlots - 1);
   const int b = q >> 1;
-  const bool live = !(q & 1) && b < qa.batch;
+  const bool live = !(q & 1) && b < B;
   if (live) {
     atomicAdd(&sh->tile_acc[slot][g][b], static_cast<unsigned long long>(t[0]));
     atomicAdd(&sh->tile_acc[slot][g + 8][b], static_cast<unsigned long long>(t[1]));
@@ -223,7 +275,7 @@ __device__ void chain_split_add(ChainShared* sh, const GemvQArgs& qa, const Meta
     fin[1] = static_cast<long long>(atomicExch(&sh->tile_acc[slot][g + 8][b], 0ull));
   }
   if (lane == 0) sh->tile_cnt[slot] = 0;
-  write_outq(qa, m, fin, q, ex0, ex1);
+  chain_write_rows(L, P, B, m, fin, q, ex0, ex1);
 }
 
 template <int kXC>
@@ -247,7 +299,10 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
       mbar_init(empty_base + i * 8, 1);
     }
     fence_mbar_init();
-    sh->abort = 0;
+    const uint32_t ep = ld_relaxed_u32(args.epoch);
+    sh->epoch = ep;
+    sh->abort = (ep & kChainPoisoned) ? 1 : 0;
+    if (ep & kChainPoisoned) atomicCAS(&g_opc_device_error, 0, kDevErrChainPoisoned);
   }
   for (int i = threadIdx.x; i < kChainSplitSlots * kTileRows * kQMaxBatch; i += blockDim.x)
     (&sh->tile_acc[0][0][0])[i] = 0ull;
@@ -255,6 +310,7 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
   if (threadIdx.x < sizeof(ChainLayer) / 16 && args.n_layers > 0)
     reinterpret_cast<uint4*>(&sh->layer[0])[threadIdx.x] = reinterpret_cast<const uint4*>(args.layers)[threadIdx.x];
   __syncthreads();
+  if (sh->abort) return;  // poisoned: no work, no flags
 
   // ------------------------------------------------------------------ producer warp
   if (warp == kQProducerWarp) {
@@ -271,7 +327,7 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     // HBM streams the next layer during this one's compute and its ring refills hit L2.
     auto prefetch_next = [&](int jn) {
       if (!args.l2_prefetch || jn >= args.n_layers) return;
-      const ChainLayer N = args.layers[jn];
+      const ChainLayer& N = args.layers[jn];
       const ChainPart p = chain_part(N, cta, G);
       int32_t a0, a1;
       chain_warp_range(p, i, &a0, &a1);
@@ -289,13 +345,12 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     auto next_range = [&]() {
       while (j < args.n_layers) {
         Lp = args.layers + j;
-        const ChainLayer L = *Lp;
-        const ChainPart p = chain_part(L, cta, G);
+        const ChainPart p = chain_part(*Lp, cta, G);
         int32_t u0;
         chain_warp_range(p, i, &u0, &u1);
         prefetch_next(j + 1);
         if (u0 < u1) {
-          pc = chain_cursor(L, u0);
+          pc = chain_cursor(*Lp, u0);
           return true;
         }
         ++j;
@@ -323,10 +378,7 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
           else
             bulk_g2s(ring + slot * kQChunkBytes, src, static_cast<uint32_t>(cnt * kUnitBytes), bar);
           pc.u += cnt;
-          if (pc.u == pc.end && pc.u < u1) {
-            const ChainLayer L = *Lp;
-            chain_next_segment(L, pc);
-          }
+          if (pc.u == pc.end && pc.u < u1) chain_next_segment(*Lp, pc);
           ++c;
           issued = true;
           if (pc.u >= u1) {
@@ -338,9 +390,10 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
       if (__any_sync(0xffffffffu, issued)) {
         t_idle = 0;
       } else {
+        if (*reinterpret_cast<volatile int32_t*>(&sh->abort)) break;  // consumers gave up (error recorded)
         const uint64_t now = globaltimer_ns();
         if (t_idle == 0) t_idle = now;
-        else if (now - t_idle > kWaitLimitNs) {
+        else if (now - t_idle > 2 * kWaitLimitNs) {  // longer than any consumer wait: theirs report first
           failed = true;
           break;
         }
@@ -348,6 +401,14 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
       }
     }
     if (failed && lane == 0) atomicCAS(&g_opc_device_error, 0, kDevErrTmaTimeout);
+    // Copies that consumers which gave up never waited for land before the CTA exits: wait
+    // (bounded) for the last chunk issued into each ring slot.
+    if (i < kQConsumers) {
+      for (int s = 0; s < S && s < c; ++s) {
+        const int32_t last = s + S * ((c - 1 - s) / S);
+        mbar_wait_bounded(full_base + (i * S + s) * 8, static_cast<uint32_t>((last / S) & 1));
+      }
+    }
     return;
   }
 
@@ -357,22 +418,47 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
   const uint32_t negz = args.negz;
   const uint32_t ring = ring_base + warp * S * kQChunkBytes + lane * 16;
   const uint32_t fullw = full_base + warp * S * 8, emptyw = empty_base + warp * S * 8;
+  const int P = args.world;
+  const bool sys = P > 1;
+  const int n_flags = P * G;
+  // This launch publishes layer j as base + j + 1 and its end as base + n_layers + 1.
+  const uint32_t base = sh->epoch * static_cast<uint32_t>(args.n_layers + 2);
   int slot = 0;
   uint32_t phase = 0;
   int32_t ex_prev[kQMaxBatch] = {0, 0};
   bool ok = true;
+
+  // Every CTA of every rank has published at least `target`; sets abort on a timeout.  The
+  // polling lanes' acquire fence plus the CTA barrier order every thread's later reads.
+  auto wait_all = [&](uint32_t target) {
+    if (warp == 0 && !poll_flags_warp(args.sync, n_flags, lane, target, sys) && lane == 0) {
+      sh->abort = 1;
+      atomicCAS(&g_opc_device_error, 0, kDevErrBarrierTimeout);
+    }
+    named_barrier(1, kQConsumerThreads);
+  };
+  // After a CTA barrier: this CTA's flag in every rank's memory.  The publishing thread's fence
+  // is cumulative: it orders every write the barrier made it observe (all threads' output rows
+  // and accumulator adds) before the flag, so no other thread fences.
+  auto publish = [&](uint32_t value) {
+    if (sys) {
+      if (tid < P) fence_acq_rel_sys();
+#pragma unroll
+      for (int p = 0; p < kMaxRanks; ++p)  // constant indices: the pointers stay in the parameter space
+        if (p == tid && p < P) st_relaxed_sys_u32(args.sync_peer[p] + args.rank * G + cta, value);
+    } else if (tid == 0) {
+      fence_acq_rel_gpu();
+      st_relaxed_u32(args.sync + cta, value);
+    }
+  };
 
   for (int j = 0; j < args.n_layers && ok; ++j) {
     // Descriptors live in shared memory (layer j+1's is copied at the end of layer j), so reading
     // them costs no global round trip and holds no registers.
     const ChainLayer& L = sh->layer[j & 1];
     // Everything about this warp's share that does not depend on x, before waiting for x.
-    GemvQArgs qa;  // the per-layer view the shared helpers take
-    qa.units = L.units; qa.ounits = L.ounits; qa.cbq = L.cbq; qa.tile_mask = L.tile_mask; qa.orow = L.orow;
-    qa.oexp = L.oexp; qa.x = L.x; qa.y = L.y; qa.acc = nullptr; qa.counters = nullptr; qa.ldx = L.ldx;
-    qa.ldy = L.ldy; qa.Up = L.Up; qa.U = L.U; qa.M = L.M; qa.K = L.K; qa.K_pad = L.K_pad; qa.MT = L.MT;
-    qa.KT = L.KT; qa.OT = L.OT; qa.KO = L.KO; qa.batch = B; qa.stages = S; qa.xs_bytes = args.xs_bytes;
-    qa.x_vec16 = 0; qa.negz = negz;
+    GemvQArgs qa;  // the per-layer view load_metaq takes
+    qa.cbq = L.cbq; qa.tile_mask = L.tile_mask; qa.orow = L.orow; qa.oexp = L.oexp; qa.M = L.M; qa.MT = L.MT;
     const ChainPart part = chain_part(L, cta, G);
     int32_t u0, u1;
     chain_warp_range(part, warp, &u0, &u1);
@@ -382,29 +468,13 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
       cur = load_metaq(qa, cc.seg, g);
       nxt = (cc.seg + 1 < L.MT + L.OT) ? load_metaq(qa, cc.seg + 1, g) : cur;
     }
-    PrevInfo P = {};
-    if (j > 0) {
-      const ChainLayer& Lp = sh->layer[(j - 1) & 1];
-      P.tile_mask = Lp.tile_mask;
-      P.orow = Lp.orow;
-      P.oexp = Lp.oexp;
-      P.cbq = Lp.cbq;
-      P.acc = Lp.acc;
-      P.y = Lp.y;
-      P.ldy = Lp.ldy;
-      P.n_slots = Lp.OT * kTileRows;
-    }
-    const bool mask_in_smem = j > 0 && (L.K + 15) / 16 <= kChainMaskMax;
+    const bool has_prev = j > 0;
+    const ChainLayer& Lp = sh->layer[(j + 1) & 1];  // layer j-1 while j > 0
+    const int n_pref = has_prev ? Lp.n_oref : 0;
+    const bool mask_in_smem = has_prev && (L.K + 15) / 16 <= kChainMaskMax;
     // ---- wait for layer j-1 everywhere
-    if (j > 0) {
-      if (warp == 0 && !poll_flags_warp(args.sync, G, lane, static_cast<uint32_t>(j))) {
-        if (lane == 0) {
-          sh->abort = 1;
-          atomicCAS(&g_opc_device_error, 0, kDevErrTmaTimeout);
-        }
-      }
-      fence_acq_rel_gpu();
-      named_barrier(1, kQConsumerThreads);
+    if (has_prev) {
+      wait_all(base + static_cast<uint32_t>(j));
       if (sh->abort) {
         ok = false;
         break;
@@ -412,17 +482,15 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     }
     unsigned long long* tr = args.trace ? args.trace + (static_cast<int64_t>(j) * G + cta) * kChainTracePhases : nullptr;
     if (tr && tid == 0) tr[0] = globaltimer_ns();
-    const bool has_prev = j > 0;
 
     // ---- stage x_j (x = the previous output when j > 0).  Round 1 issues every load at once:
-    // this thread's x chunks with the previous layer's outlier flags of their rows, and (slot
-    // threads) the previous layer's outlier values.  Outlier rows of y_{j-1} are read from the
-    // slot accumulators, never from y, and published through a shared patch table sorted by row.
+    // this thread's x chunks with the previous layer's outlier flags of their rows, and the
+    // previous layer's outlier values from their slot accumulators (on the owning rank).  Outlier
+    // rows of y_{j-1} are never read from y; their values go through a shared table.
     int ex0 = 0, ex1 = 0;  // x exponents of batch rows 0, 1 (scalars: no local memory)
     {
       const int per_row = L.K_pad / 8;
       const int total = B * per_row;
-      const int n_pslots = has_prev ? P.n_slots : 0;
       uint4 v[kXC];
       uint32_t tmw[kXC];
 #pragma unroll
@@ -445,7 +513,7 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
                                 h[4] | (uint32_t(h[5]) << 16), h[6] | (uint32_t(h[7]) << 16));
             }
             if (has_prev) {
-              const uint32_t mw = mask_in_smem ? sh->prev_mask[k >> 4] : __ldg(P.tile_mask + (k >> 4));
+              const uint32_t mw = mask_in_smem ? sh->prev_mask[k >> 4] : __ldg(Lp.mask_full + (k >> 4));
               uint32_t tm = (mw >> (k & 15)) & 0xffu;
               if (k + 8 > L.K) tm &= (1u << (L.K - k)) - 1u;
               tmw[i] = tm;
@@ -454,24 +522,39 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
         }
       }
       float mx[kQMaxBatch] = {0.f, 0.f};
-      // slot threads: the previous layer's outlier values (y rows owned by this CTA written here)
-      for (int s = tid; s < n_pslots; s += kQConsumerThreads) {
-        const int row = s < kChainPatchMax ? sh->patch_row[s] : __ldg(P.orow + s);
-        const int e0 = s < kChainPatchMax ? sh->patch_exp[s] : __ldg(P.oexp + s);
-        const long long t0 = static_cast<long long>(__ldcg(P.acc + 2 * s));
-        const long long t1 = B > 1 ? static_cast<long long>(__ldcg(P.acc + 2 * s + 1)) : 0ll;
-        const __half h0 = scale_to_half(t0, e0 + ex_prev[0]);
-        const __half h1 = scale_to_half(t1, e0 + ex_prev[1]);
-        if (row >= 0 && s % G == cta) {
-          P.y[row] = h0;
-          if (B > 1) P.y[P.ldy + row] = h1;
+      // the previous layer's outlier values (rows owned by this rank and assigned to this CTA
+      // are written to every rank's y here)
+      for (int s = tid; s < n_pref; s += kQConsumerThreads) {
+        int row, e0, own;
+        const unsigned long long* acc;
+        if (s < kChainPatchMax) {
+          row = sh->patch_row[s];
+          e0 = sh->patch_exp[s];
+          own = sh->patch_owner[s];
+          acc = sh->patch_acc[s];
+        } else {
+          const OutlierRef o = Lp.oref[s];
+          row = o.row;
+          e0 = o.exp;
+          own = o.owner;
+          acc = o.acc;
+        }
+        const long long t0 = static_cast<long long>(sys ? ld_relaxed_sys_u64(acc) : __ldcg(acc));
+        const long long t1 = B > 1 ? static_cast<long long>(sys ? ld_relaxed_sys_u64(acc + 1) : __ldcg(acc + 1)) : 0ll;
+        const __half h0 = outlier_half(t0, e0, ex_prev[0]);
+        const __half h1 = outlier_half(t1, e0, ex_prev[1]);
+        if (own == args.rank && s % G == cta) {
+          for (int p = 0; p < P; ++p) {
+            __half* yb = Lp.y_peer[p] - Lp.row_off;
+            yb[row] = h0;
+            if (B > 1) yb[Lp.ldy + row] = h1;
+          }
         }
         if (s < kChainPatchMax) {
-          sh->patch_row[s] = row;
           sh->patch_val[s][0] = __half_as_ushort(h0);
           sh->patch_val[s][1] = __half_as_ushort(h1);
         }
-        if (row >= 0 && row < L.K) {
+        if (row < L.K) {
           mx[0] = fmaxf(mx[0], fabsf(__half2float(h0)));
           if (B > 1) mx[1] = fmaxf(mx[1], fabsf(__half2float(h1)));
         }
@@ -485,7 +568,7 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
           float m = 0.f;
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
-            if ((tmw[i] >> e) & 1u) continue;  // outlier row: its value comes from the patch table
+            if ((tmw[i] >> e) & 1u) continue;  // outlier row: its value comes from the table
             const __half hv = __ushort_as_half(static_cast<unsigned short>((wv[e >> 1] >> (16 * (e & 1))) & 0xffffu));
             m = fmaxf(m, fabsf(__half2float(hv)));
           }
@@ -539,11 +622,11 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
           for (int dd = 0; dd < 3; ++dd) sts64(xs_base + (3 * b + dd) * colb + pos, d[dd][0], d[dd][1]);
         }
       }
-      if (n_pslots > 0) {
-        // Outlier rows of the previous layer: one thread per slot overwrites its row's digits
-        // (the chunks above converted whatever y held there).
+      if (n_pref > 0) {
+        // Outlier rows of the previous layer: one thread per row overwrites its digits (the
+        // chunks above converted whatever y held there).
         named_barrier(1, kQConsumerThreads);
-        for (int s = tid; s < n_pslots; s += kQConsumerThreads) {
+        for (int s = tid; s < n_pref; s += kQConsumerThreads) {
           int row;
           uint32_t hv[kQMaxBatch];
           if (s < kChainPatchMax) {
@@ -551,9 +634,13 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
             hv[0] = sh->patch_val[s][0];
             hv[1] = sh->patch_val[s][1];
           } else {
-            row = __ldg(P.orow + s);
-            hv[0] = __half_as_ushort(prev_outlier_value(P, s, 0, ex_prev[0]));
-            hv[1] = B > 1 ? __half_as_ushort(prev_outlier_value(P, s, 1, ex_prev[1])) : 0u;
+            const OutlierRef o = Lp.oref[s];
+            row = o.row;
+            const long long t0 = static_cast<long long>(sys ? ld_relaxed_sys_u64(o.acc) : __ldcg(o.acc));
+            const long long t1 =
+                B > 1 ? static_cast<long long>(sys ? ld_relaxed_sys_u64(o.acc + 1) : __ldcg(o.acc + 1)) : 0ll;
+            hv[0] = __half_as_ushort(outlier_half(t0, o.exp, ex_prev[0]));
+            hv[1] = __half_as_ushort(outlier_half(t1, o.exp, ex_prev[1]));
           }
           if (row < 0 || row >= L.K) continue;
           const uint32_t pos = static_cast<uint32_t>((row >> 7) * 128 + xs_pos8(row & 127));
@@ -657,8 +744,10 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
           } else {
             long long t[2];
             finish_dot(A, q, t);
-            if (cc.begin < u0) chain_split_add(sh, qa, cur, t, cc.seg - tile0, contrib(cc.begin), lane, g, q, ex0, ex1);
-            else write_outq(qa, cur, t, q, ex0, ex1);
+            if (cc.begin < u0)
+              chain_split_add(sh, L, P, B, cur, t, cc.seg - tile0, contrib(cc.begin), lane, g, q, ex0, ex1);
+            else
+              chain_write_rows(L, P, B, cur, t, q, ex0, ex1);
           }
           zero_accq(A);
           chain_next_segment(L, cc);
@@ -672,8 +761,10 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
         } else {
           long long t[2];
           finish_dot(A, q, t);
-          if (cc.begin >= u0 && cc.end <= u1) write_outq(qa, cur, t, q, ex0, ex1);
-          else chain_split_add(sh, qa, cur, t, cc.seg - tile0, contrib(cc.begin), lane, g, q, ex0, ex1);
+          if (cc.begin >= u0 && cc.end <= u1)
+            chain_write_rows(L, P, B, cur, t, q, ex0, ex1);
+          else
+            chain_split_add(sh, L, P, B, cur, t, cc.seg - tile0, contrib(cc.begin), lane, g, q, ex0, ex1);
         }
       } else {
         atomicCAS(&g_opc_device_error, 0, kDevErrTmaTimeout);
@@ -682,61 +773,59 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     }
     if (tr && tid == 0) tr[4] = globaltimer_ns();
     if (j + 1 < args.n_layers) {
-      // For layer j+1: its descriptor, and layer j's static outlier metadata that its staging
+      // For layer j+1: its descriptor, and layer j's outlier table and flags that its staging
       // reads (shared memory is free: layer j's staging is over).  Issued before the write
       // fence, so these loads overlap it.
       if (tid < sizeof(ChainLayer) / 16)
         reinterpret_cast<uint4*>(&sh->layer[(j + 1) & 1])[tid] = ld_nc_v4(reinterpret_cast<const uint4*>(args.layers + j + 1) + tid);
       const int kn = args.layers[j + 1].K;
       if ((kn + 15) / 16 <= kChainMaskMax)
-        for (int t = tid; t < (kn + 15) / 16; t += kQConsumerThreads) sh->prev_mask[t] = __ldg(L.tile_mask + t);
-      const int ns = L.OT * kTileRows;
-      for (int s2 = tid; s2 < ns && s2 < kChainPatchMax; s2 += kQConsumerThreads) {
-        sh->patch_row[s2] = __ldg(L.orow + s2);
-        sh->patch_exp[s2] = __ldg(L.oexp + s2);
+        for (int t = tid; t < (kn + 15) / 16; t += kQConsumerThreads) sh->prev_mask[t] = __ldg(L.mask_full + t);
+      for (int s2 = tid; s2 < L.n_oref && s2 < kChainPatchMax; s2 += kQConsumerThreads) {
+        const OutlierRef o = L.oref[s2];
+        sh->patch_acc[s2] = o.acc;
+        sh->patch_row[s2] = o.row;
+        sh->patch_exp[s2] = o.exp;
+        sh->patch_owner[s2] = static_cast<uint8_t>(o.owner);
       }
     }
-    fence_acq_rel_gpu();                  // this thread's writes of layer j are visible GPU-wide
     if (tr && tid == 0) tr[5] = globaltimer_ns();
-    named_barrier(1, kQConsumerThreads);  // ... for every thread of the CTA
+    named_barrier(1, kQConsumerThreads);  // every thread's writes of layer j, then the flag
     if (sh->abort) ok = false;
-    if (tid == 0) {
-      if (tr) tr[6] = globaltimer_ns();
-      st_relaxed_u32(args.sync + cta, static_cast<uint32_t>(j + 1));  // ordered by the fences above
-      if (tr) tr[7] = globaltimer_ns();
-    }
+    if (tr && tid == 0) tr[6] = globaltimer_ns();
+    if (ok) publish(base + static_cast<uint32_t>(j + 1));
+    if (tr && tid == 0) tr[7] = globaltimer_ns();
     ex_prev[0] = ex0;
     ex_prev[1] = ex1;
   }
 
-  // ---- last layer's outlier rows, once every CTA has finished it
+  // ---- last layer's outlier rows, once every CTA has finished it; with several ranks, a last
+  // barrier so that no rank starts its next launch while a peer still writes or reads this one's
+  // buffers.
   if (ok && args.n_layers > 0) {
-    if (warp == 0 && !poll_flags_warp(args.sync, G, lane, static_cast<uint32_t>(args.n_layers))) {
-      if (lane == 0) {
-        sh->abort = 1;
-        atomicCAS(&g_opc_device_error, 0, kDevErrTmaTimeout);
-      }
-    }
-    __threadfence();
-    named_barrier(1, kQConsumerThreads);
+    wait_all(base + static_cast<uint32_t>(args.n_layers));
     if (!sh->abort) {
-      const ChainLayer* Lp = args.layers + (args.n_layers - 1);
-      PrevInfo P = {};
-      P.orow = Lp->orow;
-      P.oexp = Lp->oexp;
-      P.acc = Lp->acc;
-      P.y = Lp->y;
-      P.ldy = Lp->ldy;
-      const int n_slots = Lp->OT * kTileRows;
-      for (int s = cta + G * tid; s < n_slots; s += G * kQConsumerThreads) {
-        const int row = __ldg(P.orow + s);
-        if (row >= 0) {
-          P.y[row] = prev_outlier_value(P, s, 0, ex_prev[0]);
-          if (B > 1) P.y[P.ldy + row] = prev_outlier_value(P, s, 1, ex_prev[1]);
+      const ChainLayer& Ll = sh->layer[(args.n_layers - 1) & 1];
+      for (int i = cta + G * tid; i < Ll.n_oref; i += G * kQConsumerThreads) {
+        const OutlierRef o = Ll.oref[i];
+        if (o.owner != args.rank) continue;
+        const __half h0 = outlier_half(static_cast<long long>(__ldcg(o.acc)), o.exp, ex_prev[0]);
+        const __half h1 = B > 1 ? outlier_half(static_cast<long long>(__ldcg(o.acc + 1)), o.exp, ex_prev[1]) : h0;
+        for (int p = 0; p < P; ++p) {
+          __half* yb = Ll.y_peer[p] - Ll.row_off;
+          yb[o.row] = h0;
+          if (B > 1) yb[Ll.ldy + o.row] = h1;
         }
       }
+      if (sys) {
+        named_barrier(1, kQConsumerThreads);
+        publish(base + static_cast<uint32_t>(args.n_layers + 1));
+        wait_all(base + static_cast<uint32_t>(args.n_layers + 1));
+      }
     }
+    if (tid == 0 && cta == 0 && !sh->abort) atomicAdd(args.epoch, 1u);
   }
+  if (tid == 0 && sh->abort) atomicOr(args.epoch, kChainPoisoned);
 }
 
 }  // namespace opc

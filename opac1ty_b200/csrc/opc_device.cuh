@@ -321,7 +321,17 @@ __device__ __forceinline__ int round_small_int(float v) {
 
 // Device error word (one per device, lives in the module; the library is one translation
 // unit).  Codes:
-enum DeviceError : int { kDevErrNone = 0, kDevErrTmaTimeout = 1, kDevErrBadIndex = 2 };
+//   1  a ring / shared-memory barrier wait gave up
+//   2  an index out of range was skipped
+//   3  a grid or cross-rank barrier of the decode chain gave up (a CTA or rank did not arrive)
+//   4  a decode chain launch found the chain poisoned by an earlier failed launch
+enum DeviceError : int {
+  kDevErrNone = 0,
+  kDevErrTmaTimeout = 1,
+  kDevErrBadIndex = 2,
+  kDevErrBarrierTimeout = 3,
+  kDevErrChainPoisoned = 4
+};
 __device__ int g_opc_device_error = 0;
 
 }  // namespace opc

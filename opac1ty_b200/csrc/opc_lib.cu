@@ -747,63 +747,172 @@ int opc_gemm(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ld
 }  // extern "C"
 
 // ---------------------------------------------------------------------------------------------
-// Decode chain (persistent cooperative kernel).
+// Decode chain (persistent cooperative kernel), on one GPU or row-sharded over a node's GPUs.
 // ---------------------------------------------------------------------------------------------
 struct opc_chain {
   int device = 0;
   int32_t n_layers = 0, batch = 1, stages = 2, xs_bytes = 0, grid = 0, xc = 8;
+  int32_t rank = 0, world = 1;
   size_t smem = 0;
-  void* dev_mem = nullptr;          // [layers | sync | acc]
+  void* dev_mem = nullptr;              // [layers | outlier tables | flag masks | epoch (| flags | acc)]
   opc::ChainLayer* d_layers = nullptr;
-  unsigned int* d_sync = nullptr;
-  size_t clear_bytes = 0;           // sync + acc, cleared before every launch
+  unsigned int* d_sync = nullptr;       // this rank's flags [world][grid]
+  unsigned int* sync_peer[opc::kMaxRanks] = {};
+  unsigned int* d_epoch = nullptr;
+  void* acc = nullptr;                  // this rank's outlier accumulators, cleared before every launch
+  size_t acc_bytes = 0;
   unsigned long long* trace = nullptr;  // optional per-phase timestamps (caller-owned)
   int32_t l2_prefetch = 0;
 };
 
-extern "C" {
+namespace {
 
-int opc_chain_create(const opc_chain_step* steps, int32_t n_steps, int32_t batch, opc_chain** out) {
-  if (!out) return fail(OPC_ERR_INVALID, "opc_chain_create: out is NULL");
-  *out = nullptr;
-  if (!steps || n_steps < 1) return fail(OPC_ERR_INVALID, "opc_chain_create: no steps");
-  if (batch < 1 || batch > opc::kQMaxBatch)
-    return fail(OPC_ERR_UNSUPPORTED, "opc_chain_create: batch %d (the chain runs batch 1..%d)", batch, opc::kQMaxBatch);
+struct OutlierSlot {
+  int32_t slot, row, exp;  // slot index, local row, exponent of the slot's integer row
+};
+
+// One rank of a chain as this process sees it (pointers valid in this process).
+struct ChainRank {
+  std::vector<int32_t> M;                       // rows of its shard, per step
+  std::vector<std::vector<OutlierSlot>> slots;  // its outlier rows, per step
+  std::vector<char*> y;                         // row 0 of its copy of each step's full output
+  std::vector<unsigned long long*> acc;         // its outlier accumulators, per step
+  unsigned int* sync = nullptr;                 // its flag array [world][grid]
+};
+
+int read_outlier_slots(const opc_layer* L, std::vector<OutlierSlot>* out) {
+  const int32_t ns = n_slots_of(L->plan);
+  std::vector<int32_t> h(2 * static_cast<size_t>(ns));
+  OPC_CUDA(cudaMemcpy(h.data(), L->outlier_rows, h.size() * sizeof(int32_t), cudaMemcpyDeviceToHost),
+           "cudaMemcpy(outlier slots)");
+  out->clear();
+  for (int32_t s = 0; s < ns; ++s)
+    if (h[s] >= 0) out->push_back({s, h[s], h[ns + s]});
+  return OPC_OK;
+}
+
+size_t chain_acc_bytes(const opc_layer_plan& p) {
+  return align_up(static_cast<size_t>(n_slots_of(p)) * opc::kQMaxBatch * sizeof(unsigned long long), 256);
+}
+size_t chain_sync_bytes(int world, int grid) {
+  return align_up(static_cast<size_t>(world) * grid * sizeof(unsigned int), 256);
+}
+
+// One rank's steps against the kernel's limits; m_full[j] = rows of step j's full output.
+int check_chain_steps(const char* fn, const opc_chain_step* steps, int32_t n, int32_t batch, const DeviceCache& dc,
+                      const std::vector<int32_t>& m_full) {
+  for (int j = 0; j < n; ++j) {
+    const opc_chain_step& st = steps[j];
+    if (!st.layer || !plan_ok(&st.layer->plan)) return fail(OPC_ERR_INVALID, "%s: step %d: invalid layer", fn, j);
+    const opc_layer* L = st.layer;
+    const opc_layer_plan& p = L->plan;
+    if (!L->units || !L->codebooks || !L->tile_mask || !L->outlier_rows || !aligned(L->units, 16))
+      return fail(OPC_ERR_INVALID, "%s: step %d: layer buffers missing or misaligned", fn, j);
+    if (!st.x || !st.y || st.ldx < p.K || st.ldy < m_full[j] || !aligned(st.x, 2) || !aligned(st.y, 2))
+      return fail(OPC_ERR_INVALID, "%s: step %d: bad x/y (ldx=%lld K=%d ldy=%lld rows=%d)", fn, j,
+                  static_cast<long long>(st.ldx), p.K, static_cast<long long>(st.ldy), m_full[j]);
+    if (j > 0) {
+      const opc_chain_step& pv = steps[j - 1];
+      if (st.x != pv.y || st.ldx != pv.ldy || p.K > m_full[j - 1])
+        return fail(OPC_ERR_UNSUPPORTED,
+                    "%s: step %d: x must be the previous step's y (same pointer and leading dimension, K <= its "
+                    "rows)", fn, j);
+    }
+    if (p.row_tiles / dc.sm_count + 2 > opc::kChainSplitSlots)
+      return fail(OPC_ERR_UNSUPPORTED, "%s: step %d: %d row tiles exceed %d per SM", fn, j, p.row_tiles,
+                  opc::kChainSplitSlots - 2);
+    if (static_cast<int64_t>(batch) * p.K_pad > 64 * opc::kQConsumerThreads)
+      return fail(OPC_ERR_UNSUPPORTED, "%s: step %d: batch*K_pad = %lld > %d", fn, j,
+                  static_cast<long long>(batch) * p.K_pad, 64 * opc::kQConsumerThreads);
+    if (p.total_units >= (int64_t(1) << 31)) return fail(OPC_ERR_UNSUPPORTED, "%s: step %d: layer too large", fn, j);
+  }
+  return OPC_OK;
+}
+
+// Builds a chain from every rank's view (ranks[rank] is this process's own).  With own_scratch,
+// the flags and accumulators are allocated here (one GPU) and ranks[rank]'s pointers are set.
+int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t batch, int32_t rank, int32_t world,
+                std::vector<ChainRank>& ranks, bool own_scratch, opc_chain** out) {
   int dev = 0;
   OPC_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
   DeviceCache dc;
   int rc = device_cache(dev, &dc);
   if (rc != OPC_OK) return rc;
-  std::vector<opc::ChainLayer> hl(n_steps);
+  std::vector<int32_t> m_full(n, 0), row_off(n, 0);
+  for (int j = 0; j < n; ++j)
+    for (int p = 0; p < world; ++p) {
+      if (p < rank) row_off[j] += ranks[p].M[j];
+      m_full[j] += ranks[p].M[j];
+    }
+  rc = check_chain_steps(fn, steps, n, batch, dc, m_full);
+  if (rc != OPC_OK) return rc;
+
   int32_t kt_max = 1;
   int64_t bk_max = 0;
-  size_t acc_bytes = 0;
-  std::vector<size_t> acc_off(n_steps);
-  for (int j = 0; j < n_steps; ++j) {
+  for (int j = 0; j < n; ++j) {
+    kt_max = std::max(kt_max, steps[j].layer->plan.k_units);
+    bk_max = std::max<int64_t>(bk_max, static_cast<int64_t>(batch) * steps[j].layer->plan.K_pad);
+  }
+  const int xs = static_cast<int>(align_up(static_cast<size_t>(3 * batch) * opc::xsq_col_bytes(kt_max) + opc::kQZeroBytes, 128));
+  auto smem_for = [&](int stages) {
+    return static_cast<size_t>(xs) + static_cast<size_t>(opc::kQConsumers) * stages * (opc::kQChunkBytes + 16) +
+           sizeof(opc::ChainShared);
+  };
+  int stages = opc::kQMaxStages;
+  while (stages >= 2 && smem_for(stages) > static_cast<size_t>(dc.max_smem_optin)) --stages;
+  if (stages < 2) return fail(OPC_ERR_UNSUPPORTED, "%s: staged x too large for shared memory", fn);
+  const size_t smem = smem_for(stages);
+  const int xc = bk_max <= 4 * 8 * opc::kQConsumerThreads ? 4 : 8;
+  auto kern = xc == 4 ? opc::chain_kernel<4> : opc::chain_kernel<8>;
+  OPC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)),
+           "cudaFuncSetAttribute(max dynamic smem, chain)");
+  int per_sm = 0;
+  OPC_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, opc::kQThreads, smem),
+           "cudaOccupancyMaxActiveBlocksPerMultiprocessor(chain)");
+  if (per_sm < 1) return fail(OPC_ERR_UNSUPPORTED, "%s: chain kernel does not fit on an SM", fn);
+
+  // device image: [layers | outlier tables | flag masks | epoch (| flags | acc)]
+  const size_t layers_bytes = align_up(sizeof(opc::ChainLayer) * n, 256);
+  std::vector<size_t> oref_off(n), mask_off(n);
+  std::vector<int32_t> n_oref(n, 0);
+  size_t off = layers_bytes;
+  for (int j = 0; j < n; ++j) {
+    for (int p = 0; p < world; ++p) n_oref[j] += static_cast<int32_t>(ranks[p].slots[j].size());
+    oref_off[j] = off;
+    off += align_up(static_cast<size_t>(n_oref[j]) * sizeof(opc::OutlierRef), 256);
+  }
+  for (int j = 0; j < n; ++j) {
+    mask_off[j] = off;
+    off += align_up(static_cast<size_t>(ceil_div(m_full[j], 16)) * sizeof(uint16_t), 256);
+  }
+  const size_t epoch_off = off;
+  off += 256;
+  const size_t image_bytes = off;
+  const size_t sync_bytes = chain_sync_bytes(world, dc.sm_count);
+  size_t acc_total = 0;
+  for (int j = 0; j < n; ++j) acc_total += chain_acc_bytes(steps[j].layer->plan);
+  const size_t sync_off = off;
+  if (own_scratch) off += sync_bytes + acc_total;
+
+  void* mem = nullptr;
+  OPC_CUDA(cudaMalloc(&mem, off), "cudaMalloc(chain)");
+  char* base = static_cast<char*>(mem);
+  ChainRank& me = ranks[rank];
+  if (own_scratch) {
+    me.sync = reinterpret_cast<unsigned int*>(base + sync_off);
+    size_t a = sync_off + sync_bytes;
+    for (int j = 0; j < n; ++j) {
+      me.acc[j] = reinterpret_cast<unsigned long long*>(base + a);
+      a += chain_acc_bytes(steps[j].layer->plan);
+    }
+  }
+
+  std::vector<unsigned char> img(image_bytes, 0);
+  for (int j = 0; j < n; ++j) {
     const opc_chain_step& st = steps[j];
-    if (!st.layer || !plan_ok(&st.layer->plan)) return fail(OPC_ERR_INVALID, "opc_chain_create: step %d: invalid layer", j);
     const opc_layer* L = st.layer;
     const opc_layer_plan& p = L->plan;
-    if (!L->units || !L->codebooks || !L->tile_mask || !L->outlier_rows || !aligned(L->units, 16))
-      return fail(OPC_ERR_INVALID, "opc_chain_create: step %d: layer buffers missing or misaligned", j);
-    if (!st.x || !st.y || st.ldx < p.K || st.ldy < p.M || !aligned(st.x, 2) || !aligned(st.y, 2))
-      return fail(OPC_ERR_INVALID, "opc_chain_create: step %d: bad x/y (ldx=%lld K=%d ldy=%lld M=%d)", j,
-                  static_cast<long long>(st.ldx), p.K, static_cast<long long>(st.ldy), p.M);
-    if (j > 0) {
-      const opc_chain_step& pv = steps[j - 1];
-      if (st.x != pv.y || st.ldx != pv.ldy || p.K > pv.layer->plan.M)
-        return fail(OPC_ERR_UNSUPPORTED,
-                    "opc_chain_create: step %d: x must be the previous step's y (same pointer and leading "
-                    "dimension, K <= previous M)", j);
-    }
-    if (p.row_tiles / dc.sm_count + 2 > opc::kChainSplitSlots)
-      return fail(OPC_ERR_UNSUPPORTED, "opc_chain_create: step %d: %d row tiles exceed %d per SM", j, p.row_tiles,
-                  opc::kChainSplitSlots - 2);
-    if (static_cast<int64_t>(batch) * p.K_pad > 64 * opc::kQConsumerThreads)
-      return fail(OPC_ERR_UNSUPPORTED, "opc_chain_create: step %d: batch*K_pad = %lld > %d", j,
-                  static_cast<long long>(batch) * p.K_pad, 64 * opc::kQConsumerThreads);
-    if (p.total_units >= (int64_t(1) << 31)) return fail(OPC_ERR_UNSUPPORTED, "opc_chain_create: layer too large");
-    opc::ChainLayer& c = hl[j];
+    opc::ChainLayer c;
     memset(&c, 0, sizeof(c));
     c.units = static_cast<const uint8_t*>(L->units);
     c.ounits = ounits_q(L);
@@ -812,7 +921,10 @@ int opc_chain_create(const opc_chain_step* steps, int32_t n_steps, int32_t batch
     c.orow = L->outlier_rows;
     c.oexp = L->outlier_rows + n_slots_of(p);
     c.x = static_cast<const __half*>(st.x);
-    c.y = static_cast<__half*>(st.y);
+    c.acc = me.acc[j];
+    for (int q = 0; q < world; ++q) c.y_peer[q] = reinterpret_cast<__half*>(ranks[q].y[j]) + row_off[j];
+    c.oref = reinterpret_cast<const opc::OutlierRef*>(base + oref_off[j]);
+    c.mask_full = reinterpret_cast<const uint16_t*>(base + mask_off[j]);
     c.ldx = st.ldx;
     c.ldy = st.ldy;
     c.Up = static_cast<int32_t>(p.packed_units);
@@ -825,63 +937,264 @@ int opc_chain_create(const opc_chain_step* steps, int32_t n_steps, int32_t batch
     c.OT = p.outlier_tiles;
     c.KO = p.outlier_k_units;
     c.x_vec16 = (p.K % 8 == 0) && (st.ldx % 8 == 0) && aligned(st.x, 16);
-    kt_max = std::max(kt_max, p.k_units);
-    bk_max = std::max<int64_t>(bk_max, static_cast<int64_t>(batch) * p.K_pad);
-    acc_off[j] = acc_bytes;
-    acc_bytes += align_up(static_cast<size_t>(n_slots_of(p)) * opc::kQMaxBatch * sizeof(unsigned long long), 256);
+    c.n_oref = n_oref[j];
+    c.row_off = row_off[j];
+    c.m_full = m_full[j];
+    memcpy(img.data() + j * sizeof(opc::ChainLayer), &c, sizeof(c));
+    // every rank's outlier rows, in rank order, and their flags in the full output
+    opc::OutlierRef* refs = reinterpret_cast<opc::OutlierRef*>(img.data() + oref_off[j]);
+    uint16_t* mask = reinterpret_cast<uint16_t*>(img.data() + mask_off[j]);
+    int32_t k = 0, roff = 0;
+    for (int q = 0; q < world; ++q) {
+      for (const OutlierSlot& s : ranks[q].slots[j]) {
+        if (s.row < 0 || s.row >= ranks[q].M[j] || s.slot < 0) {
+          cudaFree(mem);
+          return fail(OPC_ERR_INVALID, "%s: step %d: rank %d: outlier row %d outside its %d rows", fn, j, q, s.row,
+                      ranks[q].M[j]);
+        }
+        opc::OutlierRef& r = refs[k++];
+        r.acc = ranks[q].acc[j] + 2 * static_cast<int64_t>(s.slot);
+        r.row = roff + s.row;
+        r.exp = s.exp;
+        r.owner = q;
+        r.pad = 0;
+        mask[r.row >> 4] = static_cast<uint16_t>(mask[r.row >> 4] | (1u << (r.row & 15)));
+      }
+      roff += ranks[q].M[j];
+    }
   }
-  const int xs = static_cast<int>(align_up(static_cast<size_t>(3 * batch) * opc::xsq_col_bytes(kt_max) + opc::kQZeroBytes, 128));
-  auto smem_for = [&](int stages) {
-    return static_cast<size_t>(xs) + static_cast<size_t>(opc::kQConsumers) * stages * (opc::kQChunkBytes + 16) +
-           sizeof(opc::ChainShared);
-  };
-  int stages = opc::kQMaxStages;
-  while (stages >= 2 && smem_for(stages) > static_cast<size_t>(dc.max_smem_optin)) --stages;
-  if (stages < 2) return fail(OPC_ERR_UNSUPPORTED, "opc_chain_create: staged x too large for shared memory");
-  const size_t smem = smem_for(stages);
-  const int xc = bk_max <= 4 * 8 * opc::kQConsumerThreads ? 4 : 8;
-  auto kern = xc == 4 ? opc::chain_kernel<4> : opc::chain_kernel<8>;
-  OPC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)),
-           "cudaFuncSetAttribute(max dynamic smem, chain)");
-  int per_sm = 0;
-  OPC_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, opc::kQThreads, smem),
-           "cudaOccupancyMaxActiveBlocksPerMultiprocessor(chain)");
-  if (per_sm < 1) return fail(OPC_ERR_UNSUPPORTED, "opc_chain_create: chain kernel does not fit on an SM");
-  if (dc.sm_count > opc::kQConsumerThreads)
-    return fail(OPC_ERR_UNSUPPORTED, "opc_chain_create: %d SMs exceed the barrier's %d pollers", dc.sm_count,
-                opc::kQConsumerThreads);
-
-  const size_t layers_bytes = align_up(sizeof(opc::ChainLayer) * n_steps, 256);
-  const size_t sync_bytes = align_up(static_cast<size_t>(dc.sm_count) * sizeof(unsigned int), 256);
+  cudaError_t e = cudaMemcpy(base, img.data(), image_bytes, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemset(me.sync, 0, sync_bytes);
+  if (e == cudaSuccess) e = cudaMemset(me.acc[0], 0, acc_total);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    cudaFree(mem);
+    return cuda_fail(e, "chain setup copy");
+  }
   opc_chain* ch = new opc_chain();
   ch->device = dev;
-  ch->n_layers = n_steps;
+  ch->n_layers = n;
   ch->batch = batch;
   ch->stages = stages;
   ch->xs_bytes = xs;
   ch->smem = smem;
   ch->grid = dc.sm_count;
   ch->xc = xc;
-  ch->clear_bytes = sync_bytes + acc_bytes;
-  cudaError_t e = cudaMalloc(&ch->dev_mem, layers_bytes + sync_bytes + acc_bytes);
-  if (e != cudaSuccess) {
-    delete ch;
-    return cuda_fail(e, "cudaMalloc(chain)");
-  }
-  char* base = static_cast<char*>(ch->dev_mem);
+  ch->rank = rank;
+  ch->world = world;
+  ch->dev_mem = mem;
   ch->d_layers = reinterpret_cast<opc::ChainLayer*>(base);
-  ch->d_sync = reinterpret_cast<unsigned int*>(base + layers_bytes);
-  unsigned long long* acc = reinterpret_cast<unsigned long long*>(base + layers_bytes + sync_bytes);
-  for (int j = 0; j < n_steps; ++j) hl[j].acc = reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(acc) + acc_off[j]);
-  e = cudaMemcpy(ch->d_layers, hl.data(), sizeof(opc::ChainLayer) * n_steps, cudaMemcpyHostToDevice);
-  if (e == cudaSuccess) e = cudaMemset(ch->d_sync, 0, ch->clear_bytes);
-  if (e != cudaSuccess) {
-    cudaFree(ch->dev_mem);
-    delete ch;
-    return cuda_fail(e, "chain setup copy");
-  }
+  ch->d_sync = me.sync;
+  for (int q = 0; q < world; ++q) ch->sync_peer[q] = ranks[q].sync;
+  ch->d_epoch = reinterpret_cast<unsigned int*>(base + epoch_off);
+  ch->acc = me.acc[0];
+  ch->acc_bytes = acc_total;
   *out = ch;
   return OPC_OK;
+}
+
+// Exchanged description of one rank's shards (opc_chain_tp_info).
+constexpr uint32_t kTpInfoMagic = 0x4f504354u;  // "OPCT"
+struct TpInfoHeader {
+  uint32_t magic, version;
+  int32_t n_steps, grid, batch, world;
+  uint64_t region_bytes, scratch_offset, total_bytes;
+};
+struct TpInfoStep {
+  int32_t M, K, n_out, pad;
+  uint64_t y_offset, acc_offset;
+  int64_t ldy;
+};
+
+}  // namespace
+
+extern "C" {
+
+int opc_chain_create(const opc_chain_step* steps, int32_t n_steps, int32_t batch, opc_chain** out) {
+  if (!out) return fail(OPC_ERR_INVALID, "opc_chain_create: out is NULL");
+  *out = nullptr;
+  if (!steps || n_steps < 1) return fail(OPC_ERR_INVALID, "opc_chain_create: no steps");
+  if (batch < 1 || batch > opc::kQMaxBatch)
+    return fail(OPC_ERR_UNSUPPORTED, "opc_chain_create: batch %d (the chain runs batch 1..%d)", batch, opc::kQMaxBatch);
+  std::vector<ChainRank> ranks(1);
+  ChainRank& me = ranks[0];
+  me.M.resize(n_steps);
+  me.slots.resize(n_steps);
+  me.y.resize(n_steps);
+  me.acc.resize(n_steps, nullptr);
+  for (int j = 0; j < n_steps; ++j) {
+    if (!steps[j].layer || !plan_ok(&steps[j].layer->plan) || !steps[j].layer->outlier_rows)
+      return fail(OPC_ERR_INVALID, "opc_chain_create: step %d: invalid layer", j);
+    me.M[j] = steps[j].layer->plan.M;
+    me.y[j] = static_cast<char*>(steps[j].y);
+    const int rc = read_outlier_slots(steps[j].layer, &me.slots[j]);
+    if (rc != OPC_OK) return rc;
+  }
+  return chain_build("opc_chain_create", steps, n_steps, batch, 0, 1, ranks, true, out);
+}
+
+int opc_chain_tp_scratch_bytes(const opc_chain_step* steps, int32_t n_steps, int32_t world, size_t* bytes) {
+  if (!bytes) return fail(OPC_ERR_INVALID, "opc_chain_tp_scratch_bytes: bytes is NULL");
+  *bytes = 0;
+  if (!steps || n_steps < 1) return fail(OPC_ERR_INVALID, "opc_chain_tp_scratch_bytes: no steps");
+  if (world < 1 || world > opc::kMaxRanks)
+    return fail(OPC_ERR_UNSUPPORTED, "opc_chain_tp_scratch_bytes: world %d (1..%d)", world, opc::kMaxRanks);
+  int dev = 0;
+  OPC_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  DeviceCache dc;
+  const int rc = device_cache(dev, &dc);
+  if (rc != OPC_OK) return rc;
+  size_t b = chain_sync_bytes(world, dc.sm_count);
+  for (int j = 0; j < n_steps; ++j) {
+    if (!steps[j].layer || !plan_ok(&steps[j].layer->plan))
+      return fail(OPC_ERR_INVALID, "opc_chain_tp_scratch_bytes: step %d: invalid layer", j);
+    b += chain_acc_bytes(steps[j].layer->plan);
+  }
+  *bytes = b;
+  return OPC_OK;
+}
+
+int opc_chain_tp_info(const opc_chain_step* steps, int32_t n_steps, int32_t batch, int32_t world, const void* region,
+                      size_t region_bytes, size_t scratch_offset, void* info, size_t* info_bytes) {
+  if (!info_bytes) return fail(OPC_ERR_INVALID, "opc_chain_tp_info: info_bytes is NULL");
+  if (!steps || n_steps < 1 || !region) return fail(OPC_ERR_INVALID, "opc_chain_tp_info: no steps or region");
+  if (batch < 1 || batch > opc::kQMaxBatch) return fail(OPC_ERR_UNSUPPORTED, "opc_chain_tp_info: batch %d", batch);
+  if (world < 1 || world > opc::kMaxRanks) return fail(OPC_ERR_UNSUPPORTED, "opc_chain_tp_info: world %d", world);
+  size_t scratch = 0;
+  int rc = opc_chain_tp_scratch_bytes(steps, n_steps, world, &scratch);
+  if (rc != OPC_OK) return rc;
+  if (scratch_offset % 256 || scratch_offset + scratch > region_bytes)
+    return fail(OPC_ERR_INVALID, "opc_chain_tp_info: scratch [%zu, +%zu) not 256-aligned inside the %zu-byte region",
+                scratch_offset, scratch, region_bytes);
+  std::vector<std::vector<OutlierSlot>> slots(n_steps);
+  size_t need = sizeof(TpInfoHeader) + sizeof(TpInfoStep) * n_steps;
+  for (int j = 0; j < n_steps; ++j) {
+    rc = read_outlier_slots(steps[j].layer, &slots[j]);
+    if (rc != OPC_OK) return rc;
+    need += slots[j].size() * sizeof(OutlierSlot);
+  }
+  if (!info) {
+    *info_bytes = need;
+    return OPC_OK;
+  }
+  if (*info_bytes < need) return fail(OPC_ERR_INVALID, "opc_chain_tp_info: %zu bytes given, %zu needed", *info_bytes, need);
+  int dev = 0;
+  OPC_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  DeviceCache dc;
+  rc = device_cache(dev, &dc);
+  if (rc != OPC_OK) return rc;
+  unsigned char* o = static_cast<unsigned char*>(info);
+  TpInfoHeader h;
+  memset(&h, 0, sizeof(h));
+  h.magic = kTpInfoMagic;
+  h.version = 1;
+  h.n_steps = n_steps;
+  h.grid = dc.sm_count;
+  h.batch = batch;
+  h.world = world;
+  h.region_bytes = region_bytes;
+  h.scratch_offset = scratch_offset;
+  h.total_bytes = need;
+  memcpy(o, &h, sizeof(h));
+  size_t acc = scratch_offset + chain_sync_bytes(world, dc.sm_count);
+  size_t tail = sizeof(TpInfoHeader) + sizeof(TpInfoStep) * n_steps;
+  const char* rb = static_cast<const char*>(region);
+  for (int j = 0; j < n_steps; ++j) {
+    const char* y = static_cast<const char*>(steps[j].y);
+    if (!y || y < rb || y >= rb + region_bytes)
+      return fail(OPC_ERR_INVALID, "opc_chain_tp_info: step %d: y is not inside the region", j);
+    TpInfoStep s;
+    memset(&s, 0, sizeof(s));
+    s.M = steps[j].layer->plan.M;
+    s.K = steps[j].layer->plan.K;
+    s.n_out = static_cast<int32_t>(slots[j].size());
+    s.y_offset = static_cast<uint64_t>(y - rb);
+    s.acc_offset = acc;
+    s.ldy = steps[j].ldy;
+    acc += chain_acc_bytes(steps[j].layer->plan);
+    memcpy(o + sizeof(TpInfoHeader) + j * sizeof(TpInfoStep), &s, sizeof(s));
+    if (!slots[j].empty()) memcpy(o + tail, slots[j].data(), slots[j].size() * sizeof(OutlierSlot));
+    tail += slots[j].size() * sizeof(OutlierSlot);
+  }
+  *info_bytes = need;
+  return OPC_OK;
+}
+
+int opc_chain_create_tp(const opc_chain_step* steps, int32_t n_steps, int32_t batch, int32_t rank, int32_t world,
+                        void* const* regions, const void* const* infos, opc_chain** out) {
+  const char* fn = "opc_chain_create_tp";
+  if (!out) return fail(OPC_ERR_INVALID, "%s: out is NULL", fn);
+  *out = nullptr;
+  if (!steps || n_steps < 1 || !regions || !infos) return fail(OPC_ERR_INVALID, "%s: missing arguments", fn);
+  if (batch < 1 || batch > opc::kQMaxBatch) return fail(OPC_ERR_UNSUPPORTED, "%s: batch %d", fn, batch);
+  if (world < 1 || world > opc::kMaxRanks || rank < 0 || rank >= world)
+    return fail(OPC_ERR_UNSUPPORTED, "%s: rank %d of world %d (1..%d ranks)", fn, rank, world, opc::kMaxRanks);
+  std::vector<ChainRank> ranks(world);
+  int32_t grid = -1;
+  for (int p = 0; p < world; ++p) {
+    const unsigned char* b = static_cast<const unsigned char*>(infos[p]);
+    if (!b || !regions[p]) return fail(OPC_ERR_INVALID, "%s: rank %d: no info or region", fn, p);
+    TpInfoHeader h;
+    memcpy(&h, b, sizeof(h));
+    if (h.magic != kTpInfoMagic || h.version != 1) return fail(OPC_ERR_INVALID, "%s: rank %d: not a chain info", fn, p);
+    if (h.n_steps != n_steps || h.batch != batch || h.world != world)
+      return fail(OPC_ERR_INVALID, "%s: rank %d: %d steps, batch %d, world %d (here %d, %d, %d)", fn, p, h.n_steps,
+                  h.batch, h.world, n_steps, batch, world);
+    if (grid >= 0 && h.grid != grid) return fail(OPC_ERR_UNSUPPORTED, "%s: ranks run %d and %d CTAs", fn, grid, h.grid);
+    grid = h.grid;
+    ChainRank& r = ranks[p];
+    r.M.resize(n_steps);
+    r.slots.resize(n_steps);
+    r.y.resize(n_steps);
+    r.acc.resize(n_steps);
+    char* region = static_cast<char*>(regions[p]);
+    r.sync = reinterpret_cast<unsigned int*>(region + h.scratch_offset);
+    size_t tail = sizeof(TpInfoHeader) + sizeof(TpInfoStep) * n_steps;
+    for (int j = 0; j < n_steps; ++j) {
+      TpInfoStep s;
+      memcpy(&s, b + sizeof(TpInfoHeader) + j * sizeof(TpInfoStep), sizeof(s));
+      if (s.K != steps[j].layer->plan.K)
+        return fail(OPC_ERR_INVALID, "%s: rank %d step %d: K %d, here %d", fn, p, j, s.K, steps[j].layer->plan.K);
+      if (s.M < 1 || s.n_out < 0 || s.y_offset % 2 || s.acc_offset % 256 || s.acc_offset >= h.region_bytes ||
+          s.y_offset >= h.region_bytes)
+        return fail(OPC_ERR_INVALID, "%s: rank %d step %d: bad shard description", fn, p, j);
+      r.M[j] = s.M;
+      r.y[j] = region + s.y_offset;
+      r.acc[j] = reinterpret_cast<unsigned long long*>(region + s.acc_offset);
+      r.slots[j].resize(s.n_out);
+      if (s.n_out) memcpy(r.slots[j].data(), b + tail, s.n_out * sizeof(OutlierSlot));
+      tail += s.n_out * sizeof(OutlierSlot);
+    }
+    if (tail != h.total_bytes) return fail(OPC_ERR_INVALID, "%s: rank %d: info size mismatch", fn, p);
+    // every rank's copy of each full output lies inside its region
+    for (int j = 0; j < n_steps; ++j) {
+      TpInfoStep s;
+      memcpy(&s, b + sizeof(TpInfoHeader) + j * sizeof(TpInfoStep), sizeof(s));
+      int64_t rows = 0;
+      for (int q = 0; q < world; ++q) {
+        TpInfoStep sq;
+        memcpy(&sq, static_cast<const unsigned char*>(infos[q]) + sizeof(TpInfoHeader) + j * sizeof(TpInfoStep), sizeof(sq));
+        rows += sq.M;
+      }
+      const uint64_t end = s.y_offset + 2 * static_cast<uint64_t>((batch - 1) * s.ldy + rows);
+      if (s.ldy < rows || end > h.region_bytes)
+        return fail(OPC_ERR_INVALID, "%s: rank %d step %d: full output (%lld rows, ld %lld) exceeds its region", fn, p, j,
+                    static_cast<long long>(rows), static_cast<long long>(s.ldy));
+    }
+  }
+  ChainRank& me = ranks[rank];
+  for (int j = 0; j < n_steps; ++j) {
+    if (!steps[j].layer || !plan_ok(&steps[j].layer->plan) || steps[j].layer->plan.M != me.M[j] ||
+        static_cast<char*>(steps[j].y) != me.y[j])
+      return fail(OPC_ERR_INVALID, "%s: step %d: does not match this rank's info", fn, j);
+  }
+  int dev = 0;
+  OPC_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  DeviceCache dc;
+  const int rc = device_cache(dev, &dc);
+  if (rc != OPC_OK) return rc;
+  if (dc.sm_count != grid) return fail(OPC_ERR_UNSUPPORTED, "%s: this GPU has %d SMs, the ranks %d", fn, dc.sm_count, grid);
+  return chain_build(fn, steps, n_steps, batch, rank, world, ranks, false, out);
 }
 
 int opc_chain_launch(opc_chain* ch, void* stream_v) {
@@ -890,11 +1203,13 @@ int opc_chain_launch(opc_chain* ch, void* stream_v) {
   OPC_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
   if (dev != ch->device) return fail(OPC_ERR_INVALID, "opc_chain_launch: chain lives on device %d, current is %d", ch->device, dev);
   cudaStream_t s = static_cast<cudaStream_t>(stream_v);
-  OPC_CUDA(cudaMemsetAsync(ch->d_sync, 0, ch->clear_bytes, s), "cudaMemsetAsync(chain scratch)");
+  OPC_CUDA(cudaMemsetAsync(ch->acc, 0, ch->acc_bytes, s), "cudaMemsetAsync(chain accumulators)");
   opc::ChainArgs a;
   memset(&a, 0, sizeof(a));
   a.layers = ch->d_layers;
   a.sync = ch->d_sync;
+  for (int p = 0; p < ch->world; ++p) a.sync_peer[p] = ch->sync_peer[p];
+  a.epoch = ch->d_epoch;
   a.trace = ch->trace;
   a.n_layers = ch->n_layers;
   a.batch = ch->batch;
@@ -902,6 +1217,8 @@ int opc_chain_launch(opc_chain* ch, void* stream_v) {
   a.xs_bytes = ch->xs_bytes;
   a.negz = opc::kNegZero2;
   a.l2_prefetch = ch->l2_prefetch;
+  a.rank = ch->rank;
+  a.world = ch->world;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(ch->grid));
   cfg.blockDim = dim3(opc::kQThreads);
@@ -951,6 +1268,50 @@ int opc_chain_destroy(opc_chain* ch) {
   cudaSetDevice(prev);
   delete ch;
   if (e != cudaSuccess) return cuda_fail(e, "cudaFree(chain)");
+  return OPC_OK;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Peer-visible memory through CUDA IPC (one process per GPU).
+// ---------------------------------------------------------------------------------------------
+static_assert(sizeof(cudaIpcMemHandle_t) == OPC_PEER_HANDLE_BYTES, "IPC handle size");
+
+int opc_peer_alloc(size_t bytes, void** ptr, void* handle) {
+  if (!ptr || !handle || bytes == 0) return fail(OPC_ERR_INVALID, "opc_peer_alloc: bad arguments");
+  *ptr = nullptr;
+  void* p = nullptr;
+  OPC_CUDA(cudaMalloc(&p, bytes), "cudaMalloc(peer region)");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaMemset(p, 0, bytes);
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "opc_peer_alloc");
+  }
+  memcpy(handle, &h, sizeof(h));
+  *ptr = p;
+  return OPC_OK;
+}
+
+int opc_peer_open(const void* handle, void** ptr) {
+  if (!ptr || !handle) return fail(OPC_ERR_INVALID, "opc_peer_open: bad arguments");
+  *ptr = nullptr;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  OPC_CUDA(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+  return OPC_OK;
+}
+
+int opc_peer_close(void* ptr) {
+  if (!ptr) return OPC_OK;
+  OPC_CUDA(cudaIpcCloseMemHandle(ptr), "cudaIpcCloseMemHandle");
+  return OPC_OK;
+}
+
+int opc_peer_free(void* ptr) {
+  if (!ptr) return OPC_OK;
+  OPC_CUDA(cudaFree(ptr), "cudaFree(peer region)");
   return OPC_OK;
 }
 

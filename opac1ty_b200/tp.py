@@ -17,15 +17,23 @@ shorter, its padding lies past row M and is never read.
 
 The chain logic (``tp_chain_step``) takes the GEMV and the all-gather as callables, so the same
 code runs with the CUDA library and NCCL on GPUs and with a CPU GEMV and gloo in the tests.
+That per-projection GEMV + all-gather form is the baseline.
+
+``TPChain`` runs the same sharded step (batch 1..2) as ONE persistent kernel per rank
+(``opc_chain_create_tp``): every rank stores its output rows straight into every rank's copy of
+the full activations through CUDA IPC peer pointers, and a barrier over peer flags separates the
+projections, so there is neither an all-gather nor a launch per projection.
 """
 
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass, field
 from typing import Callable, Dict, List, Optional, Sequence, Tuple
 
 import torch
 
+from . import _lib
 from . import decode as D
 from . import layer as L
 from . import synthetic
@@ -138,6 +146,7 @@ class TPDecodeStack:
     group: object = None
     graph: Optional[torch.cuda.CUDAGraph] = None
     bufs: Dict[str, torch.Tensor] = field(default_factory=dict)
+    chain: object = None   # TPChain once enable_chain() ran: one kernel per step, no all-gathers
 
     @staticmethod
     def _shard_block(fused: Dict[str, dict], rank: int, world: int, batch: int, device) -> Dict[str, ShardedProj]:
@@ -201,7 +210,26 @@ class TPDecodeStack:
         return sum(dl.algorithmic_bytes(self.batch) for dl in self.layers())
 
     def launches_per_step(self) -> int:
-        return 4 * len(self.blocks)
+        return 1 if self.chain is not None else 4 * len(self.blocks)
+
+    def enable_chain(self, **kw) -> "TPChain":
+        """Collective: run every step as one fused kernel per rank (TPChain, batch 1..2);
+        bufs["x"] becomes the chain's input/output buffer (current contents carried over)."""
+        ch = TPChain(self, **kw)
+        ch.x.copy_(self.bufs["x"])
+        self.chain = ch
+        self.bufs["x"] = ch.x
+        self.graph = None
+        return ch
+
+    def close(self):
+        """Collective: release the fused chain (if any) before the process group goes away."""
+        self.graph = None
+        if self.chain is not None:
+            x = self.bufs["x"].clone()
+            self.chain.close()
+            self.chain = None
+            self.bufs["x"] = x
 
     def _gemv(self, dl, x, out):
         L.gemv(dl, x, out=out, workspace=self.workspace)
@@ -212,6 +240,9 @@ class TPDecodeStack:
         dist.all_gather_into_tensor(out, inp.reshape(-1), group=self.group)
 
     def step_eager(self):
+        if self.chain is not None:
+            self.chain.launch()
+            return self.bufs["x"]
         x = tp_chain_step(self.bufs["x"], self.blocks, self.hidden, self.intermediate, self.world,
                           self._gemv, self._all_gather)
         self.bufs["x"].copy_(x)
@@ -234,3 +265,208 @@ class TPDecodeStack:
             return self.step_eager()
         self.graph.replay()
         return self.bufs["x"]
+
+
+# ---------------------------------------------------------------------------------------------
+# The same row-sharded step as ONE persistent kernel per rank (opc_chain_create_tp): each rank
+# stores its rows of every projection straight into every rank's copy of the full output over
+# NVLink and a cross-rank barrier over peer flags separates the projections, so the step has no
+# all-gather launch and no NCCL call.
+# ---------------------------------------------------------------------------------------------
+
+PROJ_ORDER = ("qkv", "o", "gate_up", "down")
+
+
+class _DevicePtr:
+    """A device pointer as seen by ``torch.as_tensor`` (CUDA array interface, no ownership)."""
+
+    def __init__(self, ptr: int, shape, typestr: str = "<f2"):
+        self.__cuda_array_interface__ = {"shape": tuple(int(s) for s in shape), "typestr": typestr,
+                                         "data": (int(ptr), False), "version": 2}
+
+
+def device_view(ptr: int, shape, device) -> torch.Tensor:
+    """fp16 tensor of ``shape`` over device memory at ``ptr`` (not owned: keep the memory alive)."""
+    t = torch.as_tensor(_DevicePtr(ptr, shape), device=device)
+    if t.data_ptr() != int(ptr) or t.dtype != torch.float16:
+        raise RuntimeError("device_view: torch did not map the pointer as fp16")
+    return t
+
+
+def chain_region_layout(rows: Sequence[int], batch: int, scratch_bytes: int,
+                        align: int = 256) -> Tuple[List[int], List[int], int, int]:
+    """Layout of one rank's peer-visible region for a row-sharded chain: step j's full output
+    [batch][ld_j] fp16 (ld_j = rows rounded up to 8 halves, 16-byte rows) at offsets[j], then the
+    chain scratch.  Returns (offsets, lds, scratch_offset, total_bytes); every offset is a
+    multiple of ``align``.  Identical on every rank (it depends on the full row counts only)."""
+    if batch < 1 or scratch_bytes < 0 or align < 16 or align % 16:
+        raise ValueError("chain_region_layout: bad arguments")
+
+    def up(v: int) -> int:
+        return -(-v // align) * align
+
+    offsets, lds, off = [], [], 0
+    for m in rows:
+        if m < 1:
+            raise ValueError(f"chain_region_layout: step with {m} rows")
+        ld = -(-int(m) // 8) * 8
+        offsets.append(off)
+        lds.append(ld)
+        off = up(off + 2 * batch * ld)
+    scratch_offset = off
+    return offsets, lds, scratch_offset, up(scratch_offset + scratch_bytes)
+
+
+class PeerRegion:
+    """``nbytes`` of device memory on this rank, mapped into every rank's process by CUDA IPC
+    (opc_peer_alloc / opc_peer_open).  ``bases[p]`` is rank p's region as seen here."""
+
+    def __init__(self, nbytes: int, rank: int, world: int, all_gather_obj: Callable, device):
+        lib = _lib.load()
+        self.device = device
+        self.nbytes = int(nbytes)
+        self.rank = rank
+        self.local = ctypes.c_void_p()
+        self._opened: List[ctypes.c_void_p] = []
+        handle = (ctypes.c_ubyte * _lib.OPC_PEER_HANDLE_BYTES)()
+        with torch.cuda.device(device):
+            _lib.check(lib.opc_peer_alloc(self.nbytes, ctypes.byref(self.local), handle))
+        try:
+            handles = all_gather_obj(bytes(handle))
+            if len(handles) != world:
+                raise RuntimeError(f"PeerRegion: {len(handles)} handles for world {world}")
+            self.bases: List[int] = []
+            with torch.cuda.device(device):
+                for p, h in enumerate(handles):
+                    if p == rank:
+                        self.bases.append(int(self.local.value))
+                        continue
+                    buf = (ctypes.c_ubyte * len(h)).from_buffer_copy(h)
+                    ptr = ctypes.c_void_p()
+                    _lib.check(lib.opc_peer_open(buf, ctypes.byref(ptr)))
+                    self._opened.append(ptr)
+                    self.bases.append(int(ptr.value))
+        except Exception:
+            self.close_peers()
+            self.free()
+            raise
+
+    def close_peers(self):
+        lib = _lib.load()
+        with torch.cuda.device(self.device):
+            for ptr in self._opened:
+                lib.opc_peer_close(ptr)
+        self._opened = []
+
+    def free(self):
+        if self.local.value:
+            with torch.cuda.device(self.device):
+                _lib.load().opc_peer_free(self.local)
+            self.local = ctypes.c_void_p()
+
+
+class TPChain:
+    """One decode step of a TPDecodeStack (batch 1..2) as one persistent kernel per rank.
+
+    ``x`` is the step's input and output (this rank's copy of the last down projection's full
+    output): write the initial activations into it on every rank, then call ``step()`` on every
+    rank once per decode step.  Results equal ``TPDecodeStack.step_eager`` bit for bit.
+    ``all_gather_obj(obj) -> [obj of rank 0, ...]`` and ``barrier()`` default to
+    torch.distributed on the stack's group."""
+
+    def __init__(self, stack: "TPDecodeStack", all_gather_obj: Optional[Callable] = None,
+                 barrier: Optional[Callable] = None):
+        import torch.distributed as dist
+
+        if all_gather_obj is None:
+            def all_gather_obj(obj):
+                out = [None] * stack.world
+                dist.all_gather_object(out, obj, group=stack.group)
+                return out
+        if barrier is None:
+            def barrier():
+                dist.barrier(group=stack.group)
+        self._barrier = barrier
+        self.stack = stack
+        self.device = stack.device
+        self.batch = stack.batch
+        projs = [blk[name] for blk in stack.blocks for name in PROJ_ORDER]
+        if any(p.layer is None for p in projs):
+            raise ValueError("TPChain: every rank needs a non-empty shard of every projection")
+        n = len(projs)
+        lib = _lib.load()
+        arr = (_lib.ChainStep * n)()
+        for j, p in enumerate(projs):
+            arr[j].layer = ctypes.pointer(p.layer.c_layer)
+        scratch = ctypes.c_size_t(0)
+        with torch.cuda.device(self.device):
+            _lib.check(lib.opc_chain_tp_scratch_bytes(arr, n, stack.world, ctypes.byref(scratch)))
+        rows = [p.M for p in projs]
+        offs, lds, soff, total = chain_region_layout(rows, self.batch, scratch.value)
+        self.region = PeerRegion(total, stack.rank, stack.world, all_gather_obj, self.device)
+        self._handle = ctypes.c_void_p()
+        try:
+            base = self.region.bases[stack.rank]
+            for j in range(n):
+                arr[j].y = base + offs[j]
+                arr[j].ldy = lds[j]
+                arr[j].x = base + offs[j - 1]  # step 0 reads the last step's output
+                arr[j].ldx = lds[j - 1]
+            with torch.cuda.device(self.device):
+                need = ctypes.c_size_t(0)
+                _lib.check(lib.opc_chain_tp_info(arr, n, self.batch, stack.world, base, total, soff, None,
+                                                 ctypes.byref(need)))
+                info = (ctypes.c_ubyte * need.value)()
+                _lib.check(lib.opc_chain_tp_info(arr, n, self.batch, stack.world, base, total, soff, info,
+                                                 ctypes.byref(need)))
+            infos = all_gather_obj(bytes(info))
+            self._infos = [(ctypes.c_ubyte * len(b)).from_buffer_copy(b) for b in infos]
+            info_ptrs = (ctypes.c_void_p * stack.world)(*[ctypes.addressof(b) for b in self._infos])
+            regions = (ctypes.c_void_p * stack.world)(*self.region.bases)
+            with torch.cuda.device(self.device):
+                rc = lib.opc_chain_create_tp(arr, n, self.batch, stack.rank, stack.world, regions, info_ptrs,
+                                             ctypes.byref(self._handle))
+            # every rank learns every rank's outcome before anyone launches
+            oks = all_gather_obj(rc == 0)
+            _lib.check(rc)
+            if not all(oks):
+                raise RuntimeError("TPChain: opc_chain_create_tp failed on another rank")
+            barrier()
+        except Exception:
+            self._destroy_chain()
+            self.region.close_peers()
+            self.region.free()
+            raise
+        self._steps = arr
+        self.n_steps = n
+        self.outputs = [device_view(base + offs[j], (self.batch, lds[j]), self.device)[:, :rows[j]] for j in range(n)]
+        self.x = self.outputs[-1]
+
+    def launch(self):
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        _lib.check(_lib.load().opc_chain_launch(self._handle, stream))
+
+    def step(self) -> torch.Tensor:
+        self.launch()
+        return self.x
+
+    def _destroy_chain(self):
+        if self._handle.value:
+            with torch.cuda.device(self.device):
+                _lib.load().opc_chain_destroy(self._handle)
+            self._handle = ctypes.c_void_p()
+
+    def close(self):
+        """Collective: every rank calls it.  Waits for the ranks' launches, then unmaps the peers
+        and frees this rank's region once no rank maps it any more."""
+        if self.region is None:
+            return
+        torch.cuda.synchronize(self.device)
+        self._barrier()
+        self._destroy_chain()
+        self.region.close_peers()
+        self._barrier()
+        self.region.free()
+        self.region = None
+        self.outputs = []
+        self.x = None

@@ -142,3 +142,17 @@ def test_tp_chain_two_ranks_matches_unsharded(tmp_path, batch):
     y, ref = np.load(out)
     assert y.shape == (batch, CFG["hidden"])
     np.testing.assert_array_equal(y.view(np.uint16), ref.view(np.uint16))
+
+
+def test_chain_region_layout():
+    rows = [6144, 4096, 28672, 4096, 200]
+    offs, lds, soff, total = tp.chain_region_layout(rows, 2, 1000)
+    assert lds == [6144, 4096, 28672, 4096, 200]
+    assert all(o % 256 == 0 for o in offs) and soff % 256 == 0 and total % 256 == 0
+    ends = [o + 2 * 2 * ld for o, ld in zip(offs, lds)]
+    assert all(e <= n for e, n in zip(ends, offs[1:] + [soff]))   # outputs never overlap
+    assert total >= soff + 1000
+    _, lds2, _, _ = tp.chain_region_layout([13, 17], 1, 0)
+    assert lds2 == [16, 24]                                       # 16-byte rows
+    with pytest.raises(ValueError):
+        tp.chain_region_layout([0], 1, 0)
