@@ -183,19 +183,23 @@ int opc_gemm(const opc_layer* layer, const void* x, int64_t ldx, void* y, int64_
              void* stream);
 
 /* Decode chain: a sequence of dependent GEMVs run by ONE persistent cooperative kernel (one CTA
- * per SM; a producer warp streams every step's weights ahead across step boundaries; a grid
- * barrier between steps).  Replaces per-step dispatch of MetalKernelManager.dequant_gemv for
+ * per SM; a producer warp streams every step's weights ahead across step boundaries; no grid
+ * barrier between steps: every output element is also published as a tagged 32-bit word that
+ * the next step's readers poll).  Replaces per-step dispatch of MetalKernelManager.dequant_gemv for
  * a forward pass (runtime/src/inference.c:117-233 calls one layer at a time).  Each step is the
  * batch 1..2 integer GEMV of opc_gemv; results equal opc_gemv's bit for bit.
  *   steps[0].x      the chain input (device fp16, ldx)
  *   steps[j].x      for j >= 1 must be steps[j-1].y with the same leading dimension (a prefix:
  *                   steps[j].layer K <= steps[j-1].layer M)
- * Requires batch 1..2 and batch * K_pad <= 30720 for every step.  opc_chain_create copies the
- * step list to the device and allocates the chain's scratch (freed by opc_chain_destroy);
- * opc_chain_launch clears the outlier accumulators and launches on `stream` (capturable into a
- * CUDA graph).  One chain must not run on two streams at once.  A launch whose barrier wait
- * gives up (2 s) records device error 3 and poisons the chain: every later launch records error
- * 4 and does nothing; destroy and recreate it. */
+ *   steps[j].y      fp16 outputs of two steps are either disjoint or the same buffer (same
+ *                   pointer and leading dimension: only the later step's values are stored);
+ *                   step 0's output may not overlap the chain input, later ones may
+ * Requires batch 1..2, batch * K_pad <= 30720 for every step and fewer than 65535 steps.
+ * opc_chain_create copies the step list to the device and allocates the chain's scratch (freed
+ * by opc_chain_destroy); opc_chain_launch launches on `stream` (one kernel, nothing to clear;
+ * capturable into a CUDA graph).  One chain must not run on two streams at once.  A launch
+ * whose bounded wait gives up (2 s) records device error 3 and poisons the chain: every later
+ * launch records error 4 and does nothing; destroy and recreate it. */
 typedef struct opc_chain opc_chain;
 typedef struct opc_chain_step {
   const opc_layer* layer;
@@ -209,9 +213,8 @@ int opc_chain_launch(opc_chain* chain, void* stream);
 int opc_chain_destroy(opc_chain* chain);
 /* Tracing: with a device buffer of opc_chain_trace_bytes() set, every launch records per step
  * and per CTA eight %globaltimer stamps (ns), taken by the CTA's first consumer thread: input
- * ready (after the grid barrier), its own x loads done, exponents known, x staged, its own units
- * done, next step's tables requested, CTA barrier passed, flag published (after the publishing
- * thread's fence).  Layout [step][cta][8] uint64; NULL turns tracing off.
+ * start, first poll of its x words done, x complete, max barrier passed, x staged, its own units
+ * done, then two unused slots.  Layout [step][cta][8] uint64; NULL turns tracing off.
  * opc_chain_grid() is the number of CTAs (one per SM). */
 size_t opc_chain_trace_bytes(const opc_chain* chain);
 /* Options: OPC_CHAIN_L2_PREFETCH (default 0): while a step runs, prefetch each SM's share of the
@@ -225,21 +228,23 @@ int opc_chain_set_trace(opc_chain* chain, void* trace);
 /* Row-sharded decode chain over `world` GPUs of one node (one process per GPU), replacing the
  * per-layer GEMV + all-gather of tensor parallelism with ONE kernel per rank: each rank computes
  * its contiguous shard of every step's output rows from the full x and stores each finished row
- * straight into every rank's copy of the full output over NVLink; the grid barrier between steps
- * spans all ranks' CTAs (flags in every rank's memory, system-scope stores and loads, bounded
- * waits).  Outlier rows are read by every rank from the owning rank's accumulators.  No
- * all-gather, no NCCL call, no TMA multicast.  Results equal the one-GPU chain over the unsharded
- * layers bit for bit (the dot products are exact integers; every rank stages the same x).
+ * (fp16 and tagged exchange word, system-scope stores) straight into every rank's copies over
+ * NVLink; readers poll their local copy, so no barrier separates the steps.  One cross-rank flag
+ * barrier ends each launch.  No all-gather, no NCCL call, no TMA multicast.  Results equal the
+ * one-GPU chain over the unsharded layers bit for bit (the dot products are exact integers;
+ * every rank stages the same x).
  *
  * Peer-visible memory ("region"): opc_peer_alloc allocates device memory on the current GPU and
  * exports an OPC_PEER_HANDLE_BYTES handle; other ranks map it with opc_peer_open.  Each rank's
- * region holds its copy of every step's full output and the chain's scratch
- * (opc_chain_tp_scratch_bytes, at a 256-aligned offset).
+ * region holds its copy of every step's full fp16 output and the chain's scratch (flags and
+ * exchange words: opc_chain_tp_scratch_bytes, at a 256-aligned offset; call it with every
+ * step's layer and ldy set).
  *
  * Steps, per rank: layer = this rank's row shard of the step's matrix (ranks in row order: rank
  * p's shard starts after the rows of ranks < p); y = row 0 of this rank's copy of the full output
- * (inside its region, ldy >= the full row count); x as for opc_chain_create (step 0 any device
- * buffer, identical on every rank; step j a prefix of step j-1's full output).
+ * (inside its region, ldy >= the full row count and the same on every rank); x as for
+ * opc_chain_create (step 0 any device buffer holding the same values on every rank; step j a
+ * prefix of step j-1's full output).  Step 0's input may overlap the LAST step's output only.
  * Setup: every rank calls opc_chain_tp_info (info = NULL first for the size), the infos are
  * exchanged (any transport; the ranks' infos in rank order), every rank calls
  * opc_chain_create_tp with all regions mapped in its process (regions[rank] = its own), and ALL
@@ -252,7 +257,8 @@ int opc_peer_alloc(size_t bytes, void** ptr, void* handle);
 int opc_peer_open(const void* handle, void** ptr);
 int opc_peer_close(void* ptr);
 int opc_peer_free(void* ptr);
-int opc_chain_tp_scratch_bytes(const opc_chain_step* steps, int32_t n_steps, int32_t world, size_t* bytes);
+int opc_chain_tp_scratch_bytes(const opc_chain_step* steps, int32_t n_steps, int32_t batch, int32_t world,
+                               size_t* bytes);
 int opc_chain_tp_info(const opc_chain_step* steps, int32_t n_steps, int32_t batch, int32_t world, const void* region,
                       size_t region_bytes, size_t scratch_offset, void* info, size_t* info_bytes);
 int opc_chain_create_tp(const opc_chain_step* steps, int32_t n_steps, int32_t batch, int32_t rank, int32_t world,

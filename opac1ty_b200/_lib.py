@@ -135,7 +135,7 @@ PROTOTYPES = {
     "opc_peer_close": (_c.c_int, [_c.c_void_p]),
     "opc_peer_free": (_c.c_int, [_c.c_void_p]),
     "opc_chain_tp_scratch_bytes": (
-        _c.c_int, [_c.POINTER(ChainStep), _c.c_int32, _c.c_int32, _c.POINTER(_c.c_size_t)],
+        _c.c_int, [_c.POINTER(ChainStep), _c.c_int32, _c.c_int32, _c.c_int32, _c.POINTER(_c.c_size_t)],
     ),
     "opc_chain_tp_info": (
         _c.c_int,

@@ -9,27 +9,32 @@
 //    units for the CTA's 15 consumer warps through their rings and runs ahead across layer
 //    boundaries (weights do not depend on activations), so HBM keeps streaming while the
 //    consumers wait for a layer's input.
-//  * Layer j+1 needs all of layer j's output: a barrier over per-CTA flags (bounded wait)
-//    separates them.  Each CTA then stages x itself from y_j.
+//  * Dataflow instead of grid barriers: every output element of layer j is published as one
+//    32-bit exchange word (fp16 value | 16-bit tag) with a single store; the tag names the launch
+//    and the layer.  A CTA staging layer j+1 polls the words of its x chunks until every tag is
+//    the expected one, so it starts as soon as the last row it needs has landed -- no fence, no
+//    flag, no grid barrier between layers.  The fp16 value also goes to the plain output buffer
+//    y (what callers read) unless a later layer of the chain overwrites that buffer.
 //  * Packed row tiles are handed out whole (CTA c gets tiles round(c*MT/G) .. round((c+1)*MT/G)),
-//    so a tile is split only between warps of one CTA and reduced in shared memory; no
-//    cross-CTA reduction exists for them.  Outlier tiles (16 fp16 rows, 8x heavier per row) are
-//    split evenly across all CTAs and their partial dot products are added exactly into int64
-//    accumulators per outlier slot; the next layer's staging reads those for its outlier rows,
-//    and one CTA of the owning rank writes that row of y.
+//    so a tile is split only between warps of one CTA and reduced in shared memory.  Outlier
+//    tiles (16 fp16 rows, 8x heavier per row) are split evenly across all CTAs; their partial
+//    dot products are added exactly into int64 accumulators, each contributing warp then counts
+//    itself in (release), and the warp completing the tile's count (acquire) takes the sums,
+//    resets them and publishes the tile's rows.
 //
 // Row sharding over `world` GPUs (one process per GPU): every rank holds a contiguous shard of
-// each layer's output rows and computes it from the full x.  There is no separate all-gather:
-// the kernel stores each output row straight into every rank's copy of the full y over NVLink
-// (peer pointers mapped by CUDA IPC), and the barrier flags are per (rank, CTA) words in every
-// rank's memory, written by their owner with system-scope stores.  Outlier rows are read by
-// every rank from the owner's slot accumulators (system-scope loads of peer memory) through a
-// table of all ranks' outlier rows.  Nothing in this kernel uses TMA or bulk copies with
-// cluster multicast: peer memory is touched only by plain loads and stores.
+// each layer's output rows and computes it from the full x.  There is no all-gather: a rank
+// stores each finished row (fp16 and exchange word) straight into every rank's buffers over
+// NVLink, through peer pointers mapped by CUDA IPC, with system-scope stores; readers poll their
+// own local copy.  Peer memory is touched only by plain stores and the flag stores below; nothing
+// in this kernel uses TMA or bulk copies with cluster multicast.
 //
-// Flags count layers across launches (epoch * (layers + 2) + progress, compared modulo 2^32), so
-// they are never cleared between launches; a launch that gives up poisons the epoch word and
-// every later launch of the chain refuses to run.
+// Per launch, two flag values per CTA: "layer 0 staged" (a layer whose fp16 output overlaps the
+// chain input waits for it from every CTA before running) and, with several ranks, "finished"
+// (a last barrier: no rank starts its next launch while a peer still reads or writes this one's
+// buffers).  Flags and tags count launches (the epoch word), so nothing is cleared between
+// launches; the last CTA to finish advances the epoch.  A launch that gives up on a bounded wait
+// poisons the epoch word and every later launch of the chain refuses to run.
 #pragma once
 
 #include "opc_gemvq.cuh"
@@ -38,33 +43,26 @@ namespace opc {
 
 constexpr int kMaxRanks = 8;
 
-// One outlier row of a layer's full output (every rank's rows are listed on every rank).
-struct OutlierRef {
-  const unsigned long long* acc;  // its slot's int64 dot products [batch 0, 1] on the owner
-  int32_t row;                    // row of the full output
-  int32_t exp;                    // exponent of the slot's integer row
-  int32_t owner;                  // rank computing it
-  int32_t pad;
-};
-static_assert(sizeof(OutlierRef) == 24, "OutlierRef layout is shared with the host");
-
 struct ChainLayer {
-  const uint8_t* units;       // packed units (this rank's rows)
-  const uint8_t* ounits;      // int8 outlier units
-  const uint4* cbq;           // [M_pad] integer codebooks; outlier rows {0, 0, e, slot}
-  const uint16_t* tile_mask;  // [MT]
-  const int32_t* orow;        // [OT*16] local row of each outlier slot
-  const int32_t* oexp;        // [OT*16]
-  const __half* x;            // layer input (layer 0: the chain input; else a prefix of the previous y)
-  unsigned long long* acc;    // [OT*16][2] this rank's outlier-slot dot products (zero at launch)
-  __half* y_peer[kMaxRanks];  // this rank's first row in rank p's copy of the full output
-  const OutlierRef* oref;     // [n_oref] every outlier row of the full output
-  const uint16_t* mask_full;  // [ceil(m_full / 16)] outlier flags of the full output's rows
-  int64_t ldx, ldy;
+  const uint8_t* units;          // packed units (this rank's rows)
+  const uint8_t* ounits;         // int8 outlier units
+  const uint4* cbq;              // [M_pad] integer codebooks; outlier rows {0, 0, e, slot}
+  const uint16_t* tile_mask;     // [MT]
+  const int32_t* orow;           // [OT*16] local row of each outlier slot (-1: padding)
+  const int32_t* oexp;           // [OT*16]
+  const __half* x;               // layer 0: the chain input (fp16)
+  const uint32_t* xw;            // layer >= 1: the previous layer's exchange words (this rank's copy)
+  unsigned long long* acc;       // [OT*16][2] outlier-slot dot products (zero between launches)
+  int32_t* ocnt;                 // [OT] contributions received per outlier tile (zero between launches)
+  const int32_t* onc;            // [OT] warps contributing to each outlier tile
+  __half* y_peer[kMaxRanks];     // this rank's first row in rank p's fp16 copy of the full output
+  uint32_t* yw_peer[kMaxRanks];  // this rank's first row in rank p's exchange words of it
+  int64_t ldx, ldy, ldxw, ldyw;  // row strides (elements); ldxw, ldyw multiples of 8
   int32_t Up, U, M, K, K_pad, MT, KT, OT, KO;
-  int32_t x_vec16;            // x rows 16-byte loadable
-  int32_t n_oref, row_off;    // outlier rows of the full output; this rank's first row
-  int32_t m_full, pad[3];     // rows of the full output
+  int32_t x_vec16;               // layer 0: x rows 16-byte loadable
+  int32_t row_off, m_full;       // this rank's first row; rows of the full output
+  int32_t write_y;               // 0: a later layer overwrites the fp16 output (not written)
+  int32_t y_alias_x0;            // the fp16 output overlaps layer 0's input
 };
 
 static_assert(sizeof(ChainLayer) % 16 == 0, "ChainLayer is copied in 16-byte pieces");
@@ -73,11 +71,11 @@ struct ChainArgs {
   const ChainLayer* layers;
   unsigned int* sync;        // [world][grid] flags of every rank's CTAs, in this rank's memory
   unsigned int* sync_peer[kMaxRanks];  // rank p's flag array (sync_peer[rank] == sync)
-  unsigned int* epoch;       // launches completed; bit 31 = poisoned
+  unsigned int* epoch;       // [0] launches completed (bit 31: poisoned), [1] CTAs finished
   unsigned long long* trace; // optional [n_layers][grid][8] globaltimer stamps (ns) per CTA,
-                             // taken by its first consumer thread: input ready, own x loads
-                             // done, exponents known, x staged, own units done, next layer's
-                             // tables requested, CTA barrier passed, flag published (fenced)
+                             // taken by its first consumer thread: layer start, first x poll
+                             // done, x complete, max barrier passed, x staged, own units done,
+                             // then two unused slots
   int32_t n_layers, batch, stages, xs_bytes;
   uint32_t negz;
   int32_t l2_prefetch;       // prefetch each consumer's share of the next layer into L2
@@ -85,13 +83,27 @@ struct ChainArgs {
 };
 constexpr int kChainTracePhases = 8;
 constexpr uint32_t kChainPoisoned = 0x80000000u;
+constexpr uint32_t kChainTagPeriod = 65535u;  // tags run 1..65535
+constexpr int32_t kChainMaxLayers = 65534;    // so consecutive launches never share a layer's tag
+
+// Tag of layer j's exchange words in the launch with epoch e: ((e * n_layers + j) mod 65535) + 1,
+// never 0 (the value of a cleared word).  A word of layer j is rewritten once per launch, so it
+// holds this launch's tag or the previous launch's, which differs by n_layers (mod 65535).
+__host__ __device__ __forceinline__ uint32_t chain_tag_base(uint32_t epoch, int32_t n_layers) {
+  return static_cast<uint32_t>((static_cast<uint64_t>(epoch) * static_cast<uint64_t>(n_layers)) % kChainTagPeriod);
+}
+__host__ __device__ __forceinline__ uint32_t chain_tag(uint32_t base, int32_t j) {
+  uint32_t t = base + static_cast<uint32_t>(j);
+  if (t >= kChainTagPeriod) t -= kChainTagPeriod;
+  return t + 1u;
+}
 
 // This CTA's share of a layer: packed units [pu0, pu1) (whole tiles) and outlier units
 // [ou0, ou1); warps 0..wp-1 take the packed share, the other consumer warps the outlier share.
 struct ChainPart {
   int32_t pu0, pu1, ou0, ou1, wp;
 };
-__device__ __forceinline__ ChainPart chain_part(const ChainLayer& L, int c, int G) {
+__host__ __device__ __forceinline__ ChainPart chain_part(const ChainLayer& L, int c, int G) {
   ChainPart p;
   const int32_t t0 = static_cast<int32_t>((2ll * c * L.MT + G) / (2ll * G));
   const int32_t t1 = static_cast<int32_t>((2ll * (c + 1) * L.MT + G) / (2ll * G));
@@ -115,7 +127,7 @@ __device__ __forceinline__ ChainPart chain_part(const ChainLayer& L, int c, int 
   if (p.wp > np) p.wp = np;
   return p;
 }
-__device__ __forceinline__ void chain_warp_range(const ChainPart& p, int w, int32_t* u0, int32_t* u1) {
+__host__ __device__ __forceinline__ void chain_warp_range(const ChainPart& p, int w, int32_t* u0, int32_t* u1) {
   if (w < p.wp) {
     const int32_t np = p.pu1 - p.pu0;
     *u0 = p.pu0 + partq_start(w, np, p.wp);
@@ -157,8 +169,8 @@ __device__ __forceinline__ void chain_next_segment(const ChainLayer& L, ChainCur
   c.end = c.begin + (c.seg < L.MT ? L.KT : L.KO);
 }
 
-// Memory-model helpers.  One GPU: GPU scope.  Several GPUs: system scope, because peers write
-// this GPU's flags and outputs and read its accumulators over NVLink.
+// Memory-model helpers.  One GPU: GPU scope.  Several GPUs: system scope for everything peers
+// read or write (exchange words, fp16 rows, flags).
 __device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 __device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 __device__ __forceinline__ void fence_scope(bool sys) {
@@ -175,9 +187,15 @@ __device__ __forceinline__ uint32_t ld_relaxed_sys_u32(const unsigned int* p) {
   asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+// Four consecutive words, each a single-copy-atomic relaxed load.
+__device__ __forceinline__ uint4 ld_relaxed_v4(const uint32_t* p, bool sys) {
+  uint4 v;
+  if (sys)
+    asm volatile("ld.relaxed.sys.global.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p) : "memory");
+  else
+    asm volatile("ld.relaxed.gpu.global.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p) : "memory");
   return v;
 }
 __device__ __forceinline__ void st_relaxed_u32(unsigned int* p, uint32_t v) {
@@ -187,11 +205,9 @@ __device__ __forceinline__ void st_relaxed_sys_u32(unsigned int* p, uint32_t v) 
   asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Barrier over per-CTA flags: CTA c of rank r publishes "finished layer j" by storing
-// base + j + 1 into flags[r*G + c] of every rank, after its threads met at a CTA barrier and the
-// publishing thread fenced.  A waiting CTA's warp 0 polls all flags with independent relaxed
-// loads (lane l: flags l, l+32, ...; all in flight together) until every one has reached target
-// (modulo 2^32), bounded by kWaitLimitNs; then an acquire fence orders the caller's later reads.
+// One warp polls n flags (lane l: flags l, l+32, ...; independent relaxed loads, all in flight
+// together) until every one has reached target (modulo 2^32), bounded by kWaitLimitNs; then an
+// acquire fence orders the caller's later accesses.
 __device__ __forceinline__ bool poll_flags_warp(const unsigned int* flags, int n, int lane, uint32_t target, bool sys) {
   uint64_t t0 = 0;
   for (;;) {
@@ -214,39 +230,55 @@ __device__ __forceinline__ bool poll_flags_warp(const unsigned int* flags, int n
 // Exact 2^e for e in [-126, 127].
 __device__ __forceinline__ float pow2f(int e) { return __int_as_float((127 + e) << 23); }
 
-// Value of an outlier row from its slot accumulator t, slot exponent e and x exponent ex.
-__device__ __forceinline__ __half outlier_half(long long t, int e, int ex) { return scale_to_half(t, e + ex); }
+// Eight exchange words of k..k+7 (the first n_valid inside the row): do all carry `tag`?  Then
+// their fp16 values, packed in pairs, go to v.
+__device__ __forceinline__ bool chain_take_words(const uint4& a, const uint4& c, uint32_t tag, int n_valid, uint4* v) {
+  const uint32_t w[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+  bool ok = true;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) ok &= (e >= n_valid) || ((w[e] >> 16) == tag);
+  if (!ok) return false;
+  uint32_t h[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) h[e] = e < n_valid ? (w[e] & 0xffffu) : 0u;
+  *v = make_uint4(h[0] | (h[1] << 16), h[2] | (h[3] << 16), h[4] | (h[5] << 16), h[6] | (h[7] << 16));
+  return true;
+}
 
-constexpr int kChainPatchMax = 512;  // outlier rows of a layer whose values go through shared memory
-constexpr int kChainMaskMax = 2048;  // row tiles of the previous layer covered by x (tile masks in smem)
-constexpr int kChainSplitSlots = 32; // packed tiles per CTA and layer (host-checked)
+constexpr int kChainSplitSlots = 32;  // packed tiles per CTA and layer (host-checked)
 
 struct ChainShared {
   ChainLayer layer[2];                    // descriptors of layers j (slot j&1) and j+1
   float amax[kQConsumers][kQMaxBatch];    // staging: per-warp max |x|
   unsigned long long tile_acc[kChainSplitSlots][kTileRows][kQMaxBatch];  // split packed tiles
   int32_t tile_cnt[kChainSplitSlots];
-  const unsigned long long* patch_acc[kChainPatchMax];  // previous layer's outlier rows: accumulators,
-  int32_t patch_row[kChainPatchMax];      // rows of the full output,
-  int32_t patch_exp[kChainPatchMax];      // integer-row exponents,
-  uint16_t patch_val[kChainPatchMax][kQMaxBatch];  // values (written during staging),
-  uint8_t patch_owner[kChainPatchMax];    // owning ranks
-  uint16_t prev_mask[kChainMaskMax];      // previous layer's outlier flags of the rows x reads
   int32_t abort;
   uint32_t epoch;
 };
 
-// Rows m.row[0..1] (local) of this warp's tile with dot products t into every rank's output.
+// Rows m.row[0..1] (local) with dot products t: exchange words into every rank's copy (one
+// relaxed store per word) and, unless a later layer overwrites it, the fp16 output.
 __device__ __forceinline__ void chain_write_rows(const ChainLayer& L, int P, int B, const MetaQ& m, const long long t[2],
-                                                 int q, int ex0, int ex1) {
+                                                 int q, int ex0, int ex1, uint32_t tag, bool sys) {
   const int b = q >> 1;
   if ((q & 1) || b >= B) return;
   const int ex = b ? ex1 : ex0;
   const __half h0 = scale_to_half(t[0], m.e[0] + ex), h1 = scale_to_half(t[1], m.e[1] + ex);
+  const uint32_t w0 = (tag << 16) | __half_as_ushort(h0), w1 = (tag << 16) | __half_as_ushort(h1);
   for (int p = 0; p < P; ++p) {
-    __half* yb = L.y_peer[p] + b * L.ldy;
-    if (m.row[0] >= 0) yb[m.row[0]] = h0;
-    if (m.row[1] >= 0) yb[m.row[1]] = h1;
+    unsigned int* wb = L.yw_peer[p] + b * L.ldyw;
+    if (L.write_y) {
+      __half* yb = L.y_peer[p] + b * L.ldy;
+      if (m.row[0] >= 0) yb[m.row[0]] = h0;
+      if (m.row[1] >= 0) yb[m.row[1]] = h1;
+    }
+    if (sys) {
+      if (m.row[0] >= 0) st_relaxed_sys_u32(wb + m.row[0], w0);
+      if (m.row[1] >= 0) st_relaxed_sys_u32(wb + m.row[1], w1);
+    } else {
+      if (m.row[0] >= 0) st_relaxed_u32(wb + m.row[0], w0);
+      if (m.row[1] >= 0) st_relaxed_u32(wb + m.row[1], w1);
+    }
   }
 }
 
@@ -254,7 +286,8 @@ __device__ __forceinline__ void chain_write_rows(const ChainLayer& L, int P, int
 // other warps of the CTA: added exactly into the tile's shared int64 accumulators; the warp that
 // completes the count of contributors writes the tile's rows and clears the slot.
 __device__ void chain_split_add(ChainShared* sh, const ChainLayer& L, int P, int B, const MetaQ& m, const long long t[2],
-                                int lt, int n_contrib, int lane, int g, int q, int ex0, int ex1) {
+                                int lt, int n_contrib, int lane, int g, int q, int ex0, int ex1, uint32_t tag,
+                                bool sys) {
   const int slot = lt & (kChainSplitSlots - 1);
   const int b = q >> 1;
   const bool live = !(q & 1) && b < B;
@@ -275,7 +308,7 @@ __device__ void chain_split_add(ChainShared* sh, const ChainLayer& L, int P, int
     fin[1] = static_cast<long long>(atomicExch(&sh->tile_acc[slot][g + 8][b], 0ull));
   }
   if (lane == 0) sh->tile_cnt[slot] = 0;
-  chain_write_rows(L, P, B, m, fin, q, ex0, ex1);
+  chain_write_rows(L, P, B, m, fin, q, ex0, ex1, tag, sys);
 }
 
 template <int kXC>
@@ -300,7 +333,7 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     }
     fence_mbar_init();
     const uint32_t ep = ld_relaxed_u32(args.epoch);
-    sh->epoch = ep;
+    sh->epoch = ep & ~kChainPoisoned;
     sh->abort = (ep & kChainPoisoned) ? 1 : 0;
     if (ep & kChainPoisoned) atomicCAS(&g_opc_device_error, 0, kDevErrChainPoisoned);
   }
@@ -321,7 +354,6 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     ChainCursor pc = {0, 0, 0, 0};
     const ChainLayer* Lp = nullptr;
     bool active = i < kQConsumers;
-    // advance to the first layer with a non-empty range for this consumer
     const uint64_t evict_first = l2_policy_evict_first();
     // When this lane starts layer j, its consumer's share of layer j+1 is prefetched into L2, so
     // HBM streams the next layer during this one's compute and its ring refills hit L2.
@@ -342,6 +374,7 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
         bytes -= n;
       }
     };
+    // advance to the next layer with a non-empty range for this consumer
     auto next_range = [&]() {
       while (j < args.n_layers) {
         Lp = args.layers + j;
@@ -421,15 +454,16 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
   const int P = args.world;
   const bool sys = P > 1;
   const int n_flags = P * G;
-  // This launch publishes layer j as base + j + 1 and its end as base + n_layers + 1.
-  const uint32_t base = sh->epoch * static_cast<uint32_t>(args.n_layers + 2);
+  const uint32_t epoch = sh->epoch;
+  const uint32_t f_staged0 = 2u * epoch + 1u;  // flag: this CTA staged layer 0
+  const uint32_t f_done = 2u * epoch + 2u;     // flag: this CTA finished the launch (several ranks)
+  const uint32_t tag_base = chain_tag_base(epoch, args.n_layers);
   int slot = 0;
   uint32_t phase = 0;
-  int32_t ex_prev[kQMaxBatch] = {0, 0};
   bool ok = true;
 
-  // Every CTA of every rank has published at least `target`; sets abort on a timeout.  The
-  // polling lanes' acquire fence plus the CTA barrier order every thread's later reads.
+  // Every CTA of every rank has published at least `target` (bounded; sets abort on a timeout).
+  // The polling lanes' acquire fence plus the CTA barrier order every thread's later accesses.
   auto wait_all = [&](uint32_t target) {
     if (warp == 0 && !poll_flags_warp(args.sync, n_flags, lane, target, sys) && lane == 0) {
       sh->abort = 1;
@@ -438,8 +472,7 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     named_barrier(1, kQConsumerThreads);
   };
   // After a CTA barrier: this CTA's flag in every rank's memory.  The publishing thread's fence
-  // is cumulative: it orders every write the barrier made it observe (all threads' output rows
-  // and accumulator adds) before the flag, so no other thread fences.
+  // is cumulative: it orders every access the barrier made it observe before the flag.
   auto publish = [&](uint32_t value) {
     if (sys) {
       if (tid < P) fence_acq_rel_sys();
@@ -453,10 +486,12 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
   };
 
   for (int j = 0; j < args.n_layers && ok; ++j) {
-    // Descriptors live in shared memory (layer j+1's is copied at the end of layer j), so reading
-    // them costs no global round trip and holds no registers.
+    // Descriptors live in shared memory (layer j+1's is copied during layer j's staging), so
+    // reading them costs no global round trip and holds no registers.
     const ChainLayer& L = sh->layer[j & 1];
-    // Everything about this warp's share that does not depend on x, before waiting for x.
+    const uint32_t tag = chain_tag(tag_base, j);
+    const uint32_t tag_in = j > 0 ? chain_tag(tag_base, j - 1) : 0u;
+    // Everything about this warp's share that does not depend on x, before x is complete.
     GemvQArgs qa;  // the per-layer view load_metaq takes
     qa.cbq = L.cbq; qa.tile_mask = L.tile_mask; qa.orow = L.orow; qa.oexp = L.oexp; qa.M = L.M; qa.MT = L.MT;
     const ChainPart part = chain_part(L, cta, G);
@@ -464,101 +499,77 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     chain_warp_range(part, warp, &u0, &u1);
     ChainCursor cc = chain_cursor(L, u0 < u1 ? u0 : 0);
     MetaQ cur, nxt;
-    if (u0 < u1) {  // issued before the wait; first used by the units loop
+    if (u0 < u1) {
       cur = load_metaq(qa, cc.seg, g);
       nxt = (cc.seg + 1 < L.MT + L.OT) ? load_metaq(qa, cc.seg + 1, g) : cur;
     }
-    const bool has_prev = j > 0;
-    const ChainLayer& Lp = sh->layer[(j + 1) & 1];  // layer j-1 while j > 0
-    const int n_pref = has_prev ? Lp.n_oref : 0;
-    const bool mask_in_smem = has_prev && (L.K + 15) / 16 <= kChainMaskMax;
-    // ---- wait for layer j-1 everywhere
-    if (has_prev) {
-      wait_all(base + static_cast<uint32_t>(j));
-      if (sh->abort) {
-        ok = false;
-        break;
-      }
-    }
+    // next layer's descriptor: loaded now, stored to shared memory once every warp is past this
+    // layer's first staging barrier (nobody reads the slot's old descriptor after that)
+    const bool copy_desc = j + 1 < args.n_layers && tid < static_cast<int>(sizeof(ChainLayer) / 16);
+    uint4 desc_piece = make_uint4(0, 0, 0, 0);
+    if (copy_desc) desc_piece = ld_nc_v4(reinterpret_cast<const uint4*>(args.layers + j + 1) + tid);
     unsigned long long* tr = args.trace ? args.trace + (static_cast<int64_t>(j) * G + cta) * kChainTracePhases : nullptr;
     if (tr && tid == 0) tr[0] = globaltimer_ns();
 
-    // ---- stage x_j (x = the previous output when j > 0).  Round 1 issues every load at once:
-    // this thread's x chunks with the previous layer's outlier flags of their rows, and the
-    // previous layer's outlier values from their slot accumulators (on the owning rank).  Outlier
-    // rows of y_{j-1} are never read from y; their values go through a shared table.
+    // ---- stage x_j.  Layer 0 reads the fp16 input; later layers poll the previous layer's
+    // exchange words of their chunks until every tag is this launch's (bounded).
     int ex0 = 0, ex1 = 0;  // x exponents of batch rows 0, 1 (scalars: no local memory)
     {
       const int per_row = L.K_pad / 8;
       const int total = B * per_row;
       uint4 v[kXC];
-      uint32_t tmw[kXC];
+      uint32_t pending = 0;
 #pragma unroll
       for (int i = 0; i < kXC; ++i) {
         const int c = tid + i * kQConsumerThreads;
         v[i] = make_uint4(0, 0, 0, 0);
-        tmw[i] = 0;
         if (c < total) {
           const int b = c / per_row, k = (c - b * per_row) * 8;
           if (k < L.K) {
-            const __half* src = L.x + b * L.ldx + k;
-            if (L.x_vec16) {
-              v[i] = ld_cg_v4(src);
-            } else {
-              uint16_t h[8];
+            if (j == 0) {
+              const __half* src = L.x + b * L.ldx + k;
+              if (L.x_vec16) {
+                v[i] = ld_cg_v4(src);
+              } else {
+                uint16_t h[8];
 #pragma unroll
-              for (int e = 0; e < 8; ++e)
-                h[e] = (k + e < L.K) ? __ldcg(reinterpret_cast<const unsigned short*>(src) + e) : 0;
-              v[i] = make_uint4(h[0] | (uint32_t(h[1]) << 16), h[2] | (uint32_t(h[3]) << 16),
-                                h[4] | (uint32_t(h[5]) << 16), h[6] | (uint32_t(h[7]) << 16));
-            }
-            if (has_prev) {
-              const uint32_t mw = mask_in_smem ? sh->prev_mask[k >> 4] : __ldg(Lp.mask_full + (k >> 4));
-              uint32_t tm = (mw >> (k & 15)) & 0xffu;
-              if (k + 8 > L.K) tm &= (1u << (L.K - k)) - 1u;
-              tmw[i] = tm;
+                for (int e = 0; e < 8; ++e)
+                  h[e] = (k + e < L.K) ? __ldcg(reinterpret_cast<const unsigned short*>(src) + e) : 0;
+                v[i] = make_uint4(h[0] | (uint32_t(h[1]) << 16), h[2] | (uint32_t(h[3]) << 16),
+                                  h[4] | (uint32_t(h[5]) << 16), h[6] | (uint32_t(h[7]) << 16));
+              }
+            } else {
+              const uint32_t* src = L.xw + b * L.ldxw + k;
+              const uint4 a = ld_relaxed_v4(src, sys), d = ld_relaxed_v4(src + 4, sys);
+              if (!chain_take_words(a, d, tag_in, L.K - k, &v[i])) pending |= 1u << i;
             }
           }
         }
       }
+      if (tr && tid == 0) tr[1] = globaltimer_ns();
+      if (pending) {
+        const uint64_t t0 = globaltimer_ns();
+        for (;;) {
+#pragma unroll
+          for (int i = 0; i < kXC; ++i) {
+            if (pending & (1u << i)) {
+              const int c = tid + i * kQConsumerThreads;
+              const int b = c / per_row, k = (c - b * per_row) * 8;
+              const uint32_t* src = L.xw + b * L.ldxw + k;
+              const uint4 a = ld_relaxed_v4(src, sys), d = ld_relaxed_v4(src + 4, sys);
+              if (chain_take_words(a, d, tag_in, L.K - k, &v[i])) pending &= ~(1u << i);
+            }
+          }
+          if (!pending) break;
+          if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            sh->abort = 1;
+            atomicCAS(&g_opc_device_error, 0, kDevErrBarrierTimeout);
+            break;
+          }
+        }
+      }
+      if (tr && tid == 0) tr[2] = globaltimer_ns();
       float mx[kQMaxBatch] = {0.f, 0.f};
-      // the previous layer's outlier values (rows owned by this rank and assigned to this CTA
-      // are written to every rank's y here)
-      for (int s = tid; s < n_pref; s += kQConsumerThreads) {
-        int row, e0, own;
-        const unsigned long long* acc;
-        if (s < kChainPatchMax) {
-          row = sh->patch_row[s];
-          e0 = sh->patch_exp[s];
-          own = sh->patch_owner[s];
-          acc = sh->patch_acc[s];
-        } else {
-          const OutlierRef o = Lp.oref[s];
-          row = o.row;
-          e0 = o.exp;
-          own = o.owner;
-          acc = o.acc;
-        }
-        const long long t0 = static_cast<long long>(sys ? ld_relaxed_sys_u64(acc) : __ldcg(acc));
-        const long long t1 = B > 1 ? static_cast<long long>(sys ? ld_relaxed_sys_u64(acc + 1) : __ldcg(acc + 1)) : 0ll;
-        const __half h0 = outlier_half(t0, e0, ex_prev[0]);
-        const __half h1 = outlier_half(t1, e0, ex_prev[1]);
-        if (own == args.rank && s % G == cta) {
-          for (int p = 0; p < P; ++p) {
-            __half* yb = Lp.y_peer[p] - Lp.row_off;
-            yb[row] = h0;
-            if (B > 1) yb[Lp.ldy + row] = h1;
-          }
-        }
-        if (s < kChainPatchMax) {
-          sh->patch_val[s][0] = __half_as_ushort(h0);
-          sh->patch_val[s][1] = __half_as_ushort(h1);
-        }
-        if (row < L.K) {
-          mx[0] = fmaxf(mx[0], fabsf(__half2float(h0)));
-          if (B > 1) mx[1] = fmaxf(mx[1], fabsf(__half2float(h1)));
-        }
-      }
 #pragma unroll
       for (int i = 0; i < kXC; ++i) {
         const int c = tid + i * kQConsumerThreads;
@@ -568,7 +579,6 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
           float m = 0.f;
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
-            if ((tmw[i] >> e) & 1u) continue;  // outlier row: its value comes from the table
             const __half hv = __ushort_as_half(static_cast<unsigned short>((wv[e >> 1] >> (16 * (e & 1))) & 0xffffu));
             m = fmaxf(m, fabsf(__half2float(hv)));
           }
@@ -576,7 +586,6 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
           else mx[1] = fmaxf(mx[1], m);
         }
       }
-      if (tr && tid == 0) tr[1] = globaltimer_ns();
 #pragma unroll
       for (int b = 0; b < kQMaxBatch; ++b)
         for (int o = 16; o > 0; o >>= 1) mx[b] = fmaxf(mx[b], __shfl_xor_sync(0xffffffffu, mx[b], o));
@@ -585,8 +594,14 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
         sh->amax[warp][1] = mx[1];
       }
       if (tid < 8) sts128(xs_base + args.xs_bytes - kQZeroBytes + tid * 16, make_uint4(0, 0, 0, 0));
-      named_barrier(1, kQConsumerThreads);
-      if (tr && tid == 0) tr[2] = globaltimer_ns();
+      named_barrier(1, kQConsumerThreads);  // every warp is done with layer j-1 and holds its x
+      if (tr && tid == 0) tr[3] = globaltimer_ns();
+      if (sh->abort) {
+        ok = false;
+        break;
+      }
+      if (copy_desc) reinterpret_cast<uint4*>(&sh->layer[(j + 1) & 1])[tid] = desc_piece;
+      if (j == 0) publish(f_staged0);  // layer-0 input read by every thread of this CTA
       {
         float m0 = 0.f, m1 = 0.f;
         for (int w = 0; w < kQConsumers; ++w) {
@@ -602,7 +617,7 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
         const int c = tid + i * kQConsumerThreads;
         if (c < total) {
           const int b = c / per_row, k = (c - b * per_row) * 8;
-          const uint32_t wv[4] = {v[i].x, v[i].y, v[i].z, v[i].w};  // outlier rows fixed below
+          const uint32_t wv[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
           const float sc = pow2f(b == 0 ? ex0 : ex1);
           uint32_t d[3][2] = {{0, 0}, {0, 0}, {0, 0}};
 #pragma unroll
@@ -622,46 +637,18 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
           for (int dd = 0; dd < 3; ++dd) sts64(xs_base + (3 * b + dd) * colb + pos, d[dd][0], d[dd][1]);
         }
       }
-      if (n_pref > 0) {
-        // Outlier rows of the previous layer: one thread per row overwrites its digits (the
-        // chunks above converted whatever y held there).
-        named_barrier(1, kQConsumerThreads);
-        for (int s = tid; s < n_pref; s += kQConsumerThreads) {
-          int row;
-          uint32_t hv[kQMaxBatch];
-          if (s < kChainPatchMax) {
-            row = sh->patch_row[s];
-            hv[0] = sh->patch_val[s][0];
-            hv[1] = sh->patch_val[s][1];
-          } else {
-            const OutlierRef o = Lp.oref[s];
-            row = o.row;
-            const long long t0 = static_cast<long long>(sys ? ld_relaxed_sys_u64(o.acc) : __ldcg(o.acc));
-            const long long t1 =
-                B > 1 ? static_cast<long long>(sys ? ld_relaxed_sys_u64(o.acc + 1) : __ldcg(o.acc + 1)) : 0ll;
-            hv[0] = __half_as_ushort(outlier_half(t0, o.exp, ex_prev[0]));
-            hv[1] = __half_as_ushort(outlier_half(t1, o.exp, ex_prev[1]));
-          }
-          if (row < 0 || row >= L.K) continue;
-          const uint32_t pos = static_cast<uint32_t>((row >> 7) * 128 + xs_pos8(row & 127));
-#pragma unroll
-          for (int b = 0; b < kQMaxBatch; ++b) {
-            if (b >= B) break;
-            const int n = round_small_int(__half2float(__ushort_as_half(static_cast<unsigned short>(hv[b]))) *
-                                          pow2f(b ? ex1 : ex0));
-            const int d2 = ((n + 128) & 255) - 128;
-            const int n1 = (n - d2) >> 8;
-            const int d1 = ((n1 + 128) & 255) - 128;
-            const int d0 = (n1 - d1) >> 8;
-            sts8(xs_base + (3 * b + 0) * colb + pos, static_cast<uint32_t>(d0));
-            sts8(xs_base + (3 * b + 1) * colb + pos, static_cast<uint32_t>(d1));
-            sts8(xs_base + (3 * b + 2) * colb + pos, static_cast<uint32_t>(d2));
-          }
-        }
+      // a layer writing over the chain input starts once every CTA has read that input
+      if (L.y_alias_x0 && warp == 0 && !poll_flags_warp(args.sync, n_flags, lane, f_staged0, sys) && lane == 0) {
+        sh->abort = 1;
+        atomicCAS(&g_opc_device_error, 0, kDevErrBarrierTimeout);
       }
       named_barrier(1, kQConsumerThreads);
+      if (sh->abort) {
+        ok = false;
+        break;
+      }
     }
-    if (tr && tid == 0) tr[3] = globaltimer_ns();
+    if (tr && tid == 0) tr[4] = globaltimer_ns();
 
     // ---- this warp's units of layer j
     const int bcol = g >> 2, dig = g & 3;
@@ -680,18 +667,42 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     if (u0 < u1) {
       AccQ A;
       zero_accq(A);
-      // outlier segments: add this warp's partial into the slot accumulators
+      // Outlier segment done: add this warp's partial into the slot accumulators and count it in
+      // (release); the warp completing the tile's count (acquire) takes the sums, clears them and
+      // publishes the tile's rows.
       auto flush_outlier = [&](int32_t seg) {
         long long t[2];
         finish_dot(A, q, t);
         const int b = q >> 1;
-        if (!(q & 1) && b < B) {
+        const bool live = !(q & 1) && b < B;
+        const int tt = seg - L.MT;
+        if (live) {
 #pragma unroll
           for (int r = 0; r < 2; ++r) {
-            const int s = (seg - L.MT) * kTileRows + g + 8 * r;
+            const int s = tt * kTileRows + g + 8 * r;
             if (cur.row[r] >= 0) atomicAdd(L.acc + 2 * s + b, static_cast<unsigned long long>(t[r]));
           }
         }
+        __syncwarp();
+        int old = 0;
+        if (lane == 0) {
+          fence_acq_rel_gpu();
+          old = atomicAdd(L.ocnt + tt, 1);
+          fence_acq_rel_gpu();
+        }
+        old = __shfl_sync(0xffffffffu, old, 0);
+        __syncwarp();
+        if (old != static_cast<int>(ld_nc_u32(L.onc + tt)) - 1) return;
+        long long fin[2] = {0, 0};
+        if (live) {
+#pragma unroll
+          for (int r = 0; r < 2; ++r) {
+            const int s = tt * kTileRows + g + 8 * r;
+            if (cur.row[r] >= 0) fin[r] = static_cast<long long>(atomicExch(L.acc + 2 * s + b, 0ull));
+          }
+        }
+        if (lane == 0) st_relaxed_u32(reinterpret_cast<unsigned int*>(L.ocnt + tt), 0u);
+        chain_write_rows(L, P, B, cur, fin, q, ex0, ex1, tag, sys);
       };
       while (cc.u < u1) {
         if (!mbar_wait_bounded(fullw + slot * 8, phase)) {
@@ -745,9 +756,9 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
             long long t[2];
             finish_dot(A, q, t);
             if (cc.begin < u0)
-              chain_split_add(sh, L, P, B, cur, t, cc.seg - tile0, contrib(cc.begin), lane, g, q, ex0, ex1);
+              chain_split_add(sh, L, P, B, cur, t, cc.seg - tile0, contrib(cc.begin), lane, g, q, ex0, ex1, tag, sys);
             else
-              chain_write_rows(L, P, B, cur, t, q, ex0, ex1);
+              chain_write_rows(L, P, B, cur, t, q, ex0, ex1, tag, sys);
           }
           zero_accq(A);
           chain_next_segment(L, cc);
@@ -762,70 +773,38 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
           long long t[2];
           finish_dot(A, q, t);
           if (cc.begin >= u0 && cc.end <= u1)
-            chain_write_rows(L, P, B, cur, t, q, ex0, ex1);
+            chain_write_rows(L, P, B, cur, t, q, ex0, ex1, tag, sys);
           else
-            chain_split_add(sh, L, P, B, cur, t, cc.seg - tile0, contrib(cc.begin), lane, g, q, ex0, ex1);
+            chain_split_add(sh, L, P, B, cur, t, cc.seg - tile0, contrib(cc.begin), lane, g, q, ex0, ex1, tag, sys);
         }
       } else {
         atomicCAS(&g_opc_device_error, 0, kDevErrTmaTimeout);
-        sh->abort = 1;
-      }
-    }
-    if (tr && tid == 0) tr[4] = globaltimer_ns();
-    if (j + 1 < args.n_layers) {
-      // For layer j+1: its descriptor, and layer j's outlier table and flags that its staging
-      // reads (shared memory is free: layer j's staging is over).  Issued before the write
-      // fence, so these loads overlap it.
-      if (tid < sizeof(ChainLayer) / 16)
-        reinterpret_cast<uint4*>(&sh->layer[(j + 1) & 1])[tid] = ld_nc_v4(reinterpret_cast<const uint4*>(args.layers + j + 1) + tid);
-      const int kn = args.layers[j + 1].K;
-      if ((kn + 15) / 16 <= kChainMaskMax)
-        for (int t = tid; t < (kn + 15) / 16; t += kQConsumerThreads) sh->prev_mask[t] = __ldg(L.mask_full + t);
-      for (int s2 = tid; s2 < L.n_oref && s2 < kChainPatchMax; s2 += kQConsumerThreads) {
-        const OutlierRef o = L.oref[s2];
-        sh->patch_acc[s2] = o.acc;
-        sh->patch_row[s2] = o.row;
-        sh->patch_exp[s2] = o.exp;
-        sh->patch_owner[s2] = static_cast<uint8_t>(o.owner);
+        sh->abort = 1;  // every consumer sees it at the next staging barrier
+        ok = true;      // this warp still takes part in the CTA's barriers until then
       }
     }
     if (tr && tid == 0) tr[5] = globaltimer_ns();
-    named_barrier(1, kQConsumerThreads);  // every thread's writes of layer j, then the flag
-    if (sh->abort) ok = false;
-    if (tr && tid == 0) tr[6] = globaltimer_ns();
-    if (ok) publish(base + static_cast<uint32_t>(j + 1));
-    if (tr && tid == 0) tr[7] = globaltimer_ns();
-    ex_prev[0] = ex0;
-    ex_prev[1] = ex1;
   }
 
-  // ---- last layer's outlier rows, once every CTA has finished it; with several ranks, a last
-  // barrier so that no rank starts its next launch while a peer still writes or reads this one's
-  // buffers.
-  if (ok && args.n_layers > 0) {
-    wait_all(base + static_cast<uint32_t>(args.n_layers));
-    if (!sh->abort) {
-      const ChainLayer& Ll = sh->layer[(args.n_layers - 1) & 1];
-      for (int i = cta + G * tid; i < Ll.n_oref; i += G * kQConsumerThreads) {
-        const OutlierRef o = Ll.oref[i];
-        if (o.owner != args.rank) continue;
-        const __half h0 = outlier_half(static_cast<long long>(__ldcg(o.acc)), o.exp, ex_prev[0]);
-        const __half h1 = B > 1 ? outlier_half(static_cast<long long>(__ldcg(o.acc + 1)), o.exp, ex_prev[1]) : h0;
-        for (int p = 0; p < P; ++p) {
-          __half* yb = Ll.y_peer[p] - Ll.row_off;
-          yb[o.row] = h0;
-          if (B > 1) yb[Ll.ldy + o.row] = h1;
-        }
-      }
-      if (sys) {
-        named_barrier(1, kQConsumerThreads);
-        publish(base + static_cast<uint32_t>(args.n_layers + 1));
-        wait_all(base + static_cast<uint32_t>(args.n_layers + 1));
-      }
-    }
-    if (tid == 0 && cta == 0 && !sh->abort) atomicAdd(args.epoch, 1u);
+  // ---- end of the launch.  Several ranks: a last barrier, so that no rank starts its next
+  // launch while a peer still writes or reads this one's buffers (its fp16 outputs are complete
+  // when it passes).  The last CTA of this rank to finish advances the epoch.
+  named_barrier(1, kQConsumerThreads);
+  if (sh->abort) ok = false;
+  if (ok && sys && args.n_layers > 0) {
+    publish(f_done);
+    wait_all(f_done);
+    if (sh->abort) ok = false;
   }
-  if (tid == 0 && sh->abort) atomicOr(args.epoch, kChainPoisoned);
+  if (tid == 0) {
+    if (!ok) atomicOr(args.epoch, kChainPoisoned);
+    __threadfence();
+    const unsigned int done = atomicAdd(args.epoch + 1, 1u);
+    if (done == static_cast<unsigned int>(G) - 1u) {
+      st_relaxed_u32(args.epoch + 1, 0u);
+      atomicAdd(args.epoch, 1u);
+    }
+  }
 }
 
 }  // namespace opc

@@ -89,10 +89,10 @@ __device__ __forceinline__ void nextq_segment(const GemvQArgs& a, CursorQ& c) {
   c.end = c.begin + (c.seg < a.MT ? a.KT : a.KO);
 }
 
-__device__ __forceinline__ int32_t partq_start(int32_t i, int32_t n, int32_t p) {
+__host__ __device__ __forceinline__ int32_t partq_start(int32_t i, int32_t n, int32_t p) {
   return static_cast<int32_t>(static_cast<int64_t>(i) * n / p);
 }
-__device__ __forceinline__ int32_t partq_of(int32_t e, int32_t n, int32_t p) {
+__host__ __device__ __forceinline__ int32_t partq_of(int32_t e, int32_t n, int32_t p) {
   return static_cast<int32_t>((static_cast<int64_t>(e + 1) * p + n - 1) / n - 1);
 }
 

@@ -754,53 +754,46 @@ struct opc_chain {
   int32_t n_layers = 0, batch = 1, stages = 2, xs_bytes = 0, grid = 0, xc = 8;
   int32_t rank = 0, world = 1;
   size_t smem = 0;
-  void* dev_mem = nullptr;              // [layers | outlier tables | flag masks | epoch (| flags | acc)]
+  void* dev_mem = nullptr;              // [layers | onc | epoch | acc | ocnt (| flags | words)]
   opc::ChainLayer* d_layers = nullptr;
   unsigned int* d_sync = nullptr;       // this rank's flags [world][grid]
   unsigned int* sync_peer[opc::kMaxRanks] = {};
-  unsigned int* d_epoch = nullptr;
-  void* acc = nullptr;                  // this rank's outlier accumulators, cleared before every launch
-  size_t acc_bytes = 0;
+  unsigned int* d_epoch = nullptr;      // [2]
   unsigned long long* trace = nullptr;  // optional per-phase timestamps (caller-owned)
   int32_t l2_prefetch = 0;
 };
 
 namespace {
 
-struct OutlierSlot {
-  int32_t slot, row, exp;  // slot index, local row, exponent of the slot's integer row
-};
-
 // One rank of a chain as this process sees it (pointers valid in this process).
 struct ChainRank {
-  std::vector<int32_t> M;                       // rows of its shard, per step
-  std::vector<std::vector<OutlierSlot>> slots;  // its outlier rows, per step
-  std::vector<char*> y;                         // row 0 of its copy of each step's full output
-  std::vector<unsigned long long*> acc;         // its outlier accumulators, per step
-  unsigned int* sync = nullptr;                 // its flag array [world][grid]
+  std::vector<int32_t> M;   // rows of its shard, per step
+  std::vector<char*> y;     // row 0 of its fp16 copy of each step's full output
+  std::vector<char*> yw;    // row 0 of its exchange words of each step's full output
+  unsigned int* sync = nullptr;  // its flag array [world][grid]
 };
 
-int read_outlier_slots(const opc_layer* L, std::vector<OutlierSlot>* out) {
-  const int32_t ns = n_slots_of(L->plan);
-  std::vector<int32_t> h(2 * static_cast<size_t>(ns));
-  OPC_CUDA(cudaMemcpy(h.data(), L->outlier_rows, h.size() * sizeof(int32_t), cudaMemcpyDeviceToHost),
-           "cudaMemcpy(outlier slots)");
-  out->clear();
-  for (int32_t s = 0; s < ns; ++s)
-    if (h[s] >= 0) out->push_back({s, h[s], h[ns + s]});
-  return OPC_OK;
-}
-
-size_t chain_acc_bytes(const opc_layer_plan& p) {
-  return align_up(static_cast<size_t>(n_slots_of(p)) * opc::kQMaxBatch * sizeof(unsigned long long), 256);
+int64_t chain_ldyw(int64_t ldy) { return (ldy + 7) / 8 * 8; }
+size_t chain_words_bytes(int64_t ldy, int batch) {
+  return align_up(static_cast<size_t>(batch) * chain_ldyw(ldy) * sizeof(uint32_t), 256);
 }
 size_t chain_sync_bytes(int world, int grid) {
   return align_up(static_cast<size_t>(world) * grid * sizeof(unsigned int), 256);
 }
 
+// Half-open byte ranges of a [rows x ld] fp16 matrix with `batch` rows of `cols` elements.
+bool fp16_ranges_overlap(const void* a, int64_t lda, int64_t na, const void* b, int64_t ldb, int64_t nb, int batch) {
+  const char* a0 = static_cast<const char*>(a);
+  const char* b0 = static_cast<const char*>(b);
+  const char* a1 = a0 + 2 * ((batch - 1) * lda + na);
+  const char* b1 = b0 + 2 * ((batch - 1) * ldb + nb);
+  return a0 < b1 && b0 < a1;
+}
+
 // One rank's steps against the kernel's limits; m_full[j] = rows of step j's full output.
 int check_chain_steps(const char* fn, const opc_chain_step* steps, int32_t n, int32_t batch, const DeviceCache& dc,
                       const std::vector<int32_t>& m_full) {
+  if (n > opc::kChainMaxLayers) return fail(OPC_ERR_UNSUPPORTED, "%s: %d steps (at most %d)", fn, n, opc::kChainMaxLayers);
   for (int j = 0; j < n; ++j) {
     const opc_chain_step& st = steps[j];
     if (!st.layer || !plan_ok(&st.layer->plan)) return fail(OPC_ERR_INVALID, "%s: step %d: invalid layer", fn, j);
@@ -826,11 +819,37 @@ int check_chain_steps(const char* fn, const opc_chain_step* steps, int32_t n, in
                   static_cast<long long>(batch) * p.K_pad, 64 * opc::kQConsumerThreads);
     if (p.total_units >= (int64_t(1) << 31)) return fail(OPC_ERR_UNSUPPORTED, "%s: step %d: layer too large", fn, j);
   }
+  // fp16 outputs: step 0's may not overlap the input; two steps' outputs are the same buffer
+  // (then only the later one is written) or disjoint
+  if (fp16_ranges_overlap(steps[0].x, steps[0].ldx, steps[0].layer->plan.K, steps[0].y, steps[0].ldy, m_full[0], batch))
+    return fail(OPC_ERR_UNSUPPORTED, "%s: step 0 writes over its own input", fn);
+  for (int i = 0; i < n; ++i)
+    for (int j = i + 1; j < n; ++j) {
+      if (!fp16_ranges_overlap(steps[i].y, steps[i].ldy, m_full[i], steps[j].y, steps[j].ldy, m_full[j], batch)) continue;
+      if (steps[i].y != steps[j].y || steps[i].ldy != steps[j].ldy)
+        return fail(OPC_ERR_UNSUPPORTED, "%s: outputs of steps %d and %d overlap without being the same buffer", fn, i, j);
+    }
   return OPC_OK;
 }
 
-// Builds a chain from every rank's view (ranks[rank] is this process's own).  With own_scratch,
-// the flags and accumulators are allocated here (one GPU) and ranks[rank]'s pointers are set.
+// Warps contributing to each outlier tile of a layer (the kernel's partition, replayed).
+std::vector<int32_t> outlier_contributors(const opc::ChainLayer& c, int G) {
+  std::vector<int32_t> n(std::max(c.OT, 0), 0);
+  for (int cta = 0; cta < G; ++cta) {
+    const opc::ChainPart p = opc::chain_part(c, cta, G);
+    for (int w = p.wp; w < opc::kQConsumers; ++w) {
+      int32_t u0 = 0, u1 = 0;
+      opc::chain_warp_range(p, w, &u0, &u1);
+      if (u0 >= u1) continue;
+      const int32_t t0 = (u0 - c.Up) / c.KO, t1 = (u1 - 1 - c.Up) / c.KO;
+      for (int32_t t = t0; t <= t1; ++t) ++n[t];
+    }
+  }
+  return n;
+}
+
+// Builds a chain from every rank's view (ranks[rank] is this process's own).  With own_scratch
+// (one GPU) the flags and exchange words are allocated here and ranks[rank]'s pointers set.
 int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t batch, int32_t rank, int32_t world,
                 std::vector<ChainRank>& ranks, bool own_scratch, opc_chain** out) {
   int dev = 0;
@@ -870,41 +889,54 @@ int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t 
   OPC_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, opc::kQThreads, smem),
            "cudaOccupancyMaxActiveBlocksPerMultiprocessor(chain)");
   if (per_sm < 1) return fail(OPC_ERR_UNSUPPORTED, "%s: chain kernel does not fit on an SM", fn);
+  const int G = dc.sm_count;
 
-  // device image: [layers | outlier tables | flag masks | epoch (| flags | acc)]
+  // device memory: [layers | onc | epoch] (copied) then [acc | ocnt (| flags | words)] (zeroed)
+  std::vector<opc::ChainLayer> hl(n);
+  std::vector<std::vector<int32_t>> onc(n);
   const size_t layers_bytes = align_up(sizeof(opc::ChainLayer) * n, 256);
-  std::vector<size_t> oref_off(n), mask_off(n);
-  std::vector<int32_t> n_oref(n, 0);
   size_t off = layers_bytes;
+  std::vector<size_t> onc_off(n), acc_off(n), ocnt_off(n), yw_off(n);
   for (int j = 0; j < n; ++j) {
-    for (int p = 0; p < world; ++p) n_oref[j] += static_cast<int32_t>(ranks[p].slots[j].size());
-    oref_off[j] = off;
-    off += align_up(static_cast<size_t>(n_oref[j]) * sizeof(opc::OutlierRef), 256);
-  }
-  for (int j = 0; j < n; ++j) {
-    mask_off[j] = off;
-    off += align_up(static_cast<size_t>(ceil_div(m_full[j], 16)) * sizeof(uint16_t), 256);
+    const opc_layer_plan& p = steps[j].layer->plan;
+    opc::ChainLayer& c = hl[j];
+    memset(&c, 0, sizeof(c));
+    c.Up = static_cast<int32_t>(p.packed_units);
+    c.U = static_cast<int32_t>(p.total_units);
+    c.MT = p.row_tiles;
+    c.KT = p.k_units;
+    c.OT = p.outlier_tiles;
+    c.KO = p.outlier_k_units;
+    onc[j] = outlier_contributors(c, G);
+    onc_off[j] = off;
+    off += align_up(std::max<size_t>(onc[j].size(), 1) * sizeof(int32_t), 256);
   }
   const size_t epoch_off = off;
   off += 256;
   const size_t image_bytes = off;
-  const size_t sync_bytes = chain_sync_bytes(world, dc.sm_count);
-  size_t acc_total = 0;
-  for (int j = 0; j < n; ++j) acc_total += chain_acc_bytes(steps[j].layer->plan);
-  const size_t sync_off = off;
-  if (own_scratch) off += sync_bytes + acc_total;
-
+  for (int j = 0; j < n; ++j) {
+    const opc_layer_plan& p = steps[j].layer->plan;
+    acc_off[j] = off;
+    off += align_up(static_cast<size_t>(n_slots_of(p)) * opc::kQMaxBatch * sizeof(unsigned long long), 256);
+    ocnt_off[j] = off;
+    off += align_up(static_cast<size_t>(std::max(p.outlier_tiles, 1)) * sizeof(int32_t), 256);
+  }
+  size_t sync_off = 0;
+  if (own_scratch) {
+    sync_off = off;
+    off += chain_sync_bytes(world, G);
+    for (int j = 0; j < n; ++j) {
+      yw_off[j] = off;
+      off += chain_words_bytes(steps[j].ldy, batch);
+    }
+  }
   void* mem = nullptr;
   OPC_CUDA(cudaMalloc(&mem, off), "cudaMalloc(chain)");
   char* base = static_cast<char*>(mem);
   ChainRank& me = ranks[rank];
   if (own_scratch) {
     me.sync = reinterpret_cast<unsigned int*>(base + sync_off);
-    size_t a = sync_off + sync_bytes;
-    for (int j = 0; j < n; ++j) {
-      me.acc[j] = reinterpret_cast<unsigned long long*>(base + a);
-      a += chain_acc_bytes(steps[j].layer->plan);
-    }
+    for (int j = 0; j < n; ++j) me.yw[j] = base + yw_off[j];
   }
 
   std::vector<unsigned char> img(image_bytes, 0);
@@ -912,8 +944,7 @@ int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t 
     const opc_chain_step& st = steps[j];
     const opc_layer* L = st.layer;
     const opc_layer_plan& p = L->plan;
-    opc::ChainLayer c;
-    memset(&c, 0, sizeof(c));
+    opc::ChainLayer& c = hl[j];
     c.units = static_cast<const uint8_t*>(L->units);
     c.ounits = ounits_q(L);
     c.cbq = codebooks_q(L);
@@ -921,51 +952,39 @@ int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t 
     c.orow = L->outlier_rows;
     c.oexp = L->outlier_rows + n_slots_of(p);
     c.x = static_cast<const __half*>(st.x);
-    c.acc = me.acc[j];
-    for (int q = 0; q < world; ++q) c.y_peer[q] = reinterpret_cast<__half*>(ranks[q].y[j]) + row_off[j];
-    c.oref = reinterpret_cast<const opc::OutlierRef*>(base + oref_off[j]);
-    c.mask_full = reinterpret_cast<const uint16_t*>(base + mask_off[j]);
+    c.xw = j > 0 ? reinterpret_cast<const uint32_t*>(me.yw[j - 1]) : nullptr;
+    c.acc = reinterpret_cast<unsigned long long*>(base + acc_off[j]);
+    c.ocnt = reinterpret_cast<int32_t*>(base + ocnt_off[j]);
+    c.onc = reinterpret_cast<const int32_t*>(base + onc_off[j]);
+    for (int q = 0; q < world; ++q) {
+      c.y_peer[q] = reinterpret_cast<__half*>(ranks[q].y[j]) + row_off[j];
+      c.yw_peer[q] = reinterpret_cast<uint32_t*>(ranks[q].yw[j]) + row_off[j];
+    }
     c.ldx = st.ldx;
     c.ldy = st.ldy;
-    c.Up = static_cast<int32_t>(p.packed_units);
-    c.U = static_cast<int32_t>(p.total_units);
+    c.ldxw = j > 0 ? chain_ldyw(steps[j - 1].ldy) : 0;
+    c.ldyw = chain_ldyw(st.ldy);
     c.M = p.M;
     c.K = p.K;
     c.K_pad = p.K_pad;
-    c.MT = p.row_tiles;
-    c.KT = p.k_units;
-    c.OT = p.outlier_tiles;
-    c.KO = p.outlier_k_units;
     c.x_vec16 = (p.K % 8 == 0) && (st.ldx % 8 == 0) && aligned(st.x, 16);
-    c.n_oref = n_oref[j];
     c.row_off = row_off[j];
     c.m_full = m_full[j];
+    // a later step writing the same fp16 buffer makes this step's fp16 stores dead
+    c.write_y = 1;
+    for (int k = j + 1; k < n; ++k)
+      if (steps[k].y == st.y && steps[k].ldy == st.ldy && m_full[k] >= m_full[j]) c.write_y = 0;
+    c.y_alias_x0 = j > 0 && (fp16_ranges_overlap(steps[0].x, steps[0].ldx, steps[0].layer->plan.K, st.y, st.ldy,
+                                                 m_full[j], batch) ||
+                             (world > 1 && j == n - 1));
     memcpy(img.data() + j * sizeof(opc::ChainLayer), &c, sizeof(c));
-    // every rank's outlier rows, in rank order, and their flags in the full output
-    opc::OutlierRef* refs = reinterpret_cast<opc::OutlierRef*>(img.data() + oref_off[j]);
-    uint16_t* mask = reinterpret_cast<uint16_t*>(img.data() + mask_off[j]);
-    int32_t k = 0, roff = 0;
-    for (int q = 0; q < world; ++q) {
-      for (const OutlierSlot& s : ranks[q].slots[j]) {
-        if (s.row < 0 || s.row >= ranks[q].M[j] || s.slot < 0) {
-          cudaFree(mem);
-          return fail(OPC_ERR_INVALID, "%s: step %d: rank %d: outlier row %d outside its %d rows", fn, j, q, s.row,
-                      ranks[q].M[j]);
-        }
-        opc::OutlierRef& r = refs[k++];
-        r.acc = ranks[q].acc[j] + 2 * static_cast<int64_t>(s.slot);
-        r.row = roff + s.row;
-        r.exp = s.exp;
-        r.owner = q;
-        r.pad = 0;
-        mask[r.row >> 4] = static_cast<uint16_t>(mask[r.row >> 4] | (1u << (r.row & 15)));
-      }
-      roff += ranks[q].M[j];
-    }
+    if (!onc[j].empty()) memcpy(img.data() + onc_off[j], onc[j].data(), onc[j].size() * sizeof(int32_t));
   }
   cudaError_t e = cudaMemcpy(base, img.data(), image_bytes, cudaMemcpyHostToDevice);
-  if (e == cudaSuccess) e = cudaMemset(me.sync, 0, sync_bytes);
-  if (e == cudaSuccess) e = cudaMemset(me.acc[0], 0, acc_total);
+  if (e == cudaSuccess) e = cudaMemset(base + image_bytes, 0, off - image_bytes);
+  if (e == cudaSuccess && !own_scratch) e = cudaMemset(me.sync, 0, chain_sync_bytes(world, G));
+  if (e == cudaSuccess && !own_scratch)
+    for (int j = 0; j < n && e == cudaSuccess; ++j) e = cudaMemset(me.yw[j], 0, chain_words_bytes(steps[j].ldy, batch));
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) {
     cudaFree(mem);
@@ -978,7 +997,7 @@ int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t 
   ch->stages = stages;
   ch->xs_bytes = xs;
   ch->smem = smem;
-  ch->grid = dc.sm_count;
+  ch->grid = G;
   ch->xc = xc;
   ch->rank = rank;
   ch->world = world;
@@ -987,23 +1006,22 @@ int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t 
   ch->d_sync = me.sync;
   for (int q = 0; q < world; ++q) ch->sync_peer[q] = ranks[q].sync;
   ch->d_epoch = reinterpret_cast<unsigned int*>(base + epoch_off);
-  ch->acc = me.acc[0];
-  ch->acc_bytes = acc_total;
   *out = ch;
   return OPC_OK;
 }
 
 // Exchanged description of one rank's shards (opc_chain_tp_info).
 constexpr uint32_t kTpInfoMagic = 0x4f504354u;  // "OPCT"
+constexpr uint32_t kTpInfoVersion = 2;
 struct TpInfoHeader {
   uint32_t magic, version;
   int32_t n_steps, grid, batch, world;
-  uint64_t region_bytes, scratch_offset, total_bytes;
+  uint64_t region_bytes, scratch_offset;
 };
 struct TpInfoStep {
-  int32_t M, K, n_out, pad;
-  uint64_t y_offset, acc_offset;
+  int32_t M, K;
   int64_t ldy;
+  uint64_t y_offset, yw_offset;
 };
 
 }  // namespace
@@ -1019,24 +1037,24 @@ int opc_chain_create(const opc_chain_step* steps, int32_t n_steps, int32_t batch
   std::vector<ChainRank> ranks(1);
   ChainRank& me = ranks[0];
   me.M.resize(n_steps);
-  me.slots.resize(n_steps);
   me.y.resize(n_steps);
-  me.acc.resize(n_steps, nullptr);
+  me.yw.resize(n_steps, nullptr);
   for (int j = 0; j < n_steps; ++j) {
-    if (!steps[j].layer || !plan_ok(&steps[j].layer->plan) || !steps[j].layer->outlier_rows)
+    if (!steps[j].layer || !plan_ok(&steps[j].layer->plan))
       return fail(OPC_ERR_INVALID, "opc_chain_create: step %d: invalid layer", j);
     me.M[j] = steps[j].layer->plan.M;
     me.y[j] = static_cast<char*>(steps[j].y);
-    const int rc = read_outlier_slots(steps[j].layer, &me.slots[j]);
-    if (rc != OPC_OK) return rc;
   }
   return chain_build("opc_chain_create", steps, n_steps, batch, 0, 1, ranks, true, out);
 }
 
-int opc_chain_tp_scratch_bytes(const opc_chain_step* steps, int32_t n_steps, int32_t world, size_t* bytes) {
+int opc_chain_tp_scratch_bytes(const opc_chain_step* steps, int32_t n_steps, int32_t batch, int32_t world,
+                               size_t* bytes) {
   if (!bytes) return fail(OPC_ERR_INVALID, "opc_chain_tp_scratch_bytes: bytes is NULL");
   *bytes = 0;
   if (!steps || n_steps < 1) return fail(OPC_ERR_INVALID, "opc_chain_tp_scratch_bytes: no steps");
+  if (batch < 1 || batch > opc::kQMaxBatch)
+    return fail(OPC_ERR_UNSUPPORTED, "opc_chain_tp_scratch_bytes: batch %d", batch);
   if (world < 1 || world > opc::kMaxRanks)
     return fail(OPC_ERR_UNSUPPORTED, "opc_chain_tp_scratch_bytes: world %d (1..%d)", world, opc::kMaxRanks);
   int dev = 0;
@@ -1046,9 +1064,8 @@ int opc_chain_tp_scratch_bytes(const opc_chain_step* steps, int32_t n_steps, int
   if (rc != OPC_OK) return rc;
   size_t b = chain_sync_bytes(world, dc.sm_count);
   for (int j = 0; j < n_steps; ++j) {
-    if (!steps[j].layer || !plan_ok(&steps[j].layer->plan))
-      return fail(OPC_ERR_INVALID, "opc_chain_tp_scratch_bytes: step %d: invalid layer", j);
-    b += chain_acc_bytes(steps[j].layer->plan);
+    if (steps[j].ldy < 1) return fail(OPC_ERR_INVALID, "opc_chain_tp_scratch_bytes: step %d: ldy not set", j);
+    b += chain_words_bytes(steps[j].ldy, batch);
   }
   *bytes = b;
   return OPC_OK;
@@ -1058,26 +1075,18 @@ int opc_chain_tp_info(const opc_chain_step* steps, int32_t n_steps, int32_t batc
                       size_t region_bytes, size_t scratch_offset, void* info, size_t* info_bytes) {
   if (!info_bytes) return fail(OPC_ERR_INVALID, "opc_chain_tp_info: info_bytes is NULL");
   if (!steps || n_steps < 1 || !region) return fail(OPC_ERR_INVALID, "opc_chain_tp_info: no steps or region");
-  if (batch < 1 || batch > opc::kQMaxBatch) return fail(OPC_ERR_UNSUPPORTED, "opc_chain_tp_info: batch %d", batch);
-  if (world < 1 || world > opc::kMaxRanks) return fail(OPC_ERR_UNSUPPORTED, "opc_chain_tp_info: world %d", world);
-  size_t scratch = 0;
-  int rc = opc_chain_tp_scratch_bytes(steps, n_steps, world, &scratch);
-  if (rc != OPC_OK) return rc;
-  if (scratch_offset % 256 || scratch_offset + scratch > region_bytes)
-    return fail(OPC_ERR_INVALID, "opc_chain_tp_info: scratch [%zu, +%zu) not 256-aligned inside the %zu-byte region",
-                scratch_offset, scratch, region_bytes);
-  std::vector<std::vector<OutlierSlot>> slots(n_steps);
-  size_t need = sizeof(TpInfoHeader) + sizeof(TpInfoStep) * n_steps;
-  for (int j = 0; j < n_steps; ++j) {
-    rc = read_outlier_slots(steps[j].layer, &slots[j]);
-    if (rc != OPC_OK) return rc;
-    need += slots[j].size() * sizeof(OutlierSlot);
-  }
+  const size_t need = sizeof(TpInfoHeader) + sizeof(TpInfoStep) * n_steps;
   if (!info) {
     *info_bytes = need;
     return OPC_OK;
   }
   if (*info_bytes < need) return fail(OPC_ERR_INVALID, "opc_chain_tp_info: %zu bytes given, %zu needed", *info_bytes, need);
+  size_t scratch = 0;
+  int rc = opc_chain_tp_scratch_bytes(steps, n_steps, batch, world, &scratch);
+  if (rc != OPC_OK) return rc;
+  if (scratch_offset % 256 || scratch_offset + scratch > region_bytes || reinterpret_cast<uintptr_t>(region) % 256)
+    return fail(OPC_ERR_INVALID, "opc_chain_tp_info: scratch [%zu, +%zu) not 256-aligned inside the %zu-byte region",
+                scratch_offset, scratch, region_bytes);
   int dev = 0;
   OPC_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
   DeviceCache dc;
@@ -1087,19 +1096,19 @@ int opc_chain_tp_info(const opc_chain_step* steps, int32_t n_steps, int32_t batc
   TpInfoHeader h;
   memset(&h, 0, sizeof(h));
   h.magic = kTpInfoMagic;
-  h.version = 1;
+  h.version = kTpInfoVersion;
   h.n_steps = n_steps;
   h.grid = dc.sm_count;
   h.batch = batch;
   h.world = world;
   h.region_bytes = region_bytes;
   h.scratch_offset = scratch_offset;
-  h.total_bytes = need;
   memcpy(o, &h, sizeof(h));
-  size_t acc = scratch_offset + chain_sync_bytes(world, dc.sm_count);
-  size_t tail = sizeof(TpInfoHeader) + sizeof(TpInfoStep) * n_steps;
+  size_t yw = scratch_offset + chain_sync_bytes(world, dc.sm_count);
   const char* rb = static_cast<const char*>(region);
   for (int j = 0; j < n_steps; ++j) {
+    if (!steps[j].layer || !plan_ok(&steps[j].layer->plan))
+      return fail(OPC_ERR_INVALID, "opc_chain_tp_info: step %d: invalid layer", j);
     const char* y = static_cast<const char*>(steps[j].y);
     if (!y || y < rb || y >= rb + region_bytes)
       return fail(OPC_ERR_INVALID, "opc_chain_tp_info: step %d: y is not inside the region", j);
@@ -1107,14 +1116,11 @@ int opc_chain_tp_info(const opc_chain_step* steps, int32_t n_steps, int32_t batc
     memset(&s, 0, sizeof(s));
     s.M = steps[j].layer->plan.M;
     s.K = steps[j].layer->plan.K;
-    s.n_out = static_cast<int32_t>(slots[j].size());
-    s.y_offset = static_cast<uint64_t>(y - rb);
-    s.acc_offset = acc;
     s.ldy = steps[j].ldy;
-    acc += chain_acc_bytes(steps[j].layer->plan);
+    s.y_offset = static_cast<uint64_t>(y - rb);
+    s.yw_offset = yw;
+    yw += chain_words_bytes(steps[j].ldy, batch);
     memcpy(o + sizeof(TpInfoHeader) + j * sizeof(TpInfoStep), &s, sizeof(s));
-    if (!slots[j].empty()) memcpy(o + tail, slots[j].data(), slots[j].size() * sizeof(OutlierSlot));
-    tail += slots[j].size() * sizeof(OutlierSlot);
   }
   *info_bytes = need;
   return OPC_OK;
@@ -1129,71 +1135,61 @@ int opc_chain_create_tp(const opc_chain_step* steps, int32_t n_steps, int32_t ba
   if (batch < 1 || batch > opc::kQMaxBatch) return fail(OPC_ERR_UNSUPPORTED, "%s: batch %d", fn, batch);
   if (world < 1 || world > opc::kMaxRanks || rank < 0 || rank >= world)
     return fail(OPC_ERR_UNSUPPORTED, "%s: rank %d of world %d (1..%d ranks)", fn, rank, world, opc::kMaxRanks);
+  for (int j = 0; j < n_steps; ++j)
+    if (!steps[j].layer || !plan_ok(&steps[j].layer->plan)) return fail(OPC_ERR_INVALID, "%s: step %d: invalid layer", fn, j);
   std::vector<ChainRank> ranks(world);
-  int32_t grid = -1;
+  std::vector<std::vector<TpInfoStep>> st(world, std::vector<TpInfoStep>(n_steps));
+  std::vector<TpInfoHeader> hd(world);
   for (int p = 0; p < world; ++p) {
     const unsigned char* b = static_cast<const unsigned char*>(infos[p]);
     if (!b || !regions[p]) return fail(OPC_ERR_INVALID, "%s: rank %d: no info or region", fn, p);
-    TpInfoHeader h;
+    TpInfoHeader& h = hd[p];
     memcpy(&h, b, sizeof(h));
-    if (h.magic != kTpInfoMagic || h.version != 1) return fail(OPC_ERR_INVALID, "%s: rank %d: not a chain info", fn, p);
+    if (h.magic != kTpInfoMagic || h.version != kTpInfoVersion)
+      return fail(OPC_ERR_INVALID, "%s: rank %d: not a chain info of this library version", fn, p);
     if (h.n_steps != n_steps || h.batch != batch || h.world != world)
       return fail(OPC_ERR_INVALID, "%s: rank %d: %d steps, batch %d, world %d (here %d, %d, %d)", fn, p, h.n_steps,
                   h.batch, h.world, n_steps, batch, world);
-    if (grid >= 0 && h.grid != grid) return fail(OPC_ERR_UNSUPPORTED, "%s: ranks run %d and %d CTAs", fn, grid, h.grid);
-    grid = h.grid;
+    if (h.grid != hd[0].grid) return fail(OPC_ERR_UNSUPPORTED, "%s: ranks run %d and %d CTAs", fn, hd[0].grid, h.grid);
+    for (int j = 0; j < n_steps; ++j) memcpy(&st[p][j], b + sizeof(TpInfoHeader) + j * sizeof(TpInfoStep), sizeof(TpInfoStep));
+  }
+  for (int p = 0; p < world; ++p) {
     ChainRank& r = ranks[p];
     r.M.resize(n_steps);
-    r.slots.resize(n_steps);
     r.y.resize(n_steps);
-    r.acc.resize(n_steps);
+    r.yw.resize(n_steps);
     char* region = static_cast<char*>(regions[p]);
+    const TpInfoHeader& h = hd[p];
+    if (h.scratch_offset + chain_sync_bytes(world, h.grid) > h.region_bytes)
+      return fail(OPC_ERR_INVALID, "%s: rank %d: flags outside its region", fn, p);
     r.sync = reinterpret_cast<unsigned int*>(region + h.scratch_offset);
-    size_t tail = sizeof(TpInfoHeader) + sizeof(TpInfoStep) * n_steps;
     for (int j = 0; j < n_steps; ++j) {
-      TpInfoStep s;
-      memcpy(&s, b + sizeof(TpInfoHeader) + j * sizeof(TpInfoStep), sizeof(s));
-      if (s.K != steps[j].layer->plan.K)
-        return fail(OPC_ERR_INVALID, "%s: rank %d step %d: K %d, here %d", fn, p, j, s.K, steps[j].layer->plan.K);
-      if (s.M < 1 || s.n_out < 0 || s.y_offset % 2 || s.acc_offset % 256 || s.acc_offset >= h.region_bytes ||
-          s.y_offset >= h.region_bytes)
-        return fail(OPC_ERR_INVALID, "%s: rank %d step %d: bad shard description", fn, p, j);
+      const TpInfoStep& s = st[p][j];
+      int64_t rows = 0;
+      for (int q = 0; q < world; ++q) rows += st[q][j].M;
+      if (s.K != steps[j].layer->plan.K || s.M < 1 || s.ldy != st[0][j].ldy || s.ldy < rows)
+        return fail(OPC_ERR_INVALID, "%s: rank %d step %d: K %d, rows %d, ld %lld (here K %d; full rows %lld)", fn, p, j,
+                    s.K, s.M, static_cast<long long>(s.ldy), steps[j].layer->plan.K, static_cast<long long>(rows));
+      const uint64_t y_end = s.y_offset + 2 * static_cast<uint64_t>((batch - 1) * s.ldy + rows);
+      const uint64_t w_end = s.yw_offset + chain_words_bytes(s.ldy, batch);
+      if (s.y_offset % 2 || s.yw_offset % 256 || y_end > h.region_bytes || w_end > h.region_bytes)
+        return fail(OPC_ERR_INVALID, "%s: rank %d step %d: outputs exceed its region", fn, p, j);
       r.M[j] = s.M;
       r.y[j] = region + s.y_offset;
-      r.acc[j] = reinterpret_cast<unsigned long long*>(region + s.acc_offset);
-      r.slots[j].resize(s.n_out);
-      if (s.n_out) memcpy(r.slots[j].data(), b + tail, s.n_out * sizeof(OutlierSlot));
-      tail += s.n_out * sizeof(OutlierSlot);
-    }
-    if (tail != h.total_bytes) return fail(OPC_ERR_INVALID, "%s: rank %d: info size mismatch", fn, p);
-    // every rank's copy of each full output lies inside its region
-    for (int j = 0; j < n_steps; ++j) {
-      TpInfoStep s;
-      memcpy(&s, b + sizeof(TpInfoHeader) + j * sizeof(TpInfoStep), sizeof(s));
-      int64_t rows = 0;
-      for (int q = 0; q < world; ++q) {
-        TpInfoStep sq;
-        memcpy(&sq, static_cast<const unsigned char*>(infos[q]) + sizeof(TpInfoHeader) + j * sizeof(TpInfoStep), sizeof(sq));
-        rows += sq.M;
-      }
-      const uint64_t end = s.y_offset + 2 * static_cast<uint64_t>((batch - 1) * s.ldy + rows);
-      if (s.ldy < rows || end > h.region_bytes)
-        return fail(OPC_ERR_INVALID, "%s: rank %d step %d: full output (%lld rows, ld %lld) exceeds its region", fn, p, j,
-                    static_cast<long long>(rows), static_cast<long long>(s.ldy));
+      r.yw[j] = region + s.yw_offset;
     }
   }
   ChainRank& me = ranks[rank];
-  for (int j = 0; j < n_steps; ++j) {
-    if (!steps[j].layer || !plan_ok(&steps[j].layer->plan) || steps[j].layer->plan.M != me.M[j] ||
-        static_cast<char*>(steps[j].y) != me.y[j])
+  for (int j = 0; j < n_steps; ++j)
+    if (steps[j].layer->plan.M != me.M[j] || static_cast<char*>(steps[j].y) != me.y[j] || steps[j].ldy != st[rank][j].ldy)
       return fail(OPC_ERR_INVALID, "%s: step %d: does not match this rank's info", fn, j);
-  }
   int dev = 0;
   OPC_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
   DeviceCache dc;
   const int rc = device_cache(dev, &dc);
   if (rc != OPC_OK) return rc;
-  if (dc.sm_count != grid) return fail(OPC_ERR_UNSUPPORTED, "%s: this GPU has %d SMs, the ranks %d", fn, dc.sm_count, grid);
+  if (dc.sm_count != hd[0].grid)
+    return fail(OPC_ERR_UNSUPPORTED, "%s: this GPU has %d SMs, the ranks %d", fn, dc.sm_count, hd[0].grid);
   return chain_build(fn, steps, n_steps, batch, rank, world, ranks, false, out);
 }
 
@@ -1203,7 +1199,6 @@ int opc_chain_launch(opc_chain* ch, void* stream_v) {
   OPC_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
   if (dev != ch->device) return fail(OPC_ERR_INVALID, "opc_chain_launch: chain lives on device %d, current is %d", ch->device, dev);
   cudaStream_t s = static_cast<cudaStream_t>(stream_v);
-  OPC_CUDA(cudaMemsetAsync(ch->acc, 0, ch->acc_bytes, s), "cudaMemsetAsync(chain accumulators)");
   opc::ChainArgs a;
   memset(&a, 0, sizeof(a));
   a.layers = ch->d_layers;

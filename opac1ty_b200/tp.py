@@ -21,8 +21,8 @@ That per-projection GEMV + all-gather form is the baseline.
 
 ``TPChain`` runs the same sharded step (batch 1..2) as ONE persistent kernel per rank
 (``opc_chain_create_tp``): every rank stores its output rows straight into every rank's copy of
-the full activations through CUDA IPC peer pointers, and a barrier over peer flags separates the
-projections, so there is neither an all-gather nor a launch per projection.
+the full activations through CUDA IPC peer pointers, as tagged words that the next projection's
+readers poll, so there is neither an all-gather, nor a launch, nor a barrier per projection.
 """
 
 from __future__ import annotations
@@ -270,8 +270,7 @@ class TPDecodeStack:
 # ---------------------------------------------------------------------------------------------
 # The same row-sharded step as ONE persistent kernel per rank (opc_chain_create_tp): each rank
 # stores its rows of every projection straight into every rank's copy of the full output over
-# NVLink and a cross-rank barrier over peer flags separates the projections, so the step has no
-# all-gather launch and no NCCL call.
+# NVLink (tagged words the readers poll), so the step has no all-gather launch and no NCCL call.
 # ---------------------------------------------------------------------------------------------
 
 PROJ_ORDER = ("qkv", "o", "gate_up", "down")
@@ -396,12 +395,14 @@ class TPChain:
         n = len(projs)
         lib = _lib.load()
         arr = (_lib.ChainStep * n)()
+        rows = [p.M for p in projs]
+        _, lds, _, _ = chain_region_layout(rows, self.batch, 0)
         for j, p in enumerate(projs):
             arr[j].layer = ctypes.pointer(p.layer.c_layer)
+            arr[j].ldy = lds[j]
         scratch = ctypes.c_size_t(0)
         with torch.cuda.device(self.device):
-            _lib.check(lib.opc_chain_tp_scratch_bytes(arr, n, stack.world, ctypes.byref(scratch)))
-        rows = [p.M for p in projs]
+            _lib.check(lib.opc_chain_tp_scratch_bytes(arr, n, self.batch, stack.world, ctypes.byref(scratch)))
         offs, lds, soff, total = chain_region_layout(rows, self.batch, scratch.value)
         self.region = PeerRegion(total, stack.rank, stack.world, all_gather_obj, self.device)
         self._handle = ctypes.c_void_p()

@@ -96,15 +96,36 @@ def test_tp_chain_graph_replay(cuda_device):
     st.close()
 
 
-def _rank_steps(stack, region_ptr, offs, lds, arr):
+def _rank_region(stack, batch, world, arr):
+    """Fill `arr` with a rank's steps (x of step 0 = the last step's output, as TPChain does)
+    inside a freshly allocated region; returns (region pointer, its bytes, scratch offset)."""
+    lib = _lib.load()
     projs = [blk[name] for blk in stack.blocks for name in tp.PROJ_ORDER]
+    n = len(projs)
+    _, lds, _, _ = tp.chain_region_layout([p.M for p in projs], batch, 0)
     for j, p in enumerate(projs):
         arr[j].layer = ctypes.pointer(p.layer.c_layer)
-        arr[j].y = region_ptr + offs[j]
         arr[j].ldy = lds[j]
-        arr[j].x = region_ptr + offs[j - 1]
+    scratch = ctypes.c_size_t(0)
+    _lib.check(lib.opc_chain_tp_scratch_bytes(arr, n, batch, world, ctypes.byref(scratch)))
+    offs, lds, soff, total = tp.chain_region_layout([p.M for p in projs], batch, scratch.value)
+    ptr = ctypes.c_void_p()
+    handle = (ctypes.c_ubyte * _lib.OPC_PEER_HANDLE_BYTES)()
+    _lib.check(lib.opc_peer_alloc(total, ctypes.byref(ptr), handle))
+    for j in range(n):
+        arr[j].y = ptr.value + offs[j]
+        arr[j].x = ptr.value + offs[j - 1]
         arr[j].ldx = lds[j - 1]
-    return projs
+    return ptr, total, soff
+
+
+def _info(arr, n, batch, world, ptr, total, soff):
+    lib = _lib.load()
+    need = ctypes.c_size_t(0)
+    _lib.check(lib.opc_chain_tp_info(arr, n, batch, world, ptr.value, total, soff, None, ctypes.byref(need)))
+    info = (ctypes.c_ubyte * need.value)()
+    _lib.check(lib.opc_chain_tp_info(arr, n, batch, world, ptr.value, total, soff, info, ctypes.byref(need)))
+    return info
 
 
 @pytest.mark.gpu
@@ -119,20 +140,9 @@ def test_tp_chain_barrier_times_out_without_peer(cuda_device):
     try:
         for r in range(world):
             arr = (_lib.ChainStep * n)()
-            projs = _rank_steps(stacks[r], 0, [0] * n, [1] * n, arr)
-            scratch = ctypes.c_size_t(0)
-            _lib.check(lib.opc_chain_tp_scratch_bytes(arr, n, world, ctypes.byref(scratch)))
-            offs, lds, soff, total = tp.chain_region_layout([p.M for p in projs], batch, scratch.value)
-            ptr = ctypes.c_void_p()
-            handle = (ctypes.c_ubyte * _lib.OPC_PEER_HANDLE_BYTES)()
-            _lib.check(lib.opc_peer_alloc(total, ctypes.byref(ptr), handle))
+            ptr, total, soff = _rank_region(stacks[r], batch, world, arr)
             regions.append(ptr)
-            _rank_steps(stacks[r], ptr.value, offs, lds, arr)
-            need = ctypes.c_size_t(0)
-            _lib.check(lib.opc_chain_tp_info(arr, n, batch, world, ptr.value, total, soff, None, ctypes.byref(need)))
-            info = (ctypes.c_ubyte * need.value)()
-            _lib.check(lib.opc_chain_tp_info(arr, n, batch, world, ptr.value, total, soff, info, ctypes.byref(need)))
-            infos.append(info)
+            infos.append(_info(arr, n, batch, world, ptr, total, soff))
             keep.append(arr)
         assert _take_error() == 0
         rptrs = (ctypes.c_void_p * world)(*[p.value for p in regions])
@@ -163,21 +173,11 @@ def test_tp_chain_create_rejects_mismatched_infos(cuda_device):
     lib = _lib.load()
     n = 4
     arr = (_lib.ChainStep * n)()
-    projs = _rank_steps(stacks[0], 0, [0] * n, [1] * n, arr)
-    scratch = ctypes.c_size_t(0)
-    _lib.check(lib.opc_chain_tp_scratch_bytes(arr, n, world, ctypes.byref(scratch)))
-    offs, lds, soff, total = tp.chain_region_layout([p.M for p in projs], batch, scratch.value)
-    ptr = ctypes.c_void_p()
-    handle = (ctypes.c_ubyte * _lib.OPC_PEER_HANDLE_BYTES)()
-    _lib.check(lib.opc_peer_alloc(total, ctypes.byref(ptr), handle))
+    ptr, total, soff = _rank_region(stacks[0], batch, world, arr)
     try:
-        _rank_steps(stacks[0], ptr.value, offs, lds, arr)
-        need = ctypes.c_size_t(0)
-        _lib.check(lib.opc_chain_tp_info(arr, n, batch, world, ptr.value, total, soff, None, ctypes.byref(need)))
-        info = (ctypes.c_ubyte * need.value)()
-        _lib.check(lib.opc_chain_tp_info(arr, n, batch, world, ptr.value, total, soff, info, ctypes.byref(need)))
+        info = _info(arr, n, batch, world, ptr, total, soff)
         # rank 1 claiming batch 2 (byte 16 of the header) must be rejected
-        bad = (ctypes.c_ubyte * need.value).from_buffer_copy(bytes(info))
+        bad = (ctypes.c_ubyte * len(info)).from_buffer_copy(bytes(info))
         ctypes.c_int32.from_buffer(bad, 16).value = 2
         rptrs = (ctypes.c_void_p * world)(ptr.value, ptr.value)
         iptrs = (ctypes.c_void_p * world)(ctypes.addressof(info), ctypes.addressof(bad))
@@ -186,6 +186,7 @@ def test_tp_chain_create_rejects_mismatched_infos(cuda_device):
         assert rc == _lib.OPC_ERR_INVALID and not h.value
         # y outside the region is rejected when describing the shard
         arr[1].y = ptr.value + total + 64
+        need = ctypes.c_size_t(len(info))
         rc = lib.opc_chain_tp_info(arr, n, batch, world, ptr.value, total, soff, info, ctypes.byref(need))
         assert rc == _lib.OPC_ERR_INVALID
     finally:
