@@ -69,13 +69,14 @@ static_assert(sizeof(ChainLayer) % 16 == 0, "ChainLayer is copied in 16-byte pie
 
 struct ChainArgs {
   const ChainLayer* layers;
+  const int4* parts;         // [n_layers][grid][2] each CTA's share: {pu0, pu1, ou0, ou1}, {wp, 0, 0, 0}
   unsigned int* sync;        // [world][grid] flags of every rank's CTAs, in this rank's memory
   unsigned int* sync_peer[kMaxRanks];  // rank p's flag array (sync_peer[rank] == sync)
   unsigned int* epoch;       // [0] launches completed (bit 31: poisoned), [1] CTAs finished
   unsigned long long* trace; // optional [n_layers][grid][8] globaltimer stamps (ns) per CTA,
-                             // taken by its first consumer thread: layer start, first x poll
-                             // done, x complete, max barrier passed, x staged, own units done,
-                             // then two unused slots
+                             // taken by its first consumer thread: layer start, setup done,
+                             // first x poll done, x complete, max barrier passed, digits
+                             // stored, x staged, own units done
   int32_t n_layers, batch, stages, xs_bytes;
   uint32_t negz;
   int32_t l2_prefetch;       // prefetch each consumer's share of the next layer into L2
@@ -127,16 +128,27 @@ __host__ __device__ __forceinline__ ChainPart chain_part(const ChainLayer& L, in
   if (p.wp > np) p.wp = np;
   return p;
 }
+// Warp w's unit range within its CTA's share (32-bit arithmetic: a CTA's share times the 15
+// warps stays below 2^31, host-checked).
 __host__ __device__ __forceinline__ void chain_warp_range(const ChainPart& p, int w, int32_t* u0, int32_t* u1) {
   if (w < p.wp) {
     const int32_t np = p.pu1 - p.pu0;
-    *u0 = p.pu0 + partq_start(w, np, p.wp);
-    *u1 = p.pu0 + partq_start(w + 1, np, p.wp);
+    *u0 = p.pu0 + w * np / p.wp;
+    *u1 = p.pu0 + (w + 1) * np / p.wp;
   } else {
     const int32_t no = p.ou1 - p.ou0, nw = kQConsumers - p.wp;
-    *u0 = p.ou0 + partq_start(w - p.wp, no, nw);
-    *u1 = p.ou0 + partq_start(w - p.wp + 1, no, nw);
+    *u0 = p.ou0 + (w - p.wp) * no / nw;
+    *u1 = p.ou0 + (w - p.wp + 1) * no / nw;
   }
+}
+__device__ __forceinline__ ChainPart chain_part_load(const int4* e) {
+  ChainPart p;
+  p.pu0 = e[0].x;
+  p.pu1 = e[0].y;
+  p.ou0 = e[0].z;
+  p.ou1 = e[0].w;
+  p.wp = e[1].x;
+  return p;
 }
 
 // Unit cursor over a layer (segments: packed tiles of KT units, outlier tiles of KO units).
@@ -249,6 +261,7 @@ constexpr int kChainSplitSlots = 32;  // packed tiles per CTA and layer (host-ch
 
 struct ChainShared {
   ChainLayer layer[2];                    // descriptors of layers j (slot j&1) and j+1
+  int4 part[2][2];                        // this CTA's share of layers j and j+1
   float amax[kQConsumers][kQMaxBatch];    // staging: per-warp max |x|
   unsigned long long tile_acc[kChainSplitSlots][kTileRows][kQMaxBatch];  // split packed tiles
   int32_t tile_cnt[kChainSplitSlots];
@@ -343,6 +356,8 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
   if (threadIdx.x < sizeof(ChainLayer) / 16 && args.n_layers > 0)
     reinterpret_cast<uint4*>(&sh->layer[0])[threadIdx.x] = reinterpret_cast<const uint4*>(args.layers)[threadIdx.x];
   __syncthreads();
+  if (threadIdx.x < 2 && args.n_layers > 0) sh->part[0][threadIdx.x] = args.parts[2 * blockIdx.x + threadIdx.x];
+  __syncthreads();
   if (sh->abort) return;  // poisoned: no work, no flags
 
   // ------------------------------------------------------------------ producer warp
@@ -360,7 +375,7 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     auto prefetch_next = [&](int jn) {
       if (!args.l2_prefetch || jn >= args.n_layers) return;
       const ChainLayer& N = args.layers[jn];
-      const ChainPart p = chain_part(N, cta, G);
+      const ChainPart p = chain_part_load(args.parts + 2 * (static_cast<int64_t>(jn) * G + cta));
       int32_t a0, a1;
       chain_warp_range(p, i, &a0, &a1);
       if (a0 >= a1) return;
@@ -378,7 +393,7 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     auto next_range = [&]() {
       while (j < args.n_layers) {
         Lp = args.layers + j;
-        const ChainPart p = chain_part(*Lp, cta, G);
+        const ChainPart p = chain_part_load(args.parts + 2 * (static_cast<int64_t>(j) * G + cta));
         int32_t u0;
         chain_warp_range(p, i, &u0, &u1);
         prefetch_next(j + 1);
@@ -494,7 +509,9 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     // Everything about this warp's share that does not depend on x, before x is complete.
     GemvQArgs qa;  // the per-layer view load_metaq takes
     qa.cbq = L.cbq; qa.tile_mask = L.tile_mask; qa.orow = L.orow; qa.oexp = L.oexp; qa.M = L.M; qa.MT = L.MT;
-    const ChainPart part = chain_part(L, cta, G);
+    unsigned long long* tr = args.trace ? args.trace + (static_cast<int64_t>(j) * G + cta) * kChainTracePhases : nullptr;
+    if (tr && tid == 0) tr[0] = globaltimer_ns();
+    const ChainPart part = chain_part_load(sh->part[j & 1]);
     int32_t u0, u1;
     chain_warp_range(part, warp, &u0, &u1);
     ChainCursor cc = chain_cursor(L, u0 < u1 ? u0 : 0);
@@ -503,13 +520,21 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
       cur = load_metaq(qa, cc.seg, g);
       nxt = (cc.seg + 1 < L.MT + L.OT) ? load_metaq(qa, cc.seg + 1, g) : cur;
     }
-    // next layer's descriptor: loaded now, stored to shared memory once every warp is past this
-    // layer's first staging barrier (nobody reads the slot's old descriptor after that)
-    const bool copy_desc = j + 1 < args.n_layers && tid < static_cast<int>(sizeof(ChainLayer) / 16);
+    // next layer's descriptor and this CTA's share of it: loaded now, stored to shared memory
+    // once every warp is past this layer's first staging barrier (nobody reads the slots' old
+    // contents after that)
+    constexpr int kDescPieces = static_cast<int>(sizeof(ChainLayer) / 16);
+    const bool copy_desc = j + 1 < args.n_layers && tid < kDescPieces + 2;
     uint4 desc_piece = make_uint4(0, 0, 0, 0);
-    if (copy_desc) desc_piece = ld_nc_v4(reinterpret_cast<const uint4*>(args.layers + j + 1) + tid);
-    unsigned long long* tr = args.trace ? args.trace + (static_cast<int64_t>(j) * G + cta) * kChainTracePhases : nullptr;
-    if (tr && tid == 0) tr[0] = globaltimer_ns();
+    if (copy_desc) {
+      if (tid < kDescPieces) {
+        desc_piece = ld_nc_v4(reinterpret_cast<const uint4*>(args.layers + j + 1) + tid);
+      } else {
+        const int4* pe = args.parts + 2 * (static_cast<int64_t>(j + 1) * G + cta) + (tid - kDescPieces);
+        desc_piece = ld_nc_v4(reinterpret_cast<const uint4*>(pe));
+      }
+    }
+    if (tr && tid == 0) tr[1] = globaltimer_ns();
 
     // ---- stage x_j.  Layer 0 reads the fp16 input; later layers poll the previous layer's
     // exchange words of their chunks until every tag is this launch's (bounded).
@@ -546,7 +571,7 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
           }
         }
       }
-      if (tr && tid == 0) tr[1] = globaltimer_ns();
+      if (tr && tid == 0) tr[2] = globaltimer_ns();
       if (pending) {
         const uint64_t t0 = globaltimer_ns();
         for (;;) {
@@ -568,7 +593,7 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
           }
         }
       }
-      if (tr && tid == 0) tr[2] = globaltimer_ns();
+      if (tr && tid == 0) tr[3] = globaltimer_ns();
       float mx[kQMaxBatch] = {0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < kXC; ++i) {
@@ -595,12 +620,15 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
       }
       if (tid < 8) sts128(xs_base + args.xs_bytes - kQZeroBytes + tid * 16, make_uint4(0, 0, 0, 0));
       named_barrier(1, kQConsumerThreads);  // every warp is done with layer j-1 and holds its x
-      if (tr && tid == 0) tr[3] = globaltimer_ns();
+      if (tr && tid == 0) tr[4] = globaltimer_ns();
       if (sh->abort) {
         ok = false;
         break;
       }
-      if (copy_desc) reinterpret_cast<uint4*>(&sh->layer[(j + 1) & 1])[tid] = desc_piece;
+      if (copy_desc) {
+        if (tid < kDescPieces) reinterpret_cast<uint4*>(&sh->layer[(j + 1) & 1])[tid] = desc_piece;
+        else reinterpret_cast<uint4*>(sh->part[(j + 1) & 1])[tid - kDescPieces] = desc_piece;
+      }
       if (j == 0) publish(f_staged0);  // layer-0 input read by every thread of this CTA
       {
         float m0 = 0.f, m1 = 0.f;
@@ -637,6 +665,7 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
           for (int dd = 0; dd < 3; ++dd) sts64(xs_base + (3 * b + dd) * colb + pos, d[dd][0], d[dd][1]);
         }
       }
+      if (tr && tid == 0) tr[5] = globaltimer_ns();
       // a layer writing over the chain input starts once every CTA has read that input
       if (L.y_alias_x0 && warp == 0 && !poll_flags_warp(args.sync, n_flags, lane, f_staged0, sys) && lane == 0) {
         sh->abort = 1;
@@ -648,7 +677,7 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
         break;
       }
     }
-    if (tr && tid == 0) tr[4] = globaltimer_ns();
+    if (tr && tid == 0) tr[6] = globaltimer_ns();
 
     // ---- this warp's units of layer j
     const int bcol = g >> 2, dig = g & 3;
@@ -783,7 +812,7 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
         ok = true;      // this warp still takes part in the CTA's barriers until then
       }
     }
-    if (tr && tid == 0) tr[5] = globaltimer_ns();
+    if (tr && tid == 0) tr[7] = globaltimer_ns();
   }
 
   // ---- end of the launch.  Several ranks: a last barrier, so that no rank starts its next

@@ -754,8 +754,9 @@ struct opc_chain {
   int32_t n_layers = 0, batch = 1, stages = 2, xs_bytes = 0, grid = 0, xc = 8;
   int32_t rank = 0, world = 1;
   size_t smem = 0;
-  void* dev_mem = nullptr;              // [layers | onc | epoch | acc | ocnt (| flags | words)]
+  void* dev_mem = nullptr;              // [layers | onc | parts | epoch | acc | ocnt (| flags | words)]
   opc::ChainLayer* d_layers = nullptr;
+  const int4* d_parts = nullptr;        // [layers][grid][2] CTA shares
   unsigned int* d_sync = nullptr;       // this rank's flags [world][grid]
   unsigned int* sync_peer[opc::kMaxRanks] = {};
   unsigned int* d_epoch = nullptr;      // [2]
@@ -817,7 +818,9 @@ int check_chain_steps(const char* fn, const opc_chain_step* steps, int32_t n, in
     if (static_cast<int64_t>(batch) * p.K_pad > 64 * opc::kQConsumerThreads)
       return fail(OPC_ERR_UNSUPPORTED, "%s: step %d: batch*K_pad = %lld > %d", fn, j,
                   static_cast<long long>(batch) * p.K_pad, 64 * opc::kQConsumerThreads);
-    if (p.total_units >= (int64_t(1) << 31)) return fail(OPC_ERR_UNSUPPORTED, "%s: step %d: layer too large", fn, j);
+    // the kernel's warp ranges use 32-bit products of a share's size and the warp count
+    if (p.total_units * (opc::kQConsumers + 1) >= (int64_t(1) << 31))
+      return fail(OPC_ERR_UNSUPPORTED, "%s: step %d: layer too large", fn, j);
   }
   // fp16 outputs: step 0's may not overlap the input; two steps' outputs are the same buffer
   // (then only the later one is written) or disjoint
@@ -891,12 +894,13 @@ int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t 
   if (per_sm < 1) return fail(OPC_ERR_UNSUPPORTED, "%s: chain kernel does not fit on an SM", fn);
   const int G = dc.sm_count;
 
-  // device memory: [layers | onc | epoch] (copied) then [acc | ocnt (| flags | words)] (zeroed)
+  // device memory: [layers | onc | parts | epoch] (copied) then [acc | ocnt (| flags | words)] (zeroed)
   std::vector<opc::ChainLayer> hl(n);
   std::vector<std::vector<int32_t>> onc(n);
   const size_t layers_bytes = align_up(sizeof(opc::ChainLayer) * n, 256);
   size_t off = layers_bytes;
   std::vector<size_t> onc_off(n), acc_off(n), ocnt_off(n), yw_off(n);
+  std::vector<int32_t> parts(8 * static_cast<size_t>(G) * n, 0);  // [n][G][2] int4
   for (int j = 0; j < n; ++j) {
     const opc_layer_plan& p = steps[j].layer->plan;
     opc::ChainLayer& c = hl[j];
@@ -910,7 +914,19 @@ int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t 
     onc[j] = outlier_contributors(c, G);
     onc_off[j] = off;
     off += align_up(std::max<size_t>(onc[j].size(), 1) * sizeof(int32_t), 256);
+    // each CTA's share, so the kernel does no partition arithmetic: {pu0, pu1, ou0, ou1}, {wp, 0, 0, 0}
+    for (int cta = 0; cta < G; ++cta) {
+      const opc::ChainPart pt = opc::chain_part(c, cta, G);
+      int32_t* e = parts.data() + 8 * (static_cast<size_t>(j) * G + cta);
+      e[0] = pt.pu0;
+      e[1] = pt.pu1;
+      e[2] = pt.ou0;
+      e[3] = pt.ou1;
+      e[4] = pt.wp;
+    }
   }
+  const size_t parts_off = off;
+  off += align_up(parts.size() * sizeof(int32_t), 256);
   const size_t epoch_off = off;
   off += 256;
   const size_t image_bytes = off;
@@ -979,7 +995,9 @@ int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t 
                              (world > 1 && j == n - 1));
     memcpy(img.data() + j * sizeof(opc::ChainLayer), &c, sizeof(c));
     if (!onc[j].empty()) memcpy(img.data() + onc_off[j], onc[j].data(), onc[j].size() * sizeof(int32_t));
+
   }
+  memcpy(img.data() + parts_off, parts.data(), parts.size() * sizeof(int32_t));
   cudaError_t e = cudaMemcpy(base, img.data(), image_bytes, cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMemset(base + image_bytes, 0, off - image_bytes);
   if (e == cudaSuccess && !own_scratch) e = cudaMemset(me.sync, 0, chain_sync_bytes(world, G));
@@ -1003,6 +1021,7 @@ int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t 
   ch->world = world;
   ch->dev_mem = mem;
   ch->d_layers = reinterpret_cast<opc::ChainLayer*>(base);
+  ch->d_parts = reinterpret_cast<const int4*>(base + parts_off);
   ch->d_sync = me.sync;
   for (int q = 0; q < world; ++q) ch->sync_peer[q] = ranks[q].sync;
   ch->d_epoch = reinterpret_cast<unsigned int*>(base + epoch_off);
@@ -1202,6 +1221,7 @@ int opc_chain_launch(opc_chain* ch, void* stream_v) {
   opc::ChainArgs a;
   memset(&a, 0, sizeof(a));
   a.layers = ch->d_layers;
+  a.parts = ch->d_parts;
   a.sync = ch->d_sync;
   for (int p = 0; p < ch->world; ++p) a.sync_peer[p] = ch->sync_peer[p];
   a.epoch = ch->d_epoch;
