@@ -66,6 +66,7 @@ struct ChainLayer {
 };
 
 static_assert(sizeof(ChainLayer) % 16 == 0, "ChainLayer is copied in 16-byte pieces");
+static_assert(sizeof(ChainLayer) / 16 + 2 <= 32, "one warp copies a descriptor and a CTA share");
 
 struct ChainArgs {
   const ChainLayer* layers;
@@ -516,21 +517,23 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     chain_warp_range(part, warp, &u0, &u1);
     ChainCursor cc = chain_cursor(L, u0 < u1 ? u0 : 0);
     MetaQ cur, nxt;
-    if (u0 < u1) {
+    if (u0 < u1) {  // both loads issued here, first used in the units loop (no select on them)
       cur = load_metaq(qa, cc.seg, g);
-      nxt = (cc.seg + 1 < L.MT + L.OT) ? load_metaq(qa, cc.seg + 1, g) : cur;
+      nxt = load_metaq(qa, min(cc.seg + 1, L.MT + L.OT - 1), g);
     }
     // next layer's descriptor and this CTA's share of it: loaded now, stored to shared memory
     // once every warp is past this layer's first staging barrier (nobody reads the slots' old
     // contents after that)
+    // (the last consumer warp: with more chunks than threads, the first warps stage more of x)
     constexpr int kDescPieces = static_cast<int>(sizeof(ChainLayer) / 16);
-    const bool copy_desc = j + 1 < args.n_layers && tid < kDescPieces + 2;
+    const int dt = tid - (kQConsumerThreads - 32);
+    const bool copy_desc = j + 1 < args.n_layers && dt >= 0 && dt < kDescPieces + 2;
     uint4 desc_piece = make_uint4(0, 0, 0, 0);
     if (copy_desc) {
-      if (tid < kDescPieces) {
-        desc_piece = ld_nc_v4(reinterpret_cast<const uint4*>(args.layers + j + 1) + tid);
+      if (dt < kDescPieces) {
+        desc_piece = ld_nc_v4(reinterpret_cast<const uint4*>(args.layers + j + 1) + dt);
       } else {
-        const int4* pe = args.parts + 2 * (static_cast<int64_t>(j + 1) * G + cta) + (tid - kDescPieces);
+        const int4* pe = args.parts + 2 * (static_cast<int64_t>(j + 1) * G + cta) + (dt - kDescPieces);
         desc_piece = ld_nc_v4(reinterpret_cast<const uint4*>(pe));
       }
     }
@@ -626,8 +629,8 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
         break;
       }
       if (copy_desc) {
-        if (tid < kDescPieces) reinterpret_cast<uint4*>(&sh->layer[(j + 1) & 1])[tid] = desc_piece;
-        else reinterpret_cast<uint4*>(sh->part[(j + 1) & 1])[tid - kDescPieces] = desc_piece;
+        if (dt < kDescPieces) reinterpret_cast<uint4*>(&sh->layer[(j + 1) & 1])[dt] = desc_piece;
+        else reinterpret_cast<uint4*>(sh->part[(j + 1) & 1])[dt - kDescPieces] = desc_piece;
       }
       if (j == 0) publish(f_staged0);  // layer-0 input read by every thread of this CTA
       {

@@ -1,4 +1,4 @@
-"""Row-sharded decode chain on 2 GPUs, checked against the oracle's unsharded chain: the NCCL
+"""Row-sharded decode chain on 2 (and 4, 8) GPUs, checked against the oracle's unsharded chain: the NCCL
 form (GEMV + all-gather per projection) and the fused form (TPChain: one kernel per rank, rows
 stored into every rank's activations over NVLink), which must equal the NCCL form bit for bit.
 
@@ -125,15 +125,15 @@ def _rank_fused(rank, world, port, batch, out_path):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("batch", [1, 2])
-def test_tp2_fused_chain_equals_nccl_and_oracle(tmp_path, batch):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+@pytest.mark.parametrize("world,batch", [(2, 1), (2, 2), (4, 1), (8, 2)])
+def test_tp_fused_chain_equals_nccl_and_oracle(tmp_path, world, batch):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     out = str(tmp_path / "yf.npy")
-    mp.start_processes(_rank_fused, args=(2, port, batch, out), nprocs=2, join=True, start_method="spawn")
+    mp.start_processes(_rank_fused, args=(world, port, batch, out), nprocs=world, join=True, start_method="spawn")
     flags = np.load(out + ".flags.npy")
     assert flags[:, 0].all(), f"fused chain differs from the NCCL form on some rank: {flags}"
     assert (flags[:, 1] == 0).all(), f"device errors: {flags}"
