@@ -217,9 +217,8 @@ int opc_chain_destroy(opc_chain* chain);
  * done, then two unused slots.  Layout [step][cta][8] uint64; NULL turns tracing off.
  * opc_chain_grid() is the number of CTAs (one per SM). */
 size_t opc_chain_trace_bytes(const opc_chain* chain);
-/* Options: OPC_CHAIN_L2_PREFETCH (default 0): while a step runs, prefetch each SM's share of the
- * next step's weights into L2 and stream the current ones with an evict-first policy (measured
- * ~5% slower on the Llama-3.1-8B decode step, kept as an option). */
+/* Options: OPC_CHAIN_L2_PREFETCH (default 0): stream the weights with an L2 evict-first policy
+ * (measured no faster on the Llama-3.1-8B decode step, kept as an option). */
 enum { OPC_CHAIN_L2_PREFETCH = 1 };
 int opc_chain_set_option(opc_chain* chain, int32_t option, int32_t value);
 int32_t opc_chain_grid(const opc_chain* chain);

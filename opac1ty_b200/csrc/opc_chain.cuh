@@ -80,7 +80,7 @@ struct ChainArgs {
                              // stored, x staged, own units done
   int32_t n_layers, batch, stages, xs_bytes;
   uint32_t negz;
-  int32_t l2_prefetch;       // prefetch each consumer's share of the next layer into L2
+  int32_t l2_prefetch;       // stream weights with an L2 evict-first policy
   int32_t rank, world;
 };
 constexpr int kChainTracePhases = 8;
@@ -221,7 +221,7 @@ __device__ __forceinline__ void st_relaxed_sys_u32(unsigned int* p, uint32_t v) 
 // One warp polls n flags (lane l: flags l, l+32, ...; independent relaxed loads, all in flight
 // together) until every one has reached target (modulo 2^32), bounded by kWaitLimitNs; then an
 // acquire fence orders the caller's later accesses.
-__device__ __forceinline__ bool poll_flags_warp(const unsigned int* flags, int n, int lane, uint32_t target, bool sys) {
+__device__ __noinline__ bool poll_flags_warp(const unsigned int* flags, int n, int lane, uint32_t target, bool sys) {
   uint64_t t0 = 0;
   for (;;) {
     bool reached = true;
@@ -243,6 +243,11 @@ __device__ __forceinline__ bool poll_flags_warp(const unsigned int* flags, int n
 // Exact 2^e for e in [-126, 127].
 __device__ __forceinline__ float pow2f(int e) { return __int_as_float((127 + e) << 23); }
 
+// Code size matters here: the kernel's once-per-layer paths (staging, tails, the producer) run
+// while the weight stream saturates L2, where every instruction-cache miss costs a microsecond,
+// so they are kept small -- per-chunk work is an out-of-line function called per chunk, not
+// unrolled copies.  Only the units loop is unrolled.
+
 // Eight exchange words of k..k+7 (the first n_valid inside the row): do all carry `tag`?  Then
 // their fp16 values, packed in pairs, go to v.
 __device__ __forceinline__ bool chain_take_words(const uint4& a, const uint4& c, uint32_t tag, int n_valid, uint4* v) {
@@ -258,6 +263,66 @@ __device__ __forceinline__ bool chain_take_words(const uint4& a, const uint4& c,
   return true;
 }
 
+// One poll of x chunk (batch row b, columns k..k+7) of a layer >= 1: ok when every word carries
+// `tag`, with the fp16 values in v (returned by value: no address, so no local memory).
+struct ChainChunk {
+  uint4 v;
+  int ok;
+};
+__device__ __noinline__ ChainChunk chain_poll_chunk(const uint32_t* xw, int64_t ldxw, int b, int k, int K,
+                                                    uint32_t tag, bool sys) {
+  const uint32_t* src = xw + b * ldxw + k;
+  const uint4 a = ld_relaxed_v4(src, sys), d = ld_relaxed_v4(src + 4, sys);
+  ChainChunk r;
+  r.v = make_uint4(0, 0, 0, 0);
+  r.ok = chain_take_words(a, d, tag, K - k, &r.v) ? 1 : 0;
+  return r;
+}
+
+// Layer 0: x chunk (columns k..k+7 of row b) from the fp16 input.
+__device__ __noinline__ uint4 chain_load_x0(const __half* x, int64_t ldx, int b, int k, int K, int vec16) {
+  const __half* src = x + b * ldx + k;
+  if (vec16) return ld_cg_v4(src);
+  uint16_t h[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) h[e] = (k + e < K) ? __ldcg(reinterpret_cast<const unsigned short*>(src) + e) : 0;
+  return make_uint4(h[0] | (uint32_t(h[1]) << 16), h[2] | (uint32_t(h[3]) << 16), h[4] | (uint32_t(h[5]) << 16),
+                    h[6] | (uint32_t(h[7]) << 16));
+}
+
+// max |x| over a chunk's eight fp16 values
+__device__ __forceinline__ float chain_chunk_amax(const uint4& v) {
+  const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+  float m = 0.f;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const __half hv = __ushort_as_half(static_cast<unsigned short>((wv[e >> 1] >> (16 * (e & 1))) & 0xffffu));
+    m = fmaxf(m, fabsf(__half2float(hv)));
+  }
+  return m;
+}
+
+// A chunk's eight values as 24-bit integers x*2^ex split into three signed int8 digits, stored at
+// their staged positions in the three digit columns of batch row b.
+__device__ __noinline__ void chain_store_digits(const uint4 v, float sc, uint32_t col0, uint32_t colb, uint32_t pos) {
+  const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+  uint32_t d[3][2] = {{0, 0}, {0, 0}, {0, 0}};
+#pragma unroll
+  for (int t = 0; t < 8; ++t) {
+    const __half hv = __ushort_as_half(static_cast<unsigned short>((wv[t >> 1] >> (16 * (t & 1))) & 0xffffu));
+    const int n = round_small_int(__half2float(hv) * sc);
+    const int d2 = ((n + 128) & 255) - 128;
+    const int n1 = (n - d2) >> 8;
+    const int d1 = ((n1 + 128) & 255) - 128;
+    const int d0 = (n1 - d1) >> 8;
+    d[0][t >> 2] |= (static_cast<uint32_t>(d0) & 0xffu) << (8 * (t & 3));
+    d[1][t >> 2] |= (static_cast<uint32_t>(d1) & 0xffu) << (8 * (t & 3));
+    d[2][t >> 2] |= (static_cast<uint32_t>(d2) & 0xffu) << (8 * (t & 3));
+  }
+#pragma unroll
+  for (int dd = 0; dd < 3; ++dd) sts64(col0 + dd * colb + pos, d[dd][0], d[dd][1]);
+}
+
 constexpr int kChainSplitSlots = 32;  // packed tiles per CTA and layer (host-checked)
 
 struct ChainShared {
@@ -270,44 +335,46 @@ struct ChainShared {
   uint32_t epoch;
 };
 
-// Rows m.row[0..1] (local) with dot products t: exchange words into every rank's copy (one
-// relaxed store per word) and, unless a later layer overwrites it, the fp16 output.
-__device__ __forceinline__ void chain_write_rows(const ChainLayer& L, int P, int B, const MetaQ& m, const long long t[2],
-                                                 int q, int ex0, int ex1, uint32_t tag, bool sys) {
+// Rows r0, r1 (local; -1 = none) with exponents e0, e1 and dot products t0, t1: exchange words
+// into every rank's copy (one relaxed store per word) and, unless a later layer overwrites it,
+// the fp16 output.  Scalars only, so nothing of the caller goes through local memory.
+__device__ __noinline__ void chain_write_rows(const ChainLayer& L, int P, int B, int r0, int r1, int e0, int e1,
+                                              long long t0, long long t1, int q, int ex0, int ex1, uint32_t tag,
+                                              bool sys) {
   const int b = q >> 1;
   if ((q & 1) || b >= B) return;
   const int ex = b ? ex1 : ex0;
-  const __half h0 = scale_to_half(t[0], m.e[0] + ex), h1 = scale_to_half(t[1], m.e[1] + ex);
+  const __half h0 = scale_to_half(t0, e0 + ex), h1 = scale_to_half(t1, e1 + ex);
   const uint32_t w0 = (tag << 16) | __half_as_ushort(h0), w1 = (tag << 16) | __half_as_ushort(h1);
   for (int p = 0; p < P; ++p) {
     unsigned int* wb = L.yw_peer[p] + b * L.ldyw;
     if (L.write_y) {
       __half* yb = L.y_peer[p] + b * L.ldy;
-      if (m.row[0] >= 0) yb[m.row[0]] = h0;
-      if (m.row[1] >= 0) yb[m.row[1]] = h1;
+      if (r0 >= 0) yb[r0] = h0;
+      if (r1 >= 0) yb[r1] = h1;
     }
     if (sys) {
-      if (m.row[0] >= 0) st_relaxed_sys_u32(wb + m.row[0], w0);
-      if (m.row[1] >= 0) st_relaxed_sys_u32(wb + m.row[1], w1);
+      if (r0 >= 0) st_relaxed_sys_u32(wb + r0, w0);
+      if (r1 >= 0) st_relaxed_sys_u32(wb + r1, w1);
     } else {
-      if (m.row[0] >= 0) st_relaxed_u32(wb + m.row[0], w0);
-      if (m.row[1] >= 0) st_relaxed_u32(wb + m.row[1], w1);
+      if (r0 >= 0) st_relaxed_u32(wb + r0, w0);
+      if (r1 >= 0) st_relaxed_u32(wb + r1, w1);
     }
   }
 }
 
-// A warp's partial dot products of packed tile `seg` (this CTA's local tile lt), shared with
-// other warps of the CTA: added exactly into the tile's shared int64 accumulators; the warp that
+// A warp's partial dot products of a packed tile (this CTA's local tile lt), shared with other
+// warps of the CTA: added exactly into the tile's shared int64 accumulators; the warp that
 // completes the count of contributors writes the tile's rows and clears the slot.
-__device__ void chain_split_add(ChainShared* sh, const ChainLayer& L, int P, int B, const MetaQ& m, const long long t[2],
-                                int lt, int n_contrib, int lane, int g, int q, int ex0, int ex1, uint32_t tag,
-                                bool sys) {
+__device__ __noinline__ void chain_split_add(ChainShared* sh, const ChainLayer& L, int P, int B, int r0, int r1, int e0,
+                                             int e1, long long t0, long long t1, int lt, int n_contrib, int lane,
+                                             int g, int q, int ex0, int ex1, uint32_t tag, bool sys) {
   const int slot = lt & (kChainSplitSlots - 1);
   const int b = q >> 1;
   const bool live = !(q & 1) && b < B;
   if (live) {
-    atomicAdd(&sh->tile_acc[slot][g][b], static_cast<unsigned long long>(t[0]));
-    atomicAdd(&sh->tile_acc[slot][g + 8][b], static_cast<unsigned long long>(t[1]));
+    atomicAdd(&sh->tile_acc[slot][g][b], static_cast<unsigned long long>(t0));
+    atomicAdd(&sh->tile_acc[slot][g + 8][b], static_cast<unsigned long long>(t1));
   }
   __threadfence_block();
   __syncwarp();
@@ -316,13 +383,64 @@ __device__ void chain_split_add(ChainShared* sh, const ChainLayer& L, int P, int
   old = __shfl_sync(0xffffffffu, old, 0);
   if (old != n_contrib - 1) return;
   __threadfence_block();
-  long long fin[2] = {0, 0};
+  long long f0 = 0, f1 = 0;
   if (live) {
-    fin[0] = static_cast<long long>(atomicExch(&sh->tile_acc[slot][g][b], 0ull));
-    fin[1] = static_cast<long long>(atomicExch(&sh->tile_acc[slot][g + 8][b], 0ull));
+    f0 = static_cast<long long>(atomicExch(&sh->tile_acc[slot][g][b], 0ull));
+    f1 = static_cast<long long>(atomicExch(&sh->tile_acc[slot][g + 8][b], 0ull));
   }
   if (lane == 0) sh->tile_cnt[slot] = 0;
-  chain_write_rows(L, P, B, m, fin, q, ex0, ex1, tag, sys);
+  chain_write_rows(L, P, B, r0, r1, e0, e1, f0, f1, q, ex0, ex1, tag, sys);
+}
+
+// Outlier tile tt done for this warp: add its partials (rows r0, r1 = the slots' rows, -1 =
+// padding) into the slot accumulators and count it in (release); the warp completing the tile's
+// count (acquire) takes the sums, clears them and publishes the tile's rows.
+__device__ __noinline__ void chain_flush_outlier(const ChainLayer& L, int P, int B, int r0, int r1, int e0, int e1,
+                                                 long long t0, long long t1, int tt, int lane, int g, int q, int ex0,
+                                                 int ex1, uint32_t tag, bool sys) {
+  const int b = q >> 1;
+  const bool live = !(q & 1) && b < B;
+  const int s0 = tt * kTileRows + g, s1 = s0 + 8;
+  if (live) {
+    if (r0 >= 0) atomicAdd(L.acc + 2 * s0 + b, static_cast<unsigned long long>(t0));
+    if (r1 >= 0) atomicAdd(L.acc + 2 * s1 + b, static_cast<unsigned long long>(t1));
+  }
+  __syncwarp();
+  int old = 0;
+  if (lane == 0) {
+    fence_acq_rel_gpu();
+    old = atomicAdd(L.ocnt + tt, 1);
+    fence_acq_rel_gpu();
+  }
+  old = __shfl_sync(0xffffffffu, old, 0);
+  __syncwarp();
+  if (old != static_cast<int>(ld_nc_u32(L.onc + tt)) - 1) return;
+  long long f0 = 0, f1 = 0;
+  if (live) {
+    if (r0 >= 0) f0 = static_cast<long long>(atomicExch(L.acc + 2 * s0 + b, 0ull));
+    if (r1 >= 0) f1 = static_cast<long long>(atomicExch(L.acc + 2 * s1 + b, 0ull));
+  }
+  if (lane == 0) st_relaxed_u32(reinterpret_cast<unsigned int*>(L.ocnt + tt), 0u);
+  chain_write_rows(L, P, B, r0, r1, e0, e1, f0, f1, q, ex0, ex1, tag, sys);
+}
+
+// A finished segment of a warp's range (one call site in the kernel): outlier tiles count in,
+// packed tiles the warp covered whole are written, shared ones go through the CTA's reduction.
+// `lt` is the packed tile's index within the CTA's share; the contributor count is partq_of in
+// 32 bits over the share's np units and wp warps (products below 2^31, host-checked).
+__device__ __noinline__ void chain_finish_segment(ChainShared* sh, const ChainLayer& L, int P, int B, int r0, int r1,
+                                                  int e0, int e1, long long t0, long long t1, int seg, int whole,
+                                                  int lt, int sb_rel, int np, int wp, int lane, int g, int q, int ex0,
+                                                  int ex1, uint32_t tag, bool sys) {
+  if (seg >= L.MT) {
+    chain_flush_outlier(L, P, B, r0, r1, e0, e1, t0, t1, seg - L.MT, lane, g, q, ex0, ex1, tag, sys);
+  } else if (whole) {
+    chain_write_rows(L, P, B, r0, r1, e0, e1, t0, t1, q, ex0, ex1, tag, sys);
+  } else {
+    const int32_t lo = sb_rel, hi = sb_rel + L.KT - 1;
+    const int n_contrib = ((hi + 1) * wp + np - 1) / np - ((lo + 1) * wp + np - 1) / np + 1;
+    chain_split_add(sh, L, P, B, r0, r1, e0, e1, t0, t1, lt, n_contrib, lane, g, q, ex0, ex1, tag, sys);
+  }
 }
 
 template <int kXC>
@@ -362,50 +480,76 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
   if (sh->abort) return;  // poisoned: no work, no flags
 
   // ------------------------------------------------------------------ producer warp
+  // Lane i feeds consumer warp i.  Everything a lane needs about a layer lives in registers: the
+  // next layer's fields are loaded when the lane starts a layer, so a layer change costs no
+  // memory round trip (a stall there would hold up every lane of the warp).
   if (warp == kQProducerWarp) {
     const int i = lane;
     const uint32_t ring = ring_base + i * S * kQChunkBytes;
-    int j = 0;
-    int32_t u1 = 0;
-    ChainCursor pc = {0, 0, 0, 0};
-    const ChainLayer* Lp = nullptr;
-    bool active = i < kQConsumers;
     const uint64_t evict_first = l2_policy_evict_first();
-    // When this lane starts layer j, its consumer's share of layer j+1 is prefetched into L2, so
-    // HBM streams the next layer during this one's compute and its ring refills hit L2.
-    auto prefetch_next = [&](int jn) {
-      if (!args.l2_prefetch || jn >= args.n_layers) return;
-      const ChainLayer& N = args.layers[jn];
-      const ChainPart p = chain_part_load(args.parts + 2 * (static_cast<int64_t>(jn) * G + cta));
-      int32_t a0, a1;
-      chain_warp_range(p, i, &a0, &a1);
-      if (a0 >= a1) return;
-      const uint8_t* src = a0 < N.Up ? N.units + static_cast<int64_t>(a0) * kUnitBytes
-                                     : N.ounits + static_cast<int64_t>(a0 - N.Up) * kUnitBytes;
-      int64_t bytes = static_cast<int64_t>(a1 - a0) * kUnitBytes;
-      while (bytes > 0) {
-        const uint32_t n = bytes > 65536 ? 65536u : static_cast<uint32_t>(bytes);
-        l2_prefetch_bulk(src, n);
-        src += n;
-        bytes -= n;
-      }
+    // raw fields of a layer (loads in flight until first used)
+    struct Raw {
+      uint64_t units, ounits;
+      uint32_t Up, MT, KT, KO;
+      int4 p0, p1;
     };
+    auto fetch = [&](int jn, Raw& r) {
+      if (jn >= args.n_layers) return;
+      const ChainLayer* Ln = args.layers + jn;
+      r.units = ld_nc_u64(&Ln->units);
+      r.ounits = ld_nc_u64(&Ln->ounits);
+      r.Up = ld_nc_u32(&Ln->Up);
+      r.MT = ld_nc_u32(&Ln->MT);
+      r.KT = ld_nc_u32(&Ln->KT);
+      r.KO = ld_nc_u32(&Ln->KO);
+      const uint4* pe = reinterpret_cast<const uint4*>(args.parts + 2 * (static_cast<int64_t>(jn) * G + cta));
+      const uint4 a0 = ld_nc_v4(pe), a1 = ld_nc_v4(pe + 1);
+      r.p0 = make_int4(a0.x, a0.y, a0.z, a0.w);
+      r.p1 = make_int4(a1.x, a1.y, a1.z, a1.w);
+    };
+    // the current layer of this lane, in registers
+    int j = 0;
+    const uint8_t* units = nullptr;
+    const uint8_t* ounits = nullptr;
+    int32_t Up = 0, MT = 0, KT = 1, KO = 1, u1 = 0;
+    int32_t pu = 0, seg = 0, send = 0;  // cursor: unit, segment, end of segment
+    Raw nx;
+    fetch(0, nx);
     // advance to the next layer with a non-empty range for this consumer
     auto next_range = [&]() {
       while (j < args.n_layers) {
-        Lp = args.layers + j;
-        const ChainPart p = chain_part_load(args.parts + 2 * (static_cast<int64_t>(j) * G + cta));
+        units = reinterpret_cast<const uint8_t*>(nx.units);
+        ounits = reinterpret_cast<const uint8_t*>(nx.ounits);
+        Up = static_cast<int32_t>(nx.Up);
+        MT = static_cast<int32_t>(nx.MT);
+        KT = static_cast<int32_t>(nx.KT);
+        KO = static_cast<int32_t>(nx.KO);
+        ChainPart p;
+        p.pu0 = nx.p0.x;
+        p.pu1 = nx.p0.y;
+        p.ou0 = nx.p0.z;
+        p.ou1 = nx.p0.w;
+        p.wp = nx.p1.x;
+        fetch(j + 1, nx);  // in flight while this layer streams
         int32_t u0;
         chain_warp_range(p, i, &u0, &u1);
-        prefetch_next(j + 1);
         if (u0 < u1) {
-          pc = chain_cursor(*Lp, u0);
+          pu = u0;
+          if (u0 < Up) {
+            seg = u0 / KT;
+            send = (seg + 1) * KT;
+          } else {
+            const int32_t t = (u0 - Up) / KO;
+            seg = MT + t;
+            send = Up + (t + 1) * KO;
+          }
           return true;
         }
         ++j;
       }
       return false;
     };
+    bool active = i < kQConsumers;
     if (active) active = next_range();
     int32_t c = 0;
     uint64_t t_idle = 0;
@@ -416,21 +560,25 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
         const int slot = c % S;
         const int round = c / S;
         if (round == 0 || mbar_test(empty_base + (i * S + slot) * 8, static_cast<uint32_t>((round - 1) & 1))) {
-          const int32_t cnt = chain_chunk(pc, u1);
+          int32_t cnt = send - pu;
+          if (u1 - pu < cnt) cnt = u1 - pu;
+          if (cnt > kQChunkUnits) cnt = kQChunkUnits;
           const uint32_t bar = full_base + (i * S + slot) * 8;
           mbar_expect_tx(bar, static_cast<uint32_t>(cnt * kUnitBytes));
-          const int32_t Up = Lp->Up;
-          const uint8_t* src = pc.u < Up ? Lp->units + static_cast<int64_t>(pc.u) * kUnitBytes
-                                         : Lp->ounits + static_cast<int64_t>(pc.u - Up) * kUnitBytes;
+          const uint8_t* src = pu < Up ? units + static_cast<int64_t>(pu) * kUnitBytes
+                                       : ounits + static_cast<int64_t>(pu - Up) * kUnitBytes;
           if (args.l2_prefetch)
             bulk_g2s_hint(ring + slot * kQChunkBytes, src, static_cast<uint32_t>(cnt * kUnitBytes), bar, evict_first);
           else
             bulk_g2s(ring + slot * kQChunkBytes, src, static_cast<uint32_t>(cnt * kUnitBytes), bar);
-          pc.u += cnt;
-          if (pc.u == pc.end && pc.u < u1) chain_next_segment(*Lp, pc);
+          pu += cnt;
+          if (pu == send && pu < u1) {  // next segment
+            ++seg;
+            send += seg < MT ? KT : KO;
+          }
           ++c;
           issued = true;
-          if (pc.u >= u1) {
+          if (pu >= u1) {
             ++j;
             active = next_range();
           }
@@ -546,54 +694,48 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
       const int per_row = L.K_pad / 8;
       const int total = B * per_row;
       uint4 v[kXC];
-      uint32_t pending = 0;
+      uint32_t pending = 0;  // chunks still to take
 #pragma unroll
       for (int i = 0; i < kXC; ++i) {
         const int c = tid + i * kQConsumerThreads;
         v[i] = make_uint4(0, 0, 0, 0);
-        if (c < total) {
-          const int b = c / per_row, k = (c - b * per_row) * 8;
-          if (k < L.K) {
-            if (j == 0) {
-              const __half* src = L.x + b * L.ldx + k;
-              if (L.x_vec16) {
-                v[i] = ld_cg_v4(src);
-              } else {
-                uint16_t h[8];
+        if (c < total && (c - (c / per_row) * per_row) * 8 < L.K) pending |= 1u << i;
+      }
+      if (j == 0) {
 #pragma unroll
-                for (int e = 0; e < 8; ++e)
-                  h[e] = (k + e < L.K) ? __ldcg(reinterpret_cast<const unsigned short*>(src) + e) : 0;
-                v[i] = make_uint4(h[0] | (uint32_t(h[1]) << 16), h[2] | (uint32_t(h[3]) << 16),
-                                  h[4] | (uint32_t(h[5]) << 16), h[6] | (uint32_t(h[7]) << 16));
-              }
-            } else {
-              const uint32_t* src = L.xw + b * L.ldxw + k;
-              const uint4 a = ld_relaxed_v4(src, sys), d = ld_relaxed_v4(src + 4, sys);
-              if (!chain_take_words(a, d, tag_in, L.K - k, &v[i])) pending |= 1u << i;
+        for (int i = 0; i < kXC; ++i) {
+          if (pending & (1u << i)) {
+            const int c = tid + i * kQConsumerThreads;
+            const int b = c / per_row, k = (c - b * per_row) * 8;
+            v[i] = chain_load_x0(L.x, L.ldx, b, k, L.K, L.x_vec16);
+          }
+        }
+        pending = 0;
+      }
+      if (tr && tid == 0) tr[2] = globaltimer_ns();
+      // layers >= 1: poll the exchange words of every pending chunk until all carry this launch's
+      // tag (bounded)
+      uint64_t t0 = 0;
+      while (pending) {
+#pragma unroll
+        for (int i = 0; i < kXC; ++i) {
+          if (pending & (1u << i)) {
+            const int c = tid + i * kQConsumerThreads;
+            const int b = c / per_row, k = (c - b * per_row) * 8;
+            const ChainChunk r = chain_poll_chunk(L.xw, L.ldxw, b, k, L.K, tag_in, sys);
+            if (r.ok) {
+              v[i] = r.v;
+              pending &= ~(1u << i);
             }
           }
         }
-      }
-      if (tr && tid == 0) tr[2] = globaltimer_ns();
-      if (pending) {
-        const uint64_t t0 = globaltimer_ns();
-        for (;;) {
-#pragma unroll
-          for (int i = 0; i < kXC; ++i) {
-            if (pending & (1u << i)) {
-              const int c = tid + i * kQConsumerThreads;
-              const int b = c / per_row, k = (c - b * per_row) * 8;
-              const uint32_t* src = L.xw + b * L.ldxw + k;
-              const uint4 a = ld_relaxed_v4(src, sys), d = ld_relaxed_v4(src + 4, sys);
-              if (chain_take_words(a, d, tag_in, L.K - k, &v[i])) pending &= ~(1u << i);
-            }
-          }
-          if (!pending) break;
-          if (globaltimer_ns() - t0 > kWaitLimitNs) {
-            sh->abort = 1;
-            atomicCAS(&g_opc_device_error, 0, kDevErrBarrierTimeout);
-            break;
-          }
+        if (!pending) break;
+        const uint64_t now = globaltimer_ns();
+        if (t0 == 0) t0 = now;
+        else if (now - t0 > kWaitLimitNs) {
+          sh->abort = 1;
+          atomicCAS(&g_opc_device_error, 0, kDevErrBarrierTimeout);
+          break;
         }
       }
       if (tr && tid == 0) tr[3] = globaltimer_ns();
@@ -602,15 +744,8 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
       for (int i = 0; i < kXC; ++i) {
         const int c = tid + i * kQConsumerThreads;
         if (c < total) {
-          const int b = c / per_row;
-          const uint32_t wv[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
-          float m = 0.f;
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const __half hv = __ushort_as_half(static_cast<unsigned short>((wv[e >> 1] >> (16 * (e & 1))) & 0xffffu));
-            m = fmaxf(m, fabsf(__half2float(hv)));
-          }
-          if (b == 0) mx[0] = fmaxf(mx[0], m);
+          const float m = chain_chunk_amax(v[i]);
+          if (c < per_row) mx[0] = fmaxf(mx[0], m);
           else mx[1] = fmaxf(mx[1], m);
         }
       }
@@ -648,24 +783,8 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
         const int c = tid + i * kQConsumerThreads;
         if (c < total) {
           const int b = c / per_row, k = (c - b * per_row) * 8;
-          const uint32_t wv[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
-          const float sc = pow2f(b == 0 ? ex0 : ex1);
-          uint32_t d[3][2] = {{0, 0}, {0, 0}, {0, 0}};
-#pragma unroll
-          for (int t = 0; t < 8; ++t) {
-            const __half hv = __ushort_as_half(static_cast<unsigned short>((wv[t >> 1] >> (16 * (t & 1))) & 0xffffu));
-            const int n = round_small_int(__half2float(hv) * sc);
-            const int d2 = ((n + 128) & 255) - 128;
-            const int n1 = (n - d2) >> 8;
-            const int d1 = ((n1 + 128) & 255) - 128;
-            const int d0 = (n1 - d1) >> 8;
-            d[0][t >> 2] |= (static_cast<uint32_t>(d0) & 0xffu) << (8 * (t & 3));
-            d[1][t >> 2] |= (static_cast<uint32_t>(d1) & 0xffu) << (8 * (t & 3));
-            d[2][t >> 2] |= (static_cast<uint32_t>(d2) & 0xffu) << (8 * (t & 3));
-          }
-          const uint32_t pos = static_cast<uint32_t>((k >> 7) * 128 + xs_pos8(k & 127));
-#pragma unroll
-          for (int dd = 0; dd < 3; ++dd) sts64(xs_base + (3 * b + dd) * colb + pos, d[dd][0], d[dd][1]);
+          chain_store_digits(v[i], pow2f(b == 0 ? ex0 : ex1), xs_base + 3 * b * colb, colb,
+                             static_cast<uint32_t>((k >> 7) * 128 + xs_pos8(k & 127)));
         }
       }
       if (tr && tid == 0) tr[5] = globaltimer_ns();
@@ -689,53 +808,10 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     const uint32_t kts = live_col ? 128u : 0u;
     const uint32_t xq = colbase + 32 * q, xo = colbase + 4 * q;
 
-    // number of packed warps whose ranges share the tile starting at unit sb
-    const int32_t tile0 = part.pu0 / (L.KT > 0 ? L.KT : 1);
-    auto contrib = [&](int32_t sb) {
-      const int32_t n = part.pu1 - part.pu0;
-      const int32_t lo = sb - part.pu0, hi = sb + L.KT - 1 - part.pu0;
-      return partq_of(hi, n, part.wp) - partq_of(lo, n, part.wp) + 1;
-    };
+    const int32_t tile0 = part.pu0 / (L.KT > 0 ? L.KT : 1);  // this CTA's first packed tile
     if (u0 < u1) {
       AccQ A;
       zero_accq(A);
-      // Outlier segment done: add this warp's partial into the slot accumulators and count it in
-      // (release); the warp completing the tile's count (acquire) takes the sums, clears them and
-      // publishes the tile's rows.
-      auto flush_outlier = [&](int32_t seg) {
-        long long t[2];
-        finish_dot(A, q, t);
-        const int b = q >> 1;
-        const bool live = !(q & 1) && b < B;
-        const int tt = seg - L.MT;
-        if (live) {
-#pragma unroll
-          for (int r = 0; r < 2; ++r) {
-            const int s = tt * kTileRows + g + 8 * r;
-            if (cur.row[r] >= 0) atomicAdd(L.acc + 2 * s + b, static_cast<unsigned long long>(t[r]));
-          }
-        }
-        __syncwarp();
-        int old = 0;
-        if (lane == 0) {
-          fence_acq_rel_gpu();
-          old = atomicAdd(L.ocnt + tt, 1);
-          fence_acq_rel_gpu();
-        }
-        old = __shfl_sync(0xffffffffu, old, 0);
-        __syncwarp();
-        if (old != static_cast<int>(ld_nc_u32(L.onc + tt)) - 1) return;
-        long long fin[2] = {0, 0};
-        if (live) {
-#pragma unroll
-          for (int r = 0; r < 2; ++r) {
-            const int s = tt * kTileRows + g + 8 * r;
-            if (cur.row[r] >= 0) fin[r] = static_cast<long long>(atomicExch(L.acc + 2 * s + b, 0ull));
-          }
-        }
-        if (lane == 0) st_relaxed_u32(reinterpret_cast<unsigned int*>(L.ocnt + tt), 0u);
-        chain_write_rows(L, P, B, cur, fin, q, ex0, ex1, tag, sys);
-      };
       while (cc.u < u1) {
         if (!mbar_wait_bounded(fullw + slot * 8, phase)) {
           ok = false;
@@ -781,35 +857,20 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
           phase ^= 1u;
         }
         cc.u += cnt;
-        if (cc.u == cc.end && cc.u < u1) {  // segment complete inside the range
-          if (cc.seg >= L.MT) {
-            flush_outlier(cc.seg);
-          } else {
-            long long t[2];
-            finish_dot(A, q, t);
-            if (cc.begin < u0)
-              chain_split_add(sh, L, P, B, cur, t, cc.seg - tile0, contrib(cc.begin), lane, g, q, ex0, ex1, tag, sys);
-            else
-              chain_write_rows(L, P, B, cur, t, q, ex0, ex1, tag, sys);
-          }
+        if (cc.u == cc.end || cc.u == u1) {  // a segment of the range is complete (one call site)
+          long long t[2];
+          finish_dot(A, q, t);
+          chain_finish_segment(sh, L, P, B, cur.row[0], cur.row[1], cur.e[0], cur.e[1], t[0], t[1], cc.seg,
+                               cc.begin >= u0 && cc.end <= u1, cc.seg - tile0, cc.begin - part.pu0,
+                               part.pu1 - part.pu0, part.wp, lane, g, q, ex0, ex1, tag, sys);
+          if (cc.u == u1) break;
           zero_accq(A);
           chain_next_segment(L, cc);
           cur = nxt;
           if (cc.seg + 1 < L.MT + L.OT) nxt = load_metaq(qa, cc.seg + 1, g);
         }
       }
-      if (ok) {
-        if (cc.seg >= L.MT) {
-          flush_outlier(cc.seg);
-        } else {
-          long long t[2];
-          finish_dot(A, q, t);
-          if (cc.begin >= u0 && cc.end <= u1)
-            chain_write_rows(L, P, B, cur, t, q, ex0, ex1, tag, sys);
-          else
-            chain_split_add(sh, L, P, B, cur, t, cc.seg - tile0, contrib(cc.begin), lane, g, q, ex0, ex1, tag, sys);
-        }
-      } else {
+      if (!ok) {
         atomicCAS(&g_opc_device_error, 0, kDevErrTmaTimeout);
         sh->abort = 1;  // every consumer sees it at the next staging barrier
         ok = true;      // this warp still takes part in the CTA's barriers until then
