@@ -20,6 +20,7 @@
 #include "opc_gemv.cuh"
 #include "opc_gemvq.cuh"
 #include "opc_layer.cuh"
+#include "opc_vq8.cuh"
 
 #define OPC_VERSION_STRING "opc_b200 0.2.0 abi 1"
 
@@ -67,14 +68,29 @@ int device_cache(int dev, DeviceCache* out) {
   return OPC_OK;
 }
 
+// k columns per index unit: 128 (svs = 1, 512-byte units), 256 (svs = 8, 128-byte units)
+int unit_cols(int svs) { return svs == 8 ? opc::kVq8BlockCols : opc::kPackedCols; }
+
 bool plan_ok(const opc_layer_plan* p) {
-  return p && p->M > 0 && p->K > 0 && p->n_outliers >= 0 && p->n_outliers <= p->M && p->sub_vector_size == 1 &&
-         p->row_tiles == ceil_div(p->M, opc::kTileRows) && p->k_units == ceil_div(p->K, opc::kPackedCols) &&
-         p->M_pad == p->row_tiles * opc::kTileRows && p->K_pad == p->k_units * opc::kPackedCols &&
+  return p && p->M > 0 && p->K > 0 && p->n_outliers >= 0 && p->n_outliers <= p->M &&
+         (p->sub_vector_size == 1 || (p->sub_vector_size == 8 && p->K % 8 == 0)) &&
+         p->row_tiles == ceil_div(p->M, opc::kTileRows) && p->k_units == ceil_div(p->K, unit_cols(p->sub_vector_size)) &&
+         p->M_pad == p->row_tiles * opc::kTileRows && p->K_pad == p->k_units * unit_cols(p->sub_vector_size) &&
          p->outlier_tiles == ceil_div(p->n_outliers, opc::kTileRows) &&
          p->outlier_k_units == p->K_pad / opc::kDenseCols &&
          p->packed_units == static_cast<int64_t>(p->row_tiles) * p->k_units &&
          p->total_units == p->packed_units + static_cast<int64_t>(p->outlier_tiles) * p->outlier_k_units;
+}
+
+opc::Vq8Geom vq8_geom_of(const opc_layer_plan& p) {
+  opc::Vq8Geom G;
+  G.M = p.M;
+  G.K = p.K;
+  G.K_pad = p.K_pad;
+  G.MT = p.row_tiles;
+  G.KB = p.k_units;
+  G.n_slots = std::max(p.outlier_tiles, 1) * opc::kTileRows;
+  return G;
 }
 
 opc::LayerGeom geom_of(const opc_layer_plan& p) {
@@ -287,17 +303,19 @@ int opc_plan_layer(int32_t M, int32_t K, int32_t n_outliers, int32_t sub_vector_
   if (M <= 0 || K <= 0) return fail(OPC_ERR_INVALID, "opc_plan_layer: bad shape M=%d K=%d", M, K);
   if (n_outliers < 0 || n_outliers > M)
     return fail(OPC_ERR_INVALID, "opc_plan_layer: n_outliers=%d outside [0, M=%d]", n_outliers, M);
-  if (sub_vector_size != 1)
-    return fail(OPC_ERR_UNSUPPORTED, "opc_plan_layer: sub_vector_size=%d (only 1 is implemented)", sub_vector_size);
+  if (sub_vector_size != 1 && sub_vector_size != 8)
+    return fail(OPC_ERR_UNSUPPORTED, "opc_plan_layer: sub_vector_size=%d (1 and 8 are implemented)", sub_vector_size);
+  if (sub_vector_size == 8 && K % 8)
+    return fail(OPC_ERR_UNSUPPORTED, "opc_plan_layer: K=%d is not a multiple of sub_vector_size 8", K);
   memset(plan, 0, sizeof(*plan));
   plan->M = M;
   plan->K = K;
   plan->n_outliers = n_outliers;
   plan->sub_vector_size = sub_vector_size;
   plan->row_tiles = static_cast<int32_t>(ceil_div(M, opc::kTileRows));
-  plan->k_units = static_cast<int32_t>(ceil_div(K, opc::kPackedCols));
+  plan->k_units = static_cast<int32_t>(ceil_div(K, unit_cols(sub_vector_size)));
   plan->M_pad = plan->row_tiles * opc::kTileRows;
-  plan->K_pad = plan->k_units * opc::kPackedCols;
+  plan->K_pad = plan->k_units * unit_cols(sub_vector_size);
   plan->outlier_tiles = static_cast<int32_t>(ceil_div(n_outliers, opc::kTileRows));
   plan->outlier_k_units = plan->K_pad / opc::kDenseCols;
   plan->packed_units = static_cast<int64_t>(plan->row_tiles) * plan->k_units;
@@ -309,6 +327,12 @@ int opc_plan_layer(int32_t M, int32_t K, int32_t n_outliers, int32_t sub_vector_
   plan->codebook_bytes = static_cast<int64_t>(plan->M_pad) * (8 + 16);
   plan->tile_mask_bytes = static_cast<int64_t>(plan->row_tiles) * 2;
   plan->outlier_rows_bytes = static_cast<int64_t>(std::max(plan->outlier_tiles, 1)) * opc::kTileRows * 8;
+  if (sub_vector_size == 8) {
+    // 128-byte index units, then the outlier rows row-major; codebooks 64 bytes per row
+    plan->units_bytes = plan->packed_units * opc::kVq8UnitBytes +
+                        static_cast<int64_t>(std::max(plan->outlier_tiles, 1)) * opc::kTileRows * plan->K_pad * 2;
+    plan->codebook_bytes = static_cast<int64_t>(plan->M_pad) * 64;
+  }
   return OPC_OK;
 }
 
@@ -380,8 +404,32 @@ int opc_repack_layer(const opc_layer* L, const void* codebooks_f16, const uint8_
   OPC_REPACK_CUDA(cudaMemcpyAsync(d_src, src.data(), n_slots * 4, cudaMemcpyHostToDevice, stream),
                   "copy outlier sources");
 
-  const opc::LayerGeom G = geom_of(p);
   const int tpb = 256;
+  if (p.sub_vector_size == 8) {
+    const opc::Vq8Geom V = vq8_geom_of(p);
+    const int64_t n_idx_words = p.packed_units * (opc::kVq8UnitBytes / 4);
+    opc::vq8_repack_indices_kernel<<<static_cast<unsigned>(ceil_div(n_idx_words, tpb)), tpb, 0, stream>>>(
+        V, indices_u8, static_cast<uint32_t*>(L->units), d_bad);
+    OPC_REPACK_CUDA(cudaGetLastError(), "launch vq8_repack_indices_kernel");
+    const int64_t n_cb_words = static_cast<int64_t>(p.row_tiles) * 32 * 8;
+    opc::vq8_repack_codebooks_kernel<<<static_cast<unsigned>(ceil_div(n_cb_words, tpb)), tpb, 0, stream>>>(
+        V, static_cast<const uint16_t*>(codebooks_f16), static_cast<const uint16_t*>(L->tile_mask),
+        static_cast<uint32_t*>(L->codebooks));
+    OPC_REPACK_CUDA(cudaGetLastError(), "launch vq8_repack_codebooks_kernel");
+    OPC_REPACK_CUDA(cudaMemsetAsync(L->outlier_rows + n_slots, 0, n_slots * 4, stream), "clear outlier exponents");
+    const int64_t n_dense = static_cast<int64_t>(n_slots) * p.K_pad;
+    opc::vq8_repack_outliers_kernel<<<static_cast<unsigned>(ceil_div(n_dense, tpb)), tpb, 0, stream>>>(
+        V, static_cast<const uint16_t*>(outlier_f16), d_src,
+        reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(L->units) + p.packed_units * opc::kVq8UnitBytes));
+    OPC_REPACK_CUDA(cudaGetLastError(), "launch vq8_repack_outliers_kernel");
+    int bad8 = 0;
+    OPC_REPACK_CUDA(cudaMemcpyAsync(&bad8, d_bad, sizeof(int), cudaMemcpyDeviceToHost, stream), "read repack flag");
+    OPC_REPACK_CUDA(cudaStreamSynchronize(stream), "cudaStreamSynchronize(repack)");
+    cleanup();
+    if (bad8) return fail(OPC_ERR_INVALID, "opc_repack_layer: an index value is outside 0..3");
+    return OPC_OK;
+  }
+  const opc::LayerGeom G = geom_of(p);
   const int64_t n_idx_words = p.packed_units * (opc::kUnitBytes / 4);
   opc::repack_indices_kernel<<<static_cast<unsigned>(ceil_div(n_idx_words, tpb)), tpb, 0, stream>>>(
       G, indices_u8, static_cast<uint32_t*>(L->units), d_bad);
@@ -430,6 +478,40 @@ int opc_workspace_init(void* workspace, size_t bytes, void* stream) {
   return OPC_OK;
 }
 
+}  // extern "C"
+
+namespace {
+// svs = 8: one launch, no workspace (each CTA reduces its tile in shared memory).
+int launch_vq8(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ldy, int32_t batch, cudaStream_t s) {
+  const opc_layer_plan& p = L->plan;
+  opc::Vq8Args a;
+  memset(&a, 0, sizeof(a));
+  a.units = static_cast<const uint4*>(L->units);
+  a.cb = static_cast<const uint4*>(L->codebooks);
+  a.tile_mask = static_cast<const uint16_t*>(L->tile_mask);
+  a.orows = reinterpret_cast<const __half*>(static_cast<const uint8_t*>(L->units) + p.packed_units * opc::kVq8UnitBytes);
+  a.orow = L->outlier_rows;
+  a.x = static_cast<const __half*>(x);
+  a.y = static_cast<__half*>(y);
+  a.ldx = ldx;
+  a.ldy = ldy;
+  a.M = p.M;
+  a.K = p.K;
+  a.K_pad = p.K_pad;
+  a.MT = p.row_tiles;
+  a.KB = p.k_units;
+  a.n_slots = p.n_outliers > 0 ? p.outlier_tiles * opc::kTileRows : 0;
+  a.batch = batch;
+  const dim3 grid(static_cast<unsigned>(p.row_tiles + ceil_div(a.n_slots, opc::kVq8Warps)),
+                  static_cast<unsigned>(ceil_div(batch, 8)));
+  opc::vq8_gemv_kernel<<<grid, opc::kVq8Warps * 32, 0, s>>>(a);
+  OPC_CUDA(cudaGetLastError(), "launch vq8_gemv_kernel");
+  return OPC_OK;
+}
+}  // namespace
+
+extern "C" {
+
 int opc_gemv(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ldy, int32_t batch, void* workspace,
              size_t workspace_bytes_given, void* stream_v) {
   if (!L || !plan_ok(&L->plan)) return fail(OPC_ERR_INVALID, "opc_gemv: invalid layer plan");
@@ -442,8 +524,9 @@ int opc_gemv(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ld
     return fail(OPC_ERR_INVALID, "opc_gemv: ldx=%lld < K=%d or ldy=%lld < M=%d", static_cast<long long>(ldx), p.K,
                 static_cast<long long>(ldy), p.M);
   if (!aligned(x, 2) || !aligned(y, 2)) return fail(OPC_ERR_INVALID, "opc_gemv: x/y not 2-byte aligned");
-  if (!aligned(L->units, 16) || !aligned(L->codebooks, 8))
-    return fail(OPC_ERR_INVALID, "opc_gemv: layer buffers misaligned (units 16 B, codebooks 8 B)");
+  if (!aligned(L->units, 16) || !aligned(L->codebooks, 16))
+    return fail(OPC_ERR_INVALID, "opc_gemv: layer buffers misaligned (units and codebooks 16 B)");
+  if (p.sub_vector_size == 8) return launch_vq8(L, x, ldx, y, ldy, batch, static_cast<cudaStream_t>(stream_v));
   int dev = 0;
   OPC_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
   DeviceCache dc;
@@ -609,8 +692,9 @@ int opc_gemv_noalloc(const opc_layer* L, const void* x, int64_t ldx, void* y, in
     return fail(OPC_ERR_INVALID, "opc_gemv_noalloc: ldx=%lld < K=%d or ldy=%lld < M=%d", static_cast<long long>(ldx),
                 p.K, static_cast<long long>(ldy), p.M);
   if (!aligned(x, 2) || !aligned(y, 2)) return fail(OPC_ERR_INVALID, "opc_gemv_noalloc: x/y not 2-byte aligned");
-  if (!aligned(L->units, 16) || !aligned(L->codebooks, 8))
-    return fail(OPC_ERR_INVALID, "opc_gemv_noalloc: layer buffers misaligned (units 16 B, codebooks 8 B)");
+  if (!aligned(L->units, 16) || !aligned(L->codebooks, 16))
+    return fail(OPC_ERR_INVALID, "opc_gemv_noalloc: layer buffers misaligned (units and codebooks 16 B)");
+  if (p.sub_vector_size == 8) return launch_vq8(L, x, ldx, y, ldy, batch, static_cast<cudaStream_t>(stream_v));
   if (p.total_units >= (int64_t(1) << 31))
     return fail(OPC_ERR_UNSUPPORTED, "opc_gemv_noalloc: layer too large (2^31 units)");
   int dev = 0;
@@ -671,6 +755,17 @@ int opc_dequant(const opc_layer* L, void* w, int64_t ldw, void* stream_v) {
   const opc_layer_plan& p = L->plan;
   if (!w || ldw < p.K) return fail(OPC_ERR_INVALID, "opc_dequant: bad output (ldw=%lld, K=%d)", static_cast<long long>(ldw), p.K);
   if (!aligned(L->units, 16)) return fail(OPC_ERR_INVALID, "opc_dequant: units not 16-byte aligned");
+  if (p.sub_vector_size == 8) {
+    const opc::Vq8Geom V = vq8_geom_of(p);
+    const int64_t n = static_cast<int64_t>(p.M) * p.K;
+    opc::vq8_dequant_kernel<<<static_cast<unsigned>(ceil_div(n, 256)), 256, 0, static_cast<cudaStream_t>(stream_v)>>>(
+        V, static_cast<const uint32_t*>(L->units), static_cast<const uint32_t*>(L->codebooks),
+        static_cast<const uint16_t*>(L->tile_mask),
+        reinterpret_cast<const uint16_t*>(static_cast<const uint8_t*>(L->units) + p.packed_units * opc::kVq8UnitBytes),
+        L->outlier_rows, static_cast<__half*>(w), ldw);
+    OPC_CUDA(cudaGetLastError(), "launch vq8_dequant_kernel");
+    return OPC_OK;
+  }
   const opc::LayerGeom G = geom_of(p);
   const int warps = 8;
   opc::dequant_kernel<<<static_cast<unsigned>(ceil_div(p.total_units, warps)), warps * 32, 0,
@@ -683,6 +778,9 @@ int opc_dequant(const opc_layer* L, void* w, int64_t ldw, void* stream_v) {
 
 int opc_gemm(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ldy, int32_t n_tok, void* stream_v) {
   if (!L || !plan_ok(&L->plan)) return fail(OPC_ERR_INVALID, "opc_gemm: invalid layer plan");
+  if (L->plan.sub_vector_size != 1)
+    return fail(OPC_ERR_UNSUPPORTED, "opc_gemm: sub_vector_size %d (the prefill GEMM runs svs = 1; use opc_gemv)",
+                L->plan.sub_vector_size);
   const opc_layer_plan& p = L->plan;
   if (!L->units || !L->codebooks || !L->tile_mask || !L->outlier_rows)
     return fail(OPC_ERR_INVALID, "opc_gemm: layer buffers not allocated");
@@ -798,6 +896,9 @@ int check_chain_steps(const char* fn, const opc_chain_step* steps, int32_t n, in
   for (int j = 0; j < n; ++j) {
     const opc_chain_step& st = steps[j];
     if (!st.layer || !plan_ok(&st.layer->plan)) return fail(OPC_ERR_INVALID, "%s: step %d: invalid layer", fn, j);
+    if (st.layer->plan.sub_vector_size != 1)
+      return fail(OPC_ERR_UNSUPPORTED, "%s: step %d: sub_vector_size %d (the chain runs svs = 1)", fn, j,
+                  st.layer->plan.sub_vector_size);
     const opc_layer* L = st.layer;
     const opc_layer_plan& p = L->plan;
     if (!L->units || !L->codebooks || !L->tile_mask || !L->outlier_rows || !aligned(L->units, 16))

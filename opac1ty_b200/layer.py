@@ -45,10 +45,11 @@ def plan_layer(M: int, K: int, n_outliers: int, sub_vector_size: int = 1) -> _li
     return plan
 
 
-def algorithmic_bytes(M: int, K: int, n_outliers: int, batch: int = 1) -> int:
-    """Bytes a fused GEMV must move at least: 2-bit indices, fp16 codebooks, fp16 outlier rows
-    with int32 ids, x in and y out (fp16)."""
-    return M * K // 4 + 8 * M + n_outliers * (2 * K + 4) + 2 * K * batch + 2 * M * batch
+def algorithmic_bytes(M: int, K: int, n_outliers: int, batch: int = 1, sub_vector_size: int = 1) -> int:
+    """Bytes a fused GEMV must move at least: 2-bit indices (one per sub-vector), fp16 codebooks
+    (4 vectors of sub_vector_size per row), fp16 outlier rows with int32 ids, x in and y out (fp16)."""
+    svs = int(sub_vector_size)
+    return (M * (K // svs) // 4 + 8 * svs * M + n_outliers * (2 * K + 4) + 2 * K * batch + 2 * M * batch)
 
 
 @dataclass
@@ -88,8 +89,12 @@ class DeviceLayer:
     def n_outliers(self) -> int:
         return self.plan.n_outliers
 
+    @property
+    def sub_vector_size(self) -> int:
+        return self.plan.sub_vector_size
+
     def algorithmic_bytes(self, batch: int = 1) -> int:
-        return algorithmic_bytes(self.M, self.K, self.n_outliers, batch)
+        return algorithmic_bytes(self.M, self.K, self.n_outliers, batch, self.plan.sub_vector_size)
 
     def device_bytes(self) -> int:
         return sum(t.numel() * t.element_size() for t in (self.units, self.codebooks, self.tile_mask, self.outlier_rows))
@@ -116,8 +121,10 @@ def prepare_layer(layer: dict, device=None, name: Optional[str] = None) -> Devic
     cb = layer["codebooks"]
     idx = layer["indices"]
     svs = int(cb.shape[2]) if cb.dim() == 3 else 1
-    if svs != 1:
-        raise _lib.OpcError(_lib.OPC_ERR_UNSUPPORTED, f"sub_vector_size={svs}: only 1 is implemented on the GPU path")
+    if svs not in (1, 8):
+        raise _lib.OpcError(_lib.OPC_ERR_UNSUPPORTED, f"sub_vector_size={svs}: 1 and 8 are implemented on the GPU path")
+    if svs == 8 and in_f % 8:
+        raise _lib.OpcError(_lib.OPC_ERR_UNSUPPORTED, f"in_features={in_f} is not a multiple of sub_vector_size 8")
     if tuple(cb.shape[:2]) != (out_f, 4):
         raise ValueError(f"codebooks shape {tuple(cb.shape)} does not match ({out_f}, 4, {svs})")
     if tuple(idx.shape) != (out_f, in_f // svs):

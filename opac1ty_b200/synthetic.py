@@ -76,6 +76,29 @@ def random_layer(M: int, K: int, n_outliers: int, seed: int, id_dtype=torch.int6
     return layer
 
 
+def random_layer_vq8(M: int, K: int, n_outliers: int, seed: int, shuffle_ids: bool = False) -> dict:
+    """A sub_vector_size 8 "quantized" layer dict (the reference quantizer's default,
+    opacc1ty/cli/main.py:71-72): cb [M][4][8] fp16, idx [M][K/8] uint8, outlier rows [n][K]."""
+    if K % 8:
+        raise ValueError("random_layer_vq8: K must be a multiple of 8")
+    rng = rng_for(seed)
+    cb = (rng.standard_normal((M, 4, 8)) * STD).astype(np.float16)
+    idx = rng.integers(0, 4, size=(M, K // 8), dtype=np.uint8)
+    layer = {"type": "quantized", "shape": (M, K), "codebooks": torch.from_numpy(cb), "indices": torch.from_numpy(idx),
+             "outlier_values": None, "outlier_indices": None, "outlier_mask": None}
+    if n_outliers > 0:
+        ids = np.sort(rng.choice(M, size=n_outliers, replace=False)).astype(np.int64)
+        if shuffle_ids:
+            rng.shuffle(ids)
+        scale = 8 * STD / math.sqrt(NU / (NU - 2))
+        ov = (rng.standard_t(NU, size=(n_outliers, K)) * scale).astype(np.float16)
+        cb[ids] = 0
+        layer["codebooks"] = torch.from_numpy(cb)
+        layer["outlier_values"] = torch.from_numpy(ov)
+        layer["outlier_indices"] = torch.from_numpy(ids)
+    return layer
+
+
 def random_layer_device(M: int, K: int, n_outliers: int, seed: int, device) -> dict:
     """Like ``random_layer`` but generated with torch's RNG directly on ``device`` (fast for the
     full model stacks; values differ from the numpy generator, the statistics do not)."""

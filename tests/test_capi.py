@@ -57,9 +57,22 @@ def test_plan_rejects_bad_arguments():
         plan_layer(16, 16, 17)
     assert e.value.code == _lib.OPC_ERR_INVALID
     with pytest.raises(_lib.OpcError) as e:
-        plan_layer(16, 64, 0, sub_vector_size=8)
+        plan_layer(16, 64, 0, sub_vector_size=4)
     assert e.value.code == _lib.OPC_ERR_UNSUPPORTED
     assert "sub_vector_size" in _lib.last_error()
+    with pytest.raises(_lib.OpcError) as e:
+        plan_layer(16, 60, 0, sub_vector_size=8)   # K not a multiple of 8
+    assert e.value.code == _lib.OPC_ERR_UNSUPPORTED
+
+
+def test_plan_svs8_sizes():
+    from opac1ty_b200.layer import plan_layer
+
+    p = plan_layer(40, 520, 3, sub_vector_size=8)
+    assert (p.row_tiles, p.M_pad, p.k_units, p.K_pad) == (3, 48, 3, 768)
+    assert p.units_bytes == 3 * 3 * 128 + 16 * 768 * 2     # index units, then 16 outlier slots
+    assert p.codebook_bytes == 48 * 64
+    assert p.tile_mask_bytes == 3 * 2
 
 
 def test_count_distinct_ids():
