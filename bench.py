@@ -349,10 +349,21 @@ def per_layer_timing(stack, dev, reps: int = 20) -> list:
     for name, dl, x, y in plan:
         for _ in range(3):
             L.gemv(dl, x, out=y, workspace=stack.workspace)
+        torch.cuda.synchronize()
+        # replayed from a CUDA graph, so the time is the GPU's rather than the Python call rate
+        g = torch.cuda.CUDAGraph()
+        cs = torch.cuda.Stream(dev)
+        cs.wait_stream(stream)
+        with torch.cuda.stream(cs):
+            L.gemv(dl, x, out=y, workspace=stack.workspace)
+        stream.wait_stream(cs)
+        with torch.cuda.graph(g):
+            for _ in range(reps):
+                L.gemv(dl, x, out=y, workspace=stack.workspace)
+        g.replay()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for _ in range(reps):
-            L.gemv(dl, x, out=y, workspace=stack.workspace)
+        g.replay()
         e1.record(stream)
         torch.cuda.synchronize()
         us = e0.elapsed_time(e1) * 1000.0 / reps

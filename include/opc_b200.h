@@ -19,9 +19,11 @@
  *   outlier values [n][K]      fp16, whole output rows
  *   outlier ids    [n]         integer row ids
  * opc_repack_layer converts it once, at load time, into the device layout the kernels stream
- * (see opc_layer_plan below).  Only sub_vector_size == 1 (the 2 bits/weight scalar-codebook
- * case, 4 fp16 centroids per output row) is implemented; other sizes return
- * OPC_ERR_UNSUPPORTED.
+ * (see opc_layer_plan below).  sub_vector_size 1 (2 bits/weight, 4 fp16 centroids per output
+ * row) runs on every path; sub_vector_size 8 (true VQ: an index selects one of 4 fp16 vectors of
+ * 8 per row, the reference quantizer's default) runs opc_gemv / opc_gemv_noalloc (any batch)
+ * and opc_dequant, with K a multiple of 8; other sizes, and svs 8 on the GEMM or the chain,
+ * return OPC_ERR_UNSUPPORTED.
  */
 #ifndef OPC_B200_H
 #define OPC_B200_H
@@ -38,7 +40,7 @@ extern "C" {
 enum {
   OPC_OK = 0,
   OPC_ERR_INVALID = -1,     /* bad argument: shape, pointer, alignment, out-of-range id */
-  OPC_ERR_UNSUPPORTED = -2, /* valid request this build does not implement (e.g. svs != 1) */
+  OPC_ERR_UNSUPPORTED = -2, /* valid request this build does not implement (e.g. svs 4) */
   OPC_ERR_CUDA = -3,        /* a CUDA runtime call failed; message has the CUDA error */
   OPC_ERR_WORKSPACE = -4,   /* workspace missing or smaller than opc_gemv_workspace_bytes() */
   OPC_ERR_DEVICE = -5       /* a kernel reported an error through the device error word */
@@ -47,7 +49,14 @@ enum {
 /* Geometry of one repacked layer.  Filled by opc_plan_layer(); the caller allocates the four
  * device buffers with the byte sizes given here.
  *
- * Device layout ("units" are 512-byte blocks streamed by the GEMV):
+ * sub_vector_size 8: k_units = K_pad/256 (K_pad = K rounded up to 256); units = packed_units
+ * 128-byte index units (row tile t x 256-column block b = unit t*k_units + b; 16 bytes per row
+ * pair g, byte s of word w holding the 2-bit vector indices of rows g and g+8 for the two
+ * 8-column groups of k16 step 4w+s), then the outlier rows row-major [outlier_tiles*16][K_pad]
+ * fp16; codebooks [row_tiles][32 lanes][8] 32-bit words (lane 4g+q: halves 2q, 2q+1 of vectors
+ * 0..3 of row g, then of row g+8; outlier rows zero); tile_mask and outlier_rows as below.
+ *
+ * sub_vector_size 1 device layout ("units" are 512-byte blocks streamed by the GEMV):
  *   units[0 .. packed_units)      packed 2-bit indices: row tile t (16 rows) x k block b (128
  *                                 columns) is unit t*k_units + b.  Inside a unit, lane l of a
  *                                 warp owns bytes [16l, 16l+16): four 32-bit words whose 2-bit

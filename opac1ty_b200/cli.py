@@ -122,11 +122,22 @@ def _time_gemv(dl, batch: int, iters: int):
     ws = torch.zeros(L.workspace_bytes(dl, batch), dtype=torch.uint8, device=dl.device)
     for _ in range(3):
         L.gemv(dl, x, out=y, workspace=ws)
+    torch.cuda.synchronize(dl.device)
+    # the iterations are replayed from a CUDA graph: the time is the GPU's, not the Python call rate
+    g = torch.cuda.CUDAGraph()
+    cs = torch.cuda.Stream(dl.device)
+    cs.wait_stream(torch.cuda.current_stream(dl.device))
+    with torch.cuda.stream(cs):
+        L.gemv(dl, x, out=y, workspace=ws)
+    torch.cuda.current_stream(dl.device).wait_stream(cs)
+    with torch.cuda.graph(g):
+        for _ in range(iters):
+            L.gemv(dl, x, out=y, workspace=ws)
+    g.replay()
     s = torch.cuda.current_stream(dl.device)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(s)
-    for _ in range(iters):
-        L.gemv(dl, x, out=y, workspace=ws)
+    g.replay()
     e1.record(s)
     torch.cuda.synchronize(dl.device)
     return e0.elapsed_time(e1) * 1000.0 / iters
@@ -169,7 +180,8 @@ def benchmark(bf2_path, batch, iters, json_output):
 @click.option("--outliers", type=float, default=0.01, help="outlier row fraction (0 = none)")
 @click.option("--batch", type=int, default=1)
 @click.option("--iters", type=int, default=20)
-def layer_bench(shape, outliers, batch, iters):
+@click.option("--svs", type=click.Choice(["1", "8"]), default="1", help="sub_vector_size of the synthetic layer")
+def layer_bench(shape, outliers, batch, iters, svs):
     """Time one synthetic layer's fused GEMV (CUDA events); prints one JSON line."""
     import torch
 
@@ -178,12 +190,17 @@ def layer_bench(shape, outliers, batch, iters):
 
     M, K = (int(v) for v in shape.lower().split("x"))
     dev = torch.device("cuda", 0)
-    ly = synthetic.random_layer_device(M, K, synthetic.n_outliers_for(M, outliers), seed=0, device=dev)
+    n_out = synthetic.n_outliers_for(M, outliers)
+    if svs == "8":
+        ly = synthetic.random_layer_vq8(M, K, n_out, seed=0)
+    else:
+        ly = synthetic.random_layer_device(M, K, n_out, seed=0, device=dev)
     dl = L.prepare_layer(ly, dev)
     us = _time_gemv(dl, batch, iters)
     nb = dl.algorithmic_bytes(batch)
-    click.echo(json.dumps({"gpu": get_cuda_device_info().name, "shape": [M, K], "n_outliers": dl.n_outliers,
-                           "batch": batch, "us": us, "bytes": nb, "gbs": nb / us / 1e3}))
+    click.echo(json.dumps({"gpu": get_cuda_device_info().name, "shape": [M, K], "svs": int(svs),
+                           "n_outliers": dl.n_outliers, "batch": batch, "us": us, "bytes": nb, "gbs": nb / us / 1e3,
+                           "tflops": 2.0 * M * K * batch / us / 1e6}))
 
 
 @cli.command("decode-bench")

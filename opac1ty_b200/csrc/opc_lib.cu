@@ -500,11 +500,24 @@ int launch_vq8(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t 
   a.K_pad = p.K_pad;
   a.MT = p.row_tiles;
   a.KB = p.k_units;
-  a.n_slots = p.n_outliers > 0 ? p.outlier_tiles * opc::kTileRows : 0;
+  a.OT = p.n_outliers > 0 ? p.outlier_tiles : 0;
   a.batch = batch;
-  const dim3 grid(static_cast<unsigned>(p.row_tiles + ceil_div(a.n_slots, opc::kVq8Warps)),
-                  static_cast<unsigned>(ceil_div(batch, 8)));
-  opc::vq8_gemv_kernel<<<grid, opc::kVq8Warps * 32, 0, s>>>(a);
+  a.x_vec16 = aligned(x, 16) && ldx % 8 == 0;
+  // batch columns per CTA: as many of 8 as the staged x allows
+  const size_t col_bytes = static_cast<size_t>(p.K_pad + 8) * 2;
+  int nc = 8;
+  while (nc > 1 && static_cast<size_t>(nc) * col_bytes > static_cast<size_t>(opc::kVq8XsMaxBytes)) nc >>= 1;
+  while (nc > 1 && nc / 2 >= batch) nc >>= 1;
+  if (col_bytes > static_cast<size_t>(opc::kVq8XsMaxBytes))
+    return fail(OPC_ERR_UNSUPPORTED, "opc_gemv: K=%d too large for the svs=8 kernel's staged x", p.K);
+  a.nc = nc;
+  const size_t smem = static_cast<size_t>(nc) * col_bytes;
+  static std::once_flag attr_once;
+  std::call_once(attr_once, []() {
+    cudaFuncSetAttribute(opc::vq8_gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, opc::kVq8XsMaxBytes);
+  });
+  const dim3 grid(static_cast<unsigned>(p.row_tiles + a.OT), static_cast<unsigned>(ceil_div(batch, nc)));
+  opc::vq8_gemv_kernel<<<grid, opc::kVq8Warps * 32, smem, s>>>(a);
   OPC_CUDA(cudaGetLastError(), "launch vq8_gemv_kernel");
   return OPC_OK;
 }

@@ -11,10 +11,11 @@
 //  * codebooks: per tile, lane l holds 8 words: word c (0..3) = row g's vector c at halves
 //    (2q, 2q+1), word 4+c the same for row g+8.  An m16n8k16 A-fragment register is one of four
 //    such words, chosen by a 2-bit index: a 4-way select, no memory lookup.
-//  * x is read straight from global memory through the read-only path (L1-resident per CTA).
-//  * one CTA per row tile (8 warps splitting the k blocks) and per 8 batch columns; warps reduce
-//    in a fixed order through shared memory (deterministic); outlier rows (zero codebooks, masked
-//    out) are computed by extra CTAs from their row-major fp16 copies.
+//  * x is staged once per CTA in shared memory (nc batch columns, the B fragments' columns).
+//  * one CTA per row tile (8 warps splitting the k blocks, the next block's index unit loaded
+//    ahead) and per nc batch columns; warps reduce in a fixed order through shared memory
+//    (deterministic); outlier rows (zero codebooks, masked out) are computed by extra CTAs on the
+//    same tensor path, their A fragments loaded block by block from the row-major fp16 copies.
 #pragma once
 
 #include "opc_device.cuh"
@@ -26,16 +27,20 @@ constexpr int kVq8UnitBytes = 128;     // 16 rows x 32 groups x 2 bits
 constexpr int kVq8CbTileBytes = 1024;  // 16 rows x 4 vectors x 8 fp16
 constexpr int kVq8Warps = 8;
 
+constexpr int kVq8XsMaxBytes = 96 * 1024;  // staged x per CTA
+
 struct Vq8Args {
   const uint4* units;      // [MT][KB] index units (16 bytes per row pair g)
   const uint4* cb;         // [MT][32 lanes][2] codebook words
   const uint16_t* tile_mask;
-  const __half* orows;     // [slots][K_pad] fp16 outlier rows
+  const __half* orows;     // [slots][K_pad] fp16 outlier rows (zero past K)
   const int32_t* orow;     // [slots] output row, -1 = padding
   const __half* x;
   __half* y;
   int64_t ldx, ldy;
-  int32_t M, K, K_pad, MT, KB, n_slots, batch;
+  int32_t M, K, K_pad, MT, KB, OT, batch;
+  int32_t nc;              // batch columns per CTA (1, 2, 4 or 8): x[nc][K_pad] staged in smem
+  int32_t x_vec16;         // x rows 16-byte loadable
 };
 
 // 4-way select of a codebook word by a 2-bit index
@@ -45,78 +50,114 @@ __device__ __forceinline__ uint32_t vq8_sel(uint32_t c0, uint32_t c1, uint32_t c
   return (i & 2u) ? hi : lo;
 }
 
-// B fragment of x for batch column n = g (zero past the batch or K): halves k, k+1
-__device__ __forceinline__ uint32_t vq8_xpair(const Vq8Args& a, int n, int k) {
-  if (n >= a.batch || k >= a.K) return 0u;
-  const __half* p = a.x + static_cast<int64_t>(n) * a.ldx + k;
-  if (k + 1 < a.K && (reinterpret_cast<uintptr_t>(p) & 3) == 0) return ld_nc_u32(p);
-  const uint32_t h0 = ld_nc_u16(p);
-  const uint32_t h1 = (k + 1 < a.K) ? ld_nc_u16(p + 1) : 0u;
-  return h0 | (h1 << 16);
-}
-
+// Grid: x = MT packed tiles + OT outlier tiles, y = batch chunks of nc columns.  Dynamic shared
+// memory: x[nc][K_pad + 8] fp16 (the +8 halves make the B-fragment reads conflict-free).
 __global__ void __launch_bounds__(kVq8Warps * 32) vq8_gemv_kernel(const Vq8Args a) {
+  extern __shared__ __align__(16) unsigned char vq8_smem[];
   __shared__ float red[kVq8Warps][32][4];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, q = lane & 3;
-  const int n0 = blockIdx.y * 8;  // batch columns n0..n0+7
-  const int nb = n0 + g;          // this lane's B-fragment column
-  if (blockIdx.x < a.MT) {
-    const int t = blockIdx.x;
-    // this lane's 8 codebook words (rows g, g+8; pair q of every vector)
-    const uint4 c01 = ld_nc_v4(a.cb + (static_cast<int64_t>(t) * 32 + lane) * 2);
-    const uint4 c23 = ld_nc_v4(a.cb + (static_cast<int64_t>(t) * 32 + lane) * 2 + 1);
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  const int n0 = blockIdx.y * a.nc;
+  const int ncols = min(a.nc, a.batch - n0);
+  const int xstride = a.K_pad + 8;
+  __half* xs = reinterpret_cast<__half*>(vq8_smem);
+  const bool packed = blockIdx.x < a.MT;
+  const int t = packed ? blockIdx.x : blockIdx.x - a.MT;
+  // the tile's codebook words and this warp's first index unit: issued before staging x, so the
+  // three memory round trips overlap
+  uint4 c01 = make_uint4(0, 0, 0, 0), c23 = make_uint4(0, 0, 0, 0), iw = make_uint4(0, 0, 0, 0);
+  const uint4* ub = a.units + static_cast<int64_t>(t) * a.KB * 8 + g;
+  if (packed) {
+    c01 = ld_nc_v4(a.cb + (static_cast<int64_t>(t) * 32 + lane) * 2);
+    c23 = ld_nc_v4(a.cb + (static_cast<int64_t>(t) * 32 + lane) * 2 + 1);
+    if (warp < a.KB) iw = ld_nc_v4(ub + warp * 8);
+  }
+  // stage this CTA's batch columns of x (zero past K)
+  const int chunks = a.K_pad / 8;
+  for (int i = threadIdx.x; i < ncols * chunks; i += blockDim.x) {
+    const int n = i / chunks, k = (i - n * chunks) * 8;
+    const __half* src = a.x + static_cast<int64_t>(n0 + n) * a.ldx + k;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (k + 8 <= a.K && a.x_vec16) {
+      v = ld_nc_v4(src);
+    } else if (k < a.K) {
+      uint32_t h[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) h[e] = (k + e < a.K) ? ld_nc_u16(src + e) : 0u;
+      v = make_uint4(h[0] | (h[1] << 16), h[2] | (h[3] << 16), h[4] | (h[5] << 16), h[6] | (h[7] << 16));
+    }
+    *reinterpret_cast<uint4*>(xs + n * xstride + k) = v;
+  }
+  __syncthreads();
+  const bool live_col = g < ncols;  // this lane's B-fragment column
+  const uint32_t xrow = smem_u32(xs + (live_col ? g : 0) * xstride) + 4 * q;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  if (packed) {
+    // c01/c23: this lane's 8 codebook words (rows g, g+8; pair q of every vector)
     for (int kb = warp; kb < a.KB; kb += kVq8Warps) {
-      const uint4 iw = ld_nc_v4(a.units + (static_cast<int64_t>(t) * a.KB + kb) * 8 + g);
+      const uint4 nxt = kb + kVq8Warps < a.KB ? ld_nc_v4(ub + (kb + kVq8Warps) * 8) : iw;  // next block's unit
       const uint32_t words[4] = {iw.x, iw.y, iw.z, iw.w};
 #pragma unroll
       for (int s = 0; s < 16; ++s) {
         const uint32_t byte = (words[s >> 2] >> (8 * (s & 3))) & 0xffu;
-        const int k = kb * kVq8BlockCols + 16 * s + 2 * q;
+        const uint32_t xa = xrow + 2 * (kb * kVq8BlockCols + 16 * s);
         uint32_t A[4];
         A[0] = vq8_sel(c01.x, c01.y, c01.z, c01.w, byte & 3u);          // row g,   k, k+1
         A[1] = vq8_sel(c23.x, c23.y, c23.z, c23.w, (byte >> 4) & 3u);   // row g+8, k, k+1
         A[2] = vq8_sel(c01.x, c01.y, c01.z, c01.w, (byte >> 2) & 3u);   // row g,   k+8, k+9
         A[3] = vq8_sel(c23.x, c23.y, c23.z, c23.w, byte >> 6);          // row g+8, k+8, k+9
-        const uint32_t b0 = vq8_xpair(a, nb, k), b1 = vq8_xpair(a, nb, k + 8);
+        const uint32_t b0 = live_col ? lds32(xa) : 0u, b1 = live_col ? lds32(xa + 16) : 0u;
         mma16816(acc, A, b0, b1);
       }
+      iw = nxt;
     }
-    // fixed-order reduction over the warps (deterministic)
+  } else {
+    // outlier tile t: A fragments straight from the row-major fp16 rows, a block at a time
+    const __half* w0 = a.orows + static_cast<int64_t>(16 * t + g) * a.K_pad + 2 * q;
+    const __half* w1 = w0 + static_cast<int64_t>(8) * a.K_pad;
+    for (int kb = warp; kb < a.KB; kb += kVq8Warps) {
+      uint32_t Ab[16][4];
 #pragma unroll
-    for (int r = 0; r < 4; ++r) red[warp][lane][r] = acc[r];
-    __syncthreads();
-    if (warp == 0) {
-      float s[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int w = 0; w < kVq8Warps; ++w)
+      for (int s = 0; s < 16; ++s) {
+        const int k = kb * kVq8BlockCols + 16 * s;
+        Ab[s][0] = ld_nc_u32(w0 + k);
+        Ab[s][1] = ld_nc_u32(w1 + k);
+        Ab[s][2] = ld_nc_u32(w0 + k + 8);
+        Ab[s][3] = ld_nc_u32(w1 + k + 8);
+      }
 #pragma unroll
-        for (int r = 0; r < 4; ++r) s[r] += red[w][lane][r];
-      // C fragment: s[0], s[1] = row g, columns 2q, 2q+1; s[2], s[3] = row g+8
-      const uint32_t mask = a.tile_mask[t];
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const int row = 16 * t + g + 8 * (r >> 1);
-        const int n = n0 + 2 * q + (r & 1);
-        if (row < a.M && n < a.batch && !((mask >> (row & 15)) & 1u))
-          a.y[static_cast<int64_t>(n) * a.ldy + row] = __float2half_rn(s[r]);
+      for (int s = 0; s < 16; ++s) {
+        const uint32_t xa = xrow + 2 * (kb * kVq8BlockCols + 16 * s);
+        const uint32_t b0 = live_col ? lds32(xa) : 0u, b1 = live_col ? lds32(xa + 16) : 0u;
+        mma16816(acc, Ab[s], b0, b1);
       }
     }
-    return;
   }
-  // outlier rows: CTA o covers slots 8o .. 8o+7, one per warp; lanes stride over k
-  const int slot = (blockIdx.x - a.MT) * kVq8Warps + warp;
-  if (slot >= a.n_slots) return;
-  const int row = a.orow[slot];
-  if (row < 0) return;
-  const __half* w = a.orows + static_cast<int64_t>(slot) * a.K_pad;
-  for (int n = n0; n < n0 + 8 && n < a.batch; ++n) {
-    const __half* xr = a.x + static_cast<int64_t>(n) * a.ldx;
-    float s = 0.f;
-    for (int k = lane; k < a.K; k += 32) s = fmaf(__half2float(w[k]), __half2float(xr[k]), s);
+  // fixed-order reduction over the warps (deterministic)
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if (lane == 0) a.y[static_cast<int64_t>(n) * a.ldy + row] = __float2half_rn(s);
+  for (int r = 0; r < 4; ++r) red[warp][lane][r] = acc[r];
+  __syncthreads();
+  if (warp != 0) return;
+  float sum[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int w = 0; w < kVq8Warps; ++w)
+#pragma unroll
+    for (int r = 0; r < 4; ++r) sum[r] += red[w][lane][r];
+  // C fragment: sum[0], sum[1] = row g, columns 2q, 2q+1; sum[2], sum[3] = row g+8
+  const uint32_t mask = packed ? a.tile_mask[t] : 0u;
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int ri = g + 8 * (r >> 1);
+    const int n = n0 + 2 * q + (r & 1);
+    if (n >= n0 + ncols) continue;
+    int row;
+    if (packed) {
+      row = 16 * t + ri;
+      if (row >= a.M || ((mask >> ri) & 1u)) continue;
+    } else {
+      row = a.orow[16 * t + ri];
+      if (row < 0) continue;
+    }
+    a.y[static_cast<int64_t>(n) * a.ldy + row] = __float2half_rn(sum[r]);
   }
 }
 
@@ -155,7 +196,7 @@ __global__ void vq8_repack_indices_kernel(Vq8Geom G, const uint8_t* idx, uint32_
   units[wi] = v;
 }
 
-// codebooks [M][4][8] fp16 -> per-tile lane words; outlier rows (orow_mask) get zeros
+// codebooks [M][4][8] fp16 -> per-tile lane words; outlier rows (tile_mask) get zeros
 __global__ void vq8_repack_codebooks_kernel(Vq8Geom G, const uint16_t* cb, const uint16_t* tile_mask, uint32_t* out) {
   const int64_t n_words = static_cast<int64_t>(G.MT) * 32 * 8;
   const int64_t wi = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
