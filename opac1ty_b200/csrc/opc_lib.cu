@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -949,11 +950,20 @@ int check_chain_steps(const char* fn, const opc_chain_step* steps, int32_t n, in
   return OPC_OK;
 }
 
-// Warps contributing to each outlier tile of a layer (the kernel's partition, replayed).
-std::vector<int32_t> outlier_contributors(const opc::ChainLayer& c, int G) {
+// Each CTA's share of a layer for the chain kernel (opc::chain_part): packed row tiles whole,
+// outlier units evenly over all CTAs.  Measured: filling the least-loaded CTAs with the outlier
+// units instead made the step 12% slower -- the outlier rows, completed by their last
+// contributor, then finish late and every next layer waits for them.
+std::vector<opc::ChainPart> chain_parts(const opc::ChainLayer& c, int G) {
+  std::vector<opc::ChainPart> parts(G);
+  for (int cta = 0; cta < G; ++cta) parts[cta] = opc::chain_part(c, cta, G);
+  return parts;
+}
+
+// Warps contributing to each outlier tile of a layer, for the kernel's completion counts.
+std::vector<int32_t> outlier_contributors(const opc::ChainLayer& c, const std::vector<opc::ChainPart>& parts) {
   std::vector<int32_t> n(std::max(c.OT, 0), 0);
-  for (int cta = 0; cta < G; ++cta) {
-    const opc::ChainPart p = opc::chain_part(c, cta, G);
+  for (const opc::ChainPart& p : parts) {
     for (int w = p.wp; w < opc::kQConsumers; ++w) {
       int32_t u0 = 0, u1 = 0;
       opc::chain_warp_range(p, w, &u0, &u1);
@@ -1025,12 +1035,13 @@ int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t 
     c.KT = p.k_units;
     c.OT = p.outlier_tiles;
     c.KO = p.outlier_k_units;
-    onc[j] = outlier_contributors(c, G);
+    const std::vector<opc::ChainPart> cparts = chain_parts(c, G);
+    onc[j] = outlier_contributors(c, cparts);
     onc_off[j] = off;
     off += align_up(std::max<size_t>(onc[j].size(), 1) * sizeof(int32_t), 256);
     // each CTA's share, so the kernel does no partition arithmetic: {pu0, pu1, ou0, ou1}, {wp, 0, 0, 0}
     for (int cta = 0; cta < G; ++cta) {
-      const opc::ChainPart pt = opc::chain_part(c, cta, G);
+      const opc::ChainPart& pt = cparts[cta];
       int32_t* e = parts.data() + 8 * (static_cast<size_t>(j) * G + cta);
       e[0] = pt.pu0;
       e[1] = pt.pu1;
