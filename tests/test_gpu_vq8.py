@@ -98,3 +98,20 @@ def test_vq8_rejections(cuda_device):
     yb = torch.zeros(1, 256, dtype=torch.float16, device=cuda_device)
     with pytest.raises(_lib.OpcError):
         C.Chain([(dl, xb, yb)])
+
+
+@pytest.mark.gpu
+def test_vq8_through_the_kernel_manager_raw_buffers(cuda_device):
+    """The reference's call shape (metal_utils.py:202-213: codebooks, indices, input, output, M,
+    K, outlier values, outlier ids, n) with sub_vector_size 8 buffers, as its Metal kernel takes."""
+    from opac1ty_b200.utils import CudaKernelManager
+
+    M, K, n = 512, 2048, 5
+    ly = synthetic.random_layer_vq8(M, K, n, seed=21)
+    mgr = CudaKernelManager(cuda_device)
+    x = torch.from_numpy(synthetic.activations(1, K, seed=4)).to(cuda_device).reshape(K)
+    y = torch.empty(M, dtype=torch.float16, device=cuda_device)
+    mgr.dequant_gemv(ly["codebooks"].to(cuda_device).reshape(-1), ly["indices"].to(cuda_device).reshape(-1), x, y,
+                     M, K, ly["outlier_values"].to(cuda_device), ly["outlier_indices"].to(cuda_device), n)
+    y64 = oracle.gemv_f64(oracle.dequantize_np(ly), x.cpu().numpy().reshape(1, K))
+    assert oracle.rel_err(y.cpu().numpy().reshape(1, M), y64) <= REL_TOL
