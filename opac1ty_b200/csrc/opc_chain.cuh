@@ -244,9 +244,10 @@ __device__ __noinline__ bool poll_flags_warp(const unsigned int* flags, int n, i
 __device__ __forceinline__ float pow2f(int e) { return __int_as_float((127 + e) << 23); }
 
 // Code size matters here: the kernel's once-per-layer paths (staging, tails, the producer) run
-// while the weight stream saturates L2, where every instruction-cache miss costs a microsecond,
-// so they are kept small -- per-chunk work is an out-of-line function called per chunk, not
-// unrolled copies.  Only the units loop is unrolled.
+// while the weight stream saturates the memory system, and their code is fetched again for every
+// layer (running the x-conversion pass twice in a row measured 2.0 us for the first pass and
+// 0.54 us for the second), so they are kept small -- per-chunk work is an out-of-line function
+// called per chunk, not unrolled copies.
 
 // Eight exchange words of k..k+7 (the first n_valid inside the row): do all carry `tag`?  Then
 // their fp16 values, packed in pairs, go to v.
@@ -625,6 +626,7 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
   int slot = 0;
   uint32_t phase = 0;
   bool ok = true;
+  bool staged0_seen = false;  // every CTA has staged layer 0 (true for the rest of the launch once seen)
 
   // Every CTA of every rank has published at least `target` (bounded; sets abort on a timeout).
   // The polling lanes' acquire fence plus the CTA barrier order every thread's later accesses.
@@ -788,10 +790,14 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
         }
       }
       if (tr && tid == 0) tr[5] = globaltimer_ns();
-      // a layer writing over the chain input starts once every CTA has read that input
-      if (L.y_alias_x0 && warp == 0 && !poll_flags_warp(args.sync, n_flags, lane, f_staged0, sys) && lane == 0) {
-        sh->abort = 1;
-        atomicCAS(&g_opc_device_error, 0, kDevErrBarrierTimeout);
+      // a layer writing over the chain input starts once every CTA has read that input (flags
+      // only grow within a launch, so the first layer that needs it waits and later ones do not)
+      if (L.y_alias_x0 && !staged0_seen) {
+        if (warp == 0 && !poll_flags_warp(args.sync, n_flags, lane, f_staged0, sys) && lane == 0) {
+          sh->abort = 1;
+          atomicCAS(&g_opc_device_error, 0, kDevErrBarrierTimeout);
+        }
+        staged0_seen = true;  // uniform over the consumer warps; a failed wait aborts below
       }
       named_barrier(1, kQConsumerThreads);
       if (sh->abort) {
@@ -821,21 +827,22 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
         const uint32_t stage = ring + slot * kQChunkBytes;
         const int32_t k0 = cc.u - cc.begin;
         if (cc.seg < L.MT) {
+          // not unrolled: one unit carries enough independent work for the ALU and tensor pipes
+          // (unrolling 2-8 units measured no faster), and the small loop keeps the kernel's code
+          // -- which every layer re-fetches -- small
+#pragma unroll 1
+          for (int i = 0; i < cnt; ++i) {
+            const uint4 wv = lds128(stage + i * kUnitBytes);
+            const uint32_t xa = xq + static_cast<uint32_t>(k0 + i) * kts;
+            const uint4 b01 = lds128(xa), b23 = lds128(xa + 16);
+            const uint32_t w[4] = {wv.x, wv.y, wv.z, wv.w};
+            const uint32_t bb[8] = {b01.x, b01.y, b01.z, b01.w, b23.x, b23.y, b23.z, b23.w};
 #pragma unroll
-          for (int i = 0; i < kQChunkUnits; ++i) {
-            if (i < cnt) {
-              const uint4 wv = lds128(stage + i * kUnitBytes);
-              const uint32_t xa = xq + static_cast<uint32_t>(k0 + i) * kts;
-              const uint4 b01 = lds128(xa), b23 = lds128(xa + 16);
-              const uint32_t w[4] = {wv.x, wv.y, wv.z, wv.w};
-              const uint32_t bb[8] = {b01.x, b01.y, b01.z, b01.w, b23.x, b23.y, b23.z, b23.w};
-#pragma unroll
-              for (int jw = 0; jw < 4; ++jw) {
-                uint32_t Ah[4], Al[4];
-                decode_word_q(w[jw], cur.qh, cur.ql, negz, Ah, Al);
-                imma16832(A.h[jw & 1], Ah, bb[2 * jw], bb[2 * jw + 1]);
-                imma16832(A.l[jw & 1], Al, bb[2 * jw], bb[2 * jw + 1]);
-              }
+            for (int jw = 0; jw < 4; ++jw) {
+              uint32_t Ah[4], Al[4];
+              decode_word_q(w[jw], cur.qh, cur.ql, negz, Ah, Al);
+              imma16832(A.h[jw & 1], Ah, bb[2 * jw], bb[2 * jw + 1]);
+              imma16832(A.l[jw & 1], Al, bb[2 * jw], bb[2 * jw + 1]);
             }
           }
         } else {
