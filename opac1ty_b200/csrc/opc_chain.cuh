@@ -303,25 +303,12 @@ __device__ __forceinline__ float chain_chunk_amax(const uint4& v) {
   return m;
 }
 
-// A chunk's eight values as 24-bit integers x*2^ex split into three signed int8 digits, stored at
-// their staged positions in the three digit columns of batch row b.
+// A chunk's eight values as offset integers x*2^ex + 2^22 (x_digits_q), stored at their staged
+// positions in the three unsigned digit columns of batch row b.
 __device__ __noinline__ void chain_store_digits(const uint4 v, float sc, uint32_t col0, uint32_t colb, uint32_t pos) {
-  const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
-  uint32_t d[3][2] = {{0, 0}, {0, 0}, {0, 0}};
+  const XDigitsQ d = x_digits_q(v, sc);
 #pragma unroll
-  for (int t = 0; t < 8; ++t) {
-    const __half hv = __ushort_as_half(static_cast<unsigned short>((wv[t >> 1] >> (16 * (t & 1))) & 0xffffu));
-    const int n = round_small_int(__half2float(hv) * sc);
-    const int d2 = ((n + 128) & 255) - 128;
-    const int n1 = (n - d2) >> 8;
-    const int d1 = ((n1 + 128) & 255) - 128;
-    const int d0 = (n1 - d1) >> 8;
-    d[0][t >> 2] |= (static_cast<uint32_t>(d0) & 0xffu) << (8 * (t & 3));
-    d[1][t >> 2] |= (static_cast<uint32_t>(d1) & 0xffu) << (8 * (t & 3));
-    d[2][t >> 2] |= (static_cast<uint32_t>(d2) & 0xffu) << (8 * (t & 3));
-  }
-#pragma unroll
-  for (int dd = 0; dd < 3; ++dd) sts64(col0 + dd * colb + pos, d[dd][0], d[dd][1]);
+  for (int dd = 0; dd < 3; ++dd) sts64(col0 + dd * colb + pos, d.d[dd][0], d.d[dd][1]);
 }
 
 constexpr int kChainSplitSlots = 32;  // packed tiles per CTA and layer (host-checked)
@@ -758,7 +745,9 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
         sh->amax[warp][0] = mx[0];
         sh->amax[warp][1] = mx[1];
       }
-      if (tid < 8) sts128(xs_base + args.xs_bytes - kQZeroBytes + tid * 16, make_uint4(0, 0, 0, 0));
+      if (tid < 16)  // ones block, zero block (B operands of the ones and absent columns)
+        sts128(xs_base + args.xs_bytes - kQZeroBytes - kQOnesBytes + tid * 16,
+               tid < 8 ? make_uint4(0x01010101u, 0x01010101u, 0x01010101u, 0x01010101u) : make_uint4(0, 0, 0, 0));
       named_barrier(1, kQConsumerThreads);  // every warp is done with layer j-1 and holds its x
       if (tr && tid == 0) tr[4] = globaltimer_ns();
       if (sh->abort) {
@@ -810,7 +799,8 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     // ---- this warp's units of layer j
     const int bcol = g >> 2, dig = g & 3;
     const bool live_col = dig < 3 && bcol < B;
-    const uint32_t colbase = live_col ? xs_base + (3 * bcol + dig) * xsq_col_bytes(L.KT) : xs_base + args.xs_bytes - kQZeroBytes;
+    const uint32_t colbase = live_col ? xs_base + (3 * bcol + dig) * xsq_col_bytes(L.KT)
+                                      : xs_base + args.xs_bytes - (bcol < B ? kQZeroBytes + kQOnesBytes : kQZeroBytes);
     const uint32_t kts = live_col ? 128u : 0u;
     const uint32_t xq = colbase + 32 * q, xo = colbase + 4 * q;
 

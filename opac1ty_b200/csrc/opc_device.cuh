@@ -150,15 +150,16 @@ __device__ __forceinline__ void mma16816(float c[4], const uint32_t a[4], uint32
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]), "f"(c[2]), "f"(c[3]));
   c[0] = d0; c[1] = d1; c[2] = d2; c[3] = d3;
 }
-// int8 x int8 -> int32 (exact).  m16n8k32: A 4 regs (row g / g+8, k 4q.., 16+4q..), B 2 regs.
+// int8 (A, signed) x uint8 (B, unsigned) -> int32 (exact).  m16n8k32: A 4 regs (row g / g+8,
+// k 4q.., 16+4q..), B 2 regs.
 __device__ __forceinline__ void imma16832(int32_t c[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
-  asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
       : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
-// m16n8k16: A 2 regs (row g / g+8, k 4q..4q+3), B 1 reg.
+// m16n8k16, A signed, B unsigned: A 2 regs (row g / g+8, k 4q..4q+3), B 1 reg.
 __device__ __forceinline__ void imma16816(int32_t c[4], uint32_t a0, uint32_t a1, uint32_t b0) {
-  asm("mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};\n"
+  asm("mma.sync.aligned.m16n8k16.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};\n"
       : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
       : "r"(a0), "r"(a1), "r"(b0));
 }

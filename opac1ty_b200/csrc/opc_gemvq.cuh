@@ -8,9 +8,12 @@
 //    centroids within 2^4 of the row's largest, else rounded to 2^-14 of it), split into two
 //    int8 parts n = 256*hi + lo.  One PRMT per part gathers four int8 weights, its selector
 //    being the masked index word itself (decode_word_q).
-//  * x is staged per CTA as 24-bit integers m = x * 2^e_x (e_x from the CTA's max |x|), split
-//    into three int8 digits m = 65536*d0 + 256*d1 + d2, placed in three B-operand columns: one
-//    m16n8k32 per codebook part yields all six part products, in int32 and exactly.
+//  * x is staged per CTA as integers m = round(x * 2^e_x), |m| < 2^22 (e_x from the CTA's max
+//    |x|), stored offset as m' = m + 2^22 in [0, 2^23): one FFMA per value yields a float whose
+//    low three bytes are m' itself (x_digits_q), and those bytes are the unsigned digits
+//    m' = 65536*d0 + 256*d1 + d2, placed in three B-operand columns (int8 x uint8 mma.sync).  A
+//    fourth column of ones gives each row's weight sum W, and T = T' - 2^22 W removes the offset:
+//    one m16n8k32 per codebook part yields all eight column products, in int32 and exactly.
 //  * At the end of a row tile the products combine into the exact int64 dot product
 //    T = sum_k n_k m_k, and y = fp16(T * 2^-(e_r + e_x)) is rounded once.  Partial sums of a tile
 //    split between warps or CTAs are int64 and add exactly (atomics included), so the result
@@ -33,10 +36,12 @@ constexpr int kQChunkUnits = 8;   // 4 KB per bulk copy: measured 6.9 TB/s strea
 constexpr int kQChunkBytes = kQChunkUnits * kUnitBytes;
 constexpr int kQMaxStages = 4;
 constexpr int kQMaxBatch = 2;
-constexpr int kQZeroBytes = 128;                   // B operand of absent columns
+constexpr int kQZeroBytes = 128;                   // B operand of absent columns (zeros) ...
+constexpr int kQOnesBytes = 128;                   // ... and of the ones columns; both end the staged x
 
 // Staged x: column c = 3*b + d (batch row b, digit d) is a row of KT*128 + 16 bytes; k of block kt
-// sits at byte 128*kt + xs_pos8(k & 127).
+// sits at byte 128*kt + xs_pos8(k & 127).  The last 256 bytes of the staged area are a block of
+// ones and a block of zeros, read with stride 0 by the ones and absent columns.
 __host__ __device__ constexpr int xsq_col_bytes(int KT) { return KT * 128 + 16; }
 
 struct GemvQArgs {
@@ -136,8 +141,11 @@ __device__ __forceinline__ void zero_accq(AccQ& A) {
 
 // Exact int64 dot products of rows g (t[0]) and g+8 (t[1]) for batch row q>>1, valid in lanes
 // with even q.  C fragment: element e is (row g + 8*(e>>1), column 2q + (e&1)); columns 0,1,2 are
-// the digits d0,d1,d2 of batch row 0 and 4,5,6 those of batch row 1 (3 and 7 are zero).
-// T = 2^24 H0 + 2^16 (H1 + L0) + 2^8 (H2 + L1) + L2, with H/L the hi/lo codebook-part products.
+// the digits d0,d1,d2 of batch row 0 and 4,5,6 those of batch row 1; 3 and 7 are the ones
+// columns (zero for an absent batch row).
+// T = 2^24 H0 + 2^16 (H1 + L0) + 2^8 (H2 + L1) + L2 - 2^22 (2^8 H3 + L3), with H/L the hi/lo
+// codebook-part products: the digits hold m + 2^22, and the ones column's products sum the row's
+// weights over the same k (a partial range's offset cancels within that range).
 __device__ __forceinline__ void finish_dot(const AccQ& A, int q, long long t[2]) {
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
@@ -149,10 +157,41 @@ __device__ __forceinline__ void finish_dot(const AccQ& A, int q, long long t[2])
     if ((q & 1) == 0)
       v = (h0 << 24) + ((h1 + l0) << 16) + (l1 << 8);  // columns d0, d1
     else
-      v = (h0 << 8) + l0;                              // columns d2, zero
+      v = (h0 << 8) + l0 - (((h1 << 8) + l1) << 22);   // columns d2, ones
     v += __shfl_xor_sync(0xffffffffu, v, 1);
     t[r] = v;
   }
+}
+
+// Eight fp16 values of x (packed pairs) as offset integers m' = round(x * 2^ex) + 2^22, for
+// |x| * 2^ex < 2^22.  x * 2^ex is exact, and adding 1.5 * 2^23 in the same FFMA rounds it to an
+// integer (to nearest, ties to even) with a float whose low 23 bits are then m' itself.  Byte
+// permutes gather the three bytes of m' of four values into one word per digit column: d2 (low
+// byte), d1, d0 (high byte, < 128).  A zero (padding past K included) encodes as 2^22 like any
+// other zero, so the ones column may cover the whole padded row.
+struct XDigitsQ {
+  uint32_t d[3][2];  // [column d0, d1, d2][values 0-3, 4-7]
+};
+__device__ __forceinline__ XDigitsQ x_digits_q(const uint4& v, float sc) {
+  const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+  uint32_t f[8];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 p = __half22float2(*reinterpret_cast<const __half2*>(&wv[e]));
+    f[2 * e] = __float_as_uint(fmaf(p.x, sc, 12582912.0f));
+    f[2 * e + 1] = __float_as_uint(fmaf(p.y, sc, 12582912.0f));
+  }
+  XDigitsQ r;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const uint32_t* g4 = f + 4 * h;
+    const uint32_t lo01 = prmt(g4[0], g4[1], 0x5140u), lo23 = prmt(g4[2], g4[3], 0x5140u);  // bytes 0, 1
+    const uint32_t hi01 = prmt(g4[0], g4[1], 0x0062u), hi23 = prmt(g4[2], g4[3], 0x0062u);  // byte 2
+    r.d[2][h] = prmt(lo01, lo23, 0x5410u);
+    r.d[1][h] = prmt(lo01, lo23, 0x7632u);
+    r.d[0][h] = prmt(hi01, hi23, 0x5410u);
+  }
+  return r;
 }
 
 __device__ __forceinline__ __half scale_to_half(long long t, int e) {
@@ -370,10 +409,11 @@ __global__ void __launch_bounds__(kQThreads, 1) gemvq_kernel(const GemvQArgs a) 
       ss->amax[warp][0] = mx[0];
       ss->amax[warp][1] = mx[1];
     }
-    if (tid < 8)  // zero block (B operand of absent columns)
-      sts128(xs_base + a.xs_bytes - kQZeroBytes + tid * 16, make_uint4(0, 0, 0, 0));
+    if (tid < 16)  // ones block, zero block (B operands of the ones and absent columns)
+      sts128(xs_base + a.xs_bytes - kQZeroBytes - kQOnesBytes + tid * 16,
+             tid < 8 ? make_uint4(0x01010101u, 0x01010101u, 0x01010101u, 0x01010101u) : make_uint4(0, 0, 0, 0));
     named_barrier(1, kQConsumerThreads);
-    // m * 2^e in [2^21, 2^22): digits d0 in [-64, 64], d1, d2 in [-128, 127]
+    // max |x| * 2^e in [2^21, 2^22): offset digits d0 in [0, 128], d1, d2 in [0, 255]
     float m0 = 0.f, m1 = 0.f;
     for (int w = 0; w < kQConsumers; ++w) {
       m0 = fmaxf(m0, ss->amax[w][0]);
@@ -394,35 +434,23 @@ __global__ void __launch_bounds__(kQThreads, 1) gemvq_kernel(const GemvQArgs a) 
         const int c = base + i * kQConsumerThreads;
         if (c < total) {
           const int b = c / per_row, k = (c - b * per_row) * 8;
-          const uint32_t wv[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
           const float sc = __int_as_float((127 + (b == 0 ? ex0 : ex1)) << 23);  // exact 2^e
-          uint32_t d[3][2] = {{0, 0}, {0, 0}, {0, 0}};
-#pragma unroll
-          for (int t = 0; t < 8; ++t) {
-            const __half hv = __ushort_as_half(static_cast<unsigned short>((wv[t >> 1] >> (16 * (t & 1))) & 0xffffu));
-            const int n = round_small_int(__half2float(hv) * sc);
-            const int d2 = ((n + 128) & 255) - 128;
-            const int n1 = (n - d2) >> 8;
-            const int d1 = ((n1 + 128) & 255) - 128;
-            const int d0 = (n1 - d1) >> 8;
-            d[0][t >> 2] |= (static_cast<uint32_t>(d0) & 0xffu) << (8 * (t & 3));
-            d[1][t >> 2] |= (static_cast<uint32_t>(d1) & 0xffu) << (8 * (t & 3));
-            d[2][t >> 2] |= (static_cast<uint32_t>(d2) & 0xffu) << (8 * (t & 3));
-          }
+          const XDigitsQ d = x_digits_q(v[i], sc);
           const uint32_t pos = static_cast<uint32_t>((k >> 7) * 128 + xs_pos8(k & 127));
 #pragma unroll
-          for (int dd = 0; dd < 3; ++dd) sts64(xs_base + (3 * b + dd) * colb + pos, d[dd][0], d[dd][1]);
+          for (int dd = 0; dd < 3; ++dd) sts64(xs_base + (3 * b + dd) * colb + pos, d.d[dd][0], d.d[dd][1]);
         }
       }
     }
   }
   named_barrier(1, kQConsumerThreads);  // x staged, exponents published
 
-  // B-operand column of this lane: batch row g>>2, digit g&3 (digit 3 and absent rows: zeros).
+  // B-operand column of this lane: batch row g>>2, digit g&3 (digit 3: the ones block; absent
+  // batch rows: the zero block).
   const int bcol = g >> 2, dig = g & 3;
   const bool live_col = dig < 3 && bcol < a.batch;
   const uint32_t colbase = live_col ? xs_base + (3 * bcol + dig) * xsq_col_bytes(a.KT)
-                                    : xs_base + a.xs_bytes - kQZeroBytes;
+                                    : xs_base + a.xs_bytes - (bcol < a.batch ? kQZeroBytes + kQOnesBytes : kQZeroBytes);
   const uint32_t kts = live_col ? 128u : 0u;
   const uint32_t xq = colbase + 32 * q;  // packed units: 32 bytes per k block
   const uint32_t xo = colbase + 4 * q;   // outlier units: 4 bytes at 16*(s&7) per k block

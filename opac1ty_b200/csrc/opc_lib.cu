@@ -563,7 +563,7 @@ int opc_gemv(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ld
   // Batch 1..2: the integer kernel, when its staged x and at least two ring stages fit.
   if (batch <= opc::kQMaxBatch) {
     const int xs_q = static_cast<int>(align_up(static_cast<size_t>(3 * batch) * opc::xsq_col_bytes(p.k_units) +
-                                                   opc::kQZeroBytes, 128));
+                                                   opc::kQZeroBytes + opc::kQOnesBytes, 128));
     int stages = opc::kQMaxStages;
     while (stages >= 2 && gemvq_smem(xs_q, stages) > static_cast<size_t>(dc.max_smem_optin)) --stages;
     if (stages >= 2) {
@@ -999,7 +999,8 @@ int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t 
     kt_max = std::max(kt_max, steps[j].layer->plan.k_units);
     bk_max = std::max<int64_t>(bk_max, static_cast<int64_t>(batch) * steps[j].layer->plan.K_pad);
   }
-  const int xs = static_cast<int>(align_up(static_cast<size_t>(3 * batch) * opc::xsq_col_bytes(kt_max) + opc::kQZeroBytes, 128));
+  const int xs = static_cast<int>(align_up(static_cast<size_t>(3 * batch) * opc::xsq_col_bytes(kt_max) +
+                                          opc::kQZeroBytes + opc::kQOnesBytes, 128));
   auto smem_for = [&](int stages) {
     return static_cast<size_t>(xs) + static_cast<size_t>(opc::kQConsumers) * stages * (opc::kQChunkBytes + 16) +
            sizeof(opc::ChainShared);
