@@ -65,12 +65,20 @@ struct ChainLayer {
   int32_t y_alias_x0;            // the fp16 output overlaps layer 0's input
 };
 
+// Per layer and CTA, the host-computed shares of its consumer warps, so the kernel does no integer
+// division: int32 [0..14] first unit of warp w, [15] packed warps wp, [16..30] end unit of warp w,
+// [31] the CTA's first packed tile, [32..46] first segment of warp w (0 for an empty range).
+constexpr int kChainShareInts = 48;
+constexpr int kChainSharePieces = kChainShareInts / 4;  // int4 pieces
+constexpr int kShU0 = 0, kShWp = 15, kShU1 = 16, kShTile0 = 31, kShSeg0 = 32;
+
 static_assert(sizeof(ChainLayer) % 16 == 0, "ChainLayer is copied in 16-byte pieces");
-static_assert(sizeof(ChainLayer) / 16 + 2 <= 32, "one warp copies a descriptor and a CTA share");
+static_assert(sizeof(ChainLayer) / 16 + kChainSharePieces <= 32, "one warp copies a descriptor and a CTA share");
+static_assert(kQConsumers == 15, "share table layout");
 
 struct ChainArgs {
   const ChainLayer* layers;
-  const int4* parts;         // [n_layers][grid][2] each CTA's share: {pu0, pu1, ou0, ou1}, {wp, 0, 0, 0}
+  const int4* parts;         // [n_layers][grid][kChainSharePieces] each CTA's warp shares
   unsigned int* sync;        // [world][grid] flags of every rank's CTAs, in this rank's memory
   unsigned int* sync_peer[kMaxRanks];  // rank p's flag array (sync_peer[rank] == sync)
   unsigned int* epoch;       // [0] launches completed (bit 31: poisoned), [1] CTAs finished
@@ -142,33 +150,17 @@ __host__ __device__ __forceinline__ void chain_warp_range(const ChainPart& p, in
     *u1 = p.ou0 + (w - p.wp + 1) * no / nw;
   }
 }
-__device__ __forceinline__ ChainPart chain_part_load(const int4* e) {
-  ChainPart p;
-  p.pu0 = e[0].x;
-  p.pu1 = e[0].y;
-  p.ou0 = e[0].z;
-  p.ou1 = e[0].w;
-  p.wp = e[1].x;
-  return p;
-}
 
 // Unit cursor over a layer (segments: packed tiles of KT units, outlier tiles of KO units).
 struct ChainCursor {
   int32_t u, seg, begin, end;
 };
-__device__ __forceinline__ ChainCursor chain_cursor(const ChainLayer& L, int32_t u) {
+__device__ __forceinline__ ChainCursor chain_cursor_at(const ChainLayer& L, int32_t u, int32_t seg) {
   ChainCursor c;
   c.u = u;
-  if (u < L.Up) {
-    c.seg = u / L.KT;
-    c.begin = c.seg * L.KT;
-    c.end = c.begin + L.KT;
-  } else {
-    const int32_t t = (u - L.Up) / L.KO;
-    c.seg = L.MT + t;
-    c.begin = L.Up + t * L.KO;
-    c.end = c.begin + L.KO;
-  }
+  c.seg = seg;
+  c.begin = seg < L.MT ? seg * L.KT : L.Up + (seg - L.MT) * L.KO;
+  c.end = c.begin + (seg < L.MT ? L.KT : L.KO);
   return c;
 }
 __device__ __forceinline__ int32_t chain_chunk(const ChainCursor& c, int32_t u1) {
@@ -270,8 +262,9 @@ struct ChainChunk {
   uint4 v;
   int ok;
 };
+template <bool sys>
 __device__ __noinline__ ChainChunk chain_poll_chunk(const uint32_t* xw, int64_t ldxw, int b, int k, int K,
-                                                    uint32_t tag, bool sys) {
+                                                    uint32_t tag) {
   const uint32_t* src = xw + b * ldxw + k;
   const uint4 a = ld_relaxed_v4(src, sys), d = ld_relaxed_v4(src + 4, sys);
   ChainChunk r;
@@ -315,7 +308,7 @@ constexpr int kChainSplitSlots = 32;  // packed tiles per CTA and layer (host-ch
 
 struct ChainShared {
   ChainLayer layer[2];                    // descriptors of layers j (slot j&1) and j+1
-  int4 part[2][2];                        // this CTA's share of layers j and j+1
+  int4 part[2][kChainSharePieces];        // this CTA's warp shares of layers j and j+1
   float amax[kQConsumers][kQMaxBatch];    // staging: per-warp max |x|
   unsigned long long tile_acc[kChainSplitSlots][kTileRows][kQMaxBatch];  // split packed tiles
   int32_t tile_cnt[kChainSplitSlots];
@@ -326,15 +319,15 @@ struct ChainShared {
 // Rows r0, r1 (local; -1 = none) with exponents e0, e1 and dot products t0, t1: exchange words
 // into every rank's copy (one relaxed store per word) and, unless a later layer overwrites it,
 // the fp16 output.  Scalars only, so nothing of the caller goes through local memory.
+template <bool sys>
 __device__ __noinline__ void chain_write_rows(const ChainLayer& L, int P, int B, int r0, int r1, int e0, int e1,
-                                              long long t0, long long t1, int q, int ex0, int ex1, uint32_t tag,
-                                              bool sys) {
+                                              long long t0, long long t1, int q, int ex0, int ex1, uint32_t tag) {
   const int b = q >> 1;
   if ((q & 1) || b >= B) return;
   const int ex = b ? ex1 : ex0;
   const __half h0 = scale_to_half(t0, e0 + ex), h1 = scale_to_half(t1, e1 + ex);
   const uint32_t w0 = (tag << 16) | __half_as_ushort(h0), w1 = (tag << 16) | __half_as_ushort(h1);
-  for (int p = 0; p < P; ++p) {
+  for (int p = 0; p < (sys ? P : 1); ++p) {
     unsigned int* wb = L.yw_peer[p] + b * L.ldyw;
     if (L.write_y) {
       __half* yb = L.y_peer[p] + b * L.ldy;
@@ -354,9 +347,10 @@ __device__ __noinline__ void chain_write_rows(const ChainLayer& L, int P, int B,
 // A warp's partial dot products of a packed tile (this CTA's local tile lt), shared with other
 // warps of the CTA: added exactly into the tile's shared int64 accumulators; the warp that
 // completes the count of contributors writes the tile's rows and clears the slot.
+template <bool sys>
 __device__ __noinline__ void chain_split_add(ChainShared* sh, const ChainLayer& L, int P, int B, int r0, int r1, int e0,
                                              int e1, long long t0, long long t1, int lt, int n_contrib, int lane,
-                                             int g, int q, int ex0, int ex1, uint32_t tag, bool sys) {
+                                             int g, int q, int ex0, int ex1, uint32_t tag) {
   const int slot = lt & (kChainSplitSlots - 1);
   const int b = q >> 1;
   const bool live = !(q & 1) && b < B;
@@ -377,15 +371,16 @@ __device__ __noinline__ void chain_split_add(ChainShared* sh, const ChainLayer& 
     f1 = static_cast<long long>(atomicExch(&sh->tile_acc[slot][g + 8][b], 0ull));
   }
   if (lane == 0) sh->tile_cnt[slot] = 0;
-  chain_write_rows(L, P, B, r0, r1, e0, e1, f0, f1, q, ex0, ex1, tag, sys);
+  chain_write_rows<sys>(L, P, B, r0, r1, e0, e1, f0, f1, q, ex0, ex1, tag);
 }
 
 // Outlier tile tt done for this warp: add its partials (rows r0, r1 = the slots' rows, -1 =
 // padding) into the slot accumulators and count it in (release); the warp completing the tile's
 // count (acquire) takes the sums, clears them and publishes the tile's rows.
+template <bool sys>
 __device__ __noinline__ void chain_flush_outlier(const ChainLayer& L, int P, int B, int r0, int r1, int e0, int e1,
                                                  long long t0, long long t1, int tt, int lane, int g, int q, int ex0,
-                                                 int ex1, uint32_t tag, bool sys) {
+                                                 int ex1, uint32_t tag) {
   const int b = q >> 1;
   const bool live = !(q & 1) && b < B;
   const int s0 = tt * kTileRows + g, s1 = s0 + 8;
@@ -409,29 +404,37 @@ __device__ __noinline__ void chain_flush_outlier(const ChainLayer& L, int P, int
     if (r1 >= 0) f1 = static_cast<long long>(atomicExch(L.acc + 2 * s1 + b, 0ull));
   }
   if (lane == 0) st_relaxed_u32(reinterpret_cast<unsigned int*>(L.ocnt + tt), 0u);
-  chain_write_rows(L, P, B, r0, r1, e0, e1, f0, f1, q, ex0, ex1, tag, sys);
+  chain_write_rows<sys>(L, P, B, r0, r1, e0, e1, f0, f1, q, ex0, ex1, tag);
 }
 
 // A finished segment of a warp's range (one call site in the kernel): outlier tiles count in,
 // packed tiles the warp covered whole are written, shared ones go through the CTA's reduction.
-// `lt` is the packed tile's index within the CTA's share; the contributor count is partq_of in
-// 32 bits over the share's np units and wp warps (products below 2^31, host-checked).
+// `sr` is the CTA's warp-share record of this layer (shared memory); the contributors of a split
+// tile are the packed warps whose ranges meet it.
+template <bool sys>
 __device__ __noinline__ void chain_finish_segment(ChainShared* sh, const ChainLayer& L, int P, int B, int r0, int r1,
                                                   int e0, int e1, long long t0, long long t1, int seg, int whole,
-                                                  int lt, int sb_rel, int np, int wp, int lane, int g, int q, int ex0,
-                                                  int ex1, uint32_t tag, bool sys) {
+                                                  const int32_t* sr, int lane, int g, int q, int ex0, int ex1,
+                                                  uint32_t tag) {
   if (seg >= L.MT) {
-    chain_flush_outlier(L, P, B, r0, r1, e0, e1, t0, t1, seg - L.MT, lane, g, q, ex0, ex1, tag, sys);
+    chain_flush_outlier<sys>(L, P, B, r0, r1, e0, e1, t0, t1, seg - L.MT, lane, g, q, ex0, ex1, tag);
   } else if (whole) {
-    chain_write_rows(L, P, B, r0, r1, e0, e1, t0, t1, q, ex0, ex1, tag, sys);
+    chain_write_rows<sys>(L, P, B, r0, r1, e0, e1, t0, t1, q, ex0, ex1, tag);
   } else {
-    const int32_t lo = sb_rel, hi = sb_rel + L.KT - 1;
-    const int n_contrib = ((hi + 1) * wp + np - 1) / np - ((lo + 1) * wp + np - 1) / np + 1;
-    chain_split_add(sh, L, P, B, r0, r1, e0, e1, t0, t1, lt, n_contrib, lane, g, q, ex0, ex1, tag, sys);
+    const int32_t tb = seg * L.KT, te = tb + L.KT;
+    const int wp = sr[kShWp];
+    int n_contrib = 0;
+    for (int w = 0; w < wp; ++w) {
+      const int32_t a = sr[kShU0 + w], b = sr[kShU1 + w];
+      n_contrib += (a < b && a < te && b > tb) ? 1 : 0;
+    }
+    chain_split_add<sys>(sh, L, P, B, r0, r1, e0, e1, t0, t1, seg - sr[kShTile0], n_contrib, lane, g, q, ex0, ex1, tag);
   }
 }
 
-template <int kXC>
+// kMulti: several ranks (system-scope stores into every rank's copies, cross-rank flags).  The
+// one-GPU instance compiles none of that, which keeps its code small.
+template <int kXC, bool kMulti>
 __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs args) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int warp = __shfl_sync(0xffffffffu, static_cast<int>(threadIdx.x >> 5), 0);
@@ -463,7 +466,8 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
   if (threadIdx.x < sizeof(ChainLayer) / 16 && args.n_layers > 0)
     reinterpret_cast<uint4*>(&sh->layer[0])[threadIdx.x] = reinterpret_cast<const uint4*>(args.layers)[threadIdx.x];
   __syncthreads();
-  if (threadIdx.x < 2 && args.n_layers > 0) sh->part[0][threadIdx.x] = args.parts[2 * blockIdx.x + threadIdx.x];
+  if (threadIdx.x < kChainSharePieces && args.n_layers > 0)
+    sh->part[0][threadIdx.x] = args.parts[kChainSharePieces * blockIdx.x + threadIdx.x];
   __syncthreads();
   if (sh->abort) return;  // poisoned: no work, no flags
 
@@ -478,11 +482,10 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     // raw fields of a layer (loads in flight until first used)
     struct Raw {
       uint64_t units, ounits;
-      uint32_t Up, MT, KT, KO;
-      int4 p0, p1;
+      uint32_t Up, MT, KT, KO, u0, u1, seg0;
     };
     auto fetch = [&](int jn, Raw& r) {
-      if (jn >= args.n_layers) return;
+      if (jn >= args.n_layers || i >= kQConsumers) return;
       const ChainLayer* Ln = args.layers + jn;
       r.units = ld_nc_u64(&Ln->units);
       r.ounits = ld_nc_u64(&Ln->ounits);
@@ -490,10 +493,10 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
       r.MT = ld_nc_u32(&Ln->MT);
       r.KT = ld_nc_u32(&Ln->KT);
       r.KO = ld_nc_u32(&Ln->KO);
-      const uint4* pe = reinterpret_cast<const uint4*>(args.parts + 2 * (static_cast<int64_t>(jn) * G + cta));
-      const uint4 a0 = ld_nc_v4(pe), a1 = ld_nc_v4(pe + 1);
-      r.p0 = make_int4(a0.x, a0.y, a0.z, a0.w);
-      r.p1 = make_int4(a1.x, a1.y, a1.z, a1.w);
+      const int32_t* sr = reinterpret_cast<const int32_t*>(args.parts + kChainSharePieces * (static_cast<int64_t>(jn) * G + cta));
+      r.u0 = ld_nc_u32(sr + kShU0 + i);
+      r.u1 = ld_nc_u32(sr + kShU1 + i);
+      r.seg0 = ld_nc_u32(sr + kShSeg0 + i);
     };
     // the current layer of this lane, in registers
     int j = 0;
@@ -512,25 +515,13 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
         MT = static_cast<int32_t>(nx.MT);
         KT = static_cast<int32_t>(nx.KT);
         KO = static_cast<int32_t>(nx.KO);
-        ChainPart p;
-        p.pu0 = nx.p0.x;
-        p.pu1 = nx.p0.y;
-        p.ou0 = nx.p0.z;
-        p.ou1 = nx.p0.w;
-        p.wp = nx.p1.x;
+        const int32_t u0 = static_cast<int32_t>(nx.u0);
+        u1 = static_cast<int32_t>(nx.u1);
+        seg = static_cast<int32_t>(nx.seg0);
         fetch(j + 1, nx);  // in flight while this layer streams
-        int32_t u0;
-        chain_warp_range(p, i, &u0, &u1);
         if (u0 < u1) {
           pu = u0;
-          if (u0 < Up) {
-            seg = u0 / KT;
-            send = (seg + 1) * KT;
-          } else {
-            const int32_t t = (u0 - Up) / KO;
-            seg = MT + t;
-            send = Up + (t + 1) * KO;
-          }
+          send = seg < MT ? (seg + 1) * KT : Up + (seg - MT + 1) * KO;
           return true;
         }
         ++j;
@@ -539,14 +530,12 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     };
     bool active = i < kQConsumers;
     if (active) active = next_range();
-    int32_t c = 0;
+    int slot = 0, round = 0;  // ring slot and round of this lane's next chunk
     uint64_t t_idle = 0;
     bool failed = false;
     while (__any_sync(0xffffffffu, active)) {
       bool issued = false;
       if (active) {
-        const int slot = c % S;
-        const int round = c / S;
         if (round == 0 || mbar_test(empty_base + (i * S + slot) * 8, static_cast<uint32_t>((round - 1) & 1))) {
           int32_t cnt = send - pu;
           if (u1 - pu < cnt) cnt = u1 - pu;
@@ -564,7 +553,10 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
             ++seg;
             send += seg < MT ? KT : KO;
           }
-          ++c;
+          if (++slot == S) {
+            slot = 0;
+            ++round;
+          }
           issued = true;
           if (pu >= u1) {
             ++j;
@@ -589,9 +581,9 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     // Copies that consumers which gave up never waited for land before the CTA exits: wait
     // (bounded) for the last chunk issued into each ring slot.
     if (i < kQConsumers) {
-      for (int s = 0; s < S && s < c; ++s) {
-        const int32_t last = s + S * ((c - 1 - s) / S);
-        mbar_wait_bounded(full_base + (i * S + s) * 8, static_cast<uint32_t>((last / S) & 1));
+      for (int s = 0; s < S; ++s) {
+        const int n_in_slot = round + (s < slot ? 1 : 0);  // chunks issued into slot s
+        if (n_in_slot > 0) mbar_wait_bounded(full_base + (i * S + s) * 8, static_cast<uint32_t>((n_in_slot - 1) & 1));
       }
     }
     return;
@@ -603,8 +595,8 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
   const uint32_t negz = args.negz;
   const uint32_t ring = ring_base + warp * S * kQChunkBytes + lane * 16;
   const uint32_t fullw = full_base + warp * S * 8, emptyw = empty_base + warp * S * 8;
-  const int P = args.world;
-  const bool sys = P > 1;
+  const int P = kMulti ? args.world : 1;
+  constexpr bool sys = kMulti;
   const int n_flags = P * G;
   const uint32_t epoch = sh->epoch;
   const uint32_t f_staged0 = 2u * epoch + 1u;  // flag: this CTA staged layer 0
@@ -649,10 +641,9 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     qa.cbq = L.cbq; qa.tile_mask = L.tile_mask; qa.orow = L.orow; qa.oexp = L.oexp; qa.M = L.M; qa.MT = L.MT;
     unsigned long long* tr = args.trace ? args.trace + (static_cast<int64_t>(j) * G + cta) * kChainTracePhases : nullptr;
     if (tr && tid == 0) tr[0] = globaltimer_ns();
-    const ChainPart part = chain_part_load(sh->part[j & 1]);
-    int32_t u0, u1;
-    chain_warp_range(part, warp, &u0, &u1);
-    ChainCursor cc = chain_cursor(L, u0 < u1 ? u0 : 0);
+    const int32_t* sr = reinterpret_cast<const int32_t*>(sh->part[j & 1]);
+    const int32_t u0 = sr[kShU0 + warp], u1 = sr[kShU1 + warp];
+    ChainCursor cc = chain_cursor_at(L, u0, sr[kShSeg0 + warp]);
     MetaQ cur, nxt;
     if (u0 < u1) {  // both loads issued here, first used in the units loop (no select on them)
       cur = load_metaq(qa, cc.seg, g);
@@ -664,13 +655,13 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     // (the last consumer warp: with more chunks than threads, the first warps stage more of x)
     constexpr int kDescPieces = static_cast<int>(sizeof(ChainLayer) / 16);
     const int dt = tid - (kQConsumerThreads - 32);
-    const bool copy_desc = j + 1 < args.n_layers && dt >= 0 && dt < kDescPieces + 2;
+    const bool copy_desc = j + 1 < args.n_layers && dt >= 0 && dt < kDescPieces + kChainSharePieces;
     uint4 desc_piece = make_uint4(0, 0, 0, 0);
     if (copy_desc) {
       if (dt < kDescPieces) {
         desc_piece = ld_nc_v4(reinterpret_cast<const uint4*>(args.layers + j + 1) + dt);
       } else {
-        const int4* pe = args.parts + 2 * (static_cast<int64_t>(j + 1) * G + cta) + (dt - kDescPieces);
+        const int4* pe = args.parts + kChainSharePieces * (static_cast<int64_t>(j + 1) * G + cta) + (dt - kDescPieces);
         desc_piece = ld_nc_v4(reinterpret_cast<const uint4*>(pe));
       }
     }
@@ -680,6 +671,7 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     // exchange words of their chunks until every tag is this launch's (bounded).
     int ex0 = 0, ex1 = 0;  // x exponents of batch rows 0, 1 (scalars: no local memory)
     {
+      static_assert(kQMaxBatch == 2, "chunk c of batch row c >= per_row: no division");
       const int per_row = L.K_pad / 8;
       const int total = B * per_row;
       uint4 v[kXC];
@@ -688,14 +680,14 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
       for (int i = 0; i < kXC; ++i) {
         const int c = tid + i * kQConsumerThreads;
         v[i] = make_uint4(0, 0, 0, 0);
-        if (c < total && (c - (c / per_row) * per_row) * 8 < L.K) pending |= 1u << i;
+        if (c < total && (c - (c >= per_row ? per_row : 0)) * 8 < L.K) pending |= 1u << i;
       }
       if (j == 0) {
 #pragma unroll
         for (int i = 0; i < kXC; ++i) {
           if (pending & (1u << i)) {
             const int c = tid + i * kQConsumerThreads;
-            const int b = c / per_row, k = (c - b * per_row) * 8;
+            const int b = c >= per_row ? 1 : 0, k = (c - b * per_row) * 8;  // c < 2 per_row (batch <= 2)
             v[i] = chain_load_x0(L.x, L.ldx, b, k, L.K, L.x_vec16);
           }
         }
@@ -710,8 +702,8 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
         for (int i = 0; i < kXC; ++i) {
           if (pending & (1u << i)) {
             const int c = tid + i * kQConsumerThreads;
-            const int b = c / per_row, k = (c - b * per_row) * 8;
-            const ChainChunk r = chain_poll_chunk(L.xw, L.ldxw, b, k, L.K, tag_in, sys);
+            const int b = c >= per_row ? 1 : 0, k = (c - b * per_row) * 8;
+            const ChainChunk r = chain_poll_chunk<sys>(L.xw, L.ldxw, b, k, L.K, tag_in);
             if (r.ok) {
               v[i] = r.v;
               pending &= ~(1u << i);
@@ -773,7 +765,7 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
       for (int i = 0; i < kXC; ++i) {
         const int c = tid + i * kQConsumerThreads;
         if (c < total) {
-          const int b = c / per_row, k = (c - b * per_row) * 8;
+          const int b = c >= per_row ? 1 : 0, k = (c - b * per_row) * 8;
           chain_store_digits(v[i], pow2f(b == 0 ? ex0 : ex1), xs_base + 3 * b * colb, colb,
                              static_cast<uint32_t>((k >> 7) * 128 + xs_pos8(k & 127)));
         }
@@ -804,7 +796,6 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     const uint32_t kts = live_col ? 128u : 0u;
     const uint32_t xq = colbase + 32 * q, xo = colbase + 4 * q;
 
-    const int32_t tile0 = part.pu0 / (L.KT > 0 ? L.KT : 1);  // this CTA's first packed tile
     if (u0 < u1) {
       AccQ A;
       zero_accq(A);
@@ -857,9 +848,8 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
         if (cc.u == cc.end || cc.u == u1) {  // a segment of the range is complete (one call site)
           long long t[2];
           finish_dot(A, q, t);
-          chain_finish_segment(sh, L, P, B, cur.row[0], cur.row[1], cur.e[0], cur.e[1], t[0], t[1], cc.seg,
-                               cc.begin >= u0 && cc.end <= u1, cc.seg - tile0, cc.begin - part.pu0,
-                               part.pu1 - part.pu0, part.wp, lane, g, q, ex0, ex1, tag, sys);
+          chain_finish_segment<sys>(sh, L, P, B, cur.row[0], cur.row[1], cur.e[0], cur.e[1], t[0], t[1], cc.seg,
+                               cc.begin >= u0 && cc.end <= u1, sr, lane, g, q, ex0, ex1, tag);
           if (cc.u == u1) break;
           zero_accq(A);
           chain_next_segment(L, cc);

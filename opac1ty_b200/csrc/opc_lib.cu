@@ -868,7 +868,7 @@ struct opc_chain {
   size_t smem = 0;
   void* dev_mem = nullptr;              // [layers | onc | parts | epoch | acc | ocnt (| flags | words)]
   opc::ChainLayer* d_layers = nullptr;
-  const int4* d_parts = nullptr;        // [layers][grid][2] CTA shares
+  const int4* d_parts = nullptr;        // [layers][grid][kChainSharePieces] warp-share records
   unsigned int* d_sync = nullptr;       // this rank's flags [world][grid]
   unsigned int* sync_peer[opc::kMaxRanks] = {};
   unsigned int* d_epoch = nullptr;      // [2]
@@ -1010,7 +1010,9 @@ int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t 
   if (stages < 2) return fail(OPC_ERR_UNSUPPORTED, "%s: staged x too large for shared memory", fn);
   const size_t smem = smem_for(stages);
   const int xc = bk_max <= 4 * 8 * opc::kQConsumerThreads ? 4 : 8;
-  auto kern = xc == 4 ? opc::chain_kernel<4> : opc::chain_kernel<8>;
+  const bool multi = world > 1;
+  auto kern = xc == 4 ? (multi ? opc::chain_kernel<4, true> : opc::chain_kernel<4, false>)
+                      : (multi ? opc::chain_kernel<8, true> : opc::chain_kernel<8, false>);
   OPC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)),
            "cudaFuncSetAttribute(max dynamic smem, chain)");
   int per_sm = 0;
@@ -1025,7 +1027,7 @@ int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t 
   const size_t layers_bytes = align_up(sizeof(opc::ChainLayer) * n, 256);
   size_t off = layers_bytes;
   std::vector<size_t> onc_off(n), acc_off(n), ocnt_off(n), yw_off(n);
-  std::vector<int32_t> parts(8 * static_cast<size_t>(G) * n, 0);  // [n][G][2] int4
+  std::vector<int32_t> parts(opc::kChainShareInts * static_cast<size_t>(G) * n, 0);  // [n][G] warp-share records
   for (int j = 0; j < n; ++j) {
     const opc_layer_plan& p = steps[j].layer->plan;
     opc::ChainLayer& c = hl[j];
@@ -1040,15 +1042,20 @@ int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t 
     onc[j] = outlier_contributors(c, cparts);
     onc_off[j] = off;
     off += align_up(std::max<size_t>(onc[j].size(), 1) * sizeof(int32_t), 256);
-    // each CTA's share, so the kernel does no partition arithmetic: {pu0, pu1, ou0, ou1}, {wp, 0, 0, 0}
+    // each CTA's warp shares, so the kernel does no partition arithmetic (and no division):
+    // per warp its unit range and first segment, plus the packed warps and first packed tile
     for (int cta = 0; cta < G; ++cta) {
       const opc::ChainPart& pt = cparts[cta];
-      int32_t* e = parts.data() + 8 * (static_cast<size_t>(j) * G + cta);
-      e[0] = pt.pu0;
-      e[1] = pt.pu1;
-      e[2] = pt.ou0;
-      e[3] = pt.ou1;
-      e[4] = pt.wp;
+      int32_t* e = parts.data() + opc::kChainShareInts * (static_cast<size_t>(j) * G + cta);
+      for (int w = 0; w < opc::kQConsumers; ++w) {
+        int32_t u0 = 0, u1 = 0;
+        opc::chain_warp_range(pt, w, &u0, &u1);
+        e[opc::kShU0 + w] = u0;
+        e[opc::kShU1 + w] = u1;
+        e[opc::kShSeg0 + w] = u0 >= u1 ? 0 : (u0 < c.Up ? u0 / c.KT : c.MT + (u0 - c.Up) / c.KO);
+      }
+      e[opc::kShWp] = pt.wp;
+      e[opc::kShTile0] = c.KT > 0 ? pt.pu0 / c.KT : 0;
     }
   }
   const size_t parts_off = off;
@@ -1370,10 +1377,13 @@ int opc_chain_launch(opc_chain* ch, void* stream_v) {
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  const bool multi = a.world > 1;
   if (ch->xc == 4) {
-    OPC_CUDA(cudaLaunchKernelEx(&cfg, opc::chain_kernel<4>, a), "launch chain_kernel");
+    if (multi) OPC_CUDA(cudaLaunchKernelEx(&cfg, opc::chain_kernel<4, true>, a), "launch chain_kernel");
+    else OPC_CUDA(cudaLaunchKernelEx(&cfg, opc::chain_kernel<4, false>, a), "launch chain_kernel");
   } else {
-    OPC_CUDA(cudaLaunchKernelEx(&cfg, opc::chain_kernel<8>, a), "launch chain_kernel");
+    if (multi) OPC_CUDA(cudaLaunchKernelEx(&cfg, opc::chain_kernel<8, true>, a), "launch chain_kernel");
+    else OPC_CUDA(cudaLaunchKernelEx(&cfg, opc::chain_kernel<8, false>, a), "launch chain_kernel");
   }
   return OPC_OK;
 }
