@@ -257,6 +257,15 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
+// Arrival count with acquire-release semantics at GPU scope: releases the caller's (and, through
+// a preceding __syncwarp, its warp's) earlier writes and acquires those released by earlier
+// arrivals -- one atomic instead of a fence on each side of a relaxed one.
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int32_t* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
 // Every wait in this library is bounded: after kWaitLimitNs the caller records an error in
 // the device error word and gives up instead of spinning forever.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s

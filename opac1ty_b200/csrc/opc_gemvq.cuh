@@ -252,15 +252,14 @@ __device__ void reduce_segmentq(const GemvQArgs& a, SmemSlotsQ* ss, SegQ S, int3
     for (int r = 0; r < 2; ++r)
       if (m.row[r] >= 0) atomicAdd(a.acc + static_cast<int64_t>(m.row[r]) * 2 + b, static_cast<unsigned long long>(tot[r]));
   }
-  __threadfence();
-  __syncwarp();
+  __syncwarp();  // the lanes' adds are ordered before lane 0's arrival
   const int G = static_cast<int>(gridDim.x);
   const int ca = partq_of(S.begin, a.U, G), cb = partq_of(S.end - 1, a.U, G);
   int old = 0;
-  if (lane == 0) old = atomicAdd(a.counters + S.id, 1);
+  if (lane == 0) old = atom_add_acq_rel_gpu(a.counters + S.id, 1);  // release ours, acquire earlier ones
   old = __shfl_sync(0xffffffffu, old, 0);
+  __syncwarp();
   if (old != cb - ca) return;
-  __threadfence();
   if (live) {
     long long fin[2] = {0, 0};
 #pragma unroll
