@@ -2,9 +2,9 @@
 
 A chain is a fixed list of dependent GEMV steps (layer, x, y) whose step j >= 1 reads a prefix of
 step j-1's output.  ``opc_chain_launch`` runs all of them in one cooperative kernel: a producer
-warp per SM streams the weights of every step without waiting for activations, and a grid
-barrier separates dependent steps.  Results equal per-step ``opac1ty_b200.gemv`` calls bit for
-bit (batch 1..2).
+warp per SM streams the weights of every step without waiting for activations, and each step's
+outputs are published as tagged 32-bit words that the next step's readers poll (no grid barrier
+between steps).  Results equal per-step ``opac1ty_b200.gemv`` calls bit for bit (batch 1..2).
 """
 
 from __future__ import annotations
