@@ -286,14 +286,12 @@ __device__ __noinline__ uint4 chain_load_x0(const __half* x, int64_t ldx, int b,
 
 // max |x| over a chunk's eight fp16 values
 __device__ __forceinline__ float chain_chunk_amax(const uint4& v) {
-  const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
-  float m = 0.f;
-#pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    const __half hv = __ushort_as_half(static_cast<unsigned short>((wv[e >> 1] >> (16 * (e & 1))) & 0xffffu));
-    m = fmaxf(m, fabsf(__half2float(hv)));
-  }
-  return m;
+  // |x| by clearing the sign bits, maxima of half2 pairs (exact, NaN ignored like fmaxf), one
+  // conversion at the end
+  const uint32_t w[4] = {v.x & 0x7fff7fffu, v.y & 0x7fff7fffu, v.z & 0x7fff7fffu, v.w & 0x7fff7fffu};
+  const __half2* h = reinterpret_cast<const __half2*>(w);
+  const __half2 m = __hmax2(__hmax2(h[0], h[1]), __hmax2(h[2], h[3]));
+  return fmaxf(__low2float(m), __high2float(m));
 }
 
 // A chunk's eight values as offset integers x*2^ex + 2^22 (x_digits_q), stored at their staged
