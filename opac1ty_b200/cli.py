@@ -209,7 +209,8 @@ def layer_bench(shape, outliers, batch, iters, svs):
 @click.option("--batch", type=int, default=1)
 @click.option("--iters", type=int, default=20)
 @click.option("--launches", is_flag=True, help="one GEMV launch per projection instead of the chain kernel")
-def decode_bench(model, blocks, batch, iters, launches):
+@click.option("--trace", is_flag=True, help="also report the chain kernel's per-phase timeline (opc_chain_set_trace)")
+def decode_bench(model, blocks, batch, iters, launches, trace):
     """Time the decode step (q|k|v, o, gate|up, down per block) of synthetic 2-bit weights."""
     import torch
 
@@ -231,9 +232,44 @@ def decode_bench(model, blocks, batch, iters, launches):
     torch.cuda.synchronize(dev)
     ms = e0.elapsed_time(e1) / iters
     nb = st.algorithmic_bytes()
-    click.echo(json.dumps({"gpu": get_cuda_device_info().name, "model": model, "blocks": len(st.blocks),
-                           "batch": batch, "chain": st.chain is not None, "ms_per_step": ms,
-                           "tok_s": batch * 1000.0 / ms, "gbs": nb / (ms * 1e-3) / 1e9}))
+    out = {"gpu": get_cuda_device_info().name, "model": model, "blocks": len(st.blocks), "batch": batch,
+           "chain": st.chain is not None, "ms_per_step": ms, "tok_s": batch * 1000.0 / ms,
+           "gbs": nb / (ms * 1e-3) / 1e9}
+    if trace and st.chain is not None:
+        out["phases_us"] = _chain_phases(st)
+    click.echo(json.dumps(out))
+
+
+def _chain_phases(st) -> dict:
+    """Per projection of a block: median over CTAs (mean over the inner blocks) of the time between
+    consecutive trace stamps of the chain kernel's first consumer thread -- setup, wait before the
+    first poll, x polling, max barrier, digits, staged barrier, own units -- and the GEMV's span
+    (start to the next GEMV's start)."""
+    import numpy as np
+    import torch
+
+    tr = st.chain.enable_trace()
+    for _ in range(3):
+        st.step_eager()
+    torch.cuda.synchronize(st.device)
+    t = tr.cpu().numpy().astype(np.int64)  # [steps, grid, 8] ns
+    st.chain.disable_trace()
+    names = ["qkv", "o", "gate_up", "down"]
+    n_blocks = t.shape[0] // 4
+    inner = range(1, n_blocks - 1) if n_blocks > 2 else range(n_blocks)
+    starts = np.median(t[:, :, 0], axis=1)
+    res = {}
+    for p, name in enumerate(names):
+        rows = [4 * b + p for b in inner]
+        d = np.diff(t[rows], axis=2) / 1000.0
+        med = np.median(d, axis=1).mean(axis=0)
+        spans = [(starts[r + 1] - starts[r]) / 1000.0 for r in rows if r + 1 < t.shape[0]]
+        res[name] = {"setup": round(float(med[0]), 2), "pre_poll": round(float(med[1]), 2),
+                     "x_wait": round(float(med[2]), 2), "max_barrier": round(float(med[3]), 2),
+                     "digits": round(float(med[4]), 2), "staged": round(float(med[5]), 2),
+                     "units": round(float(med[6]), 2),
+                     "span": round(float(np.mean(spans)), 2) if spans else None}
+    return res
 
 
 @cli.command("gemm-bench")
