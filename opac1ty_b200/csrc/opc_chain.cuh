@@ -307,7 +307,7 @@ constexpr int kChainSplitSlots = 32;  // packed tiles per CTA and layer (host-ch
 struct ChainShared {
   ChainLayer layer[2];                    // descriptors of layers j (slot j&1) and j+1
   int4 part[2][kChainSharePieces];        // this CTA's warp shares of layers j and j+1
-  float amax[kQConsumers][kQMaxBatch];    // staging: per-warp max |x|
+  uint32_t amax_bits[2][kQMaxBatch];      // staging: max |x| (float bits) of layers with parity 0 / 1
   unsigned long long tile_acc[kChainSplitSlots][kTileRows][kQMaxBatch];  // split packed tiles
   int32_t tile_cnt[kChainSplitSlots];
   int32_t abort;
@@ -460,6 +460,7 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
   for (int i = threadIdx.x; i < kChainSplitSlots * kTileRows * kQMaxBatch; i += blockDim.x)
     (&sh->tile_acc[0][0][0])[i] = 0ull;
   for (int i = threadIdx.x; i < kChainSplitSlots; i += blockDim.x) sh->tile_cnt[i] = 0;
+  if (threadIdx.x < 2 * kQMaxBatch) (&sh->amax_bits[0][0])[threadIdx.x] = 0u;
   if (threadIdx.x < sizeof(ChainLayer) / 16 && args.n_layers > 0)
     reinterpret_cast<uint4*>(&sh->layer[0])[threadIdx.x] = reinterpret_cast<const uint4*>(args.layers)[threadIdx.x];
   __syncthreads();
@@ -727,12 +728,12 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
           else mx[1] = fmaxf(mx[1], m);
         }
       }
+      // non-negative floats order like their bit patterns: one warp max and one shared-memory
+      // atomic per warp and batch row (a NaN maximum counts as 0, as fmaxf would skip it)
 #pragma unroll
-      for (int b = 0; b < kQMaxBatch; ++b)
-        for (int o = 16; o > 0; o >>= 1) mx[b] = fmaxf(mx[b], __shfl_xor_sync(0xffffffffu, mx[b], o));
-      if (lane == 0) {
-        sh->amax[warp][0] = mx[0];
-        sh->amax[warp][1] = mx[1];
+      for (int b = 0; b < kQMaxBatch; ++b) {
+        const uint32_t m = __reduce_max_sync(0xffffffffu, mx[b] == mx[b] ? __float_as_uint(mx[b]) : 0u);
+        if (lane == 0) atomicMax(&sh->amax_bits[j & 1][b], m);
       }
       if (tid < 16)  // ones block, zero block (B operands of the ones and absent columns)
         sts128(xs_base + args.xs_bytes - kQZeroBytes - kQOnesBytes + tid * 16,
@@ -749,13 +750,12 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
       }
       if (j == 0) publish(f_staged0);  // layer-0 input read by every thread of this CTA
       {
-        float m0 = 0.f, m1 = 0.f;
-        for (int w = 0; w < kQConsumers; ++w) {
-          m0 = fmaxf(m0, sh->amax[w][0]);
-          m1 = fmaxf(m1, sh->amax[w][1]);
-        }
+        const float m0 = __uint_as_float(sh->amax_bits[j & 1][0]), m1 = __uint_as_float(sh->amax_bits[j & 1][1]);
         ex0 = m0 > 0.f ? 22 - frexp_exponent(m0) : 0;
         ex1 = m1 > 0.f ? 22 - frexp_exponent(m1) : 0;
+        // the other parity's maxima start layer j+1 at zero: their last readers (layer j-1) are
+        // past this barrier, their next writers (layer j+1) behind the staged barrier below
+        if (tid < kQMaxBatch) sh->amax_bits[(j + 1) & 1][tid] = 0u;
       }
       const uint32_t colb = static_cast<uint32_t>(xsq_col_bytes(L.KT));
 #pragma unroll
