@@ -151,6 +151,30 @@ __host__ __device__ __forceinline__ void chain_warp_range(const ChainPart& p, in
   }
 }
 
+// A segment's metadata for lane group g, loaded without using any loaded value: for a packed tile
+// row[0] is the base row and row[1] the raw tile mask (the output rows are resolved when the tile
+// is finished, so no instruction waits on these loads until then); for an outlier tile the rows
+// and exponents of its slots.
+__device__ __forceinline__ MetaQ chain_load_meta(const GemvQArgs& a, int32_t seg, int g) {
+  MetaQ m;
+  if (seg < a.MT) {
+    const int r0 = seg * kTileRows + g;
+    const uint4 c0 = ld_nc_v4(a.cbq + r0), c1 = ld_nc_v4(a.cbq + r0 + 8);
+    m.qh[0] = c0.x; m.ql[0] = c0.y; m.e[0] = static_cast<int32_t>(c0.z);
+    m.qh[1] = c1.x; m.ql[1] = c1.y; m.e[1] = static_cast<int32_t>(c1.z);
+    m.row[0] = r0;
+    m.row[1] = static_cast<int32_t>(ld_nc_u16(a.tile_mask + seg));
+  } else {
+    const int s = (seg - a.MT) * kTileRows + g;
+    m.qh[0] = m.qh[1] = m.ql[0] = m.ql[1] = 0u;
+    m.row[0] = static_cast<int32_t>(ld_nc_u32(a.orow + s));
+    m.row[1] = static_cast<int32_t>(ld_nc_u32(a.orow + s + 8));
+    m.e[0] = static_cast<int32_t>(ld_nc_u32(a.oexp + s));
+    m.e[1] = static_cast<int32_t>(ld_nc_u32(a.oexp + s + 8));
+  }
+  return m;
+}
+
 // Unit cursor over a layer (segments: packed tiles of KT units, outlier tiles of KO units).
 struct ChainCursor {
   int32_t u, seg, begin, end;
@@ -644,8 +668,8 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     ChainCursor cc = chain_cursor_at(L, u0, sr[kShSeg0 + warp]);
     MetaQ cur, nxt;
     if (u0 < u1) {  // both loads issued here, first used in the units loop (no select on them)
-      cur = load_metaq(qa, cc.seg, g);
-      nxt = load_metaq(qa, min(cc.seg + 1, L.MT + L.OT - 1), g);
+      cur = chain_load_meta(qa, cc.seg, g);
+      nxt = chain_load_meta(qa, min(cc.seg + 1, L.MT + L.OT - 1), g);
     }
     // next layer's descriptor and this CTA's share of it: loaded now, stored to shared memory
     // once every warp is past this layer's first staging barrier (nobody reads the slots' old
@@ -845,13 +869,19 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
         if (cc.u == cc.end || cc.u == u1) {  // a segment of the range is complete (one call site)
           long long t[2];
           finish_dot(A, q, t);
-          chain_finish_segment<sys>(sh, L, P, B, cur.row[0], cur.row[1], cur.e[0], cur.e[1], t[0], t[1], cc.seg,
-                               cc.begin >= u0 && cc.end <= u1, sr, lane, g, q, ex0, ex1, tag);
+          int r0 = cur.row[0], r1 = cur.row[1];
+          if (cc.seg < L.MT) {  // packed tile: base row and raw mask -> output rows (-1: masked or past M)
+            const uint32_t mask = static_cast<uint32_t>(r1);
+            r1 = (r0 + 8 < L.M && !((mask >> (g + 8)) & 1u)) ? r0 + 8 : -1;
+            r0 = (r0 < L.M && !((mask >> g) & 1u)) ? r0 : -1;
+          }
+          chain_finish_segment<sys>(sh, L, P, B, r0, r1, cur.e[0], cur.e[1], t[0], t[1], cc.seg,
+                                    cc.begin >= u0 && cc.end <= u1, sr, lane, g, q, ex0, ex1, tag);
           if (cc.u == u1) break;
           zero_accq(A);
           chain_next_segment(L, cc);
           cur = nxt;
-          if (cc.seg + 1 < L.MT + L.OT) nxt = load_metaq(qa, cc.seg + 1, g);
+          if (cc.seg + 1 < L.MT + L.OT) nxt = chain_load_meta(qa, cc.seg + 1, g);
         }
       }
       if (!ok) {

@@ -204,7 +204,7 @@ struct SmemSlotsQ {
   long long v[kQConsumers][2][32][2];  // per warp: first/last segment, per lane rows g/g+8
   int32_t seg[kQConsumers][2];
   int32_t ex[kQMaxBatch];              // x exponents
-  float amax[kQConsumers][kQMaxBatch]; // staging reduction
+  uint32_t amax_bits[kQMaxBatch];      // staging: max |x| (float bits) per batch row
 };
 
 // x exponents of batch rows 0 and 1 are passed as scalars (no array, so no local memory).
@@ -294,6 +294,7 @@ __global__ void __launch_bounds__(kQThreads, 1) gemvq_kernel(const GemvQArgs a) 
     fence_mbar_init();
   }
   if (threadIdx.x < kQConsumers * 2) ss->seg[threadIdx.x >> 1][threadIdx.x & 1] = -1;
+  if (threadIdx.x < kQMaxBatch) ss->amax_bits[threadIdx.x] = 0u;
   __syncthreads();
   griddep_launch_dependents();
 
@@ -401,23 +402,19 @@ __global__ void __launch_bounds__(kQThreads, 1) gemvq_kernel(const GemvQArgs a) 
         }
       }
     }
+    // non-negative floats order like their bit patterns: one warp max and one shared-memory
+    // atomic per warp and batch row (a NaN maximum counts as 0, as fmaxf would skip it)
 #pragma unroll
-    for (int b = 0; b < kQMaxBatch; ++b)
-      for (int o = 16; o > 0; o >>= 1) mx[b] = fmaxf(mx[b], __shfl_xor_sync(0xffffffffu, mx[b], o));
-    if (lane == 0) {
-      ss->amax[warp][0] = mx[0];
-      ss->amax[warp][1] = mx[1];
+    for (int b = 0; b < kQMaxBatch; ++b) {
+      const uint32_t m = __reduce_max_sync(0xffffffffu, mx[b] == mx[b] ? __float_as_uint(mx[b]) : 0u);
+      if (lane == 0) atomicMax(&ss->amax_bits[b], m);
     }
     if (tid < 16)  // ones block, zero block (B operands of the ones and absent columns)
       sts128(xs_base + a.xs_bytes - kQZeroBytes - kQOnesBytes + tid * 16,
              tid < 8 ? make_uint4(0x01010101u, 0x01010101u, 0x01010101u, 0x01010101u) : make_uint4(0, 0, 0, 0));
     named_barrier(1, kQConsumerThreads);
     // max |x| * 2^e in [2^21, 2^22): offset digits d0 in [0, 128], d1, d2 in [0, 255]
-    float m0 = 0.f, m1 = 0.f;
-    for (int w = 0; w < kQConsumers; ++w) {
-      m0 = fmaxf(m0, ss->amax[w][0]);
-      m1 = fmaxf(m1, ss->amax[w][1]);
-    }
+    const float m0 = __uint_as_float(ss->amax_bits[0]), m1 = __uint_as_float(ss->amax_bits[1]);
     const int ex0 = m0 > 0.f ? 22 - frexp_exponent(m0) : 0;
     const int ex1 = m1 > 0.f ? 22 - frexp_exponent(m1) : 0;
     if (tid == 0) {
