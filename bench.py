@@ -45,10 +45,10 @@ import numpy as np  # noqa: E402
 
 METRIC = "fused 2-bit VQ GEMV HBM TB/s (% peak); decode tok/s @ Llama-3.1-8B shapes"
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one chain-kernel launch over its
-# algorithmic bytes, from an ncu capture of the 4-block step (mean of two launches: 244.3 and
-# 241.1 MB for 237.3 MB); the traffic is
+# algorithmic bytes, from an ncu capture of the 4-block step (mean of two launches: 243.9 and
+# 240.8 MB for 237.3 MB); the traffic is
 # proportional to the blocks, so the full step's traffic is this ratio times its algorithmic bytes.
-CHAIN_TRAFFIC_RATIO = 1.023
+CHAIN_TRAFFIC_RATIO = 1.021
 WORKLOAD = "Llama-3.1-8B decode GEMV set, batch 1, 32 blocks (q|k|v, o, gate|up, down), 2-bit svs=1, 1% outlier rows"
 
 
