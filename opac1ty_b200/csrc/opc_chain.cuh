@@ -320,7 +320,7 @@ __device__ __forceinline__ float chain_chunk_amax(const uint4& v) {
 
 // A chunk's eight values as offset integers x*2^ex + 2^22 (x_digits_q), stored at their staged
 // positions in the three unsigned digit columns of batch row b.
-__device__ __noinline__ void chain_store_digits(const uint4 v, float sc, uint32_t col0, uint32_t colb, uint32_t pos) {
+__device__ __forceinline__ void chain_store_digits(const uint4 v, float sc, uint32_t col0, uint32_t colb, uint32_t pos) {
   const XDigitsQ d = x_digits_q(v, sc);
 #pragma unroll
   for (int dd = 0; dd < 3; ++dd) sts64(col0 + dd * colb + pos, d.d[dd][0], d.d[dd][1]);
