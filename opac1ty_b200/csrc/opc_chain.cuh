@@ -262,8 +262,10 @@ __device__ __forceinline__ float pow2f(int e) { return __int_as_float((127 + e) 
 // Code size matters here: the kernel's once-per-layer paths (staging, tails, the producer) run
 // while the weight stream saturates the memory system, and their code is fetched again for every
 // layer (running the x-conversion pass twice in a row measured 2.0 us for the first pass and
-// 0.54 us for the second), so they are kept small -- per-chunk work is an out-of-line function
-// called per chunk, not unrolled copies.
+// 0.54 us for the second), so they are kept small.  What measured smaller and faster: helpers
+// with one call site inlined (digit stores, segment finishing), the polling and the row writes
+// (several call sites) out of line, and loops over chunks calling them rather than unrolled
+// copies of their bodies.
 
 // Eight exchange words of k..k+7 (the first n_valid inside the row): do all carry `tag`?  Then
 // their fp16 values, packed in pairs, go to v.
@@ -370,7 +372,7 @@ __device__ __noinline__ void chain_write_rows(const ChainLayer& L, int P, int B,
 // warps of the CTA: added exactly into the tile's shared int64 accumulators; the warp that
 // completes the count of contributors writes the tile's rows and clears the slot.
 template <bool sys>
-__device__ __noinline__ void chain_split_add(ChainShared* sh, const ChainLayer& L, int P, int B, int r0, int r1, int e0,
+__device__ __forceinline__ void chain_split_add(ChainShared* sh, const ChainLayer& L, int P, int B, int r0, int r1, int e0,
                                              int e1, long long t0, long long t1, int lt, int n_contrib, int lane,
                                              int g, int q, int ex0, int ex1, uint32_t tag) {
   const int slot = lt & (kChainSplitSlots - 1);
@@ -400,7 +402,7 @@ __device__ __noinline__ void chain_split_add(ChainShared* sh, const ChainLayer& 
 // padding) into the slot accumulators and count it in (release); the warp completing the tile's
 // count (acquire) takes the sums, clears them and publishes the tile's rows.
 template <bool sys>
-__device__ __noinline__ void chain_flush_outlier(const ChainLayer& L, int P, int B, int r0, int r1, int e0, int e1,
+__device__ __forceinline__ void chain_flush_outlier(const ChainLayer& L, int P, int B, int r0, int r1, int e0, int e1,
                                                  long long t0, long long t1, int tt, int lane, int g, int q, int ex0,
                                                  int ex1, uint32_t tag) {
   const int b = q >> 1;
@@ -433,7 +435,7 @@ __device__ __noinline__ void chain_flush_outlier(const ChainLayer& L, int P, int
 // `sr` is the CTA's warp-share record of this layer (shared memory); the contributors of a split
 // tile are the packed warps whose ranges meet it.
 template <bool sys>
-__device__ __noinline__ void chain_finish_segment(ChainShared* sh, const ChainLayer& L, int P, int B, int r0, int r1,
+__device__ __forceinline__ void chain_finish_segment(ChainShared* sh, const ChainLayer& L, int P, int B, int r0, int r1,
                                                   int e0, int e1, long long t0, long long t1, int seg, int whole,
                                                   const int32_t* sr, int lane, int g, int q, int ex0, int ex1,
                                                   uint32_t tag) {
