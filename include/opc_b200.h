@@ -152,8 +152,9 @@ int opc_workspace_init(void* workspace, size_t bytes, void* stream);
  *   x  device fp16, row b at x + b*ldx (ldx >= K, in elements)
  *   y  device fp16, row b at y + b*ldy (ldy >= M)
  * Batch 17..64 with x 16-byte aligned and ldx % 8 == 0 runs the prefill GEMM (opc_gemm).
- * Batch 1..2 (when the staged x fits in shared memory): x is staged per CTA as 24-bit integers
- * (x * 2^e_x, e_x from max |x|), the centroids are the 15-bit integer codebooks above; the dot
+ * Batch 1..2 (when the staged x fits in shared memory): x is staged per CTA as integers
+ * round(x * 2^e_x), below 2^22 in magnitude (e_x from max |x|), the centroids are the 15-bit
+ * integer codebooks above; the dot
  * products accumulate exactly in integers (mma.sync int8, int64 combination) and are scaled and
  * rounded once to fp16.  Larger batches: fp16 x fp16 products accumulated in fp32
  * (mma.sync m16n8k16), rounded once to fp16.

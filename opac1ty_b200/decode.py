@@ -10,9 +10,9 @@ One decode step runs, for every decoder block, the projection chain the benchmar
 Attention, norms, RoPE, the activation and residual adds are outside the measured path (they
 are not part of opacc1ty's fused dequant path).  Each launch depends on the previous one, so a
 step is 4 dependent GEMVs per block.  At batch 1..2 the whole step runs as ONE persistent
-kernel (``opac1ty_b200.chain``: weights of every GEMV streamed without pause, each GEMV's outputs
-published as tagged words that the next GEMV polls, no grid barrier); otherwise every GEMV is its own launch, captured once into a CUDA
-graph, each carrying the programmatic-dependent-launch attribute so it starts streaming its
+kernel (``opac1ty_b200.chain``: weights of every GEMV streamed without pause, each GEMV's
+outputs published as tagged words that the next GEMV polls, no grid barrier); otherwise every
+GEMV is its own launch, captured once into a CUDA graph, each carrying the programmatic-dependent-launch attribute so it starts streaming its
 weights while its predecessor finishes.
 
 ``concat_rows`` builds the fused layers from per-projection reference layer dicts (codebooks,
