@@ -327,12 +327,6 @@ __device__ __forceinline__ uint32_t ld_nc_u16(const void* p) {
 // convention), from its bits; no address-taken output argument, so nothing goes to local memory.
 __device__ __forceinline__ int frexp_exponent(float m) { return ((__float_as_int(m) >> 23) & 0xff) - 126; }
 
-// Round-to-nearest-even integer of |v| < 2^22 with one FP32 add: v + 1.5*2^23 lies in
-// (2^23, 2^24), where the float spacing is exactly 1, so the sum's low mantissa bits are the
-// rounded integer (offset by the constant's bit pattern 0x4B400000).
-__device__ __forceinline__ int round_small_int(float v) {
-  return __float_as_int(v + 12582912.0f) - 0x4B400000;
-}
 
 // Device error word (one per device, lives in the module; the library is one translation
 // unit).  Codes:
