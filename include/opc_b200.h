@@ -168,11 +168,15 @@ int opc_gemv(const opc_layer* layer, const void* x, int64_t ldx, void* y, int64_
 /* Allocation-free opc_gemv, for callers that cannot allocate device memory: plugin hosts
  * that hand a plugin only its preallocated input and output buffers, or serving processes
  * whose whole device memory belongs to their own pool.  No counterpart in the reference.
- * Same computation, arguments and results as opc_gemv, but the scratch comes from a 448 KiB
- * array compiled into this library (every GPU that loads the library keeps it until exit)
- * rather than a workspace, and the call allocates and frees nothing.  Limits: batch 1..8 and
- * at most 16384 tiles (row tiles of 16 rows plus outlier tiles), i.e. M <= 262144; larger
- * requests return OPC_ERR_INVALID with the reason.  The first call on each device looks up the
+ * Same computation and arguments as opc_gemv, but the scratch comes from a 448 KiB array
+ * compiled into this library (every GPU that loads the library keeps it until exit) rather than
+ * a workspace, and the call allocates and frees nothing.  sub_vector_size 1 layers always run
+ * the fp16 GEMV kernel here: results equal opc_gemv's bit for bit at batch 3..8 (where opc_gemv
+ * runs the same kernel) and agree within the GEMV tolerance at batch 1..2 (where opc_gemv runs
+ * the integer kernel).  sub_vector_size 8 layers run the same kernel as opc_gemv and use no
+ * scratch.  Limits: batch 1..8 and, for sub_vector_size 1, at most 16384 tiles (row tiles of
+ * 16 rows plus outlier tiles), i.e. M <= 262144; larger requests return OPC_ERR_INVALID with the
+ * reason.  The first call on each device looks up the
  * array's device address (cudaGetSymbolAddress); make that first call before any stream
  * capture.  Every call shares the one array, so calls that may overlap on the GPU (different
  * streams, or different host threads on one device) race and must be serialised by the
@@ -277,6 +281,14 @@ int opc_chain_create_tp(const opc_chain_step* steps, int32_t n_steps, int32_t ba
  * layer.  Bit-exact restatement of dequantize_layer (opacc1ty/export/converter.py:26-67),
  * decoded with the same device routine the GEMV uses. */
 int opc_dequant(const opc_layer* layer, void* w, int64_t ldw, void* stream);
+
+/* GEMV -> GEMM crossover: opc_gemv runs batches above `batch` (default 16) on the prefill GEMM
+ * when x is TMA-readable, and smaller batches on the GEMV kernels.  0 sends every TMA-readable
+ * call to the GEMM, 64 none.  Process-wide; takes effect for later calls.  The reference has a
+ * single GEMV dispatch (opacc1ty/utils/metal_utils.py:202-288) and no such switch; the setting
+ * exists so the crossover can be measured (both kernels timed at every batch) and tuned. */
+int opc_set_gemm_crossover(int32_t batch);
+int32_t opc_gemm_crossover(void);
 
 /* Read and clear the device error word of `device` (synchronises the device).  Kernels with
  * bounded waits record a nonzero code there instead of hanging; 0 = no error. */

@@ -12,6 +12,7 @@ timing of the model's quantized layers on the GPU.  ``layer-bench`` times one sy
 
 from __future__ import annotations
 
+import ctypes
 import json
 import re
 import sys
@@ -143,6 +144,12 @@ def _time_gemv(dl, batch: int, iters: int):
     return e0.elapsed_time(e1) * 1000.0 / iters
 
 
+def _lib_handle():
+    from . import _lib
+
+    return _lib.load()
+
+
 @cli.command()
 @click.argument("bf2_path", type=click.Path(exists=True))
 @click.option("--batch", type=int, default=1)
@@ -181,11 +188,13 @@ def benchmark(bf2_path, batch, iters, json_output):
 @click.option("--batch", type=int, default=1)
 @click.option("--iters", type=int, default=20)
 @click.option("--svs", type=click.Choice(["1", "8"]), default="1", help="sub_vector_size of the synthetic layer")
-def layer_bench(shape, outliers, batch, iters, svs):
-    """Time one synthetic layer's fused GEMV (CUDA events); prints one JSON line."""
+@click.option("--op", type=click.Choice(["gemv", "dequant"]), default="gemv",
+              help="gemv: the fused GEMV; dequant: write W_hat [M][K] fp16 (opc_dequant)")
+def layer_bench(shape, outliers, batch, iters, svs, op):
+    """Time one synthetic layer's fused GEMV or dequantization (CUDA events); prints one JSON line."""
     import torch
 
-    from . import layer as L, synthetic
+    from . import layer as L, measure, synthetic
     from .utils import get_cuda_device_info
 
     M, K = (int(v) for v in shape.lower().split("x"))
@@ -196,6 +205,17 @@ def layer_bench(shape, outliers, batch, iters, svs):
     else:
         ly = synthetic.random_layer_device(M, K, n_out, seed=0, device=dev)
     dl = L.prepare_layer(ly, dev)
+    if op == "dequant":
+        w = torch.empty(M, K, dtype=torch.float16, device=dev)
+        lib = _lib_handle()
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        us = measure.graph_time_us(lambda: lib.opc_dequant(ctypes.byref(dl.c_layer), w.data_ptr(), w.stride(0), stream),
+                                   dev, iters)
+        # bytes: the packed layer read (indices, codebooks, outlier rows) and W_hat written
+        nb = dl.algorithmic_bytes(0) + 2 * M * K
+        click.echo(json.dumps({"gpu": get_cuda_device_info().name, "op": "dequant", "shape": [M, K], "svs": int(svs),
+                               "n_outliers": dl.n_outliers, "us": us, "bytes": nb, "gbs": nb / us / 1e3}))
+        return
     us = _time_gemv(dl, batch, iters)
     nb = dl.algorithmic_bytes(batch)
     click.echo(json.dumps({"gpu": get_cuda_device_info().name, "shape": [M, K], "svs": int(svs),

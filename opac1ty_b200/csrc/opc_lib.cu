@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -118,6 +119,8 @@ constexpr int kCtasPerSm = 2;
 #endif
 constexpr int kXsMaxBytes = OPC_XS_MAX_BYTES;
 constexpr int kMaxBatch = 64;
+// opc_gemv runs batches above this on the prefill GEMM (opc_set_gemm_crossover)
+std::atomic<int> g_gemm_crossover{16};
 
 int nt_for_batch(int batch) {
   if (batch <= 8) return 1;
@@ -482,8 +485,10 @@ int opc_workspace_init(void* workspace, size_t bytes, void* stream) {
 }  // extern "C"
 
 namespace {
-// svs = 8: one launch, no workspace (each CTA reduces its tile in shared memory).
-int launch_vq8(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ldy, int32_t batch, cudaStream_t s) {
+// svs = 8: one launch, no workspace (each CTA reduces its tile in shared memory).  `fn` names the
+// entry point in error messages.
+int launch_vq8(const char* fn, const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ldy, int32_t batch,
+               cudaStream_t s) {
   const opc_layer_plan& p = L->plan;
   opc::Vq8Args a;
   memset(&a, 0, sizeof(a));
@@ -510,13 +515,24 @@ int launch_vq8(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t 
   while (nc > 1 && static_cast<size_t>(nc) * col_bytes > static_cast<size_t>(opc::kVq8XsMaxBytes)) nc >>= 1;
   while (nc > 1 && nc / 2 >= batch) nc >>= 1;
   if (col_bytes > static_cast<size_t>(opc::kVq8XsMaxBytes))
-    return fail(OPC_ERR_UNSUPPORTED, "opc_gemv: K=%d too large for the svs=8 kernel's staged x", p.K);
+    return fail(OPC_ERR_UNSUPPORTED, "%s: K=%d too large for the svs=8 kernel's staged x", fn, p.K);
   a.nc = nc;
   const size_t smem = static_cast<size_t>(nc) * col_bytes;
-  static std::once_flag attr_once;
-  std::call_once(attr_once, []() {
-    cudaFuncSetAttribute(opc::vq8_gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, opc::kVq8XsMaxBytes);
-  });
+  int dev = 0;
+  OPC_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  {
+    // the dynamic shared-memory limit is a per-device function attribute: set it once on every
+    // device the kernel runs on
+    static std::mutex mu;
+    static std::map<int, bool> configured;
+    std::lock_guard<std::mutex> lk(mu);
+    if (!configured[dev]) {
+      OPC_CUDA(cudaFuncSetAttribute(opc::vq8_gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    opc::kVq8XsMaxBytes),
+               "cudaFuncSetAttribute(max dynamic smem, vq8_gemv)");
+      configured[dev] = true;
+    }
+  }
   const dim3 grid(static_cast<unsigned>(p.row_tiles + a.OT), static_cast<unsigned>(ceil_div(batch, nc)));
   opc::vq8_gemv_kernel<<<grid, opc::kVq8Warps * 32, smem, s>>>(a);
   OPC_CUDA(cudaGetLastError(), "launch vq8_gemv_kernel");
@@ -540,7 +556,8 @@ int opc_gemv(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ld
   if (!aligned(x, 2) || !aligned(y, 2)) return fail(OPC_ERR_INVALID, "opc_gemv: x/y not 2-byte aligned");
   if (!aligned(L->units, 16) || !aligned(L->codebooks, 16))
     return fail(OPC_ERR_INVALID, "opc_gemv: layer buffers misaligned (units and codebooks 16 B)");
-  if (p.sub_vector_size == 8) return launch_vq8(L, x, ldx, y, ldy, batch, static_cast<cudaStream_t>(stream_v));
+  if (p.sub_vector_size == 8)
+    return launch_vq8("opc_gemv", L, x, ldx, y, ldy, batch, static_cast<cudaStream_t>(stream_v));
   int dev = 0;
   OPC_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
   DeviceCache dc;
@@ -555,10 +572,11 @@ int opc_gemv(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ld
   if (p.total_units >= (int64_t(1) << 31)) return fail(OPC_ERR_UNSUPPORTED, "opc_gemv: layer too large (2^31 units)");
   cudaStream_t s = static_cast<cudaStream_t>(stream_v);
 
-  // Batch 17..64: the tcgen05 GEMM (measured 9x faster than the fp16 GEMV at 64 rows of a
-  // 14336x4096 layer; at 16 rows the two are even on 8B shapes and the GEMV wins on 70B shapes)
-  // when x can be read with TMA.
-  if (batch > 16 && aligned(x, 16) && ldx % 8 == 0) return opc_gemm(L, x, ldx, y, ldy, batch, stream_v);
+  // Batches above the crossover (default 16): the tcgen05 GEMM (measured 9x faster than the fp16
+  // GEMV at 64 rows of a 14336x4096 layer; at 16 rows the two are even on 8B shapes and the GEMV
+  // wins on 70B shapes) when x can be read with TMA.
+  if (batch > g_gemm_crossover.load(std::memory_order_relaxed) && aligned(x, 16) && ldx % 8 == 0)
+    return opc_gemm(L, x, ldx, y, ldy, batch, stream_v);
 
   // Batch 1..2: the integer kernel, when its staged x and at least two ring stages fit.
   if (batch <= opc::kQMaxBatch) {
@@ -696,11 +714,6 @@ int opc_gemv_noalloc(const opc_layer* L, const void* x, int64_t ldx, void* y, in
   if (batch < 1 || batch > kStaticMaxBatch)
     return fail(OPC_ERR_INVALID, "opc_gemv_noalloc: batch %d outside [1, %d] (the static scratch holds one n-tile)",
                 batch, kStaticMaxBatch);
-  if (static_cast<int64_t>(p.row_tiles) + p.outlier_tiles > kStaticMaxSegments)
-    return fail(OPC_ERR_INVALID,
-                "opc_gemv_noalloc: %d row tiles + %d outlier tiles exceed the static scratch limit of %d tiles "
-                "(M up to %d rows); use opc_gemv with a workspace",
-                p.row_tiles, p.outlier_tiles, kStaticMaxSegments, kStaticMaxSegments * opc::kTileRows);
   if (!x || !y) return fail(OPC_ERR_INVALID, "opc_gemv_noalloc: x or y is NULL");
   if (ldx < p.K || ldy < p.M)
     return fail(OPC_ERR_INVALID, "opc_gemv_noalloc: ldx=%lld < K=%d or ldy=%lld < M=%d", static_cast<long long>(ldx),
@@ -708,7 +721,14 @@ int opc_gemv_noalloc(const opc_layer* L, const void* x, int64_t ldx, void* y, in
   if (!aligned(x, 2) || !aligned(y, 2)) return fail(OPC_ERR_INVALID, "opc_gemv_noalloc: x/y not 2-byte aligned");
   if (!aligned(L->units, 16) || !aligned(L->codebooks, 16))
     return fail(OPC_ERR_INVALID, "opc_gemv_noalloc: layer buffers misaligned (units and codebooks 16 B)");
-  if (p.sub_vector_size == 8) return launch_vq8(L, x, ldx, y, ldy, batch, static_cast<cudaStream_t>(stream_v));
+  // sub_vector_size 8 reduces each tile inside its CTA and needs no scratch at all
+  if (p.sub_vector_size == 8)
+    return launch_vq8("opc_gemv_noalloc", L, x, ldx, y, ldy, batch, static_cast<cudaStream_t>(stream_v));
+  if (static_cast<int64_t>(p.row_tiles) + p.outlier_tiles > kStaticMaxSegments)
+    return fail(OPC_ERR_INVALID,
+                "opc_gemv_noalloc: %d row tiles + %d outlier tiles exceed the static scratch limit of %d tiles "
+                "(M up to %d rows); use opc_gemv with a workspace",
+                p.row_tiles, p.outlier_tiles, kStaticMaxSegments, kStaticMaxSegments * opc::kTileRows);
   if (p.total_units >= (int64_t(1) << 31))
     return fail(OPC_ERR_UNSUPPORTED, "opc_gemv_noalloc: layer too large (2^31 units)");
   int dev = 0;
@@ -1465,6 +1485,15 @@ int opc_peer_free(void* ptr) {
   OPC_CUDA(cudaFree(ptr), "cudaFree(peer region)");
   return OPC_OK;
 }
+
+int opc_set_gemm_crossover(int32_t batch) {
+  if (batch < 0 || batch > kMaxBatch)
+    return fail(OPC_ERR_INVALID, "opc_set_gemm_crossover: batch %d outside [0, %d]", batch, kMaxBatch);
+  g_gemm_crossover.store(batch, std::memory_order_relaxed);
+  return OPC_OK;
+}
+
+int32_t opc_gemm_crossover(void) { return g_gemm_crossover.load(std::memory_order_relaxed); }
 
 int opc_take_device_error(int32_t device, int32_t* code) {
   if (!code) return fail(OPC_ERR_INVALID, "opc_take_device_error: code is NULL");

@@ -156,6 +156,12 @@ class DecodeStack:
     def launches_per_step(self) -> int:
         return 1 if self.chain is not None else 4 * len(self.blocks)
 
+    def kernel_name(self) -> str:
+        """The kernel that runs the step."""
+        if self.chain is not None:
+            return "opc::chain_kernel"
+        return "opc::gemvq_kernel" if self.batch <= 2 else "opc::gemv_kernel"
+
     def step_eager(self):
         """One decode step on the current stream; input and output in bufs["x"]."""
         if self.chain is not None:

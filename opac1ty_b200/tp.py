@@ -212,6 +212,12 @@ class TPDecodeStack:
     def launches_per_step(self) -> int:
         return 1 if self.chain is not None else 4 * len(self.blocks)
 
+    def kernel_name(self) -> str:
+        """The kernel that runs the step (fused chain, or one GEMV launch per projection)."""
+        if self.chain is not None:
+            return "opc::chain_kernel"
+        return "opc::gemvq_kernel" if self.batch <= 2 else "opc::gemv_kernel"
+
     def enable_chain(self, **kw) -> "TPChain":
         """Collective: run every step as one fused kernel per rank (TPChain, batch 1..2);
         bufs["x"] becomes the chain's input/output buffer (current contents carried over)."""

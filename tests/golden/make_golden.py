@@ -1,8 +1,11 @@
 #!/usr/bin/env python
 """Generate the golden fixtures in this directory from the reference implementation itself.
 
-Run where the reference source tree is available (OPACC1TY_REFERENCE, default
-/root/reference); the outputs are committed so the tests need only this directory.
+Run where the reference source tree is available, naming it explicitly:
+
+    python tests/golden/make_golden.py --reference <path to the opacc1ty source tree>
+
+(or set OPACC1TY_REFERENCE); the outputs are committed so the tests need only this directory.
 
   dequant_svs1.npz      random svs=1 layer with a repeated outlier id and an outlier in the
                         last row -> reference dequantize_layer (opacc1ty/export/converter.py)
@@ -36,7 +39,22 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parent.parent
-REF = os.environ.get("OPACC1TY_REFERENCE", "/root/reference")
+
+def _reference_path() -> str:
+    """The reference source tree: --reference PATH, else $OPACC1TY_REFERENCE (no default)."""
+    argv = sys.argv[1:]
+    for i, a in enumerate(argv):
+        if a == "--reference" and i + 1 < len(argv):
+            return argv[i + 1]
+        if a.startswith("--reference="):
+            return a.split("=", 1)[1]
+    env = os.environ.get("OPACC1TY_REFERENCE")
+    if env:
+        return env
+    sys.exit("make_golden.py: name the reference source tree with --reference PATH or OPACC1TY_REFERENCE")
+
+
+REF = _reference_path()
 sys.path.insert(0, REF)
 sys.path.insert(1, str(ROOT))
 

@@ -113,3 +113,16 @@ def test_metal_manager_raises_and_cuda_manager_mirrors_methods():
         MetalKernelManager()
     for m in ("compile_kernels", "load_library", "dequant_gemv", "dequant_gemm", "prepare_layer"):
         assert callable(getattr(CudaKernelManager, m))
+
+
+def test_gemm_crossover_setting_is_validated_and_kept():
+    lib = _lib.load()
+    old = lib.opc_gemm_crossover()
+    assert old == 16
+    try:
+        assert lib.opc_set_gemm_crossover(65) == _lib.OPC_ERR_INVALID
+        assert "crossover" in _lib.last_error()
+        assert lib.opc_set_gemm_crossover(64) == _lib.OPC_OK
+        assert lib.opc_gemm_crossover() == 64
+    finally:
+        lib.opc_set_gemm_crossover(old)

@@ -101,3 +101,35 @@ def test_chain_rejects_unlinked_steps(cuda_device):
     y2 = torch.zeros_like(x)
     with pytest.raises(_lib.OpcError):
         Chain([(a, x, y1), (b, x, y2)])   # step 1 must read step 0's output
+
+
+def _blocks_8b(n_blocks, seed):
+    """Llama-3.1-8B projection shapes (the benchmark's), numpy-generated so the oracle can run them."""
+    cfg = dict(synthetic.LLAMA_8B, layers=n_blocks)
+    return cfg, _blocks(cfg, seed=seed)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("batch", [1, 2])
+def test_chain_at_llama8b_shapes(cuda_device, batch):
+    # The benchmark's shapes: K = 14336 on the down projection forces two ring stages, and at
+    # batch 2 the staged x (2 x 14336 values) selects the 8-chunk staging instance of the kernel.
+    cfg, bds = _blocks_8b(2, seed=100 + batch)
+    x = synthetic.activations(batch, cfg["hidden"], seed=31 + batch)
+    outs = []
+    for use_chain in (True, False):
+        st = D.DecodeStack.from_block_dicts(bds, cfg["hidden"], cfg["intermediate"], cfg["kv"], cuda_device,
+                                            batch=batch, use_chain=use_chain)
+        assert (st.chain is not None) == use_chain
+        st.bufs["x"].copy_(torch.from_numpy(x))
+        y = st.step_eager().clone()
+        inter = {k: v.clone() for k, v in st.bufs.items()}
+        torch.cuda.synchronize()
+        outs.append((y, inter))
+        del st
+    (yc, ic), (yl, il) = outs
+    assert torch.equal(yc, yl)
+    for k in ic:
+        assert torch.equal(ic[k], il[k]), k
+    y64 = _oracle_chain(x, bds, cfg)
+    assert oracle.rel_err(yc.cpu().numpy(), y64) <= 5e-3

@@ -115,3 +115,21 @@ def test_vq8_through_the_kernel_manager_raw_buffers(cuda_device):
                      M, K, ly["outlier_values"].to(cuda_device), ly["outlier_indices"].to(cuda_device), n)
     y64 = oracle.gemv_f64(oracle.dequantize_np(ly), x.cpu().numpy().reshape(1, K))
     assert oracle.rel_err(y.cpu().numpy().reshape(1, M), y64) <= REL_TOL
+
+
+@pytest.mark.gpu
+def test_vq8_gemv_with_large_staged_x_on_two_devices(cuda_device):
+    # batch 8 at K = 4096 stages 8 x 8.2 KB of x: more than the default 48 KB of dynamic shared
+    # memory, so the raised limit must be in force on every device the kernel runs on.
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    M, K, batch = 512, 4096, 8
+    layer = synthetic.random_layer_vq8(M, K, 4, seed=5)
+    x = synthetic.activations(batch, K, seed=6)
+    y64 = oracle.gemv_f64(oracle.dequantize_np(layer), x)
+    for d in range(2):
+        dev = torch.device("cuda", d)
+        with torch.cuda.device(dev):
+            dl = L.prepare_layer(layer, dev)
+            y = L.gemv(dl, torch.from_numpy(x).to(dev)).cpu().numpy()
+        assert oracle.rel_err(y, y64) <= REL_TOL, d

@@ -44,6 +44,40 @@ def test_noalloc_matches_workspace_gemv_twice(cuda_device, M, K, n_out, batch):
         assert oracle.rel_err(got, y64) <= REL_TOL
 
 
+@pytest.mark.parametrize("batch", [3, 8])
+def test_noalloc_equals_workspace_gemv_bit_for_bit_at_batch_3_to_8(cuda_device, batch):
+    # At batch 3..8 both entry points run the same fp16 GEMV kernel with a fixed summation order,
+    # so the only difference is where the scratch lives: the results must be identical.
+    M, K = 3000, 1536
+    layer = synthetic.random_layer(M, K, 30, seed=batch, shuffle_ids=True)
+    dl = L.prepare_layer(layer, cuda_device)
+    x = torch.from_numpy(synthetic.activations(batch, K, seed=10 + batch)).to(cuda_device)
+    y_ws = L.gemv(dl, x)
+    for _ in range(2):
+        y = torch.full((batch, M), float("nan"), dtype=torch.float16, device=cuda_device)
+        _lib.check(_call_noalloc(dl, x, y))
+        torch.cuda.synchronize()
+        assert torch.equal(y, y_ws)
+
+
+@pytest.mark.parametrize("batch", [1, 5])
+def test_noalloc_svs8_layer_against_the_oracle(cuda_device, batch):
+    # sub_vector_size 8 (the reference quantizer's default) needs no scratch; the entry point
+    # must still run it and agree with the workspace call and with the fp64 oracle.
+    M, K = 1000, 2048
+    layer = synthetic.random_layer_vq8(M, K, 10, seed=77)
+    dl = L.prepare_layer(layer, cuda_device)
+    x = torch.from_numpy(synthetic.activations(batch, K, seed=3)).to(cuda_device)
+    y64 = oracle.gemv_f64(oracle.dequantize_np(layer), x.cpu().numpy())
+    y_ws = L.gemv(dl, x)
+    for _ in range(2):
+        y = torch.full((batch, M), float("nan"), dtype=torch.float16, device=cuda_device)
+        _lib.check(_call_noalloc(dl, x, y))
+        torch.cuda.synchronize()
+        assert torch.equal(y, y_ws)
+        assert oracle.rel_err(y.cpu().numpy(), y64) <= REL_TOL
+
+
 def test_noalloc_rejects_requests_beyond_its_limits(cuda_device):
     layer = synthetic.random_layer(64, 128, 0, seed=1)
     dl = L.prepare_layer(layer, cuda_device)
