@@ -12,7 +12,6 @@ timing of the model's quantized layers on the GPU.  ``layer-bench`` times one sy
 
 from __future__ import annotations
 
-import ctypes
 import json
 import re
 import sys
@@ -144,12 +143,6 @@ def _time_gemv(dl, batch: int, iters: int):
     return e0.elapsed_time(e1) * 1000.0 / iters
 
 
-def _lib_handle():
-    from . import _lib
-
-    return _lib.load()
-
-
 @cli.command()
 @click.argument("bf2_path", type=click.Path(exists=True))
 @click.option("--batch", type=int, default=1)
@@ -207,10 +200,7 @@ def layer_bench(shape, outliers, batch, iters, svs, op):
     dl = L.prepare_layer(ly, dev)
     if op == "dequant":
         w = torch.empty(M, K, dtype=torch.float16, device=dev)
-        lib = _lib_handle()
-        stream = torch.cuda.current_stream(dev).cuda_stream
-        us = measure.graph_time_us(lambda: lib.opc_dequant(ctypes.byref(dl.c_layer), w.data_ptr(), w.stride(0), stream),
-                                   dev, iters)
+        us = measure.graph_time_us(lambda: L.dequantize(dl, out=w), dev, iters)
         # bytes: the packed layer read (indices, codebooks, outlier rows) and W_hat written
         nb = dl.algorithmic_bytes(0) + 2 * M * K
         click.echo(json.dumps({"gpu": get_cuda_device_info().name, "op": "dequant", "shape": [M, K], "svs": int(svs),

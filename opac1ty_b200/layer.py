@@ -166,11 +166,13 @@ def prepare_layer(layer: dict, device=None, name: Optional[str] = None) -> Devic
     return dl
 
 
-def dequantize(dl: DeviceLayer) -> torch.Tensor:
-    """W_hat [M][K] fp16 on the layer's device (``opc_dequant``)."""
+def dequantize(dl: DeviceLayer, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """W_hat [M][K] fp16 on the layer's device (``opc_dequant``), into ``out`` if given."""
     lib = _lib.load()
     with torch.cuda.device(dl.device):
-        w = torch.empty(dl.M, dl.K, dtype=torch.float16, device=dl.device)
+        w = torch.empty(dl.M, dl.K, dtype=torch.float16, device=dl.device) if out is None else out
+        if tuple(w.shape) != (dl.M, dl.K) or w.dtype != torch.float16 or w.stride(1) != 1:
+            raise ValueError(f"dequantize: out must be float16 [{dl.M}, {dl.K}] with unit stride")
         _lib.check(lib.opc_dequant(ctypes.byref(dl.c_layer), w.data_ptr(), w.stride(0), _stream_ptr(dl.device)))
     return w
 
