@@ -57,7 +57,8 @@ METRIC = "fused 2-bit VQ GEMV HBM TB/s (% peak); decode tok/s @ Llama-3.1-8B sha
 CHAIN_TRAFFIC_RATIO = 1.021
 WORKLOAD = "Llama-3.1-8B decode GEMV set, batch 1, 32 blocks (q|k|v, o, gate|up, down), 2-bit svs=1, 1% outlier rows"
 DTYPE = ("2-bit codebook weights, fp16 x and y; batch 1-2 dot products exact in integers: int8 x uint8 mma.sync "
-         "of 15-bit fixed-point centroids and 22-bit fixed-point x, int64 sums, one fp16 rounding")
+         "of 15-bit fixed-point centroids and fixed-point x (batch 1 decode step: 30-bit x digits at a scale "
+         "fixed from a norm bound; otherwise 22-bit x scaled by max|x|), int64 sums, one fp16 rounding per output")
 PARITY_TOL = 2e-3
 BLOCKS = 32
 
@@ -334,7 +335,8 @@ def parity_check(stack, cfg, args, dev, dist, world, rank) -> dict:
         if rank == 0:
             res["ranks_equal"] = all(torch.equal(g, gathered[0]) for g in gathered)
             log("parity: building the one-GPU stack")
-            ref = decode.DecodeStack.synthetic(cfg, device=dev, batch=B, use_chain=True)
+            # the row-sharded kernel is the barrier form: its one-GPU run is the bit-exact reference
+            ref = decode.DecodeStack.synthetic(cfg, device=dev, batch=B, use_chain=True, chain_form="barrier")
             ref.bufs["x"].copy_(x0)
             y1 = ref.step_eager().clone()
             torch.cuda.synchronize(dev)
@@ -344,7 +346,8 @@ def parity_check(stack, cfg, args, dev, dist, world, rank) -> dict:
             torch.cuda.empty_cache()
         dist.barrier()
     if rank == 0:
-        one = decode.DecodeStack.synthetic(cfg, n_layers=1, device=dev, batch=B, use_chain=True)
+        form = getattr(getattr(stack, "chain", None), "form", "barrier")
+        one = decode.DecodeStack.synthetic(cfg, n_layers=1, device=dev, batch=B, use_chain=True, chain_form=form)
         one.bufs["x"].copy_(x0)
         y = one.step_eager().clone().double()
         y64 = block0_fp64(cfg, x0, dev)
@@ -352,9 +355,10 @@ def parity_check(stack, cfg, args, dev, dist, world, rank) -> dict:
         res["tolerance"] = PARITY_TOL
         res["ok"] = res["deterministic"] and res["rel_err_block0"] <= PARITY_TOL and res.get("ranks_equal", True) \
             and res.get("bit_equal_1gpu", True)
+        res["block0_form"] = form
         res["what"] = ("two runs of the timed step from one x bit-equal; N > 1: every rank's output equal and equal to "
-                       "a one-GPU run; block 0 (one chain launch) against a float64 torch recompute from the "
-                       "dequantized weights, norm-wise max|y - y64| / max|y64|")
+                       "a one-GPU run of the same kernel form; block 0 (one chain launch of the timed form) against a "
+                       "float64 torch recompute from the dequantized weights, norm-wise max|y - y64| / max|y64|")
         del one
         torch.cuda.empty_cache()
     return res

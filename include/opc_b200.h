@@ -223,13 +223,39 @@ typedef struct opc_chain_step {
   int64_t ldy;
 } opc_chain_step;
 int opc_chain_create(const opc_chain_step* steps, int32_t n_steps, int32_t batch, opc_chain** out);
+/* The same with an explicit form of the decode-step kernel:
+ *   OPC_CHAIN_FORM_BARRIER   the step-by-step form above: each step's x is staged per CTA from the
+ *                            previous step's fp16 outputs with its exponent from max|x| (as
+ *                            opc_gemv does), so results equal opc_gemv's bit for bit; batch 1..2.
+ *   OPC_CHAIN_FORM_DATAFLOW  batch 1, one GPU, K <= 32768 (and the barrier form's other limits):
+ *                            steps exchange their outputs as fixed-point digits whose scale is
+ *                            fixed in advance from a norm bound (|y_r| <= ||W row r||_2 ||x||_2;
+ *                            30-bit integers below 2^29 in magnitude, at least as fine as the
+ *                            barrier form's 22 bits for every x whose norm is within 2^7 of its
+ *                            largest element times sqrt(K)), written by the warp that finishes each
+ *                            row and copied into every CTA per 128-column block as soon as that block
+ *                            is complete.  No barrier of any kind between steps.  Every step's fp16
+ *                            output is rounded once from an exact integer dot product, so results
+ *                            are deterministic; they agree with opc_gemv within the GEMV tolerance
+ *                            rather than bit for bit (the inputs' fixed-point scale differs).  A
+ *                            non-finite step output records device error 5.
+ *   OPC_CHAIN_FORM_AUTO      (opc_chain_create) the barrier form (measured faster on the Llama-3.1-8B
+ *                            decode step: 843 against 574 tok/s).
+ * The dataflow form replaces nothing in the reference beyond what opc_chain_create replaces. */
+enum { OPC_CHAIN_FORM_AUTO = 0, OPC_CHAIN_FORM_BARRIER = 1, OPC_CHAIN_FORM_DATAFLOW = 2 };
+int opc_chain_create_ex(const opc_chain_step* steps, int32_t n_steps, int32_t batch, int32_t form, opc_chain** out);
+/* The form a chain was built with (OPC_CHAIN_FORM_BARRIER or OPC_CHAIN_FORM_DATAFLOW). */
+int32_t opc_chain_form(const opc_chain* chain);
 int opc_chain_launch(opc_chain* chain, void* stream);
 int opc_chain_destroy(opc_chain* chain);
 /* Tracing: with a device buffer of opc_chain_trace_bytes() set, every launch records per step
- * and per CTA eight %globaltimer stamps (ns), taken by the CTA's first consumer thread: input
- * start, first poll of its x words done, x complete, max barrier passed, x staged, its own units
- * done, then two unused slots.  Layout [step][cta][8] uint64; NULL turns tracing off.
- * opc_chain_grid() is the number of CTAs (one per SM). */
+ * and per CTA eight %globaltimer stamps (ns).  Barrier form, taken by the CTA's first consumer
+ * thread: step start, setup done, first poll of its x words done, x complete, max barrier passed,
+ * digits stored, x staged, its own units done.  Dataflow form: [0] the staging warp begins the
+ * step, [1] it holds every block of x, [2] consumer warp 0 begins the step, [3] warp 0's units
+ * done, [4] / [5] the staging warp's first / last block arrival, [6] warp 0 starts waiting for
+ * its first chunk's x blocks (0 if it did not wait), [7] it has them.  Layout [step][cta][8]
+ * uint64; NULL turns tracing off.  opc_chain_grid() is the number of CTAs (one per SM). */
 size_t opc_chain_trace_bytes(const opc_chain* chain);
 /* Options: OPC_CHAIN_L2_PREFETCH (default 0): stream the weights with an L2 evict-first policy
  * (measured no faster on the Llama-3.1-8B decode step, kept as an option). */

@@ -5,6 +5,8 @@ step j-1's output.  ``opc_chain_launch`` runs all of them in one cooperative ker
 warp per SM streams the weights of every step without waiting for activations, and each step's
 outputs are published as tagged 32-bit words that the next step's readers poll (no grid barrier
 between steps).  Results equal per-step ``opac1ty_b200.gemv`` calls bit for bit (batch 1..2).
+At batch 1 the dataflow form exchanges fixed-point digits per 128-column block instead (no
+barrier or per-CTA conversion between steps; see ``Chain``).
 """
 
 from __future__ import annotations
@@ -18,10 +20,21 @@ from . import _lib
 from . import layer as L
 
 
-class Chain:
-    """Steps: (DeviceLayer, x tensor [B, >=K] fp16, y tensor [B, >=M] fp16), rows unit-stride."""
+FORMS = {"auto": _lib.OPC_CHAIN_FORM_AUTO, "barrier": _lib.OPC_CHAIN_FORM_BARRIER,
+         "dataflow": _lib.OPC_CHAIN_FORM_DATAFLOW}
 
-    def __init__(self, steps: Sequence[Tuple[L.DeviceLayer, torch.Tensor, torch.Tensor]]):
+
+class Chain:
+    """Steps: (DeviceLayer, x tensor [B, >=K] fp16, y tensor [B, >=M] fp16), rows unit-stride.
+
+    ``form``: "barrier" (each step's x staged from fp16 with its exponent from max|x|; results
+    equal per-step ``gemv`` calls bit for bit; batch 1..2), "dataflow" (batch 1: steps exchange
+    fixed-point digits at a scale fixed in advance from a norm bound, with no barrier between
+    steps; results within the GEMV tolerance) or "auto" (the barrier form, measured faster)."""
+
+    def __init__(self, steps: Sequence[Tuple[L.DeviceLayer, torch.Tensor, torch.Tensor]], form: str = "auto"):
+        if form not in FORMS:
+            raise ValueError(f"Chain: form must be one of {sorted(FORMS)}, got {form!r}")
         if not steps:
             raise ValueError("Chain: no steps")
         self.device = steps[0][0].device
@@ -44,9 +57,10 @@ class Chain:
         handle = ctypes.c_void_p()
         lib = _lib.load()
         with torch.cuda.device(self.device):
-            _lib.check(lib.opc_chain_create(arr, len(steps), batch, ctypes.byref(handle)))
+            _lib.check(lib.opc_chain_create_ex(arr, len(steps), batch, FORMS[form], ctypes.byref(handle)))
         self._handle = handle
         self._steps = arr
+        self.form = "dataflow" if lib.opc_chain_form(handle) == _lib.OPC_CHAIN_FORM_DATAFLOW else "barrier"
 
     def launch(self):
         lib = _lib.load()

@@ -219,8 +219,10 @@ def layer_bench(shape, outliers, batch, iters, svs, op):
 @click.option("--batch", type=int, default=1)
 @click.option("--iters", type=int, default=20)
 @click.option("--launches", is_flag=True, help="one GEMV launch per projection instead of the chain kernel")
+@click.option("--form", type=click.Choice(["auto", "barrier", "dataflow"]), default="auto",
+              help="chain kernel form (see opac1ty_b200.chain.Chain)")
 @click.option("--trace", is_flag=True, help="also report the chain kernel's per-phase timeline (opc_chain_set_trace)")
-def decode_bench(model, blocks, batch, iters, launches, trace):
+def decode_bench(model, blocks, batch, iters, launches, form, trace):
     """Time the decode step (q|k|v, o, gate|up, down per block) of synthetic 2-bit weights."""
     import torch
 
@@ -229,7 +231,8 @@ def decode_bench(model, blocks, batch, iters, launches, trace):
 
     cfg = synthetic.LLAMA_8B if model == "8b" else synthetic.LLAMA_70B
     dev = torch.device("cuda", 0)
-    st = decode.DecodeStack.synthetic(cfg, n_layers=blocks, device=dev, batch=batch, use_chain=not launches)
+    st = decode.DecodeStack.synthetic(cfg, n_layers=blocks, device=dev, batch=batch, use_chain=not launches,
+                                      chain_form=form)
     for _ in range(3):
         st.step_eager()
     torch.cuda.synchronize(dev)
@@ -243,10 +246,10 @@ def decode_bench(model, blocks, batch, iters, launches, trace):
     ms = e0.elapsed_time(e1) / iters
     nb = st.algorithmic_bytes()
     out = {"gpu": get_cuda_device_info().name, "model": model, "blocks": len(st.blocks), "batch": batch,
-           "chain": st.chain is not None, "ms_per_step": ms, "tok_s": batch * 1000.0 / ms,
+           "chain": st.chain is not None, "kernel": st.kernel_name(), "ms_per_step": ms, "tok_s": batch * 1000.0 / ms,
            "gbs": nb / (ms * 1e-3) / 1e9}
     if trace and st.chain is not None:
-        out["phases_us"] = _chain_phases(st)
+        out["phases_us"] = _chain_phases_dataflow(st) if st.chain.form == "dataflow" else _chain_phases(st)
     click.echo(json.dumps(out))
 
 
@@ -278,6 +281,45 @@ def _chain_phases(st) -> dict:
                      "x_wait": round(float(med[2]), 2), "max_barrier": round(float(med[3]), 2),
                      "digits": round(float(med[4]), 2), "staged": round(float(med[5]), 2),
                      "units": round(float(med[6]), 2),
+                     "span": round(float(np.mean(spans)), 2) if spans else None}
+    return res
+
+
+def _chain_phases_dataflow(st) -> dict:
+    """Dataflow form, per projection of a block (median over CTAs, mean over the inner blocks), in
+    µs relative to consumer warp 0's start of the GEMV: when the staging warp began the layer
+    (after the CTA's consumers left the layer before the previous one), saw its first and its last
+    block complete, held every block of x (the next exponent set); when warp 0 began waiting for
+    its first chunk's blocks (if it had to) and had them; when warp 0 finished its units; and the
+    GEMV's span (to the next GEMV's start)."""
+    import numpy as np
+    import torch
+
+    tr = st.chain.enable_trace()
+    for _ in range(3):
+        st.step_eager()
+    torch.cuda.synchronize(st.device)
+    t = tr.cpu().numpy().astype(np.int64)  # [steps, grid, 8] ns
+    st.chain.disable_trace()
+    names = ["qkv", "o", "gate_up", "down"]
+    n_blocks = t.shape[0] // 4
+    inner = range(1, n_blocks - 1) if n_blocks > 2 else range(n_blocks)
+    starts = np.median(t[:, :, 2], axis=1)
+    res = {}
+    for p, name in enumerate(names):
+        rows = [4 * b + p for b in inner if 4 * b + p > 0]
+
+        def rel(col):
+            vals = []
+            for r in rows:
+                ok = t[r, :, col] > 0
+                if ok.any():
+                    vals.append(np.median((t[r, ok, col] - t[r, ok, 2]) / 1000.0))
+            return round(float(np.mean(vals)), 2) if vals else None
+
+        spans = [(starts[r + 1] - starts[r]) / 1000.0 for r in rows if r + 1 < t.shape[0]]
+        res[name] = {"stage_start": rel(0), "first_block": rel(4), "last_block": rel(5), "x_complete": rel(1),
+                     "w0_wait_from": rel(6), "w0_blocks_in": rel(7), "units_done": rel(3),
                      "span": round(float(np.mean(spans)), 2) if spans else None}
     return res
 

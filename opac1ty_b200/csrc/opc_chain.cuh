@@ -113,7 +113,7 @@ __host__ __device__ __forceinline__ uint32_t chain_tag(uint32_t base, int32_t j)
 struct ChainPart {
   int32_t pu0, pu1, ou0, ou1, wp;
 };
-__host__ __device__ __forceinline__ ChainPart chain_part(const ChainLayer& L, int c, int G) {
+__host__ __device__ __forceinline__ ChainPart chain_part(const ChainLayer& L, int c, int G, int nw = kQConsumers) {
   ChainPart p;
   const int32_t t0 = static_cast<int32_t>((2ll * c * L.MT + G) / (2ll * G));
   const int32_t t1 = static_cast<int32_t>((2ll * (c + 1) * L.MT + G) / (2ll * G));
@@ -124,30 +124,31 @@ __host__ __device__ __forceinline__ ChainPart chain_part(const ChainLayer& L, in
   p.ou1 = L.Up + static_cast<int32_t>(static_cast<int64_t>(c + 1) * Uo / G);
   const int32_t np = p.pu1 - p.pu0, no = p.ou1 - p.ou0;
   if (no == 0) {
-    p.wp = kQConsumers;
+    p.wp = nw;
   } else if (np == 0) {
     p.wp = 0;
   } else {
-    int wo = static_cast<int>((2ll * kQConsumers * no + (np + no)) / (2ll * (np + no)));
-    wo = wo < 1 ? 1 : (wo > kQConsumers - 1 ? kQConsumers - 1 : wo);
-    p.wp = kQConsumers - wo;
+    int wo = static_cast<int>((2ll * nw * no + (np + no)) / (2ll * (np + no)));
+    wo = wo < 1 ? 1 : (wo > nw - 1 ? nw - 1 : wo);
+    p.wp = nw - wo;
   }
   // Every packed warp gets at least one unit, so the warps sharing a tile are exactly the parts
   // between the parts of its first and last unit (the split-tile contributor count relies on it).
   if (p.wp > np) p.wp = np;
   return p;
 }
-// Warp w's unit range within its CTA's share (32-bit arithmetic: a CTA's share times the 15
-// warps stays below 2^31, host-checked).
-__host__ __device__ __forceinline__ void chain_warp_range(const ChainPart& p, int w, int32_t* u0, int32_t* u1) {
+// Warp w's unit range within its CTA's share, for nw consumer warps (32-bit arithmetic: a CTA's
+// share times the warps stays below 2^31, host-checked).
+__host__ __device__ __forceinline__ void chain_warp_range(const ChainPart& p, int w, int32_t* u0, int32_t* u1,
+                                                         int nw = kQConsumers) {
   if (w < p.wp) {
     const int32_t np = p.pu1 - p.pu0;
     *u0 = p.pu0 + w * np / p.wp;
     *u1 = p.pu0 + (w + 1) * np / p.wp;
   } else {
-    const int32_t no = p.ou1 - p.ou0, nw = kQConsumers - p.wp;
-    *u0 = p.ou0 + (w - p.wp) * no / nw;
-    *u1 = p.ou0 + (w - p.wp + 1) * no / nw;
+    const int32_t no = p.ou1 - p.ou0, nwo = nw - p.wp;
+    *u0 = p.ou0 + (w - p.wp) * no / nwo;
+    *u1 = p.ou0 + (w - p.wp + 1) * no / nwo;
   }
 }
 

@@ -83,10 +83,11 @@ class DecodeStack:
     bufs: Dict[str, torch.Tensor] = field(default_factory=dict)
     use_chain: bool = True
     chain: object = None
+    chain_form: str = "auto"   # Chain form: "auto", "barrier" or "dataflow"
 
     @classmethod
     def from_block_dicts(cls, block_dicts: Sequence[Dict[str, dict]], hidden: int, intermediate: int, kv: int,
-                         device, batch: int = 1, use_chain: bool = True) -> "DecodeStack":
+                         device, batch: int = 1, use_chain: bool = True, chain_form: str = "auto") -> "DecodeStack":
         device = L._as_cuda_device(device)
         blocks = []
         for bd in block_dicts:
@@ -95,13 +96,14 @@ class DecodeStack:
             gu = L.prepare_layer(concat_rows([bd["gate_proj"], bd["up_proj"]]), device, "gate_up")
             down = L.prepare_layer(bd["down_proj"], device, "down_proj")
             blocks.append(Block(qkv, o, gu, down))
-        st = cls(blocks, hidden, intermediate, kv, device, batch, use_chain=use_chain)
+        st = cls(blocks, hidden, intermediate, kv, device, batch, use_chain=use_chain, chain_form=chain_form)
         st._alloc()
         return st
 
     @classmethod
     def synthetic(cls, cfg: dict, n_layers: Optional[int] = None, device=None, batch: int = 1,
-                  outlier_fraction: float = 0.01, seed: int = 0, use_chain: bool = True) -> "DecodeStack":
+                  outlier_fraction: float = 0.01, seed: int = 0, use_chain: bool = True,
+                  chain_form: str = "auto") -> "DecodeStack":
         """Random-initialised 2-bit weights with the given model shapes (synthetic.random_layer)."""
         shapes = synthetic.decoder_shapes(cfg)
         n_layers = cfg["layers"] if n_layers is None else n_layers
@@ -118,7 +120,8 @@ class DecodeStack:
             down = L.prepare_layer(bd["down_proj"], device, "down_proj")
             del bd
             blocks.append(Block(qkv, o, gu, down))
-        st = cls(blocks, cfg["hidden"], cfg["intermediate"], cfg["kv"], device, batch, use_chain=use_chain)
+        st = cls(blocks, cfg["hidden"], cfg["intermediate"], cfg["kv"], device, batch, use_chain=use_chain,
+                 chain_form=chain_form)
         st._alloc()
         return st
 
@@ -143,7 +146,7 @@ class DecodeStack:
                 steps += [(blk.qkv, b["x"], b["qkv"]), (blk.o, b["qkv"], b["o"]),
                           (blk.gate_up, b["o"], b["gu"]), (blk.down, b["gu"], b["x"])]
             try:
-                self.chain = Chain(steps)
+                self.chain = Chain(steps, form=self.chain_form)
             except _lib.OpcError:  # shape outside the chain kernel's limits: one launch per GEMV
                 self.chain = None
 
@@ -159,7 +162,7 @@ class DecodeStack:
     def kernel_name(self) -> str:
         """The kernel that runs the step."""
         if self.chain is not None:
-            return "opc::chain_kernel"
+            return "opc::chain2_kernel" if self.chain.form == "dataflow" else "opc::chain_kernel"
         return "opc::gemvq_kernel" if self.batch <= 2 else "opc::gemv_kernel"
 
     def step_eager(self):

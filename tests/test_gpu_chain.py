@@ -1,5 +1,6 @@
-"""Decode chain on one persistent kernel (opc_chain_*): bit-identical to per-GEMV launches
-(both accumulate exactly in integers at batch 1..2) and within 2e-3 of the oracle's fp64 chain."""
+"""Decode chain on one persistent kernel (opc_chain_*), barrier form: bit-identical to per-GEMV
+launches (both accumulate exactly in integers at batch 1..2, with the same fixed-point x) and
+within 2e-3 of the oracle's fp64 chain.  The dataflow form is tested in test_gpu_chain_dataflow.py."""
 
 import numpy as np
 import pytest
@@ -53,7 +54,8 @@ def test_chain_equals_launches_and_oracle(cuda_device, cfg, batch):
     outs = []
     for use_chain in (True, False):
         st = D.DecodeStack.from_block_dicts(bds, cfg["hidden"], cfg["intermediate"], cfg["kv"], cuda_device,
-                                            batch=batch, use_chain=use_chain)
+                                            batch=batch, use_chain=use_chain,
+                                            chain_form="barrier")
         assert (st.chain is not None) == use_chain
         st.bufs["x"].copy_(torch.from_numpy(x))
         y = st.step_eager().clone()
@@ -72,7 +74,8 @@ def test_chain_equals_launches_and_oracle(cuda_device, cfg, batch):
 def test_chain_repeated_launches_and_graph(cuda_device):
     cfg = CFGS[0]
     bds = _blocks(cfg, seed=7)
-    st = D.DecodeStack.from_block_dicts(bds, cfg["hidden"], cfg["intermediate"], cfg["kv"], cuda_device)
+    st = D.DecodeStack.from_block_dicts(bds, cfg["hidden"], cfg["intermediate"], cfg["kv"], cuda_device,
+                                        chain_form="barrier")
     x = torch.from_numpy(synthetic.activations(1, cfg["hidden"], seed=3)).to(cuda_device)
     st.bufs["x"].copy_(x)
     y1 = st.step_eager().clone()
@@ -101,6 +104,8 @@ def test_chain_rejects_unlinked_steps(cuda_device):
     y2 = torch.zeros_like(x)
     with pytest.raises(_lib.OpcError):
         Chain([(a, x, y1), (b, x, y2)])   # step 1 must read step 0's output
+    with pytest.raises(_lib.OpcError):
+        Chain([(a, x, y1), (b, x, y2)], form="dataflow")
 
 
 def _blocks_8b(n_blocks, seed):
@@ -119,7 +124,8 @@ def test_chain_at_llama8b_shapes(cuda_device, batch):
     outs = []
     for use_chain in (True, False):
         st = D.DecodeStack.from_block_dicts(bds, cfg["hidden"], cfg["intermediate"], cfg["kv"], cuda_device,
-                                            batch=batch, use_chain=use_chain)
+                                            batch=batch, use_chain=use_chain,
+                                            chain_form="barrier")
         assert (st.chain is not None) == use_chain
         st.bufs["x"].copy_(torch.from_numpy(x))
         y = st.step_eager().clone()
