@@ -316,6 +316,11 @@ int opc_dequant(const opc_layer* layer, void* w, int64_t ldw, void* stream);
 int opc_set_gemm_crossover(int32_t batch);
 int32_t opc_gemm_crossover(void);
 
+/* XXH64 (seed `seed`) of a HOST buffer: the checksum that the .bf2 layout places after the last
+ * layer (opacc1ty/format/header.py:26; the reference documents it but never writes it).  Files
+ * written with it set bit 0 of the file header's flags.  A format helper, not a kernel. */
+uint64_t opc_xxh64(const void* data, size_t len, uint64_t seed);
+
 /* Read and clear the device error word of `device` (synchronises the device).  Kernels with
  * bounded waits record a nonzero code there instead of hanging; 0 = no error. */
 int opc_take_device_error(int32_t device, int32_t* code);

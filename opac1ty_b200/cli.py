@@ -71,9 +71,10 @@ def _infer_model_config(sd: dict) -> dict:
 @click.option("--codebook-iters", type=int, default=100)
 @click.option("--no-error-feedback", is_flag=True)
 @click.option("--device", type=click.Choice(["cpu", "cuda"]), default="cpu")
+@click.option("--checksum", is_flag=True, help="end the file with its XXH64 checksum (flags bit 0)")
 @click.option("--json-output", is_flag=True)
 def quantize(model_path, bits, output, outlier_fraction, sub_vector_size, codebook_iters, no_error_feedback, device,
-             json_output):
+             checksum, json_output):
     """Quantize a safetensors model (file or directory) to .bf2 (options of cli/main.py:64-80)."""
     from .format import BF2Writer
     from .quantize import QuantizeConfig, VectorQuantizer
@@ -88,7 +89,7 @@ def quantize(model_path, bits, output, outlier_fraction, sub_vector_size, codebo
                                        device=device))
     res = q.quantize_model(sd, mcfg, progress=not json_output)
     elapsed = time.time() - t0
-    BF2Writer(str(out)).write(res, mcfg, res["_quantize_config"], progress=not json_output)
+    BF2Writer(str(out)).write(res, mcfg, res["_quantize_config"], progress=not json_output, checksum=checksum)
     orig = sum(t.numel() for t in sd.values()) * 2 / 1e9
     comp = out.stat().st_size / 1e9
     info = {"original_size_gb": round(orig, 2), "compressed_size_gb": round(comp, 2),
@@ -108,6 +109,7 @@ def info(bf2_path, layers, json_output):
     with BF2Reader(bf2_path) as r:
         d = {"model": r.model_config, "quantization": r.quantize_config,
              "compressed_size_gb": round(Path(bf2_path).stat().st_size / 1e9, 3), "n_layers": len(r.layer_names()),
+             "checksum": "verified" if r.checksum_ok else "absent",
              "layers": r.layer_names() if layers else None}
     click.echo(json.dumps(d, indent=2) if json_output else "\n".join(f"{k}: {v}" for k, v in d.items() if v is not None))
 

@@ -1790,6 +1790,61 @@ int opc_set_gemm_crossover(int32_t batch) {
 
 int32_t opc_gemm_crossover(void) { return g_gemm_crossover.load(std::memory_order_relaxed); }
 
+// XXH64 (xxHash, 64-bit variant, as published with its specification): four 64-bit lanes over
+// 32-byte stripes, then the tail in 8-, 4- and 1-byte steps, then the avalanche.  Host code.
+namespace {
+constexpr uint64_t kXxP1 = 0x9E3779B185EBCA87ull, kXxP2 = 0xC2B2AE3D27D4EB4Full, kXxP3 = 0x165667B19E3779F9ull,
+                   kXxP4 = 0x85EBCA77C2B2AE63ull, kXxP5 = 0x27D4EB2F165667C5ull;
+inline uint64_t xx_rotl(uint64_t v, int r) { return (v << r) | (v >> (64 - r)); }
+inline uint64_t xx_read64(const unsigned char* p) {
+  uint64_t v;
+  memcpy(&v, p, 8);  // little-endian host
+  return v;
+}
+inline uint32_t xx_read32(const unsigned char* p) {
+  uint32_t v;
+  memcpy(&v, p, 4);
+  return v;
+}
+inline uint64_t xx_round(uint64_t acc, uint64_t in) { return xx_rotl(acc + in * kXxP2, 31) * kXxP1; }
+inline uint64_t xx_merge(uint64_t acc, uint64_t v) { return (acc ^ xx_round(0, v)) * kXxP1 + kXxP4; }
+}  // namespace
+
+uint64_t opc_xxh64(const void* data, size_t len, uint64_t seed) {
+  const unsigned char* p = static_cast<const unsigned char*>(data);
+  const unsigned char* end = p + len;
+  uint64_t h;
+  if (len >= 32) {
+    uint64_t v1 = seed + kXxP1 + kXxP2, v2 = seed + kXxP2, v3 = seed, v4 = seed - kXxP1;
+    for (; end - p >= 32; p += 32) {
+      v1 = xx_round(v1, xx_read64(p));
+      v2 = xx_round(v2, xx_read64(p + 8));
+      v3 = xx_round(v3, xx_read64(p + 16));
+      v4 = xx_round(v4, xx_read64(p + 24));
+    }
+    h = xx_rotl(v1, 1) + xx_rotl(v2, 7) + xx_rotl(v3, 12) + xx_rotl(v4, 18);
+    h = xx_merge(h, v1);
+    h = xx_merge(h, v2);
+    h = xx_merge(h, v3);
+    h = xx_merge(h, v4);
+  } else {
+    h = seed + kXxP5;
+  }
+  h += static_cast<uint64_t>(len);
+  for (; end - p >= 8; p += 8) h = xx_rotl(h ^ xx_round(0, xx_read64(p)), 27) * kXxP1 + kXxP4;
+  if (end - p >= 4) {
+    h = xx_rotl(h ^ (static_cast<uint64_t>(xx_read32(p)) * kXxP1), 23) * kXxP2 + kXxP3;
+    p += 4;
+  }
+  for (; p < end; ++p) h = xx_rotl(h ^ (static_cast<uint64_t>(*p) * kXxP5), 11) * kXxP1;
+  h ^= h >> 33;
+  h *= kXxP2;
+  h ^= h >> 29;
+  h *= kXxP3;
+  h ^= h >> 32;
+  return h;
+}
+
 int opc_take_device_error(int32_t device, int32_t* code) {
   if (!code) return fail(OPC_ERR_INVALID, "opc_take_device_error: code is NULL");
   int prev = 0;

@@ -10,6 +10,10 @@ Differences from the reference, all fixes that keep the on-disk layout:
     rescan of the file per call (bf2.py:300-328).  The file is memory-mapped.
   * The file header is parsed from however many bytes it needs (the reference reads a fixed
     1024 bytes, bf2.py:181, and fails on longer model metadata).
+  * Optionally (``BF2Writer.write(..., checksum=True)``) the file ends with the XXH64 checksum
+    that the reference's format description promises (header.py:26) and the file header's flags
+    say so; the reader then verifies it.  A reader that ignores the flag (the reference's) reads
+    such a file unchanged: layers are found by their own offsets.
 """
 
 from __future__ import annotations
@@ -22,7 +26,18 @@ from typing import BinaryIO, Dict, Optional, Tuple
 import numpy as np
 import torch
 
-from .header import HEADER_SIZE, BF2Header, LayerFormat, LayerType
+import ctypes
+
+from .header import CHECKSUM_BYTES, FLAG_CHECKSUM, HEADER_SIZE, BF2Header, LayerFormat, LayerType
+
+
+def xxh64(data, seed: int = 0) -> int:
+    """XXH64 of a bytes-like object or a contiguous numpy array (the C library's opc_xxh64)."""
+    from .. import _lib
+
+    a = np.frombuffer(data, dtype=np.uint8) if not isinstance(data, np.ndarray) else data.reshape(-1).view(np.uint8)
+    ptr = a.ctypes.data_as(ctypes.c_void_p) if a.size else None
+    return int(_lib.load().opc_xxh64(ptr, a.size, seed))
 
 
 def _np(t) -> np.ndarray:
@@ -38,15 +53,24 @@ class BF2Writer:
         self.path = Path(path)
         self.file: Optional[BinaryIO] = None
 
-    def write(self, layers: Dict[str, dict], model_config: dict, quantize_config: dict, progress: bool = True):
+    def write(self, layers: Dict[str, dict], model_config: dict, quantize_config: dict, progress: bool = True,
+              checksum: bool = False):
+        """Write the layers; ``checksum`` appends the XXH64 trailer and sets FLAG_CHECKSUM."""
         items = [(k, v) for k, v in layers.items() if not k.startswith("_")]
-        header = BF2Header(model_config=model_config, quantize_config=quantize_config, layer_count=len(items))
+        header = BF2Header(model_config=model_config, quantize_config=quantize_config, layer_count=len(items),
+                           flags=FLAG_CHECKSUM if checksum else 0)
         self.file = open(self.path, "w+b")
         try:
             self.file.write(header.pack())
             for name, layer in items:
                 self._write_layer(name, layer)
             size = self.file.tell()
+            if checksum:
+                self.file.flush()
+                with mmap.mmap(self.file.fileno(), 0, access=mmap.ACCESS_READ) as mm:
+                    digest = xxh64(mm)
+                self.file.write(digest.to_bytes(CHECKSUM_BYTES, "little"))
+                size += CHECKSUM_BYTES
         finally:
             self.file.close()
             self.file = None
@@ -103,18 +127,38 @@ class BF2Writer:
 class BF2Reader:
     """Memory-mapped .bf2 reader (mirrors opacc1ty.format.bf2.BF2Reader)."""
 
-    def __init__(self, path: str):
+    def __init__(self, path: str, verify_checksum: bool = True):
         self.path = Path(path)
         self._fh = open(self.path, "rb")
         size = os.fstat(self._fh.fileno()).st_size
-        self._size = size
         self._mm = mmap.mmap(self._fh.fileno(), 0, access=mmap.ACCESS_READ) if size else b""
         self.header, self._data_start = BF2Header.unpack(self._mm[: min(size, 1 << 20)] if size else b"")
-        if self._data_start > size:
+        self.has_checksum = bool(self.header.flags & FLAG_CHECKSUM)
+        # the layers end where the checksum trailer (if any) begins
+        self._size = size - CHECKSUM_BYTES if self.has_checksum else size
+        if self._data_start > self._size:
             raise ValueError("BF2 header runs past the end of the file")
         # name -> (LayerFormat, header position, id width in bytes)
         self._index: Dict[str, Tuple[LayerFormat, int, int]] = {}
         self._build_index()
+        self.checksum_ok: Optional[bool] = None
+        if self.has_checksum and verify_checksum:
+            self.verify()
+
+    def checksum(self) -> Tuple[int, int]:
+        """(stored, computed) XXH64 of a file written with FLAG_CHECKSUM."""
+        if not self.has_checksum:
+            raise ValueError(f"{self.path}: written without a checksum")
+        stored = int.from_bytes(bytes(self._mm[self._size:self._size + CHECKSUM_BYTES]), "little")
+        return stored, xxh64(memoryview(self._mm)[: self._size])
+
+    def verify(self) -> bool:
+        """Check the trailer; raises ValueError when the file does not match it."""
+        stored, computed = self.checksum()
+        self.checksum_ok = stored == computed
+        if not self.checksum_ok:
+            raise ValueError(f"{self.path}: checksum mismatch (stored {stored:016x}, computed {computed:016x})")
+        return True
 
     # -- index ---------------------------------------------------------------------------
     def _parse_at(self, pos: int) -> Optional[Tuple[LayerFormat, int]]:

@@ -23,6 +23,11 @@ from typing import Tuple
 MAGIC = b"BF2\x00"
 VERSION = 1
 HEADER_SIZE = 64
+# File-header flag: the file ends with the XXH64 checksum (seed 0, little-endian u64) of every
+# byte before it, the trailer the reference's format description lists (header.py:26) but its
+# writer never emits.  Without the flag a file is byte-identical to the reference writer's.
+FLAG_CHECKSUM = 0x1
+CHECKSUM_BYTES = 8
 _LAYER_STRUCT = struct.Struct("<H B I I I B B H Q Q Q Q 13s")
 _FILE_PREFIX = struct.Struct("<4s I I I")
 _U32 = struct.Struct("<I")

@@ -28,6 +28,7 @@ def test_info_reads_the_reference_file():
     assert res.exit_code == 0, res.output
     d = json.loads(res.output)
     assert d["n_layers"] >= 1 and d["layers"]
+    assert d["checksum"] == "absent"   # the reference writer emits no trailer
 
 
 @pytest.mark.gpu

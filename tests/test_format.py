@@ -123,3 +123,43 @@ def test_file_size_much_smaller_than_fp16(tmp_path):
     p = tmp_path / "big.bf2"
     BF2Writer(str(p)).write(layers, {"architecture": "llama"}, {"bits": 2}, progress=False)
     assert p.stat().st_size < 8 * 256 * 256 * 2 * 0.3
+
+
+def test_xxh64_known_answers():
+    from opac1ty_b200.format import xxh64
+
+    # published XXH64 values (seed 0)
+    assert xxh64(b"") == 0xEF46DB3751D8E999
+    assert xxh64(b"a") == 0xD24EC4F1A98C6E5B
+    assert xxh64(b"abc") == 0x44BC2CF5AD770999
+    assert xxh64(b"Nobody inspects the spammish repetition") == 0xFBCEA83C8A378BF1
+    data = np.arange(1000, dtype=np.uint8)
+    assert xxh64(data) == xxh64(data.tobytes()) and xxh64(data, seed=1) != xxh64(data)
+
+
+def test_checksum_trailer_roundtrip_and_corruption(tmp_path):
+    from opac1ty_b200.format import CHECKSUM_BYTES, FLAG_CHECKSUM, xxh64
+
+    plain, summed = tmp_path / "plain.bf2", tmp_path / "summed.bf2"
+    BF2Writer(str(plain)).write(_layers(), {"m": 1}, {"q": 2}, progress=False)
+    BF2Writer(str(summed)).write(_layers(), {"m": 1}, {"q": 2}, progress=False, checksum=True)
+    a, b = plain.read_bytes(), summed.read_bytes()
+    # same layers at the same offsets; only the flags word and the 8-byte trailer differ
+    assert len(b) == len(a) + CHECKSUM_BYTES
+    assert b[:8] == a[:8] and b[12:len(a)] == a[12:]
+    assert int.from_bytes(b[8:12], "little") == FLAG_CHECKSUM
+    assert int.from_bytes(b[len(a):], "little") == xxh64(b[:len(a)])
+    with BF2Reader(str(summed)) as r, BF2Reader(str(plain)) as rp:
+        assert r.has_checksum and r.checksum_ok and not rp.has_checksum
+        for name in rp.layer_names():
+            x, y = r.load_layer(name), rp.load_layer(name)
+            for k in x:
+                if isinstance(x[k], torch.Tensor):
+                    assert torch.equal(x[k], y[k]), (name, k)
+    bad = bytearray(b)
+    bad[len(a) // 2] ^= 0x10
+    (tmp_path / "bad.bf2").write_bytes(bytes(bad))
+    with pytest.raises(ValueError, match="checksum mismatch"):
+        BF2Reader(str(tmp_path / "bad.bf2"))
+    with BF2Reader(str(tmp_path / "bad.bf2"), verify_checksum=False) as r:   # opt out: still readable
+        assert r.checksum_ok is None and len(r.layer_names()) == 3
