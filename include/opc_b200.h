@@ -249,13 +249,15 @@ int32_t opc_chain_form(const opc_chain* chain);
 int opc_chain_launch(opc_chain* chain, void* stream);
 int opc_chain_destroy(opc_chain* chain);
 /* Tracing: with a device buffer of opc_chain_trace_bytes() set, every launch records per step
- * and per CTA eight %globaltimer stamps (ns).  Barrier form, taken by the CTA's first consumer
+ * and per CTA %globaltimer stamps (ns).  Barrier form, taken by the CTA's first consumer
  * thread: step start, setup done, first poll of its x words done, x complete, max barrier passed,
  * digits stored, x staged, its own units done.  Dataflow form: [0] the staging warp begins the
  * step, [1] it holds every block of x, [2] consumer warp 0 begins the step, [3] warp 0's units
  * done, [4] / [5] the staging warp's first / last block arrival, [6] warp 0 starts waiting for
- * its first chunk's x blocks (0 if it did not wait), [7] it has them.  Layout [step][cta][8]
- * uint64; NULL turns tracing off.  opc_chain_grid() is the number of CTAs (one per SM). */
+ * its first chunk's x blocks (0 if it did not wait), [7] it has them.  Barrier form also: [8 + w]
+ * consumer warp w finished its units and row writes of the step.  Layout [step][cta][24] uint64
+ * (unused slots stay as the caller left them); NULL turns tracing off.  opc_chain_grid() is the
+ * number of CTAs (one per SM). */
 size_t opc_chain_trace_bytes(const opc_chain* chain);
 /* Options: OPC_CHAIN_L2_PREFETCH (default 0): stream the weights with an L2 evict-first policy
  * (measured no faster on the Llama-3.1-8B decode step, kept as an option). */

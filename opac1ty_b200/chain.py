@@ -20,6 +20,8 @@ from . import _lib
 from . import layer as L
 
 
+# stamps per step and CTA in a trace buffer: 8 phase stamps, then one per consumer warp
+TRACE_SLOTS = 24
 FORMS = {"auto": _lib.OPC_CHAIN_FORM_AUTO, "barrier": _lib.OPC_CHAIN_FORM_BARRIER,
          "dataflow": _lib.OPC_CHAIN_FORM_DATAFLOW}
 
@@ -68,12 +70,12 @@ class Chain:
         _lib.check(lib.opc_chain_launch(self._handle, stream))
 
     def enable_trace(self) -> torch.Tensor:
-        """Record per-step, per-CTA phase stamps on every launch; returns the [steps, grid, 8]
+        """Record per-step, per-CTA phase stamps on every launch; returns the [steps, grid, 24]
         int64 buffer (ns of %globaltimer, see opc_chain_set_trace in include/opc_b200.h)."""
         lib = _lib.load()
         n = int(lib.opc_chain_trace_bytes(self._handle)) // 8
         grid = int(lib.opc_chain_grid(self._handle))
-        self._trace = torch.zeros(self.n_steps, grid, 8, dtype=torch.int64, device=self.device)
+        self._trace = torch.zeros(self.n_steps, grid, TRACE_SLOTS, dtype=torch.int64, device=self.device)
         assert self._trace.numel() == n
         _lib.check(lib.opc_chain_set_trace(self._handle, self._trace.data_ptr()))
         return self._trace

@@ -267,8 +267,11 @@ def _chain_phases(st) -> dict:
     for _ in range(3):
         st.step_eager()
     torch.cuda.synchronize(st.device)
-    t = tr.cpu().numpy().astype(np.int64)  # [steps, grid, 8] ns
+    full = tr.cpu().numpy().astype(np.int64)  # [steps, grid, 24] ns
     st.chain.disable_trace()
+    t = full[:, :, :8]
+    warps = full[:, :, 8:23].astype(np.float64)  # [steps, grid, 15] each consumer warp's end of the step
+    warps[warps == 0] = np.nan
     names = ["qkv", "o", "gate_up", "down"]
     n_blocks = t.shape[0] // 4
     inner = range(1, n_blocks - 1) if n_blocks > 2 else range(n_blocks)
@@ -279,10 +282,19 @@ def _chain_phases(st) -> dict:
         d = np.diff(t[rows], axis=2) / 1000.0
         med = np.median(d, axis=1).mean(axis=0)
         spans = [(starts[r + 1] - starts[r]) / 1000.0 for r in rows if r + 1 < t.shape[0]]
+        # per CTA: first and last consumer warp done; across CTAs: the last CTA's lag behind the median
+        first = np.nanmin(warps[rows], axis=2)
+        last = np.nanmax(warps[rows], axis=2)
+        intra = np.median(last - first, axis=1).mean() / 1000.0
+        lag = (np.max(last, axis=1) - np.median(last, axis=1)).mean() / 1000.0
+        # the slowest CTAs: indices of the 5 latest-finishing CTAs (first inner block)
+        slow = np.argsort(last[0])[-5:][::-1].tolist()
         res[name] = {"setup": round(float(med[0]), 2), "pre_poll": round(float(med[1]), 2),
                      "x_wait": round(float(med[2]), 2), "max_barrier": round(float(med[3]), 2),
                      "digits": round(float(med[4]), 2), "staged": round(float(med[5]), 2),
                      "units": round(float(med[6]), 2),
+                     "warp_spread_in_cta": round(float(intra), 2), "last_cta_lag": round(float(lag), 2),
+                     "slowest_ctas": slow,
                      "span": round(float(np.mean(spans)), 2) if spans else None}
     return res
 
@@ -301,7 +313,7 @@ def _chain_phases_dataflow(st) -> dict:
     for _ in range(3):
         st.step_eager()
     torch.cuda.synchronize(st.device)
-    t = tr.cpu().numpy().astype(np.int64)  # [steps, grid, 8] ns
+    t = tr.cpu().numpy().astype(np.int64)[:, :, :8]  # [steps, grid, 8] ns
     st.chain.disable_trace()
     names = ["qkv", "o", "gate_up", "down"]
     n_blocks = t.shape[0] // 4

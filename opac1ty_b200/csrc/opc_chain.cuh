@@ -17,10 +17,12 @@
 //    y (what callers read) unless a later layer of the chain overwrites that buffer.
 //  * Packed row tiles are handed out whole (CTA c gets tiles round(c*MT/G) .. round((c+1)*MT/G)),
 //    so a tile is split only between warps of one CTA and reduced in shared memory.  Outlier
-//    tiles (16 fp16 rows, 8x heavier per row) are split evenly across all CTAs; their partial
-//    dot products are added exactly into int64 accumulators, each contributing warp then counts
-//    itself in (release), and the warp completing the tile's count (acquire) takes the sums,
-//    resets them and publishes the tile's rows.
+//    tiles (16 fp16 rows, 8x heavier per row) are split evenly across all CTAs.  Partial dot
+//    products of a shared tile are added exactly into int64 accumulators that also count the
+//    contributions (2^52 per contributor above the sum), one returning atomic per row: the
+//    contributor whose addition completes the count holds the exact total and publishes the row.
+//  * Within a CTA, packed warps split its units in proportion to their speed (the warps of an SM
+//    sub-partition share its issue slots; host-computed).
 //
 // Row sharding over `world` GPUs (one process per GPU): every rank holds a contiguous shard of
 // each layer's output rows and computes it from the full x.  There is no all-gather: a rank
@@ -52,8 +54,8 @@ struct ChainLayer {
   const int32_t* oexp;           // [OT*16]
   const __half* x;               // layer 0: the chain input (fp16)
   const uint32_t* xw;            // layer >= 1: the previous layer's exchange words (this rank's copy)
-  unsigned long long* acc;       // [OT*16][2] outlier-slot dot products (zero between launches)
-  int32_t* ocnt;                 // [OT] contributions received per outlier tile (zero between launches)
+  unsigned long long* acc;       // [OT*16][2] outlier-slot dot products, count-carrying (zero between launches)
+  const void* unused_;           // keeps the descriptor a whole number of 16-byte pieces
   const int32_t* onc;            // [OT] warps contributing to each outlier tile
   __half* y_peer[kMaxRanks];     // this rank's first row in rank p's fp16 copy of the full output
   uint32_t* yw_peer[kMaxRanks];  // this rank's first row in rank p's exchange words of it
@@ -67,10 +69,12 @@ struct ChainLayer {
 
 // Per layer and CTA, the host-computed shares of its consumer warps, so the kernel does no integer
 // division: int32 [0..14] first unit of warp w, [15] packed warps wp, [16..30] end unit of warp w,
-// [31] the CTA's first packed tile, [32..46] first segment of warp w (0 for an empty range).
-constexpr int kChainShareInts = 48;
+// [31] the CTA's first packed tile, [32..46] first segment of warp w (0 for an empty range),
+// [48..51] one byte per warp: the packed warps of the CTA sharing the warp's first packed tile
+// (low nibble) and its last one (high nibble).
+constexpr int kChainShareInts = 52;
 constexpr int kChainSharePieces = kChainShareInts / 4;  // int4 pieces
-constexpr int kShU0 = 0, kShWp = 15, kShU1 = 16, kShTile0 = 31, kShSeg0 = 32;
+constexpr int kShU0 = 0, kShWp = 15, kShU1 = 16, kShTile0 = 31, kShSeg0 = 32, kShNeed = 48;
 
 static_assert(sizeof(ChainLayer) % 16 == 0, "ChainLayer is copied in 16-byte pieces");
 static_assert(sizeof(ChainLayer) / 16 + kChainSharePieces <= 32, "one warp copies a descriptor and a CTA share");
@@ -82,16 +86,17 @@ struct ChainArgs {
   unsigned int* sync;        // [world][grid] flags of every rank's CTAs, in this rank's memory
   unsigned int* sync_peer[kMaxRanks];  // rank p's flag array (sync_peer[rank] == sync)
   unsigned int* epoch;       // [0] launches completed (bit 31: poisoned), [1] CTAs finished
-  unsigned long long* trace; // optional [n_layers][grid][8] globaltimer stamps (ns) per CTA,
-                             // taken by its first consumer thread: layer start, setup done,
+  unsigned long long* trace; // optional [n_layers][grid][24] globaltimer stamps (ns) per CTA:
+                             // [0..7] by its first consumer thread: layer start, setup done,
                              // first x poll done, x complete, max barrier passed, digits
-                             // stored, x staged, own units done
+                             // stored, x staged, own units done; [8 + w] consumer warp w's
+                             // units (and row writes) done
   int32_t n_layers, batch, stages, xs_bytes;
   uint32_t negz;
   int32_t l2_prefetch;       // stream weights with an L2 evict-first policy
   int32_t rank, world;
 };
-constexpr int kChainTracePhases = 8;
+constexpr int kChainTracePhases = 24;  // 8 phase stamps, then one per consumer warp (units done)
 constexpr uint32_t kChainPoisoned = 0x80000000u;
 constexpr uint32_t kChainTagPeriod = 65535u;  // tags run 1..65535
 constexpr int32_t kChainMaxLayers = 65534;    // so consecutive launches never share a layer's tag
@@ -335,8 +340,7 @@ struct ChainShared {
   ChainLayer layer[2];                    // descriptors of layers j (slot j&1) and j+1
   int4 part[2][kChainSharePieces];        // this CTA's warp shares of layers j and j+1
   uint32_t amax_bits[2][kQMaxBatch];      // staging: max |x| (float bits) of layers with parity 0 / 1
-  unsigned long long tile_acc[kChainSplitSlots][kTileRows][kQMaxBatch];  // split packed tiles
-  int32_t tile_cnt[kChainSplitSlots];
+  unsigned long long tile_acc[kChainSplitSlots][kTileRows][kQMaxBatch];  // split packed tiles (count-carrying)
   int32_t abort;
   uint32_t epoch;
 };
@@ -369,90 +373,103 @@ __device__ __noinline__ void chain_write_rows(const ChainLayer& L, int P, int B,
   }
 }
 
-// A warp's partial dot products of a packed tile (this CTA's local tile lt), shared with other
-// warps of the CTA: added exactly into the tile's shared int64 accumulators; the warp that
-// completes the count of contributors writes the tile's rows and clears the slot.
-template <bool sys>
-__device__ __forceinline__ void chain_split_add(ChainShared* sh, const ChainLayer& L, int P, int B, int r0, int r1, int e0,
-                                             int e1, long long t0, long long t1, int lt, int n_contrib, int lane,
-                                             int g, int q, int ex0, int ex1, uint32_t tag) {
-  const int slot = lt & (kChainSplitSlots - 1);
-  const int b = q >> 1;
-  const bool live = !(q & 1) && b < B;
-  if (live) {
-    atomicAdd(&sh->tile_acc[slot][g][b], static_cast<unsigned long long>(t0));
-    atomicAdd(&sh->tile_acc[slot][g + 8][b], static_cast<unsigned long long>(t1));
-  }
-  __threadfence_block();
-  __syncwarp();
-  int old = 0;
-  if (lane == 0) old = atomicAdd(&sh->tile_cnt[slot], 1);
-  old = __shfl_sync(0xffffffffu, old, 0);
-  if (old != n_contrib - 1) return;
-  __threadfence_block();
-  long long f0 = 0, f1 = 0;
-  if (live) {
-    f0 = static_cast<long long>(atomicExch(&sh->tile_acc[slot][g][b], 0ull));
-    f1 = static_cast<long long>(atomicExch(&sh->tile_acc[slot][g + 8][b], 0ull));
-  }
-  if (lane == 0) sh->tile_cnt[slot] = 0;
-  chain_write_rows<sys>(L, P, B, r0, r1, e0, e1, f0, f1, q, ex0, ex1, tag);
+// Reductions of partial dot products carry their own completion count: every contributor adds
+// 2^52 + t with ONE returning atomic per row, t its exact partial dot product.  Every partial sum of
+// a row is below 2^51 in magnitude (|centroid integer| <= 2^14, |x integer| < 2^22, K <= 2^15,
+// host-checked), so the top 12 bits count the contributions (up to 4095, host-checked) and the old
+// value tells a contributor how many came before it and -- for the one that completes the count --
+// the exact total.  No fence, no separate counter, no second round trip; the completing lane resets
+// the word to zero for the next launch and publishes the row.
+constexpr int kCountShift = 52;
+constexpr unsigned long long kCountOne = 1ull << kCountShift;
+constexpr int kMaxContributors = 4095;
+__device__ __forceinline__ bool count_add_complete(unsigned long long old, unsigned long long add, int need,
+                                                   long long* total) {
+  const unsigned long long biased = old + add + (kCountOne >> 1);
+  *total = static_cast<long long>(biased & (kCountOne - 1ull)) - static_cast<long long>(kCountOne >> 1);
+  return static_cast<int>(biased >> kCountShift) == need;
 }
 
-// Outlier tile tt done for this warp: add its partials (rows r0, r1 = the slots' rows, -1 =
-// padding) into the slot accumulators and count it in (release); the warp completing the tile's
-// count (acquire) takes the sums, clears them and publishes the tile's rows.
+// A warp's partial dot products of a packed tile (this CTA's local tile lt) shared with other warps
+// of the CTA (`need` of them, counted on the way in): added into the tile's shared accumulators;
+// the lane completing a row's count writes that row.
+template <bool sys>
+__device__ __forceinline__ void chain_split_add(ChainShared* sh, const ChainLayer& L, int P, int B, int r0, int r1, int e0,
+                                             int e1, long long t0, long long t1, int lt, int need, int g, int q,
+                                             int ex0, int ex1, uint32_t tag) {
+  const int slot = lt & (kChainSplitSlots - 1);
+  const int b = q >> 1;
+  int w0 = -1, w1 = -1;
+  long long f0 = 0, f1 = 0;
+  bool any = false;
+  if (!(q & 1) && b < B) {
+    unsigned long long* a0 = &sh->tile_acc[slot][g][b];
+    unsigned long long* a1 = &sh->tile_acc[slot][g + 8][b];
+    const unsigned long long d0 = kCountOne + static_cast<unsigned long long>(t0);
+    const unsigned long long d1 = kCountOne + static_cast<unsigned long long>(t1);
+    const unsigned long long o0 = atomicAdd(a0, d0), o1 = atomicAdd(a1, d1);
+    if (count_add_complete(o0, d0, need, &f0)) {
+      *a0 = 0ull;
+      w0 = r0;
+      any = true;
+    }
+    if (count_add_complete(o1, d1, need, &f1)) {
+      *a1 = 0ull;
+      w1 = r1;
+      any = true;
+    }
+  }
+  if (__any_sync(0xffffffffu, any)) chain_write_rows<sys>(L, P, B, w0, w1, e0, e1, f0, f1, q, ex0, ex1, tag);
+}
+
+// Outlier tile tt done for this warp: its partials (rows r0, r1 = the slots' rows, -1 = padding)
+// go into the slots' global accumulators, counted like the packed split tiles; the lane completing
+// a slot's count (every warp contributing to the tile, host-counted) publishes its row.
 template <bool sys>
 __device__ __forceinline__ void chain_flush_outlier(const ChainLayer& L, int P, int B, int r0, int r1, int e0, int e1,
-                                                 long long t0, long long t1, int tt, int lane, int g, int q, int ex0,
-                                                 int ex1, uint32_t tag) {
+                                                 long long t0, long long t1, int tt, int g, int q, int ex0, int ex1,
+                                                 uint32_t tag) {
   const int b = q >> 1;
-  const bool live = !(q & 1) && b < B;
-  const int s0 = tt * kTileRows + g, s1 = s0 + 8;
-  const int need = static_cast<int>(ld_nc_u32(L.onc + tt));  // in flight during the adds
-  if (live) {
-    if (r0 >= 0) atomicAdd(L.acc + 2 * s0 + b, static_cast<unsigned long long>(t0));
-    if (r1 >= 0) atomicAdd(L.acc + 2 * s1 + b, static_cast<unsigned long long>(t1));
-  }
-  __syncwarp();  // the lanes' adds are ordered before lane 0's count below
-  // one acq_rel atomic: releases the warp's adds and, for the completing warp, acquires everyone
-  // else's (measured 5% faster per decode step than a fence on each side of a relaxed atomic)
-  int old = 0;
-  if (lane == 0) old = atom_add_acq_rel_gpu(L.ocnt + tt, 1);
-  old = __shfl_sync(0xffffffffu, old, 0);
-  __syncwarp();
-  if (old != need - 1) return;
+  int w0 = -1, w1 = -1;
   long long f0 = 0, f1 = 0;
-  if (live) {
-    if (r0 >= 0) f0 = static_cast<long long>(atomicExch(L.acc + 2 * s0 + b, 0ull));
-    if (r1 >= 0) f1 = static_cast<long long>(atomicExch(L.acc + 2 * s1 + b, 0ull));
+  bool any = false;
+  if (!(q & 1) && b < B) {
+    const int need = static_cast<int>(ld_nc_u32(L.onc + tt));  // in flight with the atomics
+    const int s0 = tt * kTileRows + g, s1 = s0 + 8;
+    unsigned long long* a0 = L.acc + 2 * s0 + b;
+    unsigned long long* a1 = L.acc + 2 * s1 + b;
+    const unsigned long long d0 = kCountOne + static_cast<unsigned long long>(t0);
+    const unsigned long long d1 = kCountOne + static_cast<unsigned long long>(t1);
+    unsigned long long o0 = 0, o1 = 0;
+    if (r0 >= 0) o0 = atomicAdd(a0, d0);
+    if (r1 >= 0) o1 = atomicAdd(a1, d1);
+    if (r0 >= 0 && count_add_complete(o0, d0, need, &f0)) {
+      *a0 = 0ull;
+      w0 = r0;
+      any = true;
+    }
+    if (r1 >= 0 && count_add_complete(o1, d1, need, &f1)) {
+      *a1 = 0ull;
+      w1 = r1;
+      any = true;
+    }
   }
-  if (lane == 0) st_relaxed_u32(reinterpret_cast<unsigned int*>(L.ocnt + tt), 0u);
-  chain_write_rows<sys>(L, P, B, r0, r1, e0, e1, f0, f1, q, ex0, ex1, tag);
+  if (__any_sync(0xffffffffu, any)) chain_write_rows<sys>(L, P, B, w0, w1, e0, e1, f0, f1, q, ex0, ex1, tag);
 }
 
 // A finished segment of a warp's range (one call site in the kernel): outlier tiles count in,
-// packed tiles the warp covered whole are written, shared ones go through the CTA's reduction.
-// `sr` is the CTA's warp-share record of this layer (shared memory); the contributors of a split
-// tile are the packed warps whose ranges meet it.
+// packed tiles the warp covered whole are written, shared ones go through the CTA's reduction
+// (`need` = the packed warps whose ranges meet the tile, counted at the layer's setup).
 template <bool sys>
 __device__ __forceinline__ void chain_finish_segment(ChainShared* sh, const ChainLayer& L, int P, int B, int r0, int r1,
                                                   int e0, int e1, long long t0, long long t1, int seg, int whole,
-                                                  const int32_t* sr, int lane, int g, int q, int ex0, int ex1,
-                                                  uint32_t tag) {
+                                                  int need, int tile0, int g, int q, int ex0, int ex1, uint32_t tag) {
   if (seg >= L.MT) {
-    chain_flush_outlier<sys>(L, P, B, r0, r1, e0, e1, t0, t1, seg - L.MT, lane, g, q, ex0, ex1, tag);
+    chain_flush_outlier<sys>(L, P, B, r0, r1, e0, e1, t0, t1, seg - L.MT, g, q, ex0, ex1, tag);
   } else if (whole) {
     chain_write_rows<sys>(L, P, B, r0, r1, e0, e1, t0, t1, q, ex0, ex1, tag);
   } else {
-    const int32_t tb = seg * L.KT, te = tb + L.KT;
-    const int wp = sr[kShWp];
-    int n_contrib = 0;
-    for (int w = 0; w < wp; ++w) {
-      const int32_t a = sr[kShU0 + w], b = sr[kShU1 + w];
-      n_contrib += (a < b && a < te && b > tb) ? 1 : 0;
-    }
-    chain_split_add<sys>(sh, L, P, B, r0, r1, e0, e1, t0, t1, seg - sr[kShTile0], n_contrib, lane, g, q, ex0, ex1, tag);
+    chain_split_add<sys>(sh, L, P, B, r0, r1, e0, e1, t0, t1, seg - tile0, need, g, q, ex0, ex1, tag);
   }
 }
 
@@ -486,7 +503,6 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
   }
   for (int i = threadIdx.x; i < kChainSplitSlots * kTileRows * kQMaxBatch; i += blockDim.x)
     (&sh->tile_acc[0][0][0])[i] = 0ull;
-  for (int i = threadIdx.x; i < kChainSplitSlots; i += blockDim.x) sh->tile_cnt[i] = 0;
   if (threadIdx.x < 2 * kQMaxBatch) (&sh->amax_bits[0][0])[threadIdx.x] = 0u;
   if (threadIdx.x < sizeof(ChainLayer) / 16 && args.n_layers > 0)
     reinterpret_cast<uint4*>(&sh->layer[0])[threadIdx.x] = reinterpret_cast<const uint4*>(args.layers)[threadIdx.x];
@@ -674,6 +690,11 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
       cur = chain_load_meta(qa, cc.seg, g);
       nxt = chain_load_meta(qa, min(cc.seg + 1, L.MT + L.OT - 1), g);
     }
+    // contributors (packed warps of this CTA) of the first and the last packed tile of this warp's
+    // range -- the only ones it may share with other warps (host-counted)
+    const int need_nb = reinterpret_cast<const uint8_t*>(sr + kShNeed)[warp];
+    const int tile0 = sr[kShTile0];
+    const int32_t seg_first = cc.seg;
     // next layer's descriptor and this CTA's share of it: loaded now, stored to shared memory
     // once every warp is past this layer's first staging barrier (nobody reads the slots' old
     // contents after that)
@@ -851,14 +872,19 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
             }
           }
         } else {
+          // outlier units, two per iteration (one per accumulator chain), not unrolled further:
+          // they are light, and the smaller loop keeps the kernel's code small
+#pragma unroll 1
+          for (int i = 0; i < cnt; i += 2) {
 #pragma unroll
-          for (int i = 0; i < kQChunkUnits; ++i) {
-            if (i < cnt) {
-              const uint4 av = lds128(stage + i * kUnitBytes);
-              const int32_t s = k0 + i;
-              const uint32_t bv = lds32(xo + static_cast<uint32_t>(s >> 3) * kts + (s & 7) * 16);
-              imma16816(A.h[i & 1], av.x, av.y, bv);
-              imma16816(A.l[i & 1], av.z, av.w, bv);
+            for (int h = 0; h < 2; ++h) {
+              if (i + h < cnt) {
+                const uint4 av = lds128(stage + (i + h) * kUnitBytes);
+                const int32_t s = k0 + i + h;
+                const uint32_t bv = lds32(xo + static_cast<uint32_t>(s >> 3) * kts + (s & 7) * 16);
+                imma16816(A.h[h], av.x, av.y, bv);
+                imma16816(A.l[h], av.z, av.w, bv);
+              }
             }
           }
         }
@@ -879,7 +905,8 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
             r0 = (r0 < L.M && !((mask >> g) & 1u)) ? r0 : -1;
           }
           chain_finish_segment<sys>(sh, L, P, B, r0, r1, cur.e[0], cur.e[1], t[0], t[1], cc.seg,
-                                    cc.begin >= u0 && cc.end <= u1, sr, lane, g, q, ex0, ex1, tag);
+                                    cc.begin >= u0 && cc.end <= u1, cc.seg == seg_first ? (need_nb & 15) : (need_nb >> 4),
+                                    tile0, g, q, ex0, ex1, tag);
           if (cc.u == u1) break;
           zero_accq(A);
           chain_next_segment(L, cc);
@@ -894,6 +921,7 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
       }
     }
     if (tr && tid == 0) tr[7] = globaltimer_ns();
+    if (tr && lane == 0) tr[8 + warp] = globaltimer_ns();
   }
 
   // ---- end of the launch.  Several ranks: a last barrier, so that no rank starts its next

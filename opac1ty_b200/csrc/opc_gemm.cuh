@@ -4,18 +4,24 @@
 // Reference: kernels/dequant_gemm.metal:34-149 (dequantize a weight tile into threadgroup memory,
 // then a scalar multiply-accumulate); semantics opacc1ty/export/converter.py:26-67 + matmul.
 //
-// One CTA computes a 128-row x N-token tile (N = 256, or 128 for small problems), K in stages of 64:
-//   warp 0      TMA: the X tile (N tokens x 64 fp16, 128-byte swizzle) and the 8 packed units
-//               of the tile's 8 row tiles (bulk copies, no multicast) into the stage
-//   warp 1      allocates N TMEM columns; one lane issues 4 tcgen05.mma (K = 16 each) per
-//               stage and commits them to the stage's "empty" mbarrier
-//   warps 2..5  one weight row per thread: decode the row's 64 indices of the stage through its
-//               fp16 codebook (PRMT lookups) into the A tile, written in the canonical K-major
-//               128-byte-swizzle layout; after the last stage, read the row's 256 accumulators
-//               from TMEM (the warp's TMEM lane quarter) and store Y.
+// Persistent: one CTA per SM walks the output tiles c, c + grid, c + 2 grid, ...  A tile is 128
+// weight rows x N tokens (N = 16..256, chosen by the host from the token count and the SM count),
+// K in stages of 64.  Roles, all pipelined across tile boundaries:
+//   warp 0       TMA (no multicast): the X tile (N tokens x 64 fp16, 128-byte swizzle) and the
+//                packed units of the tile's 8 row tiles (one 2-D copy of 8 x 512 bytes) per stage
+//   warp 1       allocates 2N TMEM columns (two accumulators); one lane issues 4 tcgen05.mma
+//                (K = 16 each) per stage, commits each stage to its "empty" mbarrier and each
+//                finished tile to its accumulator's "full" mbarrier
+//   warps 2..17  decoders, four groups of four warps taking turns by stage (four stages decoded
+//                at once): thread = row r decodes the stage's 64 indices of row r through the
+//                row's fp16 codebook (PRMT lookups) into the A tile, written in the canonical
+//                K-major 128-byte-swizzle layout
+//   warps 18..21 epilogue: read a finished accumulator (each warp its TMEM lane quarter),
+//                round to fp16 and store Y, then hand the accumulator back -- while the MMAs of
+//                the next tile run into the other one
 // Outlier rows have all-zero codebooks, so the packed tiles compute 0 for them and skip their
-// writes; extra CTAs of the same launch (blockIdx.x >= m_tiles) compute them from the row-major
-// outlier copy (A tiles copied instead of decoded) and scatter them to their output rows.
+// writes; dense tiles (after the packed ones) compute them from the row-major outlier copy (A
+// rows copied instead of decoded) and scatter them to their output rows.
 #pragma once
 
 #include <cuda.h>
@@ -25,28 +31,37 @@
 namespace opc {
 
 constexpr int kGmM = 128, kGmK = 64;          // weight rows per tile, K per stage
-constexpr int kGmStages = 4;
-constexpr int kGmThreads = 192;
+constexpr int kGmDecWarps = 16;               // decoder warps: 4 groups of 4 (one of each group per SM sub-partition)
+constexpr int kGmDecGroups = kGmDecWarps / 4; // group i decodes the stages s with s % 4 == i, one row per thread
+constexpr int kGmEpiWarps = 4;                // epilogue warps: one TMEM lane quarter each
+constexpr int kGmDecWarp0 = 2, kGmEpiWarp0 = kGmDecWarp0 + kGmDecWarps;
+constexpr int kGmThreads = (kGmEpiWarp0 + kGmEpiWarps) * 32;
 constexpr int kGmABytes = kGmM * kGmK * 2;   // 16 KB
 constexpr int kGmUBytes = 8 * kUnitBytes;    // 8 row tiles x one unit
-// Token tile N (256, or 128 when 256-token tiles would leave SMs idle): x stage N*64 fp16,
-// N fp32 TMEM columns.
+constexpr int kGmSmemBudget = 227 * 1024 - 1024 - 512;  // dynamic shared memory less slack and barriers
+// Token tile N: x stage N*64 fp16, two accumulators of N fp32 TMEM columns.
 __host__ __device__ constexpr int gm_b_bytes(int N) { return N * kGmK * 2; }
+__host__ __device__ constexpr int gm_stage_bytes(int N) { return kGmABytes + gm_b_bytes(N) + kGmUBytes; }
+__host__ __device__ constexpr int gm_stages(int N) {
+  return kGmSmemBudget / gm_stage_bytes(N) > 8 ? 8 : kGmSmemBudget / gm_stage_bytes(N);
+}
+__host__ __device__ constexpr int gm_tmem_cols(int N) { return 2 * N < 32 ? 32 : 2 * N; }
 __host__ __device__ constexpr size_t gm_smem_bytes(int N) {
-  return 1024 /*alignment slack*/ + kGmStages * (kGmABytes + gm_b_bytes(N) + kGmUBytes) + 256;
+  return 1024 /*alignment slack*/ + static_cast<size_t>(gm_stages(N)) * gm_stage_bytes(N) + 512;
 }
 
 struct GemmArgs {
   const uint8_t* units;        // packed units
   const uint2* cb;             // [M_pad] split fp16 codebooks
   const uint16_t* tile_mask;   // [MT]
-  const __half* dense;         // [n_slots][K_pad] outlier rows (dense mode)
+  const __half* dense;         // [n_slots][K_pad] outlier rows (dense tiles)
   const int32_t* orow;         // [n_slots]
   __half* y;
   int64_t ldy;
   int32_t M, K_pad, MT, KT, n_tok, n_slots;
-  int32_t m_tiles;             // CTAs with blockIdx.x < m_tiles decode packed tiles; the rest copy
-                               // outlier rows (dense A tiles)
+  int32_t m_tiles;             // packed M tiles; M tile indices >= m_tiles are dense (outlier rows)
+  int32_t n_tiles;             // token tiles
+  int32_t tiles;               // (m_tiles + dense tiles) * n_tiles
 };
 
 // UMMA shared-memory descriptor: K-major, 128-byte swizzle, 8-row groups 1024 bytes apart.
@@ -77,7 +92,7 @@ __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// 32 consecutive fp32 columns of this thread's TMEM lane.
+// 32 (or 16) consecutive fp32 columns of this thread's TMEM lane.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t v[32]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,"
@@ -86,6 +101,14 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t v[32]) {
         "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
         "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
         "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t v[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -108,40 +131,43 @@ __device__ __forceinline__ uint32_t sw128_off(int r, int c) {
   return static_cast<uint32_t>(1024 * (r >> 3) + 128 * (r & 7) + 16 * (c ^ (r & 7)));
 }
 
+// tx: x [n_tok][K] fp16, box 64 x N, 128-byte swizzle.  tu: the packed units as a [MT][KT * 512 B]
+// array of 8-byte elements, box 512 B x 8 row tiles (one copy brings a k block of all 8 row tiles).
 template <int kN>
-__global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap tx, const GemmArgs a) {
-  const bool kDense = static_cast<int>(blockIdx.x) >= a.m_tiles;
-  constexpr int kGmBBytes = gm_b_bytes(kN);
-  constexpr int kGmTmemCols = kN;
+__global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap tx,
+                                                             const __grid_constant__ CUtensorMap tu, const GemmArgs a) {
+  constexpr int kBBytes = gm_b_bytes(kN);
+  constexpr int kS = gm_stages(kN);
+  constexpr int kCols = gm_tmem_cols(kN);
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
-  const uint32_t sA = base, sB = sA + kGmStages * kGmABytes, sU = sB + kGmStages * kGmBBytes;
-  const uint32_t bars = sU + kGmStages * kGmUBytes;
-  const uint32_t full_b = bars, afull_b = bars + 8 * kGmStages, empty_b = bars + 16 * kGmStages,
-                 accf_b = bars + 24 * kGmStages, tmem_slot = accf_b + 8;
+  const uint32_t sA = base, sB = sA + kS * kGmABytes, sU = sB + kS * kBBytes;
+  const uint32_t bars = sU + kS * kGmUBytes;
+  const uint32_t full_b = bars, afull_b = bars + 8 * kS, empty_b = bars + 16 * kS;
+  const uint32_t accf_b = bars + 24 * kS, acce_b = accf_b + 16, drain_b = acce_b + 16, tmem_slot = drain_b + 8;
   unsigned char* tmem_slot_ptr = smem_raw + (tmem_slot - raw);
 
   const int warp = __shfl_sync(0xffffffffu, static_cast<int>(threadIdx.x >> 5), 0);
   const int lane = threadIdx.x & 31;
-  const int m0 = (kDense ? static_cast<int>(blockIdx.x) - a.m_tiles : static_cast<int>(blockIdx.x)) * kGmM;
-  const int n0 = blockIdx.y * kN;
+  const int G = static_cast<int>(gridDim.x);
   const int nk = a.K_pad / kGmK;
-  const int t0 = m0 / kTileRows;
-  const int n_rt = kDense ? 0 : min(8, a.MT - t0);  // row tiles with units in this M tile
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kGmStages; ++s) {
+    for (int s = 0; s < kS; ++s) {
       mbar_init(full_b + 8 * s, 1);
-      mbar_init(afull_b + 8 * s, 4);  // one arrival per decoder warp
+      mbar_init(afull_b + 8 * s, 4);  // one arrival per warp of the stage's decoder group
       mbar_init(empty_b + 8 * s, 1);
     }
-    mbar_init(accf_b, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(accf_b + 8 * b, 1);
+      mbar_init(acce_b + 8 * b, kGmEpiWarps);  // one arrival per epilogue warp
+    }
+    mbar_init(drain_b, 1);
     fence_mbar_init();
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tmem_slot),
-                 "r"(kGmTmemCols)
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tmem_slot), "r"(kCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -154,120 +180,174 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_consta
   if (warp == 0) {
     // ---------------------------------------------------------------- producer
     if (lane == 0) {
-      const uint32_t bytes = kGmBBytes + static_cast<uint32_t>(n_rt) * kUnitBytes;
-      for (int s = 0; s < nk && ok; ++s) {
-        const int st = s % kGmStages;
-        if (s >= kGmStages && !mbar_wait_bounded(empty_b + 8 * st, ((s / kGmStages) - 1) & 1)) {
-          ok = false;
-          break;
+      int g = 0;  // stages issued (all tiles)
+      for (int i = blockIdx.x; i < a.tiles && ok; i += G) {
+        const int mi = i / a.n_tiles, n0 = (i - mi * a.n_tiles) * kN;
+        const bool packed = mi < a.m_tiles;
+        // a box past the last row tile is filled with zeros and still counts its full size
+        const uint32_t bytes = kBBytes + (packed ? static_cast<uint32_t>(kGmUBytes) : 0u);
+        for (int s = 0; s < nk; ++s, ++g) {
+          const int st = g % kS;
+          if (g >= kS && !mbar_wait_bounded(empty_b + 8 * st, ((g / kS) - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(full_b + 8 * st, bytes);
+          tma_load_2d(sB + st * kBBytes, &tx, s * kGmK, n0, full_b + 8 * st);
+          // x coordinate: k block s/2 in 8-byte elements (a multiple of 64: 512-byte aligned)
+          if (packed) tma_load_2d(sU + st * kGmUBytes, &tu, (s >> 1) * (kUnitBytes / 8), mi * 8, full_b + 8 * st);
         }
-        mbar_expect_tx(full_b + 8 * st, bytes);
-        tma_load_2d(sB + st * kGmBBytes, &tx, s * kGmK, n0, full_b + 8 * st);
-        for (int i = 0; i < n_rt; ++i)
-          bulk_g2s(sU + st * kGmUBytes + i * kUnitBytes,
-                   a.units + (static_cast<int64_t>(t0 + i) * a.KT + (s >> 1)) * kUnitBytes, kUnitBytes,
-                   full_b + 8 * st);
+      }
+      // copies nobody consumed (a role gave up) land before the CTA exits: wait (bounded) for
+      // the last one issued into each stage
+      for (int st = 0; st < kS && st < g; ++st) {
+        const int last = g - 1 - ((g - 1 - st) % kS);  // last stage counter that used slot st
+        mbar_wait_bounded(full_b + 8 * st, (last / kS) & 1);
       }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      for (int s = 0; s < nk && ok; ++s) {
-        const int st = s % kGmStages;
-        const uint32_t par = (s / kGmStages) & 1;
-        if (!mbar_wait_bounded(full_b + 8 * st, par) || !mbar_wait_bounded(afull_b + 8 * st, par)) {
+      int g = 0, tl = 0;
+      for (int i = blockIdx.x; i < a.tiles && ok; i += G, ++tl) {
+        const int b = tl & 1;
+        // the epilogue has read accumulator b's previous tile
+        if (tl >= 2 && !mbar_wait_bounded(acce_b + 8 * b, ((tl >> 1) - 1) & 1)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint64_t ad = umma_desc_sw128(sA + st * kGmABytes), bd = umma_desc_sw128(sB + st * kGmBBytes);
+        const uint32_t tacc = tmem + static_cast<uint32_t>(b * kN);
+        for (int s = 0; s < nk; ++s, ++g) {
+          const int st = g % kS;
+          const uint32_t par = (g / kS) & 1;
+          if (!mbar_wait_bounded(full_b + 8 * st, par) || !mbar_wait_bounded(afull_b + 8 * st, par)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = umma_desc_sw128(sA + st * kGmABytes), bd = umma_desc_sw128(sB + st * kBBytes);
 #pragma unroll
-        for (int kk = 0; kk < kGmK / 16; ++kk)  // +32 bytes per K = 16 step inside the swizzle atom
-          umma_f16(tmem, ad + 2 * kk, bd + 2 * kk, gm_idesc(kN), (s > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(empty_b + 8 * st);
-      }
-      if (ok) umma_commit(accf_b);
-    }
-  } else {
-    // ---------------------------------------------------------------- decoders, then epilogue
-    const int quarter = warp & 3;              // TMEM lanes 32*quarter .. +31
-    const int r = 32 * quarter + lane;         // tile row = TMEM lane
-    const int R = m0 + r;                      // weight row (packed) or outlier slot (dense)
-    uint32_t lo4 = 0, hi4 = 0;
-    bool row_live = false;
-    int out_row = -1;
-    if (kDense) {
-      row_live = R < a.n_slots;
-      out_row = row_live ? __ldg(a.orow + R) : -1;
-    } else {
-      const int t = R / kTileRows;
-      if (t < a.MT) {
-        const uint2 c = __ldg(a.cb + R);
-        lo4 = c.x;
-        hi4 = c.y;
-        row_live = true;
-        const bool outlier = (__ldg(a.tile_mask + t) >> (R % kTileRows)) & 1u;
-        out_row = (R < a.M && !outlier) ? R : -1;
-      }
-    }
-    const int gl = (R % kTileRows) & 7, hi = (R % kTileRows) >> 3, tl = (R / kTileRows) - t0;
-    for (int s = 0; s < nk; ++s) {
-      const int st = s % kGmStages;
-      const uint32_t par = (s / kGmStages) & 1;
-      if (s >= kGmStages && !mbar_wait_bounded(empty_b + 8 * st, ((s / kGmStages) - 1) & 1)) {
-        ok = false;
-        break;
-      }
-      const uint32_t dstA = sA + st * kGmABytes;
-      if (kDense) {
-        const __half* src = a.dense + static_cast<int64_t>(R) * a.K_pad + s * kGmK;
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const uint4 v = row_live ? __ldg(reinterpret_cast<const uint4*>(src) + c) : make_uint4(0, 0, 0, 0);
-          sts128(dstA + sw128_off(r, c), v);
+          for (int kk = 0; kk < kGmK / 16; ++kk)  // +32 bytes per K = 16 step inside the swizzle atom
+            umma_f16(tacc, ad + 2 * kk, bd + 2 * kk, gm_idesc(kN), (s > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(empty_b + 8 * st);
         }
+        if (!ok) break;
+        umma_commit(accf_b + 8 * b);
+      }
+      // no tensor-core operation of this CTA is in flight past this point
+      umma_commit(drain_b);
+      mbar_wait_bounded(drain_b, 0);
+    }
+  } else if (warp < kGmEpiWarp0) {
+    // ---------------------------------------------------------------- decoders
+    const int d = warp - kGmDecWarp0;
+    const int r = 32 * (d & 3) + lane;  // tile row
+    const int grp = d >> 2;             // this warp's group: every kGmDecGroups-th stage
+    const int tl_row = r >> 4, gl = (r & 15) & 7, hi = (r & 15) >> 3;
+    int g = 0;
+    for (int i = blockIdx.x; i < a.tiles && ok; i += G) {
+      const int mi = i / a.n_tiles;
+      const bool dense = mi >= a.m_tiles;
+      const int R = (dense ? mi - a.m_tiles : mi) * kGmM + r;  // weight row (packed) or outlier slot (dense)
+      uint32_t lo4 = 0, hi4 = 0;
+      bool row_live;
+      if (dense) {
+        row_live = R < a.n_slots;
       } else {
-        if (!mbar_wait_bounded(full_b + 8 * st, par)) {
+        row_live = (R >> 4) < a.MT;
+        if (row_live) {
+          const uint2 c = __ldg(a.cb + R);
+          lo4 = c.x;
+          hi4 = c.y;
+        }
+      }
+      for (int s = 0; s < nk; ++s, ++g) {
+        if ((g % kGmDecGroups) != grp) continue;  // another group's stage
+        const int st = g % kS;
+        const uint32_t par = (g / kS) & 1;
+        if (g >= kS && !mbar_wait_bounded(empty_b + 8 * st, ((g / kS) - 1) & 1)) {
           ok = false;
           break;
         }
-        // words j = 2(s&1), 2(s&1)+1 of lanes 4gl+q hold this row's k offsets 32(j - 2(s&1)) + 8q + 0..7
-        const uint32_t ub = sU + st * kGmUBytes + tl * kUnitBytes + (4 * gl) * 16 + 8 * (s & 1);
+        const uint32_t dstA = sA + st * kGmABytes;
+        if (dense) {
+          const uint4* src = reinterpret_cast<const uint4*>(a.dense + static_cast<int64_t>(R) * a.K_pad + s * kGmK);
 #pragma unroll
-        for (int jj = 0; jj < 2; ++jj)
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint4 v = make_uint4(0, 0, 0, 0);
-            if (row_live) {
-              uint32_t w = lds32(ub + q * 16 + 4 * jj);
-              if (hi) w >>= 16;
-              v = decode_row8(w, lo4, hi4);
-            }
-            sts128(dstA + sw128_off(r, 4 * jj + q), v);
+          for (int c = 0; c < 8; ++c) sts128(dstA + sw128_off(r, c), row_live ? __ldg(src + c) : make_uint4(0, 0, 0, 0));
+        } else {
+          if (!mbar_wait_bounded(full_b + 8 * st, par)) {
+            ok = false;
+            break;
           }
+          // chunk c = 4jj + q of the stage (columns 32jj + 8q + 0..7) is in word 2(s&1) + jj of lane 4gl + q
+          const uint32_t ub = sU + st * kGmUBytes + tl_row * kUnitBytes + (4 * gl) * 16 + 8 * (s & 1);
+          uint32_t w[8];
+#pragma unroll
+          for (int c = 0; c < 8; ++c) w[c] = row_live ? lds32(ub + (c & 3) * 16 + 4 * (c >> 2)) : 0u;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (row_live) v = decode_row8(hi ? w[c] >> 16 : w[c], lo4, hi4);
+            sts128(dstA + sw128_off(r, c), v);
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(afull_b + 8 * st);
       }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(afull_b + 8 * st);
     }
-    // epilogue
-    if (ok && mbar_wait_bounded(accf_b, 0)) {
+  } else {
+    // ---------------------------------------------------------------- epilogue
+    const int quarter = warp & 3;        // TMEM lanes 32*quarter .. +31 (a warp's lane quarter is warp % 4)
+    const int r = 32 * quarter + lane;   // tile row = TMEM lane
+    const uint32_t trow = tmem + (static_cast<uint32_t>(32 * quarter) << 16);
+    int tl = 0;
+    for (int i = blockIdx.x; i < a.tiles && ok; i += G, ++tl) {
+      const int mi = i / a.n_tiles, n0 = (i - mi * a.n_tiles) * kN;
+      const bool dense = mi >= a.m_tiles;
+      const int R = (dense ? mi - a.m_tiles : mi) * kGmM + r;
+      int out_row = -1;
+      if (dense) {
+        if (R < a.n_slots) out_row = __ldg(a.orow + R);
+      } else if (R < a.M) {
+        const bool outlier = (__ldg(a.tile_mask + (R >> 4)) >> (R & 15)) & 1u;
+        out_row = outlier ? -1 : R;
+      }
+      const int b = tl & 1;
+      if (!mbar_wait_bounded(accf_b + 8 * b, (tl >> 1) & 1)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
-      const uint32_t trow = tmem + (static_cast<uint32_t>(32 * quarter) << 16);
+      const uint32_t tacc = trow + static_cast<uint32_t>(b * kN);
+      if constexpr (kN >= 32) {
 #pragma unroll 1
-      for (int cc = 0; cc < kN / 32; ++cc) {
-        uint32_t v[32];
-        tmem_ld32(trow + cc * 32, v);
+        for (int cc = 0; cc < kN / 32; ++cc) {
+          uint32_t v[32];
+          tmem_ld32(tacc + cc * 32, v);
+          if (out_row >= 0) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const int tok = n0 + cc * 32 + e;
+              if (tok < a.n_tok) a.y[static_cast<int64_t>(tok) * a.ldy + out_row] = __float2half_rn(__uint_as_float(v[e]));
+            }
+          }
+        }
+      } else {
+        uint32_t v[16];
+        tmem_ld16(tacc, v);
         if (out_row >= 0) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int tok = n0 + cc * 32 + i;
-            if (tok < a.n_tok) a.y[static_cast<int64_t>(tok) * a.ldy + out_row] = __float2half_rn(__uint_as_float(v[i]));
+          for (int e = 0; e < 16; ++e) {
+            const int tok = n0 + e;
+            if (tok < a.n_tok) a.y[static_cast<int64_t>(tok) * a.ldy + out_row] = __float2half_rn(__uint_as_float(v[e]));
           }
         }
       }
-    } else {
-      ok = false;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acce_b + 8 * b);
     }
   }
   if (!ok && lane == 0) atomicCAS(&g_opc_device_error, 0, kDevErrTmaTimeout);
@@ -275,7 +355,7 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_consta
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kGmTmemCols) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
   }
 }
 

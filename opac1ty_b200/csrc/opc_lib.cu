@@ -231,7 +231,8 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 }
 
 template <int kN>
-int launch_gemm_t(const CUtensorMap& tx, const opc::GemmArgs& a, dim3 grid, cudaStream_t stream, int dev) {
+int launch_gemm_t(const CUtensorMap& tx, const CUtensorMap& tu, const opc::GemmArgs& a, unsigned grid, cudaStream_t stream,
+                  int dev) {
   static std::mutex mu;
   static std::map<int, bool> configured;
   {
@@ -243,7 +244,7 @@ int launch_gemm_t(const CUtensorMap& tx, const opc::GemmArgs& a, dim3 grid, cuda
       configured[dev] = true;
     }
   }
-  opc::gemm_kernel<kN><<<grid, opc::kGmThreads, opc::gm_smem_bytes(kN), stream>>>(tx, a);
+  opc::gemm_kernel<kN><<<grid, opc::kGmThreads, opc::gm_smem_bytes(kN), stream>>>(tx, tu, a);
   OPC_CUDA(cudaGetLastError(), "launch gemm_kernel");
   return OPC_OK;
 }
@@ -838,9 +839,25 @@ int opc_gemm(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ld
   DeviceCache dc;
   int rc = device_cache(dev, &dc);
   if (rc != OPC_OK) return rc;
-  // 256-token tiles unless they would leave more than a tenth of the SMs without a tile.
+  // Token tile N: the candidate with the least estimated time, counting waves of persistent tiles
+  // (one CTA per SM) times the cost of a K stage -- the larger of the A-tile decode (~300 cycles
+  // with 8 decoder warps) and the MMAs (~2N cycles for 128 x N x 64 on one SM).
   const int64_t m_tiles = ceil_div(p.M_pad, opc::kGmM);
-  const int tn = (m_tiles * ceil_div(n_tok, 256) * 10 >= static_cast<int64_t>(dc.sm_count) * 9) ? 256 : 128;
+  const int64_t d_tiles = p.n_outliers > 0 ? ceil_div(static_cast<int64_t>(p.outlier_tiles) * opc::kTileRows, opc::kGmM) : 0;
+  int tn = 16;
+  {
+    double best = 0.0;
+    for (int N = 16; N <= 256; N *= 2) {
+      if (N > 16 && N / 2 >= n_tok) break;  // a smaller tile already covers every token
+      const int64_t tiles = (m_tiles + d_tiles) * ceil_div(n_tok, N);
+      const double waves = static_cast<double>(ceil_div(tiles, dc.sm_count));
+      const double cost = waves * std::max(300.0, 2.0 * N);
+      if (N == 16 || cost <= best) {
+        best = cost;
+        tn = N;
+      }
+    }
+  }
   if (opc::gm_smem_bytes(tn) > static_cast<size_t>(dc.max_smem_optin))
     return fail(OPC_ERR_UNSUPPORTED, "opc_gemm: needs %zu bytes of shared memory", opc::gm_smem_bytes(tn));
 
@@ -853,6 +870,18 @@ int opc_gemm(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ld
                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (cr != CUDA_SUCCESS) return fail(OPC_ERR_CUDA, "opc_gemm: cuTensorMapEncodeTiled failed (%d)", static_cast<int>(cr));
+  // packed units as [MT][KT * 64] 8-byte elements: one box = one k block (512 B) of 8 row tiles
+  CUtensorMap tu;
+  {
+    const cuuint64_t udim[2] = {static_cast<cuuint64_t>(p.k_units) * (opc::kUnitBytes / 8), static_cast<cuuint64_t>(p.row_tiles)};
+    const cuuint64_t ustride[1] = {static_cast<cuuint64_t>(p.k_units) * opc::kUnitBytes};
+    const cuuint32_t ubox[2] = {opc::kUnitBytes / 8, 8};
+    const CUresult cu = encode(&tu, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(L->units), udim, ustride, ubox,
+                               estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (cu != CUDA_SUCCESS)
+      return fail(OPC_ERR_CUDA, "opc_gemm: cuTensorMapEncodeTiled (units) failed (%d)", static_cast<int>(cu));
+  }
 
   opc::GemmArgs a;
   memset(&a, 0, sizeof(a));
@@ -870,11 +899,19 @@ int opc_gemm(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ld
   a.n_tok = n_tok;
   a.n_slots = p.outlier_tiles * opc::kTileRows;
   cudaStream_t s = static_cast<cudaStream_t>(stream_v);
-  const unsigned n_tiles = static_cast<unsigned>(ceil_div(n_tok, tn));
   a.m_tiles = static_cast<int32_t>(m_tiles);
-  const int64_t d_tiles = p.n_outliers > 0 ? ceil_div(a.n_slots, opc::kGmM) : 0;
-  const dim3 grid(static_cast<unsigned>(m_tiles + d_tiles), n_tiles);
-  return tn == 256 ? launch_gemm_t<256>(tx, a, grid, s, dev) : launch_gemm_t<128>(tx, a, grid, s, dev);
+  a.n_tiles = static_cast<int32_t>(ceil_div(n_tok, tn));
+  const int64_t tiles = (m_tiles + d_tiles) * a.n_tiles;
+  if (tiles >= (int64_t(1) << 31)) return fail(OPC_ERR_UNSUPPORTED, "opc_gemm: too many tiles");
+  a.tiles = static_cast<int32_t>(tiles);
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(tiles, dc.sm_count));
+  switch (tn) {
+    case 256: return launch_gemm_t<256>(tx, tu, a, grid, s, dev);
+    case 128: return launch_gemm_t<128>(tx, tu, a, grid, s, dev);
+    case 64: return launch_gemm_t<64>(tx, tu, a, grid, s, dev);
+    case 32: return launch_gemm_t<32>(tx, tu, a, grid, s, dev);
+    default: return launch_gemm_t<16>(tx, tu, a, grid, s, dev);
+  }
 }
 
 }  // extern "C"
@@ -887,7 +924,7 @@ struct opc_chain {
   int32_t n_layers = 0, batch = 1, stages = 2, xs_bytes = 0, grid = 0, xc = 8;
   int32_t rank = 0, world = 1;
   size_t smem = 0;
-  void* dev_mem = nullptr;              // [layers | onc | parts | epoch | acc | ocnt (| flags | words)]
+  void* dev_mem = nullptr;              // [layers | onc | parts | epoch | acc (| flags | words)]
   opc::ChainLayer* d_layers = nullptr;
   const int4* d_parts = nullptr;        // [layers][grid][kChainSharePieces] warp-share records
   unsigned int* d_sync = nullptr;       // this rank's flags [world][grid]
@@ -986,6 +1023,43 @@ std::vector<opc::ChainPart> chain_parts(const opc::ChainLayer& c, int G, int nw 
   return parts;
 }
 
+// Unit ranges of a CTA's consumer warps (out of nw, the other warps of the CTA being the producer
+// and, in the dataflow form, the staging warp).  Packed warps split the packed share in proportion
+// to their speed: the warps of an SM sub-partition (warp index mod 4) share its issue slots, and a
+// sub-partition's packed warps run as fast as if each other busy warp on it (an outlier warp, the
+// producer) were 0.4 of a packed warp (measured on the Llama-3.1-8B decode step: warps of a
+// sub-partition with three packed warps and one other finish 1.18x faster per unit than those of a
+// sub-partition with four packed warps).  Outlier warps split their share evenly.
+void chain_warp_ranges(const opc::ChainPart& p, int nw, int32_t* u0, int32_t* u1) {
+  constexpr int kCtaWarps = opc::kQConsumers + 1;  // consumer warps plus the producer (and staging) warps
+  double busy[4] = {0, 0, 0, 0};
+  for (int w = 0; w < kCtaWarps; ++w) busy[w % 4] += w < p.wp ? 1.0 : 0.4;
+  double cum[opc::kQConsumers + 1];
+  cum[0] = 0.0;
+  for (int w = 0; w < p.wp; ++w) cum[w + 1] = cum[w] + 1.0 / busy[w % 4];
+  const int32_t np = p.pu1 - p.pu0;
+  for (int w = 0; w < nw; ++w) {
+    if (w < p.wp) {
+      u0[w] = p.pu0 + static_cast<int32_t>(std::lround(np * cum[w] / cum[p.wp]));
+      u1[w] = p.pu0 + static_cast<int32_t>(std::lround(np * cum[w + 1] / cum[p.wp]));
+    } else {
+      opc::chain_warp_range(p, w, &u0[w], &u1[w], nw);
+    }
+  }
+}
+
+// Per packed warp: how many packed warps of its CTA share its first and its last tile (the split
+// tiles' completion counts), as one byte: first | last << 4.
+void chain_warp_needs(const opc::ChainPart& p, int32_t KT, const int32_t* u0, const int32_t* u1, uint8_t* need) {
+  auto sharing = [&](int32_t t) {
+    int n = 0;
+    for (int w = 0; w < p.wp; ++w) n += (u0[w] < u1[w] && u0[w] < (t + 1) * KT && u1[w] > t * KT) ? 1 : 0;
+    return n;
+  };
+  for (int w = 0; w < p.wp; ++w)
+    need[w] = u0[w] < u1[w] ? static_cast<uint8_t>(sharing(u0[w] / KT) | (sharing((u1[w] - 1) / KT) << 4)) : 0;
+}
+
 // Warps contributing to each outlier tile of a layer, for the kernel's completion counts.
 std::vector<int32_t> outlier_contributors(const opc::ChainLayer& c, const std::vector<opc::ChainPart>& parts,
                                           int nw = opc::kQConsumers) {
@@ -1048,12 +1122,12 @@ int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t 
   if (per_sm < 1) return fail(OPC_ERR_UNSUPPORTED, "%s: chain kernel does not fit on an SM", fn);
   const int G = dc.sm_count;
 
-  // device memory: [layers | onc | parts | epoch] (copied) then [acc | ocnt (| flags | words)] (zeroed)
+  // device memory: [layers | onc | parts | epoch] (copied) then [acc (| flags | words)] (zeroed)
   std::vector<opc::ChainLayer> hl(n);
   std::vector<std::vector<int32_t>> onc(n);
   const size_t layers_bytes = align_up(sizeof(opc::ChainLayer) * n, 256);
   size_t off = layers_bytes;
-  std::vector<size_t> onc_off(n), acc_off(n), ocnt_off(n), yw_off(n);
+  std::vector<size_t> onc_off(n), acc_off(n), yw_off(n);
   std::vector<int32_t> parts(opc::kChainShareInts * static_cast<size_t>(G) * n, 0);  // [n][G] warp-share records
   for (int j = 0; j < n; ++j) {
     const opc_layer_plan& p = steps[j].layer->plan;
@@ -1067,6 +1141,10 @@ int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t 
     c.KO = p.outlier_k_units;
     const std::vector<opc::ChainPart> cparts = chain_parts(c, G);
     onc[j] = outlier_contributors(c, cparts);
+    for (int32_t v : onc[j])
+      if (v > opc::kMaxContributors)
+        return fail(OPC_ERR_UNSUPPORTED, "%s: step %d: %d warps share an outlier tile (at most %d)", fn, j, v,
+                    opc::kMaxContributors);
     onc_off[j] = off;
     off += align_up(std::max<size_t>(onc[j].size(), 1) * sizeof(int32_t), 256);
     // each CTA's warp shares, so the kernel does no partition arithmetic (and no division):
@@ -1074,15 +1152,17 @@ int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t 
     for (int cta = 0; cta < G; ++cta) {
       const opc::ChainPart& pt = cparts[cta];
       int32_t* e = parts.data() + opc::kChainShareInts * (static_cast<size_t>(j) * G + cta);
+      int32_t wu0[opc::kQConsumers], wu1[opc::kQConsumers];
+      chain_warp_ranges(pt, opc::kQConsumers, wu0, wu1);
       for (int w = 0; w < opc::kQConsumers; ++w) {
-        int32_t u0 = 0, u1 = 0;
-        opc::chain_warp_range(pt, w, &u0, &u1);
+        const int32_t u0 = wu0[w], u1 = wu1[w];
         e[opc::kShU0 + w] = u0;
         e[opc::kShU1 + w] = u1;
         e[opc::kShSeg0 + w] = u0 >= u1 ? 0 : (u0 < c.Up ? u0 / c.KT : c.MT + (u0 - c.Up) / c.KO);
       }
       e[opc::kShWp] = pt.wp;
       e[opc::kShTile0] = c.KT > 0 ? pt.pu0 / c.KT : 0;
+      chain_warp_needs(pt, c.KT, wu0, wu1, reinterpret_cast<uint8_t*>(e + opc::kShNeed));
     }
   }
   const size_t parts_off = off;
@@ -1094,8 +1174,6 @@ int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t 
     const opc_layer_plan& p = steps[j].layer->plan;
     acc_off[j] = off;
     off += align_up(static_cast<size_t>(n_slots_of(p)) * opc::kQMaxBatch * sizeof(unsigned long long), 256);
-    ocnt_off[j] = off;
-    off += align_up(static_cast<size_t>(std::max(p.outlier_tiles, 1)) * sizeof(int32_t), 256);
   }
   size_t sync_off = 0;
   if (own_scratch) {
@@ -1130,7 +1208,6 @@ int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t 
     c.x = static_cast<const __half*>(st.x);
     c.xw = j > 0 ? reinterpret_cast<const uint32_t*>(me.yw[j - 1]) : nullptr;
     c.acc = reinterpret_cast<unsigned long long*>(base + acc_off[j]);
-    c.ocnt = reinterpret_cast<int32_t*>(base + ocnt_off[j]);
     c.onc = reinterpret_cast<const int32_t*>(base + onc_off[j]);
     for (int q = 0; q < world; ++q) {
       c.y_peer[q] = reinterpret_cast<__half*>(ranks[q].y[j]) + row_off[j];

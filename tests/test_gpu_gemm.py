@@ -77,3 +77,30 @@ def test_gemm_reports_no_device_error(cuda_device):
     code = ctypes.c_int32(-1)
     _lib.check(_lib.load().opc_take_device_error(0, ctypes.byref(code)))
     assert code.value == 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("n_tok", [1, 16, 17, 32, 40, 64, 100, 128, 200, 256])
+def test_gemm_every_token_tile_size(cuda_device, n_tok):
+    # The host picks the token tile (16..256 columns of tensor memory) from the token count: every
+    # tile size must give the same result as the fp64 recompute.
+    y, y64, _ = _run(cuda_device, 1024, 1024, 9, n_tok, seed=n_tok)
+    assert y.shape == (n_tok, 1024)
+    assert oracle.rel_err(y, y64) <= REL_TOL
+
+
+@pytest.mark.gpu
+def test_gemm_persistent_ctas_cycle_both_accumulators(cuda_device):
+    # More tiles than SMs: every CTA walks several tiles, alternating its two tensor-memory
+    # accumulators (the epilogue of one tile overlaps the MMAs of the next).  Reference: fp64
+    # matmul on the GPU of the oracle's (bit-exact) dequantized weights.
+    M, K, n_out, n_tok = 8192, 1024, 50, 1024
+    ly = synthetic.random_layer(M, K, n_out, seed=11)
+    dl = L.prepare_layer(ly, cuda_device)
+    x = torch.from_numpy(synthetic.activations(n_tok, K, seed=12)).to(cuda_device)
+    y = G.gemm(dl, x)
+    w = torch.from_numpy(oracle.dequantize_np(ly)).to(cuda_device).double()
+    y64 = (x.double() @ w.T).cpu().numpy()
+    torch.cuda.synchronize()
+    assert oracle.rel_err(y.cpu().numpy(), y64) <= REL_TOL
+    assert torch.equal(y, G.gemm(dl, x))  # deterministic
