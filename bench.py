@@ -57,8 +57,8 @@ METRIC = "fused 2-bit VQ GEMV HBM TB/s (% peak); decode tok/s @ Llama-3.1-8B sha
 CHAIN_TRAFFIC_RATIO = 1.021
 WORKLOAD = "Llama-3.1-8B decode GEMV set, batch 1, 32 blocks (q|k|v, o, gate|up, down), 2-bit svs=1, 1% outlier rows"
 DTYPE = ("2-bit codebook weights, fp16 x and y; batch 1-2 dot products exact in integers: int8 x uint8 mma.sync "
-         "of 15-bit fixed-point centroids and fixed-point x (batch 1 decode step: 30-bit x digits at a scale "
-         "fixed from a norm bound; otherwise 22-bit x scaled by max|x|), int64 sums, one fp16 rounding per output")
+         "of 15-bit fixed-point centroids and 22-bit fixed-point x (scaled by max|x| of each GEMV's input), "
+         "int64 sums, one fp16 rounding per output")
 PARITY_TOL = 2e-3
 BLOCKS = 32
 

@@ -115,34 +115,16 @@ def info(bf2_path, layers, json_output):
 
 
 def _time_gemv(dl, batch: int, iters: int):
+    """Device time (us) of one fused GEMV at ``batch``: CUDA-graph replays with L2 flushed before
+    each launch (opac1ty_b200.measure.graph_time_us)."""
     import torch
 
-    from . import layer as L, synthetic
+    from . import layer as L, measure, synthetic
 
     x = torch.from_numpy(synthetic.activations(batch, dl.K, seed=1)).to(dl.device)
     y = torch.empty(batch, dl.M, dtype=torch.float16, device=dl.device)
     ws = torch.zeros(L.workspace_bytes(dl, batch), dtype=torch.uint8, device=dl.device)
-    for _ in range(3):
-        L.gemv(dl, x, out=y, workspace=ws)
-    torch.cuda.synchronize(dl.device)
-    # the iterations are replayed from a CUDA graph: the time is the GPU's, not the Python call rate
-    g = torch.cuda.CUDAGraph()
-    cs = torch.cuda.Stream(dl.device)
-    cs.wait_stream(torch.cuda.current_stream(dl.device))
-    with torch.cuda.stream(cs):
-        L.gemv(dl, x, out=y, workspace=ws)
-    torch.cuda.current_stream(dl.device).wait_stream(cs)
-    with torch.cuda.graph(g):
-        for _ in range(iters):
-            L.gemv(dl, x, out=y, workspace=ws)
-    g.replay()
-    s = torch.cuda.current_stream(dl.device)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(s)
-    g.replay()
-    e1.record(s)
-    torch.cuda.synchronize(dl.device)
-    return e0.elapsed_time(e1) * 1000.0 / iters
+    return measure.graph_time_us(lambda: L.gemv(dl, x, out=y, workspace=ws), dl.device, iters)
 
 
 @cli.command()
@@ -347,7 +329,7 @@ def gemm_bench(shape, tokens, outliers, iters):  # noqa: D401
     """Time one synthetic layer's prefill GEMM (tcgen05, CUDA events); prints one JSON line."""
     import torch
 
-    from . import gemm as G, layer as L, synthetic
+    from . import gemm as G, layer as L, measure, synthetic
     from .utils import get_cuda_device_info
 
     M, K = (int(v) for v in shape.lower().split("x"))
@@ -356,16 +338,7 @@ def gemm_bench(shape, tokens, outliers, iters):  # noqa: D401
     dl = L.prepare_layer(ly, dev)
     x = torch.randn(tokens, K, device=dev).half()
     y = torch.empty(tokens, M, dtype=torch.float16, device=dev)
-    for _ in range(3):
-        G.gemm(dl, x, out=y)
-    s = torch.cuda.current_stream(dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(s)
-    for _ in range(iters):
-        G.gemm(dl, x, out=y)
-    e1.record(s)
-    torch.cuda.synchronize(dev)
-    us = e0.elapsed_time(e1) * 1000.0 / iters
+    us = measure.graph_time_us(lambda: G.gemm(dl, x, out=y), dev, iters)  # L2 flushed before each launch
     fl = G.flops(dl, tokens)
     click.echo(json.dumps({"gpu": get_cuda_device_info().name, "shape": [M, K], "tokens": tokens,
                            "n_outliers": dl.n_outliers, "us": us, "tflops": fl / us / 1e6}))

@@ -69,12 +69,10 @@ struct ChainLayer {
 
 // Per layer and CTA, the host-computed shares of its consumer warps, so the kernel does no integer
 // division: int32 [0..14] first unit of warp w, [15] packed warps wp, [16..30] end unit of warp w,
-// [31] the CTA's first packed tile, [32..46] first segment of warp w (0 for an empty range),
-// [48..51] one byte per warp: the packed warps of the CTA sharing the warp's first packed tile
-// (low nibble) and its last one (high nibble).
-constexpr int kChainShareInts = 52;
+// [31] the CTA's first packed tile, [32..46] first segment of warp w (0 for an empty range).
+constexpr int kChainShareInts = 48;
 constexpr int kChainSharePieces = kChainShareInts / 4;  // int4 pieces
-constexpr int kShU0 = 0, kShWp = 15, kShU1 = 16, kShTile0 = 31, kShSeg0 = 32, kShNeed = 48;
+constexpr int kShU0 = 0, kShWp = 15, kShU1 = 16, kShTile0 = 31, kShSeg0 = 32;
 
 static_assert(sizeof(ChainLayer) % 16 == 0, "ChainLayer is copied in 16-byte pieces");
 static_assert(sizeof(ChainLayer) / 16 + kChainSharePieces <= 32, "one warp copies a descriptor and a CTA share");
@@ -691,9 +689,23 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
       nxt = chain_load_meta(qa, min(cc.seg + 1, L.MT + L.OT - 1), g);
     }
     // contributors (packed warps of this CTA) of the first and the last packed tile of this warp's
-    // range -- the only ones it may share with other warps (host-counted)
-    const int need_nb = reinterpret_cast<const uint8_t*>(sr + kShNeed)[warp];
+    // range -- the only ones it may share -- counted while x is not complete yet
+    int need_first = 0, need_last = 0;
     const int tile0 = sr[kShTile0];
+    if (u0 < u1 && cc.seg < L.MT) {
+      const int32_t fb = cc.begin, fe = cc.end;
+      int32_t lb = fb, le = fe;
+      while (le < u1) {
+        lb = le;
+        le += L.KT;
+      }
+      const int wp = sr[kShWp];
+      for (int w = 0; w < wp; ++w) {
+        const int32_t a = sr[kShU0 + w], b = sr[kShU1 + w];
+        need_first += (a < b && a < fe && b > fb) ? 1 : 0;
+        need_last += (a < b && a < le && b > lb) ? 1 : 0;
+      }
+    }
     const int32_t seg_first = cc.seg;
     // next layer's descriptor and this CTA's share of it: loaded now, stored to shared memory
     // once every warp is past this layer's first staging barrier (nobody reads the slots' old
@@ -872,19 +884,14 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
             }
           }
         } else {
-          // outlier units, two per iteration (one per accumulator chain), not unrolled further:
-          // they are light, and the smaller loop keeps the kernel's code small
-#pragma unroll 1
-          for (int i = 0; i < cnt; i += 2) {
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              if (i + h < cnt) {
-                const uint4 av = lds128(stage + (i + h) * kUnitBytes);
-                const int32_t s = k0 + i + h;
-                const uint32_t bv = lds32(xo + static_cast<uint32_t>(s >> 3) * kts + (s & 7) * 16);
-                imma16816(A.h[h], av.x, av.y, bv);
-                imma16816(A.l[h], av.z, av.w, bv);
-              }
+          for (int i = 0; i < kQChunkUnits; ++i) {
+            if (i < cnt) {
+              const uint4 av = lds128(stage + i * kUnitBytes);
+              const int32_t s = k0 + i;
+              const uint32_t bv = lds32(xo + static_cast<uint32_t>(s >> 3) * kts + (s & 7) * 16);
+              imma16816(A.h[i & 1], av.x, av.y, bv);
+              imma16816(A.l[i & 1], av.z, av.w, bv);
             }
           }
         }
@@ -905,7 +912,7 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
             r0 = (r0 < L.M && !((mask >> g) & 1u)) ? r0 : -1;
           }
           chain_finish_segment<sys>(sh, L, P, B, r0, r1, cur.e[0], cur.e[1], t[0], t[1], cc.seg,
-                                    cc.begin >= u0 && cc.end <= u1, cc.seg == seg_first ? (need_nb & 15) : (need_nb >> 4),
+                                    cc.begin >= u0 && cc.end <= u1, cc.seg == seg_first ? need_first : need_last,
                                     tile0, g, q, ex0, ex1, tag);
           if (cc.u == u1) break;
           zero_accq(A);

@@ -19,8 +19,9 @@
 //   warps 18..21 epilogue: read a finished accumulator (each warp its TMEM lane quarter),
 //                round to fp16 and store Y, then hand the accumulator back -- while the MMAs of
 //                the next tile run into the other one
-// Outlier rows have all-zero codebooks, so the packed tiles compute 0 for them and skip their
-// writes; dense tiles (after the packed ones) compute them from the row-major outlier copy (A
+// sub_vector_size 8 (an index selects one of the row's four 8-element fp16 vectors): a chunk of
+// 8 columns is one vector, selected from registers.  Outlier rows have all-zero codebooks, so the
+// packed tiles compute 0 for them and skip their writes; dense tiles (after the packed ones) compute them from the row-major outlier copy (A
 // rows copied instead of decoded) and scatter them to their output rows.
 #pragma once
 
@@ -38,6 +39,7 @@ constexpr int kGmDecWarp0 = 2, kGmEpiWarp0 = kGmDecWarp0 + kGmDecWarps;
 constexpr int kGmThreads = (kGmEpiWarp0 + kGmEpiWarps) * 32;
 constexpr int kGmABytes = kGmM * kGmK * 2;   // 16 KB
 constexpr int kGmUBytes = 8 * kUnitBytes;    // 8 row tiles x one unit
+constexpr int kGmPrefetch = 24;               // stages ahead whose packed units are prefetched into L2
 constexpr int kGmSmemBudget = 227 * 1024 - 1024 - 512;  // dynamic shared memory less slack and barriers
 // Token tile N: x stage N*64 fp16, two accumulators of N fp32 TMEM columns.
 __host__ __device__ constexpr int gm_b_bytes(int N) { return N * kGmK * 2; }
@@ -52,7 +54,9 @@ __host__ __device__ constexpr size_t gm_smem_bytes(int N) {
 
 struct GemmArgs {
   const uint8_t* units;        // packed units
-  const uint2* cb;             // [M_pad] split fp16 codebooks
+  const uint2* cb;             // sub_vector_size 1: [M_pad] split fp16 codebooks
+  const uint4* cb8;            // sub_vector_size 8: [MT][32 lanes][2] codebook words (opc_vq8.cuh layout)
+  int32_t svs8;                // 1: sub_vector_size 8 layer (128-byte index units of 16 rows x 256 columns)
   const uint16_t* tile_mask;   // [MT]
   const __half* dense;         // [n_slots][K_pad] outlier rows (dense tiles)
   const int32_t* orow;         // [n_slots]
@@ -78,6 +82,10 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
       "l"(map), "r"(x), "r"(y), "r"(bar)
       : "memory");
+}
+// Bring a tile of the tensor map into L2 ahead of its load (no shared memory, no completion).
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(map), "r"(x), "r"(y) : "memory");
 }
 __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accum) {
   asm volatile(
@@ -126,13 +134,22 @@ __device__ __forceinline__ uint4 decode_row8(uint32_t w, uint32_t lo4, uint32_t 
                     prmt(V[1], V[3], 0x7632u));
 }
 
+// sub_vector_size 8: word i (0..3) of v
+__device__ __forceinline__ uint32_t gm_sel4(const uint4& v, uint32_t i) {
+  const uint32_t lo = (i & 1u) ? v.y : v.x;
+  const uint32_t hi = (i & 1u) ? v.w : v.z;
+  return (i & 2u) ? hi : lo;
+}
+constexpr int kVq8UnitBytesGm = 128;  // svs-8 index unit: 16 rows x 256 columns x 2 bits
+
 // Offset of (row r, 16-byte chunk c) in a K-major 128-byte-swizzled tile of 64 fp16 per row.
 __device__ __forceinline__ uint32_t sw128_off(int r, int c) {
   return static_cast<uint32_t>(1024 * (r >> 3) + 128 * (r & 7) + 16 * (c ^ (r & 7)));
 }
 
 // tx: x [n_tok][K] fp16, box 64 x N, 128-byte swizzle.  tu: the packed units as a [MT][KT * 512 B]
-// array of 8-byte elements, box 512 B x 8 row tiles (one copy brings a k block of all 8 row tiles).
+// array of 8-byte elements, box 512 B x 8 row tiles (one copy brings a k block of all 8 row tiles);
+// sub_vector_size 8: [MT][KB * 128 B], box 128 B x 8 row tiles.
 template <int kN>
 __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap tx,
                                                              const __grid_constant__ CUtensorMap tu, const GemmArgs a) {
@@ -185,17 +202,32 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_consta
         const int mi = i / a.n_tiles, n0 = (i - mi * a.n_tiles) * kN;
         const bool packed = mi < a.m_tiles;
         // a box past the last row tile is filled with zeros and still counts its full size
-        const uint32_t bytes = kBBytes + (packed ? static_cast<uint32_t>(kGmUBytes) : 0u);
+        const uint32_t ubytes = a.svs8 ? 8u * kVq8UnitBytesGm : static_cast<uint32_t>(kGmUBytes);
+        const uint32_t bytes = kBBytes + (packed ? ubytes : 0u);
         for (int s = 0; s < nk; ++s, ++g) {
           const int st = g % kS;
           if (g >= kS && !mbar_wait_bounded(empty_b + 8 * st, ((g / kS) - 1) & 1)) {
             ok = false;
             break;
           }
+          // the packed units of the stage kGmPrefetch stages ahead go to L2 now, so that their load
+          // (HBM latency) is off the ring's round trip; one prefetch per k block
+          {
+            const int gf = g + kGmPrefetch, it = gf / nk, sf = gf - it * nk;
+            const int ifut = blockIdx.x + it * G;
+            if (ifut < a.tiles && (sf & (a.svs8 ? 3 : 1)) == 0) {
+              const int mf = ifut / a.n_tiles;
+              if (mf < a.m_tiles)
+                tma_prefetch_2d(&tu, a.svs8 ? (sf >> 2) * (kVq8UnitBytesGm / 8) : (sf >> 1) * (kUnitBytes / 8), mf * 8);
+            }
+          }
           mbar_expect_tx(full_b + 8 * st, bytes);
           tma_load_2d(sB + st * kBBytes, &tx, s * kGmK, n0, full_b + 8 * st);
-          // x coordinate: k block s/2 in 8-byte elements (a multiple of 64: 512-byte aligned)
-          if (packed) tma_load_2d(sU + st * kGmUBytes, &tu, (s >> 1) * (kUnitBytes / 8), mi * 8, full_b + 8 * st);
+          // x coordinate: the k block of the stage in 8-byte elements (512-byte units of 128 columns,
+          // or 128-byte svs-8 units of 256 columns: 16-byte aligned either way)
+          if (packed)
+            tma_load_2d(sU + st * kGmUBytes, &tu, a.svs8 ? (s >> 2) * (kVq8UnitBytesGm / 8) : (s >> 1) * (kUnitBytes / 8),
+                        mi * 8, full_b + 8 * st);
         }
       }
       // copies nobody consumed (a role gave up) land before the CTA exits: wait (bounded) for
@@ -251,16 +283,23 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_consta
       const bool dense = mi >= a.m_tiles;
       const int R = (dense ? mi - a.m_tiles : mi) * kGmM + r;  // weight row (packed) or outlier slot (dense)
       uint32_t lo4 = 0, hi4 = 0;
+      uint4 cv[4];  // sub_vector_size 8: word c of cv[q] = the row's vector c at halves 2q, 2q+1
       bool row_live;
       if (dense) {
         row_live = R < a.n_slots;
       } else {
         row_live = (R >> 4) < a.MT;
-        if (row_live) {
+        if (row_live && !a.svs8) {
           const uint2 c = __ldg(a.cb + R);
           lo4 = c.x;
           hi4 = c.y;
         }
+      }
+      if (a.svs8) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          cv[q] = (row_live && !dense) ? __ldg(a.cb8 + (static_cast<int64_t>(R >> 4) * 32 + 4 * gl + q) * 2 + hi)
+                                       : make_uint4(0, 0, 0, 0);
       }
       for (int s = 0; s < nk; ++s, ++g) {
         if ((g % kGmDecGroups) != grp) continue;  // another group's stage
@@ -280,16 +319,30 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_consta
             ok = false;
             break;
           }
-          // chunk c = 4jj + q of the stage (columns 32jj + 8q + 0..7) is in word 2(s&1) + jj of lane 4gl + q
-          const uint32_t ub = sU + st * kGmUBytes + tl_row * kUnitBytes + (4 * gl) * 16 + 8 * (s & 1);
-          uint32_t w[8];
+          if (a.svs8) {
+            // word s&3 of row pair gl's 16 bytes: byte c/2 = k16 step, bits 2(c&1) + 4hi = the index of
+            // chunk c (8 columns = one codebook vector)
+            const uint32_t w = row_live ? lds32(sU + st * kGmUBytes + tl_row * kVq8UnitBytesGm + gl * 16 + 4 * (s & 3)) : 0u;
 #pragma unroll
-          for (int c = 0; c < 8; ++c) w[c] = row_live ? lds32(ub + (c & 3) * 16 + 4 * (c >> 2)) : 0u;
+            for (int c = 0; c < 8; ++c) {
+              const uint32_t i = (w >> (8 * (c >> 1) + 2 * (c & 1) + 4 * hi)) & 3u;
+              uint32_t h[4];
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            uint4 v = make_uint4(0, 0, 0, 0);
-            if (row_live) v = decode_row8(hi ? w[c] >> 16 : w[c], lo4, hi4);
-            sts128(dstA + sw128_off(r, c), v);
+              for (int q = 0; q < 4; ++q) h[q] = gm_sel4(cv[q], i);
+              sts128(dstA + sw128_off(r, c), make_uint4(h[0], h[1], h[2], h[3]));
+            }
+          } else {
+            // chunk c = 4jj + q of the stage (columns 32jj + 8q + 0..7) is in word 2(s&1) + jj of lane 4gl + q
+            const uint32_t ub = sU + st * kGmUBytes + tl_row * kUnitBytes + (4 * gl) * 16 + 8 * (s & 1);
+            uint32_t w[8];
+#pragma unroll
+            for (int c = 0; c < 8; ++c) w[c] = row_live ? lds32(ub + (c & 3) * 16 + 4 * (c >> 2)) : 0u;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              uint4 v = make_uint4(0, 0, 0, 0);
+              if (row_live) v = decode_row8(hi ? w[c] >> 16 : w[c], lo4, hi4);
+              sts128(dstA + sw128_off(r, c), v);
+            }
           }
         }
         fence_proxy_async_smem();

@@ -814,10 +814,8 @@ int opc_dequant(const opc_layer* L, void* w, int64_t ldw, void* stream_v) {
 
 int opc_gemm(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ldy, int32_t n_tok, void* stream_v) {
   if (!L || !plan_ok(&L->plan)) return fail(OPC_ERR_INVALID, "opc_gemm: invalid layer plan");
-  if (L->plan.sub_vector_size != 1)
-    return fail(OPC_ERR_UNSUPPORTED, "opc_gemm: sub_vector_size %d (the prefill GEMM runs svs = 1; use opc_gemv)",
-                L->plan.sub_vector_size);
   const opc_layer_plan& p = L->plan;
+  const bool svs8 = p.sub_vector_size == 8;
   if (!L->units || !L->codebooks || !L->tile_mask || !L->outlier_rows)
     return fail(OPC_ERR_INVALID, "opc_gemm: layer buffers not allocated");
   if (n_tok < 1) return fail(OPC_ERR_INVALID, "opc_gemm: n_tok %d < 1", n_tok);
@@ -828,7 +826,7 @@ int opc_gemm(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ld
   if (!aligned(x, 16) || ldx % 8 != 0)
     return fail(OPC_ERR_UNSUPPORTED, "opc_gemm: x must be 16-byte aligned with ldx a multiple of 8 (TMA)");
   if (!aligned(y, 2)) return fail(OPC_ERR_INVALID, "opc_gemm: y not 2-byte aligned");
-  if (!aligned(L->units, 16) || !aligned(L->codebooks, 8))
+  if (!aligned(L->units, 16) || !aligned(L->codebooks, svs8 ? 16 : 8))
     return fail(OPC_ERR_INVALID, "opc_gemm: layer buffers misaligned");
   if (static_cast<int64_t>(n_tok) > (int64_t(65535) * 128))
     return fail(OPC_ERR_UNSUPPORTED, "opc_gemm: n_tok %d too large", n_tok);
@@ -870,12 +868,14 @@ int opc_gemm(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ld
                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (cr != CUDA_SUCCESS) return fail(OPC_ERR_CUDA, "opc_gemm: cuTensorMapEncodeTiled failed (%d)", static_cast<int>(cr));
-  // packed units as [MT][KT * 64] 8-byte elements: one box = one k block (512 B) of 8 row tiles
+  // packed units as [MT][KT * unit bytes / 8] 8-byte elements: one box = one k block of 8 row tiles
+  // (512-byte units of 128 columns; sub_vector_size 8: 128-byte units of 256 columns)
   CUtensorMap tu;
   {
-    const cuuint64_t udim[2] = {static_cast<cuuint64_t>(p.k_units) * (opc::kUnitBytes / 8), static_cast<cuuint64_t>(p.row_tiles)};
-    const cuuint64_t ustride[1] = {static_cast<cuuint64_t>(p.k_units) * opc::kUnitBytes};
-    const cuuint32_t ubox[2] = {opc::kUnitBytes / 8, 8};
+    const int ub = svs8 ? opc::kVq8UnitBytes : opc::kUnitBytes;
+    const cuuint64_t udim[2] = {static_cast<cuuint64_t>(p.k_units) * (ub / 8), static_cast<cuuint64_t>(p.row_tiles)};
+    const cuuint64_t ustride[1] = {static_cast<cuuint64_t>(p.k_units) * ub};
+    const cuuint32_t ubox[2] = {static_cast<cuuint32_t>(ub / 8), 8};
     const CUresult cu = encode(&tu, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(L->units), udim, ustride, ubox,
                                estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -887,8 +887,11 @@ int opc_gemm(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ld
   memset(&a, 0, sizeof(a));
   a.units = static_cast<const uint8_t*>(L->units);
   a.cb = static_cast<const uint2*>(L->codebooks);
+  a.cb8 = static_cast<const uint4*>(L->codebooks);
+  a.svs8 = svs8 ? 1 : 0;
   a.tile_mask = static_cast<const uint16_t*>(L->tile_mask);
-  a.dense = dense_outliers(L);
+  a.dense = svs8 ? reinterpret_cast<const __half*>(static_cast<const uint8_t*>(L->units) + p.packed_units * opc::kVq8UnitBytes)
+                 : dense_outliers(L);
   a.orow = L->outlier_rows;
   a.y = static_cast<__half*>(y);
   a.ldy = ldy;
@@ -1048,18 +1051,6 @@ void chain_warp_ranges(const opc::ChainPart& p, int nw, int32_t* u0, int32_t* u1
   }
 }
 
-// Per packed warp: how many packed warps of its CTA share its first and its last tile (the split
-// tiles' completion counts), as one byte: first | last << 4.
-void chain_warp_needs(const opc::ChainPart& p, int32_t KT, const int32_t* u0, const int32_t* u1, uint8_t* need) {
-  auto sharing = [&](int32_t t) {
-    int n = 0;
-    for (int w = 0; w < p.wp; ++w) n += (u0[w] < u1[w] && u0[w] < (t + 1) * KT && u1[w] > t * KT) ? 1 : 0;
-    return n;
-  };
-  for (int w = 0; w < p.wp; ++w)
-    need[w] = u0[w] < u1[w] ? static_cast<uint8_t>(sharing(u0[w] / KT) | (sharing((u1[w] - 1) / KT) << 4)) : 0;
-}
-
 // Warps contributing to each outlier tile of a layer, for the kernel's completion counts.
 std::vector<int32_t> outlier_contributors(const opc::ChainLayer& c, const std::vector<opc::ChainPart>& parts,
                                           int nw = opc::kQConsumers) {
@@ -1162,7 +1153,6 @@ int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t 
       }
       e[opc::kShWp] = pt.wp;
       e[opc::kShTile0] = c.KT > 0 ? pt.pu0 / c.KT : 0;
-      chain_warp_needs(pt, c.KT, wu0, wu1, reinterpret_cast<uint8_t*>(e + opc::kShNeed));
     }
   }
   const size_t parts_off = off;

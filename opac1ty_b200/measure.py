@@ -1,7 +1,9 @@
 """Device-timed measurements of the fused 2-bit path at the benchmark configurations.
 
 Every timing here replays a CUDA graph of repeated launches and reads CUDA events on the
-launching stream, so the numbers are the GPU's and not the Python call rate.  The layers are
+launching stream, so the numbers are the GPU's and not the Python call rate; per-kernel timings
+read a buffer twice the size of L2 before each launch (and subtract that read's time), so every
+launch streams its weights from HBM.  The layers are
 seeded synthetic ones (``synthetic.random_layer_device``) of the named shapes: kernel timing
 does not depend on the weight values.
 
@@ -26,22 +28,20 @@ from . import layer as L
 from . import synthetic
 
 
-def graph_time_us(call: Callable[[], None], device: torch.device, iters: int = 20) -> float:
-    """Mean device time of ``call`` (µs): ``iters`` calls captured in one CUDA graph, replayed once
-    to warm up and once timed with CUDA events on the current stream."""
-    for _ in range(2):
-        call()
-    torch.cuda.synchronize(device)
+FLUSH_BYTES = 256 << 20  # twice the B200's 126 MB L2
+
+
+def _graph_us(calls: Callable[[], None], device: torch.device, iters: int) -> float:
     g = torch.cuda.CUDAGraph()
     cs = torch.cuda.Stream(device)
     cur = torch.cuda.current_stream(device)
     cs.wait_stream(cur)
     with torch.cuda.stream(cs):
-        call()
+        calls()
     cur.wait_stream(cs)
     with torch.cuda.graph(g):
         for _ in range(iters):
-            call()
+            calls()
     g.replay()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(cur)
@@ -51,6 +51,33 @@ def graph_time_us(call: Callable[[], None], device: torch.device, iters: int = 2
     us = e0.elapsed_time(e1) * 1000.0 / iters
     del g
     return us
+
+
+def graph_time_us(call: Callable[[], None], device: torch.device, iters: int = 20, flush_l2: bool = True) -> float:
+    """Mean device time of ``call`` (µs): ``iters`` calls captured in one CUDA graph, replayed once
+    to warm up and once timed with CUDA events on the current stream.  With ``flush_l2`` every
+    call is preceded by a read of a buffer twice the size of L2 (so each call starts with its
+    weights and inputs in HBM, not L2), and the time of the reads alone, measured the same way,
+    is subtracted."""
+    for _ in range(2):
+        call()
+    torch.cuda.synchronize(device)
+    if not flush_l2:
+        return _graph_us(call, device, iters)
+    buf = torch.ones(FLUSH_BYTES // 4, dtype=torch.float32, device=device)
+    acc = torch.empty((), dtype=torch.float32, device=device)
+
+    def flush():
+        torch.sum(buf, out=acc)
+
+    def flushed_call():
+        flush()
+        call()
+
+    both = _graph_us(flushed_call, device, iters)
+    alone = _graph_us(flush, device, iters)
+    del buf
+    return max(both - alone, 0.0)
 
 
 @contextlib.contextmanager
@@ -143,7 +170,7 @@ def decode(cfg: dict, device, batch: int = 1, n_blocks: Optional[int] = None, st
 
 
 def outlier_batch_sweep(M: int, K: int, device, fractions: Sequence[float] = (0.0, 0.01, 0.02),
-                        batches: Sequence[int] = (1, 4, 16, 64), iters: int = 20) -> dict:
+                        batches: Sequence[int] = (1, 4, 8, 16, 64), iters: int = 20) -> dict:
     """One M x K layer at each outlier fraction: the GEMV (opc_gemv with the GEMM switched off)
     and the GEMM (opc_gemm) at each batch; bytes are the GEMV's algorithmic bytes.  ``crossover``
     is, per fraction, the smallest measured batch at which the GEMM is faster."""

@@ -1,7 +1,8 @@
 """sub_vector_size 8 (true vector quantization) on the GPU through the C ABI: dequantized weights
 bit-exact against the reference's own dequantize_layer (golden fixture) and the oracle; GEMV
 against the fp64 recompute (norm-wise relative error <= 2e-3) for batches 1..16, ragged shapes,
-outliers; paths that run svs = 1 only reject svs = 8 layers."""
+outliers; the tcgen05 prefill GEMM against the same recompute; the decode chain (svs = 1 only)
+rejects svs = 8 layers."""
 
 from pathlib import Path
 
@@ -90,10 +91,6 @@ def test_vq8_rejections(cuda_device):
         L.prepare_layer(trim, cuda_device)
     assert e.value.code == _lib.OPC_ERR_UNSUPPORTED
     dl = L.prepare_layer(synthetic.random_layer_vq8(256, 512, 2, seed=1), cuda_device)
-    x = torch.zeros(32, 512, dtype=torch.float16, device=cuda_device)
-    with pytest.raises(_lib.OpcError) as e:
-        Gm.gemm(dl, x)
-    assert e.value.code == _lib.OPC_ERR_UNSUPPORTED
     xb = torch.zeros(1, 512, dtype=torch.float16, device=cuda_device)
     yb = torch.zeros(1, 256, dtype=torch.float16, device=cuda_device)
     with pytest.raises(_lib.OpcError):
@@ -133,3 +130,29 @@ def test_vq8_gemv_with_large_staged_x_on_two_devices(cuda_device):
             dl = L.prepare_layer(layer, dev)
             y = L.gemv(dl, torch.from_numpy(x).to(dev)).cpu().numpy()
         assert oracle.rel_err(y, y64) <= REL_TOL, d
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,K,n_out,n_tok", [(200, 520, 5, 33), (1024, 4096, 10, 512), (300, 14336, 3, 16),
+                                             (4096, 1024, 41, 300), (2048, 2048, 20, 1)])
+def test_vq8_gemm_matches_fp64(cuda_device, M, K, n_out, n_tok):
+    # The prefill GEMM selects each 8-column chunk of the A tile (one codebook vector) by its 2-bit
+    # index; every token tile size and the outlier rows' dense tiles take part.
+    ly = synthetic.random_layer_vq8(M, K, n_out, seed=3 * M + K, shuffle_ids=True)
+    dl = L.prepare_layer(ly, cuda_device)
+    x = synthetic.activations(n_tok, K, seed=n_tok)
+    y = Gm.gemm(dl, torch.from_numpy(x).to(cuda_device)).cpu().numpy()
+    y64 = oracle.gemv_f64(oracle.dequantize_np(ly), x)
+    assert y.shape == (n_tok, M) and np.all(np.isfinite(y))
+    assert oracle.rel_err(y, y64) <= REL_TOL
+
+
+@pytest.mark.gpu
+def test_vq8_gemm_on_the_reference_golden_and_agrees_with_the_gemv(cuda_device):
+    layer, z = _golden("dequant_svs8")
+    dl = L.prepare_layer(layer, cuda_device)
+    x = torch.from_numpy(z["x"]).to(cuda_device)
+    y = Gm.gemm(dl, x)
+    assert oracle.rel_err(y.cpu().numpy(), z["y64"]) <= REL_TOL
+    assert torch.equal(y, Gm.gemm(dl, x))  # deterministic
+    assert oracle.rel_err(y.cpu().numpy(), L.gemv(dl, x).cpu().numpy().astype(np.float64)) <= REL_TOL
