@@ -21,8 +21,8 @@
  * opc_repack_layer converts it once, at load time, into the device layout the kernels stream
  * (see opc_layer_plan below).  sub_vector_size 1 (2 bits/weight, 4 fp16 centroids per output
  * row) runs on every path; sub_vector_size 8 (true VQ: an index selects one of 4 fp16 vectors of
- * 8 per row, the reference quantizer's default) runs opc_gemv / opc_gemv_noalloc (any batch)
- * and opc_dequant, with K a multiple of 8; other sizes, and svs 8 on the GEMM or the chain,
+ * 8 per row, the reference quantizer's default) runs opc_gemv / opc_gemv_noalloc (any batch),
+ * opc_gemm and opc_dequant, with K a multiple of 8; other sizes, and svs 8 on the decode chain,
  * return OPC_ERR_UNSUPPORTED.
  */
 #ifndef OPC_B200_H
@@ -189,9 +189,12 @@ int opc_gemv_noalloc(const opc_layer* layer, const void* x, int64_t ldx, void* y
  * (kernels/dequant_gemm.metal:34-149, loaded by metal_utils.py:188-196).
  *   x  device fp16 [n_tok][ldx], 16-byte aligned, ldx a multiple of 8 (read with TMA)
  *   y  device fp16 [n_tok][ldy] (ldy >= M)
- * Weight tiles of 128 rows are decoded from the packed indices into shared memory and multiplied
- * with 256-token x tiles by tcgen05.mma (fp16 x fp16 -> fp32 in tensor memory), rounded once to
- * fp16; outlier rows are computed by a second launch from the row-major outlier copy.  No
+ * One persistent kernel (one CTA per SM): weight tiles of 128 rows are decoded from the packed
+ * indices (sub_vector_size 1: through the row's fp16 codebook; 8: one codebook vector per 8
+ * columns) into shared memory and multiplied with x tiles of 16..256 tokens (the size chosen
+ * from n_tok and the SM count) by tcgen05.mma (fp16 x fp16 -> fp32 in tensor memory, two
+ * accumulators so that a tile's epilogue overlaps the next tile's MMAs), rounded once to fp16;
+ * outlier rows are computed as extra tiles from the row-major outlier copy.  Deterministic.  No
  * workspace.  Other x layouts return OPC_ERR_UNSUPPORTED (use opc_gemv, batch <= 64). */
 int opc_gemm(const opc_layer* layer, const void* x, int64_t ldx, void* y, int64_t ldy, int32_t n_tok,
              void* stream);
@@ -201,7 +204,9 @@ int opc_gemm(const opc_layer* layer, const void* x, int64_t ldx, void* y, int64_
  * barrier between steps: every output element is also published as a tagged 32-bit word that
  * the next step's readers poll).  Replaces per-step dispatch of MetalKernelManager.dequant_gemv for
  * a forward pass (runtime/src/inference.c:117-233 calls one layer at a time).  Each step is the
- * batch 1..2 integer GEMV of opc_gemv; results equal opc_gemv's bit for bit.
+ * batch 1..2 integer GEMV of opc_gemv: an exact integer dot product rounded once to fp16, so
+ * results are deterministic; with the max|x| scale they equal opc_gemv's bit for bit (see
+ * OPC_CHAIN_FORM_BARRIER and opc_chain_x_scale below).
  *   steps[0].x      the chain input (device fp16, ldx)
  *   steps[j].x      for j >= 1 must be steps[j-1].y with the same leading dimension (a prefix:
  *                   steps[j].layer K <= steps[j-1].layer M)
@@ -225,8 +230,14 @@ typedef struct opc_chain_step {
 int opc_chain_create(const opc_chain_step* steps, int32_t n_steps, int32_t batch, opc_chain** out);
 /* The same with an explicit form of the decode-step kernel:
  *   OPC_CHAIN_FORM_BARRIER   the step-by-step form above: each step's x is staged per CTA from the
- *                            previous step's fp16 outputs with its exponent from max|x| (as
- *                            opc_gemv does), so results equal opc_gemv's bit for bit; batch 1..2.
+ *                            previous step's fp16 outputs; batch 1..2.  Its fixed-point scale is
+ *                            the exponent of max|x| (as opc_gemv, results bit for bit equal to
+ *                            opc_gemv's) for step 0, for row-sharded chains and where shared memory
+ *                            holds only one copy of x; otherwise (one GPU, x double-buffered) steps
+ *                            >= 1 take it from a bound fixed before x exists, |x_j| <= (largest
+ *                            row L1 norm of step j-1) x max|x_{j-1}|, and convert each x chunk as
+ *                            it arrives: results then agree with opc_gemv within the GEMV
+ *                            tolerance and are deterministic (opc_chain_x_scale tells which).
  *   OPC_CHAIN_FORM_DATAFLOW  batch 1, one GPU, K <= 32768 (and the barrier form's other limits):
  *                            steps exchange their outputs as fixed-point digits whose scale is
  *                            fixed in advance from a norm bound (|y_r| <= ||W row r||_2 ||x||_2;
@@ -246,6 +257,12 @@ enum { OPC_CHAIN_FORM_AUTO = 0, OPC_CHAIN_FORM_BARRIER = 1, OPC_CHAIN_FORM_DATAF
 int opc_chain_create_ex(const opc_chain_step* steps, int32_t n_steps, int32_t batch, int32_t form, opc_chain** out);
 /* The form a chain was built with (OPC_CHAIN_FORM_BARRIER or OPC_CHAIN_FORM_DATAFLOW). */
 int32_t opc_chain_form(const opc_chain* chain);
+/* How a barrier-form chain scales steps >= 1's inputs: OPC_CHAIN_XSCALE_MAX (the exponent of
+ * max|x|, bit for bit as opc_gemv) or OPC_CHAIN_XSCALE_BOUND (from the layer bound above); 0 for
+ * the dataflow form or a NULL chain.  No counterpart in the reference (a property of this
+ * implementation's fused decode step). */
+enum { OPC_CHAIN_XSCALE_MAX = 1, OPC_CHAIN_XSCALE_BOUND = 2 };
+int32_t opc_chain_x_scale(const opc_chain* chain);
 int opc_chain_launch(opc_chain* chain, void* stream);
 int opc_chain_destroy(opc_chain* chain);
 /* Tracing: with a device buffer of opc_chain_trace_bytes() set, every launch records per step
@@ -271,9 +288,9 @@ int opc_chain_set_trace(opc_chain* chain, void* trace);
  * its contiguous shard of every step's output rows from the full x and stores each finished row
  * (fp16 and tagged exchange word, system-scope stores) straight into every rank's copies over
  * NVLink; readers poll their local copy, so no barrier separates the steps.  One cross-rank flag
- * barrier ends each launch.  No all-gather, no NCCL call, no TMA multicast.  Results equal the
- * one-GPU chain over the unsharded layers bit for bit (the dot products are exact integers;
- * every rank stages the same x).
+ * barrier ends each launch.  No all-gather, no NCCL call, no TMA multicast.  Every rank scales x
+ * by the exponent of max|x| (OPC_CHAIN_XSCALE_MAX), so results equal opc_gemv's and the NCCL
+ * form's bit for bit (the dot products are exact integers; every rank stages the same x).
  *
  * Peer-visible memory ("region"): opc_peer_alloc allocates device memory on the current GPU and
  * exports an OPC_PEER_HANDLE_BYTES handle; other ranks map it with opc_peer_open.  Each rank's
@@ -310,9 +327,10 @@ int opc_chain_create_tp(const opc_chain_step* steps, int32_t n_steps, int32_t ba
  * decoded with the same device routine the GEMV uses. */
 int opc_dequant(const opc_layer* layer, void* w, int64_t ldw, void* stream);
 
-/* GEMV -> GEMM crossover: opc_gemv runs batches above `batch` (default 16) on the prefill GEMM
- * when x is TMA-readable, and smaller batches on the GEMV kernels.  0 sends every TMA-readable
- * call to the GEMM, 64 none.  Process-wide; takes effect for later calls.  The reference has a
+/* GEMV -> GEMM crossover: opc_gemv runs batches above `batch` (default 8) on the prefill GEMM
+ * when x is TMA-readable, and smaller batches on the GEMV kernels.  The GEMM then uses opc_gemv's
+ * workspace (opc_gemv_workspace_bytes counts it for batches above 8) to split K for layers with
+ * fewer 128-row tiles than SMs.  0 sends every TMA-readable call to the GEMM, 64 none.  Process-wide; takes effect for later calls.  The reference has a
  * single GEMV dispatch (opacc1ty/utils/metal_utils.py:202-288) and no such switch; the setting
  * exists so the crossover can be measured (both kernels timed at every batch) and tuned. */
 int opc_set_gemm_crossover(int32_t batch);

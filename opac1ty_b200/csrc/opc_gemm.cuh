@@ -7,8 +7,9 @@
 // Persistent: one CTA per SM walks the output tiles c, c + grid, c + 2 grid, ...  A tile is 128
 // weight rows x N tokens (N = 16..256, chosen by the host from the token count and the SM count),
 // K in stages of 64.  Roles, all pipelined across tile boundaries:
-//   warp 0       TMA (no multicast): the X tile (N tokens x 64 fp16, 128-byte swizzle) and the
-//                packed units of the tile's 8 row tiles (one 2-D copy of 8 x 512 bytes) per stage
+//   warp 0       TMA (no multicast): the X tile (N tokens x 64 fp16, 128-byte swizzle) per stage
+//   warp 22      TMA: the packed units of the tile's 8 row tiles (one 2-D copy of 8 x 512 bytes)
+//                per stage into a deeper ring of its own, freed as soon as the stage is decoded
 //   warp 1       allocates 2N TMEM columns (two accumulators); one lane issues 4 tcgen05.mma
 //                (K = 16 each) per stage, commits each stage to its "empty" mbarrier and each
 //                finished tile to its accumulator's "full" mbarrier
@@ -36,20 +37,25 @@ constexpr int kGmDecWarps = 16;               // decoder warps: 4 groups of 4 (o
 constexpr int kGmDecGroups = kGmDecWarps / 4; // group i decodes the stages s with s % 4 == i, one row per thread
 constexpr int kGmEpiWarps = 4;                // epilogue warps: one TMEM lane quarter each
 constexpr int kGmDecWarp0 = 2, kGmEpiWarp0 = kGmDecWarp0 + kGmDecWarps;
-constexpr int kGmThreads = (kGmEpiWarp0 + kGmEpiWarps) * 32;
+constexpr int kGmUnitWarp = kGmEpiWarp0 + kGmEpiWarps;  // the packed units' producer
+constexpr int kGmThreads = (kGmUnitWarp + 1) * 32;
+constexpr int kGmUStages = 8;                  // packed-units ring (its own barriers, ahead of the A/B ring)
 constexpr int kGmABytes = kGmM * kGmK * 2;   // 16 KB
 constexpr int kGmUBytes = 8 * kUnitBytes;    // 8 row tiles x one unit
+constexpr int kGmMaxSplit = 8;                // K split of a tile into at most this many items
 constexpr int kGmPrefetch = 24;               // stages ahead whose packed units are prefetched into L2
 constexpr int kGmSmemBudget = 227 * 1024 - 1024 - 512;  // dynamic shared memory less slack and barriers
 // Token tile N: x stage N*64 fp16, two accumulators of N fp32 TMEM columns.
 __host__ __device__ constexpr int gm_b_bytes(int N) { return N * kGmK * 2; }
-__host__ __device__ constexpr int gm_stage_bytes(int N) { return kGmABytes + gm_b_bytes(N) + kGmUBytes; }
+__host__ __device__ constexpr int gm_stage_bytes(int N) { return kGmABytes + gm_b_bytes(N); }
 __host__ __device__ constexpr int gm_stages(int N) {
-  return kGmSmemBudget / gm_stage_bytes(N) > 8 ? 8 : kGmSmemBudget / gm_stage_bytes(N);
+  return (kGmSmemBudget - kGmUStages * kGmUBytes) / gm_stage_bytes(N) > 8
+             ? 8
+             : (kGmSmemBudget - kGmUStages * kGmUBytes) / gm_stage_bytes(N);
 }
 __host__ __device__ constexpr int gm_tmem_cols(int N) { return 2 * N < 32 ? 32 : 2 * N; }
 __host__ __device__ constexpr size_t gm_smem_bytes(int N) {
-  return 1024 /*alignment slack*/ + static_cast<size_t>(gm_stages(N)) * gm_stage_bytes(N) + 512;
+  return 1024 /*alignment slack*/ + static_cast<size_t>(gm_stages(N)) * gm_stage_bytes(N) + kGmUStages * kGmUBytes + 512;
 }
 
 struct GemmArgs {
@@ -66,6 +72,12 @@ struct GemmArgs {
   int32_t m_tiles;             // packed M tiles; M tile indices >= m_tiles are dense (outlier rows)
   int32_t n_tiles;             // token tiles
   int32_t tiles;               // (m_tiles + dense tiles) * n_tiles
+  // split K: every tile is computed as ksplit items of nk_slice stages (the last one shorter); the
+  // items' fp32 partials go to part and the last item of a tile to arrive (cnt) adds them in
+  // slice order (deterministic), zeroes them and writes y.  ksplit 1: no workspace.
+  int32_t ksplit, nk_slice;
+  float* part;                 // [tiles][ksplit][128][N] fp32
+  int32_t* cnt;                // [tiles][4] arrivals per TMEM lane quarter (zero between calls)
 };
 
 // UMMA shared-memory descriptor: K-major, 128-byte swizzle, 8-row groups 1024 bytes apart.
@@ -160,9 +172,10 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_consta
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   const uint32_t sA = base, sB = sA + kS * kGmABytes, sU = sB + kS * kBBytes;
-  const uint32_t bars = sU + kS * kGmUBytes;
+  const uint32_t bars = sU + kGmUStages * kGmUBytes;
   const uint32_t full_b = bars, afull_b = bars + 8 * kS, empty_b = bars + 16 * kS;
-  const uint32_t accf_b = bars + 24 * kS, acce_b = accf_b + 16, drain_b = acce_b + 16, tmem_slot = drain_b + 8;
+  const uint32_t ufull_b = bars + 24 * kS, uempty_b = ufull_b + 8 * kGmUStages;
+  const uint32_t accf_b = uempty_b + 8 * kGmUStages, acce_b = accf_b + 16, drain_b = acce_b + 16, tmem_slot = drain_b + 8;
   unsigned char* tmem_slot_ptr = smem_raw + (tmem_slot - raw);
 
   const int warp = __shfl_sync(0xffffffffu, static_cast<int>(threadIdx.x >> 5), 0);
@@ -175,6 +188,10 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_consta
       mbar_init(full_b + 8 * s, 1);
       mbar_init(afull_b + 8 * s, 4);  // one arrival per warp of the stage's decoder group
       mbar_init(empty_b + 8 * s, 1);
+    }
+    for (int u = 0; u < kGmUStages; ++u) {
+      mbar_init(ufull_b + 8 * u, 1);
+      mbar_init(uempty_b + 8 * u, 4);  // the decoder group of the stage
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(accf_b + 8 * b, 1);
@@ -195,39 +212,21 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_consta
   bool ok = true;
 
   if (warp == 0) {
-    // ---------------------------------------------------------------- producer
+    // ---------------------------------------------------------------- x producer
     if (lane == 0) {
-      int g = 0;  // stages issued (all tiles)
-      for (int i = blockIdx.x; i < a.tiles && ok; i += G) {
-        const int mi = i / a.n_tiles, n0 = (i - mi * a.n_tiles) * kN;
-        const bool packed = mi < a.m_tiles;
-        // a box past the last row tile is filled with zeros and still counts its full size
-        const uint32_t ubytes = a.svs8 ? 8u * kVq8UnitBytesGm : static_cast<uint32_t>(kGmUBytes);
-        const uint32_t bytes = kBBytes + (packed ? ubytes : 0u);
-        for (int s = 0; s < nk; ++s, ++g) {
+      int g = 0;  // stages issued (all items)
+      for (int it = blockIdx.x; it < a.tiles * a.ksplit && ok; it += G) {
+        const int i = it / a.ksplit, ks = it - i * a.ksplit;
+        const int s0 = ks * a.nk_slice, s1 = min(nk, s0 + a.nk_slice);
+        const int n0 = (i % a.n_tiles) * kN;
+        for (int s = s0; s < s1; ++s, ++g) {
           const int st = g % kS;
           if (g >= kS && !mbar_wait_bounded(empty_b + 8 * st, ((g / kS) - 1) & 1)) {
             ok = false;
             break;
           }
-          // the packed units of the stage kGmPrefetch stages ahead go to L2 now, so that their load
-          // (HBM latency) is off the ring's round trip; one prefetch per k block
-          {
-            const int gf = g + kGmPrefetch, it = gf / nk, sf = gf - it * nk;
-            const int ifut = blockIdx.x + it * G;
-            if (ifut < a.tiles && (sf & (a.svs8 ? 3 : 1)) == 0) {
-              const int mf = ifut / a.n_tiles;
-              if (mf < a.m_tiles)
-                tma_prefetch_2d(&tu, a.svs8 ? (sf >> 2) * (kVq8UnitBytesGm / 8) : (sf >> 1) * (kUnitBytes / 8), mf * 8);
-            }
-          }
-          mbar_expect_tx(full_b + 8 * st, bytes);
+          mbar_expect_tx(full_b + 8 * st, kBBytes);
           tma_load_2d(sB + st * kBBytes, &tx, s * kGmK, n0, full_b + 8 * st);
-          // x coordinate: the k block of the stage in 8-byte elements (512-byte units of 128 columns,
-          // or 128-byte svs-8 units of 256 columns: 16-byte aligned either way)
-          if (packed)
-            tma_load_2d(sU + st * kGmUBytes, &tu, a.svs8 ? (s >> 2) * (kVq8UnitBytesGm / 8) : (s >> 1) * (kUnitBytes / 8),
-                        mi * 8, full_b + 8 * st);
         }
       }
       // copies nobody consumed (a role gave up) land before the CTA exits: wait (bounded) for
@@ -237,11 +236,48 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_consta
         mbar_wait_bounded(full_b + 8 * st, (last / kS) & 1);
       }
     }
+  } else if (warp == kGmUnitWarp) {
+    // ---------------------------------------------------------------- packed-units producer
+    // Its ring runs ahead of the A/B stages (a slot is free once its decoder group is done), so a
+    // stage's decode waits neither for the x tile nor for the MMAs of the stages before it.
+    if (lane == 0) {
+      const uint32_t ubytes = a.svs8 ? 8u * kVq8UnitBytesGm : static_cast<uint32_t>(kGmUBytes);
+      int gu = 0;  // packed stages issued
+      for (int it = blockIdx.x; it < a.tiles * a.ksplit && ok; it += G) {
+        const int i = it / a.ksplit, ks = it - i * a.ksplit;
+        const int mi = i / a.n_tiles;
+        if (mi >= a.m_tiles) continue;  // dense tiles: no units
+        const int s0 = ks * a.nk_slice, s1 = min(nk, s0 + a.nk_slice);
+        for (int s = s0; s < s1; ++s, ++gu) {
+          const int su = gu % kGmUStages;
+          if (gu >= kGmUStages && !mbar_wait_bounded(uempty_b + 8 * su, ((gu / kGmUStages) - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          // the units kGmPrefetch stages ahead (same item) go to L2 now; one prefetch per k block
+          const int sf = s + kGmPrefetch;
+          if (sf < s1 && (sf & (a.svs8 ? 3 : 1)) == 0)
+            tma_prefetch_2d(&tu, a.svs8 ? (sf >> 2) * (kVq8UnitBytesGm / 8) : (sf >> 1) * (kUnitBytes / 8), mi * 8);
+          // a box past the last row tile is filled with zeros and still counts its full size; x
+          // coordinate: the stage's k block in 8-byte elements (512-byte units of 128 columns, or
+          // 128-byte svs-8 units of 256 columns: 16-byte aligned either way)
+          mbar_expect_tx(ufull_b + 8 * su, ubytes);
+          tma_load_2d(sU + su * kGmUBytes, &tu, a.svs8 ? (s >> 2) * (kVq8UnitBytesGm / 8) : (s >> 1) * (kUnitBytes / 8),
+                      mi * 8, ufull_b + 8 * su);
+        }
+      }
+      for (int su = 0; su < kGmUStages && su < gu; ++su) {
+        const int last = gu - 1 - ((gu - 1 - su) % kGmUStages);
+        mbar_wait_bounded(ufull_b + 8 * su, (last / kGmUStages) & 1);
+      }
+    }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       int g = 0, tl = 0;
-      for (int i = blockIdx.x; i < a.tiles && ok; i += G, ++tl) {
+      for (int it = blockIdx.x; it < a.tiles * a.ksplit && ok; it += G, ++tl) {
+        const int ks = it % a.ksplit;
+        const int s0 = ks * a.nk_slice, s1 = min(nk, s0 + a.nk_slice);
         const int b = tl & 1;
         // the epilogue has read accumulator b's previous tile
         if (tl >= 2 && !mbar_wait_bounded(acce_b + 8 * b, ((tl >> 1) - 1) & 1)) {
@@ -250,7 +286,7 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_consta
         }
         tc_fence_after();
         const uint32_t tacc = tmem + static_cast<uint32_t>(b * kN);
-        for (int s = 0; s < nk; ++s, ++g) {
+        for (int s = s0; s < s1; ++s, ++g) {
           const int st = g % kS;
           const uint32_t par = (g / kS) & 1;
           if (!mbar_wait_bounded(full_b + 8 * st, par) || !mbar_wait_bounded(afull_b + 8 * st, par)) {
@@ -261,7 +297,7 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_consta
           const uint64_t ad = umma_desc_sw128(sA + st * kGmABytes), bd = umma_desc_sw128(sB + st * kBBytes);
 #pragma unroll
           for (int kk = 0; kk < kGmK / 16; ++kk)  // +32 bytes per K = 16 step inside the swizzle atom
-            umma_f16(tacc, ad + 2 * kk, bd + 2 * kk, gm_idesc(kN), (s > 0 || kk > 0) ? 1u : 0u);
+            umma_f16(tacc, ad + 2 * kk, bd + 2 * kk, gm_idesc(kN), (s > s0 || kk > 0) ? 1u : 0u);
           umma_commit(empty_b + 8 * st);
         }
         if (!ok) break;
@@ -277,8 +313,10 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_consta
     const int r = 32 * (d & 3) + lane;  // tile row
     const int grp = d >> 2;             // this warp's group: every kGmDecGroups-th stage
     const int tl_row = r >> 4, gl = (r & 15) & 7, hi = (r & 15) >> 3;
-    int g = 0;
-    for (int i = blockIdx.x; i < a.tiles && ok; i += G) {
+    int g = 0, gu = 0;  // stages, and packed stages (the units ring's counter)
+    for (int it = blockIdx.x; it < a.tiles * a.ksplit && ok; it += G) {
+      const int i = it / a.ksplit, ks = it - i * a.ksplit;
+      const int s0 = ks * a.nk_slice, s1 = min(nk, s0 + a.nk_slice);
       const int mi = i / a.n_tiles;
       const bool dense = mi >= a.m_tiles;
       const int R = (dense ? mi - a.m_tiles : mi) * kGmM + r;  // weight row (packed) or outlier slot (dense)
@@ -301,10 +339,11 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_consta
           cv[q] = (row_live && !dense) ? __ldg(a.cb8 + (static_cast<int64_t>(R >> 4) * 32 + 4 * gl + q) * 2 + hi)
                                        : make_uint4(0, 0, 0, 0);
       }
-      for (int s = 0; s < nk; ++s, ++g) {
+      for (int s = s0; s < s1; ++s, ++g) {
+        const int gs = dense ? 0 : gu++;          // this stage's place in the units ring
         if ((g % kGmDecGroups) != grp) continue;  // another group's stage
+        const int su = gs % kGmUStages;
         const int st = g % kS;
-        const uint32_t par = (g / kS) & 1;
         if (g >= kS && !mbar_wait_bounded(empty_b + 8 * st, ((g / kS) - 1) & 1)) {
           ok = false;
           break;
@@ -315,14 +354,14 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_consta
 #pragma unroll
           for (int c = 0; c < 8; ++c) sts128(dstA + sw128_off(r, c), row_live ? __ldg(src + c) : make_uint4(0, 0, 0, 0));
         } else {
-          if (!mbar_wait_bounded(full_b + 8 * st, par)) {
+          if (!mbar_wait_bounded(ufull_b + 8 * su, (gs / kGmUStages) & 1)) {
             ok = false;
             break;
           }
           if (a.svs8) {
             // word s&3 of row pair gl's 16 bytes: byte c/2 = k16 step, bits 2(c&1) + 4hi = the index of
             // chunk c (8 columns = one codebook vector)
-            const uint32_t w = row_live ? lds32(sU + st * kGmUBytes + tl_row * kVq8UnitBytesGm + gl * 16 + 4 * (s & 3)) : 0u;
+            const uint32_t w = row_live ? lds32(sU + su * kGmUBytes + tl_row * kVq8UnitBytesGm + gl * 16 + 4 * (s & 3)) : 0u;
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
               const uint32_t i = (w >> (8 * (c >> 1) + 2 * (c & 1) + 4 * hi)) & 3u;
@@ -333,7 +372,7 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_consta
             }
           } else {
             // chunk c = 4jj + q of the stage (columns 32jj + 8q + 0..7) is in word 2(s&1) + jj of lane 4gl + q
-            const uint32_t ub = sU + st * kGmUBytes + tl_row * kUnitBytes + (4 * gl) * 16 + 8 * (s & 1);
+            const uint32_t ub = sU + su * kGmUBytes + tl_row * kUnitBytes + (4 * gl) * 16 + 8 * (s & 1);
             uint32_t w[8];
 #pragma unroll
             for (int c = 0; c < 8; ++c) w[c] = row_live ? lds32(ub + (c & 3) * 16 + 4 * (c >> 2)) : 0u;
@@ -347,7 +386,10 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_consta
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(afull_b + 8 * st);
+        if (lane == 0) {
+          mbar_arrive(afull_b + 8 * st);
+          if (!dense) mbar_arrive(uempty_b + 8 * su);  // the units slot may be refilled
+        }
       }
     }
   } else {
@@ -355,8 +397,10 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_consta
     const int quarter = warp & 3;        // TMEM lanes 32*quarter .. +31 (a warp's lane quarter is warp % 4)
     const int r = 32 * quarter + lane;   // tile row = TMEM lane
     const uint32_t trow = tmem + (static_cast<uint32_t>(32 * quarter) << 16);
+    constexpr int kCols = kN < 32 ? kN : 32;  // accumulator columns per tcgen05.ld
     int tl = 0;
-    for (int i = blockIdx.x; i < a.tiles && ok; i += G, ++tl) {
+    for (int it = blockIdx.x; it < a.tiles * a.ksplit && ok; it += G, ++tl) {
+      const int i = it / a.ksplit, ks = it - i * a.ksplit;
       const int mi = i / a.n_tiles, n0 = (i - mi * a.n_tiles) * kN;
       const bool dense = mi >= a.m_tiles;
       const int R = (dense ? mi - a.m_tiles : mi) * kGmM + r;
@@ -374,26 +418,23 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_consta
       }
       tc_fence_after();
       const uint32_t tacc = trow + static_cast<uint32_t>(b * kN);
-      if constexpr (kN >= 32) {
+      // this item's partial of row r (split K only): fp32, kN consecutive values
+      float* prow = a.ksplit > 1 ? a.part + (static_cast<int64_t>(i) * a.ksplit + ks) * (kGmM * kN) +
+                                       static_cast<int64_t>(r) * kN
+                                 : nullptr;
 #pragma unroll 1
-        for (int cc = 0; cc < kN / 32; ++cc) {
-          uint32_t v[32];
-          tmem_ld32(tacc + cc * 32, v);
-          if (out_row >= 0) {
+      for (int cc = 0; cc < kN / kCols; ++cc) {
+        uint32_t v[kCols];
+        if constexpr (kCols == 32) tmem_ld32(tacc + cc * 32, v);
+        else tmem_ld16(tacc, v);
+        if (prow) {
 #pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              const int tok = n0 + cc * 32 + e;
-              if (tok < a.n_tok) a.y[static_cast<int64_t>(tok) * a.ldy + out_row] = __float2half_rn(__uint_as_float(v[e]));
-            }
-          }
-        }
-      } else {
-        uint32_t v[16];
-        tmem_ld16(tacc, v);
-        if (out_row >= 0) {
+          for (int e = 0; e < kCols; e += 4)
+            *reinterpret_cast<uint4*>(prow + cc * kCols + e) = make_uint4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+        } else if (out_row >= 0) {
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const int tok = n0 + e;
+          for (int e = 0; e < kCols; ++e) {
+            const int tok = n0 + cc * kCols + e;
             if (tok < a.n_tok) a.y[static_cast<int64_t>(tok) * a.ldy + out_row] = __float2half_rn(__uint_as_float(v[e]));
           }
         }
@@ -401,6 +442,48 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_consta
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acce_b + 8 * b);
+      if (prow) {
+        // the warp that completes its lane quarter's count for this tile adds the slices in order
+        __syncwarp();  // the lanes' partial stores are ordered before lane 0's release below
+        int old = 0;
+        if (lane == 0) old = atom_add_acq_rel_gpu(a.cnt + 4 * i + quarter, 1);
+        old = __shfl_sync(0xffffffffu, old, 0);
+        __syncwarp();
+        if (old == a.ksplit - 1) {
+          // The workspace holds zeros between calls outside the GEMV's scratch slots (another
+          // layer's counters and accumulators may lie here), so the partials are zeroed as they
+          // are read, and the count reset.
+          if (lane == 0) a.cnt[4 * i + quarter] = 0;
+          float* p0 = a.part + static_cast<int64_t>(i) * a.ksplit * (kGmM * kN) + static_cast<int64_t>(r) * kN;
+          // every slice's values of 4 columns are loaded at once (up to kGmMaxSplit in flight),
+          // then added in slice order
+#pragma unroll 1
+          for (int e = 0; e < kN; e += 4) {
+            float4 t[kGmMaxSplit];
+#pragma unroll
+            for (int k2 = 0; k2 < kGmMaxSplit; ++k2)
+              if (k2 < a.ksplit) t[k2] = __ldcg(reinterpret_cast<const float4*>(p0 + static_cast<int64_t>(k2) * (kGmM * kN) + e));
+            float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int k2 = 0; k2 < kGmMaxSplit; ++k2) {
+              if (k2 < a.ksplit) {
+                *reinterpret_cast<float4*>(p0 + static_cast<int64_t>(k2) * (kGmM * kN) + e) = make_float4(0.f, 0.f, 0.f, 0.f);
+                sum.x += t[k2].x;
+                sum.y += t[k2].y;
+                sum.z += t[k2].z;
+                sum.w += t[k2].w;
+              }
+            }
+            if (out_row >= 0) {
+              const float vals[4] = {sum.x, sum.y, sum.z, sum.w};
+#pragma unroll
+              for (int u = 0; u < 4; ++u)
+                if (n0 + e + u < a.n_tok)
+                  a.y[static_cast<int64_t>(n0 + e + u) * a.ldy + out_row] = __float2half_rn(vals[u]);
+            }
+          }
+        }
+      }
     }
   }
   if (!ok && lane == 0) atomicCAS(&g_opc_device_error, 0, kDevErrTmaTimeout);

@@ -121,7 +121,7 @@ constexpr int kCtasPerSm = 2;
 constexpr int kXsMaxBytes = OPC_XS_MAX_BYTES;
 constexpr int kMaxBatch = 64;
 // opc_gemv runs batches above this on the prefill GEMM (opc_set_gemm_crossover)
-std::atomic<int> g_gemm_crossover{16};
+std::atomic<int> g_gemm_crossover{8};
 
 int nt_for_batch(int batch) {
   if (batch <= 8) return 1;
@@ -156,7 +156,61 @@ size_t acc_offset(const opc_layer_plan& p, int sm_count) {
   return counters_offset(sm_count) + align_up(static_cast<size_t>(p.row_tiles + p.outlier_tiles) * sizeof(int32_t), 256);
 }
 
-size_t workspace_bytes(const opc_layer_plan& p, int /*batch*/, int sm_count) {
+// Launch shape of the prefill GEMM for n_tok tokens: token tile tn (16..256) and K split, chosen
+// by the least estimated time -- waves of persistent items (one CTA per SM) times the stages of an
+// item times the cost of a stage (the larger of the A-tile decode, ~300 cycles, and the MMAs,
+// ~2N cycles for 128 x N x 64 on one SM).  A K split (only with a workspace, split_ok) cuts a tile
+// into items of at least 8 stages whose fp32 partials are added in a fixed order.
+struct GemmPlan {
+  int tn = 16, ksplit = 1, nk_slice = 1;
+  int64_t tiles = 0;        // (packed M tiles + dense tiles) x token tiles
+  size_t split_bytes = 0;   // workspace of the split: [tiles][4] counters, then the fp32 partials
+};
+GemmPlan gemm_plan(const opc_layer_plan& p, int n_tok, int sm_count, bool split_ok) {
+  const int64_t m_tiles = ceil_div(p.M_pad, opc::kGmM);
+  const int64_t d_tiles = p.n_outliers > 0 ? ceil_div(static_cast<int64_t>(p.outlier_tiles) * opc::kTileRows, opc::kGmM) : 0;
+  const int nk = p.K_pad / opc::kGmK;
+  GemmPlan best;
+  double best_cost = -1.0;
+  for (int N = 16; N <= 256; N *= 2) {
+    if (N > 16 && N / 2 >= n_tok) break;  // a smaller tile already covers every token
+    const int64_t tiles = (m_tiles + d_tiles) * ceil_div(n_tok, N);
+    for (int S = 1; S <= (split_ok ? opc::kGmMaxSplit : 1); ++S) {
+      const int slice = static_cast<int>(ceil_div(nk, S));
+      // a split only for layers with fewer tiles than SMs, into one wave of items of >= 16 stages
+      if (S > 1 && (tiles >= sm_count || tiles * S > sm_count || slice < 16 || ceil_div(nk, slice) != S)) continue;
+      const double waves = static_cast<double>(ceil_div(tiles * S, sm_count));
+      // + the split's epilogue: partials out, and the last arrival reading and adding them
+      const double cost = waves * slice * std::max(300.0, 2.0 * N) + (S > 1 ? 3000.0 + 500.0 * S : 0.0);
+      if (best_cost < 0.0 || cost < best_cost) {
+        best_cost = cost;
+        best.tn = N;
+        best.ksplit = S;
+        best.nk_slice = slice;
+        best.tiles = tiles;
+      }
+    }
+  }
+  if (best.ksplit > 1)
+    best.split_bytes = align_up(static_cast<size_t>(best.tiles) * 4 * sizeof(int32_t), 256) +
+                       static_cast<size_t>(best.tiles) * best.ksplit * opc::kGmM * best.tn * sizeof(float);
+  return best;
+}
+
+int gemm_run(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ldy, int32_t n_tok, void* ws,
+             size_t ws_bytes, void* stream_v);
+
+// The opc_gemv workspace proper (partial-sum slots, counters, int64 accumulators), before the
+// part a GEMM with a K split uses for batches routed to it.
+size_t gemv_workspace_base(const opc_layer_plan& p, int sm_count);
+
+size_t workspace_bytes(const opc_layer_plan& p, int batch, int sm_count) {
+  // batches above 8 may be routed to the GEMM (opc_set_gemm_crossover): room for its K split
+  const size_t split = batch > 8 ? align_up(gemm_plan(p, batch, sm_count, true).split_bytes, 256) : 0;
+  return gemv_workspace_base(p, sm_count) + split;
+}
+
+size_t gemv_workspace_base(const opc_layer_plan& p, int sm_count) {
   return acc_offset(p, sm_count) + static_cast<size_t>(p.M_pad) * opc::kQMaxBatch * sizeof(unsigned long long);
 }
 
@@ -574,11 +628,14 @@ int opc_gemv(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ld
   if (p.total_units >= (int64_t(1) << 31)) return fail(OPC_ERR_UNSUPPORTED, "opc_gemv: layer too large (2^31 units)");
   cudaStream_t s = static_cast<cudaStream_t>(stream_v);
 
-  // Batches above the crossover (default 16): the tcgen05 GEMM (measured 9x faster than the fp16
-  // GEMV at 64 rows of a 14336x4096 layer; at 16 rows the two are even on 8B shapes and the GEMV
-  // wins on 70B shapes) when x can be read with TMA.
-  if (batch > g_gemm_crossover.load(std::memory_order_relaxed) && aligned(x, 16) && ldx % 8 == 0)
-    return opc_gemm(L, x, ldx, y, ldy, batch, stream_v);
+  // Batches above the crossover (default 8): the tcgen05 GEMM when x can be read with TMA
+  // (measured, L2 flushed: faster than the fp16 GEMV from batch 16 on on every Llama-3.1-8B and
+  // Llama-3-70B projection -- 1.3-1.8x at 16 rows, 4-20x at 64 -- slower at 8).
+  if (batch > g_gemm_crossover.load(std::memory_order_relaxed) && aligned(x, 16) && ldx % 8 == 0) {
+    const size_t base = gemv_workspace_base(p, dc.sm_count);
+    return gemm_run(L, x, ldx, y, ldy, batch, static_cast<char*>(workspace) + base, workspace_bytes_given - base,
+                    stream_v);
+  }
 
   // Batch 1..2: the integer kernel, when its staged x and at least two ring stages fit.
   if (batch <= opc::kQMaxBatch) {
@@ -812,7 +869,14 @@ int opc_dequant(const opc_layer* L, void* w, int64_t ldw, void* stream_v) {
   return OPC_OK;
 }
 
-int opc_gemm(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ldy, int32_t n_tok, void* stream_v) {
+}  // extern "C"
+
+namespace {
+
+// The prefill GEMM for opc_gemm (no workspace) and for batches opc_gemv routes to it (its
+// workspace past the GEMV's own part: `ws`, `ws_bytes`, which allow a K split).
+int gemm_run(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ldy, int32_t n_tok, void* ws,
+             size_t ws_bytes, void* stream_v) {
   if (!L || !plan_ok(&L->plan)) return fail(OPC_ERR_INVALID, "opc_gemm: invalid layer plan");
   const opc_layer_plan& p = L->plan;
   const bool svs8 = p.sub_vector_size == 8;
@@ -837,25 +901,10 @@ int opc_gemm(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ld
   DeviceCache dc;
   int rc = device_cache(dev, &dc);
   if (rc != OPC_OK) return rc;
-  // Token tile N: the candidate with the least estimated time, counting waves of persistent tiles
-  // (one CTA per SM) times the cost of a K stage -- the larger of the A-tile decode (~300 cycles
-  // with 8 decoder warps) and the MMAs (~2N cycles for 128 x N x 64 on one SM).
+  GemmPlan gp = gemm_plan(p, n_tok, dc.sm_count, ws != nullptr);
+  if (gp.ksplit > 1 && (ws_bytes < gp.split_bytes || !aligned(ws, 256))) gp = gemm_plan(p, n_tok, dc.sm_count, false);
+  const int tn = gp.tn;
   const int64_t m_tiles = ceil_div(p.M_pad, opc::kGmM);
-  const int64_t d_tiles = p.n_outliers > 0 ? ceil_div(static_cast<int64_t>(p.outlier_tiles) * opc::kTileRows, opc::kGmM) : 0;
-  int tn = 16;
-  {
-    double best = 0.0;
-    for (int N = 16; N <= 256; N *= 2) {
-      if (N > 16 && N / 2 >= n_tok) break;  // a smaller tile already covers every token
-      const int64_t tiles = (m_tiles + d_tiles) * ceil_div(n_tok, N);
-      const double waves = static_cast<double>(ceil_div(tiles, dc.sm_count));
-      const double cost = waves * std::max(300.0, 2.0 * N);
-      if (N == 16 || cost <= best) {
-        best = cost;
-        tn = N;
-      }
-    }
-  }
   if (opc::gm_smem_bytes(tn) > static_cast<size_t>(dc.max_smem_optin))
     return fail(OPC_ERR_UNSUPPORTED, "opc_gemm: needs %zu bytes of shared memory", opc::gm_smem_bytes(tn));
 
@@ -904,10 +953,16 @@ int opc_gemm(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ld
   cudaStream_t s = static_cast<cudaStream_t>(stream_v);
   a.m_tiles = static_cast<int32_t>(m_tiles);
   a.n_tiles = static_cast<int32_t>(ceil_div(n_tok, tn));
-  const int64_t tiles = (m_tiles + d_tiles) * a.n_tiles;
-  if (tiles >= (int64_t(1) << 31)) return fail(OPC_ERR_UNSUPPORTED, "opc_gemm: too many tiles");
+  const int64_t tiles = gp.tiles;
+  if (tiles * gp.ksplit >= (int64_t(1) << 31)) return fail(OPC_ERR_UNSUPPORTED, "opc_gemm: too many tiles");
   a.tiles = static_cast<int32_t>(tiles);
-  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(tiles, dc.sm_count));
+  a.ksplit = gp.ksplit;
+  a.nk_slice = gp.ksplit > 1 ? gp.nk_slice : p.K_pad / opc::kGmK;
+  if (gp.ksplit > 1) {
+    a.cnt = static_cast<int32_t*>(ws);  // zero between calls: the last arrival of each count resets it
+    a.part = reinterpret_cast<float*>(static_cast<char*>(ws) + align_up(static_cast<size_t>(tiles) * 4 * sizeof(int32_t), 256));
+  }
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(tiles * gp.ksplit, dc.sm_count));
   switch (tn) {
     case 256: return launch_gemm_t<256>(tx, tu, a, grid, s, dev);
     case 128: return launch_gemm_t<128>(tx, tu, a, grid, s, dev);
@@ -917,6 +972,14 @@ int opc_gemm(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ld
   }
 }
 
+}  // namespace
+
+extern "C" {
+
+int opc_gemm(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ldy, int32_t n_tok, void* stream_v) {
+  return gemm_run(L, x, ldx, y, ldy, n_tok, nullptr, 0, stream_v);
+}
+
 }  // extern "C"
 
 // ---------------------------------------------------------------------------------------------
@@ -924,7 +987,7 @@ int opc_gemm(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ld
 // ---------------------------------------------------------------------------------------------
 struct opc_chain {
   int device = 0;
-  int32_t n_layers = 0, batch = 1, stages = 2, xs_bytes = 0, grid = 0, xc = 8;
+  int32_t n_layers = 0, batch = 1, stages = 2, xs_bytes = 0, xs_buf = 0, grid = 0, xc = 8;
   int32_t rank = 0, world = 1;
   size_t smem = 0;
   void* dev_mem = nullptr;              // [layers | onc | parts | epoch | acc (| flags | words)]
@@ -1091,16 +1154,21 @@ int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t 
     kt_max = std::max(kt_max, steps[j].layer->plan.k_units);
     bk_max = std::max<int64_t>(bk_max, static_cast<int64_t>(batch) * steps[j].layer->plan.K_pad);
   }
-  const int xs = static_cast<int>(align_up(static_cast<size_t>(3 * batch) * opc::xsq_col_bytes(kt_max) +
-                                          opc::kQZeroBytes + opc::kQOnesBytes, 128));
-  auto smem_for = [&](int stages) {
-    return static_cast<size_t>(xs) + static_cast<size_t>(opc::kQConsumers) * stages * (opc::kQChunkBytes + 16) +
+  // Staged x: one digit buffer, or two (by layer parity) when they fit next to two ring stages --
+  // then layers >= 1 convert x as it arrives (see the chain kernel's staging).
+  const int xs_one = static_cast<int>(align_up(static_cast<size_t>(3 * batch) * opc::xsq_col_bytes(kt_max), 128));
+  auto smem_for = [&](int xs_total, int stages) {
+    return static_cast<size_t>(xs_total) + static_cast<size_t>(opc::kQConsumers) * stages * (opc::kQChunkBytes + 16) +
            sizeof(opc::ChainShared);
   };
+  const int ones_zero = opc::kQZeroBytes + opc::kQOnesBytes;
+  // (one GPU only: the row-sharded form keeps every rank's x scale from the exact max, as opc_gemv)
+  const bool dbl = world == 1 && smem_for(2 * xs_one + ones_zero, 2) <= static_cast<size_t>(dc.max_smem_optin);
+  const int xs = (dbl ? 2 * xs_one : xs_one) + ones_zero;
   int stages = opc::kQMaxStages;
-  while (stages >= 2 && smem_for(stages) > static_cast<size_t>(dc.max_smem_optin)) --stages;
+  while (stages >= 2 && smem_for(xs, stages) > static_cast<size_t>(dc.max_smem_optin)) --stages;
   if (stages < 2) return fail(OPC_ERR_UNSUPPORTED, "%s: staged x too large for shared memory", fn);
-  const size_t smem = smem_for(stages);
+  const size_t smem = smem_for(xs, stages);
   const int xc = bk_max <= 4 * 8 * opc::kQConsumerThreads ? 4 : 8;
   const bool multi = world > 1;
   auto kern = xc == 4 ? (multi ? opc::chain_kernel<4, true> : opc::chain_kernel<4, false>)
@@ -1174,6 +1242,33 @@ int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t 
       off += chain_words_bytes(steps[j].ldy, batch);
     }
   }
+  // One GPU with double-buffered x: every layer's largest row L1 norm, the bound from which the
+  // next layer's input scale is fixed before that input exists (fp32 sums, +1 % margin).
+  std::vector<float> wbound(n, 0.0f);
+  if (dbl) {
+    unsigned int* wb_dev = nullptr;
+    OPC_CUDA(cudaMalloc(&wb_dev, sizeof(unsigned int) * n), "cudaMalloc(chain bounds)");
+    cudaError_t e = cudaMemset(wb_dev, 0, sizeof(unsigned int) * n);
+    for (int j = 0; j < n && e == cudaSuccess; ++j) {
+      const opc_layer* L = steps[j].layer;
+      const opc_layer_plan& p = L->plan;
+      const int32_t n_dense = p.n_outliers > 0 ? p.outlier_tiles * opc::kTileRows : 0;
+      const int64_t warps = static_cast<int64_t>(p.row_tiles) + n_dense;
+      opc::row_l1_max_kernel<<<static_cast<unsigned>(ceil_div(warps * 32, 256)), 256>>>(
+          static_cast<const uint8_t*>(L->units), static_cast<const uint2*>(L->codebooks), p.row_tiles, p.k_units,
+          dense_outliers(L), n_dense, p.K_pad, wb_dev + j);
+      e = cudaGetLastError();
+    }
+    std::vector<unsigned int> bits(n, 0u);
+    if (e == cudaSuccess) e = cudaMemcpy(bits.data(), wb_dev, sizeof(unsigned int) * n, cudaMemcpyDeviceToHost);
+    cudaFree(wb_dev);
+    if (e != cudaSuccess) return cuda_fail(e, "chain: layer bounds");
+    for (int j = 0; j < n; ++j) {
+      float f;
+      memcpy(&f, &bits[j], sizeof(f));
+      wbound[j] = f * 1.01f;
+    }
+  }
   void* mem = nullptr;
   OPC_CUDA(cudaMalloc(&mem, off), "cudaMalloc(chain)");
   char* base = static_cast<char*>(mem);
@@ -1213,6 +1308,7 @@ int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t 
     c.x_vec16 = (p.K % 8 == 0) && (st.ldx % 8 == 0) && aligned(st.x, 16);
     c.row_off = row_off[j];
     c.m_full = m_full[j];
+    c.wbound = wbound[j];
     // a later step writing the same fp16 buffer makes this step's fp16 stores dead
     c.write_y = 1;
     for (int k = j + 1; k < n; ++k)
@@ -1241,6 +1337,7 @@ int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t 
   ch->batch = batch;
   ch->stages = stages;
   ch->xs_bytes = xs;
+  ch->xs_buf = dbl ? xs_one : 0;
   ch->smem = smem;
   ch->grid = G;
   ch->xc = xc;
@@ -1743,6 +1840,7 @@ int opc_chain_launch(opc_chain* ch, void* stream_v) {
   a.batch = ch->batch;
   a.stages = ch->stages;
   a.xs_bytes = ch->xs_bytes;
+  a.xs_buf = ch->xs_buf;
   a.negz = opc::kNegZero2;
   a.l2_prefetch = ch->l2_prefetch;
   a.rank = ch->rank;
@@ -1776,6 +1874,11 @@ size_t opc_chain_trace_bytes(const opc_chain* ch) {
 int32_t opc_chain_grid(const opc_chain* ch) { return ch ? ch->grid : 0; }
 
 int32_t opc_chain_form(const opc_chain* ch) { return ch ? ch->form : 0; }
+
+int32_t opc_chain_x_scale(const opc_chain* ch) {
+  if (!ch || ch->form != OPC_CHAIN_FORM_BARRIER) return 0;
+  return ch->xs_buf ? OPC_CHAIN_XSCALE_BOUND : OPC_CHAIN_XSCALE_MAX;
+}
 
 int opc_chain_set_trace(opc_chain* ch, void* trace) {
   if (!ch) return fail(OPC_ERR_INVALID, "opc_chain_set_trace: chain is NULL");

@@ -68,7 +68,7 @@ def graph_time_us(call: Callable[[], None], device: torch.device, iters: int = 2
     acc = torch.empty((), dtype=torch.float32, device=device)
 
     def flush():
-        torch.sum(buf, out=acc)
+        torch.sum(buf, dim=0, out=acc)
 
     def flushed_call():
         flush()

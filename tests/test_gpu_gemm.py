@@ -104,3 +104,38 @@ def test_gemm_persistent_ctas_cycle_both_accumulators(cuda_device):
     torch.cuda.synchronize()
     assert oracle.rel_err(y.cpu().numpy(), y64) <= REL_TOL
     assert torch.equal(y, G.gemm(dl, x))  # deterministic
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,K,n_out,batch", [(1024, 4096, 10, 32), (300, 14336, 3, 20), (4096, 4096, 40, 64)])
+def test_gemv_route_to_gemm_with_k_split(cuda_device, M, K, n_out, batch):
+    # Batches above the crossover run the GEMM; with few row tiles it splits K into items whose
+    # fp32 partials the last arrival adds in slice order (deterministic).
+    ly = synthetic.random_layer(M, K, n_out, seed=M ^ K)
+    dl = L.prepare_layer(ly, cuda_device)
+    x = torch.from_numpy(synthetic.activations(batch, K, seed=batch)).to(cuda_device)
+    y1 = L.gemv(dl, x)
+    y2 = L.gemv(dl, x)
+    y64 = oracle.gemv_f64(oracle.dequantize_np(ly), x.cpu().numpy())
+    torch.cuda.synchronize()
+    assert torch.equal(y1, y2)
+    assert oracle.rel_err(y1.cpu().numpy(), y64) <= REL_TOL
+    assert oracle.rel_err(G.gemm(dl, x).cpu().numpy(), y64) <= REL_TOL  # the unsplit GEMM agrees too
+
+
+@pytest.mark.gpu
+def test_gemm_crossover_at_batch_8_uses_the_split_workspace(cuda_device):
+    from opac1ty_b200 import measure
+
+    M, K, batch = 2048, 8192, 12
+    ly = synthetic.random_layer(M, K, 20, seed=5)
+    dl = L.prepare_layer(ly, cuda_device)
+    x = torch.from_numpy(synthetic.activations(batch, K, seed=6)).to(cuda_device)
+    y64 = oracle.gemv_f64(oracle.dequantize_np(ly), x.cpu().numpy())
+    with measure.gemm_crossover(8):
+        ws = torch.zeros(L.workspace_bytes(dl, batch), dtype=torch.uint8, device=cuda_device)
+        y = L.gemv(dl, x, workspace=ws)
+        y_again = L.gemv(dl, x, workspace=ws)  # counters were left at zero by the first call
+    torch.cuda.synchronize()
+    assert torch.equal(y, y_again)
+    assert oracle.rel_err(y.cpu().numpy(), y64) <= REL_TOL
