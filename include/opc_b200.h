@@ -204,9 +204,7 @@ int opc_gemm(const opc_layer* layer, const void* x, int64_t ldx, void* y, int64_
  * barrier between steps: every output element is also published as a tagged 32-bit word that
  * the next step's readers poll).  Replaces per-step dispatch of MetalKernelManager.dequant_gemv for
  * a forward pass (runtime/src/inference.c:117-233 calls one layer at a time).  Each step is the
- * batch 1..2 integer GEMV of opc_gemv: an exact integer dot product rounded once to fp16, so
- * results are deterministic; with the max|x| scale they equal opc_gemv's bit for bit (see
- * OPC_CHAIN_FORM_BARRIER and opc_chain_x_scale below).
+ * batch 1..2 integer GEMV of opc_gemv; results equal opc_gemv's bit for bit.
  *   steps[0].x      the chain input (device fp16, ldx)
  *   steps[j].x      for j >= 1 must be steps[j-1].y with the same leading dimension (a prefix:
  *                   steps[j].layer K <= steps[j-1].layer M)
@@ -230,14 +228,8 @@ typedef struct opc_chain_step {
 int opc_chain_create(const opc_chain_step* steps, int32_t n_steps, int32_t batch, opc_chain** out);
 /* The same with an explicit form of the decode-step kernel:
  *   OPC_CHAIN_FORM_BARRIER   the step-by-step form above: each step's x is staged per CTA from the
- *                            previous step's fp16 outputs; batch 1..2.  Its fixed-point scale is
- *                            the exponent of max|x| (as opc_gemv, results bit for bit equal to
- *                            opc_gemv's) for step 0, for row-sharded chains and where shared memory
- *                            holds only one copy of x; otherwise (one GPU, x double-buffered) steps
- *                            >= 1 take it from a bound fixed before x exists, |x_j| <= (largest
- *                            row L1 norm of step j-1) x max|x_{j-1}|, and convert each x chunk as
- *                            it arrives: results then agree with opc_gemv within the GEMV
- *                            tolerance and are deterministic (opc_chain_x_scale tells which).
+ *                            previous step's fp16 outputs with its exponent from max|x| (as
+ *                            opc_gemv does), so results equal opc_gemv's bit for bit; batch 1..2.
  *   OPC_CHAIN_FORM_DATAFLOW  batch 1, one GPU, K <= 32768 (and the barrier form's other limits):
  *                            steps exchange their outputs as fixed-point digits whose scale is
  *                            fixed in advance from a norm bound (|y_r| <= ||W row r||_2 ||x||_2;
@@ -257,12 +249,6 @@ enum { OPC_CHAIN_FORM_AUTO = 0, OPC_CHAIN_FORM_BARRIER = 1, OPC_CHAIN_FORM_DATAF
 int opc_chain_create_ex(const opc_chain_step* steps, int32_t n_steps, int32_t batch, int32_t form, opc_chain** out);
 /* The form a chain was built with (OPC_CHAIN_FORM_BARRIER or OPC_CHAIN_FORM_DATAFLOW). */
 int32_t opc_chain_form(const opc_chain* chain);
-/* How a barrier-form chain scales steps >= 1's inputs: OPC_CHAIN_XSCALE_MAX (the exponent of
- * max|x|, bit for bit as opc_gemv) or OPC_CHAIN_XSCALE_BOUND (from the layer bound above); 0 for
- * the dataflow form or a NULL chain.  No counterpart in the reference (a property of this
- * implementation's fused decode step). */
-enum { OPC_CHAIN_XSCALE_MAX = 1, OPC_CHAIN_XSCALE_BOUND = 2 };
-int32_t opc_chain_x_scale(const opc_chain* chain);
 int opc_chain_launch(opc_chain* chain, void* stream);
 int opc_chain_destroy(opc_chain* chain);
 /* Tracing: with a device buffer of opc_chain_trace_bytes() set, every launch records per step
@@ -288,9 +274,9 @@ int opc_chain_set_trace(opc_chain* chain, void* trace);
  * its contiguous shard of every step's output rows from the full x and stores each finished row
  * (fp16 and tagged exchange word, system-scope stores) straight into every rank's copies over
  * NVLink; readers poll their local copy, so no barrier separates the steps.  One cross-rank flag
- * barrier ends each launch.  No all-gather, no NCCL call, no TMA multicast.  Every rank scales x
- * by the exponent of max|x| (OPC_CHAIN_XSCALE_MAX), so results equal opc_gemv's and the NCCL
- * form's bit for bit (the dot products are exact integers; every rank stages the same x).
+ * barrier ends each launch.  No all-gather, no NCCL call, no TMA multicast.  Results equal the
+ * one-GPU chain over the unsharded layers, opc_gemv and the NCCL form bit for bit (the dot
+ * products are exact integers; every rank stages the same x).
  *
  * Peer-visible memory ("region"): opc_peer_alloc allocates device memory on the current GPU and
  * exports an OPC_PEER_HANDLE_BYTES handle; other ranks map it with opc_peer_open.  Each rank's

@@ -25,8 +25,6 @@ OPC_CHAIN_L2_PREFETCH = 1
 OPC_CHAIN_FORM_AUTO = 0
 OPC_CHAIN_FORM_BARRIER = 1
 OPC_CHAIN_FORM_DATAFLOW = 2
-OPC_CHAIN_XSCALE_MAX = 1
-OPC_CHAIN_XSCALE_BOUND = 2
 OPC_PEER_HANDLE_BYTES = 64
 OPC_MAX_RANKS = 8
 
@@ -133,7 +131,6 @@ PROTOTYPES = {
         _c.c_int, [_c.POINTER(ChainStep), _c.c_int32, _c.c_int32, _c.c_int32, _c.POINTER(_c.c_void_p)],
     ),
     "opc_chain_form": (_c.c_int32, [_c.c_void_p]),
-    "opc_chain_x_scale": (_c.c_int32, [_c.c_void_p]),
     "opc_chain_launch": (_c.c_int, [_c.c_void_p, _c.c_void_p]),
     "opc_chain_destroy": (_c.c_int, [_c.c_void_p]),
     "opc_chain_trace_bytes": (_c.c_size_t, [_c.c_void_p]),

@@ -63,10 +63,6 @@ class Chain:
         self._handle = handle
         self._steps = arr
         self.form = "dataflow" if lib.opc_chain_form(handle) == _lib.OPC_CHAIN_FORM_DATAFLOW else "barrier"
-        # barrier form: "max" (steps scale x by the exponent of max|x|, bit for bit as opc_gemv) or
-        # "bound" (steps >= 1 from a bound fixed before x exists); None for the dataflow form
-        self.x_scale = {_lib.OPC_CHAIN_XSCALE_MAX: "max", _lib.OPC_CHAIN_XSCALE_BOUND: "bound"}.get(
-            int(lib.opc_chain_x_scale(handle)))
 
     def launch(self):
         lib = _lib.load()

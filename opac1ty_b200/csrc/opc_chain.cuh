@@ -55,8 +55,7 @@ struct ChainLayer {
   const __half* x;               // layer 0: the chain input (fp16)
   const uint32_t* xw;            // layer >= 1: the previous layer's exchange words (this rank's copy)
   unsigned long long* acc;       // [OT*16][2] outlier-slot dot products, count-carrying (zero between launches)
-  float wbound;                  // >= max over rows of sum_k |W_hat[r][k]| (host-computed): bounds |y| / max|x|
-  int32_t pad_;                  // keeps the descriptor a whole number of 16-byte pieces
+  const void* unused_;           // keeps the descriptor a whole number of 16-byte pieces
   const int32_t* onc;            // [OT] warps contributing to each outlier tile
   __half* y_peer[kMaxRanks];     // this rank's first row in rank p's fp16 copy of the full output
   uint32_t* yw_peer[kMaxRanks];  // this rank's first row in rank p's exchange words of it
@@ -91,7 +90,6 @@ struct ChainArgs {
                              // stored, x staged, own units done; [8 + w] consumer warp w's
                              // units (and row writes) done
   int32_t n_layers, batch, stages, xs_bytes;
-  int32_t xs_buf;            // bytes of one digit buffer when x is double-buffered by layer parity (else 0)
   uint32_t negz;
   int32_t l2_prefetch;       // stream weights with an L2 evict-first policy
   int32_t rank, world;
@@ -337,9 +335,9 @@ __device__ __forceinline__ void chain_store_digits(const uint4 v, float sc, uint
 constexpr int kChainSplitSlots = 32;  // packed tiles per CTA and layer (host-checked)
 
 struct ChainShared {
-  ChainLayer layer[3];                    // descriptors of layers j (slot j%3), j+1 and j-1
-  int4 part[3][kChainSharePieces];        // this CTA's warp shares of the same layers
-  uint32_t amax_bits[3][kQMaxBatch];      // max |x| (float bits) of layer j's input, slot j%3
+  ChainLayer layer[2];                    // descriptors of layers j (slot j&1) and j+1
+  int4 part[2][kChainSharePieces];        // this CTA's warp shares of layers j and j+1
+  uint32_t amax_bits[2][kQMaxBatch];      // staging: max |x| (float bits) of layers with parity 0 / 1
   unsigned long long tile_acc[kChainSplitSlots][kTileRows][kQMaxBatch];  // split packed tiles (count-carrying)
   int32_t abort;
   uint32_t epoch;
@@ -473,53 +471,6 @@ __device__ __forceinline__ void chain_finish_segment(ChainShared* sh, const Chai
   }
 }
 
-// Upper bound of a repacked layer's largest row L1 norm, max_r sum_k |W_hat[r][k]|, as non-negative
-// float bits atomically maxed into *out: one warp per row tile (its rows through their split fp16
-// codebooks; columns past K decode index 0 and are counted too) or per outlier row (from its fp16
-// copy).  fp32 sums (the caller adds a margin).  Run once per layer when a chain is built.
-__global__ void row_l1_max_kernel(const uint8_t* units, const uint2* cb, int32_t MT, int32_t KT, const __half* dense,
-                                  int32_t n_dense, int32_t K_pad, unsigned int* out) {
-  const int w = static_cast<int>((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
-  float m = 0.f;
-  if (w < MT) {
-    const int g = lane >> 2;
-    const uint2 c0 = cb[w * kTileRows + g], c1 = cb[w * kTileRows + g + 8];
-    float a0[4], a1[4];
-#pragma unroll
-    for (int v = 0; v < 4; ++v) {
-      a0[v] = fabsf(__half2float(__ushort_as_half(static_cast<unsigned short>(((c0.x >> (8 * v)) & 0xffu) |
-                                                                             (((c0.y >> (8 * v)) & 0xffu) << 8)))));
-      a1[v] = fabsf(__half2float(__ushort_as_half(static_cast<unsigned short>(((c1.x >> (8 * v)) & 0xffu) |
-                                                                             (((c1.y >> (8 * v)) & 0xffu) << 8)))));
-    }
-    float s0 = 0.f, s1 = 0.f;
-    for (int u = 0; u < KT; ++u) {
-      const uint4 q = ld_nc_v4(units + (static_cast<int64_t>(w) * KT + u) * kUnitBytes + lane * 16);
-      const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-#pragma unroll
-        for (int f = 0; f < 8; ++f) {  // fields 0..7: row g; 8..15: row g+8
-          s0 += a0[(wd[j] >> (2 * f)) & 3u];
-          s1 += a1[(wd[j] >> (16 + 2 * f)) & 3u];
-        }
-    }
-    s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
-    s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
-    s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
-    s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
-    m = fmaxf(s0, s1);
-  } else if (w < MT + n_dense) {
-    const __half* row = dense + static_cast<int64_t>(w - MT) * K_pad;
-    for (int k = lane; k < K_pad; k += 32) m += fabsf(__half2float(row[k]));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m += __shfl_xor_sync(0xffffffffu, m, o);
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  if (lane == 0 && w < MT + n_dense && m == m) atomicMax(out, __float_as_uint(m));
-}
-
 // kMulti: several ranks (system-scope stores into every rank's copies, cross-rank flags).  The
 // one-GPU instance compiles none of that, which keeps its code small.
 template <int kXC, bool kMulti>
@@ -550,7 +501,7 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
   }
   for (int i = threadIdx.x; i < kChainSplitSlots * kTileRows * kQMaxBatch; i += blockDim.x)
     (&sh->tile_acc[0][0][0])[i] = 0ull;
-  if (threadIdx.x < 3 * kQMaxBatch) (&sh->amax_bits[0][0])[threadIdx.x] = 0u;
+  if (threadIdx.x < 2 * kQMaxBatch) (&sh->amax_bits[0][0])[threadIdx.x] = 0u;
   if (threadIdx.x < sizeof(ChainLayer) / 16 && args.n_layers > 0)
     reinterpret_cast<uint4*>(&sh->layer[0])[threadIdx.x] = reinterpret_cast<const uint4*>(args.layers)[threadIdx.x];
   __syncthreads();
@@ -721,8 +672,7 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
   for (int j = 0; j < args.n_layers && ok; ++j) {
     // Descriptors live in shared memory (layer j+1's is copied during layer j's staging), so
     // reading them costs no global round trip and holds no registers.
-    const int dslot = j % 3;  // descriptors and x maxima are triple-buffered (see the staging below)
-    const ChainLayer& L = sh->layer[dslot];
+    const ChainLayer& L = sh->layer[j & 1];
     const uint32_t tag = chain_tag(tag_base, j);
     const uint32_t tag_in = j > 0 ? chain_tag(tag_base, j - 1) : 0u;
     // Everything about this warp's share that does not depend on x, before x is complete.
@@ -730,7 +680,7 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     qa.cbq = L.cbq; qa.tile_mask = L.tile_mask; qa.orow = L.orow; qa.oexp = L.oexp; qa.M = L.M; qa.MT = L.MT;
     unsigned long long* tr = args.trace ? args.trace + (static_cast<int64_t>(j) * G + cta) * kChainTracePhases : nullptr;
     if (tr && tid == 0) tr[0] = globaltimer_ns();
-    const int32_t* sr = reinterpret_cast<const int32_t*>(sh->part[dslot]);
+    const int32_t* sr = reinterpret_cast<const int32_t*>(sh->part[j & 1]);
     const int32_t u0 = sr[kShU0 + warp], u1 = sr[kShU1 + warp];
     ChainCursor cc = chain_cursor_at(L, u0, sr[kShSeg0 + warp]);
     MetaQ cur, nxt;
@@ -775,60 +725,28 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     }
     if (tr && tid == 0) tr[1] = globaltimer_ns();
 
-    // ---- stage x_j as offset integer digits.
-    // Layer 0 reads the caller's fp16 input and takes its scale from its exact max |x| (a CTA
-    // barrier between the max and the conversion).  Layers >= 1 poll the previous layer's exchange
-    // words.  With the digits double-buffered (args.xs_buf, when shared memory allows) their scale
-    // is fixed BEFORE they arrive, from a bound -- |x_j| <= wbound_{j-1} * max|x_{j-1}|, wbound
-    // being the previous layer's largest row L1 norm (host-computed) -- and every chunk is
-    // converted and stored the moment its words carry this launch's tag: no max pass and no
-    // barrier before the conversion, which overlaps the wait for the slowest rows.  Otherwise
-    // they take the layer-0 path.  The input's own max is reduced either way (for the next bound).
-    // Descriptors and maxima are triple-buffered by layer: slot (j+1)%3 is filled during this
-    // staging while slower warps may still read slot (j-1)%3.
+    // ---- stage x_j.  Layer 0 reads the fp16 input; later layers poll the previous layer's
+    // exchange words of their chunks until every tag is this launch's (bounded).
     int ex0 = 0, ex1 = 0;  // x exponents of batch rows 0, 1 (scalars: no local memory)
-    const uint32_t xs_cur = xs_base + ((args.xs_buf && (j & 1)) ? static_cast<uint32_t>(args.xs_buf) : 0u);
     {
       static_assert(kQMaxBatch == 2, "chunk c of batch row c >= per_row: no division");
       const int per_row = L.K_pad / 8;
       const int total = B * per_row;
-      const uint32_t colb = static_cast<uint32_t>(xsq_col_bytes(L.KT));
-      const int slot_next = dslot == 2 ? 0 : dslot + 1, slot_prev = dslot == 0 ? 2 : dslot - 1;
-      const bool on_arrival = j > 0 && args.xs_buf != 0;
-      if (j > 0 && tid < kQMaxBatch) sh->amax_bits[slot_next][tid] = 0u;  // last read at layer j-1's start
-      if (on_arrival) {
-        // the bound of this input: the previous layer's rows times the max of its input
-        const float wb = sh->layer[slot_prev].wbound * (1.0f + 1.0f / 1024.0f);  // + fp16 rounding of y
-        const float m0 = fminf(__uint_as_float(sh->amax_bits[slot_prev][0]) * wb, 65504.0f);
-        const float m1 = fminf(__uint_as_float(sh->amax_bits[slot_prev][1]) * wb, 65504.0f);
-        ex0 = m0 > 0.f ? 22 - frexp_exponent(m0) : 0;
-        ex1 = m1 > 0.f ? 22 - frexp_exponent(m1) : 0;
-      }
       uint4 v[kXC];
       uint32_t pending = 0;  // chunks still to take
 #pragma unroll
       for (int i = 0; i < kXC; ++i) {
         const int c = tid + i * kQConsumerThreads;
         v[i] = make_uint4(0, 0, 0, 0);
-        if (c < total) {
-          const int b = c >= per_row ? 1 : 0, k = (c - b * per_row) * 8;  // c < 2 per_row (batch <= 2)
-          if (k < L.K) pending |= 1u << i;
-          else if (on_arrival)  // padding past K: zero digits now
-            chain_store_digits(v[i], 1.0f, xs_cur + 3 * b * colb, colb,
-                               static_cast<uint32_t>((k >> 7) * 128 + xs_pos8(k & 127)));
-        }
+        if (c < total && (c - (c >= per_row ? per_row : 0)) * 8 < L.K) pending |= 1u << i;
       }
-      float mx[kQMaxBatch] = {0.f, 0.f};
       if (j == 0) {
 #pragma unroll
         for (int i = 0; i < kXC; ++i) {
           if (pending & (1u << i)) {
             const int c = tid + i * kQConsumerThreads;
-            const int b = c >= per_row ? 1 : 0, k = (c - b * per_row) * 8;
+            const int b = c >= per_row ? 1 : 0, k = (c - b * per_row) * 8;  // c < 2 per_row (batch <= 2)
             v[i] = chain_load_x0(L.x, L.ldx, b, k, L.K, L.x_vec16);
-            const float m = chain_chunk_amax(v[i]);
-            if (b == 0) mx[0] = fmaxf(mx[0], m);
-            else mx[1] = fmaxf(mx[1], m);
           }
         }
         pending = 0;
@@ -845,14 +763,7 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
             const int b = c >= per_row ? 1 : 0, k = (c - b * per_row) * 8;
             const ChainChunk r = chain_poll_chunk<sys>(L.xw, L.ldxw, b, k, L.K, tag_in);
             if (r.ok) {
-              const float m = chain_chunk_amax(r.v);
-              if (b == 0) mx[0] = fmaxf(mx[0], m);
-              else mx[1] = fmaxf(mx[1], m);
-              if (on_arrival)
-                chain_store_digits(r.v, pow2f(b == 0 ? ex0 : ex1), xs_cur + 3 * b * colb, colb,
-                                   static_cast<uint32_t>((k >> 7) * 128 + xs_pos8(k & 127)));
-              else
-                v[i] = r.v;
+              v[i] = r.v;
               pending &= ~(1u << i);
             }
           }
@@ -867,39 +778,54 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
         }
       }
       if (tr && tid == 0) tr[3] = globaltimer_ns();
+      float mx[kQMaxBatch] = {0.f, 0.f};
+#pragma unroll
+      for (int i = 0; i < kXC; ++i) {
+        const int c = tid + i * kQConsumerThreads;
+        if (c < total) {
+          const float m = chain_chunk_amax(v[i]);
+          if (c < per_row) mx[0] = fmaxf(mx[0], m);
+          else mx[1] = fmaxf(mx[1], m);
+        }
+      }
       // non-negative floats order like their bit patterns: one warp max and one shared-memory
       // atomic per warp and batch row (a NaN maximum counts as 0, as fmaxf would skip it)
 #pragma unroll
       for (int b = 0; b < kQMaxBatch; ++b) {
         const uint32_t m = __reduce_max_sync(0xffffffffu, mx[b] == mx[b] ? __float_as_uint(mx[b]) : 0u);
-        if (lane == 0) atomicMax(&sh->amax_bits[dslot][b], m);
+        if (lane == 0) atomicMax(&sh->amax_bits[j & 1][b], m);
       }
       if (tid < 16)  // ones block, zero block (B operands of the ones and absent columns)
         sts128(xs_base + args.xs_bytes - kQZeroBytes - kQOnesBytes + tid * 16,
                tid < 8 ? make_uint4(0x01010101u, 0x01010101u, 0x01010101u, 0x01010101u) : make_uint4(0, 0, 0, 0));
-      if (copy_desc) {  // layer j+1's descriptor and shares into slot (j+1)%3 (last read in layer j-2)
-        if (dt < kDescPieces) reinterpret_cast<uint4*>(&sh->layer[slot_next])[dt] = desc_piece;
-        else reinterpret_cast<uint4*>(sh->part[slot_next])[dt - kDescPieces] = desc_piece;
+      named_barrier(1, kQConsumerThreads);  // every warp is done with layer j-1 and holds its x
+      if (tr && tid == 0) tr[4] = globaltimer_ns();
+      if (sh->abort) {
+        ok = false;
+        break;
       }
-      if (!on_arrival) {
-        // the exact max first: every warp is done with layer j-1 and holds its chunks of x
-        named_barrier(1, kQConsumerThreads);
-        if (tr && tid == 0) tr[4] = globaltimer_ns();
-        if (j == 0) publish(f_staged0);  // layer-0 input read by every thread of this CTA
-        const float m0 = __uint_as_float(sh->amax_bits[dslot][0]), m1 = __uint_as_float(sh->amax_bits[dslot][1]);
+      if (copy_desc) {
+        if (dt < kDescPieces) reinterpret_cast<uint4*>(&sh->layer[(j + 1) & 1])[dt] = desc_piece;
+        else reinterpret_cast<uint4*>(sh->part[(j + 1) & 1])[dt - kDescPieces] = desc_piece;
+      }
+      if (j == 0) publish(f_staged0);  // layer-0 input read by every thread of this CTA
+      {
+        const float m0 = __uint_as_float(sh->amax_bits[j & 1][0]), m1 = __uint_as_float(sh->amax_bits[j & 1][1]);
         ex0 = m0 > 0.f ? 22 - frexp_exponent(m0) : 0;
         ex1 = m1 > 0.f ? 22 - frexp_exponent(m1) : 0;
+        // the other parity's maxima start layer j+1 at zero: their last readers (layer j-1) are
+        // past this barrier, their next writers (layer j+1) behind the staged barrier below
+        if (tid < kQMaxBatch) sh->amax_bits[(j + 1) & 1][tid] = 0u;
+      }
+      const uint32_t colb = static_cast<uint32_t>(xsq_col_bytes(L.KT));
 #pragma unroll
-        for (int i = 0; i < kXC; ++i) {
-          const int c = tid + i * kQConsumerThreads;
-          if (c < total) {
-            const int b = c >= per_row ? 1 : 0, k = (c - b * per_row) * 8;
-            chain_store_digits(v[i], pow2f(b == 0 ? ex0 : ex1), xs_cur + 3 * b * colb, colb,
-                               static_cast<uint32_t>((k >> 7) * 128 + xs_pos8(k & 127)));
-          }
+      for (int i = 0; i < kXC; ++i) {
+        const int c = tid + i * kQConsumerThreads;
+        if (c < total) {
+          const int b = c >= per_row ? 1 : 0, k = (c - b * per_row) * 8;
+          chain_store_digits(v[i], pow2f(b == 0 ? ex0 : ex1), xs_base + 3 * b * colb, colb,
+                             static_cast<uint32_t>((k >> 7) * 128 + xs_pos8(k & 127)));
         }
-      } else if (tr && tid == 0) {
-        tr[4] = tr[3];
       }
       if (tr && tid == 0) tr[5] = globaltimer_ns();
       // a layer writing over the chain input starts once every CTA has read that input (flags
@@ -922,7 +848,7 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     // ---- this warp's units of layer j
     const int bcol = g >> 2, dig = g & 3;
     const bool live_col = dig < 3 && bcol < B;
-    const uint32_t colbase = live_col ? xs_cur + (3 * bcol + dig) * xsq_col_bytes(L.KT)
+    const uint32_t colbase = live_col ? xs_base + (3 * bcol + dig) * xsq_col_bytes(L.KT)
                                       : xs_base + args.xs_bytes - (bcol < B ? kQZeroBytes + kQOnesBytes : kQZeroBytes);
     const uint32_t kts = live_col ? 128u : 0u;
     const uint32_t xq = colbase + 32 * q, xo = colbase + 4 * q;

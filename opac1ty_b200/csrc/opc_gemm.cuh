@@ -161,10 +161,12 @@ __device__ __forceinline__ uint32_t sw128_off(int r, int c) {
 
 // tx: x [n_tok][K] fp16, box 64 x N, 128-byte swizzle.  tu: the packed units as a [MT][KT * 512 B]
 // array of 8-byte elements, box 512 B x 8 row tiles (one copy brings a k block of all 8 row tiles);
-// sub_vector_size 8: [MT][KB * 128 B], box 128 B x 8 row tiles.
+// sub_vector_size 8: [MT][KB * 128 B], box 128 B x 8 row tiles.  td: the row-major outlier rows
+// [n_slots][K_pad] fp16, box 64 x 128 rows, 128-byte swizzle (a dense tile's A stage as is).
 template <int kN>
 __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap tx,
-                                                             const __grid_constant__ CUtensorMap tu, const GemmArgs a) {
+                                                             const __grid_constant__ CUtensorMap tu,
+                                                             const __grid_constant__ CUtensorMap td, const GemmArgs a) {
   constexpr int kBBytes = gm_b_bytes(kN);
   constexpr int kS = gm_stages(kN);
   constexpr int kCols = gm_tmem_cols(kN);
@@ -350,9 +352,18 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_consta
         }
         const uint32_t dstA = sA + st * kGmABytes;
         if (dense) {
-          const uint4* src = reinterpret_cast<const uint4*>(a.dense + static_cast<int64_t>(R) * a.K_pad + s * kGmK);
-#pragma unroll
-          for (int c = 0; c < 8; ++c) sts128(dstA + sw128_off(r, c), row_live ? __ldg(src + c) : make_uint4(0, 0, 0, 0));
+          // the outlier rows' A tile is a plain copy: one TMA in the same 128-byte-swizzled
+          // K-major layout, completing on the stage's "A full" barrier (the first warp's
+          // arrive.expect_tx is one of the group's four arrivals; rows past the slots read zeros)
+          if ((d & 3) == 0) {  // the group's first warp
+            if (lane == 0) {
+              mbar_expect_tx(afull_b + 8 * st, kGmABytes);
+              tma_load_2d(dstA, &td, s * kGmK, (mi - a.m_tiles) * kGmM, afull_b + 8 * st);
+            }
+          } else if (lane == 0) {
+            mbar_arrive(afull_b + 8 * st);
+          }
+          continue;
         } else {
           if (!mbar_wait_bounded(ufull_b + 8 * su, (gs / kGmUStages) & 1)) {
             ok = false;

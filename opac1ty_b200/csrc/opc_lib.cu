@@ -285,8 +285,8 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 }
 
 template <int kN>
-int launch_gemm_t(const CUtensorMap& tx, const CUtensorMap& tu, const opc::GemmArgs& a, unsigned grid, cudaStream_t stream,
-                  int dev) {
+int launch_gemm_t(const CUtensorMap& tx, const CUtensorMap& tu, const CUtensorMap& td, const opc::GemmArgs& a,
+                  unsigned grid, cudaStream_t stream, int dev) {
   static std::mutex mu;
   static std::map<int, bool> configured;
   {
@@ -298,7 +298,7 @@ int launch_gemm_t(const CUtensorMap& tx, const CUtensorMap& tu, const opc::GemmA
       configured[dev] = true;
     }
   }
-  opc::gemm_kernel<kN><<<grid, opc::kGmThreads, opc::gm_smem_bytes(kN), stream>>>(tx, tu, a);
+  opc::gemm_kernel<kN><<<grid, opc::kGmThreads, opc::gm_smem_bytes(kN), stream>>>(tx, tu, td, a);
   OPC_CUDA(cudaGetLastError(), "launch gemm_kernel");
   return OPC_OK;
 }
@@ -932,6 +932,24 @@ int gemm_run(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ld
       return fail(OPC_ERR_CUDA, "opc_gemm: cuTensorMapEncodeTiled (units) failed (%d)", static_cast<int>(cu));
   }
 
+  // the row-major outlier rows [slots][K_pad] fp16: a dense tile's A stage is one swizzled box
+  const __half* dense = svs8 ? reinterpret_cast<const __half*>(static_cast<const uint8_t*>(L->units) +
+                                                               p.packed_units * opc::kVq8UnitBytes)
+                             : dense_outliers(L);
+  CUtensorMap td;
+  {
+    const int64_t slots = std::max<int64_t>(p.outlier_tiles, 1) * opc::kTileRows;
+    const cuuint64_t ddim[2] = {static_cast<cuuint64_t>(p.K_pad), static_cast<cuuint64_t>(slots)};
+    const cuuint64_t dstride[1] = {static_cast<cuuint64_t>(p.K_pad) * 2};
+    const cuuint32_t dbox[2] = {opc::kGmK, opc::kGmM};
+    if (!aligned(dense, 16)) return fail(OPC_ERR_INVALID, "opc_gemm: outlier rows not 16-byte aligned");
+    const CUresult cd = encode(&td, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(dense), ddim, dstride, dbox,
+                               estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (cd != CUDA_SUCCESS)
+      return fail(OPC_ERR_CUDA, "opc_gemm: cuTensorMapEncodeTiled (outlier rows) failed (%d)", static_cast<int>(cd));
+  }
+
   opc::GemmArgs a;
   memset(&a, 0, sizeof(a));
   a.units = static_cast<const uint8_t*>(L->units);
@@ -939,8 +957,7 @@ int gemm_run(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ld
   a.cb8 = static_cast<const uint4*>(L->codebooks);
   a.svs8 = svs8 ? 1 : 0;
   a.tile_mask = static_cast<const uint16_t*>(L->tile_mask);
-  a.dense = svs8 ? reinterpret_cast<const __half*>(static_cast<const uint8_t*>(L->units) + p.packed_units * opc::kVq8UnitBytes)
-                 : dense_outliers(L);
+  a.dense = dense;
   a.orow = L->outlier_rows;
   a.y = static_cast<__half*>(y);
   a.ldy = ldy;
@@ -964,11 +981,11 @@ int gemm_run(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ld
   }
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>(tiles * gp.ksplit, dc.sm_count));
   switch (tn) {
-    case 256: return launch_gemm_t<256>(tx, tu, a, grid, s, dev);
-    case 128: return launch_gemm_t<128>(tx, tu, a, grid, s, dev);
-    case 64: return launch_gemm_t<64>(tx, tu, a, grid, s, dev);
-    case 32: return launch_gemm_t<32>(tx, tu, a, grid, s, dev);
-    default: return launch_gemm_t<16>(tx, tu, a, grid, s, dev);
+    case 256: return launch_gemm_t<256>(tx, tu, td, a, grid, s, dev);
+    case 128: return launch_gemm_t<128>(tx, tu, td, a, grid, s, dev);
+    case 64: return launch_gemm_t<64>(tx, tu, td, a, grid, s, dev);
+    case 32: return launch_gemm_t<32>(tx, tu, td, a, grid, s, dev);
+    default: return launch_gemm_t<16>(tx, tu, td, a, grid, s, dev);
   }
 }
 
@@ -987,7 +1004,7 @@ int opc_gemm(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ld
 // ---------------------------------------------------------------------------------------------
 struct opc_chain {
   int device = 0;
-  int32_t n_layers = 0, batch = 1, stages = 2, xs_bytes = 0, xs_buf = 0, grid = 0, xc = 8;
+  int32_t n_layers = 0, batch = 1, stages = 2, xs_bytes = 0, grid = 0, xc = 8;
   int32_t rank = 0, world = 1;
   size_t smem = 0;
   void* dev_mem = nullptr;              // [layers | onc | parts | epoch | acc (| flags | words)]
@@ -1154,21 +1171,16 @@ int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t 
     kt_max = std::max(kt_max, steps[j].layer->plan.k_units);
     bk_max = std::max<int64_t>(bk_max, static_cast<int64_t>(batch) * steps[j].layer->plan.K_pad);
   }
-  // Staged x: one digit buffer, or two (by layer parity) when they fit next to two ring stages --
-  // then layers >= 1 convert x as it arrives (see the chain kernel's staging).
-  const int xs_one = static_cast<int>(align_up(static_cast<size_t>(3 * batch) * opc::xsq_col_bytes(kt_max), 128));
-  auto smem_for = [&](int xs_total, int stages) {
-    return static_cast<size_t>(xs_total) + static_cast<size_t>(opc::kQConsumers) * stages * (opc::kQChunkBytes + 16) +
+  const int xs = static_cast<int>(align_up(static_cast<size_t>(3 * batch) * opc::xsq_col_bytes(kt_max) +
+                                          opc::kQZeroBytes + opc::kQOnesBytes, 128));
+  auto smem_for = [&](int stages) {
+    return static_cast<size_t>(xs) + static_cast<size_t>(opc::kQConsumers) * stages * (opc::kQChunkBytes + 16) +
            sizeof(opc::ChainShared);
   };
-  const int ones_zero = opc::kQZeroBytes + opc::kQOnesBytes;
-  // (one GPU only: the row-sharded form keeps every rank's x scale from the exact max, as opc_gemv)
-  const bool dbl = world == 1 && smem_for(2 * xs_one + ones_zero, 2) <= static_cast<size_t>(dc.max_smem_optin);
-  const int xs = (dbl ? 2 * xs_one : xs_one) + ones_zero;
   int stages = opc::kQMaxStages;
-  while (stages >= 2 && smem_for(xs, stages) > static_cast<size_t>(dc.max_smem_optin)) --stages;
+  while (stages >= 2 && smem_for(stages) > static_cast<size_t>(dc.max_smem_optin)) --stages;
   if (stages < 2) return fail(OPC_ERR_UNSUPPORTED, "%s: staged x too large for shared memory", fn);
-  const size_t smem = smem_for(xs, stages);
+  const size_t smem = smem_for(stages);
   const int xc = bk_max <= 4 * 8 * opc::kQConsumerThreads ? 4 : 8;
   const bool multi = world > 1;
   auto kern = xc == 4 ? (multi ? opc::chain_kernel<4, true> : opc::chain_kernel<4, false>)
@@ -1242,33 +1254,6 @@ int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t 
       off += chain_words_bytes(steps[j].ldy, batch);
     }
   }
-  // One GPU with double-buffered x: every layer's largest row L1 norm, the bound from which the
-  // next layer's input scale is fixed before that input exists (fp32 sums, +1 % margin).
-  std::vector<float> wbound(n, 0.0f);
-  if (dbl) {
-    unsigned int* wb_dev = nullptr;
-    OPC_CUDA(cudaMalloc(&wb_dev, sizeof(unsigned int) * n), "cudaMalloc(chain bounds)");
-    cudaError_t e = cudaMemset(wb_dev, 0, sizeof(unsigned int) * n);
-    for (int j = 0; j < n && e == cudaSuccess; ++j) {
-      const opc_layer* L = steps[j].layer;
-      const opc_layer_plan& p = L->plan;
-      const int32_t n_dense = p.n_outliers > 0 ? p.outlier_tiles * opc::kTileRows : 0;
-      const int64_t warps = static_cast<int64_t>(p.row_tiles) + n_dense;
-      opc::row_l1_max_kernel<<<static_cast<unsigned>(ceil_div(warps * 32, 256)), 256>>>(
-          static_cast<const uint8_t*>(L->units), static_cast<const uint2*>(L->codebooks), p.row_tiles, p.k_units,
-          dense_outliers(L), n_dense, p.K_pad, wb_dev + j);
-      e = cudaGetLastError();
-    }
-    std::vector<unsigned int> bits(n, 0u);
-    if (e == cudaSuccess) e = cudaMemcpy(bits.data(), wb_dev, sizeof(unsigned int) * n, cudaMemcpyDeviceToHost);
-    cudaFree(wb_dev);
-    if (e != cudaSuccess) return cuda_fail(e, "chain: layer bounds");
-    for (int j = 0; j < n; ++j) {
-      float f;
-      memcpy(&f, &bits[j], sizeof(f));
-      wbound[j] = f * 1.01f;
-    }
-  }
   void* mem = nullptr;
   OPC_CUDA(cudaMalloc(&mem, off), "cudaMalloc(chain)");
   char* base = static_cast<char*>(mem);
@@ -1308,7 +1293,6 @@ int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t 
     c.x_vec16 = (p.K % 8 == 0) && (st.ldx % 8 == 0) && aligned(st.x, 16);
     c.row_off = row_off[j];
     c.m_full = m_full[j];
-    c.wbound = wbound[j];
     // a later step writing the same fp16 buffer makes this step's fp16 stores dead
     c.write_y = 1;
     for (int k = j + 1; k < n; ++k)
@@ -1337,7 +1321,6 @@ int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t 
   ch->batch = batch;
   ch->stages = stages;
   ch->xs_bytes = xs;
-  ch->xs_buf = dbl ? xs_one : 0;
   ch->smem = smem;
   ch->grid = G;
   ch->xc = xc;
@@ -1840,7 +1823,6 @@ int opc_chain_launch(opc_chain* ch, void* stream_v) {
   a.batch = ch->batch;
   a.stages = ch->stages;
   a.xs_bytes = ch->xs_bytes;
-  a.xs_buf = ch->xs_buf;
   a.negz = opc::kNegZero2;
   a.l2_prefetch = ch->l2_prefetch;
   a.rank = ch->rank;
@@ -1875,10 +1857,6 @@ int32_t opc_chain_grid(const opc_chain* ch) { return ch ? ch->grid : 0; }
 
 int32_t opc_chain_form(const opc_chain* ch) { return ch ? ch->form : 0; }
 
-int32_t opc_chain_x_scale(const opc_chain* ch) {
-  if (!ch || ch->form != OPC_CHAIN_FORM_BARRIER) return 0;
-  return ch->xs_buf ? OPC_CHAIN_XSCALE_BOUND : OPC_CHAIN_XSCALE_MAX;
-}
 
 int opc_chain_set_trace(opc_chain* ch, void* trace) {
   if (!ch) return fail(OPC_ERR_INVALID, "opc_chain_set_trace: chain is NULL");

@@ -163,6 +163,8 @@ class DecodeStack:
         """The kernel that runs the step."""
         if self.chain is not None:
             return "opc::chain2_kernel" if self.chain.form == "dataflow" else "opc::chain_kernel"
+        if self.batch > int(_lib.load().opc_gemm_crossover()):  # opc_gemv routes these to the GEMM
+            return "opc::gemm_kernel"
         return "opc::gemvq_kernel" if self.batch <= 2 else "opc::gemv_kernel"
 
     def step_eager(self):
