@@ -151,7 +151,8 @@ int opc_workspace_init(void* workspace, size_t bytes, void* stream);
  * for b < batch (1..64), r < M, with W_hat = codebook lookup + outlier-row replacement.
  *   x  device fp16, row b at x + b*ldx (ldx >= K, in elements)
  *   y  device fp16, row b at y + b*ldy (ldy >= M)
- * Batch 17..64 with x 16-byte aligned and ldx % 8 == 0 runs the prefill GEMM (opc_gemm).
+ * Batches above opc_gemm_crossover() (default 8, up to 64) with x 16-byte aligned and
+ * ldx % 8 == 0 run the prefill GEMM (opc_gemm), splitting K in the workspace where that helps.
  * Batch 1..2 (when the staged x fits in shared memory): x is staged per CTA as integers
  * round(x * 2^e_x), below 2^22 in magnitude (e_x from max |x|), the centroids are the 15-bit
  * integer codebooks above; the dot

@@ -10,7 +10,7 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 INCLUDE = PKG.parent / "include"
-SOURCES = [CSRC / "opc_lib.cu"]
+SOURCES = [CSRC / "opc_lib.cu", CSRC / "opc_engine.cu"]
 DEPENDS = sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + sorted(INCLUDE.glob("*.h"))
 OUTPUT = PKG / "libopc_b200.so"
 

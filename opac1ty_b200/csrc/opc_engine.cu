@@ -1,0 +1,932 @@
+// opc_engine.cu -- the bf_engine_* C API (include/opc_engine.h): a Llama-style decoder over the
+// fused dequant library.  The reference declares the same calls (runtime/include/opacc1ty.h:69-212)
+// and implements them as stubs (runtime/src/inference.c:183-245, bf2_format.c:131-314); this file
+// loads a .bf2 model onto the GPU and runs it.  Projections go through the library's public C ABI
+// (opc_repack_layer, opc_gemv, opc_dequant); the small per-token operations (RMSNorm, rotary
+// embedding, attention over the KV cache, SiLU gating, residual adds) are the kernels below.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <numeric>
+#include <random>
+#include <string>
+#include <vector>
+
+#include "opc_b200.h"
+#include "opc_engine.h"
+
+extern "C" const BFSamplingParams BF_DEFAULT_SAMPLING = {1.0f, 0.0f, 0, 1.0f, 0u};
+
+namespace {
+
+constexpr uint32_t kChunk = 64;          // tokens per prompt chunk (opc_gemv's largest batch)
+constexpr uint32_t kDefaultContext = 4096;
+constexpr int kAttnWarps = 4;
+constexpr int kMaxHeadDim = 256;
+
+// ------------------------------------------------------------------------------------------------
+// .bf2 file (opacc1ty/format/header.py:63-178, bf2.py:78-150): "BF2\0", u32 version, u32 flags,
+// u32 model-JSON length twice, JSON, u32 quantize-JSON length, JSON, u32 layer count, then per
+// layer a 64-byte header "<H B I I I B B H Q Q Q Q 13s", the name, and the payload.
+// ------------------------------------------------------------------------------------------------
+constexpr int kLayerHeader = 64;
+constexpr uint8_t kQuantized = 0, kPassthrough = 2;
+
+struct FileLayer {
+  std::string name;
+  uint8_t type = 0;
+  uint32_t out_f = 0, in_f = 0, n_groups = 0;
+  uint8_t entries = 0, svs = 0;
+  uint16_t n_out = 0;
+  size_t data = 0;      // file offset of the payload (after header and name)
+  int id_bytes = 4;     // outlier id width (the reference's own files carry int64)
+};
+
+template <typename T>
+T rd(const uint8_t* p) {
+  T v;
+  std::memcpy(&v, p, sizeof(T));
+  return v;
+}
+
+size_t payload_bytes(const FileLayer& l, int id_bytes) {
+  if (l.type == kQuantized) {
+    size_t n = static_cast<size_t>(l.n_groups) * l.entries * l.svs * 2;
+    if (l.svs) n += static_cast<size_t>(l.n_groups) * (l.in_f / l.svs);
+    if (l.n_out) n += static_cast<size_t>(l.n_out) * l.in_f * 2 + static_cast<size_t>(l.n_out) * id_bytes;
+    return n;
+  }
+  if (l.type == kPassthrough) return static_cast<size_t>(l.out_f) * l.in_f * 2;
+  return 0;
+}
+
+// Parse the layer header at `pos` (false when it is not a plausible header).
+bool parse_layer_at(const uint8_t* base, size_t size, size_t pos, FileLayer* out) {
+  if (pos + kLayerHeader > size) return false;
+  const uint8_t* h = base + pos;
+  FileLayer l;
+  const uint16_t nlen = rd<uint16_t>(h);
+  l.type = h[2];
+  l.out_f = rd<uint32_t>(h + 3);
+  l.in_f = rd<uint32_t>(h + 7);
+  l.n_groups = rd<uint32_t>(h + 11);
+  l.entries = h[15];
+  l.svs = h[16];
+  l.n_out = rd<uint16_t>(h + 17);
+  if (nlen == 0 || l.type > 2 || pos + kLayerHeader + nlen > size) return false;
+  l.name.assign(reinterpret_cast<const char*>(h + kLayerHeader), nlen);
+  l.data = pos + kLayerHeader + nlen;
+  *out = l;
+  return true;
+}
+
+// Value of "key" in a flat JSON object: a number (true) or, with `str`, a string.
+bool json_number(const std::string& js, const char* key, double* v) {
+  const std::string k = std::string("\"") + key + "\"";
+  size_t p = js.find(k);
+  if (p == std::string::npos) return false;
+  p = js.find(':', p + k.size());
+  if (p == std::string::npos) return false;
+  const char* s = js.c_str() + p + 1;
+  while (*s == ' ' || *s == '\t' || *s == '\n' || *s == '\r') ++s;
+  char* end = nullptr;
+  const double d = std::strtod(s, &end);
+  if (end == s) return false;
+  *v = d;
+  return true;
+}
+bool json_string(const std::string& js, const char* key, std::string* v) {
+  const std::string k = std::string("\"") + key + "\"";
+  size_t p = js.find(k);
+  if (p == std::string::npos) return false;
+  p = js.find(':', p + k.size());
+  if (p == std::string::npos) return false;
+  p = js.find('"', p);
+  if (p == std::string::npos) return false;
+  const size_t e = js.find('"', p + 1);
+  if (e == std::string::npos) return false;
+  *v = js.substr(p + 1, e - p - 1);
+  return true;
+}
+
+// ------------------------------------------------------------------------------------------------
+// Kernels.  Rows are tokens of the current chunk; the residual stream h is fp32 [n][hidden].
+// ------------------------------------------------------------------------------------------------
+struct ChunkTokens {
+  int32_t t[kChunk];
+};
+
+__global__ void embed_kernel(const __half* __restrict__ table, int hidden, ChunkTokens tok, float* __restrict__ h) {
+  const int r = blockIdx.x;
+  const __half* src = table + static_cast<int64_t>(tok.t[r]) * hidden;
+  for (int i = threadIdx.x; i < hidden; i += blockDim.x) h[static_cast<int64_t>(r) * hidden + i] = __half2float(src[i]);
+}
+
+__device__ float block_sum(float v) {
+  __shared__ float part[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) part[w] = v;
+  __syncthreads();
+  const int nw = (blockDim.x + 31) >> 5;
+  float s = 0.f;
+  for (int i = 0; i < nw; ++i) s += part[i];
+  __syncthreads();
+  return s;
+}
+
+// out[r][i] = fp16(w[i] * h[r][i] / sqrt(mean_i h[r][i]^2 + eps)); w NULL = ones
+// (LlamaRMSNorm: the statistics in fp32, the scaled value times the weight).
+__global__ void rmsnorm_kernel(const float* __restrict__ h, int hidden, const __half* __restrict__ w, float eps,
+                               __half* __restrict__ out, int ldo) {
+  const int r = blockIdx.x;
+  const float* x = h + static_cast<int64_t>(r) * hidden;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < hidden; i += blockDim.x) ss += x[i] * x[i];
+  const float inv = rsqrtf(block_sum(ss) / static_cast<float>(hidden) + eps);
+  for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+    const float v = x[i] * inv;
+    out[static_cast<int64_t>(r) * ldo + i] = __float2half_rn(w ? __half2float(w[i]) * v : v);
+  }
+}
+
+// Rotary embedding (rotate-half pairing: dims i and i + hd/2 of a head, angle
+// pos * theta^(-2i/hd)) on q in place and on k, then k and v appended to the layer's cache
+// [kv_heads][ctx][hd] at position pos0 + r.
+__global__ void rope_cache_kernel(__half* __restrict__ q, int ldq, const __half* __restrict__ k,
+                                  const __half* __restrict__ v, int ldkv, int heads, int kv_heads, int hd, int pos0,
+                                  float theta, __half* __restrict__ kc, __half* __restrict__ vc, int ctx) {
+  const int r = blockIdx.x;
+  const int pos = pos0 + r;
+  const int half = hd / 2;
+  const int nq = heads * half, nk = kv_heads * half;
+  for (int i = threadIdx.x; i < nq + nk; i += blockDim.x) {
+    const bool isq = i < nq;
+    const int j = isq ? i : i - nq;
+    const int head = j / half, d = j - head * half;
+    const float inv_freq = powf(theta, -2.0f * static_cast<float>(d) / static_cast<float>(hd));
+    float s, c;
+    sincosf(static_cast<float>(pos) * inv_freq, &s, &c);
+    const __half* src = isq ? q + static_cast<int64_t>(r) * ldq : k + static_cast<int64_t>(r) * ldkv;
+    const float x0 = __half2float(src[head * hd + d]), x1 = __half2float(src[head * hd + d + half]);
+    const __half y0 = __float2half_rn(x0 * c - x1 * s), y1 = __float2half_rn(x1 * c + x0 * s);
+    if (isq) {
+      q[static_cast<int64_t>(r) * ldq + head * hd + d] = y0;
+      q[static_cast<int64_t>(r) * ldq + head * hd + d + half] = y1;
+    } else {
+      __half* dst = kc + (static_cast<int64_t>(head) * ctx + pos) * hd;
+      dst[d] = y0;
+      dst[d + half] = y1;
+    }
+  }
+  for (int i = threadIdx.x; i < kv_heads * hd; i += blockDim.x) {
+    const int head = i / hd, d = i - head * hd;
+    vc[(static_cast<int64_t>(head) * ctx + pos) * hd + d] = v[static_cast<int64_t>(r) * ldkv + i];
+  }
+}
+
+// Causal grouped-query attention of token r (position pos0 + r) for query head blockIdx.x over
+// cache positions 0..pos0+r: softmax(q.k / sqrt(hd)) . v with a running max per warp (each warp
+// takes every kAttnWarps-th position, lane l holds dims [E*l, E*l+E)), warps merged at the end.
+__global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(const __half* __restrict__ q, int ldq,
+                                                                    const __half* __restrict__ kc,
+                                                                    const __half* __restrict__ vc, int heads,
+                                                                    int kv_heads, int hd, int ctx, int pos0,
+                                                                    __half* __restrict__ out, int ldo) {
+  constexpr int kMaxE = kMaxHeadDim / 32;
+  __shared__ float sm_m[kAttnWarps], sm_s[kAttnWarps], sm_acc[kAttnWarps][kMaxHeadDim];
+  const int head = blockIdx.x, r = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int E = hd / 32;
+  const int kvh = head / (heads / kv_heads);
+  const int L = pos0 + r + 1;
+  const float scale = rsqrtf(static_cast<float>(hd));
+  float qv[kMaxE], acc[kMaxE];
+#pragma unroll
+  for (int e = 0; e < kMaxE; ++e) {
+    qv[e] = e < E ? __half2float(q[static_cast<int64_t>(r) * ldq + head * hd + lane * E + e]) * scale : 0.f;
+    acc[e] = 0.f;
+  }
+  float m = -INFINITY, s = 0.f;
+  const __half* kb = kc + static_cast<int64_t>(kvh) * ctx * hd;
+  const __half* vb = vc + static_cast<int64_t>(kvh) * ctx * hd;
+  for (int p = warp; p < L; p += kAttnWarps) {
+    const __half* kp = kb + static_cast<int64_t>(p) * hd + lane * E;
+    float dot = 0.f;
+#pragma unroll
+    for (int e = 0; e < kMaxE; ++e)
+      if (e < E) dot += qv[e] * __half2float(kp[e]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+    const float mn = fmaxf(m, dot);
+    const float corr = expf(m - mn), w = expf(dot - mn);
+    s = s * corr + w;
+    const __half* vp = vb + static_cast<int64_t>(p) * hd + lane * E;
+#pragma unroll
+    for (int e = 0; e < kMaxE; ++e)
+      if (e < E) acc[e] = acc[e] * corr + w * __half2float(vp[e]);
+    m = mn;
+  }
+  if (lane == 0) {
+    sm_m[warp] = m;
+    sm_s[warp] = s;
+  }
+#pragma unroll
+  for (int e = 0; e < kMaxE; ++e)
+    if (e < E) sm_acc[warp][lane * E + e] = acc[e];
+  __syncthreads();
+  float M = -INFINITY;
+  for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, sm_m[w]);
+  float S = 0.f;
+  for (int w = 0; w < kAttnWarps; ++w) S += sm_m[w] == -INFINITY ? 0.f : sm_s[w] * expf(sm_m[w] - M);
+  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+    float o = 0.f;
+    for (int w = 0; w < kAttnWarps; ++w)
+      if (sm_m[w] != -INFINITY) o += sm_acc[w][d] * expf(sm_m[w] - M);
+    out[static_cast<int64_t>(r) * ldo + head * hd + d] = __float2half_rn(o / S);
+  }
+}
+
+// h[r][i] += y[r][i]
+__global__ void residual_kernel(float* __restrict__ h, int hidden, const __half* __restrict__ y, int ldy) {
+  const int r = blockIdx.x;
+  for (int i = threadIdx.x; i < hidden; i += blockDim.x)
+    h[static_cast<int64_t>(r) * hidden + i] += __half2float(y[static_cast<int64_t>(r) * ldy + i]);
+}
+
+// a[r][i] = fp16(silu(g) * u), silu(g) = g / (1 + exp(-g))
+__global__ void silu_mul_kernel(const __half* __restrict__ g, const __half* __restrict__ u, int n, int ld,
+                                __half* __restrict__ a) {
+  const int r = blockIdx.x;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float gv = __half2float(g[static_cast<int64_t>(r) * ld + i]), uv = __half2float(u[static_cast<int64_t>(r) * ld + i]);
+    a[static_cast<int64_t>(r) * ld + i] = __float2half_rn(gv / (1.0f + expf(-gv)) * uv);
+  }
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------------------------------------
+// Engine state
+// ------------------------------------------------------------------------------------------------
+namespace {
+
+struct DevLayer {
+  opc_layer L{};
+  bool present = false;
+};
+
+struct Block {
+  DevLayer q, k, v, o, gate, up, down;
+  const __half* ln_in = nullptr;    // device; NULL = ones
+  const __half* ln_post = nullptr;
+};
+
+int pad8(int v) { return (v + 7) & ~7; }
+
+}  // namespace
+
+struct BFEngine {
+  std::string error;
+  BFModelConfig cfg{};
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  float eps = 1e-5f;
+  uint32_t ctx = 0, pos = 0;
+  int hidden = 0, heads = 0, kv_heads = 0, hd = 0, inter = 0, vocab = 0, n_layers = 0;
+  std::vector<Block> blocks;
+  DevLayer embed, lm_head;
+  bool lm_from_embed = false;
+  __half* embed_table = nullptr;
+  const __half* final_norm = nullptr;
+  __half *kcache = nullptr, *vcache = nullptr;
+  size_t kv_bytes = 0;
+  // per-chunk scratch, kChunk rows each
+  float* h = nullptr;
+  __half *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *y = nullptr, *g = nullptr,
+         *u = nullptr, *a = nullptr, *logits16 = nullptr;
+  int ld_x = 0, ld_q = 0, ld_kv = 0, ld_i = 0, ld_y = 0;
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+  __half* host_logits = nullptr;  // pinned
+  std::vector<void*> allocs;
+  size_t dev_bytes = 0;
+  std::vector<int32_t> history;   // tokens in the cache (repetition penalty)
+  BFStats stats{};
+};
+
+namespace {
+
+int fail(BFEngine* e, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  std::vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  e->error = buf;
+  return -1;
+}
+
+#define ENG_CUDA(e, call)                                                                     \
+  do {                                                                                        \
+    cudaError_t _r = (call);                                                                  \
+    if (_r != cudaSuccess) return fail((e), "%s: %s", #call, cudaGetErrorString(_r));          \
+  } while (0)
+
+#define ENG_OPC(e, call)                                                                      \
+  do {                                                                                        \
+    if ((call) != OPC_OK) return fail((e), "%s: %s", #call, opc_last_error());                \
+  } while (0)
+
+int dalloc(BFEngine* e, void** p, size_t bytes) {
+  *p = nullptr;
+  if (bytes == 0) bytes = 16;
+  ENG_CUDA(e, cudaMalloc(p, bytes));
+  e->allocs.push_back(*p);
+  e->dev_bytes += bytes;
+  return 0;
+}
+
+// The .bf2 file, memory-mapped for the duration of bf_engine_create.
+struct MappedFile {
+  int fd = -1;
+  const uint8_t* p = nullptr;
+  size_t size = 0;
+  ~MappedFile() {
+    if (p) munmap(const_cast<uint8_t*>(p), size);
+    if (fd >= 0) close(fd);
+  }
+};
+
+struct Model {
+  std::string model_json;
+  std::map<std::string, FileLayer> layers;
+};
+
+int parse_file(BFEngine* e, const MappedFile& f, Model* m) {
+  const uint8_t* b = f.p;
+  const size_t size = f.size;
+  if (size < 24 || std::memcmp(b, "BF2\0", 4) != 0) return fail(e, "Not a valid BF2 file (bad magic)");
+  const uint32_t version = rd<uint32_t>(b + 4), flags = rd<uint32_t>(b + 8);
+  if (version != 1) return fail(e, "Unsupported BF2 version: %u (expected 1)", version);
+  size_t pos = 16;
+  const uint32_t mlen = rd<uint32_t>(b + pos);
+  pos += 4;
+  if (pos + mlen + 4 > size) return fail(e, "BF2 header truncated (model JSON)");
+  m->model_json.assign(reinterpret_cast<const char*>(b + pos), mlen);
+  pos += mlen;
+  const uint32_t qlen = rd<uint32_t>(b + pos);
+  pos += 4;
+  if (pos + qlen + 4 > size) return fail(e, "BF2 header truncated (quantize JSON)");
+  pos += qlen;
+  const uint32_t count = rd<uint32_t>(b + pos);
+  pos += 4;
+  size_t end = size;
+  if (flags & 1u) {  // XXH64 trailer over everything before it
+    if (end < pos + 8) return fail(e, "BF2 file too short for its checksum");
+    end -= 8;
+    const uint64_t stored = rd<uint64_t>(b + end), computed = opc_xxh64(b, end, 0);
+    if (stored != computed)
+      return fail(e, "checksum mismatch (stored %016llx, computed %016llx)", static_cast<unsigned long long>(stored),
+                  static_cast<unsigned long long>(computed));
+  }
+  for (uint32_t i = 0; i < count; ++i) {
+    FileLayer l;
+    if (!parse_layer_at(b, end, pos, &l)) return fail(e, "layer %u header at byte %zu is invalid or truncated", i, pos);
+    l.id_bytes = 4;
+    if (l.type == kQuantized && l.n_out > 0) {  // which outlier-id width is followed by a layer (or the end)
+      FileLayer probe;
+      const size_t e4 = l.data + payload_bytes(l, 4), e8 = l.data + payload_bytes(l, 8);
+      const bool last = i + 1 == count;
+      const bool ok4 = last ? e4 == end : parse_layer_at(b, end, e4, &probe);
+      const bool ok8 = last ? e8 == end : parse_layer_at(b, end, e8, &probe);
+      if (!ok4 && ok8) l.id_bytes = 8;
+      else if (!ok4 && !ok8 && !last) return fail(e, "cannot locate the layer after '%s'", l.name.c_str());
+    }
+    const size_t next = l.data + payload_bytes(l, l.id_bytes);
+    if (next > end) return fail(e, "layer '%s' is truncated", l.name.c_str());
+    m->layers[l.name] = l;
+    pos = next;
+  }
+  return 0;
+}
+
+// Copy one quantized layer to the device and repack it.
+int load_quantized(BFEngine* e, const MappedFile& f, const FileLayer& l, DevLayer* d) {
+  if (l.type != kQuantized) return fail(e, "layer '%s' is not quantized (type %u)", l.name.c_str(), l.type);
+  if (l.entries != 4 || (l.svs != 1 && l.svs != 8) || l.n_groups != l.out_f)
+    return fail(e, "layer '%s': unsupported layout (entries %u, sub_vector_size %u)", l.name.c_str(), l.entries, l.svs);
+  const int M = static_cast<int>(l.out_f), K = static_cast<int>(l.in_f);
+  const size_t cb_bytes = static_cast<size_t>(M) * 4 * l.svs * 2, idx_bytes = static_cast<size_t>(M) * (K / l.svs);
+  const size_t ov_bytes = static_cast<size_t>(l.n_out) * K * 2;
+  const uint8_t* src = f.p + l.data;
+  std::vector<int64_t> ids(l.n_out);
+  const uint8_t* id_src = src + cb_bytes + idx_bytes + ov_bytes;
+  for (int i = 0; i < l.n_out; ++i)
+    ids[i] = l.id_bytes == 8 ? rd<int64_t>(id_src + 8 * i) : static_cast<int64_t>(rd<int32_t>(id_src + 4 * i));
+  const int32_t n_distinct = opc_count_distinct_ids(ids.empty() ? nullptr : ids.data(), l.n_out);
+  opc_layer_plan plan;
+  ENG_OPC(e, opc_plan_layer(M, K, n_distinct, l.svs, &plan));
+  d->L.plan = plan;
+  if (dalloc(e, &d->L.units, plan.units_bytes) || dalloc(e, &d->L.codebooks, plan.codebook_bytes) ||
+      dalloc(e, &d->L.tile_mask, plan.tile_mask_bytes) ||
+      dalloc(e, reinterpret_cast<void**>(&d->L.outlier_rows), plan.outlier_rows_bytes))
+    return -1;
+  void* tmp = nullptr;
+  const size_t tmp_bytes = cb_bytes + idx_bytes + ov_bytes;
+  ENG_CUDA(e, cudaMalloc(&tmp, tmp_bytes));
+  int rc = 0;
+  cudaError_t cr = cudaMemcpyAsync(tmp, src, tmp_bytes, cudaMemcpyHostToDevice, e->stream);
+  if (cr != cudaSuccess) {
+    rc = fail(e, "copying layer '%s' to the device: %s", l.name.c_str(), cudaGetErrorString(cr));
+  } else {
+    const uint8_t* t = static_cast<const uint8_t*>(tmp);
+    if (opc_repack_layer(&d->L, t, t + cb_bytes, l.n_out ? t + cb_bytes + idx_bytes : nullptr,
+                         l.n_out ? ids.data() : nullptr, l.n_out, e->stream) != OPC_OK)
+      rc = fail(e, "repacking layer '%s': %s", l.name.c_str(), opc_last_error());
+  }
+  cudaStreamSynchronize(e->stream);
+  cudaFree(tmp);
+  if (rc) return rc;
+  d->present = true;
+  return 0;
+}
+
+// A fp16 pass-through vector of `n` values on the device (NULL when the file lacks it).
+int load_vector(BFEngine* e, const MappedFile& f, const Model& m, const std::string& name, int n,
+                const __half** out) {
+  *out = nullptr;
+  auto it = m.layers.find(name);
+  if (it == m.layers.end()) return 0;
+  const FileLayer& l = it->second;
+  if (l.type != kPassthrough || static_cast<size_t>(l.out_f) * l.in_f != static_cast<size_t>(n))
+    return fail(e, "'%s': expected a pass-through fp16 vector of %d values", name.c_str(), n);
+  void* p = nullptr;
+  if (dalloc(e, &p, static_cast<size_t>(n) * 2)) return -1;
+  ENG_CUDA(e, cudaMemcpy(p, f.p + l.data, static_cast<size_t>(n) * 2, cudaMemcpyHostToDevice));
+  *out = static_cast<const __half*>(p);
+  return 0;
+}
+
+const FileLayer* find(const Model& m, const std::string& name) {
+  auto it = m.layers.find(name);
+  return it == m.layers.end() ? nullptr : &it->second;
+}
+
+int load_model(BFEngine* e, const char* path, uint32_t max_context) {
+  MappedFile f;
+  f.fd = open(path, O_RDONLY);
+  if (f.fd < 0) return fail(e, "Cannot open file: %s", path);
+  struct stat st;
+  if (fstat(f.fd, &st) != 0 || st.st_size <= 0) return fail(e, "Cannot stat file: %s", path);
+  f.size = static_cast<size_t>(st.st_size);
+  void* mp = mmap(nullptr, f.size, PROT_READ, MAP_PRIVATE, f.fd, 0);
+  if (mp == MAP_FAILED) return fail(e, "Cannot mmap file: %s", path);
+  f.p = static_cast<const uint8_t*>(mp);
+  Model m;
+  if (parse_file(e, f, &m)) return -1;
+
+  // ---- model numbers: JSON first, then the layer shapes
+  const std::string& js = m.model_json;
+  BFModelConfig& c = e->cfg;
+  std::string arch;
+  std::snprintf(c.architecture, sizeof(c.architecture), "%s", json_string(js, "architecture", &arch) ? arch.c_str() : "unknown");
+  double v;
+  const FileLayer* emb = find(m, "model.embed_tokens.weight");
+  if (!emb) return fail(e, "no 'model.embed_tokens.weight' layer");
+  e->hidden = static_cast<int>(emb->in_f);
+  e->vocab = static_cast<int>(emb->out_f);
+  if (json_number(js, "hidden_size", &v) && static_cast<int>(v) != e->hidden)
+    return fail(e, "hidden_size %d in the model JSON, %d in the embedding", static_cast<int>(v), e->hidden);
+  int n_layers = 0;
+  if (json_number(js, "num_hidden_layers", &v)) n_layers = static_cast<int>(v);
+  else
+    while (find(m, "model.layers." + std::to_string(n_layers) + ".self_attn.q_proj.weight")) ++n_layers;
+  if (n_layers <= 0) return fail(e, "the model has no decoder layers");
+  e->n_layers = n_layers;
+  const std::string p0 = "model.layers.0.";
+  const FileLayer* q0 = find(m, p0 + "self_attn.q_proj.weight");
+  const FileLayer* k0 = find(m, p0 + "self_attn.k_proj.weight");
+  const FileLayer* g0 = find(m, p0 + "mlp.gate_proj.weight");
+  if (!q0 || !k0 || !g0) return fail(e, "layer 0 lacks q_proj, k_proj or gate_proj");
+  e->heads = json_number(js, "num_attention_heads", &v) ? static_cast<int>(v) : static_cast<int>(q0->out_f) / 128;
+  if (e->heads <= 0) return fail(e, "cannot determine num_attention_heads");
+  e->hd = json_number(js, "head_dim", &v) ? static_cast<int>(v) : static_cast<int>(q0->out_f) / e->heads;
+  if (json_number(js, "num_kv_heads", &v) || json_number(js, "num_key_value_heads", &v)) e->kv_heads = static_cast<int>(v);
+  else e->kv_heads = e->hd > 0 ? static_cast<int>(k0->out_f) / e->hd : 0;
+  e->inter = static_cast<int>(g0->out_f);
+  const float theta = json_number(js, "rope_theta", &v) ? static_cast<float>(v) : 10000.0f;
+  e->eps = json_number(js, "rms_norm_eps", &v) ? static_cast<float>(v) : 1e-5f;
+  const uint32_t max_pos = json_number(js, "max_position_embeddings", &v) ? static_cast<uint32_t>(v) : 0u;
+  if (e->hd <= 0 || e->hd % 32 || e->hd > kMaxHeadDim || e->heads * e->hd != static_cast<int>(q0->out_f))
+    return fail(e, "head_dim %d with %d heads does not fit q_proj (%u rows); head_dim must be a multiple of 32 up to %d",
+                e->hd, e->heads, q0->out_f, kMaxHeadDim);
+  if (e->kv_heads <= 0 || e->heads % e->kv_heads || e->kv_heads * e->hd != static_cast<int>(k0->out_f))
+    return fail(e, "%d kv heads do not fit k_proj (%u rows) and %d query heads", e->kv_heads, k0->out_f, e->heads);
+  c.vocab_size = static_cast<uint32_t>(e->vocab);
+  c.hidden_size = static_cast<uint32_t>(e->hidden);
+  c.intermediate_size = static_cast<uint32_t>(e->inter);
+  c.num_hidden_layers = static_cast<uint32_t>(e->n_layers);
+  c.num_attention_heads = static_cast<uint32_t>(e->heads);
+  c.num_kv_heads = static_cast<uint32_t>(e->kv_heads);
+  c.max_position_embeddings = max_pos;
+  c.rope_theta = theta;
+  c.head_dim = static_cast<uint32_t>(e->hd);
+  e->ctx = max_context ? max_context : (max_pos ? std::min(max_pos, kDefaultContext) : kDefaultContext);
+
+  // ---- device
+  ENG_CUDA(e, cudaSetDevice(e->device));
+  ENG_CUDA(e, cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
+
+  // ---- weights
+  const int qd = e->heads * e->hd, kvd = e->kv_heads * e->hd;
+  e->blocks.resize(e->n_layers);
+  for (int i = 0; i < e->n_layers; ++i) {
+    Block& B = e->blocks[i];
+    const std::string p = "model.layers." + std::to_string(i) + ".";
+    struct {
+      const char* name;
+      DevLayer* d;
+      int M, K;
+    } want[] = {{"self_attn.q_proj.weight", &B.q, qd, e->hidden},   {"self_attn.k_proj.weight", &B.k, kvd, e->hidden},
+                {"self_attn.v_proj.weight", &B.v, kvd, e->hidden},  {"self_attn.o_proj.weight", &B.o, e->hidden, qd},
+                {"mlp.gate_proj.weight", &B.gate, e->inter, e->hidden}, {"mlp.up_proj.weight", &B.up, e->inter, e->hidden},
+                {"mlp.down_proj.weight", &B.down, e->hidden, e->inter}};
+    for (auto& w : want) {
+      const FileLayer* l = find(m, p + w.name);
+      if (!l) return fail(e, "missing layer '%s%s'", p.c_str(), w.name);
+      if (static_cast<int>(l->out_f) != w.M || static_cast<int>(l->in_f) != w.K)
+        return fail(e, "'%s%s' is %ux%u, expected %dx%d", p.c_str(), w.name, l->out_f, l->in_f, w.M, w.K);
+      if (load_quantized(e, f, *l, w.d)) return -1;
+    }
+    if (load_vector(e, f, m, p + "input_layernorm.weight", e->hidden, &B.ln_in) ||
+        load_vector(e, f, m, p + "post_attention_layernorm.weight", e->hidden, &B.ln_post))
+      return -1;
+  }
+  if (load_vector(e, f, m, "model.norm.weight", e->hidden, &e->final_norm)) return -1;
+  void* table = nullptr;
+  if (dalloc(e, &table, static_cast<size_t>(e->vocab) * e->hidden * 2)) return -1;
+  e->embed_table = static_cast<__half*>(table);
+  if (emb->type == kPassthrough) {
+    ENG_CUDA(e, cudaMemcpy(table, f.p + emb->data, static_cast<size_t>(e->vocab) * e->hidden * 2, cudaMemcpyHostToDevice));
+  } else {
+    if (load_quantized(e, f, *emb, &e->embed)) return -1;
+    ENG_OPC(e, opc_dequant(&e->embed.L, table, e->hidden, e->stream));
+    ENG_CUDA(e, cudaStreamSynchronize(e->stream));
+  }
+  const FileLayer* lm = find(m, "lm_head.weight");
+  if (lm) {
+    if (static_cast<int>(lm->out_f) != e->vocab || static_cast<int>(lm->in_f) != e->hidden)
+      return fail(e, "lm_head is %ux%u, expected %dx%d", lm->out_f, lm->in_f, e->vocab, e->hidden);
+    if (load_quantized(e, f, *lm, &e->lm_head)) return -1;
+  } else {
+    if (!e->embed.present) return fail(e, "no lm_head and the embedding is not quantized (tied fp16 head unsupported)");
+    e->lm_from_embed = true;
+  }
+
+  // ---- KV cache and scratch
+  e->kv_bytes = 2ull * e->n_layers * e->kv_heads * static_cast<size_t>(e->ctx) * e->hd * 2;
+  void* kv = nullptr;
+  if (dalloc(e, &kv, e->kv_bytes)) return -1;
+  e->kcache = static_cast<__half*>(kv);
+  e->vcache = e->kcache + e->kv_bytes / 4;
+  ENG_CUDA(e, cudaMemset(kv, 0, e->kv_bytes));
+  e->ld_x = pad8(e->hidden);
+  e->ld_q = pad8(qd);
+  e->ld_kv = pad8(kvd);
+  e->ld_i = pad8(e->inter);
+  e->ld_y = pad8(std::max(e->hidden, qd));
+  struct {
+    __half** p;
+    int ld;
+  } bufs[] = {{&e->xn, e->ld_x}, {&e->q, e->ld_q}, {&e->k, e->ld_kv}, {&e->v, e->ld_kv}, {&e->att, e->ld_q},
+              {&e->y, e->ld_y},  {&e->g, e->ld_i}, {&e->u, e->ld_i},   {&e->a, e->ld_i}};
+  for (auto& b : bufs) {
+    void* p = nullptr;
+    if (dalloc(e, &p, static_cast<size_t>(kChunk) * b.ld * 2)) return -1;
+    ENG_CUDA(e, cudaMemset(p, 0, static_cast<size_t>(kChunk) * b.ld * 2));
+    *b.p = static_cast<__half*>(p);
+  }
+  void* hp = nullptr;
+  if (dalloc(e, &hp, static_cast<size_t>(kChunk) * e->hidden * 4)) return -1;
+  e->h = static_cast<float*>(hp);
+  void* lp = nullptr;
+  if (dalloc(e, &lp, static_cast<size_t>(e->vocab) * 2)) return -1;
+  e->logits16 = static_cast<__half*>(lp);
+  ENG_CUDA(e, cudaMallocHost(reinterpret_cast<void**>(&e->host_logits), static_cast<size_t>(e->vocab) * 2));
+
+  // one workspace for every projection and chunk size (calls are ordered on the engine's stream)
+  std::vector<const DevLayer*> all;
+  for (auto& B : e->blocks)
+    for (const DevLayer* d : {&B.q, &B.k, &B.v, &B.o, &B.gate, &B.up, &B.down}) all.push_back(d);
+  all.push_back(e->lm_from_embed ? &e->embed : &e->lm_head);
+  for (const DevLayer* d : all)
+    for (int b = 1; b <= static_cast<int>(kChunk); ++b)
+      e->ws_bytes = std::max(e->ws_bytes, opc_gemv_workspace_bytes(&d->L.plan, b, e->device));
+  if (dalloc(e, &e->ws, e->ws_bytes)) return -1;
+  ENG_OPC(e, opc_workspace_init(e->ws, e->ws_bytes, e->stream));
+  ENG_CUDA(e, cudaStreamSynchronize(e->stream));
+  e->stats.peak_memory_bytes = e->dev_bytes;
+  return 0;
+}
+
+// Append n (<= kChunk) tokens at positions pos.. and, with `logits`, write the last one's
+// next-token logits (fp32, vocab values) to the host.
+int run_chunk(BFEngine* e, const int32_t* tokens, int n, float* logits) {
+  cudaStream_t s = e->stream;
+  ChunkTokens tk;
+  for (int i = 0; i < n; ++i) tk.t[i] = tokens[i];
+  const int pos0 = static_cast<int>(e->pos);
+  const int qd = e->heads * e->hd;
+  uint32_t launches = 0;
+  auto gemv = [&](const DevLayer& d, const __half* x, int ldx, __half* y, int ldy, int rows) -> int {
+    ++launches;
+    if (opc_gemv(&d.L, x, ldx, y, ldy, rows, e->ws, e->ws_bytes, s) != OPC_OK)
+      return fail(e, "opc_gemv (%d x %d, batch %d): %s", d.L.plan.M, d.L.plan.K, rows, opc_last_error());
+    return 0;
+  };
+  embed_kernel<<<n, 256, 0, s>>>(e->embed_table, e->hidden, tk, e->h);
+  ++launches;
+  for (int l = 0; l < e->n_layers; ++l) {
+    const Block& B = e->blocks[l];
+    __half* kc = e->kcache + static_cast<size_t>(l) * e->kv_heads * e->ctx * e->hd;
+    __half* vc = e->vcache + static_cast<size_t>(l) * e->kv_heads * e->ctx * e->hd;
+    rmsnorm_kernel<<<n, 256, 0, s>>>(e->h, e->hidden, B.ln_in, e->eps, e->xn, e->ld_x);
+    if (gemv(B.q, e->xn, e->ld_x, e->q, e->ld_q, n) || gemv(B.k, e->xn, e->ld_x, e->k, e->ld_kv, n) ||
+        gemv(B.v, e->xn, e->ld_x, e->v, e->ld_kv, n))
+      return -1;
+    rope_cache_kernel<<<n, 256, 0, s>>>(e->q, e->ld_q, e->k, e->v, e->ld_kv, e->heads, e->kv_heads, e->hd, pos0,
+                                        e->cfg.rope_theta, kc, vc, static_cast<int>(e->ctx));
+    attention_kernel<<<dim3(e->heads, n), kAttnWarps * 32, 0, s>>>(e->q, e->ld_q, kc, vc, e->heads, e->kv_heads, e->hd,
+                                                                   static_cast<int>(e->ctx), pos0, e->att, e->ld_q);
+    if (gemv(B.o, e->att, e->ld_q, e->y, e->ld_y, n)) return -1;
+    residual_kernel<<<n, 256, 0, s>>>(e->h, e->hidden, e->y, e->ld_y);
+    rmsnorm_kernel<<<n, 256, 0, s>>>(e->h, e->hidden, B.ln_post, e->eps, e->xn, e->ld_x);
+    if (gemv(B.gate, e->xn, e->ld_x, e->g, e->ld_i, n) || gemv(B.up, e->xn, e->ld_x, e->u, e->ld_i, n)) return -1;
+    silu_mul_kernel<<<n, 256, 0, s>>>(e->g, e->u, e->inter, e->ld_i, e->a);
+    if (gemv(B.down, e->a, e->ld_i, e->y, e->ld_y, n)) return -1;
+    residual_kernel<<<n, 256, 0, s>>>(e->h, e->hidden, e->y, e->ld_y);
+    launches += 6;
+  }
+  (void)qd;
+  if (logits) {
+    rmsnorm_kernel<<<1, 256, 0, s>>>(e->h + static_cast<size_t>(n - 1) * e->hidden, e->hidden, e->final_norm, e->eps,
+                                     e->xn, e->ld_x);
+    ++launches;
+    if (gemv(e->lm_from_embed ? e->embed : e->lm_head, e->xn, e->ld_x, e->logits16, e->vocab, 1)) return -1;
+    ENG_CUDA(e, cudaMemcpyAsync(e->host_logits, e->logits16, static_cast<size_t>(e->vocab) * 2,
+                                cudaMemcpyDeviceToHost, s));
+  }
+  ENG_CUDA(e, cudaGetLastError());
+  ENG_CUDA(e, cudaStreamSynchronize(s));
+  int32_t derr = 0;
+  if (opc_take_device_error(e->device, &derr) != OPC_OK || derr != 0)
+    return fail(e, "device error %d reported by a kernel", derr);
+  if (logits)
+    for (int i = 0; i < e->vocab; ++i) logits[i] = __half2float(e->host_logits[i]);
+  e->pos += static_cast<uint32_t>(n);
+  e->history.insert(e->history.end(), tokens, tokens + n);
+  e->stats.n_kernel_dispatches += launches;
+  return 0;
+}
+
+int ready(BFEngine* e) {
+  if (!e) return -1;
+  if (!e->error.empty() && e->blocks.empty()) return -1;  // failed at load: stays failed
+  return 0;
+}
+
+// Append tokens in chunks; logits of the last token when `logits` is non-NULL.
+int run_tokens(BFEngine* e, const int32_t* tokens, uint32_t n, float* logits) {
+  if (static_cast<uint64_t>(e->pos) + n > e->ctx)
+    return fail(e, "context full: %u cached + %u new tokens exceed the %u-position cache", e->pos, n, e->ctx);
+  for (uint32_t i = 0; i < n; ++i)
+    if (tokens[i] < 0 || tokens[i] >= e->vocab) return fail(e, "token id %d outside [0, %d)", tokens[i], e->vocab);
+  cudaSetDevice(e->device);
+  const auto t0 = std::chrono::steady_clock::now();
+  for (uint32_t i = 0; i < n; i += kChunk) {
+    const int c = static_cast<int>(std::min<uint32_t>(kChunk, n - i));
+    if (run_chunk(e, tokens + i, c, (logits && i + c == n) ? logits : nullptr)) return -1;
+  }
+  e->stats.total_time_seconds += std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+  return 0;
+}
+
+int32_t sample_token(const std::vector<float>& logits_in, const BFSamplingParams& p, const std::vector<int32_t>& hist,
+                     std::mt19937_64& rng) {
+  std::vector<float> l(logits_in);
+  const int V = static_cast<int>(l.size());
+  if (p.repetition_penalty > 0.f && p.repetition_penalty != 1.f) {
+    std::vector<char> seen(V, 0);
+    for (int32_t t : hist)
+      if (t >= 0 && t < V && !seen[t]) {
+        seen[t] = 1;
+        l[t] = l[t] > 0.f ? l[t] / p.repetition_penalty : l[t] * p.repetition_penalty;
+      }
+  }
+  if (!(p.temperature > 1e-6f)) return static_cast<int32_t>(std::max_element(l.begin(), l.end()) - l.begin());
+  std::vector<int> idx(V);
+  std::iota(idx.begin(), idx.end(), 0);
+  std::sort(idx.begin(), idx.end(), [&](int a, int b) { return l[a] > l[b] || (l[a] == l[b] && a < b); });
+  int keep = V;
+  if (p.top_k > 0 && p.top_k < keep) keep = p.top_k;
+  std::vector<double> w(keep);
+  const double mx = l[idx[0]];
+  double sum = 0.0;
+  for (int i = 0; i < keep; ++i) sum += (w[i] = std::exp((static_cast<double>(l[idx[i]]) - mx) / p.temperature));
+  if (p.top_p > 0.f && p.top_p < 1.f) {
+    double c = 0.0;
+    int k = 0;
+    while (k < keep) {
+      c += w[k++] / sum;
+      if (c >= p.top_p) break;
+    }
+    keep = std::max(k, 1);
+    sum = 0.0;
+    for (int i = 0; i < keep; ++i) sum += w[i];
+  }
+  const double r = std::uniform_real_distribution<double>(0.0, sum)(rng);
+  double c = 0.0;
+  for (int i = 0; i < keep; ++i) {
+    c += w[i];
+    if (r < c) return idx[i];
+  }
+  return idx[keep - 1];
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------------------------------------
+// C API
+// ------------------------------------------------------------------------------------------------
+extern "C" {
+
+BFEngine* bf_engine_create_ex(const char* path, int32_t device, uint32_t max_context) {
+  if (!path) return nullptr;
+  BFEngine* e = new (std::nothrow) BFEngine();
+  if (!e) return nullptr;
+  e->device = device;
+  if (load_model(e, path, max_context) != 0) {
+    // keep the message; release what was allocated (the handle stays, as in the reference)
+    const std::string msg = e->error;
+    for (void* p : e->allocs) cudaFree(p);
+    e->allocs.clear();
+    if (e->host_logits) cudaFreeHost(e->host_logits);
+    e->host_logits = nullptr;
+    if (e->stream) cudaStreamDestroy(e->stream);
+    e->stream = nullptr;
+    e->blocks.clear();
+    e->dev_bytes = 0;
+    e->error = msg.empty() ? "load failed" : msg;
+  }
+  return e;
+}
+
+BFEngine* bf_engine_create(const char* path) { return bf_engine_create_ex(path, 0, 0); }
+
+void bf_engine_destroy(BFEngine* e) {
+  if (!e) return;
+  if (!e->allocs.empty() || e->stream) {
+    cudaSetDevice(e->device);
+    if (e->stream) cudaStreamSynchronize(e->stream);
+    for (void* p : e->allocs) cudaFree(p);
+    if (e->host_logits) cudaFreeHost(e->host_logits);
+    if (e->stream) cudaStreamDestroy(e->stream);
+  }
+  delete e;
+}
+
+const BFModelConfig* bf_engine_get_config(const BFEngine* e) { return e ? &e->cfg : nullptr; }
+const char* bf_engine_get_error(const BFEngine* e) { return (e && !e->error.empty()) ? e->error.c_str() : nullptr; }
+uint32_t bf_engine_vocab_size(const BFEngine* e) { return e ? e->cfg.vocab_size : 0u; }
+
+int bf_engine_forward(BFEngine* e, const int32_t* tokens, uint32_t seq_len, float* logits_out, uint32_t vocab_size) {
+  if (ready(e)) return -1;
+  if (!tokens || seq_len == 0 || !logits_out) return fail(e, "bf_engine_forward: need tokens and a logits buffer");
+  if (vocab_size != e->cfg.vocab_size) return fail(e, "logits buffer holds %u values, the vocabulary %u", vocab_size, e->cfg.vocab_size);
+  bf_engine_reset_kv_cache(e);
+  e->error.clear();
+  return run_tokens(e, tokens, seq_len, logits_out);
+}
+
+int bf_engine_prefill(BFEngine* e, const int32_t* tokens, uint32_t seq_len) {
+  if (ready(e)) return -1;
+  if (seq_len == 0) return 0;
+  if (!tokens) return fail(e, "bf_engine_prefill: NULL tokens");
+  e->error.clear();
+  return run_tokens(e, tokens, seq_len, nullptr);
+}
+
+int bf_engine_forward_step(BFEngine* e, int32_t token, float* logits_out, uint32_t vocab_size) {
+  if (ready(e)) return -1;
+  if (!logits_out) return fail(e, "bf_engine_forward_step: NULL logits buffer");
+  if (vocab_size != e->cfg.vocab_size) return fail(e, "logits buffer holds %u values, the vocabulary %u", vocab_size, e->cfg.vocab_size);
+  e->error.clear();
+  return run_tokens(e, &token, 1, logits_out);
+}
+
+int32_t bf_engine_generate_tokens(BFEngine* e, const int32_t* prompt, uint32_t prompt_len, uint32_t max_new_tokens,
+                                  const BFSamplingParams* params, int32_t* out_tokens) {
+  if (ready(e)) return -1;
+  if ((prompt_len && !prompt) || (max_new_tokens && !out_tokens)) return fail(e, "bf_engine_generate: NULL buffer");
+  const BFSamplingParams& p = params ? *params : BF_DEFAULT_SAMPLING;
+  std::mt19937_64 rng(p.seed ? p.seed : static_cast<uint64_t>(std::chrono::steady_clock::now().time_since_epoch().count()));
+  bf_engine_reset_kv_cache(e);
+  e->error.clear();
+  const int32_t start = 0;  // an empty prompt starts from token 0
+  const int32_t* pr = prompt_len ? prompt : &start;
+  const uint32_t n = prompt_len ? prompt_len : 1u;
+  std::vector<float> logits(e->vocab);
+  const auto t0 = std::chrono::steady_clock::now();
+  if (n > 1 && run_tokens(e, pr, n - 1, nullptr)) return -1;
+  if (max_new_tokens == 0) return 0;
+  if (run_tokens(e, pr + n - 1, 1, logits.data())) return -1;
+  int32_t generated = 0;
+  for (uint32_t i = 0; i < max_new_tokens; ++i) {
+    const int32_t t = sample_token(logits, p, e->history, rng);
+    out_tokens[generated++] = t;
+    if (t == 0 || i + 1 == max_new_tokens) break;
+    if (run_tokens(e, &t, 1, logits.data())) return generated;
+  }
+  e->stats.total_tokens_generated += static_cast<uint64_t>(generated);
+  (void)t0;
+  e->stats.tokens_per_second =
+      e->stats.total_time_seconds > 0 ? static_cast<double>(e->stats.total_tokens_generated) / e->stats.total_time_seconds : 0.0;
+  return generated;
+}
+
+int32_t bf_engine_generate(BFEngine* e, const char* prompt, uint32_t max_new_tokens, const BFSamplingParams* params,
+                           FILE* output) {
+  if (ready(e) || !prompt) return -1;
+  std::vector<int32_t> toks;
+  for (const unsigned char* c = reinterpret_cast<const unsigned char*>(prompt); *c; ++c) toks.push_back(*c);
+  std::vector<int32_t> out(max_new_tokens);
+  const int32_t n = bf_engine_generate_tokens(e, toks.data(), static_cast<uint32_t>(toks.size()), max_new_tokens, params,
+                                              out.data());
+  if (n > 0 && output) {
+    for (int32_t i = 0; i < n; ++i) {
+      if (out[i] >= 0 && out[i] < 256) std::fputc(out[i], output);
+      else std::fputs("?", output);
+    }
+    std::fflush(output);
+  }
+  return n;
+}
+
+void bf_engine_reset_kv_cache(BFEngine* e) {
+  if (!e) return;
+  e->pos = 0;
+  e->history.clear();
+  if (e->kcache && e->stream) {
+    cudaSetDevice(e->device);
+    cudaMemsetAsync(e->kcache, 0, e->kv_bytes, e->stream);
+    cudaStreamSynchronize(e->stream);
+  }
+}
+
+size_t bf_engine_kv_cache_size(const BFEngine* e) { return e ? e->kv_bytes : 0; }
+uint32_t bf_engine_position(const BFEngine* e) { return e ? e->pos : 0u; }
+
+void bf_engine_get_stats(const BFEngine* e, BFStats* s) {
+  if (!e || !s) return;
+  *s = e->stats;
+  s->peak_memory_bytes = e->dev_bytes;
+  s->tokens_per_second = s->total_time_seconds > 0 ? static_cast<double>(s->total_tokens_generated) / s->total_time_seconds : 0.0;
+}
+
+void bf_engine_reset_stats(BFEngine* e) {
+  if (!e) return;
+  e->stats = BFStats{};
+}
+
+const char* bf_version(void) { return "opc_b200 engine 1.0 (runtime API of opacc1ty 1.0.2)"; }
+
+int bf_has_metal_gpu(void) { return 0; }
+
+int bf_has_cuda_gpu(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  for (int d = 0; d < n; ++d) {
+    cudaDeviceProp pr;
+    if (cudaGetDeviceProperties(&pr, d) == cudaSuccess && pr.major == 10) return 1;
+  }
+  return 0;
+}
+
+}  // extern "C"
