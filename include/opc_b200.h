@@ -323,6 +323,29 @@ int opc_dequant(const opc_layer* layer, void* w, int64_t ldw, void* stream);
 int opc_set_gemm_crossover(int32_t batch);
 int32_t opc_gemm_crossover(void);
 
+/* Element-wise (COO) outliers: single weights kept exactly in fp16 beside the codebook form (the
+ * "sparse_outlier" layer type the reference's format reserves, format/header.py:57-60, and its
+ * quantizer never produces).  W_hat = codebook lookup, then W_hat[r][c] = v per entry (a repeated
+ * position keeps its last value).  The codebook part is an ordinary layer without outlier rows
+ * (opc_plan_layer with n_outliers 0, opc_repack_layer); the entries become a row-compressed list:
+ *
+ * opc_coo_build (HOST pointers, load time): codebooks [M][4][svs] fp16 and indices [M][K/svs]
+ * uint8 (the layer's .bf2 arrays), coo [nnz][2] int64 (row, col), values [nnz] fp16 ->
+ * row_ptr [M+1] int32, then for the *nnz_out unique positions in (row, col) order cols int32,
+ * values fp16 and delta = value - codebook value at the position, fp32.  With cols, values_out
+ * and delta all NULL it only fills row_ptr and *nnz_out (a size query). */
+int opc_coo_build(int32_t M, int32_t K, int32_t sub_vector_size, const void* codebooks_f16, const uint8_t* indices_u8,
+                  const int64_t* coo, const void* values_f16, int64_t nnz, int32_t* row_ptr, int32_t* cols,
+                  void* values_out_f16, float* delta, int64_t* nnz_out);
+/* Epilogue after opc_gemv / opc_gemm of the codebook part (same stream; device pointers):
+ * y[b][r] = fp16(y[b][r] + sum_j delta_j * x[b][col_j]) for b < batch, the sum in fp32 in a fixed
+ * order.  x must hold every column the entries name.  One extra fp16 rounding (<= 2^-11 of |y|). */
+int opc_coo_gemv(int32_t M, const int32_t* row_ptr, const int32_t* cols, const float* delta, const void* x, int64_t ldx,
+                 void* y, int64_t ldy, int32_t batch, void* stream);
+/* After opc_dequant: w[r][col_j] = value_j (device pointers); the result is bit-exact. */
+int opc_coo_scatter(int32_t M, const int32_t* row_ptr, const int32_t* cols, const void* values_f16, void* w, int64_t ldw,
+                    void* stream);
+
 /* XXH64 (seed `seed`) of a HOST buffer: the checksum that the .bf2 layout places after the last
  * layer (opacc1ty/format/header.py:26; the reference documents it but never writes it).  Files
  * written with it set bit 0 of the file header's flags.  A format helper, not a kernel. */

@@ -158,6 +158,13 @@ PROTOTYPES = {
     "opc_set_gemm_crossover": (_c.c_int, [_c.c_int32]),
     "opc_gemm_crossover": (_c.c_int32, []),
     "opc_xxh64": (_c.c_uint64, [_c.c_void_p, _c.c_size_t, _c.c_uint64]),
+    "opc_coo_build": (_c.c_int, [_c.c_int32, _c.c_int32, _c.c_int32, _c.c_void_p, _c.c_void_p, _c.c_void_p,
+                                _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_void_p,
+                                _c.POINTER(_c.c_int64)]),
+    "opc_coo_gemv": (_c.c_int, [_c.c_int32, _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_int64,
+                               _c.c_void_p, _c.c_int64, _c.c_int32, _c.c_void_p]),
+    "opc_coo_scatter": (_c.c_int, [_c.c_int32, _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_int64,
+                                  _c.c_void_p]),
     "opc_take_device_error": (_c.c_int, [_c.c_int32, _c.POINTER(_c.c_int32)]),
 }
 

@@ -48,6 +48,9 @@ class Chain:
                 raise ValueError(f"Chain: step {i}: x/y must be fp16 with unit stride")
             if x.shape[0] != batch or y.shape[0] != batch:
                 raise ValueError(f"Chain: step {i}: batch mismatch")
+            if dl.coo is not None:
+                raise _lib.OpcError(_lib.OPC_ERR_UNSUPPORTED, f"Chain: step {i}: element-wise outliers run on "
+                                    "gemv + the CSR epilogue, not in the chain kernel")
             arr[i].layer = ctypes.pointer(dl.c_layer)
             arr[i].x = x.data_ptr()
             arr[i].ldx = x.stride(0) if x.dim() == 2 else dl.K

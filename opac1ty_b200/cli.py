@@ -67,13 +67,15 @@ def _infer_model_config(sd: dict) -> dict:
 @click.option("--bits", type=int, default=2)
 @click.option("--output", "-o", type=click.Path(), default=None)
 @click.option("--outlier-fraction", type=float, default=0.01)
+@click.option("--outlier-mode", type=click.Choice(["row", "element"]), default="row",
+              help="whole outlier rows (the reference's) or single weights kept as COO entries")
 @click.option("--sub-vector-size", type=int, default=8)
 @click.option("--codebook-iters", type=int, default=100)
 @click.option("--no-error-feedback", is_flag=True)
 @click.option("--device", type=click.Choice(["cpu", "cuda"]), default="cpu")
 @click.option("--checksum", is_flag=True, help="end the file with its XXH64 checksum (flags bit 0)")
 @click.option("--json-output", is_flag=True)
-def quantize(model_path, bits, output, outlier_fraction, sub_vector_size, codebook_iters, no_error_feedback, device,
+def quantize(model_path, bits, output, outlier_fraction, outlier_mode, sub_vector_size, codebook_iters, no_error_feedback, device,
              checksum, json_output):
     """Quantize a safetensors model (file or directory) to .bf2 (options of cli/main.py:64-80)."""
     from .format import BF2Writer
@@ -86,7 +88,7 @@ def quantize(model_path, bits, output, outlier_fraction, sub_vector_size, codebo
     t0 = time.time()
     q = VectorQuantizer(QuantizeConfig(bits=bits, sub_vector_size=sub_vector_size, outlier_fraction=outlier_fraction,
                                        use_error_feedback=not no_error_feedback, codebook_iters=codebook_iters,
-                                       device=device))
+                                       device=device, outlier_mode=outlier_mode))
     res = q.quantize_model(sd, mcfg, progress=not json_output)
     elapsed = time.time() - t0
     BF2Writer(str(out)).write(res, mcfg, res["_quantize_config"], progress=not json_output, checksum=checksum)

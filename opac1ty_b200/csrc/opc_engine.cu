@@ -42,7 +42,7 @@ constexpr int kMaxHeadDim = 256;
 // layer a 64-byte header "<H B I I I B B H Q Q Q Q 13s", the name, and the payload.
 // ------------------------------------------------------------------------------------------------
 constexpr int kLayerHeader = 64;
-constexpr uint8_t kQuantized = 0, kPassthrough = 2;
+constexpr uint8_t kQuantized = 0, kSparse = 1, kPassthrough = 2;  // kSparse: element-wise (COO) outliers
 
 struct FileLayer {
   std::string name;
@@ -50,6 +50,7 @@ struct FileLayer {
   uint32_t out_f = 0, in_f = 0, n_groups = 0;
   uint8_t entries = 0, svs = 0;
   uint16_t n_out = 0;
+  uint64_t nnz = 0;     // kSparse: entries (u64 in the first reserved bytes)
   size_t data = 0;      // file offset of the payload (after header and name)
   int id_bytes = 4;     // outlier id width (the reference's own files carry int64)
 };
@@ -62,6 +63,9 @@ T rd(const uint8_t* p) {
 }
 
 size_t payload_bytes(const FileLayer& l, int id_bytes) {
+  if (l.type == kSparse)  // codebooks, indices, values [nnz] fp16, positions [nnz][2] int32
+    return static_cast<size_t>(l.n_groups) * l.entries * l.svs * 2 +
+           (l.svs ? static_cast<size_t>(l.n_groups) * (l.in_f / l.svs) : 0) + static_cast<size_t>(l.nnz) * 10;
   if (l.type == kQuantized) {
     size_t n = static_cast<size_t>(l.n_groups) * l.entries * l.svs * 2;
     if (l.svs) n += static_cast<size_t>(l.n_groups) * (l.in_f / l.svs);
@@ -85,6 +89,7 @@ bool parse_layer_at(const uint8_t* base, size_t size, size_t pos, FileLayer* out
   l.entries = h[15];
   l.svs = h[16];
   l.n_out = rd<uint16_t>(h + 17);
+  l.nnz = l.type == kSparse ? rd<uint64_t>(h + 51) : 0;
   if (nlen == 0 || l.type > 2 || pos + kLayerHeader + nlen > size) return false;
   l.name.assign(reinterpret_cast<const char*>(h + kLayerHeader), nlen);
   l.data = pos + kLayerHeader + nlen;
@@ -287,6 +292,11 @@ namespace {
 struct DevLayer {
   opc_layer L{};
   bool present = false;
+  // element-wise outliers (kSparse layers), row-compressed by opc_coo_build
+  int64_t nnz = 0;
+  int32_t *row_ptr = nullptr, *cols = nullptr;
+  float* delta = nullptr;
+  __half* values = nullptr;
 };
 
 struct Block {
@@ -424,9 +434,12 @@ int parse_file(BFEngine* e, const MappedFile& f, Model* m) {
   return 0;
 }
 
+int load_sparse_part(BFEngine* e, const MappedFile& f, const FileLayer& l, DevLayer* d);
+
 // Copy one quantized layer to the device and repack it.
 int load_quantized(BFEngine* e, const MappedFile& f, const FileLayer& l, DevLayer* d) {
-  if (l.type != kQuantized) return fail(e, "layer '%s' is not quantized (type %u)", l.name.c_str(), l.type);
+  if (l.type != kQuantized && l.type != kSparse)
+    return fail(e, "layer '%s' is not quantized (type %u)", l.name.c_str(), l.type);
   if (l.entries != 4 || (l.svs != 1 && l.svs != 8) || l.n_groups != l.out_f)
     return fail(e, "layer '%s': unsupported layout (entries %u, sub_vector_size %u)", l.name.c_str(), l.entries, l.svs);
   const int M = static_cast<int>(l.out_f), K = static_cast<int>(l.in_f);
@@ -462,6 +475,39 @@ int load_quantized(BFEngine* e, const MappedFile& f, const FileLayer& l, DevLaye
   cudaFree(tmp);
   if (rc) return rc;
   d->present = true;
+  return l.type == kSparse ? load_sparse_part(e, f, l, d) : 0;
+}
+
+// The element outliers of a kSparse layer: row-compressed on the host, then copied to the device.
+int load_sparse_part(BFEngine* e, const MappedFile& f, const FileLayer& l, DevLayer* d) {
+  const int M = static_cast<int>(l.out_f), K = static_cast<int>(l.in_f);
+  const size_t cb_bytes = static_cast<size_t>(M) * 4 * l.svs * 2, idx_bytes = static_cast<size_t>(M) * (K / l.svs);
+  const uint8_t* src = f.p + l.data;
+  const int64_t n = static_cast<int64_t>(l.nnz);
+  const uint8_t* vals = src + cb_bytes + idx_bytes;
+  const uint8_t* posb = vals + 2 * n;
+  std::vector<int64_t> pos(static_cast<size_t>(2 * n));
+  for (int64_t i = 0; i < 2 * n; ++i) pos[i] = rd<int32_t>(posb + 4 * i);
+  std::vector<uint16_t> cb(cb_bytes / 2), vin(static_cast<size_t>(n)), vout(static_cast<size_t>(std::max<int64_t>(n, 1)));
+  std::memcpy(cb.data(), src, cb_bytes);
+  if (n) std::memcpy(vin.data(), vals, static_cast<size_t>(2 * n));
+  std::vector<int32_t> row_ptr(M + 1), cols(static_cast<size_t>(std::max<int64_t>(n, 1)));
+  std::vector<float> delta(cols.size());
+  int64_t nnz = 0;
+  ENG_OPC(e, opc_coo_build(M, K, l.svs, cb.data(), src + cb_bytes, n ? pos.data() : nullptr, n ? vin.data() : nullptr, n,
+                           row_ptr.data(), cols.data(), vout.data(), delta.data(), &nnz));
+  d->nnz = nnz;
+  if (dalloc(e, reinterpret_cast<void**>(&d->row_ptr), sizeof(int32_t) * (M + 1)) ||
+      dalloc(e, reinterpret_cast<void**>(&d->cols), sizeof(int32_t) * std::max<int64_t>(nnz, 1)) ||
+      dalloc(e, reinterpret_cast<void**>(&d->delta), sizeof(float) * std::max<int64_t>(nnz, 1)) ||
+      dalloc(e, reinterpret_cast<void**>(&d->values), 2 * std::max<int64_t>(nnz, 1)))
+    return -1;
+  ENG_CUDA(e, cudaMemcpy(d->row_ptr, row_ptr.data(), sizeof(int32_t) * (M + 1), cudaMemcpyHostToDevice));
+  if (nnz) {
+    ENG_CUDA(e, cudaMemcpy(d->cols, cols.data(), sizeof(int32_t) * nnz, cudaMemcpyHostToDevice));
+    ENG_CUDA(e, cudaMemcpy(d->delta, delta.data(), sizeof(float) * nnz, cudaMemcpyHostToDevice));
+    ENG_CUDA(e, cudaMemcpy(d->values, vout.data(), 2 * nnz, cudaMemcpyHostToDevice));
+  }
   return 0;
 }
 
@@ -585,6 +631,8 @@ int load_model(BFEngine* e, const char* path, uint32_t max_context) {
   } else {
     if (load_quantized(e, f, *emb, &e->embed)) return -1;
     ENG_OPC(e, opc_dequant(&e->embed.L, table, e->hidden, e->stream));
+    if (e->embed.nnz)
+      ENG_OPC(e, opc_coo_scatter(e->vocab, e->embed.row_ptr, e->embed.cols, e->embed.values, table, e->hidden, e->stream));
     ENG_CUDA(e, cudaStreamSynchronize(e->stream));
   }
   const FileLayer* lm = find(m, "lm_head.weight");
@@ -656,6 +704,11 @@ int run_chunk(BFEngine* e, const int32_t* tokens, int n, float* logits) {
     ++launches;
     if (opc_gemv(&d.L, x, ldx, y, ldy, rows, e->ws, e->ws_bytes, s) != OPC_OK)
       return fail(e, "opc_gemv (%d x %d, batch %d): %s", d.L.plan.M, d.L.plan.K, rows, opc_last_error());
+    if (d.nnz) {  // element-wise outliers: the CSR epilogue
+      ++launches;
+      if (opc_coo_gemv(d.L.plan.M, d.row_ptr, d.cols, d.delta, x, ldx, y, ldy, rows, s) != OPC_OK)
+        return fail(e, "opc_coo_gemv: %s", opc_last_error());
+    }
     return 0;
   };
   embed_kernel<<<n, 256, 0, s>>>(e->embed_table, e->hidden, tk, e->h);

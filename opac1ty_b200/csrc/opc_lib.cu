@@ -19,6 +19,7 @@
 #include "opc_device.cuh"
 #include "opc_chain.cuh"
 #include "opc_chain2.cuh"
+#include "opc_coo.cuh"
 #include "opc_gemm.cuh"
 #include "opc_gemv.cuh"
 #include "opc_gemvq.cuh"
@@ -2005,6 +2006,82 @@ int opc_take_device_error(int32_t device, int32_t* code) {
   cudaSetDevice(prev);
   if (e != cudaSuccess) return cuda_fail(e, "opc_take_device_error");
   *code = v;
+  return OPC_OK;
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------------------------------------
+// Element-wise (COO) outliers (opc_coo.cuh)
+// ------------------------------------------------------------------------------------------------
+extern "C" {
+
+int opc_coo_build(int32_t M, int32_t K, int32_t svs, const void* codebooks_f16, const uint8_t* indices_u8,
+                  const int64_t* coo, const void* values_f16, int64_t nnz, int32_t* row_ptr, int32_t* cols,
+                  void* values_out_f16, float* delta, int64_t* nnz_out) {
+  if (M <= 0 || K <= 0 || (svs != 1 && svs != 8) || K % svs)
+    return fail(OPC_ERR_INVALID, "opc_coo_build: M=%d K=%d sub_vector_size=%d", M, K, svs);
+  if (nnz < 0 || (nnz > 0 && (!coo || !values_f16)) || !codebooks_f16 || !indices_u8 || !row_ptr || !nnz_out)
+    return fail(OPC_ERR_INVALID, "opc_coo_build: NULL argument");
+  if (nnz > INT32_MAX) return fail(OPC_ERR_INVALID, "opc_coo_build: %lld entries exceed int32 offsets", static_cast<long long>(nnz));
+  const __half* cb = static_cast<const __half*>(codebooks_f16);
+  const __half* val = static_cast<const __half*>(values_f16);
+  // position -> last entry (a repeated position keeps its last value)
+  std::vector<std::pair<int64_t, int64_t>> key(static_cast<size_t>(nnz));
+  for (int64_t j = 0; j < nnz; ++j) {
+    const int64_t r = coo[2 * j], c = coo[2 * j + 1];
+    if (r < 0 || r >= M || c < 0 || c >= K)
+      return fail(OPC_ERR_INVALID, "opc_coo_build: entry %lld at (%lld, %lld) outside %d x %d", static_cast<long long>(j),
+                  static_cast<long long>(r), static_cast<long long>(c), M, K);
+    key[static_cast<size_t>(j)] = {r * K + c, j};
+  }
+  std::stable_sort(key.begin(), key.end(), [](const auto& a, const auto& b) { return a.first < b.first; });
+  std::vector<int64_t> keep;
+  keep.reserve(key.size());
+  for (size_t i = 0; i < key.size(); ++i)
+    if (i + 1 == key.size() || key[i + 1].first != key[i].first) keep.push_back(key[i].second);
+  const int64_t n = static_cast<int64_t>(keep.size());
+  *nnz_out = n;
+  if (!cols && !values_out_f16 && !delta) {  // size query: row_ptr only
+  } else if (!cols || !values_out_f16 || !delta) {
+    return fail(OPC_ERR_INVALID, "opc_coo_build: cols, values and delta must all be given");
+  }
+  std::fill(row_ptr, row_ptr + M + 1, 0);
+  for (int64_t j : keep) ++row_ptr[coo[2 * j] + 1];
+  for (int32_t r = 0; r < M; ++r) row_ptr[r + 1] += row_ptr[r];
+  if (!cols) return OPC_OK;
+  __half* vout = static_cast<__half*>(values_out_f16);
+  for (int64_t i = 0; i < n; ++i) {
+    const int64_t j = keep[static_cast<size_t>(i)];
+    const int64_t r = coo[2 * j], c = coo[2 * j + 1];
+    const int idx = indices_u8[r * (K / svs) + c / svs];
+    if (idx > 3) return fail(OPC_ERR_INVALID, "opc_coo_build: codebook index %d at (%lld, %lld)", idx, static_cast<long long>(r), static_cast<long long>(c));
+    const float q = __half2float(cb[(r * 4 + idx) * svs + c % svs]);
+    cols[i] = static_cast<int32_t>(c);
+    vout[i] = val[j];
+    delta[i] = __half2float(val[j]) - q;
+  }
+  return OPC_OK;
+}
+
+int opc_coo_gemv(int32_t M, const int32_t* row_ptr, const int32_t* cols, const float* delta, const void* x, int64_t ldx,
+                 void* y, int64_t ldy, int32_t batch, void* stream) {
+  if (M <= 0 || !row_ptr || !cols || !delta || !x || !y || batch < 1 || ldy < M)
+    return fail(OPC_ERR_INVALID, "opc_coo_gemv: invalid arguments (M=%d, batch=%d)", M, batch);
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(ceil_div(M, opc::kCooWarps), 148 * 8));
+  opc::coo_gemv_kernel<<<grid, opc::kCooWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      M, row_ptr, cols, delta, static_cast<const __half*>(x), ldx, static_cast<__half*>(y), ldy, batch);
+  OPC_CUDA(cudaGetLastError(), "opc_coo_gemv launch");
+  return OPC_OK;
+}
+
+int opc_coo_scatter(int32_t M, const int32_t* row_ptr, const int32_t* cols, const void* values_f16, void* w, int64_t ldw,
+                    void* stream) {
+  if (M <= 0 || !row_ptr || !cols || !values_f16 || !w) return fail(OPC_ERR_INVALID, "opc_coo_scatter: invalid arguments");
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(ceil_div(M, 8), 148 * 8));
+  opc::coo_scatter_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      M, row_ptr, cols, static_cast<const __half*>(values_f16), static_cast<__half*>(w), ldw);
+  OPC_CUDA(cudaGetLastError(), "opc_coo_scatter launch");
   return OPC_OK;
 }
 

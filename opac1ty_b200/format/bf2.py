@@ -108,6 +108,29 @@ class BF2Writer:
             if n_out:
                 f.write(_np(ov).astype(np.float16, copy=False).tobytes())
                 f.write(_np(oi).astype(np.int32).tobytes())
+        elif ltype == "sparse_outlier":
+            cb = _np(layer["codebooks"]).astype(np.float16, copy=False)
+            idx = _np(layer["indices"]).astype(np.uint8, copy=False)
+            ov = layer.get("outlier_values")
+            oi = layer.get("outlier_indices")
+            vals = np.zeros(0, np.float16) if ov is None else _np(ov).astype(np.float16, copy=False).reshape(-1)
+            pos = np.zeros((0, 2), np.int32) if oi is None else _np(oi).astype(np.int32).reshape(-1, 2)
+            if len(vals) != len(pos):
+                raise ValueError(f"{name}: {len(vals)} outlier values for {len(pos)} positions")
+            nnz = len(vals)
+            fmt = LayerFormat(
+                name=name, layer_type=LayerType.SPARSE_OUTLIER, out_features=out_f, in_features=in_f,
+                n_groups=cb.shape[0], codebook_entries=cb.shape[1], sub_vector_size=cb.shape[2], n_outliers=0,
+                cb_offset=data_start, idx_offset=data_start + cb.nbytes,
+                out_val_offset=data_start + cb.nbytes + idx.nbytes,
+                out_idx_offset=data_start + cb.nbytes + idx.nbytes + 2 * nnz, nnz=nnz,
+            )
+            f.write(fmt.pack())
+            f.write(name_bytes)
+            f.write(cb.tobytes())
+            f.write(idx.tobytes())
+            f.write(vals.tobytes())
+            f.write(np.ascontiguousarray(pos).tobytes())
         elif ltype == "fp16_passthrough":
             data = _np(layer["data"]).astype(np.float16, copy=False)
             fmt = LayerFormat(name=name, layer_type=LayerType.FP16_PASSTHROUGH, out_features=out_f, in_features=in_f,
@@ -245,6 +268,18 @@ class BF2Reader:
                                   (fmt.n_outliers,))
                 out["outlier_indices"] = ids.to(torch.int32)
             return out
+        if fmt.layer_type == LayerType.SPARSE_OUTLIER:
+            ipr = fmt.in_features // fmt.sub_vector_size
+            cb = self._array(off, fmt.codebook_bytes(), np.float16,
+                             (fmt.n_groups, fmt.codebook_entries, fmt.sub_vector_size))
+            off += fmt.codebook_bytes()
+            idx = self._array(off, fmt.index_bytes(), np.uint8, (fmt.n_groups, ipr))
+            off += fmt.index_bytes()
+            vals = self._array(off, 2 * fmt.nnz, np.float16, (fmt.nnz,))
+            off += 2 * fmt.nnz
+            pos = self._array(off, 8 * fmt.nnz, np.int32, (fmt.nnz, 2))
+            return {"type": "sparse_outlier", "shape": (fmt.out_features, fmt.in_features), "codebooks": cb,
+                    "indices": idx, "outlier_values": vals, "outlier_indices": pos.to(torch.int64)}
         if fmt.layer_type == LayerType.FP16_PASSTHROUGH:
             data = self._array(off, fmt.payload_bytes(), np.float16, (fmt.out_features, fmt.in_features))
             return {"type": "fp16_passthrough", "shape": (fmt.out_features, fmt.in_features), "data": data}

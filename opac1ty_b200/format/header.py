@@ -10,6 +10,12 @@ Layer header, 64 bytes little-endian "<H B I I I B B H Q Q Q Q 13s" (header.py:8
     n_outliers, cb_offset, idx_offset, out_val_offset, out_idx_offset, 13 reserved bytes.
 The struct layout is the reference's (a format must match byte for byte to be a drop-in); the
 code around it is this package's.
+
+Element-wise outliers use the layer type the reference reserves for them, SPARSE_OUTLIER (1),
+which its writer never emits (header.py:57-60): the payload is the quantized layer's codebooks and
+indices, then the outlier values [nnz] fp16, then their positions [nnz][2] int32 (row, col).  The
+entry count does not fit the u16 n_outliers field (1 % of a 4096 x 4096 layer is 167772), so it
+is stored as a u64 in the first 8 reserved bytes and n_outliers is 0.
 """
 
 from __future__ import annotations
@@ -56,22 +62,27 @@ class LayerFormat:
     idx_offset: int = 0
     out_val_offset: int = 0
     out_idx_offset: int = 0
+    nnz: int = 0   # SPARSE_OUTLIER: element outliers (first 8 reserved bytes)
 
     def pack(self) -> bytes:
         name_bytes = self.name.encode("utf-8")[:256]
         return _LAYER_STRUCT.pack(
             len(name_bytes), int(self.layer_type), self.out_features, self.in_features, self.n_groups,
             self.codebook_entries, self.sub_vector_size, self.n_outliers, self.cb_offset, self.idx_offset,
-            self.out_val_offset, self.out_idx_offset, b"\x00" * 13,
+            self.out_val_offset, self.out_idx_offset,
+            (int(self.nnz).to_bytes(8, "little") + b"\x00" * 5) if self.layer_type == LayerType.SPARSE_OUTLIER
+            else b"\x00" * 13,
         )
 
     @classmethod
     def unpack(cls, data: bytes) -> "LayerFormat":
         (_name_len, ltype, out_f, in_f, n_grp, cb_ent, svs, n_out, cb_off, idx_off, ov_off, oi_off,
-         _reserved) = _LAYER_STRUCT.unpack(data[:HEADER_SIZE])
-        return cls(name="", layer_type=LayerType(ltype), out_features=out_f, in_features=in_f, n_groups=n_grp,
+         reserved) = _LAYER_STRUCT.unpack(data[:HEADER_SIZE])
+        lt = LayerType(ltype)
+        nnz = int.from_bytes(reserved[:8], "little") if lt == LayerType.SPARSE_OUTLIER else 0
+        return cls(name="", layer_type=lt, out_features=out_f, in_features=in_f, n_groups=n_grp,
                    codebook_entries=cb_ent, sub_vector_size=svs, n_outliers=n_out, cb_offset=cb_off,
-                   idx_offset=idx_off, out_val_offset=ov_off, out_idx_offset=oi_off)
+                   idx_offset=idx_off, out_val_offset=ov_off, out_idx_offset=oi_off, nnz=nnz)
 
     @staticmethod
     def name_length(data: bytes) -> int:
@@ -90,6 +101,8 @@ class LayerFormat:
         return self.n_outliers * self.in_features * 2
 
     def payload_bytes(self, id_bytes: int = 4) -> int:
+        if self.layer_type == LayerType.SPARSE_OUTLIER:
+            return self.codebook_bytes() + self.index_bytes() + self.nnz * (2 + 8)
         if self.layer_type == LayerType.QUANTIZED:
             n = self.codebook_bytes() + self.index_bytes()
             if self.n_outliers > 0:

@@ -42,4 +42,6 @@ def gemm(dl: L.DeviceLayer, x: torch.Tensor, out: Optional[torch.Tensor] = None)
     stream = torch.cuda.current_stream(dl.device).cuda_stream
     _lib.check(lib.opc_gemm(ctypes.byref(dl.c_layer), x.data_ptr(), x.stride(0), out.data_ptr(), out.stride(0), n,
                             stream))
+    if dl.coo is not None:  # element-wise outliers: the CSR epilogue (opc_coo_gemv)
+        dl.coo.apply_gemv(dl.M, x, out, n, stream)
     return out

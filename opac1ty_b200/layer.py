@@ -53,6 +53,35 @@ def algorithmic_bytes(M: int, K: int, n_outliers: int, batch: int = 1, sub_vecto
 
 
 @dataclass
+class CooPart:
+    """Element-wise outliers of a "sparse_outlier" layer in row-compressed form (``opc_coo_build``):
+    row_ptr [M+1] int32, then per unique position in (row, col) order cols int32, values fp16 and
+    delta fp32 (value minus the codebook value there), all on the layer's device."""
+
+    row_ptr: torch.Tensor
+    cols: torch.Tensor
+    values: torch.Tensor
+    delta: torch.Tensor
+
+    @property
+    def nnz(self) -> int:
+        return int(self.cols.numel())
+
+    def apply_gemv(self, M: int, x2: torch.Tensor, y2: torch.Tensor, batch: int, stream: int):
+        """y += delta . x per row (``opc_coo_gemv``), after the codebook part."""
+        if self.nnz == 0:
+            return
+        _lib.check(_lib.load().opc_coo_gemv(int(M), self.row_ptr.data_ptr(), self.cols.data_ptr(), self.delta.data_ptr(),
+                                            x2.data_ptr(), x2.stride(0), y2.data_ptr(), y2.stride(0), int(batch), stream))
+
+    def apply_dequant(self, M: int, w: torch.Tensor, stream: int):
+        if self.nnz == 0:
+            return
+        _lib.check(_lib.load().opc_coo_scatter(int(M), self.row_ptr.data_ptr(), self.cols.data_ptr(),
+                                               self.values.data_ptr(), w.data_ptr(), w.stride(0), stream))
+
+
+@dataclass
 class DeviceLayer:
     """A quantized layer repacked for the sm_100a kernels, resident on ``device``."""
 
@@ -63,6 +92,7 @@ class DeviceLayer:
     outlier_rows: torch.Tensor
     device: torch.device
     name: Optional[str] = None
+    coo: Optional[CooPart] = None   # element-wise outliers ("sparse_outlier" layers)
 
     def __post_init__(self):
         self.c_layer = _lib.Layer(
@@ -94,10 +124,16 @@ class DeviceLayer:
         return self.plan.sub_vector_size
 
     def algorithmic_bytes(self, batch: int = 1) -> int:
-        return algorithmic_bytes(self.M, self.K, self.n_outliers, batch, self.plan.sub_vector_size)
+        b = algorithmic_bytes(self.M, self.K, self.n_outliers, batch, self.plan.sub_vector_size)
+        if self.coo is not None:  # CSR entries (col + delta) and the epilogue's pass over y
+            b += 8 * self.coo.nnz + 4 * (self.M + 1) + 4 * self.M * batch
+        return b
 
     def device_bytes(self) -> int:
-        return sum(t.numel() * t.element_size() for t in (self.units, self.codebooks, self.tile_mask, self.outlier_rows))
+        ts = [self.units, self.codebooks, self.tile_mask, self.outlier_rows]
+        if self.coo is not None:
+            ts += [self.coo.row_ptr, self.coo.cols, self.coo.values, self.coo.delta]
+        return sum(t.numel() * t.element_size() for t in ts)
 
 
 def _to_device_contig(t, dtype, device) -> torch.Tensor:
@@ -114,8 +150,10 @@ def prepare_layer(layer: dict, device=None, name: Optional[str] = None) -> Devic
     [M][K/svs] uint8, optional ``outlier_values`` [n][K] fp16 and ``outlier_indices`` [n]
     (int32 or int64).
     """
+    if layer.get("type") == "sparse_outlier":
+        return _prepare_sparse(layer, device, name)
     if layer.get("type") != "quantized":
-        raise ValueError(f"prepare_layer: only 'quantized' layers run on the GPU path, got {layer.get('type')!r}")
+        raise ValueError(f"prepare_layer: only quantized layers run on the GPU path, got {layer.get('type')!r}")
     device = _as_cuda_device(device)
     out_f, in_f = (int(v) for v in layer["shape"])
     cb = layer["codebooks"]
@@ -166,6 +204,44 @@ def prepare_layer(layer: dict, device=None, name: Optional[str] = None) -> Devic
     return dl
 
 
+def _prepare_sparse(layer: dict, device, name: Optional[str]) -> DeviceLayer:
+    """A "sparse_outlier" layer: the codebook part repacked without outlier rows, the entries
+    ("outlier_values" [nnz] fp16 at "outlier_indices" [nnz][2] (row, col)) row-compressed."""
+    out_f, in_f = (int(v) for v in layer["shape"])
+    base = {"type": "quantized", "shape": (out_f, in_f), "codebooks": layer["codebooks"], "indices": layer["indices"]}
+    dl = prepare_layer(base, device, name)
+    cb = np.ascontiguousarray(np.asarray(_cpu(layer["codebooks"]), dtype=np.float16))
+    idx = np.ascontiguousarray(np.asarray(_cpu(layer["indices"]), dtype=np.uint8))
+    ov, oi = layer.get("outlier_values"), layer.get("outlier_indices")
+    coo = np.zeros((0, 2), dtype=np.int64) if oi is None else np.ascontiguousarray(
+        np.asarray(_cpu(oi), dtype=np.int64).reshape(-1, 2))
+    vals = np.zeros(0, dtype=np.float16) if ov is None else np.ascontiguousarray(
+        np.asarray(_cpu(ov), dtype=np.float16).reshape(-1))
+    if len(vals) != len(coo):
+        raise ValueError(f"sparse_outlier: {len(vals)} values for {len(coo)} positions")
+    svs = int(cb.shape[2]) if cb.ndim == 3 else 1
+    lib = _lib.load()
+    M = out_f
+    row_ptr = np.zeros(M + 1, dtype=np.int32)
+    n = len(coo)
+    cols = np.zeros(max(n, 1), dtype=np.int32)
+    vout = np.zeros(max(n, 1), dtype=np.float16)
+    delta = np.zeros(max(n, 1), dtype=np.float32)
+    nnz = ctypes.c_int64(0)
+    p = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+    _lib.check(lib.opc_coo_build(M, in_f, svs, p(cb), p(idx), p(coo) if n else None, p(vals) if n else None, n,
+                                 p(row_ptr), p(cols), p(vout), p(delta), ctypes.byref(nnz)))
+    k = int(nnz.value)
+    dev = dl.device
+    dl.coo = CooPart(torch.from_numpy(row_ptr).to(dev), torch.from_numpy(cols[:k].copy()).to(dev),
+                     torch.from_numpy(vout[:k].copy()).to(dev), torch.from_numpy(delta[:k].copy()).to(dev))
+    return dl
+
+
+def _cpu(t):
+    return t.detach().cpu().numpy() if isinstance(t, torch.Tensor) else t
+
+
 def dequantize(dl: DeviceLayer, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """W_hat [M][K] fp16 on the layer's device (``opc_dequant``), into ``out`` if given."""
     lib = _lib.load()
@@ -174,6 +250,8 @@ def dequantize(dl: DeviceLayer, out: Optional[torch.Tensor] = None) -> torch.Ten
         if tuple(w.shape) != (dl.M, dl.K) or w.dtype != torch.float16 or w.stride(1) != 1:
             raise ValueError(f"dequantize: out must be float16 [{dl.M}, {dl.K}] with unit stride")
         _lib.check(lib.opc_dequant(ctypes.byref(dl.c_layer), w.data_ptr(), w.stride(0), _stream_ptr(dl.device)))
+        if dl.coo is not None:
+            dl.coo.apply_dequant(dl.M, w, _stream_ptr(dl.device))
     return w
 
 
@@ -236,6 +314,8 @@ def gemv(dl: DeviceLayer, x: torch.Tensor, out: Optional[torch.Tensor] = None,
         lib.opc_gemv(ctypes.byref(dl.c_layer), x2.data_ptr(), x2.stride(0), y2.data_ptr(), y2.stride(0), batch,
                      workspace.data_ptr(), workspace.numel() * workspace.element_size(), stream)
     )
+    if dl.coo is not None:
+        dl.coo.apply_gemv(dl.M, x2, y2, batch, stream)
     return out.squeeze(0) if squeeze and out.dim() == 2 else out
 
 
@@ -252,4 +332,6 @@ def gemv_noalloc(dl: DeviceLayer, x: torch.Tensor, out: Optional[torch.Tensor] =
     y2 = out.unsqueeze(0) if out.dim() == 1 else out
     _lib.check(_lib.load().opc_gemv_noalloc(ctypes.byref(dl.c_layer), x2.data_ptr(), x2.stride(0), y2.data_ptr(),
                                             y2.stride(0), x2.shape[0], _stream_ptr(dl.device)))
+    if dl.coo is not None:
+        dl.coo.apply_gemv(dl.M, x2, y2, x2.shape[0], _stream_ptr(dl.device))
     return out

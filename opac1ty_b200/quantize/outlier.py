@@ -3,6 +3,11 @@
 Outliers are whole output rows: the top max(1, int(M * fraction)) rows by L2 norm, plus every row
 whose norm exceeds min_magnitude_ratio x the median norm (outlier.py:84-112).  They are kept as
 dense fp16 rows and zeroed in the matrix handed to k-means (outlier.py:146-168).
+
+mode="element" keeps single weights instead (the "sparse_outlier" layers the reference's format
+reserves): the max(1, int(M * K * fraction)) weights of largest magnitude, as (row, col) fp16
+entries; in the matrix handed to k-means each is clipped to the largest magnitude of the other
+weights of its row, so the codebooks fit the rest of the row.
 """
 
 from __future__ import annotations
@@ -18,6 +23,7 @@ class OutlierConfig:
     fraction: float = 0.01
     detection_method: str = "magnitude"
     min_magnitude_ratio: float = 5.0
+    mode: str = "row"   # "row" (the reference's) or "element"
 
 
 class OutlierDetector:
@@ -65,3 +71,24 @@ class OutlierDetector:
         ids = torch.where(outlier_mask)[0]
         dense[outlier_mask] = 0
         return dense, values, ids
+
+    def detect_elements(self, weight: torch.Tensor) -> torch.Tensor:
+        """[M][K] bool: the max(1, int(M * K * fraction)) weights of largest |w| (none for fraction 0)."""
+        mask = torch.zeros_like(weight, dtype=torch.bool)
+        if self.config.fraction <= 0:
+            return mask
+        k = max(1, int(weight.numel() * self.config.fraction))
+        top = weight.abs().reshape(-1).topk(k, sorted=False).indices
+        mask.view(-1)[top] = True
+        return mask
+
+    def extract_element_outliers(self, weight: torch.Tensor, mask: torch.Tensor):
+        """(weight with each outlier clipped to its row's largest other magnitude, positions
+        [nnz][2] int64 (row, col) in row-major order, fp16 values [nnz])."""
+        pos = mask.nonzero()
+        values = weight[mask].half()
+        rest = torch.where(mask, torch.zeros_like(weight), weight.abs()).amax(dim=1, keepdim=True)
+        clipped = torch.maximum(torch.minimum(weight, rest), -rest)
+        dense = torch.where(mask, clipped, weight)
+        return dense, pos, values
+

@@ -29,6 +29,7 @@ class QuantizeConfig:
     codebook_iters: int = 100
     group_dim: int = 0
     device: str = "cpu"   # "cpu", "mps" or "cuda"
+    outlier_mode: str = "row"   # "row" (whole rows, the reference's) or "element" (single weights, COO)
 
 
 class VectorQuantizer:
@@ -37,7 +38,10 @@ class VectorQuantizer:
         self.codebook_learner = CodebookLearner(CodebookConfig(
             n_bits=self.config.bits, sub_vector_size=self.config.sub_vector_size,
             n_iters=self.config.codebook_iters, use_error_feedback=self.config.use_error_feedback))
-        self.outlier_detector = OutlierDetector(OutlierConfig(fraction=self.config.outlier_fraction))
+        if self.config.outlier_mode not in ("row", "element"):
+            raise ValueError(f"outlier_mode must be 'row' or 'element', got {self.config.outlier_mode!r}")
+        self.outlier_detector = OutlierDetector(OutlierConfig(fraction=self.config.outlier_fraction,
+                                                              mode=self.config.outlier_mode))
 
     def _device(self) -> torch.device:
         d = self.config.device
@@ -80,6 +84,8 @@ class VectorQuantizer:
         original_bytes = weight.numel() * 2
         dev = self._device()
         weight = weight.to(device=dev, dtype=torch.float32)
+        if self.config.outlier_mode == "element":
+            return self._quantize_layer_element(weight, original_bytes)
         mask, _ = self.outlier_detector.detect(weight)
         dense, values, ids = self.outlier_detector.extract_outliers(weight, mask)
         cb, idx = self.codebook_learner.learn(dense, device=str(dev))
@@ -94,6 +100,26 @@ class VectorQuantizer:
             "outlier_values": values.cpu() if len(ids) > 0 else None,
             "outlier_indices": ids.cpu() if len(ids) > 0 else None,
             "outlier_mask": mask.cpu(),
+            "compression_ratio": round(original_bytes / max(comp, 1), 2),
+        }
+
+    def _quantize_layer_element(self, weight: torch.Tensor, original_bytes: int) -> dict:
+        """Element-wise outliers: a "sparse_outlier" layer (codebooks and indices of the clipped
+        matrix, fp16 outlier values at (row, col) positions)."""
+        out_f, in_f = weight.shape
+        mask = self.outlier_detector.detect_elements(weight)
+        dense, pos, values = self.outlier_detector.extract_element_outliers(weight, mask)
+        cb, idx = self.codebook_learner.learn(dense, device=str(weight.device))
+        if self.config.use_error_feedback:
+            cb, idx = self._apply_error_feedback(dense, cb, idx)
+        comp = self._compute_compressed_size(out_f, in_f, 0, len(cb), cb.shape[1]) + len(values) * (2 + 8)
+        return {
+            "type": "sparse_outlier",
+            "shape": (out_f, in_f),
+            "codebooks": cb.cpu().half(),
+            "indices": idx.cpu(),
+            "outlier_values": values.cpu(),
+            "outlier_indices": pos.cpu(),
             "compression_ratio": round(original_bytes / max(comp, 1), 2),
         }
 

@@ -99,6 +99,23 @@ def random_layer_vq8(M: int, K: int, n_outliers: int, seed: int, shuffle_ids: bo
     return layer
 
 
+def random_layer_sparse(M: int, K: int, fraction: float, seed: int, svs: int = 1, duplicates: int = 0) -> dict:
+    """A "sparse_outlier" layer dict (element-wise outliers): codebooks and indices as above, and
+    max(1, int(M * K * fraction)) entries (plus `duplicates` repeated positions with other values)
+    of heavy-tailed fp16 values at random (row, col) positions."""
+    base = random_layer_vq8(M, K, 0, seed) if svs == 8 else random_layer(M, K, 0, seed)
+    rng = rng_for(seed + 7919)
+    n = max(1, int(M * K * fraction)) if fraction > 0 else 0
+    flat = rng.choice(M * K, size=n, replace=False)
+    pos = np.stack([flat // K, flat % K], axis=1).astype(np.int64)
+    if duplicates:
+        pos = np.concatenate([pos, pos[rng.integers(0, n, size=duplicates)]])
+    scale = 8 * STD / math.sqrt(NU / (NU - 2))
+    vals = (rng.standard_t(NU, size=len(pos)) * scale).astype(np.float16)
+    return {"type": "sparse_outlier", "shape": (M, K), "codebooks": base["codebooks"], "indices": base["indices"],
+            "outlier_values": torch.from_numpy(vals), "outlier_indices": torch.from_numpy(pos)}
+
+
 def random_layer_device(M: int, K: int, n_outliers: int, seed: int, device) -> dict:
     """Like ``random_layer`` but generated with torch's RNG directly on ``device`` (fast for the
     full model stacks; values differ from the numpy generator, the statistics do not)."""

@@ -85,7 +85,23 @@ def layer_arrays(layer: dict):
 
 
 def dequantize_np(layer: dict) -> np.ndarray:
-    """Vectorised restatement of dequantize_layer for "quantized" layers (fp16 [M][Kc])."""
+    """Vectorised restatement of dequantize_layer for "quantized" layers (fp16 [M][Kc]).
+    "sparse_outlier" layers (element-wise outliers, the layer type format/header.py:57-60
+    reserves): the codebook lookup, then W[r][c] = v per entry in order (the last entry of a
+    repeated position wins)."""
+    if layer.get("type") == "sparse_outlier":
+        base = dict(layer, type="quantized", outlier_values=None, outlier_indices=None)
+        w = dequantize_np(base)
+        ov, oi = layer.get("outlier_values"), layer.get("outlier_indices")
+        if ov is not None and oi is not None:
+            vals = _np(ov, np.float16).reshape(-1)
+            pos = _np(oi, np.int64).reshape(-1, 2)
+            M, K = w.shape
+            if len(pos) and (pos.min() < 0 or (pos[:, 0] >= M).any() or (pos[:, 1] >= K).any()):
+                raise IndexError("element outlier position out of range")
+            for (r, c), v in zip(pos, vals):
+                w[r, c] = v
+        return w
     cb, idx, ov, oi, M, K = layer_arrays(layer)
     svs = cb.shape[2]
     if idx.size and int(idx.max()) > 3:

@@ -24,7 +24,8 @@ def _scaled(layer: dict, scale: float) -> dict:
 
 
 def build(path, *, hidden=256, heads=4, kv_heads=2, n_layers=2, inter=512, vocab=320, svs=1, outliers=True,
-          tied=False, norms=True, checksum=False, seed=0, rope_theta=10000.0, json_heads=True) -> dict:
+          tied=False, norms=True, checksum=False, seed=0, rope_theta=10000.0, json_heads=True,
+          element=False) -> dict:
     """Write the model to `path`; returns the layer dicts (for the float64 forward) and numbers."""
     hd = hidden // heads
     rng = np.random.default_rng(seed)
@@ -34,6 +35,8 @@ def build(path, *, hidden=256, heads=4, kv_heads=2, n_layers=2, inter=512, vocab
 
     def q(M, K, scale):
         s[0] += 1
+        if element:  # element-wise outliers ("sparse_outlier" layers)
+            return _scaled(synthetic.random_layer_sparse(M, K, 0.01, s[0], svs=svs, duplicates=2), scale)
         n = synthetic.n_outliers_for(M, 0.01) if outliers else 0
         return _scaled(make(M, K, n, s[0]), scale)
 
@@ -86,7 +89,7 @@ def _rope(x, pos, hd, theta):
 def forward64(model: dict, tokens) -> np.ndarray:
     """float64 logits after each token of `tokens` (a fresh sequence): [T][vocab]."""
     L = model["layers"]
-    W = {k: dequantize_np(v).astype(np.float64) for k, v in L.items() if v["type"] == "quantized"}
+    W = {k: dequantize_np(v).astype(np.float64) for k, v in L.items() if v["type"] in ("quantized", "sparse_outlier")}
     vec = {k: v["data"].numpy().astype(np.float64) for k, v in L.items() if v["type"] == "fp16_passthrough"}
     hd, H, KV, eps, theta = model["hd"], model["heads"], model["kv_heads"], model["eps"], model["theta"]
     tok = np.asarray(tokens)
