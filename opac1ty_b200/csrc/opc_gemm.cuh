@@ -6,7 +6,9 @@
 //
 // Persistent: one CTA per SM walks the output tiles c, c + grid, c + 2 grid, ...  A tile is 128
 // weight rows x N tokens (N = 16..256, chosen by the host from the token count and the SM count),
-// K in stages of 64.  Roles, all pipelined across tile boundaries:
+// K in stages of 64 x kSub (kSub 2 for N <= 64: the MMA warp's per-stage cost -- two barrier
+// waits, the commit and the loop, ~550 cycles next to ~50 per tcgen05.mma (measured) -- bounds
+// small tiles, so their stages carry twice the work).  Roles, all pipelined across tile boundaries:
 //   warp 0       TMA (no multicast): the X tile (N tokens x 64 fp16, 128-byte swizzle) per stage
 //   warp 22      TMA: the packed units of the tile's 8 row tiles (one 2-D copy of 8 x 512 bytes)
 //                per stage into a deeper ring of its own, freed as soon as the stage is decoded
@@ -45,17 +47,19 @@ constexpr int kGmUBytes = 8 * kUnitBytes;    // 8 row tiles x one unit
 constexpr int kGmMaxSplit = 8;                // K split of a tile into at most this many items
 constexpr int kGmPrefetch = 24;               // stages ahead whose packed units are prefetched into L2
 constexpr int kGmSmemBudget = 227 * 1024 - 1024 - 512;  // dynamic shared memory less slack and barriers
-// Token tile N: x stage N*64 fp16, two accumulators of N fp32 TMEM columns.
+// Token tile N: x sub-tile N*64 fp16, two accumulators of N fp32 TMEM columns; a stage holds kSub
+// sub-tiles of A (128 x 64) and of x (N x 64), each in its own 128-byte-swizzled block.
 __host__ __device__ constexpr int gm_b_bytes(int N) { return N * kGmK * 2; }
-__host__ __device__ constexpr int gm_stage_bytes(int N) { return kGmABytes + gm_b_bytes(N); }
-__host__ __device__ constexpr int gm_stages(int N) {
-  return (kGmSmemBudget - kGmUStages * kGmUBytes) / gm_stage_bytes(N) > 8
+__host__ __device__ constexpr int gm_stage_bytes(int N, int sub = 1) { return sub * (kGmABytes + gm_b_bytes(N)); }
+__host__ __device__ constexpr int gm_stages(int N, int sub = 1) {
+  return (kGmSmemBudget - kGmUStages * kGmUBytes) / gm_stage_bytes(N, sub) > 8
              ? 8
-             : (kGmSmemBudget - kGmUStages * kGmUBytes) / gm_stage_bytes(N);
+             : (kGmSmemBudget - kGmUStages * kGmUBytes) / gm_stage_bytes(N, sub);
 }
 __host__ __device__ constexpr int gm_tmem_cols(int N) { return 2 * N < 32 ? 32 : 2 * N; }
-__host__ __device__ constexpr size_t gm_smem_bytes(int N) {
-  return 1024 /*alignment slack*/ + static_cast<size_t>(gm_stages(N)) * gm_stage_bytes(N) + kGmUStages * kGmUBytes + 512;
+__host__ __device__ constexpr size_t gm_smem_bytes(int N, int sub = 1) {
+  return 1024 /*alignment slack*/ + static_cast<size_t>(gm_stages(N, sub)) * gm_stage_bytes(N, sub) +
+         kGmUStages * kGmUBytes + 512;
 }
 
 struct GemmArgs {
@@ -163,17 +167,17 @@ __device__ __forceinline__ uint32_t sw128_off(int r, int c) {
 // array of 8-byte elements, box 512 B x 8 row tiles (one copy brings a k block of all 8 row tiles);
 // sub_vector_size 8: [MT][KB * 128 B], box 128 B x 8 row tiles.  td: the row-major outlier rows
 // [n_slots][K_pad] fp16, box 64 x 128 rows, 128-byte swizzle (a dense tile's A stage as is).
-template <int kN>
+template <int kN, int kSub>
 __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap tx,
                                                              const __grid_constant__ CUtensorMap tu,
                                                              const __grid_constant__ CUtensorMap td, const GemmArgs a) {
-  constexpr int kBBytes = gm_b_bytes(kN);
-  constexpr int kS = gm_stages(kN);
+  constexpr int kBBytes = gm_b_bytes(kN);   // one x sub-tile
+  constexpr int kS = gm_stages(kN, kSub);
   constexpr int kCols = gm_tmem_cols(kN);
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
-  const uint32_t sA = base, sB = sA + kS * kGmABytes, sU = sB + kS * kBBytes;
+  const uint32_t sA = base, sB = sA + kS * kSub * kGmABytes, sU = sB + kS * kSub * kBBytes;
   const uint32_t bars = sU + kGmUStages * kGmUBytes;
   const uint32_t full_b = bars, afull_b = bars + 8 * kS, empty_b = bars + 16 * kS;
   const uint32_t ufull_b = bars + 24 * kS, uempty_b = ufull_b + 8 * kGmUStages;
@@ -183,7 +187,7 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_consta
   const int warp = __shfl_sync(0xffffffffu, static_cast<int>(threadIdx.x >> 5), 0);
   const int lane = threadIdx.x & 31;
   const int G = static_cast<int>(gridDim.x);
-  const int nk = a.K_pad / kGmK;
+  const int nk = a.K_pad / (kGmK * kSub);  // stages of a tile
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kS; ++s) {
@@ -227,8 +231,10 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_consta
             ok = false;
             break;
           }
-          mbar_expect_tx(full_b + 8 * st, kBBytes);
-          tma_load_2d(sB + st * kBBytes, &tx, s * kGmK, n0, full_b + 8 * st);
+          mbar_expect_tx(full_b + 8 * st, kSub * kBBytes);
+#pragma unroll
+          for (int j = 0; j < kSub; ++j)
+            tma_load_2d(sB + (st * kSub + j) * kBBytes, &tx, (s * kSub + j) * kGmK, n0, full_b + 8 * st);
         }
       }
       // copies nobody consumed (a role gave up) land before the CTA exits: wait (bounded) for
@@ -257,15 +263,17 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_consta
             break;
           }
           // the units kGmPrefetch stages ahead (same item) go to L2 now; one prefetch per k block
-          const int sf = s + kGmPrefetch;
-          if (sf < s1 && (sf & (a.svs8 ? 3 : 1)) == 0)
-            tma_prefetch_2d(&tu, a.svs8 ? (sf >> 2) * (kVq8UnitBytesGm / 8) : (sf >> 1) * (kUnitBytes / 8), mi * 8);
+          const int sf = s + kGmPrefetch / kSub;
+          if (sf < s1 && ((sf * kSub) & (a.svs8 ? 3 : 1)) == 0)
+            tma_prefetch_2d(&tu, a.svs8 ? ((sf * kSub) >> 2) * (kVq8UnitBytesGm / 8) : ((sf * kSub) >> 1) * (kUnitBytes / 8),
+                            mi * 8);
           // a box past the last row tile is filled with zeros and still counts its full size; x
           // coordinate: the stage's k block in 8-byte elements (512-byte units of 128 columns, or
           // 128-byte svs-8 units of 256 columns: 16-byte aligned either way)
           mbar_expect_tx(ufull_b + 8 * su, ubytes);
-          tma_load_2d(sU + su * kGmUBytes, &tu, a.svs8 ? (s >> 2) * (kVq8UnitBytesGm / 8) : (s >> 1) * (kUnitBytes / 8),
-                      mi * 8, ufull_b + 8 * su);
+          tma_load_2d(sU + su * kGmUBytes, &tu,
+                      a.svs8 ? ((s * kSub) >> 2) * (kVq8UnitBytesGm / 8) : ((s * kSub) >> 1) * (kUnitBytes / 8), mi * 8,
+                      ufull_b + 8 * su);
         }
       }
       for (int su = 0; su < kGmUStages && su < gu; ++su) {
@@ -296,10 +304,14 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_consta
             break;
           }
           tc_fence_after();
-          const uint64_t ad = umma_desc_sw128(sA + st * kGmABytes), bd = umma_desc_sw128(sB + st * kBBytes);
 #pragma unroll
-          for (int kk = 0; kk < kGmK / 16; ++kk)  // +32 bytes per K = 16 step inside the swizzle atom
-            umma_f16(tacc, ad + 2 * kk, bd + 2 * kk, gm_idesc(kN), (s > s0 || kk > 0) ? 1u : 0u);
+          for (int j = 0; j < kSub; ++j) {
+            const uint64_t ad = umma_desc_sw128(sA + (st * kSub + j) * kGmABytes);
+            const uint64_t bd = umma_desc_sw128(sB + (st * kSub + j) * kBBytes);
+#pragma unroll
+            for (int kk = 0; kk < kGmK / 16; ++kk)  // +32 bytes per K = 16 step inside the swizzle atom
+              umma_f16(tacc, ad + 2 * kk, bd + 2 * kk, gm_idesc(kN), (s > s0 || j > 0 || kk > 0) ? 1u : 0u);
+          }
           umma_commit(empty_b + 8 * st);
         }
         if (!ok) break;
@@ -350,15 +362,17 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_consta
           ok = false;
           break;
         }
-        const uint32_t dstA = sA + st * kGmABytes;
+        const uint32_t dstA0 = sA + st * kSub * kGmABytes;
         if (dense) {
           // the outlier rows' A tile is a plain copy: one TMA in the same 128-byte-swizzled
           // K-major layout, completing on the stage's "A full" barrier (the first warp's
           // arrive.expect_tx is one of the group's four arrivals; rows past the slots read zeros)
           if ((d & 3) == 0) {  // the group's first warp
             if (lane == 0) {
-              mbar_expect_tx(afull_b + 8 * st, kGmABytes);
-              tma_load_2d(dstA, &td, s * kGmK, (mi - a.m_tiles) * kGmM, afull_b + 8 * st);
+              mbar_expect_tx(afull_b + 8 * st, kSub * kGmABytes);
+#pragma unroll
+              for (int j = 0; j < kSub; ++j)
+                tma_load_2d(dstA0 + j * kGmABytes, &td, (s * kSub + j) * kGmK, (mi - a.m_tiles) * kGmM, afull_b + 8 * st);
             }
           } else if (lane == 0) {
             mbar_arrive(afull_b + 8 * st);
@@ -369,10 +383,14 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_consta
             ok = false;
             break;
           }
+#pragma unroll
+          for (int j = 0; j < kSub; ++j) {
+          const int q64 = s * kSub + j;  // the 64-column sub-stage
+          const uint32_t dstA = dstA0 + j * kGmABytes;
           if (a.svs8) {
-            // word s&3 of row pair gl's 16 bytes: byte c/2 = k16 step, bits 2(c&1) + 4hi = the index of
+            // word q64&3 of row pair gl's 16 bytes: byte c/2 = k16 step, bits 2(c&1) + 4hi = the index of
             // chunk c (8 columns = one codebook vector)
-            const uint32_t w = row_live ? lds32(sU + su * kGmUBytes + tl_row * kVq8UnitBytesGm + gl * 16 + 4 * (s & 3)) : 0u;
+            const uint32_t w = row_live ? lds32(sU + su * kGmUBytes + tl_row * kVq8UnitBytesGm + gl * 16 + 4 * (q64 & 3)) : 0u;
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
               const uint32_t i = (w >> (8 * (c >> 1) + 2 * (c & 1) + 4 * hi)) & 3u;
@@ -383,7 +401,7 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_consta
             }
           } else {
             // chunk c = 4jj + q of the stage (columns 32jj + 8q + 0..7) is in word 2(s&1) + jj of lane 4gl + q
-            const uint32_t ub = sU + su * kGmUBytes + tl_row * kUnitBytes + (4 * gl) * 16 + 8 * (s & 1);
+            const uint32_t ub = sU + su * kGmUBytes + tl_row * kUnitBytes + (4 * gl) * 16 + 8 * (q64 & 1);
             uint32_t w[8];
 #pragma unroll
             for (int c = 0; c < 8; ++c) w[c] = row_live ? lds32(ub + (c & 3) * 16 + 4 * (c >> 2)) : 0u;
@@ -393,6 +411,7 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_kernel(const __grid_consta
               if (row_live) v = decode_row8(hi ? w[c] >> 16 : w[c], lo4, hi4);
               sts128(dstA + sw128_off(r, c), v);
             }
+          }
           }
         }
         fence_proxy_async_smem();

@@ -157,35 +157,44 @@ size_t acc_offset(const opc_layer_plan& p, int sm_count) {
   return counters_offset(sm_count) + align_up(static_cast<size_t>(p.row_tiles + p.outlier_tiles) * sizeof(int32_t), 256);
 }
 
-// Launch shape of the prefill GEMM for n_tok tokens: token tile tn (16..256) and K split, chosen
-// by the least estimated time -- waves of persistent items (one CTA per SM) times the stages of an
-// item times the cost of a stage (the larger of the A-tile decode, ~300 cycles, and the MMAs,
-// ~2N cycles for 128 x N x 64 on one SM).  A K split (only with a workspace, split_ok) cuts a tile
-// into items of at least 8 stages whose fp32 partials are added in a fixed order.
+// Launch shape of the prefill GEMM for n_tok tokens: token tile tn (16..256), stage depth (64 x sub
+// columns; sub 2 for tiles of up to 64 tokens) and K split, chosen by the least estimated time --
+// waves of persistent items (one CTA per SM) times the 64-column steps of an item times the cost
+// of a step: the largest of the MMA warp's per-stage work ((550 + 200 sub) / sub cycles: barrier
+// waits, commit and loop ~550, each tcgen05.mma ~50, measured), the decode (~330) and the tensor
+// time (~2.8 N for 128 x N x 64 on one SM).  A K split (only with a workspace, split_ok) cuts a tile
+// into items of at least 16 steps whose fp32 partials are added in a fixed order.
 struct GemmPlan {
-  int tn = 16, ksplit = 1, nk_slice = 1;
+  int tn = 16, sub = 1, ksplit = 1, nk_slice = 1;   // nk_slice in stages of 64 x sub columns
   int64_t tiles = 0;        // (packed M tiles + dense tiles) x token tiles
   size_t split_bytes = 0;   // workspace of the split: [tiles][4] counters, then the fp32 partials
 };
+// Stage depth of a token tile: two 64-column sub-tiles for N <= 64 (their stages still fit four
+// deep in shared memory), one above.
+int gemm_sub(int N) { return N <= 64 ? 2 : 1; }
+
 GemmPlan gemm_plan(const opc_layer_plan& p, int n_tok, int sm_count, bool split_ok) {
   const int64_t m_tiles = ceil_div(p.M_pad, opc::kGmM);
   const int64_t d_tiles = p.n_outliers > 0 ? ceil_div(static_cast<int64_t>(p.outlier_tiles) * opc::kTileRows, opc::kGmM) : 0;
-  const int nk = p.K_pad / opc::kGmK;
   GemmPlan best;
   double best_cost = -1.0;
   for (int N = 16; N <= 256; N *= 2) {
     if (N > 16 && N / 2 >= n_tok) break;  // a smaller tile already covers every token
+    const int sub = gemm_sub(N);
+    const int nk = p.K_pad / (opc::kGmK * sub);  // K_pad is a multiple of 128
+    const double step = std::max({(550.0 + 200.0 * sub) / sub, 330.0, 2.8 * N});
     const int64_t tiles = (m_tiles + d_tiles) * ceil_div(n_tok, N);
     for (int S = 1; S <= (split_ok ? opc::kGmMaxSplit : 1); ++S) {
       const int slice = static_cast<int>(ceil_div(nk, S));
-      // a split only for layers with fewer tiles than SMs, into one wave of items of >= 16 stages
-      if (S > 1 && (tiles >= sm_count || tiles * S > sm_count || slice < 16 || ceil_div(nk, slice) != S)) continue;
+      // a split only for layers with fewer tiles than SMs, into one wave of items of >= 16 steps
+      if (S > 1 && (tiles >= sm_count || tiles * S > sm_count || slice * sub < 16 || ceil_div(nk, slice) != S)) continue;
       const double waves = static_cast<double>(ceil_div(tiles * S, sm_count));
       // + the split's epilogue: partials out, and the last arrival reading and adding them
-      const double cost = waves * slice * std::max(300.0, 2.0 * N) + (S > 1 ? 3000.0 + 500.0 * S : 0.0);
+      const double cost = waves * slice * sub * step + (S > 1 ? 3000.0 + 500.0 * S : 0.0);
       if (best_cost < 0.0 || cost < best_cost) {
         best_cost = cost;
         best.tn = N;
+        best.sub = sub;
         best.ksplit = S;
         best.nk_slice = slice;
         best.tiles = tiles;
@@ -285,7 +294,7 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-template <int kN>
+template <int kN, int kSub>
 int launch_gemm_t(const CUtensorMap& tx, const CUtensorMap& tu, const CUtensorMap& td, const opc::GemmArgs& a,
                   unsigned grid, cudaStream_t stream, int dev) {
   static std::mutex mu;
@@ -293,13 +302,13 @@ int launch_gemm_t(const CUtensorMap& tx, const CUtensorMap& tu, const CUtensorMa
   {
     std::lock_guard<std::mutex> lk(mu);
     if (!configured[dev]) {
-      OPC_CUDA(cudaFuncSetAttribute(opc::gemm_kernel<kN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(opc::gm_smem_bytes(kN))),
+      OPC_CUDA(cudaFuncSetAttribute(opc::gemm_kernel<kN, kSub>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(opc::gm_smem_bytes(kN, kSub))),
                "cudaFuncSetAttribute(max dynamic smem, gemm)");
       configured[dev] = true;
     }
   }
-  opc::gemm_kernel<kN><<<grid, opc::kGmThreads, opc::gm_smem_bytes(kN), stream>>>(tx, tu, td, a);
+  opc::gemm_kernel<kN, kSub><<<grid, opc::kGmThreads, opc::gm_smem_bytes(kN, kSub), stream>>>(tx, tu, td, a);
   OPC_CUDA(cudaGetLastError(), "launch gemm_kernel");
   return OPC_OK;
 }
@@ -906,8 +915,8 @@ int gemm_run(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ld
   if (gp.ksplit > 1 && (ws_bytes < gp.split_bytes || !aligned(ws, 256))) gp = gemm_plan(p, n_tok, dc.sm_count, false);
   const int tn = gp.tn;
   const int64_t m_tiles = ceil_div(p.M_pad, opc::kGmM);
-  if (opc::gm_smem_bytes(tn) > static_cast<size_t>(dc.max_smem_optin))
-    return fail(OPC_ERR_UNSUPPORTED, "opc_gemm: needs %zu bytes of shared memory", opc::gm_smem_bytes(tn));
+  if (opc::gm_smem_bytes(tn, gp.sub) > static_cast<size_t>(dc.max_smem_optin))
+    return fail(OPC_ERR_UNSUPPORTED, "opc_gemm: needs %zu bytes of shared memory", opc::gm_smem_bytes(tn, gp.sub));
 
   CUtensorMap tx;
   const cuuint64_t gdim[2] = {static_cast<cuuint64_t>(p.K), static_cast<cuuint64_t>(n_tok)};
@@ -975,18 +984,18 @@ int gemm_run(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ld
   if (tiles * gp.ksplit >= (int64_t(1) << 31)) return fail(OPC_ERR_UNSUPPORTED, "opc_gemm: too many tiles");
   a.tiles = static_cast<int32_t>(tiles);
   a.ksplit = gp.ksplit;
-  a.nk_slice = gp.ksplit > 1 ? gp.nk_slice : p.K_pad / opc::kGmK;
+  a.nk_slice = gp.ksplit > 1 ? gp.nk_slice : p.K_pad / (opc::kGmK * gp.sub);
   if (gp.ksplit > 1) {
     a.cnt = static_cast<int32_t*>(ws);  // zero between calls: the last arrival of each count resets it
     a.part = reinterpret_cast<float*>(static_cast<char*>(ws) + align_up(static_cast<size_t>(tiles) * 4 * sizeof(int32_t), 256));
   }
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>(tiles * gp.ksplit, dc.sm_count));
   switch (tn) {
-    case 256: return launch_gemm_t<256>(tx, tu, td, a, grid, s, dev);
-    case 128: return launch_gemm_t<128>(tx, tu, td, a, grid, s, dev);
-    case 64: return launch_gemm_t<64>(tx, tu, td, a, grid, s, dev);
-    case 32: return launch_gemm_t<32>(tx, tu, td, a, grid, s, dev);
-    default: return launch_gemm_t<16>(tx, tu, td, a, grid, s, dev);
+    case 256: return launch_gemm_t<256, 1>(tx, tu, td, a, grid, s, dev);
+    case 128: return launch_gemm_t<128, 1>(tx, tu, td, a, grid, s, dev);
+    case 64: return launch_gemm_t<64, 2>(tx, tu, td, a, grid, s, dev);
+    case 32: return launch_gemm_t<32, 2>(tx, tu, td, a, grid, s, dev);
+    default: return launch_gemm_t<16, 2>(tx, tu, td, a, grid, s, dev);
   }
 }
 
