@@ -2077,7 +2077,8 @@ int opc_coo_gemv(int32_t M, const int32_t* row_ptr, const int32_t* cols, const f
                  void* y, int64_t ldy, int32_t batch, void* stream) {
   if (M <= 0 || !row_ptr || !cols || !delta || !x || !y || batch < 1 || ldy < M)
     return fail(OPC_ERR_INVALID, "opc_coo_gemv: invalid arguments (M=%d, batch=%d)", M, batch);
-  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(ceil_div(M, opc::kCooWarps), 148 * 8));
+  const unsigned grid =
+      static_cast<unsigned>(std::min<int64_t>(ceil_div(static_cast<int64_t>(M) * batch, opc::kCooWarps * 32), 148 * 16));
   opc::coo_gemv_kernel<<<grid, opc::kCooWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(
       M, row_ptr, cols, delta, static_cast<const __half*>(x), ldx, static_cast<__half*>(y), ldy, batch);
   OPC_CUDA(cudaGetLastError(), "opc_coo_gemv launch");

@@ -90,7 +90,7 @@ def forward64(model: dict, tokens) -> np.ndarray:
     """float64 logits after each token of `tokens` (a fresh sequence): [T][vocab]."""
     L = model["layers"]
     W = {k: dequantize_np(v).astype(np.float64) for k, v in L.items() if v["type"] in ("quantized", "sparse_outlier")}
-    vec = {k: v["data"].numpy().astype(np.float64) for k, v in L.items() if v["type"] == "fp16_passthrough"}
+    vec = {k: np.asarray(v["data"], dtype=np.float64).reshape(-1) for k, v in L.items() if v["type"] == "fp16_passthrough"}
     hd, H, KV, eps, theta = model["hd"], model["heads"], model["kv_heads"], model["eps"], model["theta"]
     tok = np.asarray(tokens)
     T = len(tok)
