@@ -22,8 +22,8 @@
  * (see opc_layer_plan below).  sub_vector_size 1 (2 bits/weight, 4 fp16 centroids per output
  * row) runs on every path; sub_vector_size 8 (true VQ: an index selects one of 4 fp16 vectors of
  * 8 per row, the reference quantizer's default) runs opc_gemv / opc_gemv_noalloc (any batch),
- * opc_gemm and opc_dequant, with K a multiple of 8; other sizes, and svs 8 on the decode chain,
- * return OPC_ERR_UNSUPPORTED.
+ * opc_gemm and opc_dequant, with K a multiple of 8, and the one-GPU decode chain with K a
+ * multiple of 1024; other sizes return OPC_ERR_UNSUPPORTED.
  */
 #ifndef OPC_B200_H
 #define OPC_B200_H
@@ -213,6 +213,11 @@ int opc_gemm(const opc_layer* layer, const void* x, int64_t ldx, void* y, int64_
  *                   pointer and leading dimension: only the later step's values are stored);
  *                   step 0's output may not overlap the chain input, later ones may
  * Requires batch 1..2, batch * K_pad <= 30720 for every step and fewer than 65535 steps.
+ * A sub_vector_size-8 step (K a multiple of 1024; one GPU, barrier form) runs through a view the
+ * chain builds and owns: the layer as sub_vector_size 1 over permuted columns (each 128-column unit
+ * holds element s of 128 vectors) with eight integer codebooks per row sharing one exponent, x
+ * staged in the same permuted order; the dot products are exact like svs 1's (not bit-equal to
+ * opc_gemv's svs-8 kernel, which accumulates in fp32).
  * opc_chain_create copies the step list to the device and allocates the chain's scratch (freed
  * by opc_chain_destroy); opc_chain_launch launches on `stream` (one kernel, nothing to clear;
  * capturable into a CUDA graph).  One chain must not run on two streams at once.  A launch

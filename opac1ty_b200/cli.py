@@ -208,7 +208,8 @@ def layer_bench(shape, outliers, batch, iters, svs, op):
 @click.option("--form", type=click.Choice(["auto", "barrier", "dataflow"]), default="auto",
               help="chain kernel form (see opac1ty_b200.chain.Chain)")
 @click.option("--trace", is_flag=True, help="also report the chain kernel's per-phase timeline (opc_chain_set_trace)")
-def decode_bench(model, blocks, batch, iters, launches, form, trace):
+@click.option("--svs", type=click.Choice(["1", "8"]), default="1", help="sub_vector_size of the synthetic weights")
+def decode_bench(model, blocks, batch, iters, launches, form, trace, svs):
     """Time the decode step (q|k|v, o, gate|up, down per block) of synthetic 2-bit weights."""
     import torch
 
@@ -218,7 +219,7 @@ def decode_bench(model, blocks, batch, iters, launches, form, trace):
     cfg = synthetic.LLAMA_8B if model == "8b" else synthetic.LLAMA_70B
     dev = torch.device("cuda", 0)
     st = decode.DecodeStack.synthetic(cfg, n_layers=blocks, device=dev, batch=batch, use_chain=not launches,
-                                      chain_form=form)
+                                      chain_form=form, sub_vector_size=int(svs))
     for _ in range(3):
         st.step_eager()
     torch.cuda.synchronize(dev)
@@ -231,7 +232,7 @@ def decode_bench(model, blocks, batch, iters, launches, form, trace):
     torch.cuda.synchronize(dev)
     ms = e0.elapsed_time(e1) / iters
     nb = st.algorithmic_bytes()
-    out = {"gpu": get_cuda_device_info().name, "model": model, "blocks": len(st.blocks), "batch": batch,
+    out = {"gpu": get_cuda_device_info().name, "model": model, "svs": int(svs), "blocks": len(st.blocks), "batch": batch,
            "chain": st.chain is not None, "kernel": st.kernel_name(), "ms_per_step": ms, "tok_s": batch * 1000.0 / ms,
            "gbs": nb / (ms * 1e-3) / 1e9}
     if trace and st.chain is not None:

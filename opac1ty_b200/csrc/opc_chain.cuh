@@ -65,6 +65,10 @@ struct ChainLayer {
   int32_t row_off, m_full;       // this rank's first row; rows of the full output
   int32_t write_y;               // 0: a later layer overwrites the fp16 output (not written)
   int32_t y_alias_x0;            // the fp16 output overlaps layer 0's input
+  // sub_vector_size 8 through the permuted svs-1 view (opc_layer.cuh, vq8_chain_*): x staged in
+  // the permuted column order, and unit u of a row tile decoded with codebook block u % 8
+  // (cbq + (u % 8) * cb_stride)
+  int32_t vq8, cb_stride, pad_[2];
 };
 
 // Per layer and CTA, the host-computed shares of its consumer warps, so the kernel does no integer
@@ -332,6 +336,17 @@ __device__ __forceinline__ void chain_store_digits(const uint4 v, float sc, uint
   for (int dd = 0; dd < 3; ++dd) sts64(col0 + dd * colb + pos, d.d[dd][0], d.d[dd][1]);
 }
 
+// The same for a sub_vector_size-8 layer's permuted view: the chunk is the 8-column group g, whose
+// value s goes to unit 8 (g / 128) + s, column g % 128 of that unit (opc_layer.cuh, vq8_chain_col).
+__device__ __forceinline__ void chain_store_digits_vq8(const uint4 v, float sc, uint32_t col0, uint32_t colb, int g) {
+  const XDigitsQ d = x_digits_q(v, sc);
+  const uint32_t base = static_cast<uint32_t>(8 * (g >> 7) * 128 + xs_pos8(g & 127));
+#pragma unroll
+  for (int dd = 0; dd < 3; ++dd)
+#pragma unroll
+    for (int s = 0; s < 8; ++s) sts8(col0 + dd * colb + base + s * 128, (d.d[dd][s >> 2] >> (8 * (s & 3))) & 0xffu);
+}
+
 constexpr int kChainSplitSlots = 32;  // packed tiles per CTA and layer (host-checked)
 
 struct ChainShared {
@@ -473,7 +488,9 @@ __device__ __forceinline__ void chain_finish_segment(ChainShared* sh, const Chai
 
 // kMulti: several ranks (system-scope stores into every rank's copies, cross-rank flags).  The
 // one-GPU instance compiles none of that, which keeps its code small.
-template <int kXC, bool kMulti>
+// kVq8: the instance for chains with sub_vector_size-8 layers (their permuted views); chains of
+// svs-1 layers run the instance without that code.
+template <int kXC, bool kMulti, bool kVq8 = false>
 __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs args) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int warp = __shfl_sync(0xffffffffu, static_cast<int>(threadIdx.x >> 5), 0);
@@ -823,8 +840,11 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
         const int c = tid + i * kQConsumerThreads;
         if (c < total) {
           const int b = c >= per_row ? 1 : 0, k = (c - b * per_row) * 8;
-          chain_store_digits(v[i], pow2f(b == 0 ? ex0 : ex1), xs_base + 3 * b * colb, colb,
-                             static_cast<uint32_t>((k >> 7) * 128 + xs_pos8(k & 127)));
+          if (kVq8 && L.vq8)
+            chain_store_digits_vq8(v[i], pow2f(b == 0 ? ex0 : ex1), xs_base + 3 * b * colb, colb, k >> 3);
+          else
+            chain_store_digits(v[i], pow2f(b == 0 ? ex0 : ex1), xs_base + 3 * b * colb, colb,
+                               static_cast<uint32_t>((k >> 7) * 128 + xs_pos8(k & 127)));
         }
       }
       if (tr && tid == 0) tr[5] = globaltimer_ns();
@@ -856,6 +876,9 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     if (u0 < u1) {
       AccQ A;
       zero_accq(A);
+      const bool vq8 = kVq8 && L.vq8 != 0;  // sub_vector_size-8 view: codebook block = unit % 8
+      const uint4* cbq8 = L.cbq;
+      const int64_t cb_stride = kVq8 ? L.cb_stride : 0;
       while (cc.u < u1) {
         if (!mbar_wait_bounded(fullw + slot * 8, phase)) {
           ok = false;
@@ -875,10 +898,16 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
             const uint4 b01 = lds128(xa), b23 = lds128(xa + 16);
             const uint32_t w[4] = {wv.x, wv.y, wv.z, wv.w};
             const uint32_t bb[8] = {b01.x, b01.y, b01.z, b01.w, b23.x, b23.y, b23.z, b23.w};
+            uint32_t qh[2] = {cur.qh[0], cur.qh[1]}, ql[2] = {cur.ql[0], cur.ql[1]};
+            if constexpr (kVq8) if (vq8) {
+              const uint4* cb = cbq8 + ((k0 + i) & 7) * cb_stride + cc.seg * kTileRows + g;
+              const uint4 c0 = ld_nc_v4(cb), c1 = ld_nc_v4(cb + 8);
+              qh[0] = c0.x; ql[0] = c0.y; qh[1] = c1.x; ql[1] = c1.y;
+            }
 #pragma unroll
             for (int jw = 0; jw < 4; ++jw) {
               uint32_t Ah[4], Al[4];
-              decode_word_q(w[jw], cur.qh, cur.ql, negz, Ah, Al);
+              decode_word_q(w[jw], qh, ql, negz, Ah, Al);
               imma16832(A.h[jw & 1], Ah, bb[2 * jw], bb[2 * jw + 1]);
               imma16832(A.l[jw & 1], Al, bb[2 * jw], bb[2 * jw + 1]);
             }

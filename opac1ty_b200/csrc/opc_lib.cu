@@ -1030,6 +1030,8 @@ struct opc_chain {
   int32_t nb0 = 0, nb1 = 0, s_total = 0;
   const opc::Chain2Layer* d_layers2 = nullptr;
   unsigned long long* d_s_all = nullptr;  // [2][s_total]
+  std::vector<void*> owned;             // permuted views of sub_vector_size-8 layers
+  bool vq8 = false;                     // runs the kernel instance with those views
 };
 
 namespace {
@@ -1159,8 +1161,95 @@ std::vector<int32_t> outlier_contributors(const opc::ChainLayer& c, const std::v
 
 // Builds a chain from every rank's view (ranks[rank] is this process's own).  With own_scratch
 // (one GPU) the flags and exchange words are allocated here and ranks[rank]'s pointers set.
+// The chain's view of a sub_vector_size-8 layer: the permuted svs-1 layer (opc_layer.cuh,
+// vq8_chain_*) with its eight integer codebooks; device buffers owned by the chain.
+struct Vq8View {
+  opc_layer L{};
+  uint4* cbq8 = nullptr;  // [8][M_pad]
+  std::vector<void*> owned;
+  void release() {
+    for (void* p : owned) cudaFree(p);
+    owned.clear();
+  }
+};
+
+int make_vq8_view(const char* fn, int j, const opc_layer* L8, Vq8View* v) {
+  const opc_layer_plan& p8 = L8->plan;
+  if (p8.K % 1024)
+    return fail(OPC_ERR_UNSUPPORTED, "%s: step %d: sub_vector_size 8 on the chain needs K a multiple of 1024 (K=%d)",
+                fn, j, p8.K);
+  const int slots = n_slots_of(p8);
+  std::vector<int32_t> orow(slots);
+  OPC_CUDA(cudaMemcpy(orow.data(), L8->outlier_rows, slots * sizeof(int32_t), cudaMemcpyDeviceToHost),
+           "vq8 view: outlier rows");
+  std::vector<int64_t> ids;
+  std::vector<int32_t> src;
+  for (int s = 0; s < slots; ++s)
+    if (orow[s] >= 0) {
+      ids.push_back(orow[s]);
+      src.push_back(s);
+    }
+  const int n = static_cast<int>(ids.size());
+  opc_layer_plan p1;
+  int rc = opc_plan_layer(p8.M, p8.K, n, 1, &p1);
+  if (rc != OPC_OK) return rc;
+  v->L.plan = p1;
+  auto alloc = [&](void** ptr, size_t bytes) -> int {
+    OPC_CUDA(cudaMalloc(ptr, std::max<size_t>(bytes, 16)), "vq8 view: cudaMalloc");
+    v->owned.push_back(*ptr);
+    return OPC_OK;
+  };
+  void* cbq8 = nullptr;
+  if ((rc = alloc(&v->L.units, p1.units_bytes)) || (rc = alloc(&v->L.codebooks, p1.codebook_bytes)) ||
+      (rc = alloc(&v->L.tile_mask, p1.tile_mask_bytes)) ||
+      (rc = alloc(reinterpret_cast<void**>(&v->L.outlier_rows), p1.outlier_rows_bytes)) ||
+      (rc = alloc(&cbq8, static_cast<size_t>(8) * p1.M_pad * sizeof(uint4))))
+    return rc;
+  v->cbq8 = static_cast<uint4*>(cbq8);
+  // temporaries: the permuted indices, a zero svs-1 codebook, the permuted outlier rows, slots
+  const size_t idx_bytes = static_cast<size_t>(p8.M) * p8.K, cb_bytes = static_cast<size_t>(p8.M) * 4 * 2;
+  const size_t ov_bytes = static_cast<size_t>(n) * p8.K * 2;
+  void* tmp = nullptr;
+  OPC_CUDA(cudaMalloc(&tmp, idx_bytes + cb_bytes + ov_bytes + static_cast<size_t>(std::max(n, 1)) * 4 + 256),
+           "vq8 view: temporaries");
+  uint8_t* idx1 = static_cast<uint8_t*>(tmp);
+  uint8_t* cb1 = idx1 + idx_bytes;
+  uint8_t* ov1 = cb1 + cb_bytes;
+  int32_t* src_d = reinterpret_cast<int32_t*>(align_up(reinterpret_cast<uintptr_t>(ov1 + ov_bytes), 16));
+  cudaError_t e = cudaMemset(cb1, 0, cb_bytes);
+  if (e == cudaSuccess && n) e = cudaMemcpy(src_d, src.data(), n * sizeof(int32_t), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) {
+    const int64_t total = static_cast<int64_t>(p8.M) * p8.K;
+    opc::vq8_chain_indices_kernel<<<static_cast<unsigned>(ceil_div(total, 256)), 256>>>(
+        p8.M, p8.K, p8.k_units, static_cast<const uint8_t*>(L8->units), idx1);
+    if (n)
+      opc::vq8_chain_outliers_kernel<<<n, 256>>>(
+          p8.K, p8.K_pad,
+          reinterpret_cast<const uint16_t*>(static_cast<const uint8_t*>(L8->units) + p8.packed_units * opc::kVq8UnitBytes),
+          src_d, reinterpret_cast<uint16_t*>(ov1));
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    cudaFree(tmp);
+    return cuda_fail(e, "vq8 view: permutation");
+  }
+  rc = opc_repack_layer(&v->L, cb1, idx1, n ? ov1 : nullptr, n ? ids.data() : nullptr, n, nullptr);
+  if (rc == OPC_OK) {
+    opc::vq8_chain_codebooks_kernel<<<static_cast<unsigned>(ceil_div(p1.M_pad, 128)), 128>>>(
+        p8.M, p1.M_pad, static_cast<const uint4*>(L8->codebooks), codebooks_q(&v->L),
+        static_cast<const uint16_t*>(v->L.tile_mask), v->cbq8);
+    e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) rc = cuda_fail(e, "vq8 view: codebooks");
+  }
+  cudaFree(tmp);
+  return rc;
+}
+
 int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t batch, int32_t rank, int32_t world,
-                std::vector<ChainRank>& ranks, bool own_scratch, opc_chain** out) {
+                std::vector<ChainRank>& ranks, bool own_scratch, opc_chain** out,
+                const std::vector<const uint4*>* vq8_cbq = nullptr) {
   int dev = 0;
   OPC_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
   DeviceCache dc;
@@ -1193,8 +1282,10 @@ int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t 
   const size_t smem = smem_for(stages);
   const int xc = bk_max <= 4 * 8 * opc::kQConsumerThreads ? 4 : 8;
   const bool multi = world > 1;
-  auto kern = xc == 4 ? (multi ? opc::chain_kernel<4, true> : opc::chain_kernel<4, false>)
-                      : (multi ? opc::chain_kernel<8, true> : opc::chain_kernel<8, false>);
+  const bool vq8 = vq8_cbq != nullptr;  // a chain with sub_vector_size-8 layers (one GPU)
+  if (vq8 && multi) return fail(OPC_ERR_UNSUPPORTED, "%s: sub_vector_size 8 runs on the one-GPU chain", fn);
+  auto kern = xc == 4 ? (multi ? opc::chain_kernel<4, true> : vq8 ? opc::chain_kernel<4, false, true> : opc::chain_kernel<4, false>)
+                      : (multi ? opc::chain_kernel<8, true> : vq8 ? opc::chain_kernel<8, false, true> : opc::chain_kernel<8, false>);
   OPC_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)),
            "cudaFuncSetAttribute(max dynamic smem, chain)");
   int per_sm = 0;
@@ -1282,6 +1373,11 @@ int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t 
     c.units = static_cast<const uint8_t*>(L->units);
     c.ounits = ounits_q(L);
     c.cbq = codebooks_q(L);
+    if (vq8_cbq && (*vq8_cbq)[j]) {  // a sub_vector_size-8 layer's permuted view
+      c.cbq = (*vq8_cbq)[j];
+      c.vq8 = 1;
+      c.cb_stride = p.M_pad;
+    }
     c.tile_mask = static_cast<const uint16_t*>(L->tile_mask);
     c.orow = L->outlier_rows;
     c.oexp = L->outlier_rows + n_slots_of(p);
@@ -1342,6 +1438,7 @@ int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t 
   ch->d_sync = me.sync;
   for (int q = 0; q < world; ++q) ch->sync_peer[q] = ranks[q].sync;
   ch->d_epoch = reinterpret_cast<unsigned int*>(base + epoch_off);
+  ch->vq8 = vq8;
   *out = ch;
   return OPC_OK;
 }
@@ -1639,7 +1736,30 @@ int opc_chain_create_ex(const opc_chain_step* steps, int32_t n_steps, int32_t ba
     me.M[j] = steps[j].layer->plan.M;
     me.y[j] = static_cast<char*>(steps[j].y);
   }
-  return chain_build("opc_chain_create", steps, n_steps, batch, 0, 1, ranks, true, out);
+  // sub_vector_size-8 steps run through their permuted svs-1 views (built here, owned by the chain)
+  std::vector<opc_chain_step> st(steps, steps + n_steps);
+  std::vector<Vq8View> views(n_steps);
+  std::vector<const uint4*> vq8_cbq(n_steps, nullptr);
+  bool any8 = false;
+  for (int j = 0; j < n_steps; ++j) {
+    if (steps[j].layer->plan.sub_vector_size != 8) continue;
+    any8 = true;
+    const int rc = make_vq8_view("opc_chain_create", j, steps[j].layer, &views[j]);
+    if (rc != OPC_OK) {
+      for (auto& v : views) v.release();
+      return rc;
+    }
+    st[j].layer = &views[j].L;
+    vq8_cbq[j] = views[j].cbq8;
+  }
+  const int rc = chain_build("opc_chain_create", st.data(), n_steps, batch, 0, 1, ranks, true, out,
+                             any8 ? &vq8_cbq : nullptr);
+  if (rc != OPC_OK) {
+    for (auto& v : views) v.release();
+    return rc;
+  }
+  for (auto& v : views) (*out)->owned.insert((*out)->owned.end(), v.owned.begin(), v.owned.end());
+  return OPC_OK;
 }
 
 int opc_chain_tp_scratch_bytes(const opc_chain_step* steps, int32_t n_steps, int32_t batch, int32_t world,
@@ -1850,9 +1970,11 @@ int opc_chain_launch(opc_chain* ch, void* stream_v) {
   const bool multi = a.world > 1;
   if (ch->xc == 4) {
     if (multi) OPC_CUDA(cudaLaunchKernelEx(&cfg, opc::chain_kernel<4, true>, a), "launch chain_kernel");
+    else if (ch->vq8) OPC_CUDA(cudaLaunchKernelEx(&cfg, opc::chain_kernel<4, false, true>, a), "launch chain_kernel");
     else OPC_CUDA(cudaLaunchKernelEx(&cfg, opc::chain_kernel<4, false>, a), "launch chain_kernel");
   } else {
     if (multi) OPC_CUDA(cudaLaunchKernelEx(&cfg, opc::chain_kernel<8, true>, a), "launch chain_kernel");
+    else if (ch->vq8) OPC_CUDA(cudaLaunchKernelEx(&cfg, opc::chain_kernel<8, false, true>, a), "launch chain_kernel");
     else OPC_CUDA(cudaLaunchKernelEx(&cfg, opc::chain_kernel<8, false>, a), "launch chain_kernel");
   }
   return OPC_OK;
@@ -1888,7 +2010,11 @@ int opc_chain_destroy(opc_chain* ch) {
   int prev = 0;
   cudaGetDevice(&prev);
   cudaSetDevice(ch->device);
-  const cudaError_t e = cudaFree(ch->dev_mem);
+  cudaError_t e = cudaFree(ch->dev_mem);
+  for (void* p : ch->owned) {
+    const cudaError_t e2 = cudaFree(p);
+    if (e == cudaSuccess) e = e2;
+  }
   cudaSetDevice(prev);
   delete ch;
   if (e != cudaSuccess) return cuda_fail(e, "cudaFree(chain)");

@@ -103,8 +103,9 @@ class DecodeStack:
     @classmethod
     def synthetic(cls, cfg: dict, n_layers: Optional[int] = None, device=None, batch: int = 1,
                   outlier_fraction: float = 0.01, seed: int = 0, use_chain: bool = True,
-                  chain_form: str = "auto") -> "DecodeStack":
-        """Random-initialised 2-bit weights with the given model shapes (synthetic.random_layer)."""
+                  chain_form: str = "auto", sub_vector_size: int = 1) -> "DecodeStack":
+        """Random-initialised 2-bit weights with the given model shapes (synthetic.random_layer;
+        sub_vector_size 8: synthetic.random_layer_vq8, generated on the host)."""
         shapes = synthetic.decoder_shapes(cfg)
         n_layers = cfg["layers"] if n_layers is None else n_layers
         device = L._as_cuda_device(device)
@@ -113,7 +114,10 @@ class DecodeStack:
             bd = {}
             for pi, (name, (M, K)) in enumerate(shapes.items()):
                 n_out = synthetic.n_outliers_for(M, outlier_fraction)
-                bd[name] = synthetic.random_layer_device(M, K, n_out, seed=seed + 1000 * li + pi, device=device)
+                if sub_vector_size == 8:
+                    bd[name] = synthetic.random_layer_vq8(M, K, n_out, seed=seed + 1000 * li + pi)
+                else:
+                    bd[name] = synthetic.random_layer_device(M, K, n_out, seed=seed + 1000 * li + pi, device=device)
             qkv = L.prepare_layer(concat_rows([bd["q_proj"], bd["k_proj"], bd["v_proj"]]), device, "qkv")
             o = L.prepare_layer(bd["o_proj"], device, "o_proj")
             gu = L.prepare_layer(concat_rows([bd["gate_proj"], bd["up_proj"]]), device, "gate_up")
@@ -163,6 +167,8 @@ class DecodeStack:
         """The kernel that runs the step."""
         if self.chain is not None:
             return "opc::chain2_kernel" if self.chain.form == "dataflow" else "opc::chain_kernel"
+        if self.blocks and self.blocks[0].qkv.sub_vector_size == 8:
+            return "opc::vq8_gemv_kernel"
         if self.batch > int(_lib.load().opc_gemm_crossover()):  # opc_gemv routes these to the GEMM
             return "opc::gemm_kernel"
         return "opc::gemvq_kernel" if self.batch <= 2 else "opc::gemv_kernel"
