@@ -323,6 +323,55 @@ def _chain_phases_dataflow(st) -> dict:
     return res
 
 
+@cli.command("engine-bench")
+@click.option("--model", type=click.Choice(["8b", "70b"]), default="8b")
+@click.option("--blocks", type=int, default=2, help="decoder blocks of the synthetic model")
+@click.option("--vocab", type=int, default=32000)
+@click.option("--prompt", type=int, default=64, help="prompt tokens (prefill) before the timed steps")
+@click.option("--steps", type=int, default=32, help="timed decode steps")
+@click.option("--svs", type=click.Choice(["1", "8"]), default="1")
+def engine_bench(model, blocks, vocab, prompt, steps, svs):  # noqa: D401
+    """Time the engine API (bf_engine_*) on a synthetic Llama-shaped .bf2: prefill and decode steps
+    with attention, norms and the lm_head (host-timed around each call, logits copied back)."""
+    import os
+    import tempfile
+
+    import torch
+
+    from . import synthetic
+    from .engine import Engine
+    from .utils import get_cuda_device_info
+
+    cfg = synthetic.LLAMA_8B if model == "8b" else synthetic.LLAMA_70B
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "model.bf2")
+        t0 = time.time()
+        synthetic.write_llama_bf2(path, cfg, blocks, vocab, sub_vector_size=int(svs))
+        t_write = time.time() - t0
+        t0 = time.time()
+        with Engine(path) as eng:
+            t_load = time.time() - t0
+            toks = list(range(1, prompt + 1))
+            eng.prefill(toks[:-1])
+            eng.forward_step(toks[-1])  # warm
+            eng.reset()
+            t0 = time.perf_counter()
+            eng.prefill(toks)
+            t_prefill = time.perf_counter() - t0
+            for i in range(3):
+                eng.forward_step(100 + i)
+            t0 = time.perf_counter()
+            for i in range(steps):
+                eng.forward_step(200 + i)
+            t_steps = (time.perf_counter() - t0) / steps
+            st = eng.stats()
+    click.echo(json.dumps({"gpu": get_cuda_device_info().name, "model": model, "svs": int(svs), "blocks": blocks,
+                           "vocab": vocab, "prompt_tokens": prompt, "prefill_ms": t_prefill * 1e3,
+                           "prefill_tok_s": prompt / t_prefill, "step_ms": t_steps * 1e3, "step_tok_s": 1.0 / t_steps,
+                           "kernel_dispatches_total": st["n_kernel_dispatches"], "device_bytes": st["peak_memory_bytes"],
+                           "write_s": round(t_write, 1), "load_s": round(t_load, 1)}))
+
+
 @cli.command("gemm-bench")
 @click.option("--shape", default="28672x4096", help="MxK")
 @click.option("--tokens", type=int, default=2048)

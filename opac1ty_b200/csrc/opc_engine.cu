@@ -273,12 +273,12 @@ __global__ void residual_kernel(float* __restrict__ h, int hidden, const __half*
 }
 
 // a[r][i] = fp16(silu(g) * u), silu(g) = g / (1 + exp(-g))
-__global__ void silu_mul_kernel(const __half* __restrict__ g, const __half* __restrict__ u, int n, int ld,
-                                __half* __restrict__ a) {
+__global__ void silu_mul_kernel(const __half* __restrict__ g, const __half* __restrict__ u, int ldg, int n,
+                                __half* __restrict__ a, int lda) {
   const int r = blockIdx.x;
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float gv = __half2float(g[static_cast<int64_t>(r) * ld + i]), uv = __half2float(u[static_cast<int64_t>(r) * ld + i]);
-    a[static_cast<int64_t>(r) * ld + i] = __float2half_rn(gv / (1.0f + expf(-gv)) * uv);
+    const float gv = __half2float(g[static_cast<int64_t>(r) * ldg + i]), uv = __half2float(u[static_cast<int64_t>(r) * ldg + i]);
+    a[static_cast<int64_t>(r) * lda + i] = __float2half_rn(gv / (1.0f + expf(-gv)) * uv);
   }
 }
 
@@ -301,6 +301,7 @@ struct DevLayer {
 
 struct Block {
   DevLayer q, k, v, o, gate, up, down;
+  DevLayer qkv, gu;               // q|k|v and gate|up as one layer each (rows stacked) when fusable
   const __half* ln_in = nullptr;    // device; NULL = ones
   const __half* ln_post = nullptr;
 };
@@ -327,8 +328,8 @@ struct BFEngine {
   // per-chunk scratch, kChunk rows each
   float* h = nullptr;
   __half *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *att = nullptr, *y = nullptr, *g = nullptr,
-         *u = nullptr, *a = nullptr, *logits16 = nullptr;
-  int ld_x = 0, ld_q = 0, ld_kv = 0, ld_i = 0, ld_y = 0;
+         *u = nullptr, *a = nullptr, *logits16 = nullptr, *qkv = nullptr, *gu = nullptr;
+  int ld_x = 0, ld_q = 0, ld_kv = 0, ld_i = 0, ld_y = 0, ld_qkv = 0, ld_gu = 0;
   void* ws = nullptr;
   size_t ws_bytes = 0;
   __half* host_logits = nullptr;  // pinned
@@ -478,6 +479,67 @@ int load_quantized(BFEngine* e, const MappedFile& f, const FileLayer& l, DevLaye
   return l.type == kSparse ? load_sparse_part(e, f, l, d) : 0;
 }
 
+// Several quantized layers with the same K and sub_vector_size as one layer, rows stacked in order
+// (q|k|v, gate|up): one GEMV launch instead of several.  Only plain quantized layers (no element
+// outliers) are fused.
+int load_stacked(BFEngine* e, const MappedFile& f, const std::vector<const FileLayer*>& parts, DevLayer* d) {
+  const FileLayer& l0 = *parts[0];
+  const int K = static_cast<int>(l0.in_f), svs = l0.svs;
+  int M = 0, n_out = 0;
+  for (const FileLayer* l : parts) {
+    if (l->type != kQuantized || l->in_f != l0.in_f || l->svs != l0.svs || l->entries != 4 || l->n_groups != l->out_f)
+      return fail(e, "layer '%s' cannot be stacked", l->name.c_str());
+    M += static_cast<int>(l->out_f);
+    n_out += l->n_out;
+  }
+  std::vector<uint8_t> cb, idx, ov;
+  std::vector<int64_t> ids;
+  int row0 = 0;
+  for (const FileLayer* l : parts) {
+    const int Mi = static_cast<int>(l->out_f);
+    const size_t cbb = static_cast<size_t>(Mi) * 4 * svs * 2, ib = static_cast<size_t>(Mi) * (K / svs);
+    const size_t ob = static_cast<size_t>(l->n_out) * K * 2;
+    const uint8_t* src = f.p + l->data;
+    cb.insert(cb.end(), src, src + cbb);
+    idx.insert(idx.end(), src + cbb, src + cbb + ib);
+    ov.insert(ov.end(), src + cbb + ib, src + cbb + ib + ob);
+    const uint8_t* id_src = src + cbb + ib + ob;
+    for (int i = 0; i < l->n_out; ++i)
+      ids.push_back(row0 + (l->id_bytes == 8 ? rd<int64_t>(id_src + 8 * i) : static_cast<int64_t>(rd<int32_t>(id_src + 4 * i))));
+    row0 += Mi;
+  }
+  const int32_t n_distinct = opc_count_distinct_ids(ids.empty() ? nullptr : ids.data(), n_out);
+  opc_layer_plan plan;
+  ENG_OPC(e, opc_plan_layer(M, K, n_distinct, svs, &plan));
+  d->L.plan = plan;
+  if (dalloc(e, &d->L.units, plan.units_bytes) || dalloc(e, &d->L.codebooks, plan.codebook_bytes) ||
+      dalloc(e, &d->L.tile_mask, plan.tile_mask_bytes) ||
+      dalloc(e, reinterpret_cast<void**>(&d->L.outlier_rows), plan.outlier_rows_bytes))
+    return -1;
+  void* tmp = nullptr;
+  ENG_CUDA(e, cudaMalloc(&tmp, cb.size() + idx.size() + ov.size()));
+  uint8_t* t = static_cast<uint8_t*>(tmp);
+  cudaError_t cr = cudaMemcpy(t, cb.data(), cb.size(), cudaMemcpyHostToDevice);
+  if (cr == cudaSuccess) cr = cudaMemcpy(t + cb.size(), idx.data(), idx.size(), cudaMemcpyHostToDevice);
+  if (cr == cudaSuccess && !ov.empty()) cr = cudaMemcpy(t + cb.size() + idx.size(), ov.data(), ov.size(), cudaMemcpyHostToDevice);
+  int rc = 0;
+  if (cr != cudaSuccess) rc = fail(e, "copying '%s' and the layers after it: %s", l0.name.c_str(), cudaGetErrorString(cr));
+  else if (opc_repack_layer(&d->L, t, t + cb.size(), n_out ? t + cb.size() + idx.size() : nullptr,
+                            n_out ? ids.data() : nullptr, n_out, e->stream) != OPC_OK)
+    rc = fail(e, "repacking '%s' stacked: %s", l0.name.c_str(), opc_last_error());
+  cudaStreamSynchronize(e->stream);
+  cudaFree(tmp);
+  if (rc) return rc;
+  d->present = true;
+  return 0;
+}
+
+bool stackable(const std::vector<const FileLayer*>& parts) {
+  for (const FileLayer* l : parts)
+    if (!l || l->type != kQuantized || l->svs != parts[0]->svs || l->in_f != parts[0]->in_f) return false;
+  return true;
+}
+
 // The element outliers of a kSparse layer: row-compressed on the host, then copied to the device.
 int load_sparse_part(BFEngine* e, const MappedFile& f, const FileLayer& l, DevLayer* d) {
   const int M = static_cast<int>(l.out_f), K = static_cast<int>(l.in_f);
@@ -611,13 +673,28 @@ int load_model(BFEngine* e, const char* path, uint32_t max_context) {
                 {"self_attn.v_proj.weight", &B.v, kvd, e->hidden},  {"self_attn.o_proj.weight", &B.o, e->hidden, qd},
                 {"mlp.gate_proj.weight", &B.gate, e->inter, e->hidden}, {"mlp.up_proj.weight", &B.up, e->inter, e->hidden},
                 {"mlp.down_proj.weight", &B.down, e->hidden, e->inter}};
+    std::vector<const FileLayer*> fl;
     for (auto& w : want) {
       const FileLayer* l = find(m, p + w.name);
       if (!l) return fail(e, "missing layer '%s%s'", p.c_str(), w.name);
       if (static_cast<int>(l->out_f) != w.M || static_cast<int>(l->in_f) != w.K)
         return fail(e, "'%s%s' is %ux%u, expected %dx%d", p.c_str(), w.name, l->out_f, l->in_f, w.M, w.K);
-      if (load_quantized(e, f, *l, w.d)) return -1;
+      fl.push_back(l);
     }
+    const std::vector<const FileLayer*> qkv = {fl[0], fl[1], fl[2]}, gu = {fl[4], fl[5]};
+    if (stackable(qkv)) {
+      if (load_stacked(e, f, qkv, &B.qkv)) return -1;
+    } else if (load_quantized(e, f, *fl[0], &B.q) || load_quantized(e, f, *fl[1], &B.k) ||
+               load_quantized(e, f, *fl[2], &B.v)) {
+      return -1;
+    }
+    if (load_quantized(e, f, *fl[3], &B.o)) return -1;
+    if (stackable(gu)) {
+      if (load_stacked(e, f, gu, &B.gu)) return -1;
+    } else if (load_quantized(e, f, *fl[4], &B.gate) || load_quantized(e, f, *fl[5], &B.up)) {
+      return -1;
+    }
+    if (load_quantized(e, f, *fl[6], &B.down)) return -1;
     if (load_vector(e, f, m, p + "input_layernorm.weight", e->hidden, &B.ln_in) ||
         load_vector(e, f, m, p + "post_attention_layernorm.weight", e->hidden, &B.ln_post))
       return -1;
@@ -657,11 +734,14 @@ int load_model(BFEngine* e, const char* path, uint32_t max_context) {
   e->ld_kv = pad8(kvd);
   e->ld_i = pad8(e->inter);
   e->ld_y = pad8(std::max(e->hidden, qd));
+  e->ld_qkv = pad8(qd + 2 * kvd);
+  e->ld_gu = pad8(2 * e->inter);
   struct {
     __half** p;
     int ld;
   } bufs[] = {{&e->xn, e->ld_x}, {&e->q, e->ld_q}, {&e->k, e->ld_kv}, {&e->v, e->ld_kv}, {&e->att, e->ld_q},
-              {&e->y, e->ld_y},  {&e->g, e->ld_i}, {&e->u, e->ld_i},   {&e->a, e->ld_i}};
+              {&e->y, e->ld_y},  {&e->g, e->ld_i}, {&e->u, e->ld_i},   {&e->a, e->ld_i},
+              {&e->qkv, e->ld_qkv}, {&e->gu, e->ld_gu}};
   for (auto& b : bufs) {
     void* p = nullptr;
     if (dalloc(e, &p, static_cast<size_t>(kChunk) * b.ld * 2)) return -1;
@@ -679,7 +759,8 @@ int load_model(BFEngine* e, const char* path, uint32_t max_context) {
   // one workspace for every projection and chunk size (calls are ordered on the engine's stream)
   std::vector<const DevLayer*> all;
   for (auto& B : e->blocks)
-    for (const DevLayer* d : {&B.q, &B.k, &B.v, &B.o, &B.gate, &B.up, &B.down}) all.push_back(d);
+    for (const DevLayer* d : {&B.q, &B.k, &B.v, &B.o, &B.gate, &B.up, &B.down, &B.qkv, &B.gu})
+      if (d->present) all.push_back(d);
   all.push_back(e->lm_from_embed ? &e->embed : &e->lm_head);
   for (const DevLayer* d : all)
     for (int b = 1; b <= static_cast<int>(kChunk); ++b)
@@ -718,23 +799,37 @@ int run_chunk(BFEngine* e, const int32_t* tokens, int n, float* logits) {
     __half* kc = e->kcache + static_cast<size_t>(l) * e->kv_heads * e->ctx * e->hd;
     __half* vc = e->vcache + static_cast<size_t>(l) * e->kv_heads * e->ctx * e->hd;
     rmsnorm_kernel<<<n, 256, 0, s>>>(e->h, e->hidden, B.ln_in, e->eps, e->xn, e->ld_x);
-    if (gemv(B.q, e->xn, e->ld_x, e->q, e->ld_q, n) || gemv(B.k, e->xn, e->ld_x, e->k, e->ld_kv, n) ||
-        gemv(B.v, e->xn, e->ld_x, e->v, e->ld_kv, n))
+    __half *qb = e->q, *kb = e->k, *vb = e->v;
+    int ldq = e->ld_q, ldkv = e->ld_kv;
+    if (B.qkv.present) {  // one GEMV for q|k|v
+      if (gemv(B.qkv, e->xn, e->ld_x, e->qkv, e->ld_qkv, n)) return -1;
+      qb = e->qkv;
+      kb = qb + qd;
+      vb = kb + e->kv_heads * e->hd;
+      ldq = ldkv = e->ld_qkv;
+    } else if (gemv(B.q, e->xn, e->ld_x, e->q, e->ld_q, n) || gemv(B.k, e->xn, e->ld_x, e->k, e->ld_kv, n) ||
+               gemv(B.v, e->xn, e->ld_x, e->v, e->ld_kv, n)) {
       return -1;
-    rope_cache_kernel<<<n, 256, 0, s>>>(e->q, e->ld_q, e->k, e->v, e->ld_kv, e->heads, e->kv_heads, e->hd, pos0,
-                                        e->cfg.rope_theta, kc, vc, static_cast<int>(e->ctx));
-    attention_kernel<<<dim3(e->heads, n), kAttnWarps * 32, 0, s>>>(e->q, e->ld_q, kc, vc, e->heads, e->kv_heads, e->hd,
+    }
+    rope_cache_kernel<<<n, 256, 0, s>>>(qb, ldq, kb, vb, ldkv, e->heads, e->kv_heads, e->hd, pos0, e->cfg.rope_theta, kc,
+                                        vc, static_cast<int>(e->ctx));
+    attention_kernel<<<dim3(e->heads, n), kAttnWarps * 32, 0, s>>>(qb, ldq, kc, vc, e->heads, e->kv_heads, e->hd,
                                                                    static_cast<int>(e->ctx), pos0, e->att, e->ld_q);
     if (gemv(B.o, e->att, e->ld_q, e->y, e->ld_y, n)) return -1;
     residual_kernel<<<n, 256, 0, s>>>(e->h, e->hidden, e->y, e->ld_y);
     rmsnorm_kernel<<<n, 256, 0, s>>>(e->h, e->hidden, B.ln_post, e->eps, e->xn, e->ld_x);
-    if (gemv(B.gate, e->xn, e->ld_x, e->g, e->ld_i, n) || gemv(B.up, e->xn, e->ld_x, e->u, e->ld_i, n)) return -1;
-    silu_mul_kernel<<<n, 256, 0, s>>>(e->g, e->u, e->inter, e->ld_i, e->a);
+    if (B.gu.present) {  // one GEMV for gate|up
+      if (gemv(B.gu, e->xn, e->ld_x, e->gu, e->ld_gu, n)) return -1;
+      silu_mul_kernel<<<n, 256, 0, s>>>(e->gu, e->gu + e->inter, e->ld_gu, e->inter, e->a, e->ld_i);
+    } else {
+      if (gemv(B.gate, e->xn, e->ld_x, e->g, e->ld_i, n) || gemv(B.up, e->xn, e->ld_x, e->u, e->ld_i, n)) return -1;
+      silu_mul_kernel<<<n, 256, 0, s>>>(e->g, e->u, e->ld_i, e->inter, e->a, e->ld_i);
+    }
     if (gemv(B.down, e->a, e->ld_i, e->y, e->ld_y, n)) return -1;
     residual_kernel<<<n, 256, 0, s>>>(e->h, e->hidden, e->y, e->ld_y);
-    launches += 6;
+    launches += 7;  // two RMSNorms, rotary + cache append, attention, two residual adds, SiLU gating
   }
-  (void)qd;
+
   if (logits) {
     rmsnorm_kernel<<<1, 256, 0, s>>>(e->h + static_cast<size_t>(n - 1) * e->hidden, e->hidden, e->final_norm, e->eps,
                                      e->xn, e->ld_x);

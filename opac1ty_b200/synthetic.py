@@ -162,3 +162,45 @@ def decoder_shapes(cfg: dict) -> dict:
         "q_proj": (h, h), "k_proj": (kv, h), "v_proj": (kv, h), "o_proj": (h, h),
         "gate_proj": (f, h), "up_proj": (f, h), "down_proj": (h, f),
     }
+
+
+def write_llama_bf2(path, cfg: dict, n_layers: int, vocab: int, seed: int = 0, sub_vector_size: int = 1,
+                    outlier_fraction: float = 0.01, heads: Optional[int] = None) -> dict:
+    """A synthetic Llama-style model with `cfg`'s shapes as a .bf2 file (Hugging Face tensor names,
+    random 2-bit layers with outlier rows, fp16 RMSNorm weights near 1); returns the model JSON."""
+    from .format import BF2Writer
+
+    h, f, kv = cfg["hidden"], cfg["intermediate"], cfg["kv"]
+    heads = heads or h // 128
+    make = random_layer_vq8 if sub_vector_size == 8 else random_layer
+    rng = rng_for(seed + 17)
+    layers = {}
+    n = [seed * 10000]
+
+    def q(M, K):
+        n[0] += 1
+        return make(M, K, n_outliers_for(M, outlier_fraction), n[0])
+
+    def norm():
+        return {"type": "fp16_passthrough", "shape": (h,),
+                "data": torch.from_numpy((1.0 + 0.05 * rng.standard_normal(h)).astype(np.float16))}
+
+    layers["model.embed_tokens.weight"] = q(vocab, h)
+    for i in range(n_layers):
+        p = f"model.layers.{i}."
+        layers[p + "input_layernorm.weight"] = norm()
+        layers[p + "self_attn.q_proj.weight"] = q(h, h)
+        layers[p + "self_attn.k_proj.weight"] = q(kv, h)
+        layers[p + "self_attn.v_proj.weight"] = q(kv, h)
+        layers[p + "self_attn.o_proj.weight"] = q(h, h)
+        layers[p + "post_attention_layernorm.weight"] = norm()
+        layers[p + "mlp.gate_proj.weight"] = q(f, h)
+        layers[p + "mlp.up_proj.weight"] = q(f, h)
+        layers[p + "mlp.down_proj.weight"] = q(h, f)
+    layers["model.norm.weight"] = norm()
+    layers["lm_head.weight"] = q(vocab, h)
+    model = {"architecture": "llama", "hidden_size": h, "intermediate_size": f, "num_hidden_layers": n_layers,
+             "vocab_size": vocab, "num_attention_heads": heads, "num_key_value_heads": kv // (h // heads),
+             "rope_theta": 500000.0, "rms_norm_eps": 1e-5}
+    BF2Writer(str(path)).write(layers, model, {"bits": 2, "sub_vector_size": sub_vector_size}, progress=False)
+    return model
