@@ -129,13 +129,13 @@ bool json_string(const std::string& js, const char* key, std::string* v) {
 // ------------------------------------------------------------------------------------------------
 // Kernels.  Rows are tokens of the current chunk; the residual stream h is fp32 [n][hidden].
 // ------------------------------------------------------------------------------------------------
-struct ChunkTokens {
-  int32_t t[kChunk];
-};
-
-__global__ void embed_kernel(const __half* __restrict__ table, int hidden, ChunkTokens tok, float* __restrict__ h) {
+// The chunk's tokens and first position live in device memory ([kChunk] tokens, then the position),
+// copied from pinned host memory at the start of every chunk, so that a captured decode step
+// (CUDA graph) replays with new values.
+__global__ void embed_kernel(const __half* __restrict__ table, int hidden, const int32_t* __restrict__ tokpos,
+                             float* __restrict__ h) {
   const int r = blockIdx.x;
-  const __half* src = table + static_cast<int64_t>(tok.t[r]) * hidden;
+  const __half* src = table + static_cast<int64_t>(tokpos[r]) * hidden;
   for (int i = threadIdx.x; i < hidden; i += blockDim.x) h[static_cast<int64_t>(r) * hidden + i] = __half2float(src[i]);
 }
 
@@ -172,10 +172,11 @@ __global__ void rmsnorm_kernel(const float* __restrict__ h, int hidden, const __
 // pos * theta^(-2i/hd)) on q in place and on k, then k and v appended to the layer's cache
 // [kv_heads][ctx][hd] at position pos0 + r.
 __global__ void rope_cache_kernel(__half* __restrict__ q, int ldq, const __half* __restrict__ k,
-                                  const __half* __restrict__ v, int ldkv, int heads, int kv_heads, int hd, int pos0,
-                                  float theta, __half* __restrict__ kc, __half* __restrict__ vc, int ctx) {
+                                  const __half* __restrict__ v, int ldkv, int heads, int kv_heads, int hd,
+                                  const int32_t* __restrict__ pos0p, float theta, __half* __restrict__ kc,
+                                  __half* __restrict__ vc, int ctx) {
   const int r = blockIdx.x;
-  const int pos = pos0 + r;
+  const int pos = *pos0p + r;
   const int half = hd / 2;
   const int nq = heads * half, nk = kv_heads * half;
   for (int i = threadIdx.x; i < nq + nk; i += blockDim.x) {
@@ -209,7 +210,8 @@ __global__ void rope_cache_kernel(__half* __restrict__ q, int ldq, const __half*
 __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(const __half* __restrict__ q, int ldq,
                                                                     const __half* __restrict__ kc,
                                                                     const __half* __restrict__ vc, int heads,
-                                                                    int kv_heads, int hd, int ctx, int pos0,
+                                                                    int kv_heads, int hd, int ctx,
+                                                                    const int32_t* __restrict__ pos0p,
                                                                     __half* __restrict__ out, int ldo) {
   constexpr int kMaxE = kMaxHeadDim / 32;
   __shared__ float sm_m[kAttnWarps], sm_s[kAttnWarps], sm_acc[kAttnWarps][kMaxHeadDim];
@@ -217,7 +219,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(const __half
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int E = hd / 32;
   const int kvh = head / (heads / kv_heads);
-  const int L = pos0 + r + 1;
+  const int L = *pos0p + r + 1;
   const float scale = rsqrtf(static_cast<float>(hd));
   float qv[kMaxE], acc[kMaxE];
 #pragma unroll
@@ -333,6 +335,12 @@ struct BFEngine {
   void* ws = nullptr;
   size_t ws_bytes = 0;
   __half* host_logits = nullptr;  // pinned
+  int32_t* d_tokpos = nullptr;    // [kChunk] tokens, then the chunk's first position
+  int32_t* h_tokpos = nullptr;    // pinned mirror
+  cudaGraphExec_t step_exec = nullptr;  // the captured one-token step (tokens and position from d_tokpos)
+  bool graph_tried = false;
+  uint32_t step_launches = 0;
+  uint32_t direct_steps = 0;  // one-token steps launched directly (the first one sets up the kernels)
   std::vector<void*> allocs;
   size_t dev_bytes = 0;
   std::vector<int32_t> history;   // tokens in the cache (repetition penalty)
@@ -755,6 +763,10 @@ int load_model(BFEngine* e, const char* path, uint32_t max_context) {
   if (dalloc(e, &lp, static_cast<size_t>(e->vocab) * 2)) return -1;
   e->logits16 = static_cast<__half*>(lp);
   ENG_CUDA(e, cudaMallocHost(reinterpret_cast<void**>(&e->host_logits), static_cast<size_t>(e->vocab) * 2));
+  ENG_CUDA(e, cudaMallocHost(reinterpret_cast<void**>(&e->h_tokpos), (kChunk + 1) * sizeof(int32_t)));
+  void* tp = nullptr;
+  if (dalloc(e, &tp, (kChunk + 1) * sizeof(int32_t))) return -1;
+  e->d_tokpos = static_cast<int32_t*>(tp);
 
   // one workspace for every projection and chunk size (calls are ordered on the engine's stream)
   std::vector<const DevLayer*> all;
@@ -774,11 +786,12 @@ int load_model(BFEngine* e, const char* path, uint32_t max_context) {
 
 // Append n (<= kChunk) tokens at positions pos.. and, with `logits`, write the last one's
 // next-token logits (fp32, vocab values) to the host.
-int run_chunk(BFEngine* e, const int32_t* tokens, int n, float* logits) {
+// Every launch of a chunk of n tokens, stream-ordered and asynchronous (no host synchronisation),
+// reading the tokens and the first position from d_tokpos; with want_logits the last token's
+// next-token logits are copied to host_logits.
+int enqueue_chunk(BFEngine* e, int n, bool want_logits, uint32_t* n_launches) {
   cudaStream_t s = e->stream;
-  ChunkTokens tk;
-  for (int i = 0; i < n; ++i) tk.t[i] = tokens[i];
-  const int pos0 = static_cast<int>(e->pos);
+  const int32_t* pos0 = e->d_tokpos + kChunk;
   const int qd = e->heads * e->hd;
   uint32_t launches = 0;
   auto gemv = [&](const DevLayer& d, const __half* x, int ldx, __half* y, int ldy, int rows) -> int {
@@ -792,7 +805,8 @@ int run_chunk(BFEngine* e, const int32_t* tokens, int n, float* logits) {
     }
     return 0;
   };
-  embed_kernel<<<n, 256, 0, s>>>(e->embed_table, e->hidden, tk, e->h);
+  ENG_CUDA(e, cudaMemcpyAsync(e->d_tokpos, e->h_tokpos, (kChunk + 1) * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+  embed_kernel<<<n, 256, 0, s>>>(e->embed_table, e->hidden, e->d_tokpos, e->h);
   ++launches;
   for (int l = 0; l < e->n_layers; ++l) {
     const Block& B = e->blocks[l];
@@ -811,8 +825,8 @@ int run_chunk(BFEngine* e, const int32_t* tokens, int n, float* logits) {
                gemv(B.v, e->xn, e->ld_x, e->v, e->ld_kv, n)) {
       return -1;
     }
-    rope_cache_kernel<<<n, 256, 0, s>>>(qb, ldq, kb, vb, ldkv, e->heads, e->kv_heads, e->hd, pos0, e->cfg.rope_theta, kc,
-                                        vc, static_cast<int>(e->ctx));
+    rope_cache_kernel<<<n, 256, 0, s>>>(qb, ldq, kb, vb, ldkv, e->heads, e->kv_heads, e->hd, pos0, e->cfg.rope_theta,
+                                        kc, vc, static_cast<int>(e->ctx));
     attention_kernel<<<dim3(e->heads, n), kAttnWarps * 32, 0, s>>>(qb, ldq, kc, vc, e->heads, e->kv_heads, e->hd,
                                                                    static_cast<int>(e->ctx), pos0, e->att, e->ld_q);
     if (gemv(B.o, e->att, e->ld_q, e->y, e->ld_y, n)) return -1;
@@ -830,7 +844,7 @@ int run_chunk(BFEngine* e, const int32_t* tokens, int n, float* logits) {
     launches += 7;  // two RMSNorms, rotary + cache append, attention, two residual adds, SiLU gating
   }
 
-  if (logits) {
+  if (want_logits) {
     rmsnorm_kernel<<<1, 256, 0, s>>>(e->h + static_cast<size_t>(n - 1) * e->hidden, e->hidden, e->final_norm, e->eps,
                                      e->xn, e->ld_x);
     ++launches;
@@ -839,6 +853,46 @@ int run_chunk(BFEngine* e, const int32_t* tokens, int n, float* logits) {
                                 cudaMemcpyDeviceToHost, s));
   }
   ENG_CUDA(e, cudaGetLastError());
+  *n_launches = launches;
+  return 0;
+}
+
+// Capture the one-token step with logits into a CUDA graph (once); on any failure the engine
+// keeps launching directly.
+void capture_step(BFEngine* e) {
+  e->graph_tried = true;
+  cudaGraph_t g = nullptr;
+  if (cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+    cudaGetLastError();
+    return;
+  }
+  const std::string saved = e->error;
+  uint32_t launches = 0;
+  const int rc = enqueue_chunk(e, 1, true, &launches);
+  const cudaError_t ce = cudaStreamEndCapture(e->stream, &g);
+  if (rc == 0 && ce == cudaSuccess && g && cudaGraphInstantiate(&e->step_exec, g, 0) == cudaSuccess) {
+    e->step_launches = launches;
+  } else {
+    e->step_exec = nullptr;
+    e->error = saved;
+  }
+  if (g) cudaGraphDestroy(g);
+  cudaGetLastError();
+}
+
+int run_chunk(BFEngine* e, const int32_t* tokens, int n, float* logits) {
+  cudaStream_t s = e->stream;
+  for (int i = 0; i < n; ++i) e->h_tokpos[i] = tokens[i];
+  e->h_tokpos[kChunk] = static_cast<int32_t>(e->pos);
+  uint32_t launches = 0;
+  if (n == 1 && logits && !e->graph_tried && e->direct_steps > 0) capture_step(e);
+  if (n == 1 && logits && e->step_exec) {
+    ENG_CUDA(e, cudaGraphLaunch(e->step_exec, s));
+    launches = e->step_launches;
+  } else {
+    if (enqueue_chunk(e, n, logits != nullptr, &launches)) return -1;
+    if (n == 1 && logits) ++e->direct_steps;
+  }
   ENG_CUDA(e, cudaStreamSynchronize(s));
   int32_t derr = 0;
   if (opc_take_device_error(e->device, &derr) != OPC_OK || derr != 0)
@@ -934,6 +988,8 @@ BFEngine* bf_engine_create_ex(const char* path, int32_t device, uint32_t max_con
     e->allocs.clear();
     if (e->host_logits) cudaFreeHost(e->host_logits);
     e->host_logits = nullptr;
+    if (e->h_tokpos) cudaFreeHost(e->h_tokpos);
+    e->h_tokpos = nullptr;
     if (e->stream) cudaStreamDestroy(e->stream);
     e->stream = nullptr;
     e->blocks.clear();
@@ -950,8 +1006,10 @@ void bf_engine_destroy(BFEngine* e) {
   if (!e->allocs.empty() || e->stream) {
     cudaSetDevice(e->device);
     if (e->stream) cudaStreamSynchronize(e->stream);
+    if (e->step_exec) cudaGraphExecDestroy(e->step_exec);
     for (void* p : e->allocs) cudaFree(p);
     if (e->host_logits) cudaFreeHost(e->host_logits);
+    if (e->h_tokpos) cudaFreeHost(e->h_tokpos);
     if (e->stream) cudaStreamDestroy(e->stream);
   }
   delete e;
