@@ -213,10 +213,9 @@ int opc_gemm(const opc_layer* layer, const void* x, int64_t ldx, void* y, int64_
  *                   pointer and leading dimension: only the later step's values are stored);
  *                   step 0's output may not overlap the chain input, later ones may
  * Requires batch 1..2, batch * K_pad <= 30720 for every step and fewer than 65535 steps.
- * A sub_vector_size-8 step (K a multiple of 1024; one GPU, barrier form) runs through a view the
- * chain builds and owns: the layer as sub_vector_size 1 over permuted columns (each 128-column unit
- * holds element s of 128 vectors) with eight integer codebooks per row sharing one exponent, x
- * staged in the same permuted order; the dot products are exact like svs 1's (not bit-equal to
+ * A sub_vector_size-8 step (K a multiple of 1024; one GPU, barrier form) streams the layer's own
+ * index units; the chain builds and owns the integer forms of its codebook vectors (one exponent
+ * per row) and of its outlier rows.  Its dot products are exact like svs 1's (not bit-equal to
  * opc_gemv's svs-8 kernel, which accumulates in fp32).
  * opc_chain_create copies the step list to the device and allocates the chain's scratch (freed
  * by opc_chain_destroy); opc_chain_launch launches on `stream` (one kernel, nothing to clear;

@@ -55,7 +55,7 @@ struct ChainLayer {
   const __half* x;               // layer 0: the chain input (fp16)
   const uint32_t* xw;            // layer >= 1: the previous layer's exchange words (this rank's copy)
   unsigned long long* acc;       // [OT*16][2] outlier-slot dot products, count-carrying (zero between launches)
-  const void* unused_;           // keeps the descriptor a whole number of 16-byte pieces
+  const uint4* cbv;              // sub_vector_size 8: [M_pad][4] integer vectors {hi[8], lo[8]}
   const int32_t* onc;            // [OT] warps contributing to each outlier tile
   __half* y_peer[kMaxRanks];     // this rank's first row in rank p's fp16 copy of the full output
   uint32_t* yw_peer[kMaxRanks];  // this rank's first row in rank p's exchange words of it
@@ -65,9 +65,9 @@ struct ChainLayer {
   int32_t row_off, m_full;       // this rank's first row; rows of the full output
   int32_t write_y;               // 0: a later layer overwrites the fp16 output (not written)
   int32_t y_alias_x0;            // the fp16 output overlaps layer 0's input
-  // sub_vector_size 8 through the permuted svs-1 view (opc_layer.cuh, vq8_chain_*): x staged in
-  // the permuted column order, and unit u of a row tile decoded with codebook block u % 8
-  // (cbq + (u % 8) * cb_stride)
+  // sub_vector_size 8 (opc_layer.cuh, vq8_chain_vectors_kernel): units are 512-byte groups of four
+  // 128-byte index units (16 rows x 1024 columns), decoded through the vector codebooks cbv;
+  // cb_stride = the 128-column blocks of the staged x (KT counts 1024-column units then)
   int32_t vq8, cb_stride, pad_[2];
 };
 
@@ -336,15 +336,20 @@ __device__ __forceinline__ void chain_store_digits(const uint4 v, float sc, uint
   for (int dd = 0; dd < 3; ++dd) sts64(col0 + dd * colb + pos, d.d[dd][0], d.d[dd][1]);
 }
 
-// The same for a sub_vector_size-8 layer's permuted view: the chunk is the 8-column group g, whose
-// value s goes to unit 8 (g / 128) + s, column g % 128 of that unit (opc_layer.cuh, vq8_chain_col).
-__device__ __forceinline__ void chain_store_digits_vq8(const uint4 v, float sc, uint32_t col0, uint32_t colb, int g) {
-  const XDigitsQ d = x_digits_q(v, sc);
-  const uint32_t base = static_cast<uint32_t>(8 * (g >> 7) * 128 + xs_pos8(g & 127));
-#pragma unroll
-  for (int dd = 0; dd < 3; ++dd)
-#pragma unroll
-    for (int s = 0; s < 8; ++s) sts8(col0 + dd * colb + base + s * 128, (d.d[dd][s >> 2] >> (8 * (s & 3))) & 0xffu);
+// sub_vector_size 8: per consumer warp two 1 KB slices of shared memory (current and next row
+// tile's vector codebooks, 16 rows x 64 bytes), filled with cp.async.
+constexpr int kChainVq8SliceBytes = kQConsumers * 2048 + 16;
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+// Row tile seg's vector codebooks (1 KB) into slice dst: 32 bytes per lane.
+__device__ __forceinline__ void chain_vq8_slice(uint32_t dst, const uint4* cbv, int32_t seg, int lane) {
+  const uint4* src = cbv + static_cast<int64_t>(seg) * kTileRows * 4 + 2 * lane;
+  cp_async16(dst + 32 * lane, src);
+  cp_async16(dst + 32 * lane + 16, src + 1);
+  cp_async_commit();
 }
 
 constexpr int kChainSplitSlots = 32;  // packed tiles per CTA and layer (host-checked)
@@ -488,7 +493,7 @@ __device__ __forceinline__ void chain_finish_segment(ChainShared* sh, const Chai
 
 // kMulti: several ranks (system-scope stores into every rank's copies, cross-rank flags).  The
 // one-GPU instance compiles none of that, which keeps its code small.
-// kVq8: the instance for chains with sub_vector_size-8 layers (their permuted views); chains of
+// kVq8: the instance for chains with sub_vector_size-8 layers (their own index units); chains of
 // svs-1 layers run the instance without that code.
 template <int kXC, bool kMulti, bool kVq8 = false>
 __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs args) {
@@ -504,6 +509,8 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
   const uint32_t full_base = ring_base + kQConsumers * S * kQChunkBytes;
   const uint32_t empty_base = full_base + kQConsumers * S * 8;
   ChainShared* sh = reinterpret_cast<ChainShared*>(smem + args.xs_bytes + kQConsumers * S * (kQChunkBytes + 16));
+  // sub_vector_size 8: this consumer warp's two codebook slices (after the shared state)
+  const uint32_t cbs_warp = ((smem_u32(sh) + static_cast<uint32_t>(sizeof(ChainShared)) + 15u) & ~15u) + warp * 2048u;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kQConsumers * S; ++i) {
@@ -705,6 +712,15 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
       cur = chain_load_meta(qa, cc.seg, g);
       nxt = chain_load_meta(qa, min(cc.seg + 1, L.MT + L.OT - 1), g);
     }
+    int cbuf = 0;  // sub_vector_size 8: the slice holding the current row tile's codebooks
+    if constexpr (kVq8) {
+      if (L.vq8 && u0 < u1) {
+        cp_async_wait_all();  // copies a previous layer left in flight land before the slices are reused
+        __syncwarp();
+        if (cc.seg < L.MT) chain_vq8_slice(cbs_warp, L.cbv, cc.seg, lane);
+        if (cc.seg + 1 < L.MT) chain_vq8_slice(cbs_warp + 1024, L.cbv, cc.seg + 1, lane);
+      }
+    }
     // contributors (packed warps of this CTA) of the first and the last packed tile of this warp's
     // range -- the only ones it may share -- counted while x is not complete yet
     int need_first = 0, need_last = 0;
@@ -834,17 +850,14 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
         // past this barrier, their next writers (layer j+1) behind the staged barrier below
         if (tid < kQMaxBatch) sh->amax_bits[(j + 1) & 1][tid] = 0u;
       }
-      const uint32_t colb = static_cast<uint32_t>(xsq_col_bytes(L.KT));
+      const uint32_t colb = static_cast<uint32_t>(xsq_col_bytes(kVq8 && L.vq8 ? L.cb_stride : L.KT));
 #pragma unroll
       for (int i = 0; i < kXC; ++i) {
         const int c = tid + i * kQConsumerThreads;
         if (c < total) {
           const int b = c >= per_row ? 1 : 0, k = (c - b * per_row) * 8;
-          if (kVq8 && L.vq8)
-            chain_store_digits_vq8(v[i], pow2f(b == 0 ? ex0 : ex1), xs_base + 3 * b * colb, colb, k >> 3);
-          else
-            chain_store_digits(v[i], pow2f(b == 0 ? ex0 : ex1), xs_base + 3 * b * colb, colb,
-                               static_cast<uint32_t>((k >> 7) * 128 + xs_pos8(k & 127)));
+          chain_store_digits(v[i], pow2f(b == 0 ? ex0 : ex1), xs_base + 3 * b * colb, colb,
+                             static_cast<uint32_t>((k >> 7) * 128 + xs_pos8(k & 127)));
         }
       }
       if (tr && tid == 0) tr[5] = globaltimer_ns();
@@ -868,7 +881,7 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     // ---- this warp's units of layer j
     const int bcol = g >> 2, dig = g & 3;
     const bool live_col = dig < 3 && bcol < B;
-    const uint32_t colbase = live_col ? xs_base + (3 * bcol + dig) * xsq_col_bytes(L.KT)
+    const uint32_t colbase = live_col ? xs_base + (3 * bcol + dig) * xsq_col_bytes(kVq8 && L.vq8 ? L.cb_stride : L.KT)
                                       : xs_base + args.xs_bytes - (bcol < B ? kQZeroBytes + kQOnesBytes : kQZeroBytes);
     const uint32_t kts = live_col ? 128u : 0u;
     const uint32_t xq = colbase + 32 * q, xo = colbase + 4 * q;
@@ -876,9 +889,11 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
     if (u0 < u1) {
       AccQ A;
       zero_accq(A);
-      const bool vq8 = kVq8 && L.vq8 != 0;  // sub_vector_size-8 view: codebook block = unit % 8
-      const uint4* cbq8 = L.cbq;
-      const int64_t cb_stride = kVq8 ? L.cb_stride : 0;
+      const bool vq8 = kVq8 && L.vq8 != 0;
+      if (vq8) {  // the first row tile's slice has landed
+        cp_async_wait_all();
+        __syncwarp();
+      }
       while (cc.u < u1) {
         if (!mbar_wait_bounded(fullw + slot * 8, phase)) {
           ok = false;
@@ -887,7 +902,40 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
         const int32_t cnt = chain_chunk(cc, u1);
         const uint32_t stage = ring + slot * kQChunkBytes;
         const int32_t k0 = cc.u - cc.begin;
-        if (cc.seg < L.MT) {
+        if (kVq8 && vq8 && cc.seg < L.MT) {
+          // sub_vector_size 8: unit = four 128-byte index units of 256 columns; lane (g, q) reads
+          // the 16 bytes of row pair g of each (byte b = k16 step b: bits 2w / 4+2w the vector of
+          // the step's 8-column group w for rows g / g+8), and for the 32 columns of step jw of a
+          // 128-column half the vector of its group 4jw+q: one 16-byte slice load per row gives the
+          // hi and lo parts of both vector halves (A-fragment registers k 4q.. and 16+4q..)
+          const uint32_t ub = stage - lane * 16 + g * 16;
+          const uint32_t cbs = cbs_warp + cbuf * 1024;
+#pragma unroll 1
+          for (int i = 0; i < cnt; ++i) {
+#pragma unroll 1
+            for (int v = 0; v < 4; ++v) {
+              const uint4 ib = lds128(ub + i * kUnitBytes + v * 128);
+              const uint32_t iw[4] = {ib.x, ib.y, ib.z, ib.w};
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const uint32_t xa = xq + static_cast<uint32_t>(8 * (k0 + i) + 2 * v + h) * kts;
+                const uint4 b01 = lds128(xa), b23 = lds128(xa + 16);
+                const uint32_t bb[8] = {b01.x, b01.y, b01.z, b01.w, b23.x, b23.y, b23.z, b23.w};
+#pragma unroll
+                for (int jw = 0; jw < 4; ++jw) {
+                  const int bi = 2 * jw + (q >> 1);
+                  const uint32_t byte = iw[2 * h + (bi >> 2)] >> (8 * (bi & 3));
+                  const uint32_t sft = 2 * (q & 1);
+                  const uint32_t i0 = (byte >> sft) & 3u, i1 = (byte >> (4 + sft)) & 3u;
+                  const uint4 c0 = lds128(cbs + (g * 4 + i0) * 16), c1 = lds128(cbs + ((g + 8) * 4 + i1) * 16);
+                  const uint32_t Ah[4] = {c0.x, c1.x, c0.y, c1.y}, Al[4] = {c0.z, c1.z, c0.w, c1.w};
+                  imma16832(A.h[jw & 1], Ah, bb[2 * jw], bb[2 * jw + 1]);
+                  imma16832(A.l[jw & 1], Al, bb[2 * jw], bb[2 * jw + 1]);
+                }
+              }
+            }
+          }
+        } else if (cc.seg < L.MT) {
           // not unrolled: one unit carries enough independent work for the ALU and tensor pipes
           // (unrolling 2-8 units measured no faster), and the small loop keeps the kernel's code
           // -- which every layer re-fetches -- small
@@ -898,16 +946,10 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
             const uint4 b01 = lds128(xa), b23 = lds128(xa + 16);
             const uint32_t w[4] = {wv.x, wv.y, wv.z, wv.w};
             const uint32_t bb[8] = {b01.x, b01.y, b01.z, b01.w, b23.x, b23.y, b23.z, b23.w};
-            uint32_t qh[2] = {cur.qh[0], cur.qh[1]}, ql[2] = {cur.ql[0], cur.ql[1]};
-            if constexpr (kVq8) if (vq8) {
-              const uint4* cb = cbq8 + ((k0 + i) & 7) * cb_stride + cc.seg * kTileRows + g;
-              const uint4 c0 = ld_nc_v4(cb), c1 = ld_nc_v4(cb + 8);
-              qh[0] = c0.x; ql[0] = c0.y; qh[1] = c1.x; ql[1] = c1.y;
-            }
 #pragma unroll
             for (int jw = 0; jw < 4; ++jw) {
               uint32_t Ah[4], Al[4];
-              decode_word_q(w[jw], qh, ql, negz, Ah, Al);
+              decode_word_q(w[jw], cur.qh, cur.ql, negz, Ah, Al);
               imma16832(A.h[jw & 1], Ah, bb[2 * jw], bb[2 * jw + 1]);
               imma16832(A.l[jw & 1], Al, bb[2 * jw], bb[2 * jw + 1]);
             }
@@ -948,6 +990,14 @@ __global__ void __launch_bounds__(kQThreads, 1) chain_kernel(const ChainArgs arg
           chain_next_segment(L, cc);
           cur = nxt;
           if (cc.seg + 1 < L.MT + L.OT) nxt = chain_load_meta(qa, cc.seg + 1, g);
+          if constexpr (kVq8) {
+            if (vq8 && cc.seg < L.MT) {  // the next tile's slice (issued a segment ago) lands; refill the other
+              cbuf ^= 1;
+              cp_async_wait_all();
+              __syncwarp();
+              if (cc.seg + 1 < L.MT) chain_vq8_slice(cbs_warp + (cbuf ^ 1) * 1024, L.cbv, cc.seg + 1, lane);
+            }
+          }
         }
       }
       if (!ok) {

@@ -243,58 +243,28 @@ __global__ void dequant_kernel(LayerGeom G, const uint8_t* __restrict__ units, c
 }
 
 // ------------------------------------------------------------------------------------------------
-// sub_vector_size 8 on the decode chain.  W[r][8g + s] = cb[r][idx[r][g]][s]: for a fixed s the
-// columns {8g + s} form a sub_vector_size-1 layer with the per-row codebook cb[r][.][s] and the
-// indices idx[r][g].  The chain therefore runs an svs-8 layer through its 2-bit unit layout with
-// the columns permuted so that each 128-column unit holds one s: unit u' of a row tile covers
-// column s = u' % 8 of the 128 groups g = 128 (u' / 8) .. + 127, and the unit's codebook is block
-// s of eight integer codebooks per row sharing one exponent (the largest of the row's 32 values).
-// The staged x is permuted the same way, so the integer dot product is the same sum.
+// sub_vector_size 8 on the decode chain.  The chain streams the layer's own 128-byte index units
+// (four of them, 16 rows x 1024 columns, per 512-byte chain unit) and multiplies integer forms
+// of the selected codebook vectors with its staged x digits (int8 mma.sync, exact int64 sums like
+// svs 1).  Per row the four 8-element vectors become integers n = round(v * 2^e) with one
+// exponent e for all 32 values (int_exponent of the largest), stored as 64 bytes: for vector c,
+// 16 bytes {hi[0..7], lo[0..7]} (n = 256 hi + lo), so that one 16-byte load gives the A-fragment
+// registers of both vector halves for both parts.  Outlier and padding rows are zero, and cbq
+// gets {0, 0, e, 0} per row for the chain's row metadata.  One thread per row.
 // ------------------------------------------------------------------------------------------------
-// Original column of permuted column kp (K a multiple of 1024).
-__host__ __device__ __forceinline__ int vq8_chain_col(int kp) {
-  const int u = kp >> 7;
-  return 8 * (128 * (u >> 3) + (kp & 127)) + (u & 7);
-}
-
-// indices of the permuted svs-1 view, [M][K] uint8, from the svs-8 units (opc_vq8.cuh layout:
-// 128-byte unit per 16-row tile and 256 columns; row pair g's 16 bytes, byte b = the k16 step b:
-// bits 2w / 4+2w the index of group 2b+w of rows g / g+8).  One thread per output byte.
-__global__ void vq8_chain_indices_kernel(int32_t M, int32_t K, int32_t KB8, const uint8_t* __restrict__ units8,
-                                         uint8_t* __restrict__ idx1) {
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= static_cast<int64_t>(M) * K) return;
-  const int r = static_cast<int>(i / K), kp = static_cast<int>(i - static_cast<int64_t>(r) * K);
-  const int g = vq8_chain_col(kp) >> 3;
-  const int t = r >> 4, gr = r & 15, gb = g & 31;
-  const uint8_t byte = units8[(static_cast<int64_t>(t) * KB8 + (g >> 5)) * 128 + (gr & 7) * 16 + (gb >> 1)];
-  idx1[i] = static_cast<uint8_t>((byte >> (4 * (gr >> 3) + 2 * (gb & 1))) & 3u);
-}
-
-// outlier rows of the permuted view, [n][K] fp16, from the svs-8 layer's row-major copy
-// [slots][K_pad8]: row i is slot src_slot[i].  One block per row.
-__global__ void vq8_chain_outliers_kernel(int32_t K, int32_t K_pad8, const uint16_t* __restrict__ orows8,
-                                          const int32_t* __restrict__ src_slot, uint16_t* __restrict__ ov1) {
-  const int i = blockIdx.x;
-  const uint16_t* src = orows8 + static_cast<int64_t>(src_slot[i]) * K_pad8;
-  for (int kp = threadIdx.x; kp < K; kp += blockDim.x) ov1[static_cast<int64_t>(i) * K + kp] = src[vq8_chain_col(kp)];
-}
-
-// The eight integer codebooks [8][M_pad] {4 x int8 hi, 4 x int8 lo, e, 0} of the permuted view
-// from the svs-8 codebook words (opc_vq8.cuh: lane 4g+q of tile t holds, for rows g and g+8,
-// elements 2q, 2q+1 of vectors 0..3).  Outlier and padding rows copy the view's own entry
-// ({0, 0, e, slot} or zero) into every block.
-__global__ void vq8_chain_codebooks_kernel(int32_t M, int32_t M_pad, const uint4* __restrict__ cb8,
-                                           const uint4* __restrict__ cbq1, const uint16_t* __restrict__ tile_mask,
-                                           uint4* __restrict__ cbq8) {
+__global__ void vq8_chain_vectors_kernel(int32_t M, int32_t M_pad, const uint4* __restrict__ cb8,
+                                         const uint16_t* __restrict__ tile_mask, uint4* __restrict__ cbv,
+                                         uint4* __restrict__ cbq) {
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= M_pad) return;
   const bool outlier = (tile_mask[r / kTileRows] >> (r % kTileRows)) & 1u;
   if (r >= M || outlier) {
-    const uint4 v = cbq1[r];
-    for (int s = 0; s < 8; ++s) cbq8[static_cast<int64_t>(s) * M_pad + r] = v;
+    for (int c = 0; c < 4; ++c) cbv[static_cast<int64_t>(r) * 4 + c] = make_uint4(0u, 0u, 0u, 0u);
+    cbq[r] = make_uint4(0u, 0u, 0u, 0u);
     return;
   }
+  // opc_vq8.cuh layout: lane 4g+q of tile t holds, for rows g (first uint4) and g+8 (second),
+  // elements 2q, 2q+1 of vectors 0..3 (one 32-bit word per vector)
   const int t = r >> 4, gr = r & 15, g = gr & 7, h = gr >> 3;
   float f[4][8];
   float amax = 0.f;
@@ -311,17 +281,18 @@ __global__ void vq8_chain_codebooks_kernel(int32_t M, int32_t M_pad, const uint4
   }
   const int e = int_exponent(amax);
 #pragma unroll
-  for (int s = 0; s < 8; ++s) {
-    uint4 vq = make_uint4(0u, 0u, static_cast<uint32_t>(e), 0u);
+  for (int c = 0; c < 4; ++c) {
+    uint32_t hw[2] = {0u, 0u}, lw[2] = {0u, 0u};
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
+    for (int s = 0; s < 8; ++s) {
       int hi, lo;
       int_parts(f[c][s], e, &hi, &lo);
-      vq.x |= (static_cast<uint32_t>(hi) & 0xffu) << (8 * c);
-      vq.y |= (static_cast<uint32_t>(lo) & 0xffu) << (8 * c);
+      hw[s >> 2] |= (static_cast<uint32_t>(hi) & 0xffu) << (8 * (s & 3));
+      lw[s >> 2] |= (static_cast<uint32_t>(lo) & 0xffu) << (8 * (s & 3));
     }
-    cbq8[static_cast<int64_t>(s) * M_pad + r] = vq;
+    cbv[static_cast<int64_t>(r) * 4 + c] = make_uint4(hw[0], hw[1], lw[0], lw[1]);
   }
+  cbq[r] = make_uint4(0u, 0u, static_cast<uint32_t>(e), 0u);
 }
 
 }  // namespace opc

@@ -1030,7 +1030,7 @@ struct opc_chain {
   int32_t nb0 = 0, nb1 = 0, s_total = 0;
   const opc::Chain2Layer* d_layers2 = nullptr;
   unsigned long long* d_s_all = nullptr;  // [2][s_total]
-  std::vector<void*> owned;             // permuted views of sub_vector_size-8 layers
+  std::vector<void*> owned;             // codebook and outlier forms of sub_vector_size-8 layers
   bool vq8 = false;                     // runs the kernel instance with those views
 };
 
@@ -1062,12 +1062,15 @@ bool fp16_ranges_overlap(const void* a, int64_t lda, int64_t na, const void* b, 
 }
 
 // One rank's steps against the kernel's limits; m_full[j] = rows of step j's full output.
+struct Vq8View;
 int check_chain_steps(const char* fn, const opc_chain_step* steps, int32_t n, int32_t batch, const DeviceCache& dc,
-                      const std::vector<int32_t>& m_full) {
+                      const std::vector<int32_t>& m_full, const std::vector<const Vq8View*>* views8 = nullptr) {
   if (n > opc::kChainMaxLayers) return fail(OPC_ERR_UNSUPPORTED, "%s: %d steps (at most %d)", fn, n, opc::kChainMaxLayers);
   for (int j = 0; j < n; ++j) {
     const opc_chain_step& st = steps[j];
-    if (!st.layer || !plan_ok(&st.layer->plan)) return fail(OPC_ERR_INVALID, "%s: step %d: invalid layer", fn, j);
+    const bool view = views8 && (*views8)[j];  // an svs-8 layer's chain view (its plan was checked as svs 8)
+    if (!st.layer || (!view && !plan_ok(&st.layer->plan)))
+      return fail(OPC_ERR_INVALID, "%s: step %d: invalid layer", fn, j);
     if (st.layer->plan.sub_vector_size != 1)
       return fail(OPC_ERR_UNSUPPORTED, "%s: step %d: sub_vector_size %d (the chain runs svs = 1)", fn, j,
                   st.layer->plan.sub_vector_size);
@@ -1161,11 +1164,18 @@ std::vector<int32_t> outlier_contributors(const opc::ChainLayer& c, const std::v
 
 // Builds a chain from every rank's view (ranks[rank] is this process's own).  With own_scratch
 // (one GPU) the flags and exchange words are allocated here and ranks[rank]'s pointers set.
-// The chain's view of a sub_vector_size-8 layer: the permuted svs-1 layer (opc_layer.cuh,
-// vq8_chain_*) with its eight integer codebooks; device buffers owned by the chain.
+// What the chain needs of a sub_vector_size-8 layer besides its own index units (streamed as is,
+// four 128-byte units per 512-byte chain unit): the integer vector codebooks and row metadata
+// (opc_layer.cuh, vq8_chain_vectors_kernel), and its outlier rows as the integer outlier units of
+// the svs-1 kernels, taken from an svs-1 layer holding just those rows.  `L` describes the
+// geometry the chain streams (units per row tile = K / 1024); its buffers are the svs-8 layer's
+// except the ones below.  Device buffers owned by the chain.
 struct Vq8View {
   opc_layer L{};
-  uint4* cbq8 = nullptr;  // [8][M_pad]
+  uint4* cbq = nullptr;       // [M_pad] {0, 0, e, 0}
+  uint4* cbv = nullptr;       // [M_pad][4] {hi[8], lo[8]} per vector
+  const uint8_t* ounits = nullptr;
+  int32_t* orow = nullptr;    // [slots] output row of each outlier slot, then [slots] exponents
   std::vector<void*> owned;
   void release() {
     for (void* p : owned) cudaFree(p);
@@ -1175,81 +1185,85 @@ struct Vq8View {
 
 int make_vq8_view(const char* fn, int j, const opc_layer* L8, Vq8View* v) {
   const opc_layer_plan& p8 = L8->plan;
-  if (p8.K % 1024)
+  if (p8.K % 1024 || p8.K_pad != p8.K)
     return fail(OPC_ERR_UNSUPPORTED, "%s: step %d: sub_vector_size 8 on the chain needs K a multiple of 1024 (K=%d)",
                 fn, j, p8.K);
   const int slots = n_slots_of(p8);
   std::vector<int32_t> orow(slots);
   OPC_CUDA(cudaMemcpy(orow.data(), L8->outlier_rows, slots * sizeof(int32_t), cudaMemcpyDeviceToHost),
            "vq8 view: outlier rows");
-  std::vector<int64_t> ids;
-  std::vector<int32_t> src;
-  for (int s = 0; s < slots; ++s)
-    if (orow[s] >= 0) {
-      ids.push_back(orow[s]);
-      src.push_back(s);
-    }
-  const int n = static_cast<int>(ids.size());
-  opc_layer_plan p1;
-  int rc = opc_plan_layer(p8.M, p8.K, n, 1, &p1);
-  if (rc != OPC_OK) return rc;
-  v->L.plan = p1;
+  int n = 0;  // valid slots come first (slots follow the sorted row ids)
+  while (n < slots && orow[n] >= 0) ++n;
+  for (int s = n; s < slots; ++s)
+    if (orow[s] >= 0) return fail(OPC_ERR_INVALID, "%s: step %d: outlier slots not in order", fn, j);
   auto alloc = [&](void** ptr, size_t bytes) -> int {
     OPC_CUDA(cudaMalloc(ptr, std::max<size_t>(bytes, 16)), "vq8 view: cudaMalloc");
     v->owned.push_back(*ptr);
     return OPC_OK;
   };
-  void* cbq8 = nullptr;
-  if ((rc = alloc(&v->L.units, p1.units_bytes)) || (rc = alloc(&v->L.codebooks, p1.codebook_bytes)) ||
-      (rc = alloc(&v->L.tile_mask, p1.tile_mask_bytes)) ||
-      (rc = alloc(reinterpret_cast<void**>(&v->L.outlier_rows), p1.outlier_rows_bytes)) ||
-      (rc = alloc(&cbq8, static_cast<size_t>(8) * p1.M_pad * sizeof(uint4))))
+  void *cbq = nullptr, *cbv = nullptr, *orw = nullptr;
+  int rc;
+  if ((rc = alloc(&cbq, static_cast<size_t>(p8.M_pad) * sizeof(uint4))) ||
+      (rc = alloc(&cbv, static_cast<size_t>(p8.M_pad) * 4 * sizeof(uint4))) ||
+      (rc = alloc(&orw, static_cast<size_t>(2 * slots) * sizeof(int32_t))))
     return rc;
-  v->cbq8 = static_cast<uint4*>(cbq8);
-  // temporaries: the permuted indices, a zero svs-1 codebook, the permuted outlier rows, slots
-  const size_t idx_bytes = static_cast<size_t>(p8.M) * p8.K, cb_bytes = static_cast<size_t>(p8.M) * 4 * 2;
-  const size_t ov_bytes = static_cast<size_t>(n) * p8.K * 2;
-  void* tmp = nullptr;
-  OPC_CUDA(cudaMalloc(&tmp, idx_bytes + cb_bytes + ov_bytes + static_cast<size_t>(std::max(n, 1)) * 4 + 256),
-           "vq8 view: temporaries");
-  uint8_t* idx1 = static_cast<uint8_t*>(tmp);
-  uint8_t* cb1 = idx1 + idx_bytes;
-  uint8_t* ov1 = cb1 + cb_bytes;
-  int32_t* src_d = reinterpret_cast<int32_t*>(align_up(reinterpret_cast<uintptr_t>(ov1 + ov_bytes), 16));
-  cudaError_t e = cudaMemset(cb1, 0, cb_bytes);
-  if (e == cudaSuccess && n) e = cudaMemcpy(src_d, src.data(), n * sizeof(int32_t), cudaMemcpyHostToDevice);
-  if (e == cudaSuccess) {
-    const int64_t total = static_cast<int64_t>(p8.M) * p8.K;
-    opc::vq8_chain_indices_kernel<<<static_cast<unsigned>(ceil_div(total, 256)), 256>>>(
-        p8.M, p8.K, p8.k_units, static_cast<const uint8_t*>(L8->units), idx1);
-    if (n)
-      opc::vq8_chain_outliers_kernel<<<n, 256>>>(
-          p8.K, p8.K_pad,
-          reinterpret_cast<const uint16_t*>(static_cast<const uint8_t*>(L8->units) + p8.packed_units * opc::kVq8UnitBytes),
-          src_d, reinterpret_cast<uint16_t*>(ov1));
-    e = cudaGetLastError();
-  }
-  if (e == cudaSuccess) e = cudaDeviceSynchronize();
-  if (e != cudaSuccess) {
+  v->cbq = static_cast<uint4*>(cbq);
+  v->cbv = static_cast<uint4*>(cbv);
+  v->orow = static_cast<int32_t*>(orw);
+  opc::vq8_chain_vectors_kernel<<<static_cast<unsigned>(ceil_div(p8.M_pad, 128)), 128>>>(
+      p8.M, p8.M_pad, static_cast<const uint4*>(L8->codebooks), static_cast<const uint16_t*>(L8->tile_mask), v->cbv,
+      v->cbq);
+  OPC_CUDA(cudaGetLastError(), "vq8 view: vectors");
+  OPC_CUDA(cudaMemcpy(v->orow, L8->outlier_rows, slots * sizeof(int32_t), cudaMemcpyDeviceToDevice), "vq8 view: rows");
+  // outlier rows [n][K] fp16 (row-major, first in the svs-8 layer's copy since K_pad == K) as an
+  // svs-1 layer whose rows are all outliers: its outlier units and slot exponents are the chain's
+  if (n > 0) {
+    opc_layer mini{};
+    std::vector<int64_t> ids(n);
+    for (int s = 0; s < n; ++s) ids[s] = s;
+    if ((rc = opc_plan_layer(n, p8.K, n, 1, &mini.plan)) != OPC_OK) return rc;
+    if (n_slots_of(mini.plan) != slots) return fail(OPC_ERR_INVALID, "%s: step %d: outlier slot count", fn, j);
+    if ((rc = alloc(&mini.units, mini.plan.units_bytes)) || (rc = alloc(&mini.codebooks, mini.plan.codebook_bytes)) ||
+        (rc = alloc(&mini.tile_mask, mini.plan.tile_mask_bytes)) ||
+        (rc = alloc(reinterpret_cast<void**>(&mini.outlier_rows), mini.plan.outlier_rows_bytes)))
+      return rc;
+    void* tmp = nullptr;
+    const size_t zb = static_cast<size_t>(n) * 4 * 2 + static_cast<size_t>(n) * p8.K;
+    OPC_CUDA(cudaMalloc(&tmp, zb), "vq8 view: temporaries");
+    cudaError_t e = cudaMemset(tmp, 0, zb);
+    const uint8_t* rows8 = static_cast<const uint8_t*>(L8->units) + p8.packed_units * opc::kVq8UnitBytes;
+    if (e == cudaSuccess)
+      rc = opc_repack_layer(&mini, tmp, static_cast<uint8_t*>(tmp) + static_cast<size_t>(n) * 8, rows8, ids.data(), n,
+                            nullptr);
+    if (e == cudaSuccess && rc == OPC_OK)  // the exponents of the slots
+      e = cudaMemcpy(v->orow + slots, mini.outlier_rows + slots, slots * sizeof(int32_t), cudaMemcpyDeviceToDevice);
     cudaFree(tmp);
-    return cuda_fail(e, "vq8 view: permutation");
+    if (e != cudaSuccess) return cuda_fail(e, "vq8 view: outlier units");
+    if (rc != OPC_OK) return rc;
+    v->ounits = ounits_q(&mini);
+  } else {
+    OPC_CUDA(cudaMemset(v->orow + slots, 0, slots * sizeof(int32_t)), "vq8 view: exponents");
+    v->ounits = static_cast<const uint8_t*>(L8->units);  // never read (no outlier units)
   }
-  rc = opc_repack_layer(&v->L, cb1, idx1, n ? ov1 : nullptr, n ? ids.data() : nullptr, n, nullptr);
-  if (rc == OPC_OK) {
-    opc::vq8_chain_codebooks_kernel<<<static_cast<unsigned>(ceil_div(p1.M_pad, 128)), 128>>>(
-        p8.M, p1.M_pad, static_cast<const uint4*>(L8->codebooks), codebooks_q(&v->L),
-        static_cast<const uint16_t*>(v->L.tile_mask), v->cbq8);
-    e = cudaGetLastError();
-    if (e == cudaSuccess) e = cudaDeviceSynchronize();
-    if (e != cudaSuccess) rc = cuda_fail(e, "vq8 view: codebooks");
-  }
-  cudaFree(tmp);
-  return rc;
+  OPC_CUDA(cudaDeviceSynchronize(), "vq8 view");
+  // the geometry the chain streams: K/1024 chain units per row tile, the outlier units above
+  opc_layer_plan q = p8;
+  q.sub_vector_size = 1;
+  q.k_units = p8.K / 1024;
+  q.outlier_k_units = p8.K / 16;
+  q.packed_units = static_cast<int64_t>(p8.row_tiles) * q.k_units;
+  q.total_units = q.packed_units + static_cast<int64_t>(p8.outlier_tiles) * q.outlier_k_units;
+  v->L.plan = q;
+  v->L.units = L8->units;
+  v->L.codebooks = v->cbq;
+  v->L.tile_mask = L8->tile_mask;
+  v->L.outlier_rows = v->orow;
+  return OPC_OK;
 }
 
 int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t batch, int32_t rank, int32_t world,
                 std::vector<ChainRank>& ranks, bool own_scratch, opc_chain** out,
-                const std::vector<const uint4*>* vq8_cbq = nullptr) {
+                const std::vector<const Vq8View*>* views8 = nullptr) {
   int dev = 0;
   OPC_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
   DeviceCache dc;
@@ -1261,20 +1275,22 @@ int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t 
       if (p < rank) row_off[j] += ranks[p].M[j];
       m_full[j] += ranks[p].M[j];
     }
-  rc = check_chain_steps(fn, steps, n, batch, dc, m_full);
+  rc = check_chain_steps(fn, steps, n, batch, dc, m_full, views8);
   if (rc != OPC_OK) return rc;
 
-  int32_t kt_max = 1;
+  auto view8 = [&](int j) -> const Vq8View* { return views8 ? (*views8)[j] : nullptr; };
+  int32_t kt_max = 1;  // 128-column blocks of the staged x
   int64_t bk_max = 0;
   for (int j = 0; j < n; ++j) {
-    kt_max = std::max(kt_max, steps[j].layer->plan.k_units);
+    kt_max = std::max(kt_max, view8(j) ? steps[j].layer->plan.K / 128 : steps[j].layer->plan.k_units);
     bk_max = std::max<int64_t>(bk_max, static_cast<int64_t>(batch) * steps[j].layer->plan.K_pad);
   }
   const int xs = static_cast<int>(align_up(static_cast<size_t>(3 * batch) * opc::xsq_col_bytes(kt_max) +
                                           opc::kQZeroBytes + opc::kQOnesBytes, 128));
+  const bool vq8 = views8 != nullptr;  // a chain with sub_vector_size-8 layers (one GPU)
   auto smem_for = [&](int stages) {
     return static_cast<size_t>(xs) + static_cast<size_t>(opc::kQConsumers) * stages * (opc::kQChunkBytes + 16) +
-           sizeof(opc::ChainShared);
+           sizeof(opc::ChainShared) + (vq8 ? opc::kChainVq8SliceBytes : 0);
   };
   int stages = opc::kQMaxStages;
   while (stages >= 2 && smem_for(stages) > static_cast<size_t>(dc.max_smem_optin)) --stages;
@@ -1282,7 +1298,6 @@ int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t 
   const size_t smem = smem_for(stages);
   const int xc = bk_max <= 4 * 8 * opc::kQConsumerThreads ? 4 : 8;
   const bool multi = world > 1;
-  const bool vq8 = vq8_cbq != nullptr;  // a chain with sub_vector_size-8 layers (one GPU)
   if (vq8 && multi) return fail(OPC_ERR_UNSUPPORTED, "%s: sub_vector_size 8 runs on the one-GPU chain", fn);
   auto kern = xc == 4 ? (multi ? opc::chain_kernel<4, true> : vq8 ? opc::chain_kernel<4, false, true> : opc::chain_kernel<4, false>)
                       : (multi ? opc::chain_kernel<8, true> : vq8 ? opc::chain_kernel<8, false, true> : opc::chain_kernel<8, false>);
@@ -1373,10 +1388,12 @@ int chain_build(const char* fn, const opc_chain_step* steps, int32_t n, int32_t 
     c.units = static_cast<const uint8_t*>(L->units);
     c.ounits = ounits_q(L);
     c.cbq = codebooks_q(L);
-    if (vq8_cbq && (*vq8_cbq)[j]) {  // a sub_vector_size-8 layer's permuted view
-      c.cbq = (*vq8_cbq)[j];
+    if (const Vq8View* v = view8(j)) {  // a sub_vector_size-8 layer: its own units, these codebooks
+      c.cbq = v->cbq;
+      c.cbv = v->cbv;
+      c.ounits = v->ounits;
       c.vq8 = 1;
-      c.cb_stride = p.M_pad;
+      c.cb_stride = p.K / 128;  // 128-column blocks of the staged x (p.k_units counts 1024-column units)
     }
     c.tile_mask = static_cast<const uint16_t*>(L->tile_mask);
     c.orow = L->outlier_rows;
@@ -1736,10 +1753,10 @@ int opc_chain_create_ex(const opc_chain_step* steps, int32_t n_steps, int32_t ba
     me.M[j] = steps[j].layer->plan.M;
     me.y[j] = static_cast<char*>(steps[j].y);
   }
-  // sub_vector_size-8 steps run through their permuted svs-1 views (built here, owned by the chain)
+  // sub_vector_size-8 steps: their codebook and outlier forms for the chain (built here, owned by it)
   std::vector<opc_chain_step> st(steps, steps + n_steps);
   std::vector<Vq8View> views(n_steps);
-  std::vector<const uint4*> vq8_cbq(n_steps, nullptr);
+  std::vector<const Vq8View*> views8(n_steps, nullptr);
   bool any8 = false;
   for (int j = 0; j < n_steps; ++j) {
     if (steps[j].layer->plan.sub_vector_size != 8) continue;
@@ -1750,10 +1767,10 @@ int opc_chain_create_ex(const opc_chain_step* steps, int32_t n_steps, int32_t ba
       return rc;
     }
     st[j].layer = &views[j].L;
-    vq8_cbq[j] = views[j].cbq8;
+    views8[j] = &views[j];
   }
   const int rc = chain_build("opc_chain_create", st.data(), n_steps, batch, 0, 1, ranks, true, out,
-                             any8 ? &vq8_cbq : nullptr);
+                             any8 ? &views8 : nullptr);
   if (rc != OPC_OK) {
     for (auto& v : views) v.release();
     return rc;

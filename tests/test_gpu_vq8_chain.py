@@ -1,8 +1,9 @@
-"""sub_vector_size 8 on the decode chain (one GPU, barrier form): each svs-8 layer runs through its
-permuted svs-1 view (eight integer codebooks per row, x staged in the permuted column order), so
-the step is the same exact integer dot product as for svs 1.  Checked against the oracle's fp64
-chain, against per-GEMV svs-8 launches (fp32 accumulation: within tolerance, not bit-equal), and on
-the reference quantizer's own svs-8 layer (tests/golden/dequant_svs8.npz) tiled to K = 1024."""
+"""sub_vector_size 8 on the decode chain (one GPU, barrier form): the chain streams each svs-8
+layer's own index units and multiplies integer forms of the selected codebook vectors (one
+exponent per row) with its staged x digits, so the step is an exact integer dot product like
+svs 1's.  Checked against the oracle's fp64 chain, against per-GEMV svs-8 launches (fp32
+accumulation: within tolerance, not bit-equal), and on the reference quantizer's own svs-8 layer
+(tests/golden/dequant_svs8.npz) tiled to K = 1024."""
 
 from pathlib import Path
 
