@@ -16,12 +16,13 @@
  *                       allocates the KV cache.
  *   forward / prefill / forward_step
  *                       per block: RMSNorm, q/k/v projections (opc_gemv: the integer GEMV for
- *                       one token, the fp16 GEMV or the tcgen05 GEMM for a prompt chunk), rotary
- *                       embedding, K/V appended to the cache, causal grouped-query attention,
- *                       o projection + residual, RMSNorm, gate/up projections, SiLU(gate) * up,
- *                       down projection + residual; then the final RMSNorm and the lm_head GEMV
- *                       (the embedding when the file has no lm_head).  Prompts run in chunks of
- *                       up to 64 tokens.  Residual stream fp32, GEMV inputs and outputs fp16.
+ *                       one token, the fp16 GEMV or the tcgen05 GEMM up to 64 tokens; opc_gemm
+ *                       for longer prompt chunks), rotary embedding, K/V appended to the cache,
+ *                       causal grouped-query attention, o projection + residual, RMSNorm,
+ *                       gate/up projections, SiLU(gate) * up, down projection + residual; then
+ *                       the final RMSNorm and the lm_head GEMV (the embedding when the file has
+ *                       no lm_head).  Prompts run in chunks of up to 512 tokens.  Residual stream
+ *                       fp32, GEMV inputs and outputs fp16.
  *   generate            byte-level stub tokenizer as in the reference (each prompt byte is a
  *                       token id, tokens < 256 print as that byte), prefill, then decode steps
  *                       with greedy / temperature / top-k / top-p sampling.

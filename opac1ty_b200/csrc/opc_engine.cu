@@ -31,9 +31,16 @@ extern "C" const BFSamplingParams BF_DEFAULT_SAMPLING = {1.0f, 0.0f, 0, 1.0f, 0u
 
 namespace {
 
-constexpr uint32_t kChunk = 64;          // tokens per prompt chunk (opc_gemv's largest batch)
+constexpr uint32_t kChunk = 512;         // tokens per prompt chunk
+constexpr int kGemvMaxBatch = 64;        // opc_gemv's largest batch; larger chunks call opc_gemm
 constexpr uint32_t kDefaultContext = 4096;
-constexpr int kAttnWarps = 4;
+constexpr int kAttnThreads = 128;        // attention_kernel: threads per CTA
+constexpr int kAttnTile = 256;           // attention_kernel: positions per tile
+constexpr int kAttnSplits = 16;          // attention_kernel: at most this many context ranges per (head, token)
+constexpr int kAttnMinCtas = 512;        // attention_kernel: CTAs a launch should have when the context allows
+constexpr int kNormThreads = 512;        // add_rmsnorm_kernel: one CTA per token
+constexpr int kNormPer = 16;             // values per thread held in registers (rows up to 8192)
+constexpr int kRopeSplit = 4;            // rope_cache_kernel: CTAs per token
 constexpr int kMaxHeadDim = 256;
 
 // ------------------------------------------------------------------------------------------------
@@ -129,11 +136,38 @@ bool json_string(const std::string& js, const char* key, std::string* v) {
 // ------------------------------------------------------------------------------------------------
 // Kernels.  Rows are tokens of the current chunk; the residual stream h is fp32 [n][hidden].
 // ------------------------------------------------------------------------------------------------
+// Programmatic dependent launch: the kernels below (but the first of a chunk) are launched with
+// programmatic stream serialization (launch_pdl), so each may be resident before the previous
+// kernel of the stream has finished.  Each waits for that kernel's completion (griddepcontrol.wait)
+// before it touches any buffer and only then lets the next kernel launch
+// (griddepcontrol.launch_dependents); the next kernel's prologue -- a GEMV's weight prefetch --
+// then overlaps this one.  The library's GEMV kernels also wait before reading x, and a kernel
+// completes only after its wait has returned, so every kernel still sees all earlier results.
+__device__ __forceinline__ void pdl_begin() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 // The chunk's tokens and first position live in device memory ([kChunk] tokens, then the position),
 // copied from pinned host memory at the start of every chunk, so that a captured decode step
-// (CUDA graph) replays with new values.
+// (CUDA graph) replays with new values.  Launched plainly (it follows that copy).
 __global__ void embed_kernel(const __half* __restrict__ table, int hidden, const int32_t* __restrict__ tokpos,
                              float* __restrict__ h) {
+  pdl_begin();
   const int r = blockIdx.x;
   const __half* src = table + static_cast<int64_t>(tokpos[r]) * hidden;
   for (int i = threadIdx.x; i < hidden; i += blockDim.x) h[static_cast<int64_t>(r) * hidden + i] = __half2float(src[i]);
@@ -153,33 +187,76 @@ __device__ float block_sum(float v) {
   return s;
 }
 
-// out[r][i] = fp16(w[i] * h[r][i] / sqrt(mean_i h[r][i]^2 + eps)); w NULL = ones
-// (LlamaRMSNorm: the statistics in fp32, the scaled value times the weight).
-__global__ void rmsnorm_kernel(const float* __restrict__ h, int hidden, const __half* __restrict__ w, float eps,
-                               __half* __restrict__ out, int ldo) {
-  const int r = blockIdx.x;
-  const float* x = h + static_cast<int64_t>(r) * hidden;
+// Residual add fused with the RMSNorm that follows it.  Row r = row0 + blockIdx.x: with kAdd,
+// h[r][i] += y[r][i] (fp32, written back); then
+// out[blockIdx.x][i] = fp16(w[i] * h[r][i] / sqrt(mean_i h[r][i]^2 + eps)), without kW w = ones
+// (LlamaRMSNorm: the statistics in fp32, the scaled value times the weight).  A row of up to
+// kNormPer * blockDim.x values is held in registers, all of its loads (h, y and w) in flight at
+// once; longer rows take a loop in which each thread reads back only the elements it wrote.
+template <bool kAdd, bool kW>
+__global__ void add_rmsnorm_kernel(float* __restrict__ h, int hidden, const __half* __restrict__ y, int ldy,
+                                   int row0, const __half* __restrict__ w, float eps, __half* __restrict__ out,
+                                   int ldo) {
+  pdl_begin();
+  const int r = row0 + static_cast<int>(blockIdx.x);
+  float* x = h + static_cast<int64_t>(r) * hidden;
+  const __half* yr = kAdd ? y + static_cast<int64_t>(r) * ldy : nullptr;
+  __half* o = out + static_cast<int64_t>(blockIdx.x) * ldo;
+  const int nt = blockDim.x;
   float ss = 0.f;
-  for (int i = threadIdx.x; i < hidden; i += blockDim.x) ss += x[i] * x[i];
+  if (hidden <= kNormPer * nt) {
+    float v[kNormPer], t[kNormPer], wv[kNormPer];
+#pragma unroll
+    for (int j = 0; j < kNormPer; ++j) {
+      const int i = threadIdx.x + j * nt;
+      const bool in = i < hidden;
+      v[j] = in ? x[i] : 0.f;
+      if (kAdd) t[j] = in ? __half2float(yr[i]) : 0.f;
+      if (kW) wv[j] = in ? __half2float(w[i]) : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < kNormPer; ++j) {
+      const int i = threadIdx.x + j * nt;
+      if (kAdd) {
+        v[j] += t[j];
+        if (i < hidden) x[i] = v[j];
+      }
+      ss += v[j] * v[j];
+    }
+    const float inv = rsqrtf(block_sum(ss) / static_cast<float>(hidden) + eps);
+#pragma unroll
+    for (int j = 0; j < kNormPer; ++j) {
+      const int i = threadIdx.x + j * nt;
+      if (i < hidden) o[i] = __float2half_rn(kW ? wv[j] * (v[j] * inv) : v[j] * inv);
+    }
+    return;
+  }
+  for (int i = threadIdx.x; i < hidden; i += nt) {
+    const float v = kAdd ? x[i] + __half2float(yr[i]) : x[i];
+    if (kAdd) x[i] = v;
+    ss += v * v;
+  }
   const float inv = rsqrtf(block_sum(ss) / static_cast<float>(hidden) + eps);
-  for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+  for (int i = threadIdx.x; i < hidden; i += nt) {
     const float v = x[i] * inv;
-    out[static_cast<int64_t>(r) * ldo + i] = __float2half_rn(w ? __half2float(w[i]) * v : v);
+    o[i] = __float2half_rn(kW ? __half2float(w[i]) * v : v);
   }
 }
 
 // Rotary embedding (rotate-half pairing: dims i and i + hd/2 of a head, angle
 // pos * theta^(-2i/hd)) on q in place and on k, then k and v appended to the layer's cache
-// [kv_heads][ctx][hd] at position pos0 + r.
+// [kv_heads][ctx][hd] at position pos0 + r.  Token r = blockIdx.x; blockIdx.y splits its pairs.
 __global__ void rope_cache_kernel(__half* __restrict__ q, int ldq, const __half* __restrict__ k,
                                   const __half* __restrict__ v, int ldkv, int heads, int kv_heads, int hd,
                                   const int32_t* __restrict__ pos0p, float theta, __half* __restrict__ kc,
                                   __half* __restrict__ vc, int ctx) {
+  pdl_begin();
   const int r = blockIdx.x;
   const int pos = *pos0p + r;
   const int half = hd / 2;
   const int nq = heads * half, nk = kv_heads * half;
-  for (int i = threadIdx.x; i < nq + nk; i += blockDim.x) {
+  const int t0 = blockIdx.y * blockDim.x + threadIdx.x, dt = gridDim.y * blockDim.x;
+  for (int i = t0; i < nq + nk; i += dt) {
     const bool isq = i < nq;
     const int j = isq ? i : i - nq;
     const int head = j / half, d = j - head * half;
@@ -198,87 +275,177 @@ __global__ void rope_cache_kernel(__half* __restrict__ q, int ldq, const __half*
       dst[d + half] = y1;
     }
   }
-  for (int i = threadIdx.x; i < kv_heads * hd; i += blockDim.x) {
+  for (int i = t0; i < kv_heads * hd; i += dt) {
     const int head = i / hd, d = i - head * hd;
     vc[(static_cast<int64_t>(head) * ctx + pos) * hd + d] = v[static_cast<int64_t>(r) * ldkv + i];
   }
 }
 
-// Causal grouped-query attention of token r (position pos0 + r) for query head blockIdx.x over
-// cache positions 0..pos0+r: softmax(q.k / sqrt(hd)) . v with a running max per warp (each warp
-// takes every kAttnWarps-th position, lane l holds dims [E*l, E*l+E)), warps merged at the end.
-__global__ void __launch_bounds__(kAttnWarps * 32) attention_kernel(const __half* __restrict__ q, int ldq,
-                                                                    const __half* __restrict__ kc,
-                                                                    const __half* __restrict__ vc, int heads,
-                                                                    int kv_heads, int hd, int ctx,
-                                                                    const int32_t* __restrict__ pos0p,
-                                                                    __half* __restrict__ out, int ldo) {
-  constexpr int kMaxE = kMaxHeadDim / 32;
-  __shared__ float sm_m[kAttnWarps], sm_s[kAttnWarps], sm_acc[kAttnWarps][kMaxHeadDim];
-  const int head = blockIdx.x, r = blockIdx.y;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int E = hd / 32;
+__device__ __forceinline__ float block_max(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float m = red[0];
+  for (int i = 1; i < static_cast<int>(blockDim.x >> 5); ++i) m = fmaxf(m, red[i]);
+  __syncthreads();
+  return m;
+}
+
+__device__ __forceinline__ void unpack8(const uint4& raw, float* f) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __half2float(__ushort_as_half(static_cast<unsigned short>(w[i] & 0xffffu)));
+    f[2 * i + 1] = __half2float(__ushort_as_half(static_cast<unsigned short>(w[i] >> 16)));
+  }
+}
+
+// Causal grouped-query attention of token r = blockIdx.y (position pos0 + r) for query head
+// blockIdx.x: softmax(q.k / sqrt(hd)) . v over cache positions 0..pos0+r.  The positions are split
+// into gridDim.z equal ranges (split z = blockIdx.z) so that long contexts spread over many SMs.
+// A CTA walks its range in tiles of kAttnTile positions, with a running max M and sum T:
+//   scores: thread j takes positions j, j + kAttnThreads, ... (a full dot product each, its k row
+//           read with 16-byte loads, q from shared memory);
+//   weights: the tile's max updates M (earlier sums rescaled), w = exp(score - M);
+//   values: thread (g, c) adds w * v over positions g, g + G, ... for dims [8c, 8c + 8) (a warp
+//           reads whole rows of v), the G position groups summed at the end.
+// Every load of a phase is independent of the others, so they are in flight together.  The CTA
+// writes its record (M, T, unnormalised sums) to part[r][head][z]; the CTA that completes
+// count[r][head] (one atomic per CTA after a fence) merges the ranges' records, writes the output
+// and sets the count back to 0 for the next launch.
+__global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __half* __restrict__ q, int ldq,
+                                                                 const __half* __restrict__ kc,
+                                                                 const __half* __restrict__ vc, int heads,
+                                                                 int kv_heads, int hd, int ctx,
+                                                                 const int32_t* __restrict__ pos0p,
+                                                                 __half* __restrict__ out, int ldo,
+                                                                 float* __restrict__ part, int* __restrict__ count) {
+  __shared__ float sq[kMaxHeadDim];
+  __shared__ float sp[kAttnTile];
+  __shared__ float red[kAttnThreads / 32];
+  __shared__ float sacc[kAttnThreads * 8];  // [G][hd]: G * hd <= 8 * kAttnThreads
+  __shared__ int sm_last;
+  pdl_begin();
+  const int head = blockIdx.x, r = blockIdx.y, z = blockIdx.z, S = gridDim.z;
+  const int tid = threadIdx.x;
   const int kvh = head / (heads / kv_heads);
   const int L = *pos0p + r + 1;
+  const int per = (L + S - 1) / S;
+  const int pb = min(L, z * per), pe = min(L, pb + per);
   const float scale = rsqrtf(static_cast<float>(hd));
-  float qv[kMaxE], acc[kMaxE];
-#pragma unroll
-  for (int e = 0; e < kMaxE; ++e) {
-    qv[e] = e < E ? __half2float(q[static_cast<int64_t>(r) * ldq + head * hd + lane * E + e]) * scale : 0.f;
-    acc[e] = 0.f;
-  }
-  float m = -INFINITY, s = 0.f;
+  for (int d = tid; d < hd; d += kAttnThreads) sq[d] = __half2float(q[static_cast<int64_t>(r) * ldq + head * hd + d]) * scale;
   const __half* kb = kc + static_cast<int64_t>(kvh) * ctx * hd;
   const __half* vb = vc + static_cast<int64_t>(kvh) * ctx * hd;
-  for (int p = warp; p < L; p += kAttnWarps) {
-    const __half* kp = kb + static_cast<int64_t>(p) * hd + lane * E;
-    float dot = 0.f;
+  const int nc = hd / 8;               // 16-byte chunks per row
+  const int G = kAttnThreads / nc;     // position groups of the values phase
+  const int c = tid % nc, g = tid / nc;
+  float acc[8];
 #pragma unroll
-    for (int e = 0; e < kMaxE; ++e)
-      if (e < E) dot += qv[e] * __half2float(kp[e]);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-    const float mn = fmaxf(m, dot);
-    const float corr = expf(m - mn), w = expf(dot - mn);
-    s = s * corr + w;
-    const __half* vp = vb + static_cast<int64_t>(p) * hd + lane * E;
-#pragma unroll
-    for (int e = 0; e < kMaxE; ++e)
-      if (e < E) acc[e] = acc[e] * corr + w * __half2float(vp[e]);
-    m = mn;
-  }
-  if (lane == 0) {
-    sm_m[warp] = m;
-    sm_s[warp] = s;
-  }
-#pragma unroll
-  for (int e = 0; e < kMaxE; ++e)
-    if (e < E) sm_acc[warp][lane * E + e] = acc[e];
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  float M = -INFINITY, T = 0.f;
   __syncthreads();
-  float M = -INFINITY;
-  for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, sm_m[w]);
-  float S = 0.f;
-  for (int w = 0; w < kAttnWarps; ++w) S += sm_m[w] == -INFINITY ? 0.f : sm_s[w] * expf(sm_m[w] - M);
-  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-    float o = 0.f;
-    for (int w = 0; w < kAttnWarps; ++w)
-      if (sm_m[w] != -INFINITY) o += sm_acc[w][d] * expf(sm_m[w] - M);
-    out[static_cast<int64_t>(r) * ldo + head * hd + d] = __float2half_rn(o / S);
+  for (int t0 = pb; t0 < pe; t0 += kAttnTile) {
+    const int tn = min(kAttnTile, pe - t0);
+    for (int j = tid; j < tn; j += kAttnThreads) {
+      const uint4* kp = reinterpret_cast<const uint4*>(kb + static_cast<int64_t>(t0 + j) * hd);
+      float dot = 0.f;
+#pragma unroll 8
+      for (int cc = 0; cc < nc; ++cc) {
+        float f[8];
+        unpack8(kp[cc], f);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dot += sq[8 * cc + i] * f[i];
+      }
+      sp[j] = dot;
+    }
+    __syncthreads();
+    float mx = -INFINITY;
+    for (int j = tid; j < tn; j += kAttnThreads) mx = fmaxf(mx, sp[j]);
+    const float Mn = fmaxf(M, block_max(mx, red));
+    const float corr = expf(M - Mn);
+    float ts = 0.f;
+    for (int j = tid; j < tn; j += kAttnThreads) {
+      const float w = expf(sp[j] - Mn);
+      sp[j] = w;
+      ts += w;
+    }
+    T = T * corr + block_sum(ts);  // its barriers also publish the weights
+    M = Mn;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] *= corr;
+    if (g < G) {
+#pragma unroll 4
+      for (int j = g; j < tn; j += G) {
+        float f[8];
+        unpack8(*reinterpret_cast<const uint4*>(vb + static_cast<int64_t>(t0 + j) * hd + 8 * c), f);
+        const float w = sp[j];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] += w * f[i];
+      }
+    }
+    __syncthreads();  // the next tile overwrites sp
   }
+  if (g < G) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) sacc[g * hd + 8 * c + i] = acc[i];
+  }
+  __syncthreads();
+  __half* orow = out + static_cast<int64_t>(r) * ldo + head * hd;
+  if (S == 1) {
+    for (int d = tid; d < hd; d += kAttnThreads) {
+      float o = 0.f;
+      for (int gg = 0; gg < G; ++gg) o += sacc[gg * hd + d];
+      orow[d] = __float2half_rn(o / T);
+    }
+    return;
+  }
+  const int rec = hd + 2;
+  float* mine = part + ((static_cast<int64_t>(r) * heads + head) * S + z) * rec;
+  for (int d = tid; d < hd; d += kAttnThreads) {
+    float o = 0.f;
+    for (int gg = 0; gg < G; ++gg) o += sacc[gg * hd + d];
+    mine[2 + d] = o;
+  }
+  if (tid == 0) {
+    mine[0] = M;  // -inf for an empty range
+    mine[1] = T;
+  }
+  __threadfence();
+  __syncthreads();
+  int* cnt = count + static_cast<int64_t>(r) * heads + head;
+  if (tid == 0) sm_last = atomicAdd(cnt, 1) == S - 1;
+  __syncthreads();
+  if (!sm_last) return;
+  __threadfence();
+  const float* all = part + (static_cast<int64_t>(r) * heads + head) * S * rec;
+  float MM = -INFINITY;
+  for (int j = 0; j < S; ++j) MM = fmaxf(MM, __ldcg(all + j * rec));
+  float TT = 0.f;
+  for (int j = 0; j < S; ++j) {
+    const float mj = __ldcg(all + j * rec);
+    if (mj != -INFINITY) TT += __ldcg(all + j * rec + 1) * expf(mj - MM);
+  }
+  for (int d = tid; d < hd; d += kAttnThreads) {
+    float o = 0.f;
+    for (int j = 0; j < S; ++j) {
+      const float mj = __ldcg(all + j * rec);
+      if (mj != -INFINITY) o += __ldcg(all + j * rec + 2 + d) * expf(mj - MM);
+    }
+    orow[d] = __float2half_rn(o / TT);
+  }
+  if (tid == 0) *cnt = 0;
 }
 
-// h[r][i] += y[r][i]
-__global__ void residual_kernel(float* __restrict__ h, int hidden, const __half* __restrict__ y, int ldy) {
-  const int r = blockIdx.x;
-  for (int i = threadIdx.x; i < hidden; i += blockDim.x)
-    h[static_cast<int64_t>(r) * hidden + i] += __half2float(y[static_cast<int64_t>(r) * ldy + i]);
-}
-
-// a[r][i] = fp16(silu(g) * u), silu(g) = g / (1 + exp(-g))
-__global__ void silu_mul_kernel(const __half* __restrict__ g, const __half* __restrict__ u, int ldg, int n,
+// a[r][i] = fp16(silu(g[r][i]) * u[r][i]), silu(g) = g / (1 + exp(-g)), for rows < rows and
+// i < n: one thread per element over the whole grid.
+__global__ void silu_mul_kernel(const __half* __restrict__ g, const __half* __restrict__ u, int ldg, int n, int rows,
                                 __half* __restrict__ a, int lda) {
-  const int r = blockIdx.x;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+  pdl_begin();
+  const int64_t total = static_cast<int64_t>(rows) * n;
+  for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t < total;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(t / n), i = static_cast<int>(t - static_cast<int64_t>(r) * n);
     const float gv = __half2float(g[static_cast<int64_t>(r) * ldg + i]), uv = __half2float(u[static_cast<int64_t>(r) * ldg + i]);
     a[static_cast<int64_t>(r) * lda + i] = __float2half_rn(gv / (1.0f + expf(-gv)) * uv);
   }
@@ -310,6 +477,13 @@ struct Block {
 
 int pad8(int v) { return (v + 7) & ~7; }
 
+// Context ranges per (head, token) of an attention launch over n tokens: enough CTAs to cover the
+// SMs a few times (a decode step: kAttnSplits per head), one range per CTA for long prompt chunks.
+int attention_splits(int n, int heads) {
+  const int want = (kAttnMinCtas + n * heads - 1) / (n * heads);
+  return std::max(1, std::min(kAttnSplits, want));
+}
+
 }  // namespace
 
 struct BFEngine {
@@ -334,6 +508,8 @@ struct BFEngine {
   int ld_x = 0, ld_q = 0, ld_kv = 0, ld_i = 0, ld_y = 0, ld_qkv = 0, ld_gu = 0;
   void* ws = nullptr;
   size_t ws_bytes = 0;
+  float* att_part = nullptr;      // attention: per (token, head, context range) records of hd + 2 floats
+  int* att_count = nullptr;       // attention: ranges finished per (token, head); 0 between launches
   __half* host_logits = nullptr;  // pinned
   int32_t* d_tokpos = nullptr;    // [kChunk] tokens, then the chunk's first position
   int32_t* h_tokpos = nullptr;    // pinned mirror
@@ -756,6 +932,18 @@ int load_model(BFEngine* e, const char* path, uint32_t max_context) {
     ENG_CUDA(e, cudaMemset(p, 0, static_cast<size_t>(kChunk) * b.ld * 2));
     *b.p = static_cast<__half*>(p);
   }
+  void* ap = nullptr;
+  size_t records = 0;  // the most (token, head, range) records one attention launch writes
+  for (int n = 1; n <= static_cast<int>(kChunk); ++n) {
+    const int sp = attention_splits(n, e->heads);
+    if (sp > 1) records = std::max(records, static_cast<size_t>(n) * e->heads * sp);
+  }
+  if (dalloc(e, &ap, std::max<size_t>(records, 1) * (e->hd + 2) * 4)) return -1;
+  e->att_part = static_cast<float*>(ap);
+  void* ac = nullptr;
+  if (dalloc(e, &ac, static_cast<size_t>(kChunk) * e->heads * sizeof(int))) return -1;
+  ENG_CUDA(e, cudaMemset(ac, 0, static_cast<size_t>(kChunk) * e->heads * sizeof(int)));
+  e->att_count = static_cast<int*>(ac);
   void* hp = nullptr;
   if (dalloc(e, &hp, static_cast<size_t>(kChunk) * e->hidden * 4)) return -1;
   e->h = static_cast<float*>(hp);
@@ -775,7 +963,7 @@ int load_model(BFEngine* e, const char* path, uint32_t max_context) {
       if (d->present) all.push_back(d);
   all.push_back(e->lm_from_embed ? &e->embed : &e->lm_head);
   for (const DevLayer* d : all)
-    for (int b = 1; b <= static_cast<int>(kChunk); ++b)
+    for (int b = 1; b <= kGemvMaxBatch; ++b)
       e->ws_bytes = std::max(e->ws_bytes, opc_gemv_workspace_bytes(&d->L.plan, b, e->device));
   if (dalloc(e, &e->ws, e->ws_bytes)) return -1;
   ENG_OPC(e, opc_workspace_init(e->ws, e->ws_bytes, e->stream));
@@ -789,6 +977,15 @@ int load_model(BFEngine* e, const char* path, uint32_t max_context) {
 // Every launch of a chunk of n tokens, stream-ordered and asynchronous (no host synchronisation),
 // reading the tokens and the first position from d_tokpos; with want_logits the last token's
 // next-token logits are copied to host_logits.
+// add_rmsnorm_kernel for `rows` rows from row0, with the residual add when y is given and the
+// weight when w is given.
+cudaError_t launch_norm(cudaStream_t s, int rows, float* h, int hidden, const __half* y, int ldy, int row0,
+                        const __half* w, float eps, __half* out, int ldo) {
+  auto k = y ? (w ? add_rmsnorm_kernel<true, true> : add_rmsnorm_kernel<true, false>)
+             : (w ? add_rmsnorm_kernel<false, true> : add_rmsnorm_kernel<false, false>);
+  return launch_pdl(k, dim3(rows), dim3(kNormThreads), s, h, hidden, y, ldy, row0, w, eps, out, ldo);
+}
+
 int enqueue_chunk(BFEngine* e, int n, bool want_logits, uint32_t* n_launches) {
   cudaStream_t s = e->stream;
   const int32_t* pos0 = e->d_tokpos + kChunk;
@@ -796,8 +993,11 @@ int enqueue_chunk(BFEngine* e, int n, bool want_logits, uint32_t* n_launches) {
   uint32_t launches = 0;
   auto gemv = [&](const DevLayer& d, const __half* x, int ldx, __half* y, int ldy, int rows) -> int {
     ++launches;
-    if (opc_gemv(&d.L, x, ldx, y, ldy, rows, e->ws, e->ws_bytes, s) != OPC_OK)
-      return fail(e, "opc_gemv (%d x %d, batch %d): %s", d.L.plan.M, d.L.plan.K, rows, opc_last_error());
+    const int rc = rows <= kGemvMaxBatch ? opc_gemv(&d.L, x, ldx, y, ldy, rows, e->ws, e->ws_bytes, s)
+                                         : opc_gemm(&d.L, x, ldx, y, ldy, rows, s);
+    if (rc != OPC_OK)
+      return fail(e, "%s (%d x %d, %d tokens): %s", rows <= kGemvMaxBatch ? "opc_gemv" : "opc_gemm", d.L.plan.M,
+                  d.L.plan.K, rows, opc_last_error());
     if (d.nnz) {  // element-wise outliers: the CSR epilogue
       ++launches;
       if (opc_coo_gemv(d.L.plan.M, d.row_ptr, d.cols, d.delta, x, ldx, y, ldy, rows, s) != OPC_OK)
@@ -808,11 +1008,14 @@ int enqueue_chunk(BFEngine* e, int n, bool want_logits, uint32_t* n_launches) {
   ENG_CUDA(e, cudaMemcpyAsync(e->d_tokpos, e->h_tokpos, (kChunk + 1) * sizeof(int32_t), cudaMemcpyHostToDevice, s));
   embed_kernel<<<n, 256, 0, s>>>(e->embed_table, e->hidden, e->d_tokpos, e->h);
   ++launches;
+  const __half* res = nullptr;  // the previous block's down projection, still to be added into h
+  const int64_t silu_n = static_cast<int64_t>(n) * e->inter;
+  const unsigned silu_grid = static_cast<unsigned>(std::min<int64_t>((silu_n + 255) / 256, 4 * 148));
   for (int l = 0; l < e->n_layers; ++l) {
     const Block& B = e->blocks[l];
     __half* kc = e->kcache + static_cast<size_t>(l) * e->kv_heads * e->ctx * e->hd;
     __half* vc = e->vcache + static_cast<size_t>(l) * e->kv_heads * e->ctx * e->hd;
-    rmsnorm_kernel<<<n, 256, 0, s>>>(e->h, e->hidden, B.ln_in, e->eps, e->xn, e->ld_x);
+    ENG_CUDA(e, launch_norm(s, n, e->h, e->hidden, res, e->ld_y, 0, B.ln_in, e->eps, e->xn, e->ld_x));
     __half *qb = e->q, *kb = e->k, *vb = e->v;
     int ldq = e->ld_q, ldkv = e->ld_kv;
     if (B.qkv.present) {  // one GEMV for q|k|v
@@ -825,28 +1028,29 @@ int enqueue_chunk(BFEngine* e, int n, bool want_logits, uint32_t* n_launches) {
                gemv(B.v, e->xn, e->ld_x, e->v, e->ld_kv, n)) {
       return -1;
     }
-    rope_cache_kernel<<<n, 256, 0, s>>>(qb, ldq, kb, vb, ldkv, e->heads, e->kv_heads, e->hd, pos0, e->cfg.rope_theta,
-                                        kc, vc, static_cast<int>(e->ctx));
-    attention_kernel<<<dim3(e->heads, n), kAttnWarps * 32, 0, s>>>(qb, ldq, kc, vc, e->heads, e->kv_heads, e->hd,
-                                                                   static_cast<int>(e->ctx), pos0, e->att, e->ld_q);
+    ENG_CUDA(e, launch_pdl(rope_cache_kernel, dim3(n, kRopeSplit), dim3(256), s, qb, ldq, kb, vb, ldkv, e->heads,
+                           e->kv_heads, e->hd, pos0, e->cfg.rope_theta, kc, vc, static_cast<int>(e->ctx)));
+    ENG_CUDA(e, launch_pdl(attention_kernel, dim3(e->heads, n, attention_splits(n, e->heads)), dim3(kAttnThreads), s, qb, ldq, kc, vc,
+                           e->heads, e->kv_heads, e->hd, static_cast<int>(e->ctx), pos0, e->att, e->ld_q,
+                           e->att_part, e->att_count));
     if (gemv(B.o, e->att, e->ld_q, e->y, e->ld_y, n)) return -1;
-    residual_kernel<<<n, 256, 0, s>>>(e->h, e->hidden, e->y, e->ld_y);
-    rmsnorm_kernel<<<n, 256, 0, s>>>(e->h, e->hidden, B.ln_post, e->eps, e->xn, e->ld_x);
+    ENG_CUDA(e, launch_norm(s, n, e->h, e->hidden, e->y, e->ld_y, 0, B.ln_post, e->eps, e->xn, e->ld_x));
     if (B.gu.present) {  // one GEMV for gate|up
       if (gemv(B.gu, e->xn, e->ld_x, e->gu, e->ld_gu, n)) return -1;
-      silu_mul_kernel<<<n, 256, 0, s>>>(e->gu, e->gu + e->inter, e->ld_gu, e->inter, e->a, e->ld_i);
+      ENG_CUDA(e, launch_pdl(silu_mul_kernel, dim3(silu_grid), dim3(256), s, e->gu, e->gu + e->inter, e->ld_gu,
+                             e->inter, n, e->a, e->ld_i));
     } else {
       if (gemv(B.gate, e->xn, e->ld_x, e->g, e->ld_i, n) || gemv(B.up, e->xn, e->ld_x, e->u, e->ld_i, n)) return -1;
-      silu_mul_kernel<<<n, 256, 0, s>>>(e->g, e->u, e->ld_i, e->inter, e->a, e->ld_i);
+      ENG_CUDA(e, launch_pdl(silu_mul_kernel, dim3(silu_grid), dim3(256), s, e->g, e->u, e->ld_i, e->inter, n, e->a,
+                             e->ld_i));
     }
     if (gemv(B.down, e->a, e->ld_i, e->y, e->ld_y, n)) return -1;
-    residual_kernel<<<n, 256, 0, s>>>(e->h, e->hidden, e->y, e->ld_y);
-    launches += 7;  // two RMSNorms, rotary + cache append, attention, two residual adds, SiLU gating
+    res = e->y;
+    launches += 5;  // two RMSNorms (each with the residual add before it), rotary + cache append, attention, SiLU
   }
 
-  if (want_logits) {
-    rmsnorm_kernel<<<1, 256, 0, s>>>(e->h + static_cast<size_t>(n - 1) * e->hidden, e->hidden, e->final_norm, e->eps,
-                                     e->xn, e->ld_x);
+  if (want_logits) {  // the last residual add and the final norm, for the chunk's last token only
+    ENG_CUDA(e, launch_norm(s, 1, e->h, e->hidden, res, e->ld_y, n - 1, e->final_norm, e->eps, e->xn, e->ld_x));
     ++launches;
     if (gemv(e->lm_from_embed ? e->embed : e->lm_head, e->xn, e->ld_x, e->logits16, e->vocab, 1)) return -1;
     ENG_CUDA(e, cudaMemcpyAsync(e->host_logits, e->logits16, static_cast<size_t>(e->vocab) * 2,

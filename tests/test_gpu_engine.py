@@ -53,14 +53,27 @@ def test_steps_match_float64_at_every_position(model):
         assert rel_err(lg, ref[-1]) < TOL
 
 
-def test_long_prompt_runs_in_chunks_on_the_gemm(model):
-    toks = _tokens(100, model["vocab"], seed=3)  # chunks of 64 + 36 tokens: batches above the GEMV->GEMM crossover
+def test_long_prompt_runs_on_the_gemm(model):
+    toks = _tokens(100, model["vocab"], seed=3)  # one chunk of 100 tokens: projections on opc_gemm
     ref = forward64(model, toks)
     with Engine(model["path"]) as eng:
         assert rel_err(eng.forward(toks), ref[-1]) < TOL
         eng.reset()
         eng.prefill(toks[:-1])
         assert rel_err(eng.forward_step(toks[-1]), ref[-1]) < TOL
+
+
+def test_long_context_decode_steps(model):
+    # 600 positions: a prompt of two chunks (512 + 85 tokens, projections on opc_gemm), then decode
+    # steps whose attention splits the context into ranges of many positions each and merges the
+    # ranges' partial softmax records across CTAs
+    toks = _tokens(600, model["vocab"], seed=8)
+    ref = forward64(model, toks)
+    with Engine(model["path"]) as eng:
+        eng.prefill(toks[:-3])
+        for i in range(3):
+            lg = eng.forward_step(toks[-3 + i])
+            assert rel_err(lg, ref[-3 + i]) < TOL, i
 
 
 @pytest.mark.parametrize("variant", ["svs8", "tied_no_norms", "no_outliers_json_without_heads"])
