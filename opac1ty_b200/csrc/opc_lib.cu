@@ -22,6 +22,7 @@
 #include "opc_coo.cuh"
 #include "opc_gemm.cuh"
 #include "opc_gemv.cuh"
+#include "opc_gemvd.cuh"
 #include "opc_gemvq.cuh"
 #include "opc_layer.cuh"
 #include "opc_vq8.cuh"
@@ -604,6 +605,32 @@ int launch_vq8(const char* fn, const opc_layer* L, const void* x, int64_t ldx, v
   OPC_CUDA(cudaGetLastError(), "launch vq8_gemv_kernel");
   return OPC_OK;
 }
+int launch_gemvd(const opc::GemvDArgs& args, int64_t grid, size_t smem, cudaStream_t stream, int dev) {
+  static std::mutex mu;
+  static std::map<int, size_t> configured;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = configured.find(dev);
+    if (it == configured.end() || it->second < smem) {
+      OPC_CUDA(cudaFuncSetAttribute(opc::gemvd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)),
+               "cudaFuncSetAttribute(max dynamic smem, gemvd)");
+      configured[dev] = smem;
+    }
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(opc::kDThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  OPC_CUDA(cudaLaunchKernelEx(&cfg, opc::gemvd_kernel, args), "launch gemvd_kernel");
+  return OPC_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -651,6 +678,42 @@ int opc_gemv(const opc_layer* L, const void* x, int64_t ldx, void* y, int64_t ld
   if (batch <= opc::kQMaxBatch) {
     const int xs_q = static_cast<int>(align_up(static_cast<size_t>(3 * batch) * opc::xsq_col_bytes(p.k_units) +
                                                    opc::kQZeroBytes + opc::kQOnesBytes, 128));
+    // The single-launch kernel (opc_gemvd.cuh) when its staged x and unit rings fit, its 32-bit
+    // unit arithmetic holds and the count-carrying sums stay exact (K <= 2^15); else gemvq_kernel.
+    const size_t smem_d = static_cast<size_t>(xs_q) + opc::kDRingBytes;
+    const int64_t grid_d = std::min<int64_t>(dc.sm_count, std::max<int64_t>(1, ceil_div(p.total_units, opc::kDWarps)));
+    const int64_t nw_d = std::min<int64_t>(grid_d * opc::kDWarps, p.total_units);
+    if (smem_d + 1024 <= static_cast<size_t>(dc.max_smem_optin) && p.K <= 32768 &&
+        static_cast<uint64_t>(nw_d) * static_cast<uint64_t>(p.total_units) < (1ull << 32)) {
+      opc::GemvDArgs d;
+      memset(&d, 0, sizeof(d));
+      d.units = static_cast<const uint8_t*>(L->units);
+      d.ounits = ounits_q(L);
+      d.cbq = codebooks_q(L);
+      d.tile_mask = static_cast<const uint16_t*>(L->tile_mask);
+      d.orow = L->outlier_rows;
+      d.oexp = L->outlier_rows + n_slots_of(p);
+      d.x = static_cast<const __half*>(x);
+      d.y = static_cast<__half*>(y);
+      d.acc = reinterpret_cast<unsigned long long*>(static_cast<char*>(workspace) + acc_offset(p, dc.sm_count));
+      d.ldx = ldx;
+      d.ldy = ldy;
+      d.Up = static_cast<int32_t>(p.packed_units);
+      d.U = static_cast<int32_t>(p.total_units);
+      d.NW = static_cast<int32_t>(nw_d);
+      d.M = p.M;
+      d.K = p.K;
+      d.K_pad = p.K_pad;
+      d.MT = p.row_tiles;
+      d.KT = p.k_units;
+      d.OT = p.outlier_tiles;
+      d.KO = p.outlier_k_units;
+      d.batch = batch;
+      d.xs_bytes = xs_q;
+      d.x_vec16 = (p.K % 8 == 0) && (ldx % 8 == 0) && aligned(x, 16);
+      d.negz = opc::kNegZero2;
+      return launch_gemvd(d, grid_d, smem_d, s, dev);
+    }
     int stages = opc::kQMaxStages;
     while (stages >= 2 && gemvq_smem(xs_q, stages) > static_cast<size_t>(dc.max_smem_optin)) --stages;
     if (stages >= 2) {
