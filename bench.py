@@ -19,6 +19,8 @@ steps.
   prefill / llama70b / sweep  (N = 1) the other benchmark configurations: the tcgen05 prefill
             GEMM at 512 and 2048 tokens, the Llama-3-70B decode step at batch 1 and 16, and the
             outlier x batch sweep of the 14336x4096 gate projection with the GEMV->GEMM crossover
+  engine    (N = 1) the bf_engine_* API on a 4-block Llama-3.1-8B-shaped model: a 512-token
+            prompt and decode steps with attention, norms and the lm_head, in a child process
 
 --impl reference times the reference's CPU implementation of the path (dequantize + fp32 matmul,
 restated in C in oracle/) on all host cores for the same metric: each step is one whole decode
@@ -366,6 +368,24 @@ def parity_check(stack, cfg, args, dev, dist, world, rank) -> dict:
     return res
 
 
+def engine_config(blocks: int = 4, prompt: int = 512, steps: int = 32, timeout_s: float = 240.0) -> dict:
+    """The engine API (bf_engine_*) on a synthetic Llama-3.1-8B-shaped .bf2 of `blocks` blocks and
+    a 32000-token vocabulary: a `prompt`-token prefill and `steps` decode steps (attention, norms,
+    rotary embedding and the lm_head included), run by `cli engine-bench` in a child process (its
+    own CUDA context, so a failure there cannot take this run down; host-timed around each call
+    with the logits copied back)."""
+    cmd = [sys.executable, "-m", "opac1ty_b200.cli", "engine-bench", "--blocks", str(blocks), "--prompt", str(prompt),
+           "--steps", str(steps)]
+    r = subprocess.run(cmd, cwd=str(ROOT), capture_output=True, text=True, timeout=timeout_s)
+    if r.returncode != 0:
+        return {"error": f"engine-bench exited {r.returncode}: {r.stderr.strip()[-300:]}"}
+    res = json.loads(r.stdout.strip().splitlines()[-1])
+    res["config"] = (f"bf_engine_* on a Llama-3.1-8B-shaped model of {blocks} blocks: {prompt}-token prompt, then "
+                     f"{steps} decode steps (host-timed per call, logits copied back)")
+    res["step_ms_per_block"] = round(res["step_ms"] / blocks, 4)
+    return res
+
+
 def extra_configs(dev, peaks) -> dict:
     """The other benchmark configurations (configs 2-4), device-timed; each key stands alone."""
     import torch
@@ -400,6 +420,12 @@ def extra_configs(dev, peaks) -> dict:
     except Exception as e:  # noqa: BLE001
         out["sweep"] = {"error": str(e)}
     log(f"sweep done ({time.time() - t0:.0f} s)")
+    t0 = time.time()
+    try:
+        out["engine"] = engine_config()
+    except Exception as e:  # noqa: BLE001
+        out["engine"] = {"error": str(e)}
+    log(f"engine done ({time.time() - t0:.0f} s)")
     return out
 
 
