@@ -574,7 +574,8 @@ struct Model {
 int parse_file(BFEngine* e, const MappedFile& f, Model* m) {
   const uint8_t* b = f.p;
   const size_t size = f.size;
-  if (size < 24 || std::memcmp(b, "BF2\0", 4) != 0) return fail(e, "Not a valid BF2 file (bad magic)");
+  if (size < 4 || std::memcmp(b, "BF2\0", 4) != 0) return fail(e, "Not a valid BF2 file (bad magic)");
+  if (size < 24) return fail(e, "Not a valid BF2 file (truncated file header: %zu bytes)", size);
   const uint32_t version = rd<uint32_t>(b + 4), flags = rd<uint32_t>(b + 8);
   if (version != 1) return fail(e, "Unsupported BF2 version: %u (expected 1)", version);
   size_t pos = 16;

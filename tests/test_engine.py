@@ -94,3 +94,18 @@ def test_valid_model_parses_up_to_the_device(tmp_path):
     p = tmp_path / "m.bf2"
     build(p, hidden=128, heads=2, kv_heads=1, n_layers=1, inter=256, vocab=160, checksum=True)
     assert "cudaSetDevice" in _error_of(p)
+
+
+@pytest.mark.parametrize("cut", [8, 20, 0.25, 0.5, 0.75, 0.999, -1])
+def test_truncated_file_is_rejected_while_parsing(tmp_path, cut):
+    """A file cut short anywhere -- in the file header, a layer header or a payload -- is refused
+    by the parser with an error on the handle, before any device work."""
+    from engine_model import build
+
+    p = tmp_path / "m.bf2"
+    build(p, hidden=128, heads=2, kv_heads=1, n_layers=1, inter=256, vocab=160, checksum=False)
+    data = p.read_bytes()
+    n = len(data) + cut if isinstance(cut, int) and cut < 0 else (cut if isinstance(cut, int) else int(len(data) * cut))
+    p.write_bytes(data[:n])
+    err = _error_of(p)
+    assert "cudaSetDevice" not in err and "CUDA" not in err, err
