@@ -69,23 +69,27 @@ T rd(const uint8_t* p) {
   return v;
 }
 
+// Payload bytes of a layer as its header describes it; SIZE_MAX when the fields describe more
+// than any file can hold (the sums are formed in 128 bits, so no header value wraps them around).
 size_t payload_bytes(const FileLayer& l, int id_bytes) {
-  if (l.type == kSparse)  // codebooks, indices, values [nnz] fp16, positions [nnz][2] int32
-    return static_cast<size_t>(l.n_groups) * l.entries * l.svs * 2 +
-           (l.svs ? static_cast<size_t>(l.n_groups) * (l.in_f / l.svs) : 0) + static_cast<size_t>(l.nnz) * 10;
-  if (l.type == kQuantized) {
-    size_t n = static_cast<size_t>(l.n_groups) * l.entries * l.svs * 2;
-    if (l.svs) n += static_cast<size_t>(l.n_groups) * (l.in_f / l.svs);
-    if (l.n_out) n += static_cast<size_t>(l.n_out) * l.in_f * 2 + static_cast<size_t>(l.n_out) * id_bytes;
-    return n;
+  using u128 = unsigned __int128;
+  u128 n = 0;
+  if (l.type == kSparse) {  // codebooks, indices, values [nnz] fp16, positions [nnz][2] int32
+    n = static_cast<u128>(l.n_groups) * l.entries * l.svs * 2 +
+        (l.svs ? static_cast<u128>(l.n_groups) * (l.in_f / l.svs) : 0) + static_cast<u128>(l.nnz) * 10;
+  } else if (l.type == kQuantized) {
+    n = static_cast<u128>(l.n_groups) * l.entries * l.svs * 2;
+    if (l.svs) n += static_cast<u128>(l.n_groups) * (l.in_f / l.svs);
+    if (l.n_out) n += static_cast<u128>(l.n_out) * l.in_f * 2 + static_cast<u128>(l.n_out) * id_bytes;
+  } else if (l.type == kPassthrough) {
+    n = static_cast<u128>(l.out_f) * l.in_f * 2;
   }
-  if (l.type == kPassthrough) return static_cast<size_t>(l.out_f) * l.in_f * 2;
-  return 0;
+  return n >= static_cast<u128>(SIZE_MAX) ? SIZE_MAX : static_cast<size_t>(n);
 }
 
 // Parse the layer header at `pos` (false when it is not a plausible header).
 bool parse_layer_at(const uint8_t* base, size_t size, size_t pos, FileLayer* out) {
-  if (pos + kLayerHeader > size) return false;
+  if (pos > size || size - pos < kLayerHeader) return false;
   const uint8_t* h = base + pos;
   FileLayer l;
   const uint16_t nlen = rd<uint16_t>(h);
@@ -97,7 +101,8 @@ bool parse_layer_at(const uint8_t* base, size_t size, size_t pos, FileLayer* out
   l.svs = h[16];
   l.n_out = rd<uint16_t>(h + 17);
   l.nnz = l.type == kSparse ? rd<uint64_t>(h + 51) : 0;
-  if (nlen == 0 || l.type > 2 || pos + kLayerHeader + nlen > size) return false;
+  if (nlen == 0 || l.type > 2 || size - pos - kLayerHeader < nlen) return false;
+  if (l.out_f > 0x7fffffffu || l.in_f > 0x7fffffffu || l.n_groups > 0x7fffffffu) return false;
   l.name.assign(reinterpret_cast<const char*>(h + kLayerHeader), nlen);
   l.data = pos + kLayerHeader + nlen;
   *out = l;
@@ -603,16 +608,18 @@ int parse_file(BFEngine* e, const MappedFile& f, Model* m) {
     FileLayer l;
     if (!parse_layer_at(b, end, pos, &l)) return fail(e, "layer %u header at byte %zu is invalid or truncated", i, pos);
     l.id_bytes = 4;
+    // the offset `n` payload bytes after the layer's name, SIZE_MAX past the end
+    auto after = [&](size_t n) { return n <= end - l.data ? l.data + n : SIZE_MAX; };
     if (l.type == kQuantized && l.n_out > 0) {  // which outlier-id width is followed by a layer (or the end)
       FileLayer probe;
-      const size_t e4 = l.data + payload_bytes(l, 4), e8 = l.data + payload_bytes(l, 8);
+      const size_t e4 = after(payload_bytes(l, 4)), e8 = after(payload_bytes(l, 8));
       const bool last = i + 1 == count;
       const bool ok4 = last ? e4 == end : parse_layer_at(b, end, e4, &probe);
       const bool ok8 = last ? e8 == end : parse_layer_at(b, end, e8, &probe);
       if (!ok4 && ok8) l.id_bytes = 8;
       else if (!ok4 && !ok8 && !last) return fail(e, "cannot locate the layer after '%s'", l.name.c_str());
     }
-    const size_t next = l.data + payload_bytes(l, l.id_bytes);
+    const size_t next = after(payload_bytes(l, l.id_bytes));
     if (next > end) return fail(e, "layer '%s' is truncated", l.name.c_str());
     m->layers[l.name] = l;
     pos = next;

@@ -109,3 +109,34 @@ def test_truncated_file_is_rejected_while_parsing(tmp_path, cut):
     p.write_bytes(data[:n])
     err = _error_of(p)
     assert "cudaSetDevice" not in err and "CUDA" not in err, err
+
+
+def _first_layer_header(data: bytes) -> int:
+    import struct
+
+    pos = 12
+    pos += 8 + struct.unpack_from("<I", data, pos)[0]   # model JSON (length written twice)
+    pos += 4 + struct.unpack_from("<I", data, pos)[0]   # quantize JSON
+    return pos + 4                                      # layer count
+
+
+@pytest.mark.parametrize("field,offset,width,value", [
+    ("nnz", 51, 8, 2 ** 62), ("nnz", 51, 8, 2 ** 64 - 1), ("nnz", 51, 8, 10 ** 12),
+    ("n_groups", 11, 4, 0x7FFFFFFF), ("n_groups", 11, 4, 0xFFFFFFFF),
+    ("in_features", 7, 4, 0x7FFFFFFF), ("in_features", 7, 4, 0xFFFFFFFF), ("out_features", 3, 4, 0xFFFFFFFF)])
+def test_oversized_layer_fields_are_refused(tmp_path, field, offset, width, value):
+    """Layer header fields that describe more bytes than the file holds (or sizes past 2^31) are
+    refused while parsing; sizes are summed without wrapping around, so no field value makes the
+    loader read outside the mapped file.  The first layer of this model has element-wise
+    outliers, so its header carries the entry count (u64)."""
+    from engine_model import build
+
+    p = tmp_path / "m.bf2"
+    build(p, hidden=128, heads=2, kv_heads=1, n_layers=1, inter=256, vocab=160, element=True, checksum=False)
+    data = bytearray(p.read_bytes())
+    h = _first_layer_header(bytes(data))
+    assert data[h + 2] == 1  # a sparse_outlier layer
+    data[h + offset:h + offset + width] = value.to_bytes(width, "little")
+    p.write_bytes(bytes(data))
+    err = _error_of(p)
+    assert "truncated" in err or "invalid" in err, (field, err)
