@@ -1199,11 +1199,31 @@ int32_t sample_token(const std::vector<float>& logits_in, const BFSamplingParams
       }
   }
   if (!(p.temperature > 1e-6f)) return static_cast<int32_t>(std::max_element(l.begin(), l.end()) - l.begin());
+  const bool cut_k = p.top_k > 0 && p.top_k < V, cut_p = p.top_p > 0.f && p.top_p < 1.f;
+  if (!cut_k && !cut_p) {  // the whole softmax: a draw needs no ordering of the vocabulary
+    const double mx = *std::max_element(l.begin(), l.end());
+    std::vector<double> w(V);
+    double sum = 0.0;
+    for (int i = 0; i < V; ++i) sum += (w[i] = std::exp((static_cast<double>(l[i]) - mx) / p.temperature));
+    const double r = std::uniform_real_distribution<double>(0.0, sum)(rng);
+    double c = 0.0;
+    for (int i = 0; i < V; ++i) {
+      c += w[i];
+      if (r < c) return i;
+    }
+    return V - 1;
+  }
+  // candidates by descending logit (ties: lower id first); with top-k only the first k are ordered
   std::vector<int> idx(V);
   std::iota(idx.begin(), idx.end(), 0);
-  std::sort(idx.begin(), idx.end(), [&](int a, int b) { return l[a] > l[b] || (l[a] == l[b] && a < b); });
+  const auto before = [&](int a, int b) { return l[a] > l[b] || (l[a] == l[b] && a < b); };
   int keep = V;
-  if (p.top_k > 0 && p.top_k < keep) keep = p.top_k;
+  if (cut_k) {
+    keep = p.top_k;
+    std::partial_sort(idx.begin(), idx.begin() + keep, idx.end(), before);
+  } else {
+    std::sort(idx.begin(), idx.end(), before);
+  }
   std::vector<double> w(keep);
   const double mx = l[idx[0]];
   double sum = 0.0;
