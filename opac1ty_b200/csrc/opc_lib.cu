@@ -2217,7 +2217,7 @@ int opc_take_device_error(int32_t device, int32_t* code) {
   int v = 0, zero = 0;
   cudaError_t e = cudaDeviceSynchronize();
   if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&v, opc::g_opc_device_error, sizeof(int));
-  if (e == cudaSuccess) e = cudaMemcpyToSymbol(opc::g_opc_device_error, &zero, sizeof(int));
+  if (e == cudaSuccess && v != 0) e = cudaMemcpyToSymbol(opc::g_opc_device_error, &zero, sizeof(int));  // (already 0 otherwise)
   cudaSetDevice(prev);
   if (e != cudaSuccess) return cuda_fail(e, "opc_take_device_error");
   *code = v;
