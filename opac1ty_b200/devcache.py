@@ -17,6 +17,7 @@ import ctypes
 import json
 import mmap
 import os
+import zipfile
 from pathlib import Path
 from typing import Dict, Optional
 
@@ -116,8 +117,8 @@ def load_bf2_layers(path, device=None, cache_dir: Optional[str] = None) -> Dict[
     if cache is not None and cache.exists():
         try:
             return load_layers(cache, device)
-        except (CacheMismatch, KeyError, ValueError, OSError):
-            pass
+        except (CacheMismatch, KeyError, ValueError, OSError, EOFError, zipfile.BadZipFile):
+            pass  # unreadable or foreign: repack and rewrite it
     layers: Dict[str, L.DeviceLayer] = {}
     with BF2Reader(str(path)) as r:
         for name in r.layer_names():

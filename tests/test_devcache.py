@@ -73,6 +73,16 @@ def test_buffers_must_match_the_plan(tmp_path):
         devcache.load_layers(p, CPU)
 
 
+@pytest.mark.parametrize("content", [b"garbage", b"PK\x03\x04" + b"\x00" * 40])
+def test_unreadable_cache_file_raises_what_the_loader_catches(tmp_path, content):
+    import zipfile
+
+    p = tmp_path / "c.npz"
+    p.write_bytes(content)
+    with pytest.raises((devcache.CacheMismatch, KeyError, ValueError, OSError, EOFError, zipfile.BadZipFile)):
+        devcache.load_layers(p, CPU)
+
+
 def test_key_follows_the_file(tmp_path):
     a, b = tmp_path / "a.bf2", tmp_path / "b.bf2"
     for path, seed in ((a, 1), (b, 2)):
